@@ -1,0 +1,128 @@
+/*
+ * kokopop_b200 — C ABI of the B200 (sm_100a) Kokoro-82M synthesis hot path.
+ *
+ * This is the thin layer that kokopop's C++ host code calls in place of the
+ * ggml graph for the hot-path ops only. Everything above it (include/kokopop.h,
+ * the session / streaming layer, the GGUF loader) is unchanged.
+ *
+ * Conventions (mirroring the reference's C API, include/kokopop.h:125-132 and
+ * src/kokopop.cpp:38-59):
+ *   - every call returns a KK_* status; on failure a message is stored in a
+ *     thread-local slot read by kk_last_error() (src/core/error.cpp:4-15);
+ *   - no C++ exception and no CUDA error crosses this boundary;
+ *   - a kk_ctx owns one CUDA stream and all device memory it uses; it is not
+ *     thread-safe, exactly like a kokopop_model (docs/c-api.md:284-286);
+ *   - pointers are plain host pointers unless the name ends in _device, in
+ *     which case they are device pointers on the context's device and the
+ *     call is asynchronous on `stream` (NULL = the context's own stream).
+ *
+ * Layouts follow ggml (ne[0] fastest). Per utterance, an activation written
+ * "[L, C]" is time-fastest: x[c * L + t] (src/arch/kokoro/kokoro.h:200-212).
+ * Ragged batches are the per-utterance arrays concatenated back to back.
+ */
+#ifndef KOKOPOP_B200_H
+#define KOKOPOP_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same numeric values as KOKOPOP_OK .. KOKOPOP_ERROR_INFERENCE
+ * (include/kokopop.h:125-132), so the host can return them unchanged. */
+enum {
+    KK_OK = 0,
+    KK_ERROR_INVALID_ARGUMENT = 1,
+    KK_ERROR_IO = 2,
+    KK_ERROR_MODEL = 3,
+    KK_ERROR_INFERENCE = 5
+};
+
+/* Same numeric values as GGML_TYPE_F32 / GGML_TYPE_F16. */
+enum { KK_DTYPE_F32 = 0, KK_DTYPE_F16 = 1 };
+
+/* One weight tensor as the reference's loader holds it: logical GGUF name
+ * (tools/convert_kokoro_to_gguf.py layout, dims already reversed to ggml
+ * order), type and host data. Replaces the weight upload of
+ * src/model/model.cpp:429-443 for the tensors the hot path reads. */
+typedef struct kk_tensor_desc {
+    const char *name;
+    int32_t dtype;     /* KK_DTYPE_F32 or KK_DTYPE_F16 (raw IEEE half bits) */
+    int32_t n_dims;
+    int64_t ne[4];     /* unused trailing dims = 1 */
+    const void *data;  /* host pointer, copied during the call */
+} kk_tensor_desc;
+
+typedef struct kk_ctx kk_ctx;
+
+/* Creates a context on CUDA device `device` (the value KOKOPOP_CUDA_DEVICE
+ * selects in src/backend/cuda.cpp:38-45). Fails on a device that is not
+ * sm_100. */
+int kk_ctx_create(int device, kk_ctx **out);
+void kk_ctx_destroy(kk_ctx *ctx);
+
+/* Uploads the hot-path weights once (replaces KokoroArch::preload_tensor_cache,
+ * src/arch/kokoro/kokoro_arch.cpp:389-607, for these tensors). Tensors the hot
+ * path does not read are ignored. May be called again to replace weights. */
+int kk_weights_upload(kk_ctx *ctx, const kk_tensor_desc *descs, size_t n);
+
+/* Thread-local message of the last failed call on this thread. */
+const char *kk_last_error(void);
+
+/* Decoder encode/decode + ISTFTNet generator + iSTFT for a ragged batch of
+ * independent utterances. Replaces, per utterance, the decoder sub-graph of
+ * run_kokoro_generation_probe (src/arch/kokoro/kokoro.cpp:716-763) followed by
+ * ggml_generator (src/arch/kokoro/audio_utils.cpp:594-1051).
+ *   n_frames[u] = T_u (asr frames, 40 per second of audio), 1 <= T_u <= 8192
+ *   asr   : per utterance [T_u, 512]   (time-fastest)
+ *   f0    : per utterance [2 T_u]      (F0 curve, Hz)
+ *   noise : per utterance [2 T_u]      (N curve)
+ *   style : per utterance [128]        (decoder half of the voice row)
+ *   audio : per utterance [600 T_u]    samples at 24 kHz, clamped to +-1
+ */
+int kk_decoder_forward(kk_ctx *ctx, int32_t n_utts, const int32_t *n_frames,
+                       const float *asr, const float *f0, const float *noise,
+                       const float *style, float *audio);
+
+/* Same as kk_decoder_forward with device-resident inputs and output; the
+ * lengths stay on the host. Asynchronous on `stream`. */
+int kk_decoder_forward_device(kk_ctx *ctx, int32_t n_utts, const int32_t *n_frames,
+                              const float *asr, const float *f0,
+                              const float *noise, const float *style,
+                              float *audio, void *stream);
+
+/* The ggml_generator seam (src/arch/kokoro/kokoro.h:214-219) for a ragged
+ * batch: decoder output [L_u, 512] with L_u = 2 T_u, f0 [L_u], style [128]
+ * -> audio [300 L_u]. Host buffers. */
+int kk_generator_forward(kk_ctx *ctx, int32_t n_utts, const int32_t *n_decoder_frames,
+                         const float *decoder, const float *f0, const float *style,
+                         float *audio);
+
+/* The Kokoro iSTFT seam (cpu_istft, src/arch/kokoro/audio_utils.cpp:462-536):
+ * post [n_frames, 22] (bin-major: post[r * n_frames + t]) -> audio
+ * [(n_frames - 1) * 5], clamped to +-1. n_frames may be 0 or 1 (no samples). */
+int kk_istft(kk_ctx *ctx, int64_t n_frames, const float *post, float *audio);
+
+/* Counters of a context, for measurement (no counterpart in the reference,
+ * which prints ggml_time_us stage timings under KOKOPOP_GEN_PROFILE,
+ * src/arch/kokoro/audio_utils.cpp:834-893). */
+typedef struct kk_profile {
+    uint64_t launches;       /* kernels this context launched */
+    uint64_t conv_launches;  /* dense-convolution launches timed */
+    double conv_ms;          /* their summed device time (CUDA events) */
+    double conv_flop;        /* their algorithmic FLOPs: 2*OC*IC*K per valid position */
+} kk_profile;
+
+/* When enabled, every dense-convolution launch is bracketed by CUDA events
+ * on its stream. */
+int kk_profile_enable(kk_ctx *ctx, int enable);
+/* Reads (after synchronising the context's work) and optionally resets. */
+int kk_profile_read(kk_ctx *ctx, kk_profile *out, int reset);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KOKOPOP_B200_H */

@@ -1,0 +1,194 @@
+"""kokopop_b200 — B200 (sm_100a) Kokoro-82M synthesis hot path.
+
+Python access to the C ABI of include/kokopop_b200.h through ctypes. The
+product is the in-tree shared library libkokopop_b200.so (CUDA kernels plus
+the C++ host layer); this module only marshals arguments. There is no CPU
+fallback: without the library, or without a B200, every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Dict, List, Optional, Sequence
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libkokopop_b200.so")
+HEADER = os.path.join(HERE, "..", "include", "kokopop_b200.h")
+
+KK_OK = 0
+KK_ERROR_INVALID_ARGUMENT = 1
+KK_ERROR_IO = 2
+KK_ERROR_MODEL = 3
+KK_ERROR_INFERENCE = 5
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_i32p = ctypes.POINTER(ctypes.c_int32)
+
+
+class TensorDesc(ctypes.Structure):
+    _fields_ = [
+        ("name", ctypes.c_char_p),
+        ("dtype", ctypes.c_int32),
+        ("n_dims", ctypes.c_int32),
+        ("ne", ctypes.c_int64 * 4),
+        ("data", ctypes.c_void_p),
+    ]
+
+
+class Profile(ctypes.Structure):
+    _fields_ = [
+        ("launches", ctypes.c_uint64),
+        ("conv_launches", ctypes.c_uint64),
+        ("conv_ms", ctypes.c_double),
+        ("conv_flop", ctypes.c_double),
+    ]
+
+
+class KKError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"[{code}] {msg}")
+        self.code = code
+
+
+_lib = None
+
+
+def load_library():
+    """Loads libkokopop_b200.so and declares its signatures. Raises when the
+    library has not been built (python -m kokopop_b200.build)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is missing: build it with `python -m kokopop_b200.build`")
+    L = ctypes.CDLL(LIB_PATH)
+    vp = ctypes.c_void_p
+    L.kk_last_error.restype = ctypes.c_char_p
+    L.kk_ctx_create.argtypes = [ctypes.c_int, ctypes.POINTER(vp)]
+    L.kk_ctx_destroy.argtypes = [vp]
+    L.kk_ctx_destroy.restype = None
+    L.kk_weights_upload.argtypes = [vp, vp, ctypes.c_size_t]
+    L.kk_decoder_forward.argtypes = [vp, ctypes.c_int32, _i32p, _f32p, _f32p, _f32p, _f32p, _f32p]
+    L.kk_decoder_forward_device.argtypes = [vp, ctypes.c_int32, _i32p, vp, vp, vp, vp, vp, vp]
+    L.kk_generator_forward.argtypes = [vp, ctypes.c_int32, _i32p, _f32p, _f32p, _f32p, _f32p]
+    L.kk_istft.argtypes = [vp, ctypes.c_int64, _f32p, _f32p]
+    L.kk_profile_enable.argtypes = [vp, ctypes.c_int]
+    L.kk_profile_read.argtypes = [vp, ctypes.POINTER(Profile), ctypes.c_int]
+    _lib = L
+    return L
+
+
+def declared_symbols() -> List[str]:
+    """Every kk_* function declared in include/kokopop_b200.h."""
+    import re
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"\b(kk_[a-z0-9_]+)\s*\(", src)))
+
+
+def _ptr(a: Optional[np.ndarray], t=_f32p):
+    return None if a is None else a.ctypes.data_as(t)
+
+
+def _descs(weights) -> tuple:
+    items = list(weights.values())
+    arr = (TensorDesc * len(items))()
+    keep = []
+    for i, t in enumerate(items):
+        nm = t.name.encode()
+        data = np.ascontiguousarray(t.data)
+        keep += [nm, data]
+        arr[i].name = nm
+        arr[i].dtype = t.dtype
+        arr[i].n_dims = len(t.ne)
+        for d in range(4):
+            arr[i].ne[d] = t.ne[d] if d < len(t.ne) else 1
+        arr[i].data = data.ctypes.data
+    return arr, keep
+
+
+class Context:
+    """One kk_ctx: a CUDA device, its stream and the uploaded weights."""
+
+    def __init__(self, device: int = 0):
+        self.L = load_library()
+        h = ctypes.c_void_p()
+        self._check(self.L.kk_ctx_create(device, ctypes.byref(h)))
+        self.h = h
+        self.device = device
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.L.kk_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _check(self, rc: int):
+        if rc != KK_OK:
+            raise KKError(rc, self.L.kk_last_error().decode())
+
+    def upload(self, weights) -> None:
+        arr, keep = _descs(weights)
+        self._check(self.L.kk_weights_upload(self.h, ctypes.cast(arr, ctypes.c_void_p), len(arr)))
+        del keep
+
+    def decoder_forward(self, utts: Sequence) -> List[np.ndarray]:
+        """Decoder + generator + iSTFT for a ragged batch of workload.Utterance."""
+        from .workload import pack
+        n_frames, asr, f0, noise, style = pack(utts)
+        audio = np.zeros(600 * int(n_frames.sum()), np.float32)
+        self._check(self.L.kk_decoder_forward(self.h, len(utts), _ptr(n_frames, _i32p), _ptr(asr), _ptr(f0),
+                                              _ptr(noise), _ptr(style), _ptr(audio)))
+        out, o = [], 0
+        for t in n_frames:
+            out.append(audio[o:o + 600 * int(t)])
+            o += 600 * int(t)
+        return out
+
+    def decoder_forward_packed(self, n_frames, asr, f0, noise, style, audio) -> None:
+        """Host-buffer call on pre-packed arrays (the bench's end-to-end leg)."""
+        self._check(self.L.kk_decoder_forward(self.h, len(n_frames), _ptr(n_frames, _i32p), _ptr(asr), _ptr(f0),
+                                              _ptr(noise), _ptr(style), _ptr(audio)))
+
+    def decoder_forward_device(self, n_frames: np.ndarray, asr_ptr: int, f0_ptr: int, noise_ptr: int,
+                               style_ptr: int, audio_ptr: int, stream: int = 0) -> None:
+        n_frames = np.ascontiguousarray(n_frames, np.int32)
+        self._check(self.L.kk_decoder_forward_device(self.h, len(n_frames), _ptr(n_frames, _i32p), asr_ptr, f0_ptr,
+                                                     noise_ptr, style_ptr, audio_ptr, stream or None))
+
+    def generator_forward(self, decoders: Sequence[np.ndarray], f0s: Sequence[np.ndarray],
+                          styles: Sequence[np.ndarray]) -> List[np.ndarray]:
+        lens = np.array([d.shape[1] for d in decoders], np.int32)
+        dec = np.concatenate([np.ascontiguousarray(d, np.float32).reshape(-1) for d in decoders])
+        f0 = np.concatenate([np.asarray(f, np.float32) for f in f0s])
+        style = np.concatenate([np.asarray(s, np.float32)[:128] for s in styles])
+        audio = np.zeros(300 * int(lens.sum()), np.float32)
+        self._check(self.L.kk_generator_forward(self.h, len(lens), _ptr(lens, _i32p), _ptr(dec), _ptr(f0),
+                                                _ptr(style), _ptr(audio)))
+        out, o = [], 0
+        for t in lens:
+            out.append(audio[o:o + 300 * int(t)])
+            o += 300 * int(t)
+        return out
+
+    def profile_enable(self, on: bool = True) -> None:
+        self._check(self.L.kk_profile_enable(self.h, 1 if on else 0))
+
+    def profile_read(self, reset: bool = False) -> Dict[str, float]:
+        p = Profile()
+        self._check(self.L.kk_profile_read(self.h, ctypes.byref(p), 1 if reset else 0))
+        return {"launches": int(p.launches), "conv_launches": int(p.conv_launches),
+                "conv_ms": float(p.conv_ms), "conv_flop": float(p.conv_flop)}
+
+    def istft(self, post: np.ndarray) -> np.ndarray:
+        post = np.ascontiguousarray(post, np.float32)
+        n = post.shape[1]
+        audio = np.zeros(max(1, (n - 1) * 5), np.float32)
+        self._check(self.L.kk_istft(self.h, n, _ptr(post), _ptr(audio)))
+        return audio[: max(0, (n - 1) * 5)]

@@ -1,0 +1,978 @@
+// Host side of the B200 Kokoro-82M hot path: the context, the weight
+// registry, the packed ragged-batch plan, the decoder / generator
+// orchestration and the C ABI of include/kokopop_b200.h.
+//
+// The orchestration follows the reference's graph builders op for op:
+//   decoder   run_kokoro_generation_probe, src/arch/kokoro/kokoro.cpp:716-763
+//   block     adain_resblk1d,              src/arch/kokoro/graph_ops.cpp:996-1065
+//   generator ggml_generator,              src/arch/kokoro/audio_utils.cpp:594-1051
+//   resblock  graph_generator_resblock,    src/arch/kokoro/graph_ops.cpp:1071-1111
+//   3 branches graph_3branch_main_sum,     src/arch/kokoro/graph_ops.cpp:1300-1320
+// Errors follow src/kokopop.cpp:38-59: no exception leaves this file, every
+// failure becomes a status code plus a thread-local message.
+#include "../../include/kokopop_b200.h"
+#include "kk_kernels.h"
+#include "kk_host.h"
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+namespace {
+
+thread_local std::string g_last_error;
+
+constexpr float kInvSqrt2 = 0.7071067811865476f;  // KOKOPOP_INV_SQRT2
+constexpr int kDil[3] = {1, 3, 5};                // KOKOPOP_RESBLOCK_DILATIONS
+constexpr int kKs[3] = {3, 7, 11};                // KOKOPOP_RESBLOCK_KERNELS
+
+}  // namespace
+
+namespace kk {
+
+KKError::KKError(int c, const std::string &m) : std::runtime_error(m), code(c) {}
+
+void check_cuda(cudaError_t e, const char *what) {
+    if (e != cudaSuccess)
+        throw KKError(KK_ERROR_INFERENCE, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+void DevBuf::ensure(size_t b) {
+    if (b <= bytes) return;
+    if (p) cudaFree(p);
+    p = nullptr;
+    bytes = 0;
+    check_cuda(cudaMalloc(&p, b), "cudaMalloc workspace");
+    bytes = b;
+}
+
+void DevBuf::release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    bytes = 0;
+}
+
+float half_to_float(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    uint32_t exp = (h >> 10) & 0x1fu, man = h & 0x3ffu, bits;
+    if (exp == 0) {
+        if (man == 0) {
+            bits = sign;
+        } else {
+            exp = 127 - 15 + 1;
+            while ((man & 0x400u) == 0) {
+                man <<= 1;
+                exp--;
+            }
+            man &= 0x3ffu;
+            bits = sign | (exp << 23) | (man << 13);
+        }
+    } else if (exp == 31) {
+        bits = sign | 0x7f800000u | (man << 13);
+    } else {
+        bits = sign | ((exp + 127 - 15) << 23) | (man << 13);
+    }
+    float f;
+    std::memcpy(&f, &bits, 4);
+    return f;
+}
+
+}  // namespace kk
+
+using namespace kk;
+
+// ---------------------------------------------------------------------------
+// context
+// ---------------------------------------------------------------------------
+
+kk_ctx::~kk_ctx() {
+    for (auto &t : timed) {
+        cudaEventDestroy(t.a);
+        cudaEventDestroy(t.b);
+    }
+    for (auto e : event_pool) cudaEventDestroy(e);
+    for (auto &kv : w) cudaFree(kv.second.d);
+    for (auto &kv : ws) kv.second.release();
+    for (auto &b : convt_phase) b.release();
+    d_sites.release();
+    d_tables.release();
+    d_batch.release();
+    if (ev_inputs) cudaEventDestroy(ev_inputs);
+    if (ev_src) cudaEventDestroy(ev_src);
+    if (st2) cudaStreamDestroy(st2);
+    if (st) cudaStreamDestroy(st);
+}
+
+const DevTensor &kk_ctx::W(const std::string &name) const {
+    auto it = w.find(name);
+    if (it == w.end()) throw KKError(KK_ERROR_MODEL, "missing tensor: " + name);
+    return it->second;
+}
+
+const DevTensor *kk_ctx::Wopt(const std::string &name) const {
+    auto it = w.find(name);
+    return it == w.end() ? nullptr : &it->second;
+}
+
+cudaEvent_t kk_ctx::take_event() {
+    if (!event_pool.empty()) {
+        cudaEvent_t e = event_pool.back();
+        event_pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e;
+    check_cuda(cudaEventCreate(&e), "cudaEventCreate");
+    return e;
+}
+
+float *kk_ctx::buf(const char *name, size_t floats) {
+    DevBuf &b = ws[name];
+    b.ensure(floats * sizeof(float));
+    return (float *)b.p;
+}
+
+// Host tables, computed with the C library exactly as the reference does.
+static void make_tables(StftTables &st, IstftTables &is) {
+    for (int n = 0; n < kStftN; ++n) {
+        // hann_window_20 (audio_utils.cpp:36-45) and the iSTFT plan's window
+        // (src/audio/istft.cpp:236-242): the double expression, rounded.
+        const float wv = (float)(0.5 - 0.5 * std::cos(2.0 * M_PI * (double)n / (double)kStftN));
+        st.window[n] = wv;
+        is.window[n] = wv;
+        is.window_sq[n] = wv * wv;
+        // StftTwiddles (audio_utils.cpp:47-64)
+        for (int k = 0; k < kBins; ++k) {
+            const float a = (float)(2.0 * M_PI * (double)(float)(k * n) / (double)(float)kStftN);
+            st.c[n][k] = std::cos(a);
+            st.s[n][k] = std::sin(a);
+        }
+    }
+    // DirectDft tables (src/audio/istft.cpp:244-254)
+    for (int k = 0; k < kBins; ++k)
+        for (int i = 0; i < kStftN; ++i) {
+            const float a = (float)(2.0 * M_PI * (double)(k * i) / (double)kStftN);
+            is.c[k][i] = std::cos(a);
+            is.s[k][i] = std::sin(a);
+        }
+}
+
+static std::vector<std::string> adain_site_prefixes() {
+    std::vector<std::string> v;
+    const std::string d = "kokopop.decoder.";
+    v.push_back(d + "encode.norm1");
+    v.push_back(d + "encode.norm2");
+    for (int i = 0; i < 4; ++i) {
+        v.push_back(d + "decode." + std::to_string(i) + ".norm1");
+        v.push_back(d + "decode." + std::to_string(i) + ".norm2");
+    }
+    std::vector<std::string> blocks = {d + "generator.noise_res.0", d + "generator.noise_res.1"};
+    for (int b = 0; b < 6; ++b) blocks.push_back(d + "generator.resblocks." + std::to_string(b));
+    for (auto &p : blocks)
+        for (int i = 0; i < 3; ++i) {
+            v.push_back(p + ".adain1." + std::to_string(i));
+            v.push_back(p + ".adain2." + std::to_string(i));
+        }
+    return v;
+}
+
+// Builds everything derived from the raw weights: ConvTranspose phase
+// weights, the AdaIN site table, the harmonic-source constants and tables.
+void kk_ctx::derive() {
+    generator_ready = decoder_ready = false;
+    missing.clear();
+    auto need = [&](const std::string &n) {
+        if (!Wopt(n) && missing.empty()) missing = n;
+        return Wopt(n) != nullptr;
+    };
+    // ConvTranspose ups.s as s phase convolutions with 2 taps each:
+    // phase r, tap 0 reads t_in = q - 1 with W[r + s], tap 1 reads q with W[r].
+    static const int strides[2] = {10, 6};
+    bool ok = true;
+    for (int s = 0; s < 2; ++s) {
+        const std::string nm = "kokopop.decoder.generator.ups." + std::to_string(s) + ".weight";
+        if (!need(nm)) {
+            ok = false;
+            continue;
+        }
+        const DevTensor &t = W(nm);
+        const int K = (int)t.ne[0], OC = (int)t.ne[1], IC = (int)t.ne[2], S = strides[s];
+        if (K > 2 * S) throw KKError(KK_ERROR_MODEL, "ConvTranspose kernel longer than 2 strides: " + nm);
+        std::vector<float> h((size_t)t.n), ph((size_t)S * OC * IC * 2, 0.f);
+        check_cuda(cudaMemcpy(h.data(), t.d, h.size() * 4, cudaMemcpyDeviceToHost), "read ups weight");
+        for (int r = 0; r < S; ++r)
+            for (int oc = 0; oc < OC; ++oc)
+                for (int ic = 0; ic < IC; ++ic) {
+                    const size_t o = (((size_t)r * OC + oc) * IC + ic) * 2;
+                    const size_t src = ((size_t)ic * OC + oc) * K;
+                    ph[o + 0] = (r + S < K) ? h[src + r + S] : 0.f;
+                    ph[o + 1] = (r < K) ? h[src + r] : 0.f;
+                }
+        convt_phase[s].ensure(ph.size() * 4);
+        check_cuda(cudaMemcpy(convt_phase[s].p, ph.data(), ph.size() * 4, cudaMemcpyHostToDevice),
+                   "upload phase weights");
+        convt_f16[s] = t.f16;
+    }
+    // AdaIN sites
+    sites.clear();
+    site_total_C = 0;
+    for (const auto &p : adain_site_prefixes()) {
+        const DevTensor *gw = Wopt(p + ".fc.gamma.weight"), *gb = Wopt(p + ".fc.gamma.bias");
+        const DevTensor *bw = Wopt(p + ".fc.beta.weight"), *bb = Wopt(p + ".fc.beta.bias");
+        if (!gw || !gb || !bw || !bb || !Wopt(p + ".norm.weight") || !Wopt(p + ".norm.bias")) {
+            if (missing.empty()) missing = p + ".fc/norm";
+            ok = false;
+            continue;
+        }
+        SiteInfo si;
+        si.prefix = p;
+        si.C = (int)gw->ne[1];
+        si.f16 = gw->f16;
+        si.gw = gw->d;
+        si.gb = gb->d;
+        si.bw = bw->d;
+        si.bb = bb->d;
+        si.off = site_total_C;
+        site_total_C += si.C;
+        site_index[p] = (int)sites.size();
+        sites.push_back(si);
+    }
+    // harmonic source constants (audio_utils.cpp:145-176)
+    const std::string mw_n = "kokopop.decoder.generator.m_source.l_linear.weight";
+    const std::string mb_n = "kokopop.decoder.generator.m_source.l_linear.bias";
+    if (need(mw_n) && need(mb_n)) {
+        const DevTensor &mw = W(mw_n), &mb = W(mb_n);
+        if (mw.host.size() < (size_t)kHarmonics || mb.host.empty())
+            throw KKError(KK_ERROR_MODEL, "invalid harmonic source merge weight size");
+        for (int h = 0; h < kHarmonics; ++h) sine.mw_scaled[h] = mw.host[h] * 0.1f;
+        sine.mb = mb.host[0];
+        sine.unvoiced = std::tanh(sine.mb);
+    } else {
+        ok = false;
+    }
+    // remaining generator / decoder tensors
+    for (const char *n : {"kokopop.decoder.generator.conv_post.weight", "kokopop.decoder.generator.conv_post.bias",
+                          "kokopop.decoder.generator.noise_convs.0.weight", "kokopop.decoder.generator.noise_convs.1.weight"})
+        ok = need(n) && ok;
+    generator_ready = ok;
+    bool dok = ok;
+    for (const char *n : {"kokopop.decoder.F0_conv.weight", "kokopop.decoder.N_conv.weight",
+                          "kokopop.decoder.asr_res.0.weight", "kokopop.decoder.encode.conv1.weight",
+                          "kokopop.decoder.decode.3.pool.weight"})
+        dok = need(n) && dok;
+    decoder_ready = dok;
+    // tables
+    StftTables stt;
+    IstftTables ist;
+    make_tables(stt, ist);
+    d_tables.ensure(sizeof(StftTables) + sizeof(IstftTables));
+    check_cuda(cudaMemcpy(d_tables.p, &stt, sizeof stt, cudaMemcpyHostToDevice), "upload tables");
+    check_cuda(cudaMemcpy((char *)d_tables.p + sizeof(StftTables), &ist, sizeof ist, cudaMemcpyHostToDevice),
+               "upload tables");
+}
+
+// ---------------------------------------------------------------------------
+// packed ragged-batch plan
+// ---------------------------------------------------------------------------
+
+Plan kk::make_plan(const int32_t *lens, int n) {
+    Plan P;
+    P.n = n;
+    P.T.assign(lens, lens + n);
+    P.off.resize(n);
+    P.cum.resize(n);
+    int64_t off = 4, cum = 0;
+    P.maxT = 0;
+    for (int u = 0; u < n; ++u) {
+        if (lens[u] < 1 || lens[u] > kMaxFrames)
+            throw KKError(KK_ERROR_INVALID_ARGUMENT, "utterance length out of range [1, 8192]");
+        P.off[u] = off;
+        P.cum[u] = cum;
+        off += ((int64_t)lens[u] + 4 + 3) / 4 * 4;
+        cum += lens[u];
+        if (lens[u] > P.maxT) P.maxT = lens[u];
+    }
+    P.S = off;
+    P.total = cum;
+    return P;
+}
+
+// ---------------------------------------------------------------------------
+// the forward pass
+// ---------------------------------------------------------------------------
+
+namespace {
+
+struct Runner {
+    kk_ctx &c;
+    const Plan &P;
+    cudaStream_t st;
+    Batch B{};
+    const int64_t *d_cum = nullptr;
+    float2 *ms = nullptr;
+    float *gbase = nullptr, *bbase = nullptr;
+
+    Runner(kk_ctx &ctx, const Plan &plan, cudaStream_t s) : c(ctx), P(plan), st(s) {}
+
+    int64_t R(int m) const { return P.R(m); }
+
+    void setup_batch() {
+        const size_t n = (size_t)P.n;
+        c.h_batch.resize(n * 5 + 8);
+        int32_t *hT = (int32_t *)c.h_batch.data();
+        int64_t *hoff = c.h_batch.data() + (n + 1) / 2 + 1;
+        int64_t *hcum = hoff + n;
+        for (size_t u = 0; u < n; ++u) {
+            hT[u] = P.T[u];
+            hoff[u] = P.off[u];
+            hcum[u] = P.cum[u];
+        }
+        const size_t bytes = (size_t)((char *)(hcum + n) - (char *)hT);
+        c.d_batch.ensure(bytes);
+        check_cuda(cudaMemcpyAsync(c.d_batch.p, hT, bytes, cudaMemcpyHostToDevice, st), "upload batch");
+        char *base = (char *)c.d_batch.p;
+        B.n = P.n;
+        B.T = (const int32_t *)base;
+        B.offT = (const int64_t *)(base + ((char *)hoff - (char *)hT));
+        d_cum = (const int64_t *)(base + ((char *)hcum - (char *)hT));
+    }
+
+    void setup_adain(const float *style_dev) {
+        const size_t n = (size_t)P.n;
+        gbase = c.buf("gamma", n * (size_t)c.site_total_C);
+        bbase = c.buf("beta", n * (size_t)c.site_total_C);
+        c.h_sites.resize(c.sites.size());
+        for (size_t i = 0; i < c.sites.size(); ++i) {
+            const SiteInfo &s = c.sites[i];
+            AdainSite &a = c.h_sites[i];
+            a.gw = s.gw;
+            a.gb = s.gb;
+            a.bw = s.bw;
+            a.bb = s.bb;
+            a.C = s.C;
+            a.f16 = s.f16;
+            a.gamma = gbase + n * (size_t)s.off;
+            a.beta = bbase + n * (size_t)s.off;
+        }
+        c.d_sites.ensure(c.h_sites.size() * sizeof(AdainSite));
+        check_cuda(cudaMemcpyAsync(c.d_sites.p, c.h_sites.data(), c.h_sites.size() * sizeof(AdainSite),
+                                   cudaMemcpyHostToDevice, st),
+                   "upload adain sites");
+        adain_affine((const AdainSite *)c.d_sites.p, (int)c.h_sites.size(), style_dev, P.n, st);
+        ++c.n_launches;
+        ms = (float2 *)c.buf("stats", n * 1090 * 2);
+    }
+
+    const AdainSite &site(const std::string &prefix) {
+        auto it = c.site_index.find(prefix);
+        if (it == c.site_index.end()) throw KKError(KK_ERROR_MODEL, "missing AdaIN weights: " + prefix);
+        return c.h_sites[it->second];
+    }
+
+    struct Epi {
+        const DevTensor *bias = nullptr;
+        const float *resid = nullptr;
+        int64_t R_resid = 0;
+        int resid_half = 0;
+        float scale1 = 1.f;
+        int accum = 0;
+        float scale2 = 1.f;
+        int64_t omul = 1, oadd = 0;
+        int64_t valid = 0;  // valid output positions (algorithmic FLOP count)
+    };
+
+    // sum over utterances of the length at level m (+ extra per utterance)
+    int64_t sum_len(int m, int extra) const { return (int64_t)m * P.total + (int64_t)extra * P.n; }
+
+    // y = conv(w, in); 2-D ggml weight [IC*K, OC] (or the 3-D phase tensor).
+    void conv(const float *w, bool f16, int OC, const float *in, int64_t R_in, int IC, int K, int s, int p,
+              int d, float *out, int64_t R_out, int64_t n_pos, const Epi &e) {
+        ConvArgs a{};
+        a.in = in;
+        a.R_in = R_in;
+        a.IC = IC;
+        a.w = w;
+        a.OC = OC;
+        a.K = K;
+        a.s = s;
+        a.p = p;
+        a.d = d;
+        a.out = out;
+        a.R_out = R_out;
+        a.n_pos = n_pos;
+        a.omul = e.omul;
+        a.oadd = e.oadd;
+        a.bias = e.bias ? e.bias->d : nullptr;
+        a.resid = e.resid;
+        a.R_resid = e.R_resid;
+        a.resid_half = e.resid_half;
+        a.scale1 = e.scale1;
+        a.accum = e.accum;
+        a.scale2 = e.scale2;
+        a.round16 = f16 ? 1 : 0;
+        cudaEvent_t e0 = nullptr, e1 = nullptr;
+        if (c.profiling) {
+            e0 = c.take_event();
+            e1 = c.take_event();
+            check_cuda(cudaEventRecord(e0, st), "event");
+        }
+        conv_simt(a, st);
+        ++c.n_launches;
+        if (c.profiling) {
+            check_cuda(cudaEventRecord(e1, st), "event");
+            c.timed.push_back({e0, e1, 2.0 * OC * (double)IC * K * (double)e.valid});
+        }
+    }
+
+    void conv_w(const std::string &wname, const std::string &bname, const float *in, int64_t R_in, int IC,
+                int K, int s, int p, int d, float *out, int64_t R_out, int64_t n_pos, Epi e, int64_t valid) {
+        e.valid = valid;
+        const DevTensor &w = c.W(wname);
+        const int OC = (int)(w.ne[2] > 1 ? w.ne[2] : w.ne[1]);
+        if (w.n != (int64_t)OC * IC * K) throw KKError(KK_ERROR_MODEL, "conv weight shape mismatch: " + wname);
+        if (!bname.empty()) e.bias = &c.W(bname);
+        conv(w.d, w.f16, OC, in, R_in, IC, K, s, p, d, out, R_out, n_pos, e);
+    }
+
+    // stats + AdaIN + activation into the operand buffer
+    void adain_act(const std::string &prefix, const float *x, float *y, int64_t Rm, int C, int m, int extra,
+                   int act, float slope, const std::string &alpha) {
+        const AdainSite &s = site(prefix);
+        if (s.C != C) throw KKError(KK_ERROR_MODEL, "AdaIN channel mismatch: " + prefix);
+        stats(x, Rm, C, m, extra, B, ms, st);
+        ++c.n_launches;
+        PrologueArgs a{};
+        a.norm = 1;
+        a.ms = ms;
+        a.norm_w = c.W(prefix + ".norm.weight").d;
+        a.norm_b = c.W(prefix + ".norm.bias").d;
+        a.gamma = s.gamma;
+        a.beta = s.beta;
+        a.act = act;
+        a.slope = slope;
+        a.alpha = alpha.empty() ? nullptr : c.W(alpha).d;
+        a.round16 = 0;
+        prologue(x, y, Rm, C, m, extra, B, m * P.maxT + extra, a, st);
+        ++c.n_launches;
+    }
+
+    void act_only(const float *x, float *y, int64_t Rm, int C, int m, int extra, float slope) {
+        PrologueArgs a{};
+        a.norm = 0;
+        a.act = ACT_LEAKY;
+        a.slope = slope;
+        prologue(x, y, Rm, C, m, extra, B, m * P.maxT + extra, a, st);
+        ++c.n_launches;
+    }
+
+    // adain_resblk1d (graph_ops.cpp:996-1065) on the T level.
+    void adain_resblk(const std::string &pf, const float *x, int Cin, bool up, float *out) {
+        const int64_t R1 = R(1), R2 = R(2);
+        const DevTensor &c1 = c.W(pf + ".conv1.weight");
+        const int Cout = (int)c1.ne[1];
+        float *opT = c.buf("opT", 1090 * (size_t)R1);
+        adain_act(pf + ".norm1", x, opT, R1, Cin, 1, 0, ACT_LEAKY, 0.2f, "");
+        const float *c1_in = opT;
+        int64_t Rc = R1;
+        int m = 1;
+        float *op = opT, *tmp = c.buf("tmpT", 1024 * (size_t)R1);
+        if (up) {
+            float *op2 = c.buf("op2", 1090 * (size_t)R2);
+            const DevTensor &pw = c.W(pf + ".pool.weight"), &pb = c.W(pf + ".pool.bias");
+            if (pw.ne[0] != 3 || pw.ne[1] != 1 || pw.ne[2] != Cin)
+                throw KKError(KK_ERROR_MODEL, "invalid depthwise upsample pool shape: " + pf);
+            pool_up(opT, op2, R1, R2, Cin, pw.d, pb.d, B, P.maxT, 0, st);
+        ++c.n_launches;
+            c1_in = op2;
+            Rc = R2;
+            m = 2;
+            op = op2;
+            tmp = c.buf("tmp2", 512 * (size_t)R2);
+        }
+        conv_w(pf + ".conv1.weight", pf + ".conv1.bias", c1_in, Rc, Cin, 3, 1, 1, 1, tmp, Rc, Rc, Epi{}, sum_len(m, 0));
+        adain_act(pf + ".norm2", tmp, op, Rc, Cout, m, 0, ACT_LEAKY, 0.2f, "");
+        Epi e;
+        e.scale1 = kInvSqrt2;
+        e.resid_half = up ? 1 : 0;
+        if (c.Wopt(pf + ".conv1x1.weight")) {
+            float *sc = c.buf("scT", 1024 * (size_t)R1);
+            conv_w(pf + ".conv1x1.weight", "", x, R1, Cin, 1, 1, 0, 1, sc, R1, R1, Epi{}, sum_len(1, 0));
+            e.resid = sc;
+        } else {
+            if (Cin != Cout) throw KKError(KK_ERROR_MODEL, "missing conv1x1 for " + pf);
+            e.resid = x;
+        }
+        e.R_resid = R1;
+        conv_w(pf + ".conv2.weight", pf + ".conv2.bias", op, Rc, Cout, 3, 1, 1, 1, out, Rc, Rc, e, sum_len(m, 0));
+    }
+
+    // graph_generator_resblock: x_in -> (3 iterations) -> wb, the last
+    // iteration writing final_out (accumulating / scaling) when given.
+    void gen_resblock(const std::string &pf, int K, const float *x_in, float *wb, float *final_out, int accum,
+                      float scale2, int C, int m, int extra, float *op, float *tmp) {
+        const int64_t Rm = R(m);
+        const float *cur = x_in;
+        for (int i = 0; i < 3; ++i) {
+            const std::string is = std::to_string(i);
+            const int d = kDil[i];
+            adain_act(pf + ".adain1." + is, cur, op, Rm, C, m, extra, ACT_SNAKE, 0.f, pf + ".alpha1." + is);
+            conv_w(pf + ".convs1." + is + ".weight", pf + ".convs1." + is + ".bias", op, Rm, C, K, 1,
+                   (K * d - d) / 2, d, tmp, Rm, Rm, Epi{}, sum_len(m, extra));
+            adain_act(pf + ".adain2." + is, tmp, op, Rm, C, m, extra, ACT_SNAKE, 0.f, pf + ".alpha2." + is);
+            Epi e;
+            e.resid = cur;
+            e.R_resid = Rm;
+            float *o = wb;
+            if (i == 2 && final_out) {
+                o = final_out;
+                e.accum = accum;
+                e.scale2 = scale2;
+            }
+            conv_w(pf + ".convs2." + is + ".weight", pf + ".convs2." + is + ".bias", op, Rm, C, K, 1, K / 2, 1, o,
+                   Rm, Rm, e, sum_len(m, extra));
+            cur = wb;
+        }
+    }
+
+    // ggml_generator (audio_utils.cpp:594-1051) with the input at level gm.
+    void generator(int gm, const float *x_in, float *har, float *audio) {
+        static const struct {
+            int kernel, up_stride, up_padding, noise_stride, noise_padding, noise_kernel;
+        } sp[2] = {{7, 10, 5, 6, 3, 12}, {11, 6, 3, 1, 0, 1}};
+        const int mlev[2] = {10 * gm, 60 * gm};
+        const int extra[2] = {0, 1};
+        const int64_t R_har = R(60 * gm);
+        const float *x = x_in;
+        int C = 512, m_prev = gm;
+        const std::string g = "kokopop.decoder.generator.";
+        for (int s = 0; s < 2; ++s) {
+            const int m = mlev[s];
+            const int64_t Rm = R(m);
+            const std::string ss = std::to_string(s);
+            const DevTensor &ncw = c.W(g + "noise_convs." + ss + ".weight");
+            const int Cs = (int)ncw.ne[1];
+            const std::string lv = std::to_string(s);
+            float *xs = c.buf(("xs" + lv).c_str(), (size_t)Cs * Rm);
+            float *xst = c.buf(("xst" + lv).c_str(), (size_t)Cs * Rm);
+            float *acc = c.buf(("acc" + lv).c_str(), (size_t)Cs * Rm);
+            float *xb = c.buf(("xb" + lv).c_str(), (size_t)Cs * Rm);
+            float *tmp = c.buf(("tmp" + lv).c_str(), (size_t)Cs * Rm);
+            float *op = c.buf(("op" + lv).c_str(), (size_t)Cs * Rm);
+            // noise branch: noise_convs + noise_res (audio_utils.cpp:714-731)
+            conv_w(g + "noise_convs." + ss + ".weight", g + "noise_convs." + ss + ".bias", har, R_har, 22,
+                   sp[s].noise_kernel, sp[s].noise_stride, sp[s].noise_padding, 1, xs, Rm, Rm, Epi{},
+                   sum_len(m, extra[s]));
+            gen_resblock(g + "noise_res." + ss, sp[s].kernel, xs, xs, nullptr, 0, 1.f, Cs, m, extra[s], op, tmp);
+            // LeakyReLU(0.1) then ConvTranspose as phase convolutions,
+            // + bias, [reflect pad], + noise branch (audio_utils.cpp:687-760)
+            const int64_t Rp = R(m_prev);
+            float *opp = s == 0 ? c.buf("op2", 1090 * (size_t)R(gm)) : c.buf("op0", (size_t)256 * R(10 * gm));
+            act_only(x, opp, Rp, C, m_prev, 0, 0.1f);
+            const DevTensor &uw = c.W(g + "ups." + ss + ".weight");
+            const DevTensor &ub = c.W(g + "ups." + ss + ".bias");
+            if ((int)uw.ne[1] != Cs || (int)uw.ne[2] != C) throw KKError(KK_ERROR_MODEL, "ups shape mismatch");
+            const int S = sp[s].up_stride, crop = sp[s].up_padding, pad = s == 1 ? 1 : 0;
+            for (int r = 0; r < S; ++r) {
+                Epi e;
+                e.bias = &ub;
+                e.resid = xs;
+                e.R_resid = Rm;
+                e.omul = S;
+                e.oadd = r - crop + pad;
+                e.valid = sum_len(m_prev, 0);
+                conv((const float *)c.convt_phase[s].p + (size_t)r * Cs * C * 2, c.convt_f16[s], Cs, opp, Rp, C, 2, 1,
+                     1, 1, xst, Rm, Rp, e);
+            }
+            if (pad) {
+                ConvTRow0Args a{};
+                a.in = opp;
+                a.R_in = Rp;
+                a.IC = C;
+                a.m_in = m_prev;
+                a.w = uw.d;
+                a.OC = Cs;
+                a.K = (int)uw.ne[0];
+                a.crop = crop;
+                a.m_out = m;
+                a.bias = ub.d;
+                a.add = xs;
+                a.out = xst;
+                a.R_out = Rm;
+                a.round16 = uw.f16 ? 1 : 0;
+                convt_row0(a, B, st);
+        ++c.n_launches;
+            }
+            // three main resblocks, averaged (graph_ops.cpp:1300-1320)
+            for (int k = 0; k < 3; ++k) {
+                const std::string pf = g + "resblocks." + std::to_string(s * 3 + k);
+                float *wb = k == 0 ? acc : xb;
+                gen_resblock(pf, kKs[k], xst, wb, acc, k == 0 ? 0 : 1, k == 2 ? 1.0f / 3.0f : 1.f, Cs, m, extra[s],
+                             op, tmp);
+            }
+            x = acc;
+            C = Cs;
+            m_prev = m;
+        }
+        // LeakyReLU(0.01) -> conv_post -> iSTFT (audio_utils.cpp:814-831, :1043)
+        const int m = mlev[1];
+        const int64_t Rm = R(m);
+        float *op = c.buf("op1", (size_t)128 * Rm);
+        act_only(x, op, Rm, C, m, 1, 0.01f);
+        float *post = c.buf("post", (size_t)22 * Rm);
+        conv_w(g + "conv_post.weight", g + "conv_post.bias", op, Rm, C, 7, 1, 3, 1, post, Rm, Rm, Epi{},
+               sum_len(m, 1));
+        const IstftTables *it = (const IstftTables *)((char *)c.d_tables.p + sizeof(StftTables));
+        istft(post, Rm, 60 * gm, audio, B, d_cum, it, P.maxT, st);
+        ++c.n_launches;
+    }
+
+    // memset every operand buffer whose gaps must read as zero
+    void zero_operands(int gm, bool decoder) {
+        auto z = [&](const char *n, size_t floats) {
+            float *p = c.buf(n, floats);
+            check_cuda(cudaMemsetAsync(p, 0, floats * sizeof(float), st), "memset");
+        };
+        if (decoder) z("opT", 1090 * (size_t)R(1));
+        z("op2", 1090 * (size_t)R(gm));
+        z("op0", 256 * (size_t)R(10 * gm));
+        z("op1", 128 * (size_t)R(60 * gm));
+    }
+
+    // harmonic source + STFT on the side stream, from the packed F0 (level mf)
+    float *source_and_har(const float *f0p, int mf) {
+        const int64_t Rh = R(60 * mf);
+        float *har = c.buf("har", (size_t)22 * Rh);
+        float *src = c.buf("source", (size_t)kUpsample * mf * (size_t)P.total + 1);
+        check_cuda(cudaEventRecord(c.ev_inputs, st), "event");
+        check_cuda(cudaStreamWaitEvent(c.st2, c.ev_inputs, 0), "wait");
+        check_cuda(cudaMemsetAsync(har, 0, (size_t)22 * Rh * sizeof(float), c.st2), "memset har");
+        sinegen(f0p, mf, src, B, d_cum, c.sine, c.st2);
+        ++c.n_launches;
+        const StftTables *tab = (const StftTables *)c.d_tables.p;
+        stft(src, har, Rh, mf, B, d_cum, tab, P.maxT, c.st2);
+        ++c.n_launches;
+        check_cuda(cudaEventRecord(c.ev_src, c.st2), "event");
+        return har;
+    }
+
+    // decoder encode / decode (kokoro.cpp:716-763) then the generator.
+    void decoder_forward(const float *asr, const float *f0, const float *noise, const float *style, float *audio) {
+        setup_batch();
+        const int64_t R1 = R(1), R2 = R(2);
+        float *Xenc = c.buf("Xenc", 514 * (size_t)R1);
+        float *Xdec = c.buf("Xdec", 1090 * (size_t)R1);
+        float *f0p = c.buf("f0p", (size_t)R2);
+        float *np = c.buf("np", (size_t)R2);
+        check_cuda(cudaMemsetAsync(f0p, 0, (size_t)R2 * 4, st), "memset");
+        check_cuda(cudaMemsetAsync(np, 0, (size_t)R2 * 4, st), "memset");
+        zero_operands(2, true);
+        scatter(asr, Xenc, R1, 512, 1, 0, B, d_cum, P.maxT, st);
+        ++c.n_launches;
+        scatter(f0, f0p, R2, 1, 2, 0, B, d_cum, 2 * P.maxT, st);
+        ++c.n_launches;
+        scatter(noise, np, R2, 1, 2, 0, B, d_cum, 2 * P.maxT, st);
+        ++c.n_launches;
+        float *har = source_and_har(f0p, 2);
+        setup_adain(style);
+        const std::string d = "kokopop.decoder.";
+        const DevTensor &f0w = c.W(d + "F0_conv.weight"), &f0b = c.W(d + "F0_conv.bias");
+        const DevTensor &nw = c.W(d + "N_conv.weight"), &nb = c.W(d + "N_conv.bias");
+        f0n_conv(f0p, R2, Xenc + 512 * R1, Xdec + 1088 * R1, R1, f0w.d, f0b.d, B, P.maxT, st);
+        ++c.n_launches;
+        f0n_conv(np, R2, Xenc + 513 * R1, Xdec + 1089 * R1, R1, nw.d, nb.d, B, P.maxT, st);
+        ++c.n_launches;
+        conv_w(d + "asr_res.0.weight", d + "asr_res.0.bias", Xenc, R1, 512, 1, 1, 0, 1, Xdec + 1024 * R1, R1, R1,
+               Epi{}, sum_len(1, 0));
+        adain_resblk(d + "encode", Xenc, 514, false, Xdec);
+        for (int i = 0; i < 3; ++i) adain_resblk(d + "decode." + std::to_string(i), Xdec, 1090, false, Xdec);
+        float *dec = c.buf("dec_out", 512 * (size_t)R2);
+        adain_resblk(d + "decode.3", Xdec, 1090, true, dec);
+        check_cuda(cudaStreamWaitEvent(st, c.ev_src, 0), "wait source");
+        generator(2, dec, har, audio);
+    }
+
+    // ggml_generator seam: decoder output given per utterance.
+    void generator_forward(const float *decoder, const float *f0, const float *style, float *audio) {
+        setup_batch();
+        const int64_t R1 = R(1);
+        float *dec = c.buf("dec_in", 512 * (size_t)R1);
+        float *f0p = c.buf("f0p1", (size_t)R1);
+        check_cuda(cudaMemsetAsync(f0p, 0, (size_t)R1 * 4, st), "memset");
+        zero_operands(1, false);
+        scatter(decoder, dec, R1, 512, 1, 0, B, d_cum, P.maxT, st);
+        ++c.n_launches;
+        scatter(f0, f0p, R1, 1, 1, 0, B, d_cum, P.maxT, st);
+        ++c.n_launches;
+        float *har = source_and_har(f0p, 1);
+        setup_adain(style);
+        check_cuda(cudaStreamWaitEvent(st, c.ev_src, 0), "wait source");
+        generator(1, dec, har, audio);
+    }
+};
+
+template <typename F>
+int guarded(F &&f) noexcept {
+    try {
+        return f();
+    } catch (const KKError &e) {
+        g_last_error = e.what();
+        return e.code;
+    } catch (const std::exception &e) {
+        g_last_error = e.what();
+        return KK_ERROR_INFERENCE;
+    } catch (...) {
+        g_last_error = "unknown C++ exception";
+        return KK_ERROR_INFERENCE;
+    }
+}
+
+void use_device(kk_ctx *ctx) { check_cuda(cudaSetDevice(ctx->device), "cudaSetDevice"); }
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+
+extern "C" {
+
+const char *kk_last_error(void) { return g_last_error.c_str(); }
+
+int kk_ctx_create(int device, kk_ctx **out) {
+    return guarded([&] {
+        if (!out) throw KKError(KK_ERROR_INVALID_ARGUMENT, "out is null");
+        *out = nullptr;
+        int n = 0;
+        check_cuda(cudaGetDeviceCount(&n), "cudaGetDeviceCount");
+        if (device < 0 || device >= n) throw KKError(KK_ERROR_INVALID_ARGUMENT, "CUDA device out of range");
+        cudaDeviceProp prop;
+        check_cuda(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+        if (prop.major != 10)
+            throw KKError(KK_ERROR_INVALID_ARGUMENT, std::string("device is not sm_100 (B200): ") + prop.name);
+        std::unique_ptr<kk_ctx> c(new kk_ctx());
+        c->device = device;
+        check_cuda(cudaSetDevice(device), "cudaSetDevice");
+        check_cuda(cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking), "stream");
+        check_cuda(cudaStreamCreateWithFlags(&c->st2, cudaStreamNonBlocking), "stream");
+        check_cuda(cudaEventCreateWithFlags(&c->ev_inputs, cudaEventDisableTiming), "event");
+        check_cuda(cudaEventCreateWithFlags(&c->ev_src, cudaEventDisableTiming), "event");
+        check_cuda(conv_simt_init(), "conv init");
+        *out = c.release();
+        return KK_OK;
+    });
+}
+
+void kk_ctx_destroy(kk_ctx *ctx) {
+    if (!ctx) return;
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->st);
+    cudaStreamSynchronize(ctx->st2);
+    delete ctx;
+}
+
+int kk_weights_upload(kk_ctx *ctx, const kk_tensor_desc *descs, size_t n) {
+    return guarded([&] {
+        if (!ctx || (!descs && n)) throw KKError(KK_ERROR_INVALID_ARGUMENT, "null argument");
+        use_device(ctx);
+        check_cuda(cudaStreamSynchronize(ctx->st), "sync");
+        std::vector<float> tmp;
+        for (size_t i = 0; i < n; ++i) {
+            const kk_tensor_desc &d = descs[i];
+            if (!d.name || !d.data) throw KKError(KK_ERROR_INVALID_ARGUMENT, "tensor without name or data");
+            if (d.dtype != KK_DTYPE_F32 && d.dtype != KK_DTYPE_F16)
+                throw KKError(KK_ERROR_MODEL, std::string("unsupported tensor type for ") + d.name);
+            if (d.n_dims < 1 || d.n_dims > 4) throw KKError(KK_ERROR_MODEL, std::string("bad rank: ") + d.name);
+            DevTensor t;
+            int64_t cnt = 1;
+            for (int k = 0; k < 4; ++k) {
+                t.ne[k] = k < d.n_dims ? d.ne[k] : 1;
+                if (t.ne[k] < 1) throw KKError(KK_ERROR_MODEL, std::string("bad shape: ") + d.name);
+                cnt *= t.ne[k];
+            }
+            t.n = cnt;
+            t.f16 = d.dtype == KK_DTYPE_F16;
+            tmp.resize((size_t)cnt);
+            if (t.f16) {
+                const uint16_t *s = (const uint16_t *)d.data;
+                for (int64_t j = 0; j < cnt; ++j) tmp[j] = half_to_float(s[j]);
+            } else {
+                std::memcpy(tmp.data(), d.data, (size_t)cnt * 4);
+            }
+            if (cnt <= 4096) t.host = tmp;
+            auto it = ctx->w.find(d.name);
+            if (it != ctx->w.end()) {
+                cudaFree(it->second.d);
+                ctx->w.erase(it);
+            }
+            check_cuda(cudaMalloc(&t.d, (size_t)cnt * 4), "cudaMalloc weight");
+            check_cuda(cudaMemcpy(t.d, tmp.data(), (size_t)cnt * 4, cudaMemcpyHostToDevice), "upload weight");
+            ctx->w.emplace(d.name, std::move(t));
+        }
+        ctx->derive();
+        return KK_OK;
+    });
+}
+
+static void check_ready(kk_ctx *ctx, bool decoder) {
+    if (decoder ? !ctx->decoder_ready : !ctx->generator_ready)
+        throw KKError(KK_ERROR_MODEL, "weights incomplete, first missing: " + ctx->missing);
+}
+
+int kk_decoder_forward_device(kk_ctx *ctx, int32_t n_utts, const int32_t *n_frames, const float *asr,
+                              const float *f0, const float *noise, const float *style, float *audio,
+                              void *stream) {
+    return guarded([&] {
+        if (!ctx || n_utts < 0 || (n_utts && (!n_frames || !asr || !f0 || !noise || !style || !audio)))
+            throw KKError(KK_ERROR_INVALID_ARGUMENT, "null argument");
+        if (n_utts == 0) return KK_OK;
+        use_device(ctx);
+        check_ready(ctx, true);
+        const Plan P = make_plan(n_frames, n_utts);
+        cudaStream_t st = stream ? (cudaStream_t)stream : ctx->st;
+        Runner r(*ctx, P, st);
+        r.decoder_forward(asr, f0, noise, style, audio);
+        check_cuda(cudaGetLastError(), "kernel launch");
+        return KK_OK;
+    });
+}
+
+int kk_decoder_forward(kk_ctx *ctx, int32_t n_utts, const int32_t *n_frames, const float *asr, const float *f0,
+                       const float *noise, const float *style, float *audio) {
+    return guarded([&] {
+        if (!ctx || n_utts < 0 || (n_utts && (!n_frames || !asr || !f0 || !noise || !style || !audio)))
+            throw KKError(KK_ERROR_INVALID_ARGUMENT, "null argument");
+        if (n_utts == 0) return KK_OK;
+        use_device(ctx);
+        check_ready(ctx, true);
+        const Plan P = make_plan(n_frames, n_utts);
+        const size_t tot = (size_t)P.total;
+        float *d_asr = ctx->buf("in_asr", 512 * tot);
+        float *d_f0 = ctx->buf("in_f0", 2 * tot);
+        float *d_n = ctx->buf("in_n", 2 * tot);
+        float *d_style = ctx->buf("in_style", (size_t)kStyle * n_utts);
+        float *d_audio = ctx->buf("out_audio", 600 * tot);
+        cudaStream_t st = ctx->st;
+        check_cuda(cudaMemcpyAsync(d_asr, asr, 512 * tot * 4, cudaMemcpyHostToDevice, st), "H2D");
+        check_cuda(cudaMemcpyAsync(d_f0, f0, 2 * tot * 4, cudaMemcpyHostToDevice, st), "H2D");
+        check_cuda(cudaMemcpyAsync(d_n, noise, 2 * tot * 4, cudaMemcpyHostToDevice, st), "H2D");
+        check_cuda(cudaMemcpyAsync(d_style, style, (size_t)kStyle * n_utts * 4, cudaMemcpyHostToDevice, st), "H2D");
+        Runner r(*ctx, P, st);
+        r.decoder_forward(d_asr, d_f0, d_n, d_style, d_audio);
+        check_cuda(cudaGetLastError(), "kernel launch");
+        check_cuda(cudaMemcpyAsync(audio, d_audio, 600 * tot * 4, cudaMemcpyDeviceToHost, st), "D2H");
+        check_cuda(cudaStreamSynchronize(st), "decoder forward");
+        return KK_OK;
+    });
+}
+
+int kk_generator_forward(kk_ctx *ctx, int32_t n_utts, const int32_t *n_decoder_frames, const float *decoder,
+                         const float *f0, const float *style, float *audio) {
+    return guarded([&] {
+        if (!ctx || n_utts < 0 || (n_utts && (!n_decoder_frames || !decoder || !f0 || !style || !audio)))
+            throw KKError(KK_ERROR_INVALID_ARGUMENT, "null argument");
+        if (n_utts == 0) return KK_OK;
+        use_device(ctx);
+        check_ready(ctx, false);
+        const Plan P = make_plan(n_decoder_frames, n_utts);
+        const size_t tot = (size_t)P.total;
+        float *d_dec = ctx->buf("in_dec", 512 * tot);
+        float *d_f0 = ctx->buf("in_f0", tot);
+        float *d_style = ctx->buf("in_style", (size_t)kStyle * n_utts);
+        float *d_audio = ctx->buf("out_audio", 300 * tot);
+        cudaStream_t st = ctx->st;
+        check_cuda(cudaMemcpyAsync(d_dec, decoder, 512 * tot * 4, cudaMemcpyHostToDevice, st), "H2D");
+        check_cuda(cudaMemcpyAsync(d_f0, f0, tot * 4, cudaMemcpyHostToDevice, st), "H2D");
+        check_cuda(cudaMemcpyAsync(d_style, style, (size_t)kStyle * n_utts * 4, cudaMemcpyHostToDevice, st), "H2D");
+        Runner r(*ctx, P, st);
+        r.generator_forward(d_dec, d_f0, d_style, d_audio);
+        check_cuda(cudaGetLastError(), "kernel launch");
+        check_cuda(cudaMemcpyAsync(audio, d_audio, 300 * tot * 4, cudaMemcpyDeviceToHost, st), "D2H");
+        check_cuda(cudaStreamSynchronize(st), "generator forward");
+        return KK_OK;
+    });
+}
+
+int kk_istft(kk_ctx *ctx, int64_t n_frames, const float *post, float *audio) {
+    return guarded([&] {
+        if (!ctx || n_frames < 0 || (n_frames > 1 && (!post || !audio)))
+            throw KKError(KK_ERROR_INVALID_ARGUMENT, "null argument");
+        if (n_frames <= 1) return KK_OK;  // (frames - 1) * hop = 0 samples
+        if (n_frames - 1 > (int64_t)INT32_MAX) throw KKError(KK_ERROR_INVALID_ARGUMENT, "too many frames");
+        use_device(ctx);
+        if (!ctx->d_tables.p) {
+            StftTables stt;
+            IstftTables ist;
+            make_tables(stt, ist);
+            ctx->d_tables.ensure(sizeof stt + sizeof ist);
+            check_cuda(cudaMemcpy(ctx->d_tables.p, &stt, sizeof stt, cudaMemcpyHostToDevice), "tables");
+            check_cuda(cudaMemcpy((char *)ctx->d_tables.p + sizeof stt, &ist, sizeof ist, cudaMemcpyHostToDevice),
+                       "tables");
+        }
+        cudaStream_t st = ctx->st;
+        // one utterance with base length n_frames - 1 and a_nf = 1:
+        // frames = T + 1, samples = 5 T, offsets 0
+        const int32_t T = (int32_t)(n_frames - 1);
+        Plan P;
+        P.n = 1;
+        P.T = {T};
+        P.off = {0};
+        P.cum = {0};
+        P.S = n_frames;
+        P.total = T;
+        P.maxT = T;
+        float *d_post = ctx->buf("istft_post", 22 * (size_t)n_frames);
+        float *d_audio = ctx->buf("istft_audio", 5 * (size_t)T);
+        check_cuda(cudaMemcpyAsync(d_post, post, 22 * (size_t)n_frames * 4, cudaMemcpyHostToDevice, st), "H2D");
+        Runner r(*ctx, P, st);
+        r.setup_batch();
+        const IstftTables *it = (const IstftTables *)((char *)ctx->d_tables.p + sizeof(StftTables));
+        istft(d_post, n_frames, 1, d_audio, r.B, r.d_cum, it, T, st);
+        check_cuda(cudaGetLastError(), "kernel launch");
+        check_cuda(cudaMemcpyAsync(audio, d_audio, 5 * (size_t)T * 4, cudaMemcpyDeviceToHost, st), "D2H");
+        check_cuda(cudaStreamSynchronize(st), "istft");
+        return KK_OK;
+    });
+}
+
+int kk_profile_enable(kk_ctx *ctx, int enable) {
+    return guarded([&] {
+        if (!ctx) throw KKError(KK_ERROR_INVALID_ARGUMENT, "null context");
+        ctx->profiling = enable != 0;
+        return KK_OK;
+    });
+}
+
+int kk_profile_read(kk_ctx *ctx, kk_profile *out, int reset) {
+    return guarded([&] {
+        if (!ctx || !out) throw KKError(KK_ERROR_INVALID_ARGUMENT, "null argument");
+        use_device(ctx);
+        for (auto &t : ctx->timed) {
+            check_cuda(cudaEventSynchronize(t.b), "profile sync");
+            float ms = 0.f;
+            check_cuda(cudaEventElapsedTime(&ms, t.a, t.b), "profile elapsed");
+            ctx->conv_ms += ms;
+            ctx->conv_flop += t.flop;
+            ctx->conv_launches += 1;
+            ctx->event_pool.push_back(t.a);
+            ctx->event_pool.push_back(t.b);
+        }
+        ctx->timed.clear();
+        out->launches = ctx->n_launches;
+        out->conv_launches = ctx->conv_launches;
+        out->conv_ms = ctx->conv_ms;
+        out->conv_flop = ctx->conv_flop;
+        if (reset) {
+            ctx->n_launches = 0;
+            ctx->conv_launches = 0;
+            ctx->conv_ms = 0.0;
+            ctx->conv_flop = 0.0;
+        }
+        return KK_OK;
+    });
+}
+
+}  // extern "C"

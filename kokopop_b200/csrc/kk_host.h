@@ -1,0 +1,106 @@
+// Host-side state of a kk_ctx (see kk_host.cpp).
+#pragma once
+
+#include "../../include/kokopop_b200.h"
+#include "kk_kernels.h"
+
+#include <stdexcept>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+namespace kk {
+
+constexpr int32_t kMaxFrames = 8192;  // per-utterance asr frames (kokoro.cpp:584-590 warns above this)
+
+struct KKError : std::runtime_error {
+    int code;
+    KKError(int c, const std::string &m);
+};
+
+void check_cuda(cudaError_t e, const char *what);
+float half_to_float(uint16_t h);
+
+// A weight as F32 values on the device (F16 tensors are widened exactly);
+// `f16` records the stored type because it selects ggml's F16 arithmetic.
+struct DevTensor {
+    float *d = nullptr;
+    int64_t ne[4] = {1, 1, 1, 1};
+    int64_t n = 0;
+    bool f16 = false;
+    std::vector<float> host;  // small tensors only (<= 4096 values)
+};
+
+struct DevBuf {
+    void *p = nullptr;
+    size_t bytes = 0;
+    void ensure(size_t b);
+    void release();
+};
+
+struct SiteInfo {
+    std::string prefix;
+    int C = 0;
+    int f16 = 0;
+    const float *gw = nullptr, *gb = nullptr, *bw = nullptr, *bb = nullptr;
+    int64_t off = 0;  // channel offset into the per-forward gamma/beta buffers
+};
+
+// Ragged batch plan: utterance u occupies base rows [off[u], off[u] + T[u])
+// inside a slot of round_up(T[u] + 4, 4) rows, after a 4-row lead gap. A
+// level with multiplier m uses rows m * off[u] .. and R(m) rows in total,
+// padded to the 128-row tile.
+struct Plan {
+    int n = 0;
+    std::vector<int32_t> T;
+    std::vector<int64_t> off, cum;
+    int64_t S = 0;      // base rows including gaps
+    int64_t total = 0;  // sum of T
+    int32_t maxT = 0;
+    int64_t R(int m) const { return ((int64_t)m * S + 127) / 128 * 128; }
+};
+
+Plan make_plan(const int32_t *lens, int n);
+
+}  // namespace kk
+
+struct kk_ctx {
+    int device = 0;
+    cudaStream_t st = nullptr, st2 = nullptr;
+    cudaEvent_t ev_inputs = nullptr, ev_src = nullptr;
+    std::unordered_map<std::string, kk::DevTensor> w;
+    // derived from the weights
+    bool decoder_ready = false, generator_ready = false;
+    std::string missing;
+    kk::DevBuf convt_phase[2];
+    bool convt_f16[2] = {false, false};
+    kk::SineArgs sine{};
+    std::vector<kk::SiteInfo> sites;
+    std::unordered_map<std::string, int> site_index;
+    int64_t site_total_C = 0;
+    kk::DevBuf d_tables;
+    // per-forward staging
+    std::vector<kk::AdainSite> h_sites;
+    kk::DevBuf d_sites;
+    std::vector<int64_t> h_batch;
+    kk::DevBuf d_batch;
+    std::unordered_map<std::string, kk::DevBuf> ws;
+    // measurement
+    uint64_t n_launches = 0;
+    bool profiling = false;
+    struct TimedConv {
+        cudaEvent_t a, b;
+        double flop;
+    };
+    std::vector<TimedConv> timed;
+    std::vector<cudaEvent_t> event_pool;
+    uint64_t conv_launches = 0;
+    double conv_ms = 0.0, conv_flop = 0.0;
+    cudaEvent_t take_event();
+
+    ~kk_ctx();
+    const kk::DevTensor &W(const std::string &name) const;
+    const kk::DevTensor *Wopt(const std::string &name) const;
+    float *buf(const char *name, size_t floats);
+    void derive();
+};

@@ -1,0 +1,511 @@
+// Memory-bound and small kernels of the Kokoro-82M hot path (sm_100a):
+// harmonic source + STFT, instance-norm statistics, the AdaIN / Snake /
+// LeakyReLU operand prologue, ConvTranspose upsampling, the depthwise pool,
+// F0/N convs and the fused iSTFT. Dense convolutions live in kk_conv*.cu.
+//
+// Element-wise arithmetic uses the _rn intrinsics wherever the reference
+// rounds each operation separately (its translation units build without FMA
+// contraction), so these kernels reproduce the reference's rounding exactly
+// except inside the transcendental functions.
+#include "kk_kernels.h"
+
+#include <math.h>
+
+namespace kk {
+
+// ---------------------------------------------------------------------------
+// packing helpers
+// ---------------------------------------------------------------------------
+
+// Copies per-utterance [C, m*T + extra] tensors (concatenated back to back,
+// src offset C * (m*cumT + extra*u)) into the packed [C, R] buffer.
+__global__ void k_scatter(const float *__restrict__ src, float *__restrict__ dst, int64_t R, int C,
+                          int m, int extra, Batch b, const int64_t *__restrict__ cumT) {
+    const int u = blockIdx.z;
+    const int c = blockIdx.y;
+    const int64_t len = (int64_t)m * b.T[u] + extra;
+    const float *s = src + (int64_t)C * ((int64_t)m * cumT[u] + (int64_t)extra * u) + (int64_t)c * len;
+    float *d = dst + (int64_t)c * R + (int64_t)m * b.offT[u];
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < len;
+         t += (int64_t)gridDim.x * blockDim.x)
+        d[t] = s[t];
+}
+
+void scatter(const float *src, float *dst, int64_t R, int C, int m, int extra, const Batch &b,
+             const int64_t *cumT, int max_len, cudaStream_t st) {
+    dim3 grid((unsigned)((max_len + 255) / 256 < 64 ? (max_len + 255) / 256 : 64), C, b.n);
+    k_scatter<<<grid, 256, 0, st>>>(src, dst, R, C, m, extra, b, cumT);
+}
+
+// ---------------------------------------------------------------------------
+// AdaIN affine terms: gamma = Wg . style + bg, beta = Wb . style + bb
+// (linear(), graph_ops.cpp:636-654). Sequential F32 sum over the 128 style
+// features; ggml converts the style to half when the weight is F16.
+// ---------------------------------------------------------------------------
+
+__global__ void k_adain_affine(const AdainSite *__restrict__ sites, const float *__restrict__ style,
+                               int n_utts) {
+    const AdainSite s = sites[blockIdx.x];
+    const int u = blockIdx.y;
+    __shared__ float st[kStyle];
+    for (int i = threadIdx.x; i < kStyle; i += blockDim.x) {
+        const float v = style[(int64_t)u * kStyle + i];
+        st[i] = s.f16 ? round_f16(v) : v;
+    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < s.C; c += blockDim.x) {
+        const float *gw = s.gw + (int64_t)c * kStyle;
+        const float *bw = s.bw + (int64_t)c * kStyle;
+        float g = 0.f, be = 0.f;
+        for (int i = 0; i < kStyle; ++i) {
+            g = __fadd_rn(g, __fmul_rn(gw[i], st[i]));
+            be = __fadd_rn(be, __fmul_rn(bw[i], st[i]));
+        }
+        s.gamma[(int64_t)u * s.C + c] = __fadd_rn(g, s.gb[c]);
+        s.beta[(int64_t)u * s.C + c] = __fadd_rn(be, s.bb[c]);
+    }
+}
+
+void adain_affine(const AdainSite *sites_dev, int n_sites, const float *style, int n_utts,
+                  cudaStream_t st) {
+    if (n_sites == 0 || n_utts == 0) return;
+    k_adain_affine<<<dim3(n_sites, n_utts), 256, 0, st>>>(sites_dev, style, n_utts);
+}
+
+// ---------------------------------------------------------------------------
+// Instance-norm statistics, ggml_norm semantics (eps 1e-5): per (channel,
+// utterance), mean = (float)sum_double / n, var = sum_double((x-mean)^2) / n,
+// scale = 1 / sqrtf(var + eps).
+// ---------------------------------------------------------------------------
+
+template <int NT>
+__device__ double block_sum_double(double v, double *red) {
+    v = warp_sum(v);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    double r = 0.0;
+    if (threadIdx.x < 32) {
+        r = threadIdx.x < NT / 32 ? red[threadIdx.x] : 0.0;
+        r = warp_sum(r);
+        if (threadIdx.x == 0) red[0] = r;
+    }
+    __syncthreads();
+    return red[0];
+}
+
+__global__ void __launch_bounds__(256) k_stats(const float *__restrict__ x, int64_t R, int C, int m,
+                                               int extra, Batch b, float2 *__restrict__ ms) {
+    __shared__ double red[32];
+    const int c = blockIdx.x, u = blockIdx.y;
+    const int64_t len = (int64_t)m * b.T[u] + extra;
+    const float *p = x + (int64_t)c * R + (int64_t)m * b.offT[u];
+    double s = 0.0;
+    for (int64_t t = threadIdx.x; t < len; t += 256) s += (double)p[t];
+    s = block_sum_double<256>(s, red);
+    const float mean = __fdiv_rn((float)s, (float)len);
+    double s2 = 0.0;
+    for (int64_t t = threadIdx.x; t < len; t += 256) {
+        const float v = __fsub_rn(p[t], mean);
+        s2 += (double)__fmul_rn(v, v);
+    }
+    s2 = block_sum_double<256>(s2, red);
+    if (threadIdx.x == 0) {
+        const float var = (float)(s2 / (double)len);
+        const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
+        ms[(int64_t)u * C + c] = make_float2(mean, scale);
+    }
+}
+
+void stats(const float *x, int64_t R, int C, int m, int extra, const Batch &b, float2 *ms,
+           cudaStream_t st) {
+    k_stats<<<dim3(C, b.n), 256, 0, st>>>(x, R, C, m, extra, b, ms);
+}
+
+// ---------------------------------------------------------------------------
+// Operand prologue: y = act(adain(x)), written only on valid rows (gaps of
+// the operand buffer stay zero). adain_1d (graph_ops.cpp:888-907):
+//   cur = ((x - mean) * scale) * norm_w + norm_b; cur = cur + cur * gamma;
+//   cur = cur + beta
+// act: none, LeakyReLU(slope) or Snake (graph_ops.cpp:392-497):
+//   y = v + sinf(v * alpha)^2 * (1 / alpha)
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(256) k_prologue(const float *__restrict__ x, float *__restrict__ y,
+                                                  int64_t R, int C, int m, int extra, Batch b,
+                                                  PrologueArgs a) {
+    const int u = blockIdx.z, c = blockIdx.y;
+    const int64_t len = (int64_t)m * b.T[u] + extra;
+    const int64_t base = (int64_t)c * R + (int64_t)m * b.offT[u];
+    float mean = 0.f, scale = 1.f, nw = 1.f, nb = 0.f, g = 0.f, be = 0.f;
+    if (a.norm) {
+        const float2 s = a.ms[(int64_t)u * C + c];
+        mean = s.x;
+        scale = s.y;
+        nw = a.norm_w[c];
+        nb = a.norm_b[c];
+        g = a.gamma[(int64_t)u * C + c];
+        be = a.beta[(int64_t)u * C + c];
+    }
+    float alpha = 0.f, inv_a = 0.f;
+    if (a.act == ACT_SNAKE) {
+        alpha = a.alpha[c];
+        inv_a = __fdiv_rn(1.0f, alpha);
+    }
+    for (int64_t t = blockIdx.x * 256 + threadIdx.x; t < len; t += (int64_t)gridDim.x * 256) {
+        float v = x[base + t];
+        if (a.norm) {
+            v = __fmul_rn(__fsub_rn(v, mean), scale);
+            v = __fadd_rn(__fmul_rn(v, nw), nb);
+            v = __fadd_rn(v, __fmul_rn(v, g));
+            v = __fadd_rn(v, be);
+        }
+        if (a.act == ACT_LEAKY) {
+            v = leaky(v, a.slope);
+        } else if (a.act == ACT_SNAKE) {
+            const float s = sinf(__fmul_rn(v, alpha));
+            v = __fadd_rn(v, __fmul_rn(__fmul_rn(s, s), inv_a));
+        }
+        if (a.round16) v = round_f16(v);
+        y[base + t] = v;
+    }
+}
+
+void prologue(const float *x, float *y, int64_t R, int C, int m, int extra, const Batch &b,
+              int max_len, const PrologueArgs &a, cudaStream_t st) {
+    int bx = (max_len + 255) / 256;
+    if (bx > 32) bx = 32;
+    k_prologue<<<dim3(bx, C, b.n), 256, 0, st>>>(x, y, R, C, m, extra, b, a);
+}
+
+// ---------------------------------------------------------------------------
+// ConvTranspose row 0 under the left reflect pad of stage 1
+// (ggml_pad_reflect_1d(x, 1, 0), audio_utils.cpp:750-752): out'[0] = out'[2]
+// = the cropped conv-transpose output at position 1. The phase convolutions
+// write every other row; this fills row 0 of each utterance:
+// (dot(x[0], W[:, oc, 1 + crop]) + bias) + noise[0]. Only tap t_in = 0
+// contributes because 1 + crop < s.
+// ---------------------------------------------------------------------------
+
+__global__ void k_convt_row0(ConvTRow0Args a, Batch b) {
+    const int u = blockIdx.y;
+    const int oc = blockIdx.x * blockDim.x + threadIdx.x;
+    if (oc >= a.OC) return;
+    const int64_t in_row = (int64_t)a.m_in * b.offT[u];
+    const int64_t out_row = (int64_t)a.m_out * b.offT[u];
+    const int k = 1 + a.crop;
+    float acc = 0.f;
+    for (int ic = 0; ic < a.IC; ++ic) {
+        float x = a.in[(int64_t)ic * a.R_in + in_row];
+        if (a.round16) x = round_f16(x);
+        acc += x * a.w[((int64_t)ic * a.OC + oc) * a.K + k];
+    }
+    float v = __fadd_rn(acc, a.bias[oc]);
+    const int64_t o = (int64_t)oc * a.R_out + out_row;
+    v = __fadd_rn(v, a.add[o]);
+    a.out[o] = v;
+}
+
+void convt_row0(const ConvTRow0Args &a, const Batch &b, cudaStream_t st) {
+    k_convt_row0<<<dim3((a.OC + 127) / 128, b.n), 128, 0, st>>>(a, b);
+}
+
+// ---------------------------------------------------------------------------
+// Depthwise x2 pool upsample (depthwise_pool_upsample, audio_utils.cpp:
+// 73-114): the dense [3, C, C] expansion through the F32 conv-transpose path
+// reduces to out[j] = sum over t_in ascending of w[c][k] * x[c][t_in]
+// (j + 1 = 2 t_in + k), + bias. Output length 2T.
+// ---------------------------------------------------------------------------
+
+__global__ void k_pool_up(const float *__restrict__ x, float *__restrict__ y, int64_t R_in,
+                          int64_t R_out, int C, const float *__restrict__ w,
+                          const float *__restrict__ bias, Batch b, int round16) {
+    const int u = blockIdx.z, c = blockIdx.y;
+    const int64_t L = b.T[u];
+    const float *xp = x + (int64_t)c * R_in + b.offT[u];
+    float *yp = y + (int64_t)c * R_out + 2 * b.offT[u];
+    const float w0 = w[c * 3 + 0], w1 = w[c * 3 + 1], w2 = w[c * 3 + 2], bc = bias[c];
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < 2 * L;
+         t += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t j = t + 1;
+        float acc = 0.f;
+        if (j & 1) {
+            const int64_t q = j >> 1;  // k = 1
+            if (q < L) acc = __fadd_rn(acc, __fmul_rn(w1, xp[q]));
+        } else {
+            const int64_t q = j >> 1;
+            if (q - 1 >= 0 && q - 1 < L) acc = __fadd_rn(acc, __fmul_rn(w2, xp[q - 1]));  // k = 2
+            if (q < L) acc = __fadd_rn(acc, __fmul_rn(w0, xp[q]));                        // k = 0
+        }
+        float v = __fadd_rn(acc, bc);
+        if (round16) v = round_f16(v);
+        yp[t] = v;
+    }
+}
+
+void pool_up(const float *x, float *y, int64_t R_in, int64_t R_out, int C, const float *w,
+             const float *bias, const Batch &b, int max_T, int round16, cudaStream_t st) {
+    int bx = (2 * max_T + 255) / 256;
+    if (bx > 16) bx = 16;
+    k_pool_up<<<dim3(bx, C, b.n), 256, 0, st>>>(x, y, R_in, R_out, C, w, bias, b, round16);
+}
+
+// ---------------------------------------------------------------------------
+// F0_conv / N_conv (kokoro.cpp:751-752): Conv1d(1, 1, k=3, stride 2, pad 1)
+// from 2T to T frames. Its weight has ne[0] == K, so the reference takes
+// ggml_conv_1d, whose im2col is F16: input and weights rounded to half.
+// ---------------------------------------------------------------------------
+
+__global__ void k_f0n_conv(const float *__restrict__ in, int64_t R_in, float *__restrict__ out0,
+                           float *__restrict__ out1, int64_t R_out, const float *__restrict__ w,
+                           const float *__restrict__ bias, Batch b) {
+    const int u = blockIdx.y;
+    const int64_t T = b.T[u];
+    const float *xp = in + 2 * b.offT[u];
+    const float w0 = round_f16(w[0]), w1 = round_f16(w[1]), w2 = round_f16(w[2]);
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < T;
+         t += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t i0 = 2 * t - 1;
+        const float x0 = i0 >= 0 ? round_f16(xp[i0]) : 0.f;
+        const float x1 = round_f16(xp[i0 + 1]);
+        const float x2 = i0 + 2 < 2 * T ? round_f16(xp[i0 + 2]) : 0.f;
+        float acc = __fmul_rn(w0, x0);
+        acc = __fadd_rn(acc, __fmul_rn(w1, x1));
+        acc = __fadd_rn(acc, __fmul_rn(w2, x2));
+        const float v = __fadd_rn(acc, bias[0]);
+        out0[b.offT[u] + t] = v;
+        if (out1) out1[b.offT[u] + t] = v;
+    }
+    (void)R_in;
+    (void)R_out;
+}
+
+void f0n_conv(const float *in, int64_t R_in, float *out0, float *out1, int64_t R_out, const float *w,
+              const float *bias, const Batch &b, int max_T, cudaStream_t st) {
+    int bx = (max_T + 255) / 256;
+    k_f0n_conv<<<dim3(bx, b.n), 256, 0, st>>>(in, R_in, out0, out1, R_out, w, bias, b);
+}
+
+// ---------------------------------------------------------------------------
+// Harmonic source (fill_harmonic_stft, audio_utils.cpp:120-353, scalar
+// path). Per utterance one warp: lanes 0..8 each carry one harmonic's phasor
+// sequentially through all voiced segments (rotation by (cos d, sin d) with
+// each product rounded separately), stage the 300 new sines of a segment in
+// shared memory, then all 32 lanes form merged = b + sum_h w_h * 0.1 * sin_h
+// in harmonic order and tanh it. Unvoiced segments (f0 <= 10) hold
+// tanh(b) (computed on the host with the C library, like the reference) and
+// leave the phases untouched. The phasors are renormalised every 16 voiced
+// segments.
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(32) k_sinegen(const float *__restrict__ f0, int mf,
+                                                float *__restrict__ source, Batch b,
+                                                const int64_t *__restrict__ cumT, SineArgs a) {
+    __shared__ float sbuf[kHarmonics][kUpsample];
+    const int u = blockIdx.x;
+    const int lane = threadIdx.x;
+    const int64_t nseg = (int64_t)mf * b.T[u];
+    const float *fp = f0 + (int64_t)mf * b.offT[u];
+    float *src = source + (int64_t)kUpsample * mf * cumT[u];
+    float ps = 0.f, pc = 1.f;
+    const bool chain = lane < kHarmonics;
+    const float mws = chain ? a.mw_scaled[lane] : 0.f;
+    for (int64_t seg = 0; seg < nseg; ++seg) {
+        const float base_f0 = fp[seg];
+        float *out = src + seg * kUpsample;
+        if (base_f0 > 10.0f) {
+            if (chain) {
+                // delta = (float)(2 pi f0 (h+1) / 24000) evaluated in double
+                const float delta = (float)(2.0 * 3.14159265358979323846 * (double)base_f0 *
+                                            (double)(lane + 1) / 24000.0);
+                const float sd = (float)sin((double)delta);
+                const float cd = (float)cos((double)delta);
+                for (int j = 0; j < kUpsample; ++j) {
+                    const float ns = __fadd_rn(__fmul_rn(ps, cd), __fmul_rn(pc, sd));
+                    const float nc = __fsub_rn(__fmul_rn(pc, cd), __fmul_rn(ps, sd));
+                    ps = ns;
+                    pc = nc;
+                    sbuf[lane][j] = ns;
+                }
+                if ((seg + 1) % 16 == 0) {
+                    const float norm = __fsqrt_rn(__fadd_rn(__fmul_rn(ps, ps), __fmul_rn(pc, pc)));
+                    if (norm > 0.0f) {
+                        ps = __fdiv_rn(ps, norm);
+                        pc = __fdiv_rn(pc, norm);
+                    }
+                }
+            }
+            __syncwarp();
+            for (int j = lane; j < kUpsample; j += 32) {
+                float merged = a.mb;
+#pragma unroll
+                for (int h = 0; h < kHarmonics; ++h)
+                    merged = __fadd_rn(merged, __fmul_rn(a.mw_scaled[h], sbuf[h][j]));
+                out[j] = tanhf(merged);
+            }
+            __syncwarp();
+        } else {
+            for (int j = lane; j < kUpsample; j += 32) out[j] = a.unvoiced;
+        }
+    }
+    (void)mws;
+}
+
+void sinegen(const float *f0, int mf, float *source, const Batch &b, const int64_t *cumT,
+             const SineArgs &a, cudaStream_t st) {
+    k_sinegen<<<b.n, 32, 0, st>>>(f0, mf, source, b, cumT, a);
+}
+
+// Forward STFT of the source (audio_utils.cpp:381-419): Hann-20 window, hop
+// 5, center padding 10 with the reference's edge rule (src < 0 -> -src - 1,
+// src >= n -> 2n - src - 1), 11-bin DFT accumulated over n in order with
+// separately rounded products; rows 0..10 = |X|, rows 11..21 = atan2(im, re).
+__global__ void k_stft(const float *__restrict__ source, float *__restrict__ har, int64_t R, int mf,
+                       Batch b, const int64_t *__restrict__ cumT, const StftTables *__restrict__ tab) {
+    __shared__ float tc[kStftN][kBins], ts[kStftN][kBins], win[kStftN];
+    for (int i = threadIdx.x; i < kStftN * kBins; i += blockDim.x) {
+        tc[i / kBins][i % kBins] = tab->c[i / kBins][i % kBins];
+        ts[i / kBins][i % kBins] = tab->s[i / kBins][i % kBins];
+    }
+    for (int i = threadIdx.x; i < kStftN; i += blockDim.x) win[i] = tab->window[i];
+    __syncthreads();
+    const int u = blockIdx.y;
+    const int64_t n_samples = (int64_t)kUpsample * mf * b.T[u];
+    const int64_t frames = 60 * (int64_t)mf * b.T[u] + 1;
+    const float *src = source + (int64_t)kUpsample * mf * cumT[u];
+    const int64_t out_base = 60 * (int64_t)mf * b.offT[u];
+    for (int64_t f = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; f < frames;
+         f += (int64_t)gridDim.x * blockDim.x) {
+        float ws[kStftN];
+        const int64_t first = f * kHop - kStftN / 2;
+#pragma unroll
+        for (int n = 0; n < kStftN; ++n) {
+            int64_t si = first + n;
+            if (si < 0) si = -si - 1;
+            else if (si >= n_samples) si = 2 * n_samples - si - 1;
+            ws[n] = (si >= 0 && si < n_samples) ? __fmul_rn(src[si], win[n]) : 0.f;
+        }
+        float re[kBins], im[kBins];
+#pragma unroll
+        for (int k = 0; k < kBins; ++k) re[k] = im[k] = 0.f;
+#pragma unroll
+        for (int n = 0; n < kStftN; ++n) {
+#pragma unroll
+            for (int k = 0; k < kBins; ++k) {
+                re[k] = __fadd_rn(re[k], __fmul_rn(ws[n], tc[n][k]));
+                im[k] = __fsub_rn(im[k], __fmul_rn(ws[n], ts[n][k]));
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kBins; ++k) {
+            har[(int64_t)k * R + out_base + f] =
+                __fsqrt_rn(__fadd_rn(__fmul_rn(re[k], re[k]), __fmul_rn(im[k], im[k])));
+            har[(int64_t)(k + kBins) * R + out_base + f] = atan2f(im[k], re[k]);
+        }
+    }
+}
+
+void stft(const float *source, float *har, int64_t R, int mf, const Batch &b, const int64_t *cumT,
+          const StftTables *tab, int max_T, cudaStream_t st) {
+    const int64_t frames = 60 * (int64_t)mf * max_T + 1;
+    int bx = (int)((frames + 127) / 128);
+    k_stft<<<dim3(bx, b.n), 128, 0, st>>>(source, har, R, mf, b, cumT, tab);
+}
+
+// ---------------------------------------------------------------------------
+// iSTFT (cpu_istft_data, audio_utils.cpp:462-532, and the DirectDft path of
+// src/audio/istft.cpp:334-523): per frame mag = exp(clamp(p, -20, 8)),
+// phase = sin(p'), X = mag (cos phase, sin phase); frame[i] = X0 +- X10 then
+// += (2 re_k) cos - (2 im_k) sin for k = 1..9; * (1/20) * window; overlap-add
+// in ascending frame order with the window-square envelope; out = env > 1e-8
+// ? ola / env : 0; trim 10 samples each side; clamp to +-1.
+// Block: 256 frames of one utterance (+3 frames of left context).
+// ---------------------------------------------------------------------------
+
+constexpr int IS_FB = 256;
+
+__global__ void __launch_bounds__(256) k_istft(const float *__restrict__ post, int64_t R, int a_nf,
+                                               float *__restrict__ audio, Batch b,
+                                               const int64_t *__restrict__ cumT,
+                                               const IstftTables *__restrict__ tab) {
+    __shared__ float fr[(IS_FB + 3) * kStftN];
+    __shared__ float dc[kBins][kStftN], ds[kBins][kStftN], win[kStftN], win2[kStftN];
+    for (int i = threadIdx.x; i < kBins * kStftN; i += blockDim.x) {
+        dc[i / kStftN][i % kStftN] = tab->c[i / kStftN][i % kStftN];
+        ds[i / kStftN][i % kStftN] = tab->s[i / kStftN][i % kStftN];
+    }
+    for (int i = threadIdx.x; i < kStftN; i += blockDim.x) {
+        win[i] = tab->window[i];
+        win2[i] = tab->window_sq[i];
+    }
+    __syncthreads();
+    const int u = blockIdx.y;
+    const int64_t nf = (int64_t)a_nf * b.T[u] + 1;
+    const int64_t f0 = (int64_t)blockIdx.x * IS_FB;
+    if (f0 >= nf) return;
+    const int64_t base = (int64_t)a_nf * b.offT[u];
+    // frames f0-3 .. f0+FB-1
+    for (int q = threadIdx.x; q < IS_FB + 3; q += blockDim.x) {
+        const int64_t f = f0 - 3 + q;
+        float *o = fr + q * kStftN;
+        if (f < 0 || f >= nf) {
+            for (int i = 0; i < kStftN; ++i) o[i] = 0.f;
+            continue;
+        }
+        float re[kBins], im[kBins];
+#pragma unroll
+        for (int k = 0; k < kBins; ++k) {
+            float v = post[(int64_t)k * R + base + f];
+            v = fminf(fmaxf(v, -20.0f), 8.0f);
+            const float mag = expf(v);
+            const float ph = sinf(post[(int64_t)(k + kBins) * R + base + f]);
+            re[k] = __fmul_rn(mag, cosf(ph));
+            im[k] = __fmul_rn(mag, sinf(ph));
+        }
+        float x[kStftN];
+        const float d0 = re[0], ny = re[kBins - 1];
+#pragma unroll
+        for (int i = 0; i < kStftN; i += 2) {
+            x[i] = __fadd_rn(d0, ny);
+            x[i + 1] = __fsub_rn(d0, ny);
+        }
+#pragma unroll
+        for (int k = 1; k < kStftN / 2; ++k) {
+            const float cr = __fmul_rn(2.0f, re[k]), ci = __fmul_rn(2.0f, im[k]);
+#pragma unroll
+            for (int i = 0; i < kStftN; ++i)
+                x[i] = __fadd_rn(x[i], __fsub_rn(__fmul_rn(cr, dc[k][i]), __fmul_rn(ci, ds[k][i])));
+        }
+#pragma unroll
+        for (int i = 0; i < kStftN; ++i) o[i] = __fmul_rn(__fmul_rn(x[i], 0.05f), win[i]);
+    }
+    __syncthreads();
+    // padded positions p in [5 f0, 5 (f0 + FB)), output j = p - 10 in [0, 600 T)
+    const int64_t n_out = 5 * (int64_t)a_nf * b.T[u];
+    float *out = audio + 5 * (int64_t)a_nf * cumT[u];
+    for (int q = threadIdx.x; q < IS_FB * kHop; q += blockDim.x) {
+        const int64_t p = 5 * f0 + q;
+        const int64_t j = p - 10;
+        if (j < 0 || j >= n_out) continue;
+        const int64_t fhi = p / 5;
+        float ola = 0.f, env = 0.f;
+        for (int64_t f = fhi - 3; f <= fhi; ++f) {
+            if (f < 0 || f >= nf) continue;
+            const int i = (int)(p - 5 * f);
+            ola = __fadd_rn(ola, fr[(f - (f0 - 3)) * kStftN + i]);
+            env = __fadd_rn(env, win2[i]);
+        }
+        float v = env > 1e-8f ? __fdiv_rn(ola, env) : 0.0f;
+        out[j] = fminf(fmaxf(v, -1.0f), 1.0f);
+    }
+}
+
+void istft(const float *post, int64_t R, int a_nf, float *audio, const Batch &b, const int64_t *cumT,
+           const IstftTables *tab, int max_T, cudaStream_t st) {
+    const int64_t nf = (int64_t)a_nf * max_T + 1;
+    k_istft<<<dim3((unsigned)((nf + IS_FB - 1) / IS_FB), b.n), 256, 0, st>>>(post, R, a_nf, audio, b, cumT,
+                                                                            tab);
+}
+
+}  // namespace kk

@@ -1,0 +1,118 @@
+// Kernel launch interface of the Kokoro-82M hot path (host side of the .cu
+// files). All launches are asynchronous on the given stream.
+#pragma once
+
+#include "kk_common.cuh"
+
+namespace kk {
+
+enum { ACT_NONE = 0, ACT_LEAKY = 1, ACT_SNAKE = 2 };
+
+// One AdaIN site (adain_1d / ada_layer_norm): fc weights [C, 128] as F32
+// values, and per-utterance outputs gamma/beta [n_utts, C].
+struct AdainSite {
+    const float *gw, *gb, *bw, *bb;
+    float *gamma, *beta;
+    int C;
+    int f16;  // weight stored as F16: ggml rounds the style to half
+};
+
+struct PrologueArgs {
+    int norm;                 // apply the AdaIN normalisation
+    const float2 *ms;         // [n, C] (mean, scale)
+    const float *norm_w, *norm_b;
+    const float *gamma, *beta;  // [n, C]
+    int act;                  // ACT_*
+    float slope;              // LeakyReLU slope
+    const float *alpha;       // Snake alpha [C]
+    int round16;              // round the result to half (F16 conv operand)
+};
+
+// Dense convolution over a packed [IC, R_in] operand (zero gaps):
+//   y[oc, orow(q)] = epi( sum_{ic,k} W[oc, ic, k] * x[ic, q*s - p + k*d] )
+// for q in [0, n_pos), orow(q) = q * omul + oadd (rows outside [0, R_out)
+// are skipped). Epilogue, with each step rounded as the reference's
+// separate ggml ops:
+//   v = acc (+ bias[oc]); if resid: v = resid[oc, rrow] + v;
+//   v *= scale1; if accum: v = y_old + v; v *= scale2; y = v
+// rrow = orow, or orow / 2 when resid_half (nearest x2 upsample of the
+// shortcut, maybe_upsample_nearest at graph_ops.cpp:925-933).
+struct ConvArgs {
+    const float *in;
+    int64_t R_in;
+    int IC;
+    const float *w;  // [OC, IC, K] F32 values
+    int OC, K, s, p, d;
+    float *out;
+    int64_t R_out;
+    int64_t n_pos;
+    int64_t omul, oadd;
+    const float *bias;
+    const float *resid;
+    int64_t R_resid;
+    int resid_half;
+    float scale1;
+    int accum;
+    float scale2;
+    int round16;  // round the operand to half on load (F16 weights)
+};
+
+struct ConvTRow0Args {
+    const float *in;
+    int64_t R_in;
+    int IC, m_in;
+    const float *w;  // ggml [K, OC, IC]
+    int OC, K, crop, m_out;
+    const float *bias;
+    const float *add;
+    float *out;
+    int64_t R_out;
+    int round16;
+};
+
+struct SineArgs {
+    float mw_scaled[kHarmonics];  // merge weights * 0.1
+    float mb;                     // merge bias
+    float unvoiced;               // tanhf(mb), host C library
+};
+
+struct StftTables {
+    float c[kStftN][kBins], s[kStftN][kBins];
+    float window[kStftN];
+};
+
+struct IstftTables {
+    float c[kBins][kStftN], s[kBins][kStftN];
+    float window[kStftN], window_sq[kStftN];
+};
+
+void scatter(const float *src, float *dst, int64_t R, int C, int m, int extra, const Batch &b,
+             const int64_t *cumT, int max_len, cudaStream_t st);
+void adain_affine(const AdainSite *sites_dev, int n_sites, const float *style, int n_utts,
+                  cudaStream_t st);
+void stats(const float *x, int64_t R, int C, int m, int extra, const Batch &b, float2 *ms,
+           cudaStream_t st);
+void prologue(const float *x, float *y, int64_t R, int C, int m, int extra, const Batch &b,
+              int max_len, const PrologueArgs &a, cudaStream_t st);
+void convt_row0(const ConvTRow0Args &a, const Batch &b, cudaStream_t st);
+void pool_up(const float *x, float *y, int64_t R_in, int64_t R_out, int C, const float *w,
+             const float *bias, const Batch &b, int max_T, int round16, cudaStream_t st);
+void f0n_conv(const float *in, int64_t R_in, float *out0, float *out1, int64_t R_out, const float *w,
+              const float *bias, const Batch &b, int max_T, cudaStream_t st);
+// Packed per-utterance lengths are multiples of the base unit b.T: the F0
+// curve has mf * T frames (mf = 2 for asr-frame units, 1 for decoder-frame
+// units), the source 300 mf T samples, the STFT 60 mf T + 1 frames.
+void sinegen(const float *f0, int mf, float *source, const Batch &b, const int64_t *cumT,
+             const SineArgs &a, cudaStream_t st);
+void stft(const float *source, float *har, int64_t R, int mf, const Batch &b, const int64_t *cumT,
+          const StftTables *tab, int max_T, cudaStream_t st);
+// post has a_nf * T + 1 frames per utterance at rows a_nf * offT; audio is
+// 5 a_nf T samples per utterance, back to back.
+void istft(const float *post, int64_t R, int a_nf, float *audio, const Batch &b, const int64_t *cumT,
+           const IstftTables *tab, int max_T, cudaStream_t st);
+
+// kk_conv_simt.cu
+void conv_simt(const ConvArgs &a, cudaStream_t st);
+cudaError_t conv_simt_init();
+
+}  // namespace kk

@@ -1,0 +1,270 @@
+"""Synthetic Kokoro-82M weights and inputs for the hot path.
+
+No checkpoint or dataset is available, so every run uses seeded random-init
+weights with the real Kokoro-82M tensor names and shapes, and seeded inputs
+with the shapes and value ranges the workloads specify:
+
+  * weights are laid out exactly as the reference's converter writes them
+    (tools/convert_kokoro_to_gguf.py): dims reversed to ggml order, regular
+    Conv1d weights reshaped [OC, IC, K] -> [OC, IC*K] (:67-84, :376-378),
+    ConvTranspose (``.ups.``) and ``.pool.`` kept 3-D (:112-116), AdaIN ``fc``
+    split into ``.fc.gamma.*`` / ``.fc.beta.*`` (:502-509), LSTMs in PyTorch
+    packed gate order i, f, g, o (:479-499);
+  * F16 models follow the converter's type policy (:140-177): tensors of two
+    or more dims become F16, 1-D tensors and Snake ``.alpha*`` stay F32.
+
+Shapes come from the Kokoro-82M module definitions (ISTFTNet generator:
+upsample rates 10/6, kernels 20/12, initial channels 512, resblock kernels
+3/7/11 with dilations 1/3/5, n_fft 20, hop 5; decoder: AdainResBlk1d encode
+514->1024, decode 1090->1024 x3 and 1090->512 with upsample; prosody duration
+encoder: 3 x (biLSTM 640->2x256 + AdaLayerNorm(128, 512))).
+"""
+from __future__ import annotations
+
+import dataclasses
+from typing import Dict, List, Sequence, Tuple
+
+import numpy as np
+
+STYLE_DIM = 128
+HIDDEN = 512          # decoder input channels (asr features)
+GEN_CH = (256, 128)   # generator channels after ups.0 / ups.1
+RES_KERNELS = (3, 7, 11)
+
+F32 = 0
+F16 = 1
+
+
+@dataclasses.dataclass
+class Tensor:
+    name: str
+    ne: Tuple[int, ...]   # ggml order, ne[0] fastest
+    data: np.ndarray      # float32 or float16, C-contiguous, shape = ne[::-1]
+
+    @property
+    def dtype(self) -> int:
+        return F16 if self.data.dtype == np.float16 else F32
+
+
+def _adain(prefix: str, channels: int) -> List[Tuple[str, Tuple[int, ...]]]:
+    return [
+        (f"{prefix}.norm.weight", (channels,)),
+        (f"{prefix}.norm.bias", (channels,)),
+        (f"{prefix}.fc.gamma.weight", (STYLE_DIM, channels)),
+        (f"{prefix}.fc.gamma.bias", (channels,)),
+        (f"{prefix}.fc.beta.weight", (STYLE_DIM, channels)),
+        (f"{prefix}.fc.beta.bias", (channels,)),
+    ]
+
+
+def _gen_resblock(prefix: str, ch: int, k: int) -> List[Tuple[str, Tuple[int, ...]]]:
+    out: List[Tuple[str, Tuple[int, ...]]] = []
+    for i in range(3):
+        out += [
+            (f"{prefix}.convs1.{i}.weight", (ch * k, ch)),
+            (f"{prefix}.convs1.{i}.bias", (ch,)),
+            (f"{prefix}.convs2.{i}.weight", (ch * k, ch)),
+            (f"{prefix}.convs2.{i}.bias", (ch,)),
+            (f"{prefix}.alpha1.{i}", (1, ch, 1)),
+            (f"{prefix}.alpha2.{i}", (1, ch, 1)),
+        ]
+        out += _adain(f"{prefix}.adain1.{i}", ch)
+        out += _adain(f"{prefix}.adain2.{i}", ch)
+    return out
+
+
+def _adain_resblk(prefix: str, cin: int, cout: int, upsample: bool) -> List[Tuple[str, Tuple[int, ...]]]:
+    out = [
+        (f"{prefix}.conv1.weight", (cin * 3, cout)),
+        (f"{prefix}.conv1.bias", (cout,)),
+        (f"{prefix}.conv2.weight", (cout * 3, cout)),
+        (f"{prefix}.conv2.bias", (cout,)),
+    ]
+    out += _adain(f"{prefix}.norm1", cin)
+    out += _adain(f"{prefix}.norm2", cout)
+    if cin != cout:
+        out.append((f"{prefix}.conv1x1.weight", (cin, cout)))
+    if upsample:
+        out += [(f"{prefix}.pool.weight", (3, 1, cin)), (f"{prefix}.pool.bias", (cin,))]
+    return out
+
+
+def decoder_spec() -> List[Tuple[str, Tuple[int, ...]]]:
+    """Tensors read by the decoder encode/decode blocks and the generator."""
+    p = "kokopop.decoder"
+    g = f"{p}.generator"
+    spec: List[Tuple[str, Tuple[int, ...]]] = [
+        (f"{p}.F0_conv.weight", (3, 1)),
+        (f"{p}.F0_conv.bias", (1,)),
+        (f"{p}.N_conv.weight", (3, 1)),
+        (f"{p}.N_conv.bias", (1,)),
+        (f"{p}.asr_res.0.weight", (HIDDEN, 64)),
+        (f"{p}.asr_res.0.bias", (64,)),
+    ]
+    spec += _adain_resblk(f"{p}.encode", HIDDEN + 2, 1024, False)
+    for i in range(3):
+        spec += _adain_resblk(f"{p}.decode.{i}", 1024 + 66, 1024, False)
+    spec += _adain_resblk(f"{p}.decode.3", 1024 + 66, HIDDEN, True)
+    spec += [
+        (f"{g}.m_source.l_linear.weight", (9, 1)),
+        (f"{g}.m_source.l_linear.bias", (1,)),
+        (f"{g}.noise_convs.0.weight", (22 * 12, GEN_CH[0])),
+        (f"{g}.noise_convs.0.bias", (GEN_CH[0],)),
+        (f"{g}.noise_convs.1.weight", (22, GEN_CH[1])),
+        (f"{g}.noise_convs.1.bias", (GEN_CH[1],)),
+        (f"{g}.ups.0.weight", (20, GEN_CH[0], HIDDEN)),
+        (f"{g}.ups.0.bias", (GEN_CH[0],)),
+        (f"{g}.ups.1.weight", (12, GEN_CH[1], GEN_CH[0])),
+        (f"{g}.ups.1.bias", (GEN_CH[1],)),
+        (f"{g}.conv_post.weight", (GEN_CH[1] * 7, 22)),
+        (f"{g}.conv_post.bias", (22,)),
+    ]
+    spec += _gen_resblock(f"{g}.noise_res.0", GEN_CH[0], 7)
+    spec += _gen_resblock(f"{g}.noise_res.1", GEN_CH[1], 11)
+    for s in range(2):
+        for j, k in enumerate(RES_KERNELS):
+            spec += _gen_resblock(f"{g}.resblocks.{s * 3 + j}", GEN_CH[s], k)
+    return spec
+
+
+def lstm_spec(prefix: str, in_dim: int, hidden: int = 256) -> List[Tuple[str, Tuple[int, ...]]]:
+    out = []
+    for sfx in ("", "_reverse"):
+        out += [
+            (f"{prefix}.weight_ih_l0{sfx}", (in_dim, 4 * hidden)),
+            (f"{prefix}.weight_hh_l0{sfx}", (hidden, 4 * hidden)),
+            (f"{prefix}.bias_ih_l0{sfx}", (4 * hidden,)),
+            (f"{prefix}.bias_hh_l0{sfx}", (4 * hidden,)),
+        ]
+    return out
+
+
+def duration_encoder_spec() -> List[Tuple[str, Tuple[int, ...]]]:
+    """predictor.text_encoder: 3 x (biLSTM 640 -> 2x256, AdaLayerNorm(128, 512))."""
+    p = "kokopop.predictor.text_encoder.lstms"
+    spec: List[Tuple[str, Tuple[int, ...]]] = []
+    for blk in range(3):
+        spec += lstm_spec(f"{p}.{2 * blk}", HIDDEN + STYLE_DIM)
+        spec += [
+            (f"{p}.{2 * blk + 1}.fc.gamma.weight", (STYLE_DIM, HIDDEN)),
+            (f"{p}.{2 * blk + 1}.fc.gamma.bias", (HIDDEN,)),
+            (f"{p}.{2 * blk + 1}.fc.beta.weight", (STYLE_DIM, HIDDEN)),
+            (f"{p}.{2 * blk + 1}.fc.beta.bias", (HIDDEN,)),
+        ]
+    return spec
+
+
+def _is_f16_under_converter_policy(name: str, ne: Sequence[int]) -> bool:
+    """_target_type (tools/convert_kokoro_to_gguf.py:140-177) for these tensors."""
+    if len(ne) <= 1:
+        return False
+    if ".alpha" in name and ".weight" not in name:
+        return False
+    return True
+
+
+def make_weights(spec: Sequence[Tuple[str, Tuple[int, ...]]], seed: int, dist: str = "normal",
+                 scale: float = 0.02, f16: bool = False) -> Dict[str, Tensor]:
+    """Seeded random-init weights, drawn in sorted-name order.
+
+    dist "normal": N(0, scale); dist "uniform": U(-scale, scale). Snake alphas
+    are kept away from exactly 0 (the reference computes 1/alpha,
+    graph_ops.cpp:425).
+    """
+    rng = np.random.default_rng(seed)
+    out: Dict[str, Tensor] = {}
+    for name, ne in sorted(spec):
+        shape = tuple(reversed(ne))
+        if dist == "normal":
+            v = rng.normal(0.0, scale, size=shape).astype(np.float32)
+        else:
+            v = rng.uniform(-scale, scale, size=shape).astype(np.float32)
+        if ".alpha" in name:
+            v = np.where(np.abs(v) < 1e-6, np.float32(1e-6), v).astype(np.float32)
+        if f16 and _is_f16_under_converter_policy(name, ne):
+            v = v.astype(np.float16)
+        out[name] = Tensor(name, tuple(ne), np.ascontiguousarray(v))
+    return out
+
+
+def config0_weights() -> Dict[str, Tensor]:
+    """Decoder weights: seed 0, N(0, 0.02), all F32."""
+    return make_weights(decoder_spec(), seed=0, dist="normal", scale=0.02, f16=False)
+
+
+def config2_weights() -> Dict[str, Tensor]:
+    """Decoder weights: seed 2, N(0, 0.02), F16 under the converter's policy."""
+    return make_weights(decoder_spec(), seed=2, dist="normal", scale=0.02, f16=True)
+
+
+def config1_weights(f16: bool = False) -> Dict[str, Tensor]:
+    """Duration-encoder LSTM stack: seed 1, U(-1/16, 1/16)."""
+    return make_weights(duration_encoder_spec(), seed=1, dist="uniform", scale=1.0 / 16.0, f16=f16)
+
+
+# --------------------------------------------------------------------------
+# inputs
+# --------------------------------------------------------------------------
+
+def f0_curve(rng: np.random.Generator, n: int) -> np.ndarray:
+    """Smooth random walk in 80-300 Hz with ~20% of frames zeroed in
+    contiguous spans (<= 10 Hz is unvoiced, audio_utils.cpp:179)."""
+    f = np.empty(n, dtype=np.float64)
+    v = rng.uniform(80.0, 300.0)
+    for i in range(n):
+        v += rng.normal(0.0, 3.0)
+        if v < 80.0:
+            v = 160.0 - v
+        if v > 300.0:
+            v = 600.0 - v
+        f[i] = v
+    zero = np.zeros(n, dtype=bool)
+    target = int(round(0.2 * n))
+    guard = 0
+    while zero.sum() < target and guard < 10000:
+        guard += 1
+        span = int(rng.integers(3, max(4, min(30, n // 4 + 4))))
+        start = int(rng.integers(0, max(1, n - span + 1)))
+        zero[start:start + span] = True
+    f[zero] = 0.0
+    return f.astype(np.float32)
+
+
+@dataclasses.dataclass
+class Utterance:
+    T: int                 # asr frames
+    asr: np.ndarray        # [512, T] time-fastest (torch [1, 512, T])
+    f0: np.ndarray         # [2T]
+    noise: np.ndarray      # [2T]
+    style: np.ndarray      # [128] decoder style
+
+
+def make_utterance(rng: np.random.Generator, T: int, style_dim: int = STYLE_DIM) -> Utterance:
+    asr = rng.normal(0.0, 1.0, size=(HIDDEN, T)).astype(np.float32)
+    f0 = f0_curve(rng, 2 * T)
+    noise = rng.normal(0.0, 0.5, size=2 * T).astype(np.float32)
+    style = rng.normal(0.0, 0.1, size=style_dim).astype(np.float32)
+    return Utterance(T, asr, f0, noise, np.ascontiguousarray(style[:STYLE_DIM]))
+
+
+def config0_inputs(T: int = 200) -> Utterance:
+    """T=200 frames (5 s, 120000 samples), input seed 100."""
+    return make_utterance(np.random.default_rng(100), T)
+
+
+def config3_utterances(n: int = 256, t_min: int = 40, t_max: int = 800, seed: int = 103) -> List[Utterance]:
+    """256 independent utterances, T ~ U[40, 800]; style is the decoder half
+    ([0:128]) of a 256-d N(0, 0.1) voice row."""
+    rng = np.random.default_rng(seed)
+    lens = rng.integers(t_min, t_max + 1, size=n)
+    return [make_utterance(rng, int(t), style_dim=256) for t in lens]
+
+
+def pack(utts: Sequence[Utterance]):
+    """Concatenate a ragged batch into the C ABI's back-to-back layout."""
+    n_frames = np.array([u.T for u in utts], dtype=np.int32)
+    asr = np.concatenate([u.asr.reshape(-1) for u in utts]).astype(np.float32)
+    f0 = np.concatenate([u.f0 for u in utts]).astype(np.float32)
+    noise = np.concatenate([u.noise for u in utts]).astype(np.float32)
+    style = np.concatenate([u.style for u in utts]).astype(np.float32)
+    return n_frames, asr, f0, noise, style

@@ -1,0 +1,257 @@
+"""ctypes access to the oracle (oracle/_build/libkk_oracle.so) and to the
+reference's own compiled iSTFT / LSTM (oracle/_ref/libkk_ref.so).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and
+bench.py's CPU-baseline leg, always as the checker or the timed CPU
+reference, never as the product path.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from typing import Callable, Dict, Optional
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_build", "libkk_oracle.so")
+REF_PATH = os.path.join(HERE, "_ref", "libkk_ref.so")
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+
+
+class TensorDesc(ctypes.Structure):
+    _fields_ = [
+        ("name", ctypes.c_char_p),
+        ("dtype", ctypes.c_int32),
+        ("n_dims", ctypes.c_int32),
+        ("ne", ctypes.c_int64 * 4),
+        ("data", ctypes.c_void_p),
+    ]
+
+
+def build() -> None:
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def _ptr(a: np.ndarray):
+    return a.ctypes.data_as(_f32p)
+
+
+def descs_for(weights) -> tuple:
+    """kk_tensor_desc array for a {name: workload.Tensor} dict. The returned
+    tuple keeps the name buffers and arrays alive."""
+    items = list(weights.values())
+    arr = (TensorDesc * len(items))()
+    keep = []
+    for i, t in enumerate(items):
+        nm = t.name.encode()
+        keep.append(nm)
+        data = np.ascontiguousarray(t.data)
+        keep.append(data)
+        arr[i].name = nm
+        arr[i].dtype = t.dtype
+        arr[i].n_dims = len(t.ne)
+        for d in range(4):
+            arr[i].ne[d] = t.ne[d] if d < len(t.ne) else 1
+        arr[i].data = data.ctypes.data
+    return arr, keep
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = ctypes.CDLL(LIB_PATH)
+        L.kko_model_create.restype = ctypes.c_void_p
+        L.kko_model_create.argtypes = [ctypes.c_void_p, ctypes.c_size_t]
+        L.kko_model_free.argtypes = [ctypes.c_void_p]
+        L.kko_last_error.restype = ctypes.c_char_p
+        L.kko_round_f16.restype = ctypes.c_float
+        L.kko_round_f16.argtypes = [ctypes.c_float]
+        _lib = L
+    return _lib
+
+
+TAP_FN = ctypes.CFUNCTYPE(None, ctypes.c_char_p, _f32p, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p)
+
+
+class OracleModel:
+    """The oracle over one weight set."""
+
+    def __init__(self, weights):
+        self.L = lib()
+        arr, self._keep = descs_for(weights)
+        self.h = self.L.kko_model_create(ctypes.cast(arr, ctypes.c_void_p), len(arr))
+        if not self.h:
+            raise RuntimeError("kko_model_create failed")
+        self._tap_cb = None
+        self.taps: Dict[str, np.ndarray] = {}
+
+    def __del__(self):
+        try:
+            if self.h:
+                self.L.kko_model_free(ctypes.c_void_p(self.h))
+        except Exception:
+            pass
+
+    def _check(self, rc: int):
+        if rc != 0:
+            raise RuntimeError(self.L.kko_last_error().decode())
+
+    def record_taps(self, enable: bool = True):
+        self.taps = {}
+        if enable:
+            def cb(name, data, ne0, ne1, user):
+                self.taps[name.decode()] = np.ctypeslib.as_array(data, shape=(ne1, ne0)).copy()
+            self._tap_cb = TAP_FN(cb)
+            self.L.kko_set_tap(ctypes.c_void_p(self.h), self._tap_cb, None)
+        else:
+            self.L.kko_set_tap(ctypes.c_void_p(self.h), TAP_FN(), None)
+
+    def harmonic_stft(self, f0: np.ndarray, target_frames: int):
+        f0 = np.ascontiguousarray(f0, dtype=np.float32)
+        har = np.zeros((22, target_frames), np.float32)
+        src = np.zeros(len(f0) * 300, np.float32)
+        self._check(self.L.kko_harmonic_stft(ctypes.c_void_p(self.h), _ptr(f0), ctypes.c_int64(len(f0)),
+                                             ctypes.c_int64(target_frames), _ptr(har), _ptr(src)))
+        return har, src
+
+    def generator(self, decoder: np.ndarray, f0: np.ndarray, style: np.ndarray, want_post: bool = False):
+        decoder = np.ascontiguousarray(decoder, dtype=np.float32)
+        L = decoder.shape[1]
+        audio = np.zeros(L * 300, np.float32)
+        post = np.zeros((22, 60 * L + 1), np.float32) if want_post else None
+        self._check(self.L.kko_generator(ctypes.c_void_p(self.h), ctypes.c_int64(L), _ptr(decoder),
+                                         _ptr(np.ascontiguousarray(f0, np.float32)),
+                                         _ptr(np.ascontiguousarray(style, np.float32)), _ptr(audio),
+                                         _ptr(post) if post is not None else None))
+        return (audio, post) if want_post else audio
+
+    def decoder(self, asr, f0, noise, style):
+        T = asr.shape[1]
+        out = np.zeros((512, 2 * T), np.float32)
+        self._check(self.L.kko_decoder(ctypes.c_void_p(self.h), ctypes.c_int64(T),
+                                       _ptr(np.ascontiguousarray(asr, np.float32)),
+                                       _ptr(np.ascontiguousarray(f0, np.float32)),
+                                       _ptr(np.ascontiguousarray(noise, np.float32)),
+                                       _ptr(np.ascontiguousarray(style, np.float32)), _ptr(out)))
+        return out
+
+    def decoder_forward(self, asr, f0, noise, style):
+        T = asr.shape[1]
+        audio = np.zeros(600 * T, np.float32)
+        self._check(self.L.kko_decoder_forward(ctypes.c_void_p(self.h), ctypes.c_int64(T),
+                                               _ptr(np.ascontiguousarray(asr, np.float32)),
+                                               _ptr(np.ascontiguousarray(f0, np.float32)),
+                                               _ptr(np.ascontiguousarray(noise, np.float32)),
+                                               _ptr(np.ascontiguousarray(style, np.float32)), _ptr(audio)))
+        return audio
+
+    def bilstm(self, prefix: str, x: np.ndarray, hidden: int = 256):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        N, D = x.shape
+        out = np.zeros((N, 2 * hidden), np.float32)
+        self._check(self.L.kko_bilstm(ctypes.c_void_p(self.h), prefix.encode(), ctypes.c_int64(N),
+                                      ctypes.c_int64(D), _ptr(x), _ptr(out)))
+        return out
+
+    def duration_encoder(self, x: np.ndarray, style: np.ndarray):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        N = x.shape[0]
+        out = np.zeros((N, 640), np.float32)
+        self._check(self.L.kko_duration_encoder(ctypes.c_void_p(self.h), ctypes.c_int64(N), _ptr(x),
+                                                _ptr(np.ascontiguousarray(style, np.float32)), _ptr(out)))
+        return out
+
+
+def istft(post: np.ndarray) -> np.ndarray:
+    post = np.ascontiguousarray(post, dtype=np.float32)
+    n = post.shape[1]
+    audio = np.zeros(max(0, (n - 1) * 5), np.float32)
+    n_out = ctypes.c_int64(0)
+    rc = lib().kko_istft(_ptr(post), ctypes.c_int64(n), _ptr(audio) if audio.size else None, ctypes.byref(n_out))
+    if rc != 0:
+        raise RuntimeError(lib().kko_last_error().decode())
+    return audio[: n_out.value]
+
+
+def lstm_direction(pre: np.ndarray, w_hh_rowwise: np.ndarray, b_hh: np.ndarray, reverse: bool) -> np.ndarray:
+    pre = np.ascontiguousarray(pre, np.float32)
+    N, H4 = pre.shape
+    H = H4 // 4
+    out = np.zeros((N, H), np.float32)
+    lib().kko_lstm_direction(_ptr(pre), _ptr(np.ascontiguousarray(w_hh_rowwise, np.float32)),
+                             _ptr(np.ascontiguousarray(b_hh, np.float32)), ctypes.c_int64(H),
+                             ctypes.c_int64(N), ctypes.c_int(1 if reverse else 0), _ptr(out))
+    return out
+
+
+def align_durations(durations: np.ndarray, speed: float, hidden: Optional[np.ndarray] = None):
+    d = np.ascontiguousarray(durations, np.float32)
+    n = len(d)
+    frames = np.zeros(n, np.int32)
+    total = ctypes.c_int64(0)
+    L = lib()
+    L.kko_align_durations.argtypes = [_f32p, ctypes.c_int64, ctypes.c_float, ctypes.POINTER(ctypes.c_int32),
+                                      ctypes.POINTER(ctypes.c_int64), _f32p, ctypes.c_int64, _f32p, ctypes.c_int64]
+    if hidden is None:
+        rc = L.kko_align_durations(_ptr(d), n, ctypes.c_float(speed),
+                                   frames.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), ctypes.byref(total),
+                                   None, 0, None, 0)
+        if rc != 0:
+            raise RuntimeError(L.kko_last_error().decode())
+        return frames, total.value, None
+    hidden = np.ascontiguousarray(hidden, np.float32)
+    cap = 50 * n
+    en = np.zeros((cap, hidden.shape[1]), np.float32)
+    rc = L.kko_align_durations(_ptr(d), n, ctypes.c_float(speed),
+                               frames.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), ctypes.byref(total),
+                               _ptr(hidden), hidden.shape[1], _ptr(en), cap)
+    if rc != 0:
+        raise RuntimeError(L.kko_last_error().decode())
+    return frames, total.value, en[: total.value]
+
+
+# --- the reference's own compiled code (oracle/_ref) ----------------------
+
+_ref = None
+
+
+def ref_available() -> bool:
+    return os.path.exists(REF_PATH)
+
+
+def ref():
+    global _ref
+    if _ref is None:
+        R = ctypes.CDLL(REF_PATH)
+        R.kkref_istft_kokoro.argtypes = [_f32p, ctypes.c_int64, _f32p, ctypes.POINTER(ctypes.c_int64)]
+        R.kkref_lstm_direction.argtypes = [_f32p, _f32p, _f32p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, _f32p]
+        _ref = R
+    return _ref
+
+
+def ref_istft(post: np.ndarray) -> np.ndarray:
+    post = np.ascontiguousarray(post, np.float32)
+    n = post.shape[1]
+    audio = np.zeros(max(1, (n - 1) * 5), np.float32)
+    n_out = ctypes.c_int64(0)
+    if ref().kkref_istft_kokoro(_ptr(post), n, _ptr(audio), ctypes.byref(n_out)) != 0:
+        raise RuntimeError("reference istft failed")
+    return audio[: n_out.value]
+
+
+def ref_lstm_direction(pre: np.ndarray, w_hh_rowwise: np.ndarray, b_hh: np.ndarray, reverse: bool) -> np.ndarray:
+    pre = np.ascontiguousarray(pre, np.float32)
+    N, H4 = pre.shape
+    H = H4 // 4
+    out = np.full((N, H), -99.0, np.float32)
+    ref().kkref_lstm_direction(_ptr(pre), _ptr(np.ascontiguousarray(w_hh_rowwise, np.float32)),
+                               _ptr(np.ascontiguousarray(b_hh, np.float32)), H, N, 1 if reverse else 0, _ptr(out))
+    return out

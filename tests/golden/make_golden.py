@@ -1,0 +1,83 @@
+"""Generates the golden fixtures in tests/golden/.
+
+  istft_ref.npz   seeded Kokoro post tensors and the iSTFT output of the
+                  reference's own src/audio/istft.cpp (compiled unchanged into
+                  oracle/_ref/ by oracle/Makefile), incl. the 3-frame known
+                  answer of tests/test_audio_utils.cpp:371-399
+  lstm_ref.npz    the deterministic inputs of tests/test_lstm_fused.cpp:64-73
+                  (H=33, N=9, forward and reverse) plus a seeded H=64 case,
+                  with outputs of the reference's own lstm_fused.cpp
+  oracle_small.npz  regression vectors of the oracle itself (decoder + generator
+                  at T=3 for the F32 and F16 weight sets); these are NOT
+                  reference outputs (the reference's generator needs ggml,
+                  which is absent), they pin the restatement against drift.
+
+Run from the repository root with the reference tree present:
+    python tests/golden/make_golden.py
+"""
+import os
+import sys
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+sys.path.insert(0, ROOT)
+
+from oracle import oracle as O  # noqa: E402
+from kokopop_b200 import workload as W  # noqa: E402
+
+OUT = os.path.dirname(os.path.abspath(__file__))
+
+
+def lstm_inputs(H, N):
+    i = np.arange(4 * H * N, dtype=np.float32)
+    pre = (np.float32(0.17) * np.sin(i * np.float32(0.37)) + np.float32(0.05) * np.cos(i * np.float32(0.11)))
+    j = np.arange(4 * H * H, dtype=np.float32)
+    w_hh = np.float32(0.08) * np.sin(j * np.float32(0.19))
+    k = np.arange(4 * H, dtype=np.float32)
+    b_hh = np.float32(0.03) * np.cos(k * np.float32(0.23))
+    # w_hh is ggml [H, 4H] (w[k + H*j]); the rowwise copy has the same layout
+    return pre.astype(np.float32).reshape(N, 4 * H), w_hh.astype(np.float32).reshape(4 * H, H), b_hh.astype(np.float32)
+
+
+def main():
+    if not O.ref_available():
+        O.build()
+    rng = np.random.default_rng(7)
+    ist = {}
+    known = np.full((22, 3), -20.0, np.float32)
+    known[1, :] = 0.0
+    known[11:, :] = 0.0
+    ist["known_post"] = known
+    ist["known_audio"] = O.ref_istft(known)
+    for n in (2, 3, 17, 50):
+        post = rng.normal(0.0, 2.0, size=(22, n)).astype(np.float32)
+        ist[f"post_{n}"] = post
+        ist[f"audio_{n}"] = O.ref_istft(post)
+    np.savez_compressed(os.path.join(OUT, "istft_ref.npz"), **ist)
+
+    ls = {}
+    for rev in (0, 1):
+        pre, w, b = lstm_inputs(33, 9)
+        ls[f"h33_pre"], ls[f"h33_w"], ls[f"h33_b"] = pre, w, b
+        ls[f"h33_out_{rev}"] = O.ref_lstm_direction(pre, w, b, bool(rev))
+    pre = rng.normal(0.0, 3.0, size=(12, 256)).astype(np.float32)
+    w = rng.uniform(-0.5, 0.5, size=(256, 64)).astype(np.float32)
+    b = rng.uniform(-1 / 16, 1 / 16, size=256).astype(np.float32)
+    ls["h64_pre"], ls["h64_w"], ls["h64_b"] = pre, w, b
+    ls["h64_out_0"] = O.ref_lstm_direction(pre, w, b, False)
+    ls["h64_out_1"] = O.ref_lstm_direction(pre, w, b, True)
+    np.savez_compressed(os.path.join(OUT, "lstm_ref.npz"), **ls)
+
+    sm = {}
+    u = W.make_utterance(np.random.default_rng(11), 3)
+    sm["asr"], sm["f0"], sm["noise"], sm["style"] = u.asr, u.f0, u.noise, u.style
+    for tag, wts in (("f32", W.config0_weights()), ("f16", W.config2_weights())):
+        m = O.OracleModel(wts)
+        sm[f"audio_{tag}"] = m.decoder_forward(u.asr, u.f0, u.noise, u.style)
+    np.savez_compressed(os.path.join(OUT, "oracle_small.npz"), **sm)
+    print("wrote", sorted(os.listdir(OUT)))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,145 @@
+"""GPU parity of the decoder / generator / iSTFT path against the oracle,
+through the C ABI. Tolerance: 1e-3 max-abs on F32 waveform samples (the
+bar for this path); the iSTFT alone is held to 1e-5."""
+import numpy as np
+import pytest
+
+import kokopop_b200 as kb
+from kokopop_b200 import workload as W
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+AUDIO_TOL = 1e-3
+
+
+@pytest.fixture(scope="module")
+def w32():
+    return W.config0_weights()
+
+
+@pytest.fixture(scope="module")
+def w16():
+    return W.config2_weights()
+
+
+@pytest.fixture(scope="module")
+def o32(w32):
+    return O.OracleModel(w32)
+
+
+@pytest.fixture(scope="module")
+def o16(w16):
+    return O.OracleModel(w16)
+
+
+def test_istft_known_answer(ctx):
+    post = np.full((22, 3), -20.0, np.float32)
+    post[1, :] = 0.0
+    post[11:, :] = 0.0
+    out = ctx.istft(post)
+    assert out.shape == (10,) and abs(out[0] + 0.08) < 1e-4
+
+
+@pytest.mark.parametrize("n", [0, 1, 2, 3, 50, 1001, 24001])
+def test_istft_matches_oracle(ctx, n):
+    rng = np.random.default_rng(n)
+    post = rng.normal(0.0, 2.0, size=(22, n)).astype(np.float32)
+    got = ctx.istft(post)
+    want = O.istft(post) if n else np.zeros(0, np.float32)
+    assert got.shape == want.shape
+    if n > 1:
+        assert np.abs(got - want).max() < 1e-5
+
+
+def _check(got, want, tol=AUDIO_TOL):
+    assert got.shape == want.shape
+    assert np.all(np.isfinite(got))
+    err = float(np.abs(got - want).max())
+    assert err < tol, f"max abs err {err}"
+    return err
+
+
+@pytest.mark.parametrize("T", [1, 3, 20])
+def test_decoder_forward_f32_small(ctx, w32, o32, T):
+    ctx.upload(w32)
+    u = W.make_utterance(np.random.default_rng(100 + T), T)
+    got = ctx.decoder_forward([u])[0]
+    _check(got, o32.decoder_forward(u.asr, u.f0, u.noise, u.style))
+
+
+@pytest.mark.parametrize("T", [1, 3, 20])
+def test_decoder_forward_f16_small(ctx, w16, o16, T):
+    ctx.upload(w16)
+    u = W.make_utterance(np.random.default_rng(200 + T), T)
+    got = ctx.decoder_forward([u])[0]
+    _check(got, o16.decoder_forward(u.asr, u.f0, u.noise, u.style))
+
+
+def test_decoder_forward_config0_full_size(ctx, w32, o32):
+    """T=200 frames, 120000 samples, F32 weights seed 0, inputs seed 100."""
+    ctx.upload(w32)
+    u = W.config0_inputs(200)
+    got = ctx.decoder_forward([u])[0]
+    assert got.shape == (120000,)
+    _check(got, o32.decoder_forward(u.asr, u.f0, u.noise, u.style))
+
+
+def test_decoder_forward_f16_full_size(ctx, w16, o16):
+    ctx.upload(w16)
+    u = W.config0_inputs(200)
+    _check(ctx.decoder_forward([u])[0], o16.decoder_forward(u.asr, u.f0, u.noise, u.style))
+
+
+def test_generator_seam_matches_oracle(ctx, w32, o32):
+    ctx.upload(w32)
+    rng = np.random.default_rng(5)
+    decs, f0s, styles, want = [], [], [], []
+    for L in (2, 7, 40):
+        dec = rng.normal(0, 1, size=(512, L)).astype(np.float32)
+        f0 = W.f0_curve(rng, L)
+        st = rng.normal(0, 0.1, size=128).astype(np.float32)
+        decs.append(dec)
+        f0s.append(f0)
+        styles.append(st)
+        want.append(o32.generator(dec, f0, st))
+    got = ctx.generator_forward(decs, f0s, styles)
+    for g_, w_ in zip(got, want):
+        _check(g_, w_)
+
+
+def test_ragged_batch_equals_single_calls(ctx, w16):
+    """Packing utterances into one batch changes nothing, bit for bit."""
+    ctx.upload(w16)
+    rng = np.random.default_rng(9)
+    utts = [W.make_utterance(rng, t) for t in (5, 1, 13, 2, 8)]
+    batch = ctx.decoder_forward(utts)
+    for u, b in zip(utts, batch):
+        np.testing.assert_array_equal(ctx.decoder_forward([u])[0], b)
+
+
+def test_unvoiced_everywhere(ctx, w32, o32):
+    ctx.upload(w32)
+    u = W.make_utterance(np.random.default_rng(4), 6)
+    u.f0[:] = 0.0
+    _check(ctx.decoder_forward([u])[0], o32.decoder_forward(u.asr, u.f0, u.noise, u.style))
+
+
+def test_invalid_lengths_are_rejected(ctx, w32):
+    ctx.upload(w32)
+    u = W.make_utterance(np.random.default_rng(1), 2)
+    u.T = 0
+    with pytest.raises(kb.KKError) as e:
+        ctx.decoder_forward([u])
+    assert e.value.code == kb.KK_ERROR_INVALID_ARGUMENT
+
+
+def test_missing_weights_is_model_error():
+    c = kb.Context(0)
+    try:
+        u = W.make_utterance(np.random.default_rng(1), 2)
+        with pytest.raises(kb.KKError) as e:
+            c.decoder_forward([u])
+        assert e.value.code == kb.KK_ERROR_MODEL
+    finally:
+        c.close()

@@ -1,0 +1,184 @@
+"""CPU tests of the oracle: pinned against the reference's own compiled code
+(golden vectors from oracle/_ref) and against the reference's known answers.
+No GPU needed."""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from kokopop_b200 import workload as W
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def g(name):
+    return np.load(os.path.join(GOLDEN, name))
+
+
+# --- R9 iSTFT ---------------------------------------------------------------
+
+def test_istft_known_answer():
+    """tests/test_audio_utils.cpp:371-399: k=1 bin, 3 frames -> out[0] = -0.08."""
+    post = np.full((22, 3), -20.0, np.float32)
+    post[1, :] = 0.0
+    post[11:, :] = 0.0
+    out = O.istft(post)
+    assert out.shape == (10,)
+    assert abs(out[0] - (-0.08)) < 1e-4
+
+
+def test_istft_matches_reference_golden_bit_exact():
+    z = g("istft_ref.npz")
+    np.testing.assert_array_equal(O.istft(z["known_post"]), z["known_audio"])
+    for n in (2, 3, 17, 50):
+        np.testing.assert_array_equal(O.istft(z[f"post_{n}"]), z[f"audio_{n}"])
+
+
+@pytest.mark.skipif(not O.ref_available(), reason="oracle/_ref not built")
+@pytest.mark.parametrize("n", [2, 5, 64, 1001])
+def test_istft_matches_reference_library(n):
+    rng = np.random.default_rng(n)
+    post = rng.normal(0.0, 3.0, size=(22, n)).astype(np.float32)
+    np.testing.assert_array_equal(O.istft(post), O.ref_istft(post))
+
+
+def test_istft_edge_lengths_and_bounds():
+    # tests/test_audio_utils.cpp:61-162
+    assert O.istft(np.zeros((22, 0), np.float32)).size == 0
+    assert O.istft(np.zeros((22, 1), np.float32)).size == 0
+    out = O.istft(np.zeros((22, 50), np.float32))
+    assert out.size == 245 and np.all(np.abs(out) <= 1.0)
+    for v in (8.0, 100.0):
+        out = O.istft(np.full((22, 100), v, np.float32))
+        assert np.all(np.abs(out) <= 1.0)
+    out = O.istft(np.full((22, 100), -20.0, np.float32))
+    assert np.all(np.abs(out) < 1e-5)
+
+
+# --- R7 LSTM recurrence -------------------------------------------------------
+
+def test_lstm_matches_reference_golden_bit_exact():
+    z = g("lstm_ref.npz")
+    for rev in (0, 1):
+        np.testing.assert_array_equal(O.lstm_direction(z["h33_pre"], z["h33_w"], z["h33_b"], bool(rev)),
+                                      z[f"h33_out_{rev}"])
+        np.testing.assert_array_equal(O.lstm_direction(z["h64_pre"], z["h64_w"], z["h64_b"], bool(rev)),
+                                      z[f"h64_out_{rev}"])
+
+
+def _naive_lstm(pre, w, b, reverse):
+    """The scalar reference of tests/test_lstm_fused.cpp:15-55 (naive sigmoid,
+    c clamped to +-50)."""
+    N, H4 = pre.shape
+    H = H4 // 4
+    h = np.zeros(H, np.float32)
+    c = np.zeros(H, np.float32)
+    out = np.zeros((N, H), np.float32)
+    sig = lambda x: np.float32(1.0) / (np.float32(1.0) + np.exp(-x))
+    for step in range(N):
+        t = N - 1 - step if reverse else step
+        gates = b + pre[t] + (w @ h).astype(np.float32)
+        i, f, gg, o = sig(gates[:H]), sig(gates[H:2 * H]), np.tanh(gates[2 * H:3 * H]), sig(gates[3 * H:])
+        c = np.clip(f * c + i * gg, -50, 50).astype(np.float32)
+        h = (o * np.tanh(c)).astype(np.float32)
+        out[t] = h
+    return out
+
+
+@pytest.mark.parametrize("reverse", [False, True])
+def test_lstm_matches_scalar_reference_within_2e5(reverse):
+    """tests/test_lstm_fused.cpp:114-118 tolerance."""
+    z = g("lstm_ref.npz")
+    out = O.lstm_direction(z["h33_pre"], z["h33_w"], z["h33_b"], reverse)
+    ref = _naive_lstm(z["h33_pre"], z["h33_w"], z["h33_b"], reverse)
+    assert np.abs(out - ref).max() < 2e-5
+
+
+# --- ggml semantics used by the oracle -------------------------------------------
+
+def test_round_f16_matches_ieee_half():
+    rng = np.random.default_rng(0)
+    vals = np.concatenate([
+        rng.normal(0, 1, 2000), rng.normal(0, 300, 2000), rng.normal(0, 1e-5, 2000),
+        [0.0, -0.0, 65504.0, 65519.0, 65520.0, 1e9, -1e9, 2 ** -24, 2 ** -25, 3 * 2 ** -26, 5.96e-8, 6.1e-5],
+    ]).astype(np.float32)
+    L = O.lib()
+    got = np.array([L.kko_round_f16(float(v)) for v in vals], np.float32)
+    want = vals.astype(np.float16).astype(np.float32)
+    np.testing.assert_array_equal(got, want)
+
+
+def test_norm_time_is_ggml_two_pass():
+    rng = np.random.default_rng(1)
+    x = (rng.normal(3.0, 0.5, size=(4, 1000))).astype(np.float32)
+    y = np.zeros_like(x)
+    import ctypes
+    L = O.lib()
+    f = ctypes.POINTER(ctypes.c_float)
+    L.kko_norm_time(x.ctypes.data_as(f), ctypes.c_int64(4), ctypes.c_int64(1000), ctypes.c_float(1e-5),
+                    y.ctypes.data_as(f))
+    mean = x.astype(np.float64).mean(1, keepdims=True)
+    ref = (x - mean) / np.sqrt(x.astype(np.float64).var(1, keepdims=True) + 1e-5)
+    assert np.abs(y - ref).max() < 1e-5
+
+
+# --- R11 durations -> frames (bit-exact integer path) ---------------------------
+
+def test_duration_to_frames_rounding_and_clamps():
+    # kokoro.cpp:181-193: lrint (half to even), clamp [1, 50], non-finite -> 1
+    d = np.array([0.0, 0.4, 0.5, 1.5, 2.5, 2.5000002, 3.49, 49.5, 50.5, 1e9, np.inf, -np.inf, np.nan, -3.0,
+                  3e9], np.float32)
+    frames, total, _ = O.align_durations(d, 1.0)
+    assert frames.tolist() == [1, 1, 1, 2, 2, 3, 3, 50, 50, 50, 1, 1, 1, 1, 1]
+    assert total == sum(frames.tolist())
+
+
+def test_duration_speed_and_alignment_copies_rows():
+    d = np.array([2.2, 4.6, 1.0, 7.5], np.float32)
+    frames, total, _ = O.align_durations(d, 2.0)
+    assert frames.tolist() == [1, 2, 1, 4]
+    frames, total, _ = O.align_durations(d, -1.0)  # invalid speed -> 1
+    assert frames.tolist() == [2, 5, 1, 8]
+    hidden = np.arange(4 * 3, dtype=np.float32).reshape(4, 3)
+    frames, total, en = O.align_durations(d, 1.0, hidden)
+    assert total == 16 and en.shape == (16, 3)
+    expect = np.repeat(hidden, frames, axis=0)
+    np.testing.assert_array_equal(en, expect)
+
+
+# --- R1 harmonic source -----------------------------------------------------
+
+def test_harmonic_source_unvoiced_is_constant_and_phase_held():
+    wts = W.config0_weights()
+    m = O.OracleModel(wts)
+    mb = wts["kokopop.decoder.generator.m_source.l_linear.bias"].data[0]
+    f0 = np.zeros(6, np.float32)
+    har, src = m.harmonic_stft(f0, 6 * 60 + 1)
+    assert np.all(src == src[0])
+    assert abs(float(src[0]) - np.tanh(float(mb))) < 1e-9
+    # a voiced-unvoiced-voiced curve: the phase continues across the gap
+    f0 = np.array([200, 200, 0, 0, 200, 200], np.float32)
+    _, s1 = m.harmonic_stft(f0, 361)
+    f0b = np.array([200, 200, 200, 200], np.float32)
+    _, s2 = m.harmonic_stft(f0b, 241)
+    np.testing.assert_array_equal(s1[1200:1800], s2[600:1200])
+
+
+def test_oracle_regression_small():
+    z = g("oracle_small.npz")
+    for tag, wts in (("f32", W.config0_weights()), ("f16", W.config2_weights())):
+        m = O.OracleModel(wts)
+        a = m.decoder_forward(z["asr"], z["f0"], z["noise"], z["style"])
+        np.testing.assert_array_equal(a, z[f"audio_{tag}"])
+
+
+def test_oracle_shapes_follow_reference_invariants():
+    """tests/test_kokoro_real.cpp:54-88: decoder = 2T frames x 512, audio = 600 T."""
+    m = O.OracleModel(W.config0_weights())
+    u = W.make_utterance(np.random.default_rng(3), 2)
+    dec = m.decoder(u.asr, u.f0, u.noise, u.style)
+    assert dec.shape == (512, 4)
+    audio = m.generator(dec, u.f0, u.style)
+    assert audio.shape == (1200,)
+    assert np.all(np.isfinite(audio)) and np.all(np.abs(audio) <= 1.0)
