@@ -232,7 +232,9 @@ def main():
         host.append({"n": n_frames, "asr": p(asr), "f0": p(f0), "noise": p(noise), "style": p(style),
                      "audio": torch.empty(600 * int(n_frames.sum()), dtype=torch.float32).pin_memory()})
 
-    stream = torch.cuda.current_stream()
+    # A dedicated stream: the C ABI runs the path on the stream it is given,
+    # and the CUDA events below are recorded on that same stream.
+    stream = torch.cuda.Stream()
 
     def step_device(k):
         d = dev[k % len(dev)]

@@ -250,7 +250,7 @@ void kk_ctx::derive() {
             throw KKError(KK_ERROR_MODEL, "invalid harmonic source merge weight size");
         for (int h = 0; h < kHarmonics; ++h) sine.mw_scaled[h] = mw.host[h] * 0.1f;
         sine.mb = mb.host[0];
-        sine.unvoiced = std::tanh(sine.mb);
+        sine.unvoiced = (float)std::tanh((double)sine.mb);  // correctly rounded, as in the kernel
     } else {
         ok = false;
     }

@@ -289,13 +289,15 @@ void f0n_conv(const float *in, int64_t R_in, float *out0, float *out1, int64_t R
 
 // ---------------------------------------------------------------------------
 // Harmonic source (fill_harmonic_stft, audio_utils.cpp:120-353, scalar
-// path). Per utterance one warp: lanes 0..8 each carry one harmonic's phasor
+// path). tanh, sin and cos are the correctly rounded float values (double
+// evaluation, rounded once): the generator output depends on the last bit of
+// the source through the phases of near-silent STFT bins, and only the
+// correctly rounded values are reproducible across implementations. Per utterance one warp: lanes 0..8 each carry one harmonic's phasor
 // sequentially through all voiced segments (rotation by (cos d, sin d) with
 // each product rounded separately), stage the 300 new sines of a segment in
 // shared memory, then all 32 lanes form merged = b + sum_h w_h * 0.1 * sin_h
 // in harmonic order and tanh it. Unvoiced segments (f0 <= 10) hold
-// tanh(b) (computed on the host with the C library, like the reference) and
-// leave the phases untouched. The phasors are renormalised every 16 voiced
+// tanh(b) (computed once on the host) and leave the phases untouched. The phasors are renormalised every 16 voiced
 // segments.
 // ---------------------------------------------------------------------------
 
@@ -342,7 +344,7 @@ __global__ void __launch_bounds__(32) k_sinegen(const float *__restrict__ f0, in
 #pragma unroll
                 for (int h = 0; h < kHarmonics; ++h)
                     merged = __fadd_rn(merged, __fmul_rn(a.mw_scaled[h], sbuf[h][j]));
-                out[j] = tanhf(merged);
+                out[j] = (float)tanh((double)merged);
             }
             __syncwarp();
         } else {

@@ -132,6 +132,7 @@ struct kko_model {
     size_t n;
     kko_tap_fn tap;
     void *tap_user;
+    int source_libm;  /* 1: harmonic source uses the C library's float tanhf/sinf/cosf */
 };
 
 kko_model *kko_model_create(const kk_tensor_desc *descs, size_t n) {
@@ -169,6 +170,19 @@ void kko_model_free(kko_model *m) {
     free(m->t);
     free(m);
 }
+
+void kko_set_source_libm(kko_model *m, int use_libm) { m->source_libm = use_libm; }
+
+/* Correctly rounded float tanh / sin / cos: evaluated in double, rounded
+ * once. The reference calls the C library's float functions here
+ * (audio_utils.cpp:182-183, :329, :352); their last bit varies between C
+ * libraries (glibc 2.39 tanhf differs from the correctly rounded value for
+ * about a third of inputs in [-0.1, 0.1]) and the generator amplifies that
+ * last bit through the phases of near-silent STFT bins, so the source is
+ * pinned to the correctly rounded values instead. */
+static float cr_tanhf(float x) { return (float)tanh((double)x); }
+static float cr_sinf(float x) { return (float)sin((double)x); }
+static float cr_cosf(float x) { return (float)cos((double)x); }
 
 void kko_set_tap(kko_model *m, kko_tap_fn fn, void *user) {
     m->tap = fn;
@@ -574,6 +588,9 @@ int kko_harmonic_stft(kko_model *m, const float *f0, int64_t n_f0, int64_t targe
     const float mb = mb_t->data[0];
     const float *mw = mw_t->data;
     const int64_t n_samples = n_f0 * KO_UPSAMPLE;
+    float (*f_tanh)(float) = m->source_libm ? tanhf : cr_tanhf;
+    float (*f_sin)(float) = m->source_libm ? sinf : cr_sinf;
+    float (*f_cos)(float) = m->source_libm ? cosf : cr_cosf;
     float *source = fbuf((size_t)n_samples);
 
     /* scalar path of audio_utils.cpp:318-353 */
@@ -590,8 +607,8 @@ int kko_harmonic_stft(kko_model *m, const float *f0, int64_t n_f0, int64_t targe
             for (int h = 0; h < KO_HARMONICS; ++h) {
                 const float delta = (float)(2.0 * M_PI * (double)base_f0 * (double)(float)(h + 1) /
                                             (double)(float)KO_SAMPLE_RATE);
-                sin_delta[h] = sinf(delta);
-                cos_delta[h] = cosf(delta);
+                sin_delta[h] = f_sin(delta);
+                cos_delta[h] = f_cos(delta);
                 mw_scaled[h] = mw[h] * KO_SINE_AMP;
             }
             for (int64_t j = 0; j < KO_UPSAMPLE; ++j) {
@@ -604,7 +621,7 @@ int kko_harmonic_stft(kko_model *m, const float *f0, int64_t n_f0, int64_t targe
                     phase_cos[h] = nc;
                     merged += mw_scaled[h] * ns;
                 }
-                source[seg_start + j] = tanhf(merged);
+                source[seg_start + j] = f_tanh(merged);
             }
             if ((seg + 1) % 16 == 0) {
                 for (int h = 0; h < KO_HARMONICS; ++h) {
@@ -616,7 +633,7 @@ int kko_harmonic_stft(kko_model *m, const float *f0, int64_t n_f0, int64_t targe
                 }
             }
         } else {
-            const float unvoiced = tanhf(mb);
+            const float unvoiced = f_tanh(mb);
             for (int64_t j = 0; j < KO_UPSAMPLE; ++j) source[seg_start + j] = unvoiced;
         }
     }

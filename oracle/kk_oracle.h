@@ -41,6 +41,11 @@ typedef void (*kko_tap_fn)(const char *name, const float *data, int64_t ne0,
                            int64_t ne1, void *user);
 void kko_set_tap(kko_model *m, kko_tap_fn fn, void *user);
 
+/* 1: evaluate the harmonic source's tanh / sin / cos with the C library's
+ * float functions, exactly the calls the reference makes; 0 (default): the
+ * correctly rounded values (see kk_oracle.c). */
+void kko_set_source_libm(kko_model *m, int use_libm);
+
 /* Last error message of the calling thread ("" when none). */
 const char *kko_last_error(void);
 

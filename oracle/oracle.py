@@ -104,6 +104,11 @@ class OracleModel:
         if rc != 0:
             raise RuntimeError(self.L.kko_last_error().decode())
 
+    def set_source_libm(self, use_libm: bool):
+        """True: the harmonic source uses the C library's float tanhf/sinf/cosf
+        (the reference's literal calls); False (default): correctly rounded."""
+        self.L.kko_set_source_libm(ctypes.c_void_p(self.h), 1 if use_libm else 0)
+
     def record_taps(self, enable: bool = True):
         self.taps = {}
         if enable:

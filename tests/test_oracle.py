@@ -165,6 +165,26 @@ def test_harmonic_source_unvoiced_is_constant_and_phase_held():
     np.testing.assert_array_equal(s1[1200:1800], s2[600:1200])
 
 
+def test_source_last_bit_sensitivity_is_why_the_source_is_correctly_rounded():
+    """The generator amplifies the last bit of the harmonic source: evaluating
+    its tanh/sin/cos with glibc's float functions instead of the correctly
+    rounded values moves the waveform far beyond the 1e-3 bar, while a 1-ulp
+    perturbation of the asr input moves it by ~1e-5. The reference's own
+    waveform therefore depends on the C library at this level; the oracle and
+    the kernel both use the correctly rounded values."""
+    wts = W.config0_weights()
+    m = O.OracleModel(wts)
+    u = W.make_utterance(np.random.default_rng(220), 20)
+    cr = m.decoder_forward(u.asr, u.f0, u.noise, u.style)
+    m.set_source_libm(True)
+    libm = m.decoder_forward(u.asr, u.f0, u.noise, u.style)
+    m.set_source_libm(False)
+    assert np.abs(cr - libm).max() > 1e-2
+    asr2 = (u.asr * np.float32(1 + 6e-8)).astype(np.float32)
+    pert = m.decoder_forward(asr2, u.f0, u.noise, u.style)
+    assert np.abs(cr - pert).max() < 1e-4
+
+
 def test_oracle_regression_small():
     z = g("oracle_small.npz")
     for tag, wts in (("f32", W.config0_weights()), ("f16", W.config2_weights())):
