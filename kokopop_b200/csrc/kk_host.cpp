@@ -180,6 +180,52 @@ static std::vector<std::string> adain_site_prefixes() {
     return v;
 }
 
+// Packs a convolution weight W[oc, ic, k] (via `get`) into the tensor-core
+// kernel's shared-memory images: half [K][IC_pad/64][n_tiles][8][128][8],
+// zero in the channel padding. The values are F16 already, so the
+// conversion is exact.
+template <typename Get>
+static void pack_tc(PackedW &pw, int OC, int IC, int K, Get get) {
+    pw.IC = IC;
+    pw.OC = OC;
+    pw.K = K;
+    pw.IC_pad = (IC + 63) / 64 * 64;
+    pw.n_tiles = (OC + 127) / 128;
+    const int NB = pw.IC_pad / 64;
+    std::vector<__half> h((size_t)K * NB * pw.n_tiles * 8 * 128 * 8, __float2half_rn(0.f));
+    for (int k = 0; k < K; ++k)
+        for (int oc = 0; oc < OC; ++oc)
+            for (int ic = 0; ic < IC; ++ic) {
+                const int b = ic / 64, c = (ic % 64) / 8, e = ic % 8, nt = oc / 128, n = oc % 128;
+                const size_t idx = ((((size_t)k * NB + b) * pw.n_tiles + nt) * 8 + c) * (128 * 8) + (size_t)n * 8 + e;
+                h[idx] = __float2half_rn(get(oc, ic, k));
+            }
+    pw.buf.ensure(h.size() * sizeof(__half));
+    check_cuda(cudaMemcpy(pw.buf.p, h.data(), h.size() * sizeof(__half), cudaMemcpyHostToDevice), "upload packed");
+}
+
+// The convolutions that run on the tensor cores, with their tap counts.
+static std::vector<std::pair<std::string, int>> tc_convs() {
+    std::vector<std::pair<std::string, int>> v;
+    const std::string d = "kokopop.decoder.", g = d + "generator.";
+    v.push_back({d + "asr_res.0.weight", 1});
+    for (const std::string &b : {d + "encode", d + "decode.0", d + "decode.1", d + "decode.2", d + "decode.3"}) {
+        v.push_back({b + ".conv1.weight", 3});
+        v.push_back({b + ".conv2.weight", 3});
+        v.push_back({b + ".conv1x1.weight", 1});
+    }
+    const std::pair<std::string, int> blocks[8] = {{"noise_res.0", 7}, {"noise_res.1", 11}, {"resblocks.0", 3},
+                                                   {"resblocks.1", 7},  {"resblocks.2", 11}, {"resblocks.3", 3},
+                                                   {"resblocks.4", 7},  {"resblocks.5", 11}};
+    for (const auto &bk : blocks)
+        for (int i = 0; i < 3; ++i) {
+            v.push_back({g + bk.first + ".convs1." + std::to_string(i) + ".weight", bk.second});
+            v.push_back({g + bk.first + ".convs2." + std::to_string(i) + ".weight", bk.second});
+        }
+    v.push_back({g + "conv_post.weight", 7});
+    return v;
+}
+
 // Builds everything derived from the raw weights: ConvTranspose phase
 // weights, the AdaIN site table, the harmonic-source constants and tables.
 void kk_ctx::derive() {
@@ -193,6 +239,7 @@ void kk_ctx::derive() {
     // phase r, tap 0 reads t_in = q - 1 with W[r + s], tap 1 reads q with W[r].
     static const int strides[2] = {10, 6};
     bool ok = true;
+    std::vector<float> phase_host[2];
     for (int s = 0; s < 2; ++s) {
         const std::string nm = "kokopop.decoder.generator.ups." + std::to_string(s) + ".weight";
         if (!need(nm)) {
@@ -216,6 +263,39 @@ void kk_ctx::derive() {
         check_cuda(cudaMemcpy(convt_phase[s].p, ph.data(), ph.size() * 4, cudaMemcpyHostToDevice),
                    "upload phase weights");
         convt_f16[s] = t.f16;
+        phase_host[s] = std::move(ph);
+    }
+    // tensor-core path: taken when every convolution weight is stored as F16
+    // (the converter's policy); F32 weight sets keep the F32 CUDA-core path.
+    packed.clear();
+    tc_mode = ok && convt_f16[0] && convt_f16[1];
+    for (const auto &cv : tc_convs()) {
+        const DevTensor *t = Wopt(cv.first);
+        if (t && !t->f16) tc_mode = false;
+        if (!t && cv.first.find("conv1x1") == std::string::npos) tc_mode = false;
+    }
+    if (tc_mode) {
+        check_cuda(conv_tc_init(), "tensor-core conv init");
+        std::vector<float> h;
+        for (const auto &cv : tc_convs()) {
+            const DevTensor *t = Wopt(cv.first);
+            if (!t) continue;
+            const int K = cv.second, OC = (int)t->ne[1], IC = (int)(t->ne[0] / K);
+            h.resize((size_t)t->n);
+            check_cuda(cudaMemcpy(h.data(), t->d, h.size() * 4, cudaMemcpyDeviceToHost), "read conv weight");
+            pack_tc(packed[cv.first], OC, IC, K,
+                    [&](int oc, int ic, int k) { return h[((size_t)oc * IC + ic) * K + k]; });
+        }
+        for (int s = 0; s < 2; ++s) {
+            const DevTensor &t = W("kokopop.decoder.generator.ups." + std::to_string(s) + ".weight");
+            const int OC = (int)t.ne[1], IC = (int)t.ne[2], S = strides[s];
+            const std::vector<float> &ph = phase_host[s];
+            for (int r = 0; r < S; ++r)
+                pack_tc(packed["ups." + std::to_string(s) + ".phase." + std::to_string(r)], OC, IC, 2,
+                        [&](int oc, int ic, int k) { return ph[(((size_t)r * OC + oc) * IC + ic) * 2 + k]; });
+        }
+        d_err.ensure(sizeof(int));
+        check_cuda(cudaMemset(d_err.p, 0, sizeof(int)), "clear error");
     }
     // AdaIN sites
     sites.clear();
@@ -307,6 +387,15 @@ Plan kk::make_plan(const int32_t *lens, int n) {
 
 namespace {
 
+// An activation operand of a convolution: F32 channel-major [C][R] for the
+// CUDA-core path, or half chunk-major [C/8][R][8] for the tensor-core path.
+// Its gap rows (and padding channels) read as zero.
+struct Op {
+    float *f = nullptr;
+    __half *h = nullptr;
+    int64_t R = 0;
+};
+
 struct Runner {
     kk_ctx &c;
     const Plan &P;
@@ -315,8 +404,9 @@ struct Runner {
     const int64_t *d_cum = nullptr;
     float2 *ms = nullptr;
     float *gbase = nullptr, *bbase = nullptr;
+    const bool tc;
 
-    Runner(kk_ctx &ctx, const Plan &plan, cudaStream_t s) : c(ctx), P(plan), st(s) {}
+    Runner(kk_ctx &ctx, const Plan &plan, cudaStream_t s) : c(ctx), P(plan), st(s), tc(ctx.tc_mode) {}
 
     int64_t R(int m) const { return P.R(m); }
 
@@ -373,6 +463,29 @@ struct Runner {
         return c.h_sites[it->second];
     }
 
+    // sum over utterances of the length at level m (+ extra per utterance)
+    int64_t sum_len(int m, int extra) const { return (int64_t)m * P.total + (int64_t)extra * P.n; }
+
+    // The operand buffer of a level (multiplier m) with room for C channels.
+    Op op(const char *name, int m, int C) {
+        Op o;
+        o.R = R(m);
+        if (tc) {
+            const int cpad = (C + 63) / 64 * 64;
+            o.h = (__half *)c.buf(name, ((size_t)cpad * o.R + 1) / 2);
+        } else {
+            o.f = c.buf(name, (size_t)C * o.R);
+        }
+        return o;
+    }
+
+    void zero(const Op &o, int C) {
+        if (o.h)
+            check_cuda(cudaMemsetAsync(o.h, 0, (size_t)((C + 63) / 64 * 64) * o.R * sizeof(__half), st), "memset");
+        else
+            check_cuda(cudaMemsetAsync(o.f, 0, (size_t)C * o.R * sizeof(float), st), "memset");
+    }
+
     struct Epi {
         const DevTensor *bias = nullptr;
         const float *resid = nullptr;
@@ -385,12 +498,23 @@ struct Runner {
         int64_t valid = 0;  // valid output positions (algorithmic FLOP count)
     };
 
-    // sum over utterances of the length at level m (+ extra per utterance)
-    int64_t sum_len(int m, int extra) const { return (int64_t)m * P.total + (int64_t)extra * P.n; }
+    void timed_begin(cudaEvent_t &e0, cudaEvent_t &e1) {
+        if (!c.profiling) return;
+        e0 = c.take_event();
+        e1 = c.take_event();
+        check_cuda(cudaEventRecord(e0, st), "event");
+    }
 
-    // y = conv(w, in); 2-D ggml weight [IC*K, OC] (or the 3-D phase tensor).
-    void conv(const float *w, bool f16, int OC, const float *in, int64_t R_in, int IC, int K, int s, int p,
-              int d, float *out, int64_t R_out, int64_t n_pos, const Epi &e) {
+    void timed_end(cudaEvent_t e0, cudaEvent_t e1, double flop) {
+        ++c.n_launches;
+        if (!c.profiling) return;
+        check_cuda(cudaEventRecord(e1, st), "event");
+        c.timed.push_back({e0, e1, flop});
+    }
+
+    // CUDA-core convolution on an F32 operand.
+    void conv_f32(const float *w, bool f16, int OC, const float *in, int64_t R_in, int IC, int K, int s, int p,
+                  int d, float *out, int64_t R_out, int64_t n_pos, const Epi &e) {
         ConvArgs a{};
         a.in = in;
         a.R_in = R_in;
@@ -415,31 +539,62 @@ struct Runner {
         a.scale2 = e.scale2;
         a.round16 = f16 ? 1 : 0;
         cudaEvent_t e0 = nullptr, e1 = nullptr;
-        if (c.profiling) {
-            e0 = c.take_event();
-            e1 = c.take_event();
-            check_cuda(cudaEventRecord(e0, st), "event");
-        }
+        timed_begin(e0, e1);
         conv_simt(a, st);
-        ++c.n_launches;
-        if (c.profiling) {
-            check_cuda(cudaEventRecord(e1, st), "event");
-            c.timed.push_back({e0, e1, 2.0 * OC * (double)IC * K * (double)e.valid});
-        }
+        timed_end(e0, e1, 2.0 * OC * (double)IC * K * (double)e.valid);
     }
 
-    void conv_w(const std::string &wname, const std::string &bname, const float *in, int64_t R_in, int IC,
-                int K, int s, int p, int d, float *out, int64_t R_out, int64_t n_pos, Epi e, int64_t valid) {
+    // Tensor-core convolution on a half chunk-major operand.
+    void conv_h(const PackedW &pw, const Op &in, int K, int p, int d, float *out, int64_t R_out, int64_t n_pos,
+                const Epi &e) {
+        ConvTcArgs a{};
+        a.in = in.h;
+        a.R_in = in.R;
+        a.IC_pad = pw.IC_pad;
+        a.w = (const __half *)pw.buf.p;
+        a.n_tiles = pw.n_tiles;
+        a.OC = pw.OC;
+        a.K = K;
+        a.p = p;
+        a.d = d;
+        a.out = out;
+        a.R_out = R_out;
+        a.n_pos = n_pos;
+        a.omul = e.omul;
+        a.oadd = e.oadd;
+        a.bias = e.bias ? e.bias->d : nullptr;
+        a.resid = e.resid;
+        a.R_resid = e.R_resid;
+        a.resid_half = e.resid_half;
+        a.scale1 = e.scale1;
+        a.accum = e.accum;
+        a.scale2 = e.scale2;
+        a.err = (int *)c.d_err.p;
+        cudaEvent_t e0 = nullptr, e1 = nullptr;
+        timed_begin(e0, e1);
+        check_cuda(conv_tc(a, st), "tensor-core conv launch");
+        timed_end(e0, e1, 2.0 * pw.OC * (double)pw.IC * K * (double)e.valid);
+    }
+
+    // Convolution by weight name on an operand of the current path (stride 1).
+    void conv_w(const std::string &wname, const std::string &bname, const Op &in, int IC, int K, int p, int d,
+                float *out, int64_t R_out, int64_t n_pos, Epi e, int64_t valid) {
         e.valid = valid;
+        if (!bname.empty()) e.bias = &c.W(bname);
         const DevTensor &w = c.W(wname);
         const int OC = (int)(w.ne[2] > 1 ? w.ne[2] : w.ne[1]);
         if (w.n != (int64_t)OC * IC * K) throw KKError(KK_ERROR_MODEL, "conv weight shape mismatch: " + wname);
-        if (!bname.empty()) e.bias = &c.W(bname);
-        conv(w.d, w.f16, OC, in, R_in, IC, K, s, p, d, out, R_out, n_pos, e);
+        if (tc) {
+            auto it = c.packed.find(wname);
+            if (it == c.packed.end()) throw KKError(KK_ERROR_MODEL, "no packed weight for " + wname);
+            conv_h(it->second, in, K, p, d, out, R_out, n_pos, e);
+        } else {
+            conv_f32(w.d, w.f16, OC, in.f, in.R, IC, K, 1, p, d, out, R_out, n_pos, e);
+        }
     }
 
-    // stats + AdaIN + activation into the operand buffer
-    void adain_act(const std::string &prefix, const float *x, float *y, int64_t Rm, int C, int m, int extra,
+    // stats + AdaIN + activation into an operand (or an F32 buffer)
+    void adain_act(const std::string &prefix, const float *x, const Op &y, int64_t Rm, int C, int m, int extra,
                    int act, float slope, const std::string &alpha) {
         const AdainSite &s = site(prefix);
         if (s.C != C) throw KKError(KK_ERROR_MODEL, "AdaIN channel mismatch: " + prefix);
@@ -456,16 +611,22 @@ struct Runner {
         a.slope = slope;
         a.alpha = alpha.empty() ? nullptr : c.W(alpha).d;
         a.round16 = 0;
-        prologue(x, y, Rm, C, m, extra, B, m * P.maxT + extra, a, st);
+        if (y.h)
+            prologue_h(x, y.h, Rm, C, m, extra, B, m * P.maxT + extra, a, st);
+        else
+            prologue(x, y.f, Rm, C, m, extra, B, m * P.maxT + extra, a, st);
         ++c.n_launches;
     }
 
-    void act_only(const float *x, float *y, int64_t Rm, int C, int m, int extra, float slope) {
+    void act_only(const float *x, const Op &y, int64_t Rm, int C, int m, int extra, int act, float slope) {
         PrologueArgs a{};
         a.norm = 0;
-        a.act = ACT_LEAKY;
+        a.act = act;
         a.slope = slope;
-        prologue(x, y, Rm, C, m, extra, B, m * P.maxT + extra, a, st);
+        if (y.h)
+            prologue_h(x, y.h, Rm, C, m, extra, B, m * P.maxT + extra, a, st);
+        else
+            prologue(x, y.f, Rm, C, m, extra, B, m * P.maxT + extra, a, st);
         ++c.n_launches;
     }
 
@@ -474,66 +635,81 @@ struct Runner {
         const int64_t R1 = R(1), R2 = R(2);
         const DevTensor &c1 = c.W(pf + ".conv1.weight");
         const int Cout = (int)c1.ne[1];
-        float *opT = c.buf("opT", 1090 * (size_t)R1);
-        adain_act(pf + ".norm1", x, opT, R1, Cin, 1, 0, ACT_LEAKY, 0.2f, "");
-        const float *c1_in = opT;
-        int64_t Rc = R1;
-        int m = 1;
-        float *op = opT, *tmp = c.buf("tmpT", 1024 * (size_t)R1);
+        const int m = up ? 2 : 1;
+        const int64_t Rc = up ? R2 : R1;
+        Op opT = op("opT", 1, 1152);
+        Op opL = up ? op("op2", 2, 1152) : opT;
+        float *tmp = up ? c.buf("tmp2", 512 * (size_t)R2) : c.buf("tmpT", 1024 * (size_t)R1);
+        // shortcut: nearest x2 upsample (folded into the epilogue's row map)
+        // then the bias-free 1x1 conv, on the raw input
+        Epi e2;
+        e2.scale1 = kInvSqrt2;
+        e2.resid_half = up ? 1 : 0;
+        e2.R_resid = R1;
+        if (c.Wopt(pf + ".conv1x1.weight")) {
+            float *sc = c.buf("scT", 1024 * (size_t)R1);
+            Op xin;
+            if (tc) {
+                act_only(x, opT, R1, Cin, 1, 0, ACT_NONE, 0.f);
+                xin = opT;
+            } else {
+                xin.f = const_cast<float *>(x);
+                xin.R = R1;
+            }
+            conv_w(pf + ".conv1x1.weight", "", xin, Cin, 1, 0, 1, sc, R1, R1, Epi{}, sum_len(1, 0));
+            e2.resid = sc;
+        } else {
+            if (Cin != Cout) throw KKError(KK_ERROR_MODEL, "missing conv1x1 for " + pf);
+            e2.resid = x;
+        }
+        // residual: AdaIN(norm1) -> LeakyReLU(0.2) -> [pool x2] -> conv1
         if (up) {
-            float *op2 = c.buf("op2", 1090 * (size_t)R2);
             const DevTensor &pw = c.W(pf + ".pool.weight"), &pb = c.W(pf + ".pool.bias");
             if (pw.ne[0] != 3 || pw.ne[1] != 1 || pw.ne[2] != Cin)
                 throw KKError(KK_ERROR_MODEL, "invalid depthwise upsample pool shape: " + pf);
-            pool_up(opT, op2, R1, R2, Cin, pw.d, pb.d, B, P.maxT, 0, st);
-        ++c.n_launches;
-            c1_in = op2;
-            Rc = R2;
-            m = 2;
-            op = op2;
-            tmp = c.buf("tmp2", 512 * (size_t)R2);
-        }
-        conv_w(pf + ".conv1.weight", pf + ".conv1.bias", c1_in, Rc, Cin, 3, 1, 1, 1, tmp, Rc, Rc, Epi{}, sum_len(m, 0));
-        adain_act(pf + ".norm2", tmp, op, Rc, Cout, m, 0, ACT_LEAKY, 0.2f, "");
-        Epi e;
-        e.scale1 = kInvSqrt2;
-        e.resid_half = up ? 1 : 0;
-        if (c.Wopt(pf + ".conv1x1.weight")) {
-            float *sc = c.buf("scT", 1024 * (size_t)R1);
-            conv_w(pf + ".conv1x1.weight", "", x, R1, Cin, 1, 1, 0, 1, sc, R1, R1, Epi{}, sum_len(1, 0));
-            e.resid = sc;
+            // the pool reads F32 activations (the reference's dense F32 kernel)
+            Op pf32;
+            pf32.f = c.buf("pfT", 1090 * (size_t)R1);
+            pf32.R = R1;
+            adain_act(pf + ".norm1", x, pf32, R1, Cin, 1, 0, ACT_LEAKY, 0.2f, "");
+            if (tc)
+                pool_up_h(nullptr, pf32.f, opL.h, R1, R2, Cin, pw.d, pb.d, B, P.maxT, st);
+            else
+                pool_up(pf32.f, opL.f, R1, R2, Cin, pw.d, pb.d, B, P.maxT, 0, st);
+            ++c.n_launches;
         } else {
-            if (Cin != Cout) throw KKError(KK_ERROR_MODEL, "missing conv1x1 for " + pf);
-            e.resid = x;
+            adain_act(pf + ".norm1", x, opT, R1, Cin, 1, 0, ACT_LEAKY, 0.2f, "");
         }
-        e.R_resid = R1;
-        conv_w(pf + ".conv2.weight", pf + ".conv2.bias", op, Rc, Cout, 3, 1, 1, 1, out, Rc, Rc, e, sum_len(m, 0));
+        conv_w(pf + ".conv1.weight", pf + ".conv1.bias", opL, Cin, 3, 1, 1, tmp, Rc, Rc, Epi{}, sum_len(m, 0));
+        // AdaIN(norm2) -> LeakyReLU(0.2) -> conv2, + shortcut, * 1/sqrt(2)
+        adain_act(pf + ".norm2", tmp, opL, Rc, Cout, m, 0, ACT_LEAKY, 0.2f, "");
+        conv_w(pf + ".conv2.weight", pf + ".conv2.bias", opL, Cout, 3, 1, 1, out, Rc, Rc, e2, sum_len(m, 0));
     }
 
     // graph_generator_resblock: x_in -> (3 iterations) -> wb, the last
     // iteration writing final_out (accumulating / scaling) when given.
     void gen_resblock(const std::string &pf, int K, const float *x_in, float *wb, float *final_out, int accum,
-                      float scale2, int C, int m, int extra, float *op, float *tmp) {
+                      float scale2, int C, int m, int extra, const Op &o, float *tmp) {
         const int64_t Rm = R(m);
         const float *cur = x_in;
         for (int i = 0; i < 3; ++i) {
             const std::string is = std::to_string(i);
             const int d = kDil[i];
-            adain_act(pf + ".adain1." + is, cur, op, Rm, C, m, extra, ACT_SNAKE, 0.f, pf + ".alpha1." + is);
-            conv_w(pf + ".convs1." + is + ".weight", pf + ".convs1." + is + ".bias", op, Rm, C, K, 1,
-                   (K * d - d) / 2, d, tmp, Rm, Rm, Epi{}, sum_len(m, extra));
-            adain_act(pf + ".adain2." + is, tmp, op, Rm, C, m, extra, ACT_SNAKE, 0.f, pf + ".alpha2." + is);
+            adain_act(pf + ".adain1." + is, cur, o, Rm, C, m, extra, ACT_SNAKE, 0.f, pf + ".alpha1." + is);
+            conv_w(pf + ".convs1." + is + ".weight", pf + ".convs1." + is + ".bias", o, C, K, (K * d - d) / 2, d, tmp,
+                   Rm, Rm, Epi{}, sum_len(m, extra));
+            adain_act(pf + ".adain2." + is, tmp, o, Rm, C, m, extra, ACT_SNAKE, 0.f, pf + ".alpha2." + is);
             Epi e;
             e.resid = cur;
             e.R_resid = Rm;
-            float *o = wb;
+            float *out = wb;
             if (i == 2 && final_out) {
-                o = final_out;
+                out = final_out;
                 e.accum = accum;
                 e.scale2 = scale2;
             }
-            conv_w(pf + ".convs2." + is + ".weight", pf + ".convs2." + is + ".bias", op, Rm, C, K, 1, K / 2, 1, o,
-                   Rm, Rm, e, sum_len(m, extra));
+            conv_w(pf + ".convs2." + is + ".weight", pf + ".convs2." + is + ".bias", o, C, K, K / 2, 1, out, Rm, Rm,
+                   e, sum_len(m, extra));
             cur = wb;
         }
     }
@@ -548,6 +724,7 @@ struct Runner {
         const int64_t R_har = R(60 * gm);
         const float *x = x_in;
         int C = 512, m_prev = gm;
+        Op op_prev = op("op2", gm, 1152);
         const std::string g = "kokopop.decoder.generator.";
         for (int s = 0; s < 2; ++s) {
             const int m = mlev[s];
@@ -555,23 +732,28 @@ struct Runner {
             const std::string ss = std::to_string(s);
             const DevTensor &ncw = c.W(g + "noise_convs." + ss + ".weight");
             const int Cs = (int)ncw.ne[1];
-            const std::string lv = std::to_string(s);
-            float *xs = c.buf(("xs" + lv).c_str(), (size_t)Cs * Rm);
-            float *xst = c.buf(("xst" + lv).c_str(), (size_t)Cs * Rm);
-            float *acc = c.buf(("acc" + lv).c_str(), (size_t)Cs * Rm);
-            float *xb = c.buf(("xb" + lv).c_str(), (size_t)Cs * Rm);
-            float *tmp = c.buf(("tmp" + lv).c_str(), (size_t)Cs * Rm);
-            float *op = c.buf(("op" + lv).c_str(), (size_t)Cs * Rm);
-            // noise branch: noise_convs + noise_res (audio_utils.cpp:714-731)
-            conv_w(g + "noise_convs." + ss + ".weight", g + "noise_convs." + ss + ".bias", har, R_har, 22,
-                   sp[s].noise_kernel, sp[s].noise_stride, sp[s].noise_padding, 1, xs, Rm, Rm, Epi{},
-                   sum_len(m, extra[s]));
-            gen_resblock(g + "noise_res." + ss, sp[s].kernel, xs, xs, nullptr, 0, 1.f, Cs, m, extra[s], op, tmp);
+            float *xs = c.buf(("xs" + ss).c_str(), (size_t)Cs * Rm);
+            float *xst = c.buf(("xst" + ss).c_str(), (size_t)Cs * Rm);
+            float *acc = c.buf(("acc" + ss).c_str(), (size_t)Cs * Rm);
+            float *xb = c.buf(("xb" + ss).c_str(), (size_t)Cs * Rm);
+            float *tmp = c.buf(("tmp" + ss).c_str(), (size_t)Cs * Rm);
+            Op o = op(s == 0 ? "op0" : "op1", m, Cs);
+            // noise branch: noise_convs + noise_res (audio_utils.cpp:714-731).
+            // The 22-channel input does not fill a tensor-core tile: CUDA cores.
+            {
+                Epi e;
+                e.bias = &c.W(g + "noise_convs." + ss + ".bias");
+                e.valid = sum_len(m, extra[s]);
+                const int K = sp[s].noise_kernel;
+                if (ncw.n != (int64_t)Cs * 22 * K) throw KKError(KK_ERROR_MODEL, "noise_convs shape mismatch");
+                conv_f32(ncw.d, ncw.f16, Cs, har, R_har, 22, K, sp[s].noise_stride, sp[s].noise_padding, 1, xs, Rm,
+                         Rm, e);
+            }
+            gen_resblock(g + "noise_res." + ss, sp[s].kernel, xs, xs, nullptr, 0, 1.f, Cs, m, extra[s], o, tmp);
             // LeakyReLU(0.1) then ConvTranspose as phase convolutions,
             // + bias, [reflect pad], + noise branch (audio_utils.cpp:687-760)
             const int64_t Rp = R(m_prev);
-            float *opp = s == 0 ? c.buf("op2", 1090 * (size_t)R(gm)) : c.buf("op0", (size_t)256 * R(10 * gm));
-            act_only(x, opp, Rp, C, m_prev, 0, 0.1f);
+            act_only(x, op_prev, Rp, C, m_prev, 0, ACT_LEAKY, 0.1f);
             const DevTensor &uw = c.W(g + "ups." + ss + ".weight");
             const DevTensor &ub = c.W(g + "ups." + ss + ".bias");
             if ((int)uw.ne[1] != Cs || (int)uw.ne[2] != C) throw KKError(KK_ERROR_MODEL, "ups shape mismatch");
@@ -584,12 +766,18 @@ struct Runner {
                 e.omul = S;
                 e.oadd = r - crop + pad;
                 e.valid = sum_len(m_prev, 0);
-                conv((const float *)c.convt_phase[s].p + (size_t)r * Cs * C * 2, c.convt_f16[s], Cs, opp, Rp, C, 2, 1,
-                     1, 1, xst, Rm, Rp, e);
+                if (tc) {
+                    const PackedW &pw = c.packed.at("ups." + ss + ".phase." + std::to_string(r));
+                    conv_h(pw, op_prev, 2, 1, 1, xst, Rm, Rp, e);
+                } else {
+                    conv_f32((const float *)c.convt_phase[s].p + (size_t)r * Cs * C * 2, c.convt_f16[s], Cs,
+                             op_prev.f, Rp, C, 2, 1, 1, 1, xst, Rm, Rp, e);
+                }
             }
             if (pad) {
                 ConvTRow0Args a{};
-                a.in = opp;
+                a.in = op_prev.f;
+                a.in_h = op_prev.h;
                 a.R_in = Rp;
                 a.IC = C;
                 a.m_in = m_prev;
@@ -604,42 +792,38 @@ struct Runner {
                 a.R_out = Rm;
                 a.round16 = uw.f16 ? 1 : 0;
                 convt_row0(a, B, st);
-        ++c.n_launches;
+                ++c.n_launches;
             }
             // three main resblocks, averaged (graph_ops.cpp:1300-1320)
             for (int k = 0; k < 3; ++k) {
                 const std::string pf = g + "resblocks." + std::to_string(s * 3 + k);
                 float *wb = k == 0 ? acc : xb;
                 gen_resblock(pf, kKs[k], xst, wb, acc, k == 0 ? 0 : 1, k == 2 ? 1.0f / 3.0f : 1.f, Cs, m, extra[s],
-                             op, tmp);
+                             o, tmp);
             }
             x = acc;
             C = Cs;
             m_prev = m;
+            op_prev = o;
         }
         // LeakyReLU(0.01) -> conv_post -> iSTFT (audio_utils.cpp:814-831, :1043)
         const int m = mlev[1];
         const int64_t Rm = R(m);
-        float *op = c.buf("op1", (size_t)128 * Rm);
-        act_only(x, op, Rm, C, m, 1, 0.01f);
+        act_only(x, op_prev, Rm, C, m, 1, ACT_LEAKY, 0.01f);
         float *post = c.buf("post", (size_t)22 * Rm);
-        conv_w(g + "conv_post.weight", g + "conv_post.bias", op, Rm, C, 7, 1, 3, 1, post, Rm, Rm, Epi{},
+        conv_w(g + "conv_post.weight", g + "conv_post.bias", op_prev, C, 7, 3, 1, post, Rm, Rm, Epi{},
                sum_len(m, 1));
         const IstftTables *it = (const IstftTables *)((char *)c.d_tables.p + sizeof(StftTables));
         istft(post, Rm, 60 * gm, audio, B, d_cum, it, P.maxT, st);
         ++c.n_launches;
     }
 
-    // memset every operand buffer whose gaps must read as zero
+    // zero every operand buffer whose gaps must read as zero
     void zero_operands(int gm, bool decoder) {
-        auto z = [&](const char *n, size_t floats) {
-            float *p = c.buf(n, floats);
-            check_cuda(cudaMemsetAsync(p, 0, floats * sizeof(float), st), "memset");
-        };
-        if (decoder) z("opT", 1090 * (size_t)R(1));
-        z("op2", 1090 * (size_t)R(gm));
-        z("op0", 256 * (size_t)R(10 * gm));
-        z("op1", 128 * (size_t)R(60 * gm));
+        if (decoder) zero(op("opT", 1, 1152), 1152);
+        zero(op("op2", gm, 1152), 1152);
+        zero(op("op0", 10 * gm, 256), 256);
+        zero(op("op1", 60 * gm, 128), 128);
     }
 
     // harmonic source + STFT on the side stream, from the packed F0 (level mf)
@@ -671,22 +855,28 @@ struct Runner {
         check_cuda(cudaMemsetAsync(np, 0, (size_t)R2 * 4, st), "memset");
         zero_operands(2, true);
         scatter(asr, Xenc, R1, 512, 1, 0, B, d_cum, P.maxT, st);
-        ++c.n_launches;
         scatter(f0, f0p, R2, 1, 2, 0, B, d_cum, 2 * P.maxT, st);
-        ++c.n_launches;
         scatter(noise, np, R2, 1, 2, 0, B, d_cum, 2 * P.maxT, st);
-        ++c.n_launches;
+        c.n_launches += 3;
         float *har = source_and_har(f0p, 2);
         setup_adain(style);
         const std::string d = "kokopop.decoder.";
         const DevTensor &f0w = c.W(d + "F0_conv.weight"), &f0b = c.W(d + "F0_conv.bias");
         const DevTensor &nw = c.W(d + "N_conv.weight"), &nb = c.W(d + "N_conv.bias");
         f0n_conv(f0p, R2, Xenc + 512 * R1, Xdec + 1088 * R1, R1, f0w.d, f0b.d, B, P.maxT, st);
-        ++c.n_launches;
         f0n_conv(np, R2, Xenc + 513 * R1, Xdec + 1089 * R1, R1, nw.d, nb.d, B, P.maxT, st);
-        ++c.n_launches;
-        conv_w(d + "asr_res.0.weight", d + "asr_res.0.bias", Xenc, R1, 512, 1, 1, 0, 1, Xdec + 1024 * R1, R1, R1,
-               Epi{}, sum_len(1, 0));
+        c.n_launches += 2;
+        // asr_res: 1x1 conv 512 -> 64 on the raw asr features
+        Op a_in;
+        if (tc) {
+            a_in = op("opT", 1, 1152);
+            act_only(Xenc, a_in, R1, 512, 1, 0, ACT_NONE, 0.f);
+        } else {
+            a_in.f = Xenc;
+            a_in.R = R1;
+        }
+        conv_w(d + "asr_res.0.weight", d + "asr_res.0.bias", a_in, 512, 1, 0, 1, Xdec + 1024 * R1, R1, R1, Epi{},
+               sum_len(1, 0));
         adain_resblk(d + "encode", Xenc, 514, false, Xdec);
         for (int i = 0; i < 3; ++i) adain_resblk(d + "decode." + std::to_string(i), Xdec, 1090, false, Xdec);
         float *dec = c.buf("dec_out", 512 * (size_t)R2);
@@ -704,9 +894,8 @@ struct Runner {
         check_cuda(cudaMemsetAsync(f0p, 0, (size_t)R1 * 4, st), "memset");
         zero_operands(1, false);
         scatter(decoder, dec, R1, 512, 1, 0, B, d_cum, P.maxT, st);
-        ++c.n_launches;
         scatter(f0, f0p, R1, 1, 1, 0, B, d_cum, P.maxT, st);
-        ++c.n_launches;
+        c.n_launches += 2;
         float *har = source_and_har(f0p, 1);
         setup_adain(style);
         check_cuda(cudaStreamWaitEvent(st, c.ev_src, 0), "wait source");
@@ -731,6 +920,18 @@ int guarded(F &&f) noexcept {
 }
 
 void use_device(kk_ctx *ctx) { check_cuda(cudaSetDevice(ctx->device), "cudaSetDevice"); }
+
+// After a synchronising call: surfaces a bounded-wait expiry recorded by the
+// tensor-core kernel (and clears it).
+void check_device_error(kk_ctx *ctx) {
+    if (!ctx->d_err.p) return;
+    int e = 0;
+    check_cuda(cudaMemcpy(&e, ctx->d_err.p, sizeof e, cudaMemcpyDeviceToHost), "read device status");
+    if (e != 0) {
+        cudaMemset(ctx->d_err.p, 0, sizeof(int));
+        throw KKError(KK_ERROR_INFERENCE, "tensor-core convolution timed out waiting (code " + std::to_string(e) + ")");
+    }
+}
 
 }  // namespace
 
@@ -865,6 +1066,7 @@ int kk_decoder_forward(kk_ctx *ctx, int32_t n_utts, const int32_t *n_frames, con
         check_cuda(cudaGetLastError(), "kernel launch");
         check_cuda(cudaMemcpyAsync(audio, d_audio, 600 * tot * 4, cudaMemcpyDeviceToHost, st), "D2H");
         check_cuda(cudaStreamSynchronize(st), "decoder forward");
+        check_device_error(ctx);
         return KK_OK;
     });
 }
@@ -892,6 +1094,7 @@ int kk_generator_forward(kk_ctx *ctx, int32_t n_utts, const int32_t *n_decoder_f
         check_cuda(cudaGetLastError(), "kernel launch");
         check_cuda(cudaMemcpyAsync(audio, d_audio, 300 * tot * 4, cudaMemcpyDeviceToHost, st), "D2H");
         check_cuda(cudaStreamSynchronize(st), "generator forward");
+        check_device_error(ctx);
         return KK_OK;
     });
 }

@@ -38,6 +38,14 @@ struct DevBuf {
     void release();
 };
 
+// A convolution weight packed for the tensor-core kernel: half,
+// [K][IC_pad/64][n_tiles][8][128][8] (the shared-memory image of each
+// (tap, 64-channel block, 128-channel tile)).
+struct PackedW {
+    DevBuf buf;
+    int IC = 0, IC_pad = 0, OC = 0, K = 0, n_tiles = 0;
+};
+
 struct SiteInfo {
     std::string prefix;
     int C = 0;
@@ -74,6 +82,10 @@ struct kk_ctx {
     std::string missing;
     kk::DevBuf convt_phase[2];
     bool convt_f16[2] = {false, false};
+    // tensor-core path: every convolution weight is F16
+    bool tc_mode = false;
+    std::unordered_map<std::string, kk::PackedW> packed;
+    kk::DevBuf d_err;  // device-side error code of the tensor-core kernel
     kk::SineArgs sine{};
     std::vector<kk::SiteInfo> sites;
     std::unordered_map<std::string, int> site_index;

@@ -197,8 +197,13 @@ __global__ void k_convt_row0(ConvTRow0Args a, Batch b) {
     const int k = 1 + a.crop;
     float acc = 0.f;
     for (int ic = 0; ic < a.IC; ++ic) {
-        float x = a.in[(int64_t)ic * a.R_in + in_row];
-        if (a.round16) x = round_f16(x);
+        float x;
+        if (a.in_h) {
+            x = __half2float(a.in_h[(((int64_t)(ic >> 3)) * a.R_in + in_row) * 8 + (ic & 7)]);
+        } else {
+            x = a.in[(int64_t)ic * a.R_in + in_row];
+            if (a.round16) x = round_f16(x);
+        }
         acc += x * a.w[((int64_t)ic * a.OC + oc) * a.K + k];
     }
     float v = __fadd_rn(acc, a.bias[oc]);
@@ -209,6 +214,112 @@ __global__ void k_convt_row0(ConvTRow0Args a, Batch b) {
 
 void convt_row0(const ConvTRow0Args &a, const Batch &b, cudaStream_t st) {
     k_convt_row0<<<dim3((a.OC + 127) / 128, b.n), 128, 0, st>>>(a, b);
+}
+
+// Half chunk-major variant of the prologue, the operand of the tensor-core
+// convolution: each thread produces the 8 channels of one row as one 16-byte
+// store at y[(c/8 * R + row) * 8 + c%8]. Same arithmetic as k_prologue, then
+// the round-to-nearest-even to half that ggml's F16 im2col applies.
+__global__ void __launch_bounds__(256) k_prologue_h(const float *__restrict__ x, __half *__restrict__ y,
+                                                    int64_t R, int C, int m, int extra, Batch b,
+                                                    PrologueArgs a) {
+    const int u = blockIdx.z, ch = blockIdx.y;
+    const int64_t len = (int64_t)m * b.T[u] + extra;
+    const int64_t row0 = (int64_t)m * b.offT[u];
+    float mean[8], scale[8], nw[8], nb[8], g[8], be[8], al[8], ia[8];
+    bool live[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        const int c = ch * 8 + e;
+        live[e] = c < C;
+        mean[e] = 0.f, scale[e] = 1.f, nw[e] = 1.f, nb[e] = 0.f, g[e] = 0.f, be[e] = 0.f, al[e] = 0.f, ia[e] = 0.f;
+        if (!live[e]) continue;
+        if (a.norm) {
+            const float2 s = a.ms[(int64_t)u * C + c];
+            mean[e] = s.x;
+            scale[e] = s.y;
+            nw[e] = a.norm_w[c];
+            nb[e] = a.norm_b[c];
+            g[e] = a.gamma[(int64_t)u * C + c];
+            be[e] = a.beta[(int64_t)u * C + c];
+        }
+        if (a.act == ACT_SNAKE) {
+            al[e] = a.alpha[c];
+            ia[e] = __fdiv_rn(1.0f, al[e]);
+        }
+    }
+    for (int64_t t = blockIdx.x * 256 + threadIdx.x; t < len; t += (int64_t)gridDim.x * 256) {
+        const int64_t row = row0 + t;
+        __align__(16) __half h[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            float v = 0.f;
+            if (live[e]) {
+                v = x[(int64_t)(ch * 8 + e) * R + row];
+                if (a.norm) {
+                    v = __fmul_rn(__fsub_rn(v, mean[e]), scale[e]);
+                    v = __fadd_rn(__fmul_rn(v, nw[e]), nb[e]);
+                    v = __fadd_rn(v, __fmul_rn(v, g[e]));
+                    v = __fadd_rn(v, be[e]);
+                }
+                if (a.act == ACT_LEAKY) {
+                    v = leaky(v, a.slope);
+                } else if (a.act == ACT_SNAKE) {
+                    const float sn = sinf(__fmul_rn(v, al[e]));
+                    v = __fadd_rn(v, __fmul_rn(__fmul_rn(sn, sn), ia[e]));
+                }
+            }
+            h[e] = __float2half_rn(v);
+        }
+        *reinterpret_cast<uint4 *>(y + ((int64_t)ch * R + row) * 8) = *reinterpret_cast<const uint4 *>(h);
+    }
+}
+
+void prologue_h(const float *x, __half *y, int64_t R, int C, int m, int extra, const Batch &b, int max_len,
+                const PrologueArgs &a, cudaStream_t st) {
+    int bx = (max_len + 255) / 256;
+    if (bx > 32) bx = 32;
+    k_prologue_h<<<dim3(bx, (C + 7) / 8, b.n), 256, 0, st>>>(x, y, R, C, m, extra, b, a);
+}
+
+// Depthwise x2 pool (see k_pool_up) written as the half chunk-major operand
+// of the following F16 convolution (its input is rounded to half there).
+__global__ void k_pool_up_h(const float *__restrict__ x, __half *__restrict__ y, int64_t R_in, int64_t R_out,
+                            int C, const float *__restrict__ w, const float *__restrict__ bias, Batch b) {
+    const int u = blockIdx.z, ch = blockIdx.y;
+    const int64_t L = b.T[u];
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < 2 * L;
+         t += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t j = t + 1;
+        __align__(16) __half h[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const int c = ch * 8 + e;
+            float v = 0.f;
+            if (c < C) {
+                const float *xp = x + (int64_t)c * R_in + b.offT[u];
+                float acc = 0.f;
+                const int64_t q = j >> 1;
+                if (j & 1) {
+                    if (q < L) acc = __fadd_rn(acc, __fmul_rn(w[c * 3 + 1], xp[q]));
+                } else {
+                    if (q - 1 >= 0 && q - 1 < L) acc = __fadd_rn(acc, __fmul_rn(w[c * 3 + 2], xp[q - 1]));
+                    if (q < L) acc = __fadd_rn(acc, __fmul_rn(w[c * 3 + 0], xp[q]));
+                }
+                v = __fadd_rn(acc, bias[c]);
+            }
+            h[e] = __float2half_rn(v);
+        }
+        *reinterpret_cast<uint4 *>(y + ((int64_t)ch * R_out + 2 * b.offT[u] + t) * 8) =
+            *reinterpret_cast<const uint4 *>(h);
+    }
+}
+
+void pool_up_h(const __half *, const float *x, __half *y, int64_t R_in, int64_t R_out, int C, const float *w,
+               const float *bias, const Batch &b, int max_T, cudaStream_t st) {
+    int bx = (2 * max_T + 255) / 256;
+    if (bx > 16) bx = 16;
+    k_pool_up_h<<<dim3(bx, (C + 7) / 8, b.n), 256, 0, st>>>(x, y, R_in, R_out, C, w, bias, b);
 }
 
 // ---------------------------------------------------------------------------

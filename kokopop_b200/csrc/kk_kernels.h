@@ -58,7 +58,8 @@ struct ConvArgs {
 };
 
 struct ConvTRow0Args {
-    const float *in;
+    const float *in;      // F32 [C][R] operand, or
+    const __half *in_h;   // half chunk-major operand (when non-null)
     int64_t R_in;
     int IC, m_in;
     const float *w;  // ggml [K, OC, IC]
@@ -114,5 +115,40 @@ void istft(const float *post, int64_t R, int a_nf, float *audio, const Batch &b,
 // kk_conv_simt.cu
 void conv_simt(const ConvArgs &a, cudaStream_t st);
 cudaError_t conv_simt_init();
+
+// kk_conv_tc.cu: tensor-core convolution, stride 1, half operands.
+// in: chunk-major half [IC_pad/8][R_in][8]; w: packed half
+// [K][IC_pad/64][n_tiles][8][128][8]; epilogue as ConvArgs.
+struct ConvTcArgs {
+    const __half *in;
+    int64_t R_in;
+    int IC_pad;
+    const __half *w;
+    int n_tiles;
+    int OC, K, p, d;
+    float *out;
+    int64_t R_out;
+    int64_t n_pos;
+    int64_t omul, oadd;
+    const float *bias;
+    const float *resid;
+    int64_t R_resid;
+    int resid_half;
+    float scale1;
+    int accum;
+    float scale2;
+    int *err;
+};
+cudaError_t conv_tc_init();
+cudaError_t conv_tc(const ConvTcArgs &a, cudaStream_t st);
+int conv_tc_max_halo();
+
+// Half-precision chunk-major operands for the tensor-core path.
+// prologue_h: y[c/8][row][c%8] = half(act(adain(x[c][row]))) on valid rows.
+void prologue_h(const float *x, __half *y, int64_t R, int C, int m, int extra, const Batch &b, int max_len,
+                const PrologueArgs &a, cudaStream_t st);
+// pool_up_h: the depthwise x2 pool written as a half chunk-major operand.
+void pool_up_h(const __half *x_unused, const float *x, __half *y, int64_t R_in, int64_t R_out, int C,
+               const float *w, const float *bias, const Batch &b, int max_T, cudaStream_t st);
 
 }  // namespace kk
