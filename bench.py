@@ -179,11 +179,11 @@ def reference_arm(args):
     return 0
 
 
-def config_dict():
+def config_dict(batch=BATCH):
     return {
         "workload": "Kokoro-82M decoder (AdainResBlk1d encode/decode) + ISTFTNet generator + iSTFT; "
-                    "256 utterances T~U[40,800] asr frames, F16 weights seed 2, batch 64 per GPU",
-        "batch_per_gpu": BATCH, "pool": POOL, "weights": "F16 (converter policy), N(0,0.02), seed 2",
+                    f"256 utterances T~U[40,800] asr frames, F16 weights seed 2, batch {batch} per GPU",
+        "batch_per_gpu": batch, "pool": POOL, "weights": "F16 (converter policy), N(0,0.02), seed 2",
         "l2": "no flush: per-step working set (activations ~15 GB) is >100x the 126 MB L2",
     }
 
@@ -195,7 +195,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--ttfa-runs", type=int, default=50)
+    ap.add_argument("--ttfa-runs", type=int, default=50, help="0 skips the TTFA measurement")
+    ap.add_argument("--batch", type=int, default=BATCH, help="utterances per GPU step (profiling cases)")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg (profiling cases)")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
@@ -218,7 +220,7 @@ def main():
     weights = W.config2_weights()
     ctx = kb.Context(local)
     ctx.upload(weights)
-    batches = rank_batches(POOL, rank, world, BATCH)
+    batches = rank_batches(POOL, rank, world, args.batch)
     dev = []
     host = []
     for idx in batches:
@@ -308,23 +310,25 @@ def main():
     value = secs_all / t_max
 
     # ---- end to end through the host-buffer C ABI (pinned host memory) ----
-    for k in range(min(args.warmup, 2)):
-        step_host(k)
-    barrier()
-    t0 = time.perf_counter()
-    e2e_secs = 0.0
-    for k in range(args.steps):
-        e2e_secs += step_host(k)
-    e2e_t = time.perf_counter() - t0
-    barrier()
-    e2e_value = sum_over_ranks(e2e_secs) / max_over_ranks(e2e_t)
+    e2e_value = None
+    if not args.no_e2e:
+        for k in range(min(args.warmup, 2)):
+            step_host(k)
+        barrier()
+        t0 = time.perf_counter()
+        e2e_secs = 0.0
+        for k in range(args.steps):
+            e2e_secs += step_host(k)
+        e2e_t = time.perf_counter() - t0
+        barrier()
+        e2e_value = sum_over_ranks(e2e_secs) / max_over_ranks(e2e_t)
     tot_frames = [int(h["n"].sum()) for h in host]
-    h2d = statistics.mean([(512 + 2 + 2) * 4 * f + 4 * 128 * BATCH + 4 * BATCH for f in tot_frames])
+    h2d = statistics.mean([(512 + 2 + 2) * 4 * f + 4 * 128 * args.batch + 4 * args.batch for f in tot_frames])
     d2h = statistics.mean([600 * 4 * f for f in tot_frames])
 
     ttfa = None
     cpu = None
-    if rank == 0:
+    if rank == 0 and args.ttfa_runs > 0:
         # p50 time to first audio: one config-0 utterance (T=200, F32 weights
         # seed 0), submitted alone on an idle GPU, until its samples are in
         # host memory; the whole utterance is returned in one piece.
@@ -340,6 +344,7 @@ def main():
             lat.append(time.perf_counter() - t)
         ttfa = 1e3 * statistics.median(lat)
         c0.close()
+    if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
             sample = cpu_sample(pool)
             s_audio, s_wall, thr = run_cpu_oracle(weights, sample)
@@ -354,8 +359,9 @@ def main():
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * t_max / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": config_dict(),
-        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
+        "config": config_dict(args.batch),
+        "e2e": ({"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)}
+                if e2e_value is not None else None),
         "roofline": {"bound": "tensor", "kernel": "dense conv (all conv launches of a step)",
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak if peak else None, "traffic": None,

@@ -39,6 +39,22 @@ __device__ __forceinline__ float leaky(float x, float slope) {
     return __fadd_rn(x > 0.f ? x : 0.f, __fmul_rn(slope, x < 0.f ? x : 0.f));
 }
 
+// sin for the Snake activation. Its arguments v * alpha are small in
+// practice, where the odd Taylor polynomial of sin to x^9 (Horner in x^2)
+// is accurate to float rounding: the first omitted term x^11/11! is below
+// 3e-9 relative for |x| <= pi/4. Larger arguments take the library sinf.
+__device__ __forceinline__ float snake_sin(float x) {
+    if (fabsf(x) <= 0.78539816f) {
+        const float x2 = x * x;
+        float p = 2.7557319e-06f;         // 1/9!
+        p = fmaf(p, x2, -1.9841270e-04f);  // -1/7!
+        p = fmaf(p, x2, 8.3333333e-03f);   // 1/5!
+        p = fmaf(p, x2, -1.6666667e-01f);  // -1/3!
+        return fmaf(x * x2, p, x);
+    }
+    return sinf(x);
+}
+
 template <typename T>
 __device__ __forceinline__ T warp_sum(T v) {
 #pragma unroll

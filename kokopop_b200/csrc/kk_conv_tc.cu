@@ -19,11 +19,12 @@
 //      (tap, 64-channel block, 128-channel tile): [8 chunks][128 oc][16 B],
 //      fetched with one bulk copy.
 //
-// Roles (128 threads): warp 0 lane 0 issues the copies, warp 1 allocates
-// tensor memory and lane 0 issues tcgen05.mma, then all four warps drain the
-// accumulator (tcgen05.ld 32x32b: warp w owns TMEM lanes 32w..32w+31) through
-// the epilogue. Every mbarrier wait is bounded in time; on expiry the kernel
-// records an error code and skips the rest of its work.
+// Roles (192 threads, persistent over tiles): warp 0 lane 0 issues the
+// copies, warp 1 allocates tensor memory (two 128-column accumulators) and
+// lane 0 issues tcgen05.mma, warps 2-5 drain the other accumulator through
+// the epilogue (tcgen05.ld 32x32b: warp w owns TMEM lanes 32 (w % 4) ...).
+// Every mbarrier wait is bounded in time; on expiry the kernel records an
+// error code and the waiting role stops.
 #include "kk_kernels.h"
 
 #include <cuda.h>
@@ -39,6 +40,7 @@ constexpr int TC_B_BYTES = 8 * TC_BN * 16;       // 16 KB
 constexpr int TC_NSA = 2;                        // A slab stages
 constexpr int TC_NSB = 3;                        // B tile stages
 constexpr int TC_SMEM = TC_NSA * TC_A_BYTES + TC_NSB * TC_B_BYTES + 1024 /*barriers*/ + 1024 /*align*/;
+constexpr int TC_CTAS_PER_SM = 2;  // 2 x 98 KB shared memory, 2 x 256 TMEM columns
 constexpr unsigned long long TC_WAIT_NS = 2000000000ull;  // 2 s
 
 // ---------------------------------------------------------------------------
@@ -164,6 +166,8 @@ struct TcParams {
     int BR;          // slab rows = 127 + (K - 1) d + 1
     int OC;          // real output channels
     int n_tiles;     // OC tiles of 128 in the packed weights
+    int n_oc_tiles;  // OC tiles computed
+    int64_t m_tiles; // position tiles of 128
     const __half *w; // packed [K][IC_blocks][n_tiles][8][128][8]
     float *out;
     int64_t R_out;
@@ -179,22 +183,26 @@ struct TcParams {
     int *err;
 };
 
-__global__ void __launch_bounds__(128) k_conv_tc(const __grid_constant__ CUtensorMap amap, TcParams P) {
+// Persistent: CTA i takes tiles i, i + grid, ... (OC tile fastest, so the
+// CTAs working on one slab of positions run close together and share it in
+// L2). Warp 0 lane 0: copies. Warp 1: TMEM owner, lane 0 issues MMAs into
+// one of two accumulators (128 columns each) so the epilogue of a tile
+// overlaps the MMAs of the next. Warps 2-5: epilogue (warp w reads TMEM lanes
+// 32 (w % 4) ...).
+__global__ void __launch_bounds__(192, 2) k_conv_tc(const __grid_constant__ CUtensorMap amap, TcParams P) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t *sA = smem;
     uint8_t *sB = smem + TC_NSA * TC_A_BYTES;
     uint64_t *bars = (uint64_t *)(sB + TC_NSB * TC_B_BYTES);
-    // bars: A_full[2], A_empty[2], B_full[3], B_empty[3], acc_full, tmem slot
+    // A_full[2] A_empty[2] B_full[NSB] B_empty[NSB] acc_full[2] acc_empty[2] tmem slot
     const uint32_t bA_full = smem_u32(bars + 0), bA_empty = smem_u32(bars + 2);
-    const uint32_t bB_full = smem_u32(bars + 4), bB_empty = smem_u32(bars + 7);
-    const uint32_t b_acc = smem_u32(bars + 10);
-    uint32_t *tmem_slot = (uint32_t *)(bars + 11);
+    const uint32_t bB_full = smem_u32(bars + 4), bB_empty = smem_u32(bars + 4 + TC_NSB);
+    const uint32_t bAcc_full = smem_u32(bars + 4 + 2 * TC_NSB), bAcc_empty = smem_u32(bars + 6 + 2 * TC_NSB);
+    uint32_t *tmem_slot = (uint32_t *)(bars + 8 + 2 * TC_NSB);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t q0 = (int64_t)blockIdx.x * TC_BM;
-    const int nt = blockIdx.y;
-    const int n0 = nt * TC_BN;
+    const int64_t n_tiles_total = P.m_tiles * P.n_oc_tiles;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < TC_NSA; ++i) {
@@ -205,12 +213,15 @@ __global__ void __launch_bounds__(128) k_conv_tc(const __grid_constant__ CUtenso
             mbar_init(bB_full + 8 * i, 1);
             mbar_init(bB_empty + 8 * i, 1);
         }
-        mbar_init(b_acc, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(bAcc_full + 8 * i, 1);
+            mbar_init(bAcc_empty + 8 * i, 4);  // one arrive per epilogue warp
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(TC_BN)
+                     "r"(2 * TC_BN)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -219,7 +230,6 @@ __global__ void __launch_bounds__(128) k_conv_tc(const __grid_constant__ CUtenso
     fence_after_sync();
     const uint32_t tmem = *tmem_slot;
 
-    const int n_iter = P.IC_blocks * P.K;
     const uint32_t a_bytes = 8u * (uint32_t)P.BR * 16u;
     const uint32_t lbo_a = (uint32_t)P.BR * 16u;
     const uint32_t lbo_b = (uint32_t)TC_BN * 16u;
@@ -227,25 +237,27 @@ __global__ void __launch_bounds__(128) k_conv_tc(const __grid_constant__ CUtenso
     if (warp == 0) {
         if (lane == 0) {
             // producer
-            const int row0 = (int)(q0 - P.p);
             bool ok = true;
-            for (int b = 0; b < P.IC_blocks && ok; ++b) {
-                const int sa = b % TC_NSA;
-                const uint32_t ua = (uint32_t)(b / TC_NSA);
-                if (b >= TC_NSA) ok = mbar_wait(bA_empty + 8 * sa, (ua & 1) ^ 1, P.err, 11);
-                if (!ok) break;
-                mbar_expect_tx(bA_full + 8 * sa, a_bytes);
-                tma_load_3d(smem_u32(sA + sa * TC_A_BYTES), &amap, bA_full + 8 * sa, 0, row0, 8 * b);
-                for (int k = 0; k < P.K; ++k) {
-                    const int j = b * P.K + k;
-                    const int sb = j % TC_NSB;
-                    const uint32_t ub = (uint32_t)(j / TC_NSB);
-                    if (j >= TC_NSB) ok = mbar_wait(bB_empty + 8 * sb, (ub & 1) ^ 1, P.err, 12);
+            uint32_t ia = 0, ib = 0;  // running slab / tile counters
+            for (int64_t tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x) {
+                const int64_t mt = tile / P.n_oc_tiles;
+                const int nt = (int)(tile % P.n_oc_tiles);
+                const int row0 = (int)(mt * TC_BM - P.p);
+                for (int b = 0; b < P.IC_blocks && ok; ++b, ++ia) {
+                    const int sa = ia % TC_NSA;
+                    if (ia >= TC_NSA) ok = mbar_wait(bA_empty + 8 * sa, ((ia / TC_NSA) & 1) ^ 1, P.err, 11);
                     if (!ok) break;
-                    mbar_expect_tx(bB_full + 8 * sb, TC_B_BYTES);
-                    const __half *src =
-                        P.w + ((((size_t)k * P.IC_blocks + b) * P.n_tiles + nt) * (size_t)(8 * TC_BN * 8));
-                    bulk_load(smem_u32(sB + sb * TC_B_BYTES), src, TC_B_BYTES, bB_full + 8 * sb);
+                    mbar_expect_tx(bA_full + 8 * sa, a_bytes);
+                    tma_load_3d(smem_u32(sA + sa * TC_A_BYTES), &amap, bA_full + 8 * sa, 0, row0, 8 * b);
+                    for (int k = 0; k < P.K; ++k, ++ib) {
+                        const int sb = ib % TC_NSB;
+                        if (ib >= TC_NSB) ok = mbar_wait(bB_empty + 8 * sb, ((ib / TC_NSB) & 1) ^ 1, P.err, 12);
+                        if (!ok) break;
+                        mbar_expect_tx(bB_full + 8 * sb, TC_B_BYTES);
+                        const __half *src =
+                            P.w + ((((size_t)k * P.IC_blocks + b) * P.n_tiles + nt) * (size_t)(8 * TC_BN * 8));
+                        bulk_load(smem_u32(sB + sb * TC_B_BYTES), src, TC_B_BYTES, bB_full + 8 * sb);
+                    }
                 }
             }
         }
@@ -255,80 +267,99 @@ __global__ void __launch_bounds__(128) k_conv_tc(const __grid_constant__ CUtenso
             // MMA issuer
             const uint32_t idesc = idesc_f16(TC_BM, TC_BN);
             bool ok = true;
-            uint32_t acc = 0;
-            for (int b = 0; b < P.IC_blocks && ok; ++b) {
-                const int sa = b % TC_NSA;
-                const uint32_t ua = (uint32_t)(b / TC_NSA);
-                ok = mbar_wait(bA_full + 8 * sa, ua & 1, P.err, 13);
+            uint32_t ia = 0, ib = 0, it = 0;
+            for (int64_t tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x, ++it) {
+                const int ab = it & 1;
+                if (it >= 2) ok = mbar_wait(bAcc_empty + 8 * ab, ((it >> 1) & 1) ^ 1, P.err, 17);
                 if (!ok) break;
                 fence_after_sync();
-                const uint32_t a_base = smem_u32(sA + sa * TC_A_BYTES);
-                for (int k = 0; k < P.K; ++k) {
-                    const int j = b * P.K + k;
-                    const int sb = j % TC_NSB;
-                    const uint32_t ub = (uint32_t)(j / TC_NSB);
-                    ok = mbar_wait(bB_full + 8 * sb, ub & 1, P.err, 14);
+                const uint32_t d_tmem = tmem + (uint32_t)(ab * TC_BN);
+                uint32_t acc = 0;
+                for (int b = 0; b < P.IC_blocks && ok; ++b, ++ia) {
+                    const int sa = ia % TC_NSA;
+                    ok = mbar_wait(bA_full + 8 * sa, (ia / TC_NSA) & 1, P.err, 13);
                     if (!ok) break;
                     fence_after_sync();
-                    const uint32_t b_base = smem_u32(sB + sb * TC_B_BYTES);
-                    const uint32_t a_tap = a_base + (uint32_t)(k * P.d) * 16u;
+                    const uint32_t a_base = smem_u32(sA + sa * TC_A_BYTES);
+                    for (int k = 0; k < P.K; ++k, ++ib) {
+                        const int sb = ib % TC_NSB;
+                        ok = mbar_wait(bB_full + 8 * sb, (ib / TC_NSB) & 1, P.err, 14);
+                        if (!ok) break;
+                        fence_after_sync();
+                        const uint32_t b_base = smem_u32(sB + sb * TC_B_BYTES);
+                        const uint32_t a_tap = a_base + (uint32_t)(k * P.d) * 16u;
 #pragma unroll
-                    for (int ks = 0; ks < 4; ++ks) {
-                        const uint64_t ad = sdesc(a_tap + (uint32_t)(2 * ks) * lbo_a, lbo_a, 128);
-                        const uint64_t bd = sdesc(b_base + (uint32_t)(2 * ks) * lbo_b, lbo_b, 128);
-                        mma_f16(tmem, ad, bd, idesc, acc);
-                        acc = 1;
+                        for (int ks = 0; ks < 4; ++ks) {
+                            const uint64_t ad = sdesc(a_tap + (uint32_t)(2 * ks) * lbo_a, lbo_a, 128);
+                            const uint64_t bd = sdesc(b_base + (uint32_t)(2 * ks) * lbo_b, lbo_b, 128);
+                            mma_f16(d_tmem, ad, bd, idesc, acc);
+                            acc = 1;
+                        }
+                        mma_commit(bB_empty + 8 * sb);
                     }
-                    mma_commit(bB_empty + 8 * sb);
+                    mma_commit(bA_empty + 8 * sa);
                 }
-                mma_commit(bA_empty + 8 * sa);
+                mma_commit(bAcc_full + 8 * ab);
             }
-            mma_commit(b_acc);
         }
         __syncwarp();
-    }
-    (void)n_iter;
-
-    // epilogue: all four warps; lane 0 waits so the decision is warp-uniform
-    // (tcgen05.ld is .sync.aligned)
-    int ok_lane = 0;
-    if (lane == 0) ok_lane = mbar_wait(b_acc, 0, P.err, 15) ? 1 : 0;
-    const bool acc_ok = __shfl_sync(0xffffffffu, ok_lane, 0) != 0;
-    fence_after_sync();
-    if (acc_ok) {
-        const int64_t q = q0 + warp * 32 + lane;
-        const int64_t orow = q * P.omul + P.oadd;
-        const bool row_ok = q < P.n_pos && orow >= 0 && orow < P.R_out;
-        const int64_t rrow = P.resid_half ? (orow >> 1) : orow;
-        for (int c0 = 0; c0 < TC_BN; c0 += 32) {
-            if (n0 + c0 >= P.OC) break;  // warp-uniform
-            uint32_t r[32];
-            tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, r);
-            if (!row_ok) continue;
+    } else {
+        // epilogue warps 2..5
+        const int lg = warp & 3;  // TMEM lane group
+        uint32_t it = 0;
+        for (int64_t tile = blockIdx.x; tile < n_tiles_total; tile += gridDim.x, ++it) {
+            const int64_t mt = tile / P.n_oc_tiles;
+            const int n0 = (int)(tile % P.n_oc_tiles) * TC_BN;
+            const int ab = it & 1;
+            int ok_lane = 0;
+            if (lane == 0) ok_lane = mbar_wait(bAcc_full + 8 * ab, (it >> 1) & 1, P.err, 15) ? 1 : 0;
+            if (__shfl_sync(0xffffffffu, ok_lane, 0) == 0) break;
+            fence_after_sync();
+            const int64_t q = mt * TC_BM + lg * 32 + lane;
+            const int64_t orow = q * P.omul + P.oadd;
+            const bool row_ok = q < P.n_pos && orow >= 0 && orow < P.R_out;
+            const int64_t rrow = P.resid_half ? (orow >> 1) : orow;
+            for (int c0 = 0; c0 < TC_BN; c0 += 32) {
+                if (n0 + c0 >= P.OC) break;  // warp-uniform
+                uint32_t r[32];
+                tmem_ld32(tmem + ((uint32_t)(lg * 32) << 16) + (uint32_t)(ab * TC_BN + c0), r);
+                if (!row_ok) continue;
+                // The residual and the accumulated output may alias the output
+                // (in-place updates): read all 32 of this row's values first so
+                // the loads overlap, then compute and store.
+                const int nj = P.OC - (n0 + c0) < 32 ? P.OC - (n0 + c0) : 32;
+                float res[32], old[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const int oc = n0 + c0 + j;
-                if (oc >= P.OC) break;
-                float v = __uint_as_float(r[j]);
-                if (P.bias) v = __fadd_rn(v, P.bias[oc]);
-                if (P.resid) v = __fadd_rn(P.resid[(int64_t)oc * P.R_resid + rrow], v);
-                if (P.scale1 != 1.0f) v = __fmul_rn(v, P.scale1);
-                float *o = P.out + (int64_t)oc * P.R_out + orow;
-                if (P.accum) v = __fadd_rn(*o, v);
-                if (P.scale2 != 1.0f) v = __fmul_rn(v, P.scale2);
-                *o = v;
+                for (int j = 0; j < 32; ++j) {
+                    const int oc = n0 + c0 + j;
+                    res[j] = (P.resid && j < nj) ? P.resid[(int64_t)oc * P.R_resid + rrow] : 0.f;
+                    old[j] = (P.accum && j < nj) ? P.out[(int64_t)oc * P.R_out + orow] : 0.f;
+                }
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    if (j >= nj) break;
+                    const int oc = n0 + c0 + j;
+                    float v = __uint_as_float(r[j]);
+                    if (P.bias) v = __fadd_rn(v, P.bias[oc]);
+                    if (P.resid) v = __fadd_rn(res[j], v);
+                    if (P.scale1 != 1.0f) v = __fmul_rn(v, P.scale1);
+                    if (P.accum) v = __fadd_rn(old[j], v);
+                    if (P.scale2 != 1.0f) v = __fmul_rn(v, P.scale2);
+                    P.out[(int64_t)oc * P.R_out + orow] = v;
+                }
             }
+            // hand the accumulator back to the MMA warp
+            fence_before_sync();
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bAcc_empty + 8 * ab) : "memory");
         }
     }
+
     fence_before_sync();
     __syncthreads();
-    if (threadIdx.x == 0 && !acc_ok) {
-        // make sure no copy is still landing in this CTA's shared memory
-        for (int i = 0; i < TC_NSA; ++i) mbar_wait(bA_full + 8 * i, 0, P.err, 16);
-    }
     if (warp == 1) {
         fence_after_sync();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_BN) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * TC_BN) : "memory");
     }
 }
 
@@ -337,6 +368,7 @@ __global__ void __launch_bounds__(128) k_conv_tc(const __grid_constant__ CUtenso
 // ---------------------------------------------------------------------------
 
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+static int g_num_sms = 148;
 
 cudaError_t conv_tc_init() {
     if (!g_encode) {
@@ -346,6 +378,8 @@ cudaError_t conv_tc_init() {
         if (e != cudaSuccess) return e;
         if (q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
         g_encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
+        int dev = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
     }
     return cudaFuncSetAttribute(k_conv_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
 }
@@ -386,9 +420,12 @@ cudaError_t conv_tc(const ConvTcArgs &a, cudaStream_t st) {
     P.accum = a.accum;
     P.scale2 = a.scale2;
     P.err = a.err;
-    const int n_oc_tiles = (a.OC + TC_BN - 1) / TC_BN;
-    dim3 grid((unsigned)((a.n_pos + TC_BM - 1) / TC_BM), n_oc_tiles);
-    k_conv_tc<<<grid, 128, TC_SMEM, st>>>(map, P);
+    P.n_oc_tiles = (a.OC + TC_BN - 1) / TC_BN;
+    P.m_tiles = (a.n_pos + TC_BM - 1) / TC_BM;
+    const int64_t tiles = P.m_tiles * P.n_oc_tiles;
+    const int64_t slots = (int64_t)g_num_sms * TC_CTAS_PER_SM;
+    const unsigned grid = (unsigned)(tiles < slots ? tiles : slots);
+    k_conv_tc<<<grid, 192, TC_SMEM, st>>>(map, P);
     return cudaGetLastError();
 }
 

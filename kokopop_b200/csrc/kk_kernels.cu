@@ -164,7 +164,7 @@ __global__ void __launch_bounds__(256) k_prologue(const float *__restrict__ x, f
         if (a.act == ACT_LEAKY) {
             v = leaky(v, a.slope);
         } else if (a.act == ACT_SNAKE) {
-            const float s = sinf(__fmul_rn(v, alpha));
+            const float s = snake_sin(__fmul_rn(v, alpha));
             v = __fadd_rn(v, __fmul_rn(__fmul_rn(s, s), inv_a));
         }
         if (a.round16) v = round_f16(v);
@@ -217,23 +217,24 @@ void convt_row0(const ConvTRow0Args &a, const Batch &b, cudaStream_t st) {
 }
 
 // Half chunk-major variant of the prologue, the operand of the tensor-core
-// convolution: each thread produces the 8 channels of one row as one 16-byte
-// store at y[(c/8 * R + row) * 8 + c%8]. Same arithmetic as k_prologue, then
-// the round-to-nearest-even to half that ggml's F16 im2col applies.
+// convolution: y[(c/8 * R + row) * 8 + c%8]. Same arithmetic as k_prologue,
+// then the round-to-nearest-even to half that ggml's F16 im2col applies.
+// A thread produces 4 consecutive rows x 8 channels: eight 16-byte loads
+// (one float4 per channel) and four contiguous 16-byte stores, so enough
+// bytes are in flight to stream at HBM rate. Rows of the 4-row group that
+// fall past the utterance are written as zero (they are gap rows).
 __global__ void __launch_bounds__(256) k_prologue_h(const float *__restrict__ x, __half *__restrict__ y,
                                                     int64_t R, int C, int m, int extra, Batch b,
                                                     PrologueArgs a) {
     const int u = blockIdx.z, ch = blockIdx.y;
     const int64_t len = (int64_t)m * b.T[u] + extra;
-    const int64_t row0 = (int64_t)m * b.offT[u];
+    const int64_t row0 = (int64_t)m * b.offT[u];  // a multiple of 4
     float mean[8], scale[8], nw[8], nb[8], g[8], be[8], al[8], ia[8];
-    bool live[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
         const int c = ch * 8 + e;
-        live[e] = c < C;
         mean[e] = 0.f, scale[e] = 1.f, nw[e] = 1.f, nb[e] = 0.f, g[e] = 0.f, be[e] = 0.f, al[e] = 0.f, ia[e] = 0.f;
-        if (!live[e]) continue;
+        if (c >= C) continue;
         if (a.norm) {
             const float2 s = a.ms[(int64_t)u * C + c];
             mean[e] = s.x;
@@ -248,14 +249,21 @@ __global__ void __launch_bounds__(256) k_prologue_h(const float *__restrict__ x,
             ia[e] = __fdiv_rn(1.0f, al[e]);
         }
     }
-    for (int64_t t = blockIdx.x * 256 + threadIdx.x; t < len; t += (int64_t)gridDim.x * 256) {
+    const int nc = C - ch * 8 < 8 ? C - ch * 8 : 8;
+    for (int64_t t = (blockIdx.x * 256 + threadIdx.x) * 4; t < len; t += (int64_t)gridDim.x * 256 * 4) {
         const int64_t row = row0 + t;
-        __align__(16) __half h[8];
+        float4 v4[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+            v4[e] = e < nc ? *reinterpret_cast<const float4 *>(x + (int64_t)(ch * 8 + e) * R + row)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+        __align__(16) __half h[4][8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-            float v = 0.f;
-            if (live[e]) {
-                v = x[(int64_t)(ch * 8 + e) * R + row];
+            const float in[4] = {v4[e].x, v4[e].y, v4[e].z, v4[e].w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float v = in[i];
                 if (a.norm) {
                     v = __fmul_rn(__fsub_rn(v, mean[e]), scale[e]);
                     v = __fadd_rn(__fmul_rn(v, nw[e]), nb[e]);
@@ -265,20 +273,23 @@ __global__ void __launch_bounds__(256) k_prologue_h(const float *__restrict__ x,
                 if (a.act == ACT_LEAKY) {
                     v = leaky(v, a.slope);
                 } else if (a.act == ACT_SNAKE) {
-                    const float sn = sinf(__fmul_rn(v, al[e]));
+                    const float sn = snake_sin(__fmul_rn(v, al[e]));
                     v = __fadd_rn(v, __fmul_rn(__fmul_rn(sn, sn), ia[e]));
                 }
+                if (e >= nc || t + i >= len) v = 0.f;
+                h[i][e] = __float2half_rn(v);
             }
-            h[e] = __float2half_rn(v);
         }
-        *reinterpret_cast<uint4 *>(y + ((int64_t)ch * R + row) * 8) = *reinterpret_cast<const uint4 *>(h);
+        uint4 *dst = reinterpret_cast<uint4 *>(y + ((int64_t)ch * R + row) * 8);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dst[i] = *reinterpret_cast<const uint4 *>(h[i]);
     }
 }
 
 void prologue_h(const float *x, __half *y, int64_t R, int C, int m, int extra, const Batch &b, int max_len,
                 const PrologueArgs &a, cudaStream_t st) {
-    int bx = (max_len + 255) / 256;
-    if (bx > 32) bx = 32;
+    int bx = (max_len + 1023) / 1024;
+    if (bx > 16) bx = 16;
     k_prologue_h<<<dim3(bx, (C + 7) / 8, b.n), 256, 0, st>>>(x, y, R, C, m, extra, b, a);
 }
 
