@@ -286,6 +286,27 @@ void kk_ctx::derive() {
             pack_tc(packed[cv.first], OC, IC, K,
                     [&](int oc, int ic, int k) { return h[((size_t)oc * IC + ic) * K + k]; });
         }
+        // noise_convs.1: 1x1 over the 22 har channels
+        {
+            const DevTensor &t = W("kokopop.decoder.generator.noise_convs.1.weight");
+            const int OC = (int)t.ne[1], IC = (int)t.ne[0];
+            h.resize((size_t)t.n);
+            check_cuda(cudaMemcpy(h.data(), t.d, h.size() * 4, cudaMemcpyDeviceToHost), "read noise conv");
+            pack_tc(packed["noise_convs.1"], OC, IC, 1, [&](int oc, int ic, int) { return h[(size_t)oc * IC + ic]; });
+        }
+        // noise_convs.0 (k=12, stride 6, pad 3) as 2 taps over the
+        // space-to-depth operand: channel r*22+ic, tap j <- W[oc][ic][6j + r]
+        {
+            const DevTensor &t = W("kokopop.decoder.generator.noise_convs.0.weight");
+            const int OC = (int)t.ne[1], K = 12, IC = (int)(t.ne[0] / K);
+            if (IC * K != (int)t.ne[0] || IC != 22) throw KKError(KK_ERROR_MODEL, "noise_convs.0 shape mismatch");
+            h.resize((size_t)t.n);
+            check_cuda(cudaMemcpy(h.data(), t.d, h.size() * 4, cudaMemcpyDeviceToHost), "read noise conv");
+            pack_tc(packed["noise_convs.0.s2d"], OC, 6 * IC, 2, [&](int oc, int c6, int j) {
+                const int r = c6 / IC, ic = c6 % IC;
+                return h[((size_t)oc * IC + ic) * K + 6 * j + r];
+            });
+        }
         for (int s = 0; s < 2; ++s) {
             const DevTensor &t = W("kokopop.decoder.generator.ups." + std::to_string(s) + ".weight");
             const int OC = (int)t.ne[1], IC = (int)t.ne[2], S = strides[s];
@@ -312,9 +333,23 @@ void kk_ctx::derive() {
         si.prefix = p;
         si.C = (int)gw->ne[1];
         si.f16 = gw->f16;
-        si.gw = gw->d;
+        // transpose [C][128] -> [128][C] for coalesced reads in adain_affine
+        {
+            const int C = si.C;
+            std::vector<float> h((size_t)C * kStyle), t2((size_t)2 * C * kStyle);
+            for (int which = 0; which < 2; ++which) {
+                check_cuda(cudaMemcpy(h.data(), (which ? bw : gw)->d, h.size() * 4, cudaMemcpyDeviceToHost),
+                           "read adain fc");
+                for (int c = 0; c < C; ++c)
+                    for (int i = 0; i < kStyle; ++i) t2[(size_t)which * C * kStyle + (size_t)i * C + c] = h[(size_t)c * kStyle + i];
+            }
+            DevBuf &db = adain_t[p];
+            db.ensure(t2.size() * 4);
+            check_cuda(cudaMemcpy(db.p, t2.data(), t2.size() * 4, cudaMemcpyHostToDevice), "upload adain fc");
+            si.gw = (const float *)db.p;
+            si.bw = (const float *)db.p + (size_t)C * kStyle;
+        }
         si.gb = gb->d;
-        si.bw = bw->d;
         si.bb = bb->d;
         si.off = site_total_C;
         site_total_C += si.C;
@@ -595,14 +630,16 @@ struct Runner {
 
     // stats + AdaIN + activation into an operand (or an F32 buffer)
     void adain_act(const std::string &prefix, const float *x, const Op &y, int64_t Rm, int C, int m, int extra,
-                   int act, float slope, const std::string &alpha) {
+                   int act, float slope, const std::string &alpha, const float2 *pre = nullptr) {
         const AdainSite &s = site(prefix);
         if (s.C != C) throw KKError(KK_ERROR_MODEL, "AdaIN channel mismatch: " + prefix);
-        stats(x, Rm, C, m, extra, B, ms, st);
-        ++c.n_launches;
+        if (!pre) {
+            stats(x, Rm, C, m, extra, B, ms, st);
+            ++c.n_launches;
+        }
         PrologueArgs a{};
         a.norm = 1;
-        a.ms = ms;
+        a.ms = pre ? pre : ms;
         a.norm_w = c.W(prefix + ".norm.weight").d;
         a.norm_b = c.W(prefix + ".norm.bias").d;
         a.gamma = s.gamma;
@@ -689,13 +726,14 @@ struct Runner {
     // graph_generator_resblock: x_in -> (3 iterations) -> wb, the last
     // iteration writing final_out (accumulating / scaling) when given.
     void gen_resblock(const std::string &pf, int K, const float *x_in, float *wb, float *final_out, int accum,
-                      float scale2, int C, int m, int extra, const Op &o, float *tmp) {
+                      float scale2, int C, int m, int extra, const Op &o, float *tmp, const float2 *x_in_stats) {
         const int64_t Rm = R(m);
         const float *cur = x_in;
         for (int i = 0; i < 3; ++i) {
             const std::string is = std::to_string(i);
             const int d = kDil[i];
-            adain_act(pf + ".adain1." + is, cur, o, Rm, C, m, extra, ACT_SNAKE, 0.f, pf + ".alpha1." + is);
+            adain_act(pf + ".adain1." + is, cur, o, Rm, C, m, extra, ACT_SNAKE, 0.f, pf + ".alpha1." + is,
+                      i == 0 ? x_in_stats : nullptr);
             conv_w(pf + ".convs1." + is + ".weight", pf + ".convs1." + is + ".bias", o, C, K, (K * d - d) / 2, d, tmp,
                    Rm, Rm, Epi{}, sum_len(m, extra));
             adain_act(pf + ".adain2." + is, tmp, o, Rm, C, m, extra, ACT_SNAKE, 0.f, pf + ".alpha2." + is);
@@ -738,18 +776,33 @@ struct Runner {
             float *xb = c.buf(("xb" + ss).c_str(), (size_t)Cs * Rm);
             float *tmp = c.buf(("tmp" + ss).c_str(), (size_t)Cs * Rm);
             Op o = op(s == 0 ? "op0" : "op1", m, Cs);
-            // noise branch: noise_convs + noise_res (audio_utils.cpp:714-731).
-            // The 22-channel input does not fill a tensor-core tile: CUDA cores.
+            // noise branch: noise_convs + noise_res (audio_utils.cpp:714-731)
             {
                 Epi e;
                 e.bias = &c.W(g + "noise_convs." + ss + ".bias");
                 e.valid = sum_len(m, extra[s]);
                 const int K = sp[s].noise_kernel;
                 if (ncw.n != (int64_t)Cs * 22 * K) throw KKError(KK_ERROR_MODEL, "noise_convs shape mismatch");
-                conv_f32(ncw.d, ncw.f16, Cs, har, R_har, 22, K, sp[s].noise_stride, sp[s].noise_padding, 1, xs, Rm,
-                         Rm, e);
+                if (tc && s == 0) {
+                    // stride 6 as 2 taps over the space-to-depth operand
+                    Op sd;
+                    sd.R = Rm;
+                    sd.h = (__half *)c.buf("s2d", ((size_t)192 * Rm + 1) / 2);
+                    har_s2d(har, R_har, sd.h, Rm, st);
+                    ++c.n_launches;
+                    e.valid = sum_len(m, extra[s]);
+                    conv_h(c.packed.at("noise_convs.0.s2d"), sd, 2, 0, 1, xs, Rm, Rm, e);
+                } else if (tc) {
+                    Op hh = op("op1", m, Cs);
+                    act_only(har, hh, R_har, 22, m, extra[s], ACT_NONE, 0.f);
+                    conv_h(c.packed.at("noise_convs.1"), hh, 1, 0, 1, xs, Rm, Rm, e);
+                } else {
+                    conv_f32(ncw.d, ncw.f16, Cs, har, R_har, 22, K, sp[s].noise_stride, sp[s].noise_padding, 1, xs,
+                             Rm, Rm, e);
+                }
             }
-            gen_resblock(g + "noise_res." + ss, sp[s].kernel, xs, xs, nullptr, 0, 1.f, Cs, m, extra[s], o, tmp);
+            gen_resblock(g + "noise_res." + ss, sp[s].kernel, xs, xs, nullptr, 0, 1.f, Cs, m, extra[s], o, tmp,
+                         nullptr);
             // LeakyReLU(0.1) then ConvTranspose as phase convolutions,
             // + bias, [reflect pad], + noise branch (audio_utils.cpp:687-760)
             const int64_t Rp = R(m_prev);
@@ -794,12 +847,16 @@ struct Runner {
                 convt_row0(a, B, st);
                 ++c.n_launches;
             }
-            // three main resblocks, averaged (graph_ops.cpp:1300-1320)
+            // three main resblocks, averaged (graph_ops.cpp:1300-1320); they
+            // share the input, so its statistics are computed once
+            float2 *ms_stage = (float2 *)c.buf("stats_stage", (size_t)P.n * 1090 * 2);
+            stats(xst, Rm, Cs, m, extra[s], B, ms_stage, st);
+            ++c.n_launches;
             for (int k = 0; k < 3; ++k) {
                 const std::string pf = g + "resblocks." + std::to_string(s * 3 + k);
                 float *wb = k == 0 ? acc : xb;
                 gen_resblock(pf, kKs[k], xst, wb, acc, k == 0 ? 0 : 1, k == 2 ? 1.0f / 3.0f : 1.f, Cs, m, extra[s],
-                             o, tmp);
+                             o, tmp, ms_stage);
             }
             x = acc;
             C = Cs;

@@ -85,6 +85,7 @@ struct kk_ctx {
     // tensor-core path: every convolution weight is F16
     bool tc_mode = false;
     std::unordered_map<std::string, kk::PackedW> packed;
+    std::unordered_map<std::string, kk::DevBuf> adain_t;  // fc weights transposed to [128][C]
     kk::DevBuf d_err;  // device-side error code of the tensor-core kernel
     kk::SineArgs sine{};
     std::vector<kk::SiteInfo> sites;

@@ -53,13 +53,13 @@ __global__ void k_adain_affine(const AdainSite *__restrict__ sites, const float 
         st[i] = s.f16 ? round_f16(v) : v;
     }
     __syncthreads();
+    // weights transposed at upload ([128][C]) so the threads of a warp read
+    // consecutive channels; the sum over the style features stays sequential
     for (int c = threadIdx.x; c < s.C; c += blockDim.x) {
-        const float *gw = s.gw + (int64_t)c * kStyle;
-        const float *bw = s.bw + (int64_t)c * kStyle;
         float g = 0.f, be = 0.f;
         for (int i = 0; i < kStyle; ++i) {
-            g = __fadd_rn(g, __fmul_rn(gw[i], st[i]));
-            be = __fadd_rn(be, __fmul_rn(bw[i], st[i]));
+            g = __fadd_rn(g, __fmul_rn(s.gw[(int64_t)i * s.C + c], st[i]));
+            be = __fadd_rn(be, __fmul_rn(s.bw[(int64_t)i * s.C + c], st[i]));
         }
         s.gamma[(int64_t)u * s.C + c] = __fadd_rn(g, s.gb[c]);
         s.beta[(int64_t)u * s.C + c] = __fadd_rn(be, s.bb[c]);
@@ -75,7 +75,7 @@ void adain_affine(const AdainSite *sites_dev, int n_sites, const float *style, i
 // ---------------------------------------------------------------------------
 // Instance-norm statistics, ggml_norm semantics (eps 1e-5): per (channel,
 // utterance), mean = (float)sum_double / n, var = sum_double((x-mean)^2) / n,
-// scale = 1 / sqrtf(var + eps).
+// scale = 1 / sqrtf(var + eps) (ggml's norm, restated in the oracle).
 // ---------------------------------------------------------------------------
 
 template <int NT>
@@ -97,22 +97,27 @@ __device__ double block_sum_double(double v, double *red) {
 
 __global__ void __launch_bounds__(256) k_stats(const float *__restrict__ x, int64_t R, int C, int m,
                                                int extra, Batch b, float2 *__restrict__ ms) {
+    // One pass: sum and sum of squares in double, then the two-pass result of
+    // ggml_norm recovered exactly enough: var = sum((x - mean)^2) / n with the
+    // float mean, expanded as (S2 - 2 mean S1 + n mean^2) / n in double.
     __shared__ double red[32];
     const int c = blockIdx.x, u = blockIdx.y;
     const int64_t len = (int64_t)m * b.T[u] + extra;
     const float *p = x + (int64_t)c * R + (int64_t)m * b.offT[u];
-    double s = 0.0;
-    for (int64_t t = threadIdx.x; t < len; t += 256) s += (double)p[t];
-    s = block_sum_double<256>(s, red);
-    const float mean = __fdiv_rn((float)s, (float)len);
-    double s2 = 0.0;
+    double s1 = 0.0, s2 = 0.0;
     for (int64_t t = threadIdx.x; t < len; t += 256) {
-        const float v = __fsub_rn(p[t], mean);
-        s2 += (double)__fmul_rn(v, v);
+        const double v = (double)p[t];
+        s1 += v;
+        s2 += v * v;
     }
+    s1 = block_sum_double<256>(s1, red);
     s2 = block_sum_double<256>(s2, red);
     if (threadIdx.x == 0) {
-        const float var = (float)(s2 / (double)len);
+        const float mean = __fdiv_rn((float)s1, (float)len);
+        const double md = (double)mean;
+        double q = s2 - 2.0 * md * s1 + (double)len * md * md;
+        if (q < 0.0) q = 0.0;
+        const float var = (float)(q / (double)len);
         const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
         ms[(int64_t)u * C + c] = make_float2(mean, scale);
     }
@@ -331,6 +336,36 @@ void pool_up_h(const __half *, const float *x, __half *y, int64_t R_in, int64_t 
     int bx = (2 * max_T + 255) / 256;
     if (bx > 16) bx = 16;
     k_pool_up_h<<<dim3(bx, (C + 7) / 8, b.n), 256, 0, st>>>(x, y, R_in, R_out, C, w, bias, b);
+}
+
+// Space-to-depth operand of the stride-6 noise convolution: every packed row
+// t' of the stage-0 level gets the 132 channels x[r * 22 + ic] =
+// half(har[ic][6 t' + r - 3]), r = 0..5, so that the k=12 / stride-6 / pad-3
+// convolution becomes a stride-1 convolution with 2 taps. All rows are
+// written: outside an utterance they read the zero gaps of har.
+__global__ void k_har_s2d(const float *__restrict__ har, int64_t R_har, __half *__restrict__ y, int64_t R) {
+    const int ch = blockIdx.y;  // output chunk of 8 (24 chunks = 192 padded channels)
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < R; t += (int64_t)gridDim.x * blockDim.x) {
+        __align__(16) __half h[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const int c6 = ch * 8 + e;
+            float v = 0.f;
+            if (c6 < 132) {
+                const int r = c6 / 22, ic = c6 % 22;
+                const int64_t row = 6 * t + r - 3;
+                if (row >= 0 && row < R_har) v = har[(int64_t)ic * R_har + row];
+            }
+            h[e] = __float2half_rn(v);
+        }
+        *reinterpret_cast<uint4 *>(y + ((int64_t)ch * R + t) * 8) = *reinterpret_cast<const uint4 *>(h);
+    }
+}
+
+void har_s2d(const float *har, int64_t R_har, __half *y, int64_t R, cudaStream_t st) {
+    int bx = (int)((R + 255) / 256);
+    if (bx > 2048) bx = 2048;
+    k_har_s2d<<<dim3(bx, 24), 256, 0, st>>>(har, R_har, y, R);
 }
 
 // ---------------------------------------------------------------------------

@@ -8,8 +8,8 @@ namespace kk {
 
 enum { ACT_NONE = 0, ACT_LEAKY = 1, ACT_SNAKE = 2 };
 
-// One AdaIN site (adain_1d / ada_layer_norm): fc weights [C, 128] as F32
-// values, and per-utterance outputs gamma/beta [n_utts, C].
+// One AdaIN site (adain_1d / ada_layer_norm): fc weights transposed to
+// [128, C] (F32 values), and per-utterance outputs gamma/beta [n_utts, C].
 struct AdainSite {
     const float *gw, *gb, *bw, *bb;
     float *gamma, *beta;
@@ -147,6 +147,9 @@ int conv_tc_max_halo();
 // prologue_h: y[c/8][row][c%8] = half(act(adain(x[c][row]))) on valid rows.
 void prologue_h(const float *x, __half *y, int64_t R, int C, int m, int extra, const Batch &b, int max_len,
                 const PrologueArgs &a, cudaStream_t st);
+// har_s2d: space-to-depth half operand [192/8][R][8] of the stride-6
+// noise convolution (132 real channels), all R rows of the stage-0 level.
+void har_s2d(const float *har, int64_t R_har, __half *y, int64_t R, cudaStream_t st);
 // pool_up_h: the depthwise x2 pool written as a half chunk-major operand.
 void pool_up_h(const __half *x_unused, const float *x, __half *y, int64_t R_in, int64_t R_out, int C,
                const float *w, const float *bias, const Batch &b, int max_T, cudaStream_t st);
