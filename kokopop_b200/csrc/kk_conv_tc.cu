@@ -2,46 +2,74 @@
 //
 //   y[oc, orow(q)] = epi( sum_{ic,k} W[oc, ic, k] * x[ic, q - p + k*d] )
 //
-// as an implicit GEMM: M = 128 output positions, N = 128 output channels,
-// K = input channels x taps. F16 operands (ggml's F16 arithmetic: both the
-// F16 weights and the im2col'd activations are half), F32 accumulation in
-// tensor memory.
+// as an implicit GEMM: M = 256 output positions (two 128-row MMAs), N = 128
+// output channels, K = input channels x taps. F16 operands (ggml's F16
+// arithmetic: both the F16 weights and the im2col'd activations are half),
+// F32 accumulation in tensor memory.
 //
 // Operands
-//   A  activations, half, chunk-major in HBM: [IC/8][R][8] (8 channels of one
-//      row are 16 contiguous bytes). One 3-D TMA box (8 x BR x 8) brings the
-//      rows [q0 - p, q0 - p + BR) of 64 channels, halo included, into shared
-//      memory as [8 chunks][BR rows][16 B]: the K-major, no-swizzle canonical
-//      layout (8-row core matrices 128 B apart, chunks BR*16 B apart). Tap k
-//      of the same slab is the same layout starting k*d rows further, so all
-//      taps reuse one load.
+//   A  activations, half, chunk-major in HBM: [IC/8][Ry][8] (8 channels of one
+//      row are 16 contiguous bytes) with zero margins of kHalfLo rows before
+//      and kHalfHi rows after every chunk. One slab = rows [q0 - p, q0 - p +
+//      TC_SLAB) of 64 channels, halo included, is 8 plain bulk copies (one
+//      contiguous 5 KB run per chunk) into shared memory as
+//      [8 chunks][TC_SLAB rows][16 B]: the K-major, no-swizzle canonical
+//      layout (8-row core matrices 128 B apart, chunks TC_SLAB*16 B apart).
+//      Tap k and the second 128-row half are the same layout starting k*d
+//      (+128) rows further, so all taps and both halves reuse one slab.
 //   B  weights, packed at upload into the exact shared-memory image of each
 //      (tap, 64-channel block, 128-channel tile): [8 chunks][128 oc][16 B],
 //      fetched with one bulk copy.
 //
-// Roles (192 threads, persistent over tiles): warp 0 lane 0 issues the
-// copies, warp 1 allocates tensor memory (two 128-column accumulators) and
-// lane 0 issues tcgen05.mma, warps 2-5 drain the other accumulator through
-// the epilogue (tcgen05.ld 32x32b: warp w owns TMEM lanes 32 (w % 4) ...).
+// Roles (320 threads, one CTA per SM, persistent over tiles): warp 0 lane 0
+// issues the copies, warp 1 allocates tensor memory (two 256-column
+// accumulators) and lane 0 issues tcgen05.mma, warps 2-9 drain the other
+// accumulator through the epilogue (tcgen05.ld 32x32b: warp w owns TMEM
+// lanes 32 (w % 4) ... of the 128-row half (w - 2) / 4).
+//
+// Epilogue, two forms. Where output row = position (every stride-1 conv that
+// writes its own level), each warp works on [32 channels][32 rows] blocks in
+// shared memory: the residual block arrives by a TMA load issued one block
+// ahead, the warp adds bias / residual / scales in place, and a TMA store
+// writes the block back, so the warps never wait on global loads or queue
+// scalar stores. Otherwise (strided row maps of the transposed-conv phases,
+// the x2-upsampled shortcut) the values go through registers with plain
+// loads and stores.
 // Every mbarrier wait is bounded in time; on expiry the kernel records an
-// error code and the waiting role stops.
+// error code and the waiting role stops. Before the tensor memory is freed
+// the producer waits (bounded) for its last copies and the MMA thread for its
+// last MMAs.
 #include "kk_kernels.h"
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstring>
+
 namespace kk {
 
-constexpr int TC_BM = 128;
-constexpr int TC_BN = 128;
-constexpr int TC_MAX_BR = 192;                   // rows per slab incl. halo
-constexpr int TC_A_BYTES = 8 * TC_MAX_BR * 16;   // 24 KB
+constexpr int TC_BM = 256;                       // positions per tile
+constexpr int TC_HM = 128;                       // rows per MMA
+constexpr int TC_BN = 128;                       // output channels per tile
+constexpr int TC_SLAB = 320;                     // rows per slab incl. halo
+constexpr int TC_A_BYTES = 8 * TC_SLAB * 16;     // 40 KB
 constexpr int TC_B_BYTES = 8 * TC_BN * 16;       // 16 KB
 constexpr int TC_NSA = 2;                        // A slab stages
-constexpr int TC_NSB = 3;                        // B tile stages
-constexpr int TC_SMEM = TC_NSA * TC_A_BYTES + TC_NSB * TC_B_BYTES + 1024 /*barriers*/ + 1024 /*align*/;
-constexpr int TC_CTAS_PER_SM = 2;  // 2 x 98 KB shared memory, 2 x 256 TMEM columns
-constexpr unsigned long long TC_WAIT_NS = 2000000000ull;  // 2 s
+constexpr int TC_EPI_WARPS = 8;
+constexpr int TC_THREADS = 64 + 32 * TC_EPI_WARPS;
+constexpr int TC_TMEM_COLS = 2 * (TC_BM / TC_HM) * TC_BN;  // 512: two accumulators
+constexpr int TC_BLK_BYTES = 32 * 32 * 4;        // one [32 ch][32 rows] F32 epilogue block
+// B tile stages: 8 with the register epilogue, 4 when the shared-memory
+// epilogue blocks (2 per warp) take the rest of the space
+__host__ __device__ constexpr int tc_nsb(bool tma_epi) { return tma_epi ? 4 : 8; }
+__host__ __device__ constexpr int tc_smem(bool tma_epi) {
+    return TC_NSA * TC_A_BYTES + tc_nsb(tma_epi) * TC_B_BYTES + (tma_epi ? TC_EPI_WARPS * 2 * TC_BLK_BYTES : 0) +
+           2048 /*bias*/ + 1024 /*barriers*/ + 1024 /*align*/;
+}
+constexpr unsigned long long TC_WAIT_NS = 2000000000ull;   // 2 s
+constexpr unsigned long long TC_DRAIN_NS = 200000000ull;   // 0.2 s
+static_assert(tc_smem(true) <= 227 * 1024 && tc_smem(false) <= 227 * 1024, "shared memory");
+static_assert(TC_SLAB - TC_BM <= kHalfLo + kHalfHi, "slab overhang");
 
 // ---------------------------------------------------------------------------
 // PTX helpers
@@ -78,26 +106,18 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 }
 
 // Bounded wait: returns false (and records `code`) when the phase has not
-// completed within TC_WAIT_NS.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int *err, int code) {
+// completed within `limit_ns`.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int *err, int code,
+                                          unsigned long long limit_ns = TC_WAIT_NS) {
     if (mbar_try(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     while (true) {
         if (mbar_try(bar, parity)) return true;
-        if (globaltimer() - t0 > TC_WAIT_NS) {
+        if (globaltimer() - t0 > limit_ns) {
             atomicCAS(err, 0, code);
             return false;
         }
     }
-}
-
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int x, int y,
-                                            int z) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
-        "[%5];" ::"r"(dst),
-        "l"(map), "r"(x), "r"(y), "r"(z), "r"(bar)
-        : "memory");
 }
 
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
@@ -106,6 +126,33 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_
         "l"(src), "r"(bytes), "r"(bar)
         : "memory");
 }
+
+// 2-D tensor copies of one [32 ch][32 rows] F32 block (x = row, y = channel).
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            dst),
+        "l"(map), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, uint32_t src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map), "r"(src),
+                 "r"(x), "r"(y)
+                 : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// the shared-memory source of all but the newest N committed stores has been read
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // Shared-memory matrix descriptor, K-major, no swizzle (sm_100 layout:
 // start >> 4 in [0,14), LBO >> 4 in [16,30), SBO >> 4 in [32,46), version 1
@@ -161,14 +208,15 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 // ---------------------------------------------------------------------------
 
 struct TcParams {
-    int IC_blocks;   // input channels / 64 (padded)
-    int K, p, d;     // taps, padding, dilation
-    int BR;          // slab rows = 127 + (K - 1) d + 1
-    int OC;          // real output channels
-    int n_tiles;     // OC tiles of 128 in the packed weights
-    int n_oc_tiles;  // OC tiles computed
-    int64_t m_tiles; // position tiles of 128
-    const __half *w; // packed [K][IC_blocks][n_tiles][8][128][8]
+    int IC_blocks;    // input channels / 64 (padded)
+    int K, p, d;      // taps, padding, dilation
+    int OC;           // real output channels
+    int n_tiles;      // OC tiles of 128 in the packed weights
+    int n_oc_tiles;   // OC tiles computed
+    int64_t m_tiles;  // position tiles of 256
+    const __half *a;  // half operand, row 0 of chunk 0
+    int64_t R_a;      // chunk stride (rows)
+    const __half *w;  // packed [K][IC_blocks][n_tiles][8][128][8]
     float *out;
     int64_t R_out;
     int64_t n_pos;
@@ -185,21 +233,28 @@ struct TcParams {
 
 // Persistent: CTA i takes tiles i, i + grid, ... (OC tile fastest, so the
 // CTAs working on one slab of positions run close together and share it in
-// L2). Warp 0 lane 0: copies. Warp 1: TMEM owner, lane 0 issues MMAs into
-// one of two accumulators (128 columns each) so the epilogue of a tile
-// overlaps the MMAs of the next. Warps 2-5: epilogue (warp w reads TMEM lanes
-// 32 (w % 4) ...).
-__global__ void __launch_bounds__(192, 2) k_conv_tc(const __grid_constant__ CUtensorMap amap, TcParams P) {
+// L2). TMA_EPI selects the shared-memory epilogue; omap / rmap are then the
+// 2-D maps of the output and the residual ([OC][R] F32, 32 x 32 boxes).
+template <bool TMA_EPI>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    k_conv_tc(const __grid_constant__ TcParams P, const __grid_constant__ CUtensorMap omap,
+              const __grid_constant__ CUtensorMap rmap) {
+    constexpr int NSB = tc_nsb(TMA_EPI);
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t *sA = smem;
     uint8_t *sB = smem + TC_NSA * TC_A_BYTES;
-    uint64_t *bars = (uint64_t *)(sB + TC_NSB * TC_B_BYTES);
-    // A_full[2] A_empty[2] B_full[NSB] B_empty[NSB] acc_full[2] acc_empty[2] tmem slot
+    uint8_t *sE = sB + NSB * TC_B_BYTES;  // epilogue blocks (TMA_EPI)
+    float *sbias = (float *)(sE + (TMA_EPI ? TC_EPI_WARPS * 2 * TC_BLK_BYTES : 0));  // [512]
+    uint64_t *bars = (uint64_t *)((uint8_t *)sbias + 2048);
+    // A_full[2] A_empty[2] B_full[NSB] B_empty[NSB] acc_full[2] acc_empty[2]
+    // drain res[8 warps][2] tmem-slot
     const uint32_t bA_full = smem_u32(bars + 0), bA_empty = smem_u32(bars + 2);
-    const uint32_t bB_full = smem_u32(bars + 4), bB_empty = smem_u32(bars + 4 + TC_NSB);
-    const uint32_t bAcc_full = smem_u32(bars + 4 + 2 * TC_NSB), bAcc_empty = smem_u32(bars + 6 + 2 * TC_NSB);
-    uint32_t *tmem_slot = (uint32_t *)(bars + 8 + 2 * TC_NSB);
+    const uint32_t bB_full = smem_u32(bars + 4), bB_empty = smem_u32(bars + 4 + NSB);
+    const uint32_t bAcc_full = smem_u32(bars + 4 + 2 * NSB), bAcc_empty = smem_u32(bars + 6 + 2 * NSB);
+    const uint32_t bDrain = smem_u32(bars + 8 + 2 * NSB);
+    const uint32_t bRes = smem_u32(bars + 9 + 2 * NSB);
+    uint32_t *tmem_slot = (uint32_t *)(bars + 9 + 2 * NSB + 2 * TC_EPI_WARPS);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t n_tiles_total = P.m_tiles * P.n_oc_tiles;
@@ -209,30 +264,35 @@ __global__ void __launch_bounds__(192, 2) k_conv_tc(const __grid_constant__ CUte
             mbar_init(bA_full + 8 * i, 1);
             mbar_init(bA_empty + 8 * i, 1);
         }
-        for (int i = 0; i < TC_NSB; ++i) {
+        for (int i = 0; i < NSB; ++i) {
             mbar_init(bB_full + 8 * i, 1);
             mbar_init(bB_empty + 8 * i, 1);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(bAcc_full + 8 * i, 1);
-            mbar_init(bAcc_empty + 8 * i, 4);  // one arrive per epilogue warp
+            mbar_init(bAcc_empty + 8 * i, TC_EPI_WARPS);  // one arrive per epilogue warp
         }
+        mbar_init(bDrain, 1);
+        for (int i = 0; i < 2 * TC_EPI_WARPS; ++i) mbar_init(bRes + 8 * i, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(2 * TC_BN)
+                     "r"(TC_TMEM_COLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (TMA_EPI && warp >= 2) {
+        for (int i = threadIdx.x - 64; i < 512; i += 32 * TC_EPI_WARPS)
+            sbias[i] = (P.bias && i < P.OC) ? P.bias[i] : 0.f;
     }
     fence_before_sync();
     __syncthreads();
     fence_after_sync();
     const uint32_t tmem = *tmem_slot;
 
-    const uint32_t a_bytes = 8u * (uint32_t)P.BR * 16u;
-    const uint32_t lbo_a = (uint32_t)P.BR * 16u;
-    const uint32_t lbo_b = (uint32_t)TC_BN * 16u;
+    constexpr uint32_t lbo_a = (uint32_t)TC_SLAB * 16u;
+    constexpr uint32_t lbo_b = (uint32_t)TC_BN * 16u;
 
     if (warp == 0) {
         if (lane == 0) {
@@ -242,16 +302,21 @@ __global__ void __launch_bounds__(192, 2) k_conv_tc(const __grid_constant__ CUte
             for (int64_t tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x) {
                 const int64_t mt = tile / P.n_oc_tiles;
                 const int nt = (int)(tile % P.n_oc_tiles);
-                const int row0 = (int)(mt * TC_BM - P.p);
+                const int64_t row0 = mt * TC_BM - P.p;  // >= -kHalfLo (checked on the host)
                 for (int b = 0; b < P.IC_blocks && ok; ++b, ++ia) {
                     const int sa = ia % TC_NSA;
                     if (ia >= TC_NSA) ok = mbar_wait(bA_empty + 8 * sa, ((ia / TC_NSA) & 1) ^ 1, P.err, 11);
                     if (!ok) break;
-                    mbar_expect_tx(bA_full + 8 * sa, a_bytes);
-                    tma_load_3d(smem_u32(sA + sa * TC_A_BYTES), &amap, bA_full + 8 * sa, 0, row0, 8 * b);
+                    mbar_expect_tx(bA_full + 8 * sa, TC_A_BYTES);
+                    const uint32_t dst = smem_u32(sA + sa * TC_A_BYTES);
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        const __half *src = P.a + ((int64_t)(8 * b + c) * P.R_a + row0) * 8;
+                        bulk_load(dst + (uint32_t)c * lbo_a, src, lbo_a, bA_full + 8 * sa);
+                    }
                     for (int k = 0; k < P.K; ++k, ++ib) {
-                        const int sb = ib % TC_NSB;
-                        if (ib >= TC_NSB) ok = mbar_wait(bB_empty + 8 * sb, ((ib / TC_NSB) & 1) ^ 1, P.err, 12);
+                        const int sb = ib % NSB;
+                        if (ib >= NSB) ok = mbar_wait(bB_empty + 8 * sb, ((ib / NSB) & 1) ^ 1, P.err, 12);
                         if (!ok) break;
                         mbar_expect_tx(bB_full + 8 * sb, TC_B_BYTES);
                         const __half *src =
@@ -260,12 +325,18 @@ __global__ void __launch_bounds__(192, 2) k_conv_tc(const __grid_constant__ CUte
                     }
                 }
             }
+            // Drain: the last copy issued into each stage has landed (already
+            // consumed on the normal path, so these return at once).
+            for (uint32_t i = (ia > TC_NSA ? ia - TC_NSA : 0); i < ia; ++i)
+                mbar_wait(bA_full + 8 * (i % TC_NSA), (i / TC_NSA) & 1, P.err, 18, TC_DRAIN_NS);
+            for (uint32_t i = (ib > NSB ? ib - NSB : 0); i < ib; ++i)
+                mbar_wait(bB_full + 8 * (i % NSB), (i / NSB) & 1, P.err, 18, TC_DRAIN_NS);
         }
         __syncwarp();
     } else if (warp == 1) {
         if (lane == 0) {
             // MMA issuer
-            const uint32_t idesc = idesc_f16(TC_BM, TC_BN);
+            const uint32_t idesc = idesc_f16(TC_HM, TC_BN);
             bool ok = true;
             uint32_t ia = 0, ib = 0, it = 0;
             for (int64_t tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x, ++it) {
@@ -273,8 +344,7 @@ __global__ void __launch_bounds__(192, 2) k_conv_tc(const __grid_constant__ CUte
                 if (it >= 2) ok = mbar_wait(bAcc_empty + 8 * ab, ((it >> 1) & 1) ^ 1, P.err, 17);
                 if (!ok) break;
                 fence_after_sync();
-                const uint32_t d_tmem = tmem + (uint32_t)(ab * TC_BN);
-                uint32_t acc = 0;
+                const uint32_t d_tmem = tmem + (uint32_t)(ab * 2 * TC_BN);
                 for (int b = 0; b < P.IC_blocks && ok; ++b, ++ia) {
                     const int sa = ia % TC_NSA;
                     ok = mbar_wait(bA_full + 8 * sa, (ia / TC_NSA) & 1, P.err, 13);
@@ -282,76 +352,162 @@ __global__ void __launch_bounds__(192, 2) k_conv_tc(const __grid_constant__ CUte
                     fence_after_sync();
                     const uint32_t a_base = smem_u32(sA + sa * TC_A_BYTES);
                     for (int k = 0; k < P.K; ++k, ++ib) {
-                        const int sb = ib % TC_NSB;
-                        ok = mbar_wait(bB_full + 8 * sb, (ib / TC_NSB) & 1, P.err, 14);
+                        const int sb = ib % NSB;
+                        ok = mbar_wait(bB_full + 8 * sb, (ib / NSB) & 1, P.err, 14);
                         if (!ok) break;
                         fence_after_sync();
                         const uint32_t b_base = smem_u32(sB + sb * TC_B_BYTES);
                         const uint32_t a_tap = a_base + (uint32_t)(k * P.d) * 16u;
 #pragma unroll
                         for (int ks = 0; ks < 4; ++ks) {
-                            const uint64_t ad = sdesc(a_tap + (uint32_t)(2 * ks) * lbo_a, lbo_a, 128);
                             const uint64_t bd = sdesc(b_base + (uint32_t)(2 * ks) * lbo_b, lbo_b, 128);
-                            mma_f16(d_tmem, ad, bd, idesc, acc);
-                            acc = 1;
+                            const uint32_t acc = (b > 0 || k > 0 || ks > 0) ? 1u : 0u;
+#pragma unroll
+                            for (int h = 0; h < TC_BM / TC_HM; ++h) {
+                                const uint64_t ad =
+                                    sdesc(a_tap + (uint32_t)(h * TC_HM) * 16u + (uint32_t)(2 * ks) * lbo_a, lbo_a, 128);
+                                mma_f16(d_tmem + (uint32_t)(h * TC_BN), ad, bd, idesc, acc);
+                            }
                         }
                         mma_commit(bB_empty + 8 * sb);
                     }
                     mma_commit(bA_empty + 8 * sa);
                 }
-                mma_commit(bAcc_full + 8 * ab);
+                if (ok) mma_commit(bAcc_full + 8 * ab);
             }
+            // Drain: every MMA issued above has completed before the
+            // accumulators are freed.
+            mma_commit(bDrain);
+            mbar_wait(bDrain, 0, P.err, 19, TC_DRAIN_NS);
         }
         __syncwarp();
     } else {
-        // epilogue warps 2..5
-        const int lg = warp & 3;  // TMEM lane group
+        // epilogue warps 2..9
+        const int ew = warp - 2;
+        const int lg = warp & 3;           // TMEM lane group
+        const int half = ew >> 2;          // 128-row half of the tile
+        float *blk = (float *)(sE + ew * 2 * TC_BLK_BYTES);  // TMA_EPI: two blocks of this warp
+        const uint32_t bR = bRes + 8 * 2 * ew;
+        const bool has_res = P.resid != nullptr;
         uint32_t it = 0;
-        for (int64_t tile = blockIdx.x; tile < n_tiles_total; tile += gridDim.x, ++it) {
+        uint32_t ci = 0, n_res = 0;  // blocks done / residual blocks requested (TMA_EPI)
+        bool stop = false;
+        for (int64_t tile = blockIdx.x; tile < n_tiles_total && !stop; tile += gridDim.x, ++it) {
             const int64_t mt = tile / P.n_oc_tiles;
             const int n0 = (int)(tile % P.n_oc_tiles) * TC_BN;
             const int ab = it & 1;
+            const int64_t qw = mt * TC_BM + half * TC_HM + lg * 32;  // first row of this warp
+            if (TMA_EPI && has_res && lane == 0) {
+                // the residual of this tile's first block, requested before the
+                // accumulator is ready
+                bulk_wait_read<0>();
+                mbar_expect_tx(bR + 8 * (ci & 1), TC_BLK_BYTES);
+                tma_load_2d(smem_u32(blk + (ci & 1) * 1024), &rmap, bR + 8 * (ci & 1), (int)qw, n0);
+                ++n_res;
+            }
             int ok_lane = 0;
             if (lane == 0) ok_lane = mbar_wait(bAcc_full + 8 * ab, (it >> 1) & 1, P.err, 15) ? 1 : 0;
             if (__shfl_sync(0xffffffffu, ok_lane, 0) == 0) break;
+            __syncwarp();
             fence_after_sync();
-            const int64_t q = mt * TC_BM + lg * 32 + lane;
+            const int64_t q = qw + lane;
             const int64_t orow = q * P.omul + P.oadd;
             const bool row_ok = q < P.n_pos && orow >= 0 && orow < P.R_out;
-            const int64_t rrow = P.resid_half ? (orow >> 1) : orow;
+            const uint32_t t_base = tmem + ((uint32_t)(lg * 32) << 16) + (uint32_t)(ab * 2 * TC_BN + half * TC_BN);
             for (int c0 = 0; c0 < TC_BN; c0 += 32) {
                 if (n0 + c0 >= P.OC) break;  // warp-uniform
+                // every lane takes part in the warp-collective TMEM load and
+                // shuffles; row_ok only predicates the memory accesses
                 uint32_t r[32];
-                tmem_ld32(tmem + ((uint32_t)(lg * 32) << 16) + (uint32_t)(ab * TC_BN + c0), r);
-                if (!row_ok) continue;
-                // The residual and the accumulated output may alias the output
-                // (in-place updates): read all 32 of this row's values first so
-                // the loads overlap, then compute and store.
+                tmem_ld32(t_base + (uint32_t)c0, r);
                 const int nj = P.OC - (n0 + c0) < 32 ? P.OC - (n0 + c0) : 32;
-                float res[32], old[32];
+                if (TMA_EPI) {
+                    const int s = ci & 1;
+                    float *buf = blk + s * 1024;
+                    if (has_res) {
+                        if (lane == 0 && c0 + 32 < TC_BN && n0 + c0 + 32 < P.OC) {
+                            // request the next block's residual into the other buffer
+                            bulk_wait_read<0>();
+                            mbar_expect_tx(bR + 8 * (s ^ 1), TC_BLK_BYTES);
+                            tma_load_2d(smem_u32(blk + (s ^ 1) * 1024), &rmap, bR + 8 * (s ^ 1), (int)qw,
+                                        n0 + c0 + 32);
+                            ++n_res;
+                        }
+                        // every lane waits: each reader needs its own acquire of
+                        // the bytes the copy engine wrote
+                        if (!__all_sync(0xffffffffu, mbar_wait(bR + 8 * s, (ci >> 1) & 1, P.err, 20))) {
+                            stop = true;
+                            break;
+                        }
+                    } else {
+                        if (lane == 0) bulk_wait_read<1>();  // this buffer's previous store has read it
+                        __syncwarp();
+                    }
+                    float old[32];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int oc = n0 + c0 + j;
-                    res[j] = (P.resid && j < nj) ? P.resid[(int64_t)oc * P.R_resid + rrow] : 0.f;
-                    old[j] = (P.accum && j < nj) ? P.out[(int64_t)oc * P.R_out + orow] : 0.f;
-                }
+                    for (int j = 0; j < 32; ++j) {
+                        const bool live = row_ok && j < nj;
+                        old[j] = (P.accum && live) ? P.out[(int64_t)(n0 + c0 + j) * P.R_out + orow] : 0.f;
+                    }
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    if (j >= nj) break;
-                    const int oc = n0 + c0 + j;
-                    float v = __uint_as_float(r[j]);
-                    if (P.bias) v = __fadd_rn(v, P.bias[oc]);
-                    if (P.resid) v = __fadd_rn(res[j], v);
-                    if (P.scale1 != 1.0f) v = __fmul_rn(v, P.scale1);
-                    if (P.accum) v = __fadd_rn(old[j], v);
-                    if (P.scale2 != 1.0f) v = __fmul_rn(v, P.scale2);
-                    P.out[(int64_t)oc * P.R_out + orow] = v;
+                    for (int j = 0; j < 32; ++j) {
+                        float v = __uint_as_float(r[j]);
+                        if (P.bias) v = __fadd_rn(v, sbias[n0 + c0 + j]);
+                        if (has_res) v = __fadd_rn(buf[j * 32 + lane], v);
+                        if (P.scale1 != 1.0f) v = __fmul_rn(v, P.scale1);
+                        if (P.accum) v = __fadd_rn(old[j], v);
+                        if (P.scale2 != 1.0f) v = __fmul_rn(v, P.scale2);
+                        buf[j * 32 + lane] = v;
+                    }
+                    fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0) {
+                        // rows past R_out and channels past OC are clipped by the map
+                        tma_store_2d(&omap, smem_u32(buf), (int)qw, n0 + c0);
+                        bulk_commit();
+                    }
+                    ++ci;
+                } else {
+                    const int64_t rrow = P.resid_half ? (orow >> 1) : orow;
+                    const float b_lane = (P.bias && lane < nj) ? __ldg(P.bias + n0 + c0 + lane) : 0.f;
+                    // The residual and the accumulated output may alias the
+                    // output (in-place updates): read all of this row's values
+                    // first so the loads overlap, then compute and store.
+                    float res[32], old[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const bool live = row_ok && j < nj;
+                        const int64_t oc = n0 + c0 + j;
+                        res[j] = (has_res && live) ? P.resid[oc * P.R_resid + rrow] : 0.f;
+                        old[j] = (P.accum && live) ? P.out[oc * P.R_out + orow] : 0.f;
+                    }
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float bj = __shfl_sync(0xffffffffu, b_lane, j);
+                        float v = __uint_as_float(r[j]);
+                        if (P.bias) v = __fadd_rn(v, bj);
+                        if (has_res) v = __fadd_rn(res[j], v);
+                        if (P.scale1 != 1.0f) v = __fmul_rn(v, P.scale1);
+                        if (P.accum) v = __fadd_rn(old[j], v);
+                        if (P.scale2 != 1.0f) v = __fmul_rn(v, P.scale2);
+                        if (row_ok && j < nj) P.out[(int64_t)(n0 + c0 + j) * P.R_out + orow] = v;
+                    }
                 }
             }
+            if (stop) break;
             // hand the accumulator back to the MMA warp
             fence_before_sync();
             __syncwarp();
             if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bAcc_empty + 8 * ab) : "memory");
+        }
+        if (TMA_EPI) {
+            if (lane == 0) {
+                // residual blocks requested but not used (only after an error)
+                for (uint32_t i = ci; i < n_res; ++i)
+                    mbar_wait(bR + 8 * (i & 1), (i >> 1) & 1, P.err, 21, TC_DRAIN_NS);
+                bulk_wait_all();  // every output block written
+            }
+            __syncwarp();
         }
     }
 
@@ -359,7 +515,8 @@ __global__ void __launch_bounds__(192, 2) k_conv_tc(const __grid_constant__ CUte
     __syncthreads();
     if (warp == 1) {
         fence_after_sync();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * TC_BN) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS)
+                     : "memory");
     }
 }
 
@@ -367,10 +524,17 @@ __global__ void __launch_bounds__(192, 2) k_conv_tc(const __grid_constant__ CUte
 // host side
 // ---------------------------------------------------------------------------
 
+static int g_num_sms = 0;
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
-static int g_num_sms = 148;
 
 cudaError_t conv_tc_init() {
+    if (!g_num_sms) {
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return e;
+        e = cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+    }
     if (!g_encode) {
         cudaDriverEntryPointQueryResult q;
         void *fn = nullptr;
@@ -378,34 +542,46 @@ cudaError_t conv_tc_init() {
         if (e != cudaSuccess) return e;
         if (q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
         g_encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
-        int dev = 0;
-        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
     }
-    return cudaFuncSetAttribute(k_conv_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
+    cudaError_t e = cudaFuncSetAttribute(k_conv_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem(true));
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(k_conv_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem(false));
 }
 
-int conv_tc_max_halo() { return TC_MAX_BR - TC_BM; }
+int conv_tc_max_halo() { return TC_SLAB - TC_BM; }
+
+// 2-D map of an F32 [C][R] tensor in 32 x 32 boxes (x = row, y = channel).
+static bool block_map(CUtensorMap *m, const float *base, int64_t R, int C) {
+    if (((uintptr_t)base & 15) || (R & 3)) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)R, (cuuint64_t)C};
+    cuuint64_t strides[1] = {(cuuint64_t)R * 4};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)base, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 cudaError_t conv_tc(const ConvTcArgs &a, cudaStream_t st) {
-    const int BR = (TC_BM - 1) + (a.K - 1) * a.d + 1;
-    if (BR > TC_MAX_BR || a.IC_pad % 64 != 0 || a.OC > a.n_tiles * TC_BN) return cudaErrorInvalidValue;
-    CUtensorMap map;
-    cuuint64_t dims[3] = {8, (cuuint64_t)a.R_in, (cuuint64_t)(a.IC_pad / 8)};
-    cuuint64_t strides[2] = {16, (cuuint64_t)a.R_in * 16};
-    cuuint32_t box[3] = {8, (cuuint32_t)BR, 8};
-    cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = g_encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, (void *)a.in, dims, strides, box, estr,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                          CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+    const int halo = (a.K - 1) * a.d;
+    if (a.K < 1 || a.d < 1 || a.p < 0 || halo > TC_SLAB - TC_BM || a.p > kHalfLo || a.IC_pad % 64 != 0 ||
+        a.OC > a.n_tiles * TC_BN || a.n_pos < 1 || a.R_in < half_stride(0))
+        return cudaErrorInvalidValue;
     TcParams P;
     P.IC_blocks = a.IC_pad / 64;
     P.K = a.K;
     P.p = a.p;
     P.d = a.d;
-    P.BR = BR;
     P.OC = a.OC;
     P.n_tiles = a.n_tiles;
+    P.n_oc_tiles = (a.OC + TC_BN - 1) / TC_BN;
+    P.m_tiles = (a.n_pos + TC_BM - 1) / TC_BM;
+    // the last slab must stay inside the chunk: rows < R + kHalfHi where the
+    // operand has R = R_in - kHalfLo - kHalfHi rows
+    const int64_t rows = a.R_in - kHalfLo - kHalfHi;
+    if (a.n_pos > rows || (P.m_tiles - 1) * TC_BM - a.p + TC_SLAB > rows + kHalfHi) return cudaErrorInvalidValue;
+    P.a = a.in;
+    P.R_a = a.R_in;
     P.w = a.w;
     P.out = a.out;
     P.R_out = a.R_out;
@@ -420,12 +596,20 @@ cudaError_t conv_tc(const ConvTcArgs &a, cudaStream_t st) {
     P.accum = a.accum;
     P.scale2 = a.scale2;
     P.err = a.err;
-    P.n_oc_tiles = (a.OC + TC_BN - 1) / TC_BN;
-    P.m_tiles = (a.n_pos + TC_BM - 1) / TC_BM;
+    // shared-memory epilogue where output row = position over the whole level
+    CUtensorMap omap, rmap;
+    memset(&omap, 0, sizeof(omap));
+    memset(&rmap, 0, sizeof(rmap));
+    bool tma = g_encode && a.omul == 1 && a.oadd == 0 && a.n_pos == a.R_out && !a.resid_half && a.OC >= 64 &&
+               a.OC <= 512 && (!a.resid || a.R_resid == a.R_out);
+    if (tma) tma = block_map(&omap, a.out, a.R_out, a.OC) && block_map(&rmap, a.resid ? a.resid : a.out, a.R_out, a.OC);
     const int64_t tiles = P.m_tiles * P.n_oc_tiles;
-    const int64_t slots = (int64_t)g_num_sms * TC_CTAS_PER_SM;
+    const int64_t slots = g_num_sms > 0 ? g_num_sms : 148;
     const unsigned grid = (unsigned)(tiles < slots ? tiles : slots);
-    k_conv_tc<<<grid, 192, TC_SMEM, st>>>(map, P);
+    if (tma)
+        k_conv_tc<true><<<grid, TC_THREADS, tc_smem(true), st>>>(P, omap, rmap);
+    else
+        k_conv_tc<false><<<grid, TC_THREADS, tc_smem(false), st>>>(P, omap, rmap);
     return cudaGetLastError();
 }
 

@@ -423,12 +423,14 @@ Plan kk::make_plan(const int32_t *lens, int n) {
 namespace {
 
 // An activation operand of a convolution: F32 channel-major [C][R] for the
-// CUDA-core path, or half chunk-major [C/8][R][8] for the tensor-core path.
-// Its gap rows (and padding channels) read as zero.
+// CUDA-core path, or half chunk-major [C/8][Ry][8] with zero margins for the
+// tensor-core path (h addresses row 0 of chunk 0, Ry = half_stride(R)).
+// Its gap rows, margins and padding channels read as zero.
 struct Op {
     float *f = nullptr;
     __half *h = nullptr;
     int64_t R = 0;
+    int64_t Ry = 0;
 };
 
 struct Runner {
@@ -505,9 +507,11 @@ struct Runner {
     Op op(const char *name, int m, int C) {
         Op o;
         o.R = R(m);
+        o.Ry = o.R;
         if (tc) {
             const int cpad = (C + 63) / 64 * 64;
-            o.h = (__half *)c.buf(name, ((size_t)cpad * o.R + 1) / 2);
+            o.Ry = half_stride(o.R);
+            o.h = (__half *)c.buf(name, ((size_t)cpad * o.Ry + 1) / 2) + kHalfLo * 8;
         } else {
             o.f = c.buf(name, (size_t)C * o.R);
         }
@@ -516,7 +520,8 @@ struct Runner {
 
     void zero(const Op &o, int C) {
         if (o.h)
-            check_cuda(cudaMemsetAsync(o.h, 0, (size_t)((C + 63) / 64 * 64) * o.R * sizeof(__half), st), "memset");
+            check_cuda(cudaMemsetAsync(o.h - kHalfLo * 8, 0, (size_t)((C + 63) / 64 * 64) * o.Ry * sizeof(__half), st),
+                       "memset");
         else
             check_cuda(cudaMemsetAsync(o.f, 0, (size_t)C * o.R * sizeof(float), st), "memset");
     }
@@ -584,7 +589,7 @@ struct Runner {
                 const Epi &e) {
         ConvTcArgs a{};
         a.in = in.h;
-        a.R_in = in.R;
+        a.R_in = in.Ry;
         a.IC_pad = pw.IC_pad;
         a.w = (const __half *)pw.buf.p;
         a.n_tiles = pw.n_tiles;
@@ -649,7 +654,7 @@ struct Runner {
         a.alpha = alpha.empty() ? nullptr : c.W(alpha).d;
         a.round16 = 0;
         if (y.h)
-            prologue_h(x, y.h, Rm, C, m, extra, B, m * P.maxT + extra, a, st);
+            prologue_h(x, y.h, Rm, y.Ry, C, m, extra, B, m * P.maxT + extra, a, st);
         else
             prologue(x, y.f, Rm, C, m, extra, B, m * P.maxT + extra, a, st);
         ++c.n_launches;
@@ -661,7 +666,7 @@ struct Runner {
         a.act = act;
         a.slope = slope;
         if (y.h)
-            prologue_h(x, y.h, Rm, C, m, extra, B, m * P.maxT + extra, a, st);
+            prologue_h(x, y.h, Rm, y.Ry, C, m, extra, B, m * P.maxT + extra, a, st);
         else
             prologue(x, y.f, Rm, C, m, extra, B, m * P.maxT + extra, a, st);
         ++c.n_launches;
@@ -710,7 +715,7 @@ struct Runner {
             pf32.R = R1;
             adain_act(pf + ".norm1", x, pf32, R1, Cin, 1, 0, ACT_LEAKY, 0.2f, "");
             if (tc)
-                pool_up_h(nullptr, pf32.f, opL.h, R1, R2, Cin, pw.d, pb.d, B, P.maxT, st);
+                pool_up_h(pf32.f, opL.h, R1, opL.Ry, Cin, pw.d, pb.d, B, P.maxT, st);
             else
                 pool_up(pf32.f, opL.f, R1, R2, Cin, pw.d, pb.d, B, P.maxT, 0, st);
             ++c.n_launches;
@@ -785,10 +790,8 @@ struct Runner {
                 if (ncw.n != (int64_t)Cs * 22 * K) throw KKError(KK_ERROR_MODEL, "noise_convs shape mismatch");
                 if (tc && s == 0) {
                     // stride 6 as 2 taps over the space-to-depth operand
-                    Op sd;
-                    sd.R = Rm;
-                    sd.h = (__half *)c.buf("s2d", ((size_t)192 * Rm + 1) / 2);
-                    har_s2d(har, R_har, sd.h, Rm, st);
+                    Op sd = op("s2d", m, 192);
+                    har_s2d(har, R_har, sd.h, Rm, sd.Ry, st);
                     ++c.n_launches;
                     e.valid = sum_len(m, extra[s]);
                     conv_h(c.packed.at("noise_convs.0.s2d"), sd, 2, 0, 1, xs, Rm, Rm, e);
@@ -831,7 +834,7 @@ struct Runner {
                 ConvTRow0Args a{};
                 a.in = op_prev.f;
                 a.in_h = op_prev.h;
-                a.R_in = Rp;
+                a.R_in = op_prev.h ? op_prev.Ry : Rp;
                 a.IC = C;
                 a.m_in = m_prev;
                 a.w = uw.d;
@@ -881,6 +884,7 @@ struct Runner {
         zero(op("op2", gm, 1152), 1152);
         zero(op("op0", 10 * gm, 256), 256);
         zero(op("op1", 60 * gm, 128), 128);
+        if (tc) zero(op("s2d", 10 * gm, 192), 192);
     }
 
     // harmonic source + STFT on the side stream, from the packed F0 (level mf)

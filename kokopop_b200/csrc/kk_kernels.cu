@@ -222,15 +222,18 @@ void convt_row0(const ConvTRow0Args &a, const Batch &b, cudaStream_t st) {
 }
 
 // Half chunk-major variant of the prologue, the operand of the tensor-core
-// convolution: y[(c/8 * R + row) * 8 + c%8]. Same arithmetic as k_prologue,
+// convolution: y[(c/8 * Ry + row) * 8 + c%8]. Same arithmetic as k_prologue,
 // then the round-to-nearest-even to half that ggml's F16 im2col applies.
 // A thread produces 4 consecutive rows x 8 channels: eight 16-byte loads
 // (one float4 per channel) and four contiguous 16-byte stores, so enough
 // bytes are in flight to stream at HBM rate. Rows of the 4-row group that
-// fall past the utterance are written as zero (they are gap rows).
-__global__ void __launch_bounds__(256) k_prologue_h(const float *__restrict__ x, __half *__restrict__ y,
-                                                    int64_t R, int C, int m, int extra, Batch b,
-                                                    PrologueArgs a) {
+// fall past the utterance are written as zero (they are gap rows). The
+// normalisation and the activation are template parameters so that each
+// variant keeps only the registers it needs (3 blocks per SM).
+template <bool NORM, int ACT>
+__global__ void __launch_bounds__(256, 3) k_prologue_h(const float *__restrict__ x, __half *__restrict__ y,
+                                                       int64_t R, int64_t Ry, int C, int m, int extra, Batch b,
+                                                       PrologueArgs a) {
     const int u = blockIdx.z, ch = blockIdx.y;
     const int64_t len = (int64_t)m * b.T[u] + extra;
     const int64_t row0 = (int64_t)m * b.offT[u];  // a multiple of 4
@@ -240,7 +243,7 @@ __global__ void __launch_bounds__(256) k_prologue_h(const float *__restrict__ x,
         const int c = ch * 8 + e;
         mean[e] = 0.f, scale[e] = 1.f, nw[e] = 1.f, nb[e] = 0.f, g[e] = 0.f, be[e] = 0.f, al[e] = 0.f, ia[e] = 0.f;
         if (c >= C) continue;
-        if (a.norm) {
+        if (NORM) {
             const float2 s = a.ms[(int64_t)u * C + c];
             mean[e] = s.x;
             scale[e] = s.y;
@@ -249,7 +252,7 @@ __global__ void __launch_bounds__(256) k_prologue_h(const float *__restrict__ x,
             g[e] = a.gamma[(int64_t)u * C + c];
             be[e] = a.beta[(int64_t)u * C + c];
         }
-        if (a.act == ACT_SNAKE) {
+        if (ACT == ACT_SNAKE) {
             al[e] = a.alpha[c];
             ia[e] = __fdiv_rn(1.0f, al[e]);
         }
@@ -269,15 +272,15 @@ __global__ void __launch_bounds__(256) k_prologue_h(const float *__restrict__ x,
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 float v = in[i];
-                if (a.norm) {
+                if (NORM) {
                     v = __fmul_rn(__fsub_rn(v, mean[e]), scale[e]);
                     v = __fadd_rn(__fmul_rn(v, nw[e]), nb[e]);
                     v = __fadd_rn(v, __fmul_rn(v, g[e]));
                     v = __fadd_rn(v, be[e]);
                 }
-                if (a.act == ACT_LEAKY) {
+                if (ACT == ACT_LEAKY) {
                     v = leaky(v, a.slope);
-                } else if (a.act == ACT_SNAKE) {
+                } else if (ACT == ACT_SNAKE) {
                     const float sn = snake_sin(__fmul_rn(v, al[e]));
                     v = __fadd_rn(v, __fmul_rn(__fmul_rn(sn, sn), ia[e]));
                 }
@@ -285,22 +288,37 @@ __global__ void __launch_bounds__(256) k_prologue_h(const float *__restrict__ x,
                 h[i][e] = __float2half_rn(v);
             }
         }
-        uint4 *dst = reinterpret_cast<uint4 *>(y + ((int64_t)ch * R + row) * 8);
+        uint4 *dst = reinterpret_cast<uint4 *>(y + ((int64_t)ch * Ry + row) * 8);
 #pragma unroll
         for (int i = 0; i < 4; ++i) dst[i] = *reinterpret_cast<const uint4 *>(h[i]);
     }
 }
 
-void prologue_h(const float *x, __half *y, int64_t R, int C, int m, int extra, const Batch &b, int max_len,
-                const PrologueArgs &a, cudaStream_t st) {
+void prologue_h(const float *x, __half *y, int64_t R, int64_t Ry, int C, int m, int extra, const Batch &b,
+                int max_len, const PrologueArgs &a, cudaStream_t st) {
     int bx = (max_len + 1023) / 1024;
     if (bx > 16) bx = 16;
-    k_prologue_h<<<dim3(bx, (C + 7) / 8, b.n), 256, 0, st>>>(x, y, R, C, m, extra, b, a);
+    const dim3 grid(bx, (C + 7) / 8, b.n);
+    if (a.norm) {
+        if (a.act == ACT_SNAKE)
+            k_prologue_h<true, ACT_SNAKE><<<grid, 256, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
+        else if (a.act == ACT_LEAKY)
+            k_prologue_h<true, ACT_LEAKY><<<grid, 256, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
+        else
+            k_prologue_h<true, ACT_NONE><<<grid, 256, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
+    } else {
+        if (a.act == ACT_SNAKE)
+            k_prologue_h<false, ACT_SNAKE><<<grid, 256, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
+        else if (a.act == ACT_LEAKY)
+            k_prologue_h<false, ACT_LEAKY><<<grid, 256, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
+        else
+            k_prologue_h<false, ACT_NONE><<<grid, 256, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
+    }
 }
 
 // Depthwise x2 pool (see k_pool_up) written as the half chunk-major operand
 // of the following F16 convolution (its input is rounded to half there).
-__global__ void k_pool_up_h(const float *__restrict__ x, __half *__restrict__ y, int64_t R_in, int64_t R_out,
+__global__ void k_pool_up_h(const float *__restrict__ x, __half *__restrict__ y, int64_t R_in, int64_t Ry_out,
                             int C, const float *__restrict__ w, const float *__restrict__ bias, Batch b) {
     const int u = blockIdx.z, ch = blockIdx.y;
     const int64_t L = b.T[u];
@@ -326,16 +344,16 @@ __global__ void k_pool_up_h(const float *__restrict__ x, __half *__restrict__ y,
             }
             h[e] = __float2half_rn(v);
         }
-        *reinterpret_cast<uint4 *>(y + ((int64_t)ch * R_out + 2 * b.offT[u] + t) * 8) =
+        *reinterpret_cast<uint4 *>(y + ((int64_t)ch * Ry_out + 2 * b.offT[u] + t) * 8) =
             *reinterpret_cast<const uint4 *>(h);
     }
 }
 
-void pool_up_h(const __half *, const float *x, __half *y, int64_t R_in, int64_t R_out, int C, const float *w,
-               const float *bias, const Batch &b, int max_T, cudaStream_t st) {
+void pool_up_h(const float *x, __half *y, int64_t R_in, int64_t Ry_out, int C, const float *w, const float *bias,
+               const Batch &b, int max_T, cudaStream_t st) {
     int bx = (2 * max_T + 255) / 256;
     if (bx > 16) bx = 16;
-    k_pool_up_h<<<dim3(bx, (C + 7) / 8, b.n), 256, 0, st>>>(x, y, R_in, R_out, C, w, bias, b);
+    k_pool_up_h<<<dim3(bx, (C + 7) / 8, b.n), 256, 0, st>>>(x, y, R_in, Ry_out, C, w, bias, b);
 }
 
 // Space-to-depth operand of the stride-6 noise convolution: every packed row
@@ -343,7 +361,8 @@ void pool_up_h(const __half *, const float *x, __half *y, int64_t R_in, int64_t 
 // half(har[ic][6 t' + r - 3]), r = 0..5, so that the k=12 / stride-6 / pad-3
 // convolution becomes a stride-1 convolution with 2 taps. All rows are
 // written: outside an utterance they read the zero gaps of har.
-__global__ void k_har_s2d(const float *__restrict__ har, int64_t R_har, __half *__restrict__ y, int64_t R) {
+__global__ void k_har_s2d(const float *__restrict__ har, int64_t R_har, __half *__restrict__ y, int64_t R,
+                          int64_t Ry) {
     const int ch = blockIdx.y;  // output chunk of 8 (24 chunks = 192 padded channels)
     for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < R; t += (int64_t)gridDim.x * blockDim.x) {
         __align__(16) __half h[8];
@@ -358,14 +377,14 @@ __global__ void k_har_s2d(const float *__restrict__ har, int64_t R_har, __half *
             }
             h[e] = __float2half_rn(v);
         }
-        *reinterpret_cast<uint4 *>(y + ((int64_t)ch * R + t) * 8) = *reinterpret_cast<const uint4 *>(h);
+        *reinterpret_cast<uint4 *>(y + ((int64_t)ch * Ry + t) * 8) = *reinterpret_cast<const uint4 *>(h);
     }
 }
 
-void har_s2d(const float *har, int64_t R_har, __half *y, int64_t R, cudaStream_t st) {
+void har_s2d(const float *har, int64_t R_har, __half *y, int64_t R, int64_t Ry, cudaStream_t st) {
     int bx = (int)((R + 255) / 256);
     if (bx > 2048) bx = 2048;
-    k_har_s2d<<<dim3(bx, 24), 256, 0, st>>>(har, R_har, y, R);
+    k_har_s2d<<<dim3(bx, 24), 256, 0, st>>>(har, R_har, y, R, Ry);
 }
 
 // ---------------------------------------------------------------------------

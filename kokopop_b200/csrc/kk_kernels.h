@@ -60,7 +60,7 @@ struct ConvArgs {
 struct ConvTRow0Args {
     const float *in;      // F32 [C][R] operand, or
     const __half *in_h;   // half chunk-major operand (when non-null)
-    int64_t R_in;
+    int64_t R_in;         // row stride of `in`, or the chunk stride of `in_h`
     int IC, m_in;
     const float *w;  // ggml [K, OC, IC]
     int OC, K, crop, m_out;
@@ -116,8 +116,20 @@ void istft(const float *post, int64_t R, int a_nf, float *audio, const Batch &b,
 void conv_simt(const ConvArgs &a, cudaStream_t st);
 cudaError_t conv_simt_init();
 
+// Half chunk-major operands of the tensor-core path. Channel chunk j (8
+// channels) holds rows [-kHalfLo, R + kHalfHi) at a stride of
+// Ry = R + kHalfLo + kHalfHi rows of 16 bytes; the pointer handed around
+// addresses row 0 of chunk 0, so row r of chunk j is y[(j * Ry + r) * 8 ...].
+// The margins (and all gap rows) read as zero: they are the convolution's
+// zero padding, fetched with plain bulk copies instead of a clipped tensor
+// map.
+constexpr int64_t kHalfLo = 64;
+constexpr int64_t kHalfHi = 256;
+__host__ __device__ constexpr int64_t half_stride(int64_t R) { return R + kHalfLo + kHalfHi; }
+
 // kk_conv_tc.cu: tensor-core convolution, stride 1, half operands.
-// in: chunk-major half [IC_pad/8][R_in][8]; w: packed half
+// in: half operand (row 0 of chunk 0), chunk stride R_in = half_stride(R)
+// for an operand of R rows; n_pos <= R. w: packed half
 // [K][IC_pad/64][n_tiles][8][128][8]; epilogue as ConvArgs.
 struct ConvTcArgs {
     const __half *in;
@@ -143,15 +155,17 @@ cudaError_t conv_tc_init();
 cudaError_t conv_tc(const ConvTcArgs &a, cudaStream_t st);
 int conv_tc_max_halo();
 
-// Half-precision chunk-major operands for the tensor-core path.
-// prologue_h: y[c/8][row][c%8] = half(act(adain(x[c][row]))) on valid rows.
-void prologue_h(const float *x, __half *y, int64_t R, int C, int m, int extra, const Batch &b, int max_len,
-                const PrologueArgs &a, cudaStream_t st);
-// har_s2d: space-to-depth half operand [192/8][R][8] of the stride-6
-// noise convolution (132 real channels), all R rows of the stage-0 level.
-void har_s2d(const float *har, int64_t R_har, __half *y, int64_t R, cudaStream_t st);
-// pool_up_h: the depthwise x2 pool written as a half chunk-major operand.
-void pool_up_h(const __half *x_unused, const float *x, __half *y, int64_t R_in, int64_t R_out, int C,
-               const float *w, const float *bias, const Batch &b, int max_T, cudaStream_t st);
+// prologue_h: y[c/8][row][c%8] = half(act(adain(x[c][row]))) on valid rows
+// (x is F32 [C][R]; y a half operand of chunk stride Ry).
+void prologue_h(const float *x, __half *y, int64_t R, int64_t Ry, int C, int m, int extra, const Batch &b,
+                int max_len, const PrologueArgs &a, cudaStream_t st);
+// har_s2d: space-to-depth half operand [192/8][R][8] (chunk stride Ry) of the
+// stride-6 noise convolution (132 real channels), all R rows of the stage-0
+// level.
+void har_s2d(const float *har, int64_t R_har, __half *y, int64_t R, int64_t Ry, cudaStream_t st);
+// pool_up_h: the depthwise x2 pool written as a half operand of chunk stride
+// Ry_out.
+void pool_up_h(const float *x, __half *y, int64_t R_in, int64_t Ry_out, int C, const float *w, const float *bias,
+               const Batch &b, int max_T, cudaStream_t st);
 
 }  // namespace kk
