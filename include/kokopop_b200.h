@@ -105,6 +105,27 @@ int kk_generator_forward(kk_ctx *ctx, int32_t n_utts, const int32_t *n_decoder_f
  * [(n_frames - 1) * 5], clamped to +-1. n_frames may be 0 or 1 (no samples). */
 int kk_istft(kk_ctx *ctx, int64_t n_frames, const float *post, float *audio);
 
+/* kk_istft without any device allocation (no counterpart in the reference,
+ * whose iSTFT runs on the host). Same arguments and results as kk_istft, but
+ * no kk_ctx: input, output, tables and descriptor are staged in one static
+ * device array of the library (about 3.5 MB per device, reserved when the
+ * library's device code loads), so the call never allocates or frees device
+ * memory. For callers that cannot allocate mid-run: a real-time audio thread
+ * (cudaMalloc / cudaFree can synchronise the whole device) or a process that
+ * fixes its device-memory budget up front.
+ *   device   CUDA device to run on (made current for the call, then restored)
+ *   stream   a stream of that device, or NULL for its legacy default stream;
+ *            the call returns after the stream has finished the copy back
+ *   n_frames at most KK_ISTFT_STATIC_MAX_FRAMES; larger inputs are rejected
+ *            with KK_ERROR_INVALID_ARGUMENT (use kk_istft for them)
+ * The first call on each device looks up the array's address and uploads the
+ * tables (synchronous): make it before any stream capture starts. Nothing in
+ * the array has to start at zero. Calls that overlap in time on one device
+ * (from several threads, or on several streams) share the array and
+ * overwrite each other's data: serialise them. */
+#define KK_ISTFT_STATIC_MAX_FRAMES 32768
+int kk_istft_static(int device, int64_t n_frames, const float *post, float *audio, void *stream);
+
 /* Counters of a context, for measurement (no counterpart in the reference,
  * which prints ggml_time_us stage timings under KOKOPOP_GEN_PROFILE,
  * src/arch/kokoro/audio_utils.cpp:834-893). */

@@ -74,6 +74,7 @@ def load_library():
     L.kk_decoder_forward_device.argtypes = [vp, ctypes.c_int32, _i32p, vp, vp, vp, vp, vp, vp]
     L.kk_generator_forward.argtypes = [vp, ctypes.c_int32, _i32p, _f32p, _f32p, _f32p, _f32p]
     L.kk_istft.argtypes = [vp, ctypes.c_int64, _f32p, _f32p]
+    L.kk_istft_static.argtypes = [ctypes.c_int, ctypes.c_int64, _f32p, _f32p, vp]
     L.kk_profile_enable.argtypes = [vp, ctypes.c_int]
     L.kk_profile_read.argtypes = [vp, ctypes.POINTER(Profile), ctypes.c_int]
     _lib = L

@@ -161,6 +161,11 @@ static void make_tables(StftTables &st, IstftTables &is) {
         }
 }
 
+namespace kk {
+void fill_tables(StftTables &st, IstftTables &is) { make_tables(st, is); }
+void set_last_error(const std::string &msg) { g_last_error = msg; }
+}  // namespace kk
+
 static std::vector<std::string> adain_site_prefixes() {
     std::vector<std::string> v;
     const std::string d = "kokopop.decoder.";

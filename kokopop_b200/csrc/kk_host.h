@@ -70,6 +70,11 @@ struct Plan {
 
 Plan make_plan(const int32_t *lens, int n);
 
+// The STFT / iSTFT tables (C library values) and the calling thread's
+// kk_last_error() slot, for entry points outside kk_host.cpp.
+void fill_tables(StftTables &st, IstftTables &is);
+void set_last_error(const std::string &msg);
+
 }  // namespace kk
 
 struct kk_ctx {
