@@ -64,7 +64,7 @@ constexpr int TC_BLK_BYTES = 32 * 32 * 4;        // one [32 ch][32 rows] F32 epi
 __host__ __device__ constexpr int tc_nsb(bool tma_epi) { return tma_epi ? 4 : 8; }
 __host__ __device__ constexpr int tc_smem(bool tma_epi) {
     return TC_NSA * TC_A_BYTES + tc_nsb(tma_epi) * TC_B_BYTES + (tma_epi ? TC_EPI_WARPS * 2 * TC_BLK_BYTES : 0) +
-           2048 /*bias*/ + 1024 /*barriers*/ + 1024 /*align*/;
+           4096 /*bias*/ + 1024 /*barriers*/ + 1024 /*align*/;
 }
 constexpr unsigned long long TC_WAIT_NS = 2000000000ull;   // 2 s
 constexpr unsigned long long TC_DRAIN_NS = 200000000ull;   // 0.2 s
@@ -213,6 +213,8 @@ struct TcParams {
     int OC;           // real output channels
     int n_tiles;      // OC tiles of 128 in the packed weights
     int n_oc_tiles;   // OC tiles computed
+    int mma_n;        // MMA N: 128, or the channel count rounded to 16 when it is smaller
+    int phase_oc;     // > 0: output channel n is channel n % phase_oc of phase n / phase_oc
     int64_t m_tiles;  // position tiles of 256
     const __half *a;  // half operand, row 0 of chunk 0
     int64_t R_a;      // chunk stride (rows)
@@ -245,8 +247,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     uint8_t *sA = smem;
     uint8_t *sB = smem + TC_NSA * TC_A_BYTES;
     uint8_t *sE = sB + NSB * TC_B_BYTES;  // epilogue blocks (TMA_EPI)
-    float *sbias = (float *)(sE + (TMA_EPI ? TC_EPI_WARPS * 2 * TC_BLK_BYTES : 0));  // [512]
-    uint64_t *bars = (uint64_t *)((uint8_t *)sbias + 2048);
+    float *sbias = (float *)(sE + (TMA_EPI ? TC_EPI_WARPS * 2 * TC_BLK_BYTES : 0));  // [1024]
+    uint64_t *bars = (uint64_t *)((uint8_t *)sbias + 4096);
     // A_full[2] A_empty[2] B_full[NSB] B_empty[NSB] acc_full[2] acc_empty[2]
     // drain res[8 warps][2] tmem-slot
     const uint32_t bA_full = smem_u32(bars + 0), bA_empty = smem_u32(bars + 2);
@@ -283,7 +285,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     if (TMA_EPI && warp >= 2) {
-        for (int i = threadIdx.x - 64; i < 512; i += 32 * TC_EPI_WARPS)
+        for (int i = threadIdx.x - 64; i < 1024; i += 32 * TC_EPI_WARPS)
             sbias[i] = (P.bias && i < P.OC) ? P.bias[i] : 0.f;
     }
     fence_before_sync();
@@ -336,7 +338,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     } else if (warp == 1) {
         if (lane == 0) {
             // MMA issuer
-            const uint32_t idesc = idesc_f16(TC_HM, TC_BN);
+            const uint32_t idesc = idesc_f16(TC_HM, P.mma_n);
             bool ok = true;
             uint32_t ia = 0, ib = 0, it = 0;
             for (int64_t tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x, ++it) {
@@ -397,6 +399,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const int n0 = (int)(tile % P.n_oc_tiles) * TC_BN;
             const int ab = it & 1;
             const int64_t qw = mt * TC_BM + half * TC_HM + lg * 32;  // first row of this warp
+            // phase-packed transposed conv: this tile's channels belong to
+            // phase r, whose output rows are q * omul + oadd + r
+            const int ph = P.phase_oc > 0 ? n0 / P.phase_oc : 0;
+            const int oc0 = n0 - ph * P.phase_oc;
             if (TMA_EPI && has_res && lane == 0) {
                 // the residual of this tile's first block, requested before the
                 // accumulator is ready
@@ -411,7 +417,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             __syncwarp();
             fence_after_sync();
             const int64_t q = qw + lane;
-            const int64_t orow = q * P.omul + P.oadd;
+            const int64_t orow = q * P.omul + P.oadd + ph;
             const bool row_ok = q < P.n_pos && orow >= 0 && orow < P.R_out;
             const uint32_t t_base = tmem + ((uint32_t)(lg * 32) << 16) + (uint32_t)(ab * 2 * TC_BN + half * TC_BN);
             for (int c0 = 0; c0 < TC_BN; c0 += 32) {
@@ -469,7 +475,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     ++ci;
                 } else {
                     const int64_t rrow = P.resid_half ? (orow >> 1) : orow;
-                    const float b_lane = (P.bias && lane < nj) ? __ldg(P.bias + n0 + c0 + lane) : 0.f;
+                    const float b_lane = (P.bias && lane < nj) ? __ldg(P.bias + oc0 + c0 + lane) : 0.f;
                     // The residual and the accumulated output may alias the
                     // output (in-place updates): read all of this row's values
                     // first so the loads overlap, then compute and store.
@@ -477,7 +483,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
                         const bool live = row_ok && j < nj;
-                        const int64_t oc = n0 + c0 + j;
+                        const int64_t oc = oc0 + c0 + j;
                         res[j] = (has_res && live) ? P.resid[oc * P.R_resid + rrow] : 0.f;
                         old[j] = (P.accum && live) ? P.out[oc * P.R_out + orow] : 0.f;
                     }
@@ -490,7 +496,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         if (P.scale1 != 1.0f) v = __fmul_rn(v, P.scale1);
                         if (P.accum) v = __fadd_rn(old[j], v);
                         if (P.scale2 != 1.0f) v = __fmul_rn(v, P.scale2);
-                        if (row_ok && j < nj) P.out[(int64_t)(n0 + c0 + j) * P.R_out + orow] = v;
+                        if (row_ok && j < nj) P.out[(int64_t)(oc0 + c0 + j) * P.R_out + orow] = v;
                     }
                 }
             }
@@ -575,6 +581,10 @@ cudaError_t conv_tc(const ConvTcArgs &a, cudaStream_t st) {
     P.OC = a.OC;
     P.n_tiles = a.n_tiles;
     P.n_oc_tiles = (a.OC + TC_BN - 1) / TC_BN;
+    P.mma_n = a.OC < TC_BN ? (a.OC + 15) / 16 * 16 : TC_BN;
+    P.phase_oc = a.phase_oc;
+    if (a.phase_oc < 0 || (a.phase_oc > 0 && (a.phase_oc % TC_BN != 0 || a.OC % a.phase_oc != 0)))
+        return cudaErrorInvalidValue;
     P.m_tiles = (a.n_pos + TC_BM - 1) / TC_BM;
     // the last slab must stay inside the chunk: rows < R + kHalfHi where the
     // operand has R = R_in - kHalfLo - kHalfHi rows
@@ -600,8 +610,8 @@ cudaError_t conv_tc(const ConvTcArgs &a, cudaStream_t st) {
     CUtensorMap omap, rmap;
     memset(&omap, 0, sizeof(omap));
     memset(&rmap, 0, sizeof(rmap));
-    bool tma = g_encode && a.omul == 1 && a.oadd == 0 && a.n_pos == a.R_out && !a.resid_half && a.OC >= 64 &&
-               a.OC <= 512 && (!a.resid || a.R_resid == a.R_out);
+    bool tma = g_encode && a.omul == 1 && a.oadd == 0 && a.phase_oc == 0 && a.n_pos == a.R_out && !a.resid_half &&
+               a.OC >= 64 && a.OC <= 1024 && (!a.resid || a.R_resid == a.R_out);
     if (tma) tma = block_map(&omap, a.out, a.R_out, a.OC) && block_map(&rmap, a.resid ? a.resid : a.out, a.R_out, a.OC);
     const int64_t tiles = P.m_tiles * P.n_oc_tiles;
     const int64_t slots = g_num_sms > 0 ? g_num_sms : 148;

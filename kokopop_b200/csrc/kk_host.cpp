@@ -316,9 +316,17 @@ void kk_ctx::derive() {
             const DevTensor &t = W("kokopop.decoder.generator.ups." + std::to_string(s) + ".weight");
             const int OC = (int)t.ne[1], IC = (int)t.ne[2], S = strides[s];
             const std::vector<float> &ph = phase_host[s];
-            for (int r = 0; r < S; ++r)
-                pack_tc(packed["ups." + std::to_string(s) + ".phase." + std::to_string(r)], OC, IC, 2,
-                        [&](int oc, int ic, int k) { return ph[(((size_t)r * OC + oc) * IC + ic) * 2 + k]; });
+            if (OC % 128 == 0) {
+                // all phases as one convolution, phase-major output channels
+                // n = r * OC + oc, so the CTAs writing the interleaved rows of
+                // one position tile run together
+                pack_tc(packed["ups." + std::to_string(s) + ".phases"], S * OC, IC, 2,
+                        [&](int n, int ic, int k) { return ph[((size_t)n * IC + ic) * 2 + k]; });
+            } else {
+                for (int r = 0; r < S; ++r)
+                    pack_tc(packed["ups." + std::to_string(s) + ".phase." + std::to_string(r)], OC, IC, 2,
+                            [&](int oc, int ic, int k) { return ph[(((size_t)r * OC + oc) * IC + ic) * 2 + k]; });
+            }
         }
         d_err.ensure(sizeof(int));
         check_cuda(cudaMemset(d_err.p, 0, sizeof(int)), "clear error");
@@ -591,8 +599,9 @@ struct Runner {
 
     // Tensor-core convolution on a half chunk-major operand.
     void conv_h(const PackedW &pw, const Op &in, int K, int p, int d, float *out, int64_t R_out, int64_t n_pos,
-                const Epi &e) {
+                const Epi &e, int phase_oc = 0) {
         ConvTcArgs a{};
+        a.phase_oc = phase_oc;
         a.in = in.h;
         a.R_in = in.Ry;
         a.IC_pad = pw.IC_pad;
@@ -819,7 +828,18 @@ struct Runner {
             const DevTensor &ub = c.W(g + "ups." + ss + ".bias");
             if ((int)uw.ne[1] != Cs || (int)uw.ne[2] != C) throw KKError(KK_ERROR_MODEL, "ups shape mismatch");
             const int S = sp[s].up_stride, crop = sp[s].up_padding, pad = s == 1 ? 1 : 0;
-            for (int r = 0; r < S; ++r) {
+            auto all_phases = c.packed.find("ups." + ss + ".phases");
+            if (tc && all_phases != c.packed.end()) {
+                Epi e;
+                e.bias = &ub;
+                e.resid = xs;
+                e.R_resid = Rm;
+                e.omul = S;
+                e.oadd = -crop + pad;
+                e.valid = sum_len(m_prev, 0);
+                conv_h(all_phases->second, op_prev, 2, 1, 1, xst, Rm, Rp, e, Cs);
+            }
+            for (int r = 0; r < S && !(tc && all_phases != c.packed.end()); ++r) {
                 Epi e;
                 e.bias = &ub;
                 e.resid = xs;

@@ -150,6 +150,9 @@ struct ConvTcArgs {
     int accum;
     float scale2;
     int *err;
+    // > 0: the weights are phase-packed (OC = phases x phase_oc, phase-major);
+    // channel n writes channel n % phase_oc at rows q * omul + oadd + n / phase_oc
+    int phase_oc;
 };
 cudaError_t conv_tc_init();
 cudaError_t conv_tc(const ConvTcArgs &a, cudaStream_t st);
