@@ -621,7 +621,9 @@ __global__ void __launch_bounds__(256) k_istft(const float *__restrict__ post, i
     const int u = blockIdx.y;
     const int64_t nf = (int64_t)a_nf * b.T[u] + 1;
     const int64_t f0 = (int64_t)blockIdx.x * IS_FB;
-    if (f0 >= nf) return;
+    // output j = p - 10 reaches p = 5 nf + 4, so the block starting at
+    // f0 = nf (when nf is a multiple of the block) still has samples to write
+    if (f0 > nf) return;
     const int64_t base = (int64_t)a_nf * b.offT[u];
     // frames f0-3 .. f0+FB-1
     for (int q = threadIdx.x; q < IS_FB + 3; q += blockDim.x) {
@@ -682,7 +684,7 @@ __global__ void __launch_bounds__(256) k_istft(const float *__restrict__ post, i
 void istft(const float *post, int64_t R, int a_nf, float *audio, const Batch &b, const int64_t *cumT,
            const IstftTables *tab, int max_T, cudaStream_t st) {
     const int64_t nf = (int64_t)a_nf * max_T + 1;
-    k_istft<<<dim3((unsigned)((nf + IS_FB - 1) / IS_FB), b.n), 256, 0, st>>>(post, R, a_nf, audio, b, cumT,
+    k_istft<<<dim3((unsigned)(nf / IS_FB + 1), b.n), 256, 0, st>>>(post, R, a_nf, audio, b, cumT,
                                                                             tab);
 }
 

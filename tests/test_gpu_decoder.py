@@ -41,7 +41,7 @@ def test_istft_known_answer(ctx):
     assert out.shape == (10,) and abs(out[0] + 0.08) < 1e-4
 
 
-@pytest.mark.parametrize("n", [0, 1, 2, 3, 50, 1001, 24001])
+@pytest.mark.parametrize("n", [0, 1, 2, 3, 50, 255, 256, 257, 512, 1001, 24001])
 def test_istft_matches_oracle(ctx, n):
     rng = np.random.default_rng(n)
     post = rng.normal(0.0, 2.0, size=(22, n)).astype(np.float32)
