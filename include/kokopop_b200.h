@@ -105,6 +105,40 @@ int kk_generator_forward(kk_ctx *ctx, int32_t n_utts, const int32_t *n_decoder_f
  * [(n_frames - 1) * 5], clamped to +-1. n_frames may be 0 or 1 (no samples). */
 int kk_istft(kk_ctx *ctx, int64_t n_frames, const float *post, float *audio);
 
+/* Bidirectional LSTM layer `prefix` (weights prefix.weight_ih_l0[_reverse],
+ * .weight_hh_l0[_reverse], .bias_ih_l0[_reverse], .bias_hh_l0[_reverse];
+ * hidden size 256) over a ragged batch. Replaces bidirectional_lstm
+ * (src/arch/kokoro/graph_ops.cpp:1514-1529): the input projection of
+ * lstm_direction (:1439-1512) and the fused recurrence cpu_lstm_contiguous
+ * (src/arch/kokoro/lstm_fused.cpp:200-247), gate order i, f, g, o.
+ *   n_steps[b] = N_b in [1, 65536]
+ *   x   : per sequence [N_b, in_dim] (feature-fastest), back to back
+ *   out : per sequence [N_b, 512]: forward h in [0, 256), backward in [256, 512)
+ * Host buffers. */
+int kk_bilstm_forward(kk_ctx *ctx, const char *prefix, int32_t n_seqs, const int32_t *n_steps, int64_t in_dim,
+                      const float *x, float *out);
+
+/* The prosody duration encoder (duration_encoder,
+ * src/arch/kokoro/graph_ops.cpp:1535-1576): 3 x (concat style -> biLSTM
+ * kokopop.predictor.text_encoder.lstms.{0,2,4} -> AdaLayerNorm
+ * ...lstms.{1,3,5}), output concatenated with the style once more.
+ *   x     : per sequence [N_b, 512]
+ *   style : per sequence [128] (the prosody half of the voice row)
+ *   out   : per sequence [N_b, 640]
+ * Host buffers. */
+int kk_duration_encoder_forward(kk_ctx *ctx, int32_t n_seqs, const int32_t *n_steps, const float *x,
+                                const float *style, float *out);
+
+/* Durations -> frames and the alignment (duration_to_frames,
+ * src/arch/kokoro/kokoro.cpp:181-193; build_duration_mask :115-152 and
+ * en = d . mask :669-674): frames[i] = clamp(int(lrint(d[i] / speed)), 1, 50)
+ * (non-finite -> 1; a non-finite or non-positive speed counts as 1),
+ * *total = sum(frames). If hidden != NULL (then en != NULL): en[f, :] =
+ * hidden[token(f), :] for every frame f, en holding en_capacity rows of
+ * hidden_dim. At most 65535 tokens. Host buffers. */
+int kk_align_durations(kk_ctx *ctx, int64_t n_tokens, const float *durations, float speed, int32_t *frames,
+                       int64_t *total, const float *hidden, int64_t hidden_dim, float *en, int64_t en_capacity);
+
 /* kk_istft without any device allocation (no counterpart in the reference,
  * whose iSTFT runs on the host). Same arguments and results as kk_istft, but
  * no kk_ctx: input, output, tables and descriptor are staged in one static

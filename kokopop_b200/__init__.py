@@ -75,6 +75,10 @@ def load_library():
     L.kk_generator_forward.argtypes = [vp, ctypes.c_int32, _i32p, _f32p, _f32p, _f32p, _f32p]
     L.kk_istft.argtypes = [vp, ctypes.c_int64, _f32p, _f32p]
     L.kk_istft_static.argtypes = [ctypes.c_int, ctypes.c_int64, _f32p, _f32p, vp]
+    L.kk_bilstm_forward.argtypes = [vp, ctypes.c_char_p, ctypes.c_int32, _i32p, ctypes.c_int64, _f32p, _f32p]
+    L.kk_duration_encoder_forward.argtypes = [vp, ctypes.c_int32, _i32p, _f32p, _f32p, _f32p]
+    L.kk_align_durations.argtypes = [vp, ctypes.c_int64, _f32p, ctypes.c_float, _i32p,
+                                     ctypes.POINTER(ctypes.c_int64), _f32p, ctypes.c_int64, _f32p, ctypes.c_int64]
     L.kk_profile_enable.argtypes = [vp, ctypes.c_int]
     L.kk_profile_read.argtypes = [vp, ctypes.POINTER(Profile), ctypes.c_int]
     _lib = L
@@ -193,3 +197,45 @@ class Context:
         audio = np.zeros(max(1, (n - 1) * 5), np.float32)
         self._check(self.L.kk_istft(self.h, n, _ptr(post), _ptr(audio)))
         return audio[: max(0, (n - 1) * 5)]
+
+    # ---- LSTM stack and durations ----
+
+    def bilstm(self, prefix: str, xs: Sequence[np.ndarray]) -> List[np.ndarray]:
+        """kk_bilstm_forward over sequences xs[b] of shape [N_b, in_dim];
+        returns [N_b, 512] each (forward h, then backward h)."""
+        xs = [np.ascontiguousarray(x, np.float32) for x in xs]
+        lens = np.array([x.shape[0] for x in xs], np.int32)
+        x = np.concatenate(xs, axis=0)
+        out = np.zeros((int(lens.sum()), 512), np.float32)
+        self._check(self.L.kk_bilstm_forward(self.h, prefix.encode(), len(xs), _ptr(lens, _i32p), x.shape[1],
+                                             _ptr(x), _ptr(out)))
+        return np.split(out, np.cumsum(lens)[:-1])
+
+    def duration_encoder(self, xs: Sequence[np.ndarray], styles: Sequence[np.ndarray]) -> List[np.ndarray]:
+        """kk_duration_encoder_forward: xs[b] [N_b, 512], styles[b] [128] ->
+        [N_b, 640] each."""
+        xs = [np.ascontiguousarray(x, np.float32) for x in xs]
+        lens = np.array([x.shape[0] for x in xs], np.int32)
+        x = np.concatenate(xs, axis=0)
+        st = np.ascontiguousarray(np.stack(styles), np.float32)
+        out = np.zeros((int(lens.sum()), 640), np.float32)
+        self._check(self.L.kk_duration_encoder_forward(self.h, len(xs), _ptr(lens, _i32p), _ptr(x), _ptr(st),
+                                                       _ptr(out)))
+        return np.split(out, np.cumsum(lens)[:-1])
+
+    def align_durations(self, durations: np.ndarray, speed: float, hidden: Optional[np.ndarray] = None):
+        """kk_align_durations: (frames int32 [n], total, en [total, D] or None)."""
+        d = np.ascontiguousarray(durations, np.float32)
+        n = len(d)
+        frames = np.zeros(max(n, 1), np.int32)
+        total = ctypes.c_int64(0)
+        if hidden is None:
+            self._check(self.L.kk_align_durations(self.h, n, _ptr(d), speed, _ptr(frames, _i32p),
+                                                  ctypes.byref(total), None, 0, None, 0))
+            return frames[:n], total.value, None
+        hidden = np.ascontiguousarray(hidden, np.float32)
+        cap = 50 * max(n, 1)
+        en = np.zeros((cap, hidden.shape[1]), np.float32)
+        self._check(self.L.kk_align_durations(self.h, n, _ptr(d), speed, _ptr(frames, _i32p), ctypes.byref(total),
+                                              _ptr(hidden), hidden.shape[1], _ptr(en), cap))
+        return frames[:n], total.value, en[: total.value]

@@ -99,6 +99,14 @@ kk_ctx::~kk_ctx() {
     for (auto &kv : w) cudaFree(kv.second.d);
     for (auto &kv : ws) kv.second.release();
     for (auto &b : convt_phase) b.release();
+    for (auto &kv : packed) kv.second.buf.release();
+    for (auto &kv : adain_t) kv.second.release();
+    for (auto &kv : lstm) {
+        kv.second.wih.release();
+        kv.second.wih_tc.buf.release();
+        kv.second.bih_buf.release();
+    }
+    d_err.release();
     d_sites.release();
     d_tables.release();
     d_batch.release();
@@ -272,7 +280,14 @@ void kk_ctx::derive() {
     }
     // tensor-core path: taken when every convolution weight is stored as F16
     // (the converter's policy); F32 weight sets keep the F32 CUDA-core path.
+    for (auto &kv : packed) kv.second.buf.release();
     packed.clear();
+    for (auto &kv : lstm) {
+        kv.second.wih.release();
+        kv.second.wih_tc.buf.release();
+        kv.second.bih_buf.release();
+    }
+    lstm.clear();
     tc_mode = ok && convt_f16[0] && convt_f16[1];
     for (const auto &cv : tc_convs()) {
         const DevTensor *t = Wopt(cv.first);
@@ -429,6 +444,46 @@ Plan kk::make_plan(const int32_t *lens, int n) {
     return P;
 }
 
+const LstmLayer &kk_ctx::lstm_layer(const std::string &prefix) {
+    auto it = lstm.find(prefix);
+    if (it != lstm.end()) return it->second;
+    const DevTensor &wf = W(prefix + ".weight_ih_l0"), &wb = W(prefix + ".weight_ih_l0_reverse");
+    const DevTensor &hf = W(prefix + ".weight_hh_l0"), &hb = W(prefix + ".weight_hh_l0_reverse");
+    const DevTensor &bif = W(prefix + ".bias_ih_l0"), &bib = W(prefix + ".bias_ih_l0_reverse");
+    const DevTensor &bhf = W(prefix + ".bias_hh_l0"), &bhb = W(prefix + ".bias_hh_l0_reverse");
+    // load_lstm_weights (graph_ops.cpp:1439-1450): w_ih ne [in, 4H], w_hh ne [H, 4H]
+    const int64_t H = hf.ne[0], H4 = hf.ne[1], in = wf.ne[0];
+    if (H != 256 || H4 != 4 * H || hb.ne[0] != H || hb.ne[1] != H4 || wf.ne[1] != H4 || wb.ne[0] != in ||
+        wb.ne[1] != H4 || bif.n != H4 || bib.n != H4 || bhf.n != H4 || bhb.n != H4)
+        throw KKError(KK_ERROR_MODEL, "unsupported LSTM shapes (hidden must be 256): " + prefix);
+    if (wf.f16 != wb.f16) throw KKError(KK_ERROR_MODEL, "mixed W_ih types: " + prefix);
+    LstmLayer L;
+    L.in_dim = (int)in;
+    L.H = (int)H;
+    L.f16 = wf.f16;
+    const size_t nw = (size_t)H4 * in;
+    L.wih.ensure(2 * nw * sizeof(float));
+    check_cuda(cudaMemcpy(L.wih.p, wf.d, nw * sizeof(float), cudaMemcpyDeviceToDevice), "stack W_ih");
+    check_cuda(cudaMemcpy((float *)L.wih.p + nw, wb.d, nw * sizeof(float), cudaMemcpyDeviceToDevice), "stack W_ih");
+    L.bih_buf.ensure(2 * (size_t)H4 * sizeof(float));
+    check_cuda(cudaMemcpy(L.bih_buf.p, bif.d, (size_t)H4 * 4, cudaMemcpyDeviceToDevice), "stack b_ih");
+    check_cuda(cudaMemcpy((float *)L.bih_buf.p + H4, bib.d, (size_t)H4 * 4, cudaMemcpyDeviceToDevice), "stack b_ih");
+    L.bih.d = (float *)L.bih_buf.p;
+    L.bih.ne[0] = 2 * H4;
+    L.bih.n = 2 * H4;
+    if (L.f16) {
+        check_cuda(conv_tc_init(), "tensor-core conv init");
+        std::vector<float> h(2 * nw);
+        check_cuda(cudaMemcpy(h.data(), L.wih.p, h.size() * 4, cudaMemcpyDeviceToHost), "read W_ih");
+        pack_tc(L.wih_tc, (int)(2 * H4), (int)in, 1, [&](int oc, int ic, int) { return h[(size_t)oc * in + ic]; });
+    }
+    L.whh[0] = hf.d;
+    L.whh[1] = hb.d;
+    L.bhh[0] = bhf.d;
+    L.bhh[1] = bhb.d;
+    return lstm.emplace(prefix, std::move(L)).first->second;
+}
+
 // ---------------------------------------------------------------------------
 // the forward pass
 // ---------------------------------------------------------------------------
@@ -517,11 +572,14 @@ struct Runner {
     int64_t sum_len(int m, int extra) const { return (int64_t)m * P.total + (int64_t)extra * P.n; }
 
     // The operand buffer of a level (multiplier m) with room for C channels.
-    Op op(const char *name, int m, int C) {
+    Op op(const char *name, int m, int C) { return op(name, m, C, tc); }
+
+    // half == true: the tensor-core operand whatever the context's mode
+    Op op(const char *name, int m, int C, bool half) {
         Op o;
         o.R = R(m);
         o.Ry = o.R;
-        if (tc) {
+        if (half) {
             const int cpad = (C + 63) / 64 * 64;
             o.Ry = half_stride(o.R);
             o.h = (__half *)c.buf(name, ((size_t)cpad * o.Ry + 1) / 2) + kHalfLo * 8;
@@ -903,6 +961,55 @@ struct Runner {
         ++c.n_launches;
     }
 
+    // ---- LSTM stack: the plan is one "utterance" of R rows (rows t * B + b) ----
+
+    // Sequences of a bidirectional layer: device lengths and output offsets.
+    struct Seqs {
+        int B = 0, max_len = 0;
+        int64_t rows = 0;  // sum of lengths
+        const int32_t *d_len = nullptr;
+        const int64_t *d_cum = nullptr;
+    };
+
+    // bidirectional_lstm (graph_ops.cpp:1514-1529) over X [in_dim][R]:
+    // hout [2H][R] (forward units first, the ggml_concat order).
+    void bilstm(const LstmLayer &L, const float *X, float *hout, const Seqs &q) {
+        const int64_t Rr = R(1);
+        const int OC = 8 * L.H;
+        float *pre = c.buf("lstm_pre", (size_t)OC * Rr);
+        Epi e;
+        e.bias = &L.bih;
+        e.valid = q.rows;
+        if (L.f16 && L.wih_tc.buf.p) {
+            Op xh = op("lstm_xh", 1, L.in_dim, true);
+            zero(xh, L.in_dim);
+            act_only(X, xh, Rr, L.in_dim, 1, 0, ACT_NONE, 0.f);
+            conv_h(L.wih_tc, xh, 1, 0, 1, pre, Rr, Rr, e);
+        } else {
+            conv_f32((const float *)L.wih.p, L.f16, OC, X, Rr, L.in_dim, 1, 1, 0, 1, pre, Rr, Rr, e);
+        }
+        LstmRecArgs a{};
+        a.pre = pre;
+        a.R = Rr;
+        a.whh[0] = L.whh[0];
+        a.whh[1] = L.whh[1];
+        a.bhh[0] = L.bhh[0];
+        a.bhh[1] = L.bhh[1];
+        a.hout = hout;
+        a.len = q.d_len;
+        a.B = q.B;
+        a.max_len = q.max_len;
+        // smallest group that keeps the clusters (2 per group) within one wave
+        a.Bc = 32;
+        for (int bc : {1, 2, 4, 8, 16, 32})
+            if ((q.B + bc - 1) / bc <= 8) {
+                a.Bc = bc;
+                break;
+            }
+        check_cuda(lstm_recurrence(a, st), "LSTM recurrence launch");
+        ++c.n_launches;
+    }
+
     // zero every operand buffer whose gaps must read as zero
     void zero_operands(int gm, bool decoder) {
         if (decoder) zero(op("opT", 1, 1152), 1152);
@@ -1223,6 +1330,180 @@ int kk_istft(kk_ctx *ctx, int64_t n_frames, const float *post, float *audio) {
         check_cuda(cudaGetLastError(), "kernel launch");
         check_cuda(cudaMemcpyAsync(audio, d_audio, 5 * (size_t)T * 4, cudaMemcpyDeviceToHost, st), "D2H");
         check_cuda(cudaStreamSynchronize(st), "istft");
+        return KK_OK;
+    });
+}
+
+// ---------------------------------------------------------------------------
+// LSTM stack and duration alignment
+// ---------------------------------------------------------------------------
+
+namespace {
+
+constexpr int32_t kMaxSteps = 65536;
+
+// One plan "utterance" covering the R rows of a time-major packed batch.
+Plan lstm_plan(int B, int max_len) {
+    Plan P;
+    P.n = 1;
+    const int64_t rows = (int64_t)max_len * B;
+    P.T = {(int32_t)rows};
+    P.off = {0};
+    P.cum = {0};
+    P.S = rows;
+    P.total = rows;
+    P.maxT = (int32_t)rows;
+    return P;
+}
+
+// Validates lengths and uploads them (int32) with the output offsets (int64).
+Runner::Seqs lstm_seqs(kk_ctx &c, int32_t n_seqs, const int32_t *n_steps, cudaStream_t st) {
+    if (n_seqs < 1 || !n_steps) throw KKError(KK_ERROR_INVALID_ARGUMENT, "need at least one sequence");
+    Runner::Seqs q;
+    q.B = n_seqs;
+    std::vector<int64_t> h((size_t)n_seqs * 2);
+    int32_t *hl = (int32_t *)h.data();
+    int64_t *hc = h.data() + ((size_t)n_seqs + 1) / 2;
+    for (int b = 0; b < n_seqs; ++b) {
+        if (n_steps[b] < 1 || n_steps[b] > kMaxSteps)
+            throw KKError(KK_ERROR_INVALID_ARGUMENT, "sequence length out of range [1, 65536]");
+        hl[b] = n_steps[b];
+        hc[b] = q.rows;
+        q.rows += n_steps[b];
+        if (n_steps[b] > q.max_len) q.max_len = n_steps[b];
+    }
+    if ((int64_t)q.max_len * n_seqs > INT32_MAX) throw KKError(KK_ERROR_INVALID_ARGUMENT, "batch too large");
+    const size_t bytes = (size_t)((char *)(hc + n_seqs) - (char *)h.data());
+    float *d = c.buf("lstm_seq", (bytes + 3) / 4);
+    check_cuda(cudaMemcpyAsync(d, h.data(), bytes, cudaMemcpyHostToDevice, st), "upload lengths");
+    q.d_len = (const int32_t *)d;
+    q.d_cum = (const int64_t *)((char *)d + ((char *)hc - (char *)h.data()));
+    return q;
+}
+
+}  // namespace
+
+int kk_bilstm_forward(kk_ctx *ctx, const char *prefix, int32_t n_seqs, const int32_t *n_steps, int64_t in_dim,
+                      const float *x, float *out) {
+    return guarded([&] {
+        if (!ctx || !prefix || !x || !out) throw KKError(KK_ERROR_INVALID_ARGUMENT, "null argument");
+        use_device(ctx);
+        kk_ctx &c = *ctx;
+        const LstmLayer &L = c.lstm_layer(prefix);
+        if (in_dim != L.in_dim) throw KKError(KK_ERROR_INVALID_ARGUMENT, "in_dim does not match the weights");
+        cudaStream_t st = c.st;
+        Runner::Seqs q = lstm_seqs(c, n_seqs, n_steps, st);
+        Plan P = lstm_plan(n_seqs, q.max_len);
+        Runner r(c, P, st);
+        r.setup_batch();
+        const int64_t Rr = P.R(1);
+        float *xin = c.buf("lstm_xin", (size_t)q.rows * in_dim);
+        check_cuda(cudaMemcpyAsync(xin, x, (size_t)q.rows * in_dim * 4, cudaMemcpyHostToDevice, st), "upload x");
+        float *X = c.buf("lstm_X", (size_t)in_dim * Rr);
+        check_cuda(cudaMemsetAsync(X, 0, (size_t)in_dim * Rr * 4, st), "memset");
+        lstm_pack(xin, (int)in_dim, nullptr, 0, X, Rr, q.d_len, q.d_cum, n_seqs, q.max_len, st);
+        float *hout = c.buf("lstm_h", (size_t)2 * L.H * Rr);
+        r.bilstm(L, X, hout, q);
+        float *od = c.buf("lstm_out", (size_t)q.rows * 2 * L.H);
+        lstm_unpack(hout, Rr, 2 * L.H, od, q.d_len, q.d_cum, n_seqs, q.max_len, st);
+        check_cuda(cudaGetLastError(), "kernel launch");
+        check_cuda(cudaMemcpyAsync(out, od, (size_t)q.rows * 2 * L.H * 4, cudaMemcpyDeviceToHost, st), "D2H");
+        check_cuda(cudaStreamSynchronize(st), "bilstm");
+        check_device_error(ctx);
+        return KK_OK;
+    });
+}
+
+int kk_duration_encoder_forward(kk_ctx *ctx, int32_t n_seqs, const int32_t *n_steps, const float *x,
+                                const float *style, float *out) {
+    return guarded([&] {
+        if (!ctx || !x || !style || !out) throw KKError(KK_ERROR_INVALID_ARGUMENT, "null argument");
+        use_device(ctx);
+        kk_ctx &c = *ctx;
+        const std::string p = "kokopop.predictor.text_encoder.lstms.";
+        const LstmLayer *Ls[3];
+        for (int blk = 0; blk < 3; ++blk) {
+            Ls[blk] = &c.lstm_layer(p + std::to_string(2 * blk));
+            if (Ls[blk]->in_dim != 640) throw KKError(KK_ERROR_MODEL, "duration encoder LSTM input must be 640");
+        }
+        cudaStream_t st = c.st;
+        Runner::Seqs q = lstm_seqs(c, n_seqs, n_steps, st);
+        Plan P = lstm_plan(n_seqs, q.max_len);
+        Runner r(c, P, st);
+        r.setup_batch();
+        const int64_t Rr = P.R(1);
+        const int B = n_seqs;
+        float *xin = c.buf("lstm_xin", (size_t)q.rows * 512);
+        check_cuda(cudaMemcpyAsync(xin, x, (size_t)q.rows * 512 * 4, cudaMemcpyHostToDevice, st), "upload x");
+        float *sd = c.buf("lstm_style", (size_t)B * 128);
+        check_cuda(cudaMemcpyAsync(sd, style, (size_t)B * 128 * 4, cudaMemcpyHostToDevice, st), "upload style");
+        // AdaLayerNorm gamma / beta per sequence
+        float *gam = c.buf("lstm_gamma", (size_t)3 * B * 512), *bet = c.buf("lstm_beta", (size_t)3 * B * 512);
+        for (int blk = 0; blk < 3; ++blk) {
+            const std::string ln = p + std::to_string(2 * blk + 1) + ".fc.";
+            const DevTensor &gw = c.W(ln + "gamma.weight"), &gb = c.W(ln + "gamma.bias");
+            const DevTensor &bw = c.W(ln + "beta.weight"), &bb = c.W(ln + "beta.bias");
+            if (gw.ne[0] != 128 || gw.ne[1] != 512 || bw.ne[0] != 128 || bw.ne[1] != 512 || gb.n != 512 ||
+                bb.n != 512)
+                throw KKError(KK_ERROR_MODEL, "AdaLayerNorm fc shape mismatch: " + ln);
+            style_linear(gw.d, gb.d, gw.f16, sd, 128, 512, B, gam + (size_t)blk * B * 512, st);
+            style_linear(bw.d, bb.d, bw.f16, sd, 128, 512, B, bet + (size_t)blk * B * 512, st);
+        }
+        float *X = c.buf("lstm_X", (size_t)640 * Rr);
+        check_cuda(cudaMemsetAsync(X, 0, (size_t)640 * Rr * 4, st), "memset");
+        lstm_pack(xin, 512, sd, 128, X, Rr, q.d_len, q.d_cum, B, q.max_len, st);
+        float *hout = c.buf("lstm_h", (size_t)512 * Rr);
+        for (int blk = 0; blk < 3; ++blk) {
+            r.bilstm(*Ls[blk], X, hout, q);
+            ada_layer_norm(hout, Rr, 512, gam + (size_t)blk * B * 512, bet + (size_t)blk * B * 512, X, q.d_len, B,
+                           st);
+        }
+        float *od = c.buf("lstm_out", (size_t)q.rows * 640);
+        lstm_unpack(X, Rr, 640, od, q.d_len, q.d_cum, B, q.max_len, st);
+        check_cuda(cudaGetLastError(), "kernel launch");
+        check_cuda(cudaMemcpyAsync(out, od, (size_t)q.rows * 640 * 4, cudaMemcpyDeviceToHost, st), "D2H");
+        check_cuda(cudaStreamSynchronize(st), "duration encoder");
+        check_device_error(ctx);
+        return KK_OK;
+    });
+}
+
+int kk_align_durations(kk_ctx *ctx, int64_t n_tokens, const float *durations, float speed, int32_t *frames,
+                       int64_t *total, const float *hidden, int64_t hidden_dim, float *en, int64_t en_capacity) {
+    return guarded([&] {
+        if (!ctx || !total || n_tokens < 0 || (n_tokens > 0 && (!durations || !frames)) || (!hidden != !en) ||
+            (hidden && hidden_dim < 1))
+            throw KKError(KK_ERROR_INVALID_ARGUMENT, "null or invalid argument");
+        if (n_tokens > 65535) throw KKError(KK_ERROR_INVALID_ARGUMENT, "too many tokens (at most 65535)");
+        *total = 0;
+        if (n_tokens == 0) return KK_OK;
+        use_device(ctx);
+        kk_ctx &c = *ctx;
+        cudaStream_t st = c.st;
+        // duration_to_frames (kokoro.cpp:181-193): a non-finite or
+        // non-positive speed counts as 1
+        if (!std::isfinite(speed) || speed <= 0.0f) speed = 1.0f;
+        float *dd = c.buf("align_dur", (size_t)n_tokens);
+        check_cuda(cudaMemcpyAsync(dd, durations, (size_t)n_tokens * 4, cudaMemcpyHostToDevice, st), "upload");
+        float *idx = c.buf("align_idx", (size_t)n_tokens * 3 + 4);
+        int64_t *dstart = (int64_t *)idx;
+        int32_t *dframes = (int32_t *)(dstart + n_tokens + 1);
+        duration_frames(dd, n_tokens, speed, dframes, dstart, st);
+        check_cuda(cudaGetLastError(), "kernel launch");
+        int64_t tot = 0;
+        check_cuda(cudaMemcpyAsync(frames, dframes, (size_t)n_tokens * 4, cudaMemcpyDeviceToHost, st), "D2H");
+        check_cuda(cudaMemcpyAsync(&tot, dstart + n_tokens, sizeof tot, cudaMemcpyDeviceToHost, st), "D2H");
+        check_cuda(cudaStreamSynchronize(st), "durations");
+        *total = tot;
+        if (!hidden) return KK_OK;
+        if (tot > en_capacity) throw KKError(KK_ERROR_INVALID_ARGUMENT, "alignment output too small");
+        float *hd = c.buf("align_hidden", (size_t)n_tokens * hidden_dim);
+        float *ed = c.buf("align_en", (size_t)tot * hidden_dim);
+        check_cuda(cudaMemcpyAsync(hd, hidden, (size_t)n_tokens * hidden_dim * 4, cudaMemcpyHostToDevice, st), "H2D");
+        align_gather(hd, hidden_dim, dframes, dstart, n_tokens, ed, st);
+        check_cuda(cudaGetLastError(), "kernel launch");
+        check_cuda(cudaMemcpyAsync(en, ed, (size_t)tot * hidden_dim * 4, cudaMemcpyDeviceToHost, st), "D2H");
+        check_cuda(cudaStreamSynchronize(st), "alignment");
         return KK_OK;
     });
 }

@@ -46,6 +46,20 @@ struct PackedW {
     int IC = 0, IC_pad = 0, OC = 0, K = 0, n_tiles = 0;
 };
 
+// One bidirectional LSTM layer (prefix.weight_ih_l0[_reverse], ...), derived
+// on first use: W_ih of both directions stacked as one K = 1 convolution
+// weight [8H][in_dim] (forward rows first) with its bias, W_hh / b_hh as F32.
+struct LstmLayer {
+    int in_dim = 0, H = 0;
+    bool f16 = false;   // W_ih stored as F16: ggml rounds the input to half
+    DevBuf wih;         // F32 values [8H][in_dim]
+    PackedW wih_tc;     // tensor-core packing of wih (F16 weights)
+    DevBuf bih_buf;     // [8H]
+    DevTensor bih;      // view of bih_buf
+    const float *whh[2] = {nullptr, nullptr};  // rowwise [4H][H] (the uploaded tensors)
+    const float *bhh[2] = {nullptr, nullptr};
+};
+
 struct SiteInfo {
     std::string prefix;
     int C = 0;
@@ -103,6 +117,7 @@ struct kk_ctx {
     std::vector<int64_t> h_batch;
     kk::DevBuf d_batch;
     std::unordered_map<std::string, kk::DevBuf> ws;
+    std::unordered_map<std::string, kk::LstmLayer> lstm;
     // measurement
     uint64_t n_launches = 0;
     bool profiling = false;
@@ -121,4 +136,5 @@ struct kk_ctx {
     const kk::DevTensor *Wopt(const std::string &name) const;
     float *buf(const char *name, size_t floats);
     void derive();
+    const kk::LstmLayer &lstm_layer(const std::string &prefix);
 };

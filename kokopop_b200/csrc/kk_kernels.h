@@ -171,4 +171,32 @@ void har_s2d(const float *har, int64_t R_har, __half *y, int64_t R, int64_t Ry, 
 void pool_up_h(const float *x, __half *y, int64_t R_in, int64_t Ry_out, int C, const float *w, const float *bias,
                const Batch &b, int max_T, cudaStream_t st);
 
+// kk_lstm.cu: bidirectional LSTM stack and the duration alignment.
+// Sequences are packed time-major: row = t * B + b of a [C][R] activation.
+struct LstmRecArgs {
+    const float *pre;      // [2 * 4H][R]: W_ih x + b_ih, forward rows then backward rows
+    int64_t R;
+    const float *whh[2];   // per direction, rowwise [4H][H] F32 (gate order i, f, g, o)
+    const float *bhh[2];   // per direction, [4H]
+    float *hout;           // [2H][R]: forward units then backward units
+    const int32_t *len;    // [B] steps of each sequence (device)
+    int B;                 // sequences
+    int Bc;                // sequences per cluster: 1, 2, 4, 8, 16 or 32
+    int max_len;           // max over len
+};
+size_t lstm_rec_smem(int Bc);
+cudaError_t lstm_recurrence(const LstmRecArgs &a, cudaStream_t st);  // H = 256
+void lstm_pack(const float *x, int D, const float *style, int Ds, float *X, int64_t R, const int32_t *len,
+               const int64_t *cum, int B, int max_len, cudaStream_t st);
+void lstm_unpack(const float *X, int64_t R, int C, float *out, const int32_t *len, const int64_t *cum, int B,
+                 int max_len, cudaStream_t st);
+void style_linear(const float *w, const float *bias, int f16, const float *style, int Ds, int C, int B, float *out,
+                  cudaStream_t st);
+void ada_layer_norm(const float *h, int64_t R, int D, const float *gamma, const float *beta, float *X,
+                    const int32_t *len, int B, cudaStream_t st);
+// frames[i] and start[0..n] (start[n] = total frames)
+void duration_frames(const float *d, int64_t n, float speed, int32_t *frames, int64_t *start, cudaStream_t st);
+void align_gather(const float *hidden, int64_t D, const int32_t *frames, const int64_t *start, int64_t n, float *en,
+                  cudaStream_t st);
+
 }  // namespace kk

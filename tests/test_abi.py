@@ -27,6 +27,14 @@ def test_null_context_is_invalid_argument_with_message():
     assert L.kk_last_error().decode()
     assert L.kk_istft(None, 3, z.ctypes.data_as(f), z.ctypes.data_as(f)) == kb.KK_ERROR_INVALID_ARGUMENT
     assert L.kk_weights_upload(None, None, 0) == kb.KK_ERROR_INVALID_ARGUMENT
+    i32p = ctypes.POINTER(ctypes.c_int32)
+    assert L.kk_bilstm_forward(None, b"p", 1, n.ctypes.data_as(i32p), 640, z.ctypes.data_as(f), z.ctypes.data_as(f)) \
+        == kb.KK_ERROR_INVALID_ARGUMENT
+    assert L.kk_duration_encoder_forward(None, 1, n.ctypes.data_as(i32p), *(z.ctypes.data_as(f),) * 3) \
+        == kb.KK_ERROR_INVALID_ARGUMENT
+    tot = ctypes.c_int64(0)
+    assert L.kk_align_durations(None, 1, z.ctypes.data_as(f), 1.0, n.ctypes.data_as(i32p), ctypes.byref(tot),
+                                None, 0, None, 0) == kb.KK_ERROR_INVALID_ARGUMENT
     assert L.kk_ctx_create(0, None) == kb.KK_ERROR_INVALID_ARGUMENT
     L.kk_ctx_destroy(None)  # no-op
 

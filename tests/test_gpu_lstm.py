@@ -1,0 +1,191 @@
+"""GPU parity of the LSTM stack and the duration alignment, through the C ABI,
+against the oracle on the same seeded inputs.
+
+Tolerances: the recurrence keeps the reference's scalar dot order, but the
+input projection accumulates in a different order (tensor cores / CUDA-core
+tiles) and the GPU evaluates exp / tanh correctly rounded where the reference
+calls the C library's expf / tanhf, so h differs from the oracle in the last
+bits. The bound for one layer is 5e-6 max-abs on h in [-1, 1] (measured
+~5e-7; the reference's own fused-vs-scalar LSTM test allows 2e-5 on the
+recurrence alone, tests/test_lstm_fused.cpp:114-118); the duration encoder
+renormalises h three times (AdaLayerNorm divides by the per-step spread of
+h), so its bound is 1e-4 on outputs of order 1 (measured ~1e-5). With F16
+weights every layer input is rounded to half, so a last-bit difference can
+flip one half rounding (half an ulp of half is 2.4e-4 at 0.5) and the
+AdaLayerNorms amplify it: a 1-ulp perturbation of the input moves the oracle
+itself by ~1.2e-3 (tests/test_oracle.py), so that case is held to 3e-3
+max-abs and 1e-4 mean-abs. Durations -> frames and the alignment are integer /
+copy work: bit-exact.
+"""
+import numpy as np
+import pytest
+
+import kokopop_b200 as kb
+from kokopop_b200 import workload as W
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+TOL_LAYER = 5e-6
+TOL_ENCODER = 1e-4
+TOL_ENCODER_F16 = 3e-3
+TOL_ENCODER_F16_MEAN = 1e-4
+PFX = "kokopop.predictor.text_encoder.lstms.0"
+
+
+@pytest.fixture(scope="module")
+def f32_setup():
+    wts = W.config1_weights(f16=False)
+    c = kb.Context(0)
+    c.upload(wts)
+    yield c, O.OracleModel(wts)
+    c.close()
+
+
+@pytest.fixture(scope="module")
+def f16_setup():
+    wts = W.config1_weights(f16=True)
+    c = kb.Context(0)
+    c.upload(wts)
+    yield c, O.OracleModel(wts)
+    c.close()
+
+
+def _seqs(rng, lens, dim):
+    return [rng.normal(0.0, 1.0, size=(n, dim)).astype(np.float32) for n in lens]
+
+
+def _max_err(got, want):
+    return max(float(np.abs(g - w).max()) for g, w in zip(got, want))
+
+
+@pytest.mark.parametrize("lens", [[17], [17, 5, 40]])
+def test_bilstm_f32_matches_oracle(f32_setup, lens):
+    c, m = f32_setup
+    xs = _seqs(np.random.default_rng(11), lens, 640)
+    got = c.bilstm(PFX, xs)
+    want = [m.bilstm(PFX, x) for x in xs]
+    err = _max_err(got, want)
+    print(f"bilstm f32 lens={lens}: max abs err {err:.3g}")
+    assert all(g.shape == (n, 512) for g, n in zip(got, lens))
+    assert err < TOL_LAYER
+
+
+def test_bilstm_batch_of_32_ragged_matches_oracle(f32_setup):
+    """32 sequences: clusters take groups of 4 (8 groups x 2 directions)."""
+    c, m = f32_setup
+    rng = np.random.default_rng(12)
+    lens = rng.integers(8, 48, size=32).tolist()
+    xs = _seqs(rng, lens, 640)
+    got = c.bilstm(PFX, xs)
+    want = [m.bilstm(PFX, x) for x in xs]
+    err = _max_err(got, want)
+    print(f"bilstm f32 batch 32: max abs err {err:.3g}")
+    assert err < TOL_LAYER
+
+
+def test_bilstm_batch_results_equal_single_sequence_results(f32_setup):
+    """A sequence's output does not depend on the other sequences of the
+    batch (grouping and packing only): bit-exact."""
+    c, _ = f32_setup
+    rng = np.random.default_rng(13)
+    lens = [9, 30, 3, 21, 14]
+    xs = _seqs(rng, lens, 640)
+    batch = c.bilstm(PFX, xs)
+    for x, b in zip(xs, batch):
+        np.testing.assert_array_equal(c.bilstm(PFX, [x])[0], b)
+
+
+def test_bilstm_f16_weights_tensor_cores_match_oracle(f16_setup):
+    """F16 W_ih (converter policy): the projection runs on the tensor cores
+    with the input rounded to half, as ggml's F16 mul_mat."""
+    c, m = f16_setup
+    xs = _seqs(np.random.default_rng(14), [25, 7], 640)
+    got = c.bilstm(PFX, xs)
+    want = [m.bilstm(PFX, x) for x in xs]
+    err = _max_err(got, want)
+    print(f"bilstm f16: max abs err {err:.3g}")
+    assert err < TOL_LAYER
+
+
+@pytest.mark.parametrize("lens", [[33], [33, 12, 50]])
+def test_duration_encoder_matches_oracle(f32_setup, lens):
+    c, m = f32_setup
+    rng = np.random.default_rng(15)
+    xs = _seqs(rng, lens, 512)
+    styles = [rng.normal(0.0, 1.0, size=128).astype(np.float32) for _ in lens]
+    got = c.duration_encoder(xs, styles)
+    want = [m.duration_encoder(x, s) for x, s in zip(xs, styles)]
+    err = _max_err(got, want)
+    print(f"duration encoder lens={lens}: max abs err {err:.3g}")
+    assert all(g.shape == (n, 640) for g, n in zip(got, lens))
+    # the style half is copied, exactly
+    for g, s in zip(got, styles):
+        np.testing.assert_array_equal(g[:, 512:], np.broadcast_to(s, (g.shape[0], 128)))
+    assert err < TOL_ENCODER
+
+
+def test_duration_encoder_f16_weights_matches_oracle(f16_setup):
+    c, m = f16_setup
+    rng = np.random.default_rng(16)
+    xs = _seqs(rng, [20, 9], 512)
+    styles = [rng.normal(0.0, 1.0, size=128).astype(np.float32) for _ in xs]
+    got = c.duration_encoder(xs, styles)
+    want = [m.duration_encoder(x, s) for x, s in zip(xs, styles)]
+    err = _max_err(got, want)
+    mean = max(float(np.abs(g - w).mean()) for g, w in zip(got, want))
+    print(f"duration encoder f16: max abs err {err:.3g}, mean {mean:.3g}")
+    assert err < TOL_ENCODER_F16 and mean < TOL_ENCODER_F16_MEAN
+
+
+def test_lstm_rejects_bad_arguments(f32_setup):
+    c, _ = f32_setup
+    with pytest.raises(kb.KKError) as e:
+        c.bilstm(PFX, [np.zeros((4, 512), np.float32)])  # in_dim 512 != 640
+    assert e.value.code == kb.KK_ERROR_INVALID_ARGUMENT
+    with pytest.raises(kb.KKError) as e:
+        c.bilstm("kokopop.no.such.lstm", [np.zeros((4, 640), np.float32)])
+    assert e.value.code == kb.KK_ERROR_MODEL
+
+
+# --- R11: durations -> frames, alignment (bit-exact) -----------------------
+
+EDGE = np.array([0.0, 0.4, 0.5, 1.5, 2.5, 2.5000002, 3.49, 49.5, 50.5, 1e9, np.inf, -np.inf, np.nan, -3.0,
+                 3e9, 1e30, -1e30, 0.49999997, 7.5, 8.5], np.float32)
+
+
+@pytest.mark.parametrize("speed", [1.0, 2.0, 0.7, -1.0, float("nan"), float("inf")])
+def test_duration_frames_bit_exact(ctx, speed):
+    rng = np.random.default_rng(17)
+    d = np.concatenate([EDGE, rng.uniform(0.0, 30.0, 300).astype(np.float32)])
+    frames, total, _ = ctx.align_durations(d, speed)
+    f_ref, t_ref, _ = O.align_durations(d, speed)
+    np.testing.assert_array_equal(frames, f_ref)
+    assert total == t_ref
+
+
+def test_alignment_copies_token_rows_bit_exact(ctx):
+    rng = np.random.default_rng(18)
+    d = rng.uniform(0.0, 12.0, 130).astype(np.float32)
+    hidden = rng.normal(0.0, 1.0, size=(130, 640)).astype(np.float32)
+    frames, total, en = ctx.align_durations(d, 1.0, hidden)
+    f_ref, t_ref, en_ref = O.align_durations(d, 1.0, hidden)
+    np.testing.assert_array_equal(frames, f_ref)
+    assert total == t_ref and en.shape == en_ref.shape
+    np.testing.assert_array_equal(en, en_ref)
+
+
+def test_alignment_empty_and_capacity(ctx):
+    frames, total, _ = ctx.align_durations(np.zeros(0, np.float32), 1.0)
+    assert total == 0 and frames.size == 0
+    L = kb.load_library()
+    import ctypes
+    d = np.full(4, 10.0, np.float32)
+    fr = np.zeros(4, np.int32)
+    tot = ctypes.c_int64(0)
+    hid = np.zeros((4, 8), np.float32)
+    en = np.zeros((8, 8), np.float32)  # 40 frames needed
+    f32p = ctypes.POINTER(ctypes.c_float)
+    rc = L.kk_align_durations(ctx.h, 4, d.ctypes.data_as(f32p), 1.0, fr.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                              ctypes.byref(tot), hid.ctypes.data_as(f32p), 8, en.ctypes.data_as(f32p), 8)
+    assert rc == kb.KK_ERROR_INVALID_ARGUMENT and tot.value == 40
