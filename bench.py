@@ -33,6 +33,10 @@ UNIT = "audio-s/s"
 POOL = 256
 BATCH = 64
 FLOP_PER_AUDIO_S = None  # filled from the model dimensions below
+# DRAM bytes of all tensor-core conv launches per audio second, from one ncu
+# capture of the batch-8 step (dram__bytes_read.sum + dram__bytes_write.sum;
+# profiles/conv_dram_batch8.md); traffic grows with the rows processed.
+CONV_DRAM_BYTES_PER_AUDIO_S = 1.506e8
 
 
 def algorithmic_flop_per_asr_frame() -> float:
@@ -179,6 +183,50 @@ def reference_arm(args):
     return 0
 
 
+def bench_lstm(kb, W, device, runs):
+    """The prosody duration encoder (3 x biLSTM 640 -> 2x256 + AdaLayerNorm),
+    seed-1 weights U(-1/16, 1/16), inputs N(0, 1), device-resident, timed with
+    CUDA events on the launch stream: ms per call, us per sequential step
+    (3 layers x L steps), tokens/s, and the W_ih projection's TFLOP/s."""
+    import torch
+    cases = [(32, 512, False), (1, 512, False), (32, 512, True)]
+    out = {"workload": "duration encoder: 3 x (biLSTM 640 -> 2x256, AdaLayerNorm 512), seed 1 U(-1/16,1/16)",
+           "cases": []}
+    stream = torch.cuda.Stream()
+    for B, L, f16 in cases:
+        c = kb.Context(device)
+        c.upload(W.config1_weights(f16=f16))
+        g = torch.Generator(device="cuda").manual_seed(101)
+        x = torch.randn(B * L, 512, device="cuda", generator=g)
+        st = torch.randn(B, 128, device="cuda", generator=g)
+        o = torch.empty(B * L, 640, device="cuda")
+        lens = np.full(B, L, np.int32)
+        call = lambda: c.duration_encoder_device(lens, x.data_ptr(), st.data_ptr(), o.data_ptr(), stream.cuda_stream)
+        for _ in range(2):
+            call()
+        torch.cuda.synchronize()
+        c.profile_read(reset=True)
+        c.profile_enable(True)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(runs):
+            call()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        c.profile_enable(False)
+        prof = c.profile_read(reset=True)
+        ms = e0.elapsed_time(e1) / runs
+        gemm_tf = prof["conv_flop"] / (prof["conv_ms"] / 1e3) / 1e12 if prof["conv_ms"] > 0 else None
+        out["cases"].append({
+            "batch": B, "steps": L, "weights": "f16" if f16 else "f32",
+            "wih_path": "tcgen05 f16" if f16 else "fp32 cuda cores",
+            "ms_per_call": ms, "us_per_step": 1e3 * ms / (3 * L), "tokens_per_s": B * L / (ms / 1e3),
+            "wih_gemm_tflops": gemm_tf, "wih_share": (prof["conv_ms"] / runs) / ms if ms > 0 else None,
+        })
+        c.close()
+    return out
+
+
 def config_dict(batch=BATCH):
     return {
         "workload": "Kokoro-82M decoder (AdainResBlk1d encode/decode) + ISTFTNet generator + iSTFT; "
@@ -198,6 +246,7 @@ def main():
     ap.add_argument("--ttfa-runs", type=int, default=50, help="0 skips the TTFA measurement")
     ap.add_argument("--batch", type=int, default=BATCH, help="utterances per GPU step (profiling cases)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg (profiling cases)")
+    ap.add_argument("--lstm-runs", type=int, default=5, help="timed calls per LSTM-stack case (0 skips)")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
@@ -344,6 +393,9 @@ def main():
             lat.append(time.perf_counter() - t)
         ttfa = 1e3 * statistics.median(lat)
         c0.close()
+    lstm = None
+    if rank == 0 and args.lstm_runs > 0:
+        lstm = bench_lstm(kb, W, local, args.lstm_runs)
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
             sample = cpu_sample(pool)
@@ -364,13 +416,16 @@ def main():
                 if e2e_value is not None else None),
         "roofline": {"bound": "tensor", "kernel": "dense conv (all conv launches of a step)",
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": achieved / peak if peak else None, "traffic": None,
+                     "frac": achieved / peak if peak else None,
+                     "traffic": CONV_DRAM_BYTES_PER_AUDIO_S * secs_all / world / args.steps,
+                     "traffic_unit": "DRAM bytes per step, all conv launches (ncu, batch 8, scaled by audio s)",
                      "peak_source": f"{pk_kind} bf16 dense, sustained",
                      "conv_share_of_step": (prof["conv_ms"] / 1e3) / elapsed if elapsed else None},
         "cpu_baseline": cpu,
         "clocks": clk,
         "gpu_launches": prof["launches"],
         "ttfa_p50_ms": ttfa,
+        "lstm": lstm,
         "pipeline_tflops": value / world * algorithmic_flop_per_asr_frame() * 40.0 / 1e12,
     }
     if rank == 0:

@@ -129,6 +129,11 @@ int kk_bilstm_forward(kk_ctx *ctx, const char *prefix, int32_t n_seqs, const int
 int kk_duration_encoder_forward(kk_ctx *ctx, int32_t n_seqs, const int32_t *n_steps, const float *x,
                                 const float *style, float *out);
 
+/* Same with device-resident x, style and out; the lengths stay on the host.
+ * Asynchronous on `stream` (NULL = the context's stream). */
+int kk_duration_encoder_forward_device(kk_ctx *ctx, int32_t n_seqs, const int32_t *n_steps, const float *x,
+                                       const float *style, float *out, void *stream);
+
 /* Durations -> frames and the alignment (duration_to_frames,
  * src/arch/kokoro/kokoro.cpp:181-193; build_duration_mask :115-152 and
  * en = d . mask :669-674): frames[i] = clamp(int(lrint(d[i] / speed)), 1, 50)

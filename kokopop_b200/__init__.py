@@ -77,6 +77,7 @@ def load_library():
     L.kk_istft_static.argtypes = [ctypes.c_int, ctypes.c_int64, _f32p, _f32p, vp]
     L.kk_bilstm_forward.argtypes = [vp, ctypes.c_char_p, ctypes.c_int32, _i32p, ctypes.c_int64, _f32p, _f32p]
     L.kk_duration_encoder_forward.argtypes = [vp, ctypes.c_int32, _i32p, _f32p, _f32p, _f32p]
+    L.kk_duration_encoder_forward_device.argtypes = [vp, ctypes.c_int32, _i32p, vp, vp, vp, vp]
     L.kk_align_durations.argtypes = [vp, ctypes.c_int64, _f32p, ctypes.c_float, _i32p,
                                      ctypes.POINTER(ctypes.c_int64), _f32p, ctypes.c_int64, _f32p, ctypes.c_int64]
     L.kk_profile_enable.argtypes = [vp, ctypes.c_int]
@@ -222,6 +223,13 @@ class Context:
         self._check(self.L.kk_duration_encoder_forward(self.h, len(xs), _ptr(lens, _i32p), _ptr(x), _ptr(st),
                                                        _ptr(out)))
         return np.split(out, np.cumsum(lens)[:-1])
+
+    def duration_encoder_device(self, lens: np.ndarray, x_ptr: int, style_ptr: int, out_ptr: int,
+                                stream: int = 0) -> None:
+        """kk_duration_encoder_forward_device on device pointers (asynchronous)."""
+        lens = np.ascontiguousarray(lens, np.int32)
+        self._check(self.L.kk_duration_encoder_forward_device(self.h, len(lens), _ptr(lens, _i32p), x_ptr,
+                                                              style_ptr, out_ptr, stream or None))
 
     def align_durations(self, durations: np.ndarray, speed: float, hidden: Optional[np.ndarray] = None):
         """kk_align_durations: (frames int32 [n], total, en [total, D] or None)."""

@@ -1414,56 +1414,89 @@ int kk_bilstm_forward(kk_ctx *ctx, const char *prefix, int32_t n_seqs, const int
     });
 }
 
+namespace {
+
+// The duration encoder on device-resident x [rows][512], style [B][128] and
+// out [rows][640], asynchronous on st.
+void duration_encoder_device(kk_ctx &c, int32_t n_seqs, const int32_t *n_steps, const float *xin, const float *sd,
+                             float *od, cudaStream_t st) {
+    const std::string p = "kokopop.predictor.text_encoder.lstms.";
+    const LstmLayer *Ls[3];
+    for (int blk = 0; blk < 3; ++blk) {
+        Ls[blk] = &c.lstm_layer(p + std::to_string(2 * blk));
+        if (Ls[blk]->in_dim != 640) throw KKError(KK_ERROR_MODEL, "duration encoder LSTM input must be 640");
+    }
+    Runner::Seqs q = lstm_seqs(c, n_seqs, n_steps, st);
+    Plan P = lstm_plan(n_seqs, q.max_len);
+    Runner r(c, P, st);
+    r.setup_batch();
+    const int64_t Rr = P.R(1);
+    const int B = n_seqs;
+    // AdaLayerNorm gamma / beta per sequence
+    float *gam = c.buf("lstm_gamma", (size_t)3 * B * 512), *bet = c.buf("lstm_beta", (size_t)3 * B * 512);
+    for (int blk = 0; blk < 3; ++blk) {
+        const std::string ln = p + std::to_string(2 * blk + 1) + ".fc.";
+        const DevTensor &gw = c.W(ln + "gamma.weight"), &gb = c.W(ln + "gamma.bias");
+        const DevTensor &bw = c.W(ln + "beta.weight"), &bb = c.W(ln + "beta.bias");
+        if (gw.ne[0] != 128 || gw.ne[1] != 512 || bw.ne[0] != 128 || bw.ne[1] != 512 || gb.n != 512 || bb.n != 512)
+            throw KKError(KK_ERROR_MODEL, "AdaLayerNorm fc shape mismatch: " + ln);
+        style_linear(gw.d, gb.d, gw.f16, sd, 128, 512, B, gam + (size_t)blk * B * 512, st);
+        style_linear(bw.d, bb.d, bw.f16, sd, 128, 512, B, bet + (size_t)blk * B * 512, st);
+    }
+    float *X = c.buf("lstm_X", (size_t)640 * Rr);
+    check_cuda(cudaMemsetAsync(X, 0, (size_t)640 * Rr * 4, st), "memset");
+    lstm_pack(xin, 512, sd, 128, X, Rr, q.d_len, q.d_cum, B, q.max_len, st);
+    float *hout = c.buf("lstm_h", (size_t)512 * Rr);
+    for (int blk = 0; blk < 3; ++blk) {
+        r.bilstm(*Ls[blk], X, hout, q);
+        ada_layer_norm(hout, Rr, 512, gam + (size_t)blk * B * 512, bet + (size_t)blk * B * 512, X, q.d_len, B, st);
+    }
+    lstm_unpack(X, Rr, 640, od, q.d_len, q.d_cum, B, q.max_len, st);
+    c.n_launches += 3 + 6 + 3 + 2;
+    check_cuda(cudaGetLastError(), "kernel launch");
+}
+
+int64_t total_steps(int32_t n_seqs, const int32_t *n_steps) {
+    int64_t rows = 0;
+    for (int b = 0; b < n_seqs; ++b) rows += n_steps[b];
+    return rows;
+}
+
+}  // namespace
+
 int kk_duration_encoder_forward(kk_ctx *ctx, int32_t n_seqs, const int32_t *n_steps, const float *x,
                                 const float *style, float *out) {
     return guarded([&] {
-        if (!ctx || !x || !style || !out) throw KKError(KK_ERROR_INVALID_ARGUMENT, "null argument");
+        if (!ctx || !x || !style || !out || !n_steps || n_seqs < 1)
+            throw KKError(KK_ERROR_INVALID_ARGUMENT, "null argument");
         use_device(ctx);
         kk_ctx &c = *ctx;
-        const std::string p = "kokopop.predictor.text_encoder.lstms.";
-        const LstmLayer *Ls[3];
-        for (int blk = 0; blk < 3; ++blk) {
-            Ls[blk] = &c.lstm_layer(p + std::to_string(2 * blk));
-            if (Ls[blk]->in_dim != 640) throw KKError(KK_ERROR_MODEL, "duration encoder LSTM input must be 640");
-        }
         cudaStream_t st = c.st;
-        Runner::Seqs q = lstm_seqs(c, n_seqs, n_steps, st);
-        Plan P = lstm_plan(n_seqs, q.max_len);
-        Runner r(c, P, st);
-        r.setup_batch();
-        const int64_t Rr = P.R(1);
-        const int B = n_seqs;
-        float *xin = c.buf("lstm_xin", (size_t)q.rows * 512);
-        check_cuda(cudaMemcpyAsync(xin, x, (size_t)q.rows * 512 * 4, cudaMemcpyHostToDevice, st), "upload x");
-        float *sd = c.buf("lstm_style", (size_t)B * 128);
-        check_cuda(cudaMemcpyAsync(sd, style, (size_t)B * 128 * 4, cudaMemcpyHostToDevice, st), "upload style");
-        // AdaLayerNorm gamma / beta per sequence
-        float *gam = c.buf("lstm_gamma", (size_t)3 * B * 512), *bet = c.buf("lstm_beta", (size_t)3 * B * 512);
-        for (int blk = 0; blk < 3; ++blk) {
-            const std::string ln = p + std::to_string(2 * blk + 1) + ".fc.";
-            const DevTensor &gw = c.W(ln + "gamma.weight"), &gb = c.W(ln + "gamma.bias");
-            const DevTensor &bw = c.W(ln + "beta.weight"), &bb = c.W(ln + "beta.bias");
-            if (gw.ne[0] != 128 || gw.ne[1] != 512 || bw.ne[0] != 128 || bw.ne[1] != 512 || gb.n != 512 ||
-                bb.n != 512)
-                throw KKError(KK_ERROR_MODEL, "AdaLayerNorm fc shape mismatch: " + ln);
-            style_linear(gw.d, gb.d, gw.f16, sd, 128, 512, B, gam + (size_t)blk * B * 512, st);
-            style_linear(bw.d, bb.d, bw.f16, sd, 128, 512, B, bet + (size_t)blk * B * 512, st);
-        }
-        float *X = c.buf("lstm_X", (size_t)640 * Rr);
-        check_cuda(cudaMemsetAsync(X, 0, (size_t)640 * Rr * 4, st), "memset");
-        lstm_pack(xin, 512, sd, 128, X, Rr, q.d_len, q.d_cum, B, q.max_len, st);
-        float *hout = c.buf("lstm_h", (size_t)512 * Rr);
-        for (int blk = 0; blk < 3; ++blk) {
-            r.bilstm(*Ls[blk], X, hout, q);
-            ada_layer_norm(hout, Rr, 512, gam + (size_t)blk * B * 512, bet + (size_t)blk * B * 512, X, q.d_len, B,
-                           st);
-        }
-        float *od = c.buf("lstm_out", (size_t)q.rows * 640);
-        lstm_unpack(X, Rr, 640, od, q.d_len, q.d_cum, B, q.max_len, st);
-        check_cuda(cudaGetLastError(), "kernel launch");
-        check_cuda(cudaMemcpyAsync(out, od, (size_t)q.rows * 640 * 4, cudaMemcpyDeviceToHost, st), "D2H");
+        for (int b = 0; b < n_seqs; ++b)
+            if (n_steps[b] < 1 || n_steps[b] > kMaxSteps)
+                throw KKError(KK_ERROR_INVALID_ARGUMENT, "sequence length out of range [1, 65536]");
+        const int64_t rows = total_steps(n_seqs, n_steps);
+        float *xin = c.buf("lstm_xin", (size_t)rows * 512);
+        check_cuda(cudaMemcpyAsync(xin, x, (size_t)rows * 512 * 4, cudaMemcpyHostToDevice, st), "upload x");
+        float *sd = c.buf("lstm_style", (size_t)n_seqs * 128);
+        check_cuda(cudaMemcpyAsync(sd, style, (size_t)n_seqs * 128 * 4, cudaMemcpyHostToDevice, st), "upload style");
+        float *od = c.buf("lstm_out", (size_t)rows * 640);
+        duration_encoder_device(c, n_seqs, n_steps, xin, sd, od, st);
+        check_cuda(cudaMemcpyAsync(out, od, (size_t)rows * 640 * 4, cudaMemcpyDeviceToHost, st), "D2H");
         check_cuda(cudaStreamSynchronize(st), "duration encoder");
         check_device_error(ctx);
+        return KK_OK;
+    });
+}
+
+int kk_duration_encoder_forward_device(kk_ctx *ctx, int32_t n_seqs, const int32_t *n_steps, const float *x,
+                                       const float *style, float *out, void *stream) {
+    return guarded([&] {
+        if (!ctx || !x || !style || !out || !n_steps || n_seqs < 1)
+            throw KKError(KK_ERROR_INVALID_ARGUMENT, "null argument");
+        use_device(ctx);
+        cudaStream_t st = stream ? (cudaStream_t)stream : ctx->st;
+        duration_encoder_device(*ctx, n_seqs, n_steps, x, style, out, st);
         return KK_OK;
     });
 }

@@ -189,3 +189,23 @@ def test_alignment_empty_and_capacity(ctx):
     rc = L.kk_align_durations(ctx.h, 4, d.ctypes.data_as(f32p), 1.0, fr.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
                               ctypes.byref(tot), hid.ctypes.data_as(f32p), 8, en.ctypes.data_as(f32p), 8)
     assert rc == kb.KK_ERROR_INVALID_ARGUMENT and tot.value == 40
+
+
+def test_duration_encoder_device_variant_equals_host_variant(f32_setup):
+    """kk_duration_encoder_forward_device (timed by the bench) computes the
+    same bits as the host-buffer entry point."""
+    import torch
+    c, _ = f32_setup
+    rng = np.random.default_rng(19)
+    lens = [12, 30]
+    xs = _seqs(rng, lens, 512)
+    styles = [rng.normal(0.0, 1.0, size=128).astype(np.float32) for _ in lens]
+    want = np.concatenate(c.duration_encoder(xs, styles))
+    xd = torch.from_numpy(np.concatenate(xs)).cuda()
+    sd = torch.from_numpy(np.stack(styles)).cuda()
+    od = torch.zeros(sum(lens), 640, device="cuda")
+    stream = torch.cuda.Stream()
+    c.duration_encoder_device(np.array(lens, np.int32), xd.data_ptr(), sd.data_ptr(), od.data_ptr(),
+                              stream.cuda_stream)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(od.cpu().numpy(), want)
