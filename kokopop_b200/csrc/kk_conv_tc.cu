@@ -449,17 +449,33 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         if (lane == 0) bulk_wait_read<1>();  // this buffer's previous store has read it
                         __syncwarp();
                     }
+                    // All reads of the block (residual, accumulated output, bias)
+                    // come before the first write of it: the block and the bias
+                    // share one shared-memory array, so interleaved reads and
+                    // writes would run as one serial load -> add -> store chain.
+                    // The bias is one load per lane and a shuffle per column.
+                    const float b_lane = lane < nj ? sbias[n0 + c0 + lane] : 0.f;
+                    // Warp-uniform branch: a per-element (accum && live)
+                    // predicate still costs 32 address computations and
+                    // predicated loads per block when nothing accumulates.
                     float old[32];
+                    if (P.accum) {
+                        const float *op = P.out + (int64_t)(n0 + c0) * P.R_out + orow;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const bool live = row_ok && j < nj;
-                        old[j] = (P.accum && live) ? P.out[(int64_t)(n0 + c0 + j) * P.R_out + orow] : 0.f;
+                        for (int j = 0; j < 32; ++j) old[j] = (row_ok && j < nj) ? op[(int64_t)j * P.R_out] : 0.f;
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) old[j] = 0.f;
                     }
+                    float res[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) res[j] = has_res ? buf[j * 32 + lane] : 0.f;
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
+                        const float bj = __shfl_sync(0xffffffffu, b_lane, j);
                         float v = __uint_as_float(r[j]);
-                        if (P.bias) v = __fadd_rn(v, sbias[n0 + c0 + j]);
-                        if (has_res) v = __fadd_rn(buf[j * 32 + lane], v);
+                        if (P.bias) v = __fadd_rn(v, bj);
+                        if (has_res) v = __fadd_rn(res[j], v);
                         if (P.scale1 != 1.0f) v = __fmul_rn(v, P.scale1);
                         if (P.accum) v = __fadd_rn(old[j], v);
                         if (P.scale2 != 1.0f) v = __fmul_rn(v, P.scale2);
@@ -481,11 +497,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     // first so the loads overlap, then compute and store.
                     float res[32], old[32];
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const bool live = row_ok && j < nj;
-                        const int64_t oc = oc0 + c0 + j;
-                        res[j] = (has_res && live) ? P.resid[oc * P.R_resid + rrow] : 0.f;
-                        old[j] = (P.accum && live) ? P.out[oc * P.R_out + orow] : 0.f;
+                    for (int j = 0; j < 32; ++j) res[j] = old[j] = 0.f;
+                    if (has_res) {
+                        const float *rp = P.resid + (int64_t)(oc0 + c0) * P.R_resid + rrow;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (row_ok && j < nj) res[j] = rp[(int64_t)j * P.R_resid];
+                    }
+                    if (P.accum) {
+                        const float *op = P.out + (int64_t)(oc0 + c0) * P.R_out + orow;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (row_ok && j < nj) old[j] = op[(int64_t)j * P.R_out];
                     }
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
