@@ -43,15 +43,20 @@ __device__ __forceinline__ float leaky(float x, float slope) {
 // practice, where the odd Taylor polynomial of sin to x^9 (Horner in x^2)
 // is accurate to float rounding: the first omitted term x^11/11! is below
 // 3e-9 relative for |x| <= pi/4. Larger arguments take the library sinf.
+constexpr float kSnakeSmall = 0.78539816f;  // pi / 4: the polynomial's range
+
+// The polynomial alone, for |x| <= kSnakeSmall.
+__device__ __forceinline__ float snake_sin_small(float x) {
+    const float x2 = x * x;
+    float p = 2.7557319e-06f;         // 1/9!
+    p = fmaf(p, x2, -1.9841270e-04f);  // -1/7!
+    p = fmaf(p, x2, 8.3333333e-03f);   // 1/5!
+    p = fmaf(p, x2, -1.6666667e-01f);  // -1/3!
+    return fmaf(x * x2, p, x);
+}
+
 __device__ __forceinline__ float snake_sin(float x) {
-    if (fabsf(x) <= 0.78539816f) {
-        const float x2 = x * x;
-        float p = 2.7557319e-06f;         // 1/9!
-        p = fmaf(p, x2, -1.9841270e-04f);  // -1/7!
-        p = fmaf(p, x2, 8.3333333e-03f);   // 1/5!
-        p = fmaf(p, x2, -1.6666667e-01f);  // -1/3!
-        return fmaf(x * x2, p, x);
-    }
+    if (fabsf(x) <= kSnakeSmall) return snake_sin_small(x);
     return sinf(x);
 }
 

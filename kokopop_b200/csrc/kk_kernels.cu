@@ -265,29 +265,55 @@ __global__ void __launch_bounds__(256, 3) k_prologue_h(const float *__restrict__
         for (int e = 0; e < 8; ++e)
             v4[e] = e < nc ? *reinterpret_cast<const float4 *>(x + (int64_t)(ch * 8 + e) * R + row)
                            : make_float4(0.f, 0.f, 0.f, 0.f);
-        __align__(16) __half h[4][8];
+        float v[4][8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
             const float in[4] = {v4[e].x, v4[e].y, v4[e].z, v4[e].w};
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                float v = in[i];
+                float w = in[i];
                 if (NORM) {
-                    v = __fmul_rn(__fsub_rn(v, mean[e]), scale[e]);
-                    v = __fadd_rn(__fmul_rn(v, nw[e]), nb[e]);
-                    v = __fadd_rn(v, __fmul_rn(v, g[e]));
-                    v = __fadd_rn(v, be[e]);
+                    w = __fmul_rn(__fsub_rn(w, mean[e]), scale[e]);
+                    w = __fadd_rn(__fmul_rn(w, nw[e]), nb[e]);
+                    w = __fadd_rn(w, __fmul_rn(w, g[e]));
+                    w = __fadd_rn(w, be[e]);
                 }
-                if (ACT == ACT_LEAKY) {
-                    v = leaky(v, a.slope);
-                } else if (ACT == ACT_SNAKE) {
-                    const float sn = snake_sin(__fmul_rn(v, al[e]));
-                    v = __fadd_rn(v, __fmul_rn(__fmul_rn(sn, sn), ia[e]));
-                }
-                if (e >= nc || t + i >= len) v = 0.f;
-                h[i][e] = __float2half_rn(v);
+                if (ACT == ACT_LEAKY) w = leaky(w, a.slope);
+                v[i][e] = w;
             }
         }
+        if (ACT == ACT_SNAKE) {
+            // One warp-wide test instead of a branch per element: when every
+            // argument is in the polynomial's range the 32 elements run as
+            // straight-line code (the general path gives the same values).
+            bool small = true;
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) small = small && fabsf(__fmul_rn(v[i][e], al[e])) <= kSnakeSmall;
+            if (__all_sync(__activemask(), small)) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float sn = snake_sin_small(__fmul_rn(v[i][e], al[e]));
+                        v[i][e] = __fadd_rn(v[i][e], __fmul_rn(__fmul_rn(sn, sn), ia[e]));
+                    }
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float sn = snake_sin(__fmul_rn(v[i][e], al[e]));
+                        v[i][e] = __fadd_rn(v[i][e], __fmul_rn(__fmul_rn(sn, sn), ia[e]));
+                    }
+            }
+        }
+        __align__(16) __half h[4][8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) h[i][e] = __float2half_rn((e >= nc || t + i >= len) ? 0.f : v[i][e]);
         uint4 *dst = reinterpret_cast<uint4 *>(y + ((int64_t)ch * Ry + row) * 8);
 #pragma unroll
         for (int i = 0; i < 4; ++i) dst[i] = *reinterpret_cast<const uint4 *>(h[i]);
