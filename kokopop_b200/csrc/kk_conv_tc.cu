@@ -2,39 +2,38 @@
 //
 //   y[oc, orow(q)] = epi( sum_{ic,k} W[oc, ic, k] * x[ic, q - p + k*d] )
 //
-// as an implicit GEMM: M = 256 output positions (two 128-row MMAs), N = 128
-// output channels, K = input channels x taps. F16 operands (ggml's F16
-// arithmetic: both the F16 weights and the im2col'd activations are half),
-// F32 accumulation in tensor memory.
+// as an implicit GEMM over tiles of 256 output positions x 128 output
+// channels, K = input channels x taps. F16 operands (ggml's F16 arithmetic:
+// both the F16 weights and the im2col'd activations are half), F32
+// accumulation in tensor memory.
 //
-// Operands
-//   A  activations, half, chunk-major in HBM: [IC/8][Ry][8] (8 channels of one
-//      row are 16 contiguous bytes) with zero margins of kHalfLo rows before
-//      and kHalfHi rows after every chunk. One slab = rows [q0 - p, q0 - p +
+// Shared-memory operands
+//   activations  half, chunk-major in HBM: [IC/8][Ry][8] (8 channels of one row
+//      are 16 contiguous bytes) with zero margins of kHalfLo rows before and
+//      kHalfHi rows after every chunk. One slab = rows [q0 - p, q0 - p +
 //      TC_SLAB) of 64 channels, halo included, is 8 plain bulk copies (one
 //      contiguous 5 KB run per chunk) into shared memory as
 //      [8 chunks][TC_SLAB rows][16 B]: the K-major, no-swizzle canonical
 //      layout (8-row core matrices 128 B apart, chunks TC_SLAB*16 B apart).
-//      Tap k and the second 128-row half are the same layout starting k*d
-//      (+128) rows further, so all taps and both halves reuse one slab.
-//   B  weights, packed at upload into the exact shared-memory image of each
+//      Tap k is the same layout starting k*d rows further, so all taps reuse
+//      one slab.
+//   weights  packed at upload into the exact shared-memory image of each
 //      (tap, 64-channel block, 128-channel tile): [8 chunks][128 oc][16 B],
 //      fetched with one bulk copy.
+//
+// Two kernels. k_conv_tct (channels x positions, every conv whose output row
+// is its position, >= 64 channels): one M = 128 channels x N = 256 positions
+// MMA per 16-channel step, weights as operand A, the shifted slab as operand
+// B; an epilogue thread owns one channel and 32 consecutive positions.
+// k_conv_tc (positions x channels): two M = 128 positions x N = 128 channels
+// MMAs per step; its register epilogue serves the strided row maps of the
+// ConvTranspose phases, the x2-upsampled shortcut and narrow outputs.
 //
 // Roles (320 threads, one CTA per SM, persistent over tiles): warp 0 lane 0
 // issues the copies, warp 1 allocates tensor memory (two 256-column
 // accumulators) and lane 0 issues tcgen05.mma, warps 2-9 drain the other
 // accumulator through the epilogue (tcgen05.ld 32x32b: warp w owns TMEM
-// lanes 32 (w % 4) ... of the 128-row half (w - 2) / 4).
-//
-// Epilogue, two forms. Where output row = position (every stride-1 conv that
-// writes its own level), each warp works on [32 channels][32 rows] blocks in
-// shared memory: the residual block arrives by a TMA load issued one block
-// ahead, the warp adds bias / residual / scales in place, and a TMA store
-// writes the block back, so the warps never wait on global loads or queue
-// scalar stores. Otherwise (strided row maps of the transposed-conv phases,
-// the x2-upsampled shortcut) the values go through registers with plain
-// loads and stores.
+// lanes 32 (w % 4) ...).
 // Every mbarrier wait is bounded in time; on expiry the kernel records an
 // error code and the waiting role stops. Before the tensor memory is freed
 // the producer waits (bounded) for its last copies and the MMA thread for its
@@ -231,6 +230,7 @@ struct TcParams {
     int accum;
     float scale2;
     int *err;
+    int vec;  // output / residual rows are 16-byte aligned: float4 accesses allowed
 };
 
 // Persistent: CTA i takes tiles i, i + grid, ... (OC tile fastest, so the
@@ -550,6 +550,324 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------
+// kernel, channels x positions
+// ---------------------------------------------------------------------------
+//
+// The same convolution with the roles swapped: D[oc][q] = sum W[oc][.] x[.][q]
+// with M = 128 output channels (the weight tile is operand A) and N = 256
+// positions (the activation slab, shifted by k d rows for tap k, is operand
+// B), one MMA per 16-channel step instead of two. Each MMA reads 4 KB of
+// weights and 8 KB of activations from shared memory, three quarters of the
+// 16 KB that two 128 x 128 MMAs read for the same work, which keeps the tensor
+// pipe under the shared-memory bandwidth limit.
+// The accumulator holds channels in TMEM lanes and positions in columns, so
+// an epilogue thread owns one output channel and 32 consecutive positions:
+// exactly a 128-byte run of the channel-major output, read and written with
+// float4 accesses, no staging. Output row = position (omul 1, oadd 0).
+
+// STAGED (output row = position over the whole level, TMA maps available):
+// each warp moves [32 channels][32 positions] blocks through shared memory
+// with a 128-byte swizzle (thread = channel writes and reads its 128-byte row
+// without bank conflicts) and TMA loads / stores of whole 4 KB blocks, the
+// residual prefetched one block ahead. Otherwise each thread reads and writes
+// its 128-byte run of the output directly.
+__host__ __device__ constexpr int tt_nsa(bool staged) { return staged ? 2 : 3; }  // activation slab stages
+__host__ __device__ constexpr int tt_nsw(bool staged) { return staged ? 4 : 6; }  // weight tile stages
+__host__ __device__ constexpr int tt_smem(bool staged) {
+    return tt_nsa(staged) * TC_A_BYTES + tt_nsw(staged) * TC_B_BYTES + (staged ? TC_EPI_WARPS * 2 * TC_BLK_BYTES : 0) +
+           1024 /*barriers*/ + 1024 /*align*/;
+}
+static_assert(tt_smem(true) <= 227 * 1024 && tt_smem(false) <= 227 * 1024, "shared memory");
+
+// Byte offset of 16-byte chunk i of row r in a 128-byte-swizzled block (the
+// layout TMA reads and writes with CU_TENSOR_MAP_SWIZZLE_128B).
+__device__ __forceinline__ uint32_t swz128(int r, int i) { return (uint32_t)(r * 128 + ((i ^ (r & 7)) << 4)); }
+
+template <bool STAGED>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    k_conv_tct(const __grid_constant__ TcParams P, const __grid_constant__ CUtensorMap omap,
+               const __grid_constant__ CUtensorMap rmap) {
+    constexpr int NSA = tt_nsa(STAGED), NSW = tt_nsw(STAGED);
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t *sA = smem;                     // activation slabs
+    uint8_t *sW = smem + NSA * TC_A_BYTES;  // weight tiles
+    uint8_t *sE = sW + NSW * TC_B_BYTES;    // STAGED: two 4 KB blocks per epilogue warp (1 KB aligned)
+    uint64_t *bars = (uint64_t *)(sE + (STAGED ? TC_EPI_WARPS * 2 * TC_BLK_BYTES : 0));
+    // A_full[NSA] A_empty[NSA] W_full[NSW] W_empty[NSW] acc_full[2] acc_empty[2]
+    // drain res[8 warps][2] tmem-slot
+    const uint32_t bA_full = smem_u32(bars), bA_empty = smem_u32(bars + NSA);
+    const uint32_t bW_full = smem_u32(bars + 2 * NSA), bW_empty = smem_u32(bars + 2 * NSA + NSW);
+    const uint32_t bAcc_full = smem_u32(bars + 2 * NSA + 2 * NSW);
+    const uint32_t bAcc_empty = smem_u32(bars + 2 * NSA + 2 * NSW + 2);
+    const uint32_t bDrain = smem_u32(bars + 2 * NSA + 2 * NSW + 4);
+    const uint32_t bRes = smem_u32(bars + 2 * NSA + 2 * NSW + 5);
+    uint32_t *tmem_slot = (uint32_t *)(bars + 2 * NSA + 2 * NSW + 5 + 2 * TC_EPI_WARPS);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t n_tiles_total = P.m_tiles * P.n_oc_tiles;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < NSA; ++i) {
+            mbar_init(bA_full + 8 * i, 1);
+            mbar_init(bA_empty + 8 * i, 1);
+        }
+        for (int i = 0; i < NSW; ++i) {
+            mbar_init(bW_full + 8 * i, 1);
+            mbar_init(bW_empty + 8 * i, 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(bAcc_full + 8 * i, 1);
+            mbar_init(bAcc_empty + 8 * i, TC_EPI_WARPS);
+        }
+        mbar_init(bDrain, 1);
+        for (int i = 0; i < 2 * TC_EPI_WARPS; ++i) mbar_init(bRes + 8 * i, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TC_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+
+    constexpr uint32_t lbo_a = (uint32_t)TC_SLAB * 16u;  // activation chunk stride
+    constexpr uint32_t lbo_w = (uint32_t)TC_BN * 16u;    // weight chunk stride
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // producer
+            bool ok = true;
+            uint32_t ia = 0, iw = 0;
+            for (int64_t tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x) {
+                const int64_t mt = tile / P.n_oc_tiles;
+                const int nt = (int)(tile % P.n_oc_tiles);
+                const int64_t row0 = mt * TC_BM - P.p;  // >= -kHalfLo (checked on the host)
+                for (int b = 0; b < P.IC_blocks && ok; ++b, ++ia) {
+                    const int sa = ia % NSA;
+                    if (ia >= NSA) ok = mbar_wait(bA_empty + 8 * sa, ((ia / NSA) & 1) ^ 1, P.err, 11);
+                    if (!ok) break;
+                    mbar_expect_tx(bA_full + 8 * sa, TC_A_BYTES);
+                    const uint32_t dst = smem_u32(sA + sa * TC_A_BYTES);
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        const __half *src = P.a + ((int64_t)(8 * b + c) * P.R_a + row0) * 8;
+                        bulk_load(dst + (uint32_t)c * lbo_a, src, lbo_a, bA_full + 8 * sa);
+                    }
+                    for (int k = 0; k < P.K; ++k, ++iw) {
+                        const int sw = iw % NSW;
+                        if (iw >= NSW) ok = mbar_wait(bW_empty + 8 * sw, ((iw / NSW) & 1) ^ 1, P.err, 12);
+                        if (!ok) break;
+                        mbar_expect_tx(bW_full + 8 * sw, TC_B_BYTES);
+                        const __half *src =
+                            P.w + ((((size_t)k * P.IC_blocks + b) * P.n_tiles + nt) * (size_t)(8 * TC_BN * 8));
+                        bulk_load(smem_u32(sW + sw * TC_B_BYTES), src, TC_B_BYTES, bW_full + 8 * sw);
+                    }
+                }
+            }
+            for (uint32_t i = (ia > NSA ? ia - NSA : 0); i < ia; ++i)
+                mbar_wait(bA_full + 8 * (i % NSA), (i / NSA) & 1, P.err, 18, TC_DRAIN_NS);
+            for (uint32_t i = (iw > NSW ? iw - NSW : 0); i < iw; ++i)
+                mbar_wait(bW_full + 8 * (i % NSW), (i / NSW) & 1, P.err, 18, TC_DRAIN_NS);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // MMA issuer: A = weights (M = 128 channels), B = activations (N = 256 positions)
+            const uint32_t idesc = idesc_f16(TC_BN, TC_BM);
+            bool ok = true;
+            uint32_t ia = 0, iw = 0, it = 0;
+            for (int64_t tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x, ++it) {
+                const int ab = it & 1;
+                if (it >= 2) ok = mbar_wait(bAcc_empty + 8 * ab, ((it >> 1) & 1) ^ 1, P.err, 17);
+                if (!ok) break;
+                fence_after_sync();
+                const uint32_t d_tmem = tmem + (uint32_t)(ab * TC_BM);
+                for (int b = 0; b < P.IC_blocks && ok; ++b, ++ia) {
+                    const int sa = ia % NSA;
+                    ok = mbar_wait(bA_full + 8 * sa, (ia / NSA) & 1, P.err, 13);
+                    if (!ok) break;
+                    fence_after_sync();
+                    const uint32_t a_base = smem_u32(sA + sa * TC_A_BYTES);
+                    for (int k = 0; k < P.K; ++k, ++iw) {
+                        const int sw = iw % NSW;
+                        ok = mbar_wait(bW_full + 8 * sw, (iw / NSW) & 1, P.err, 14);
+                        if (!ok) break;
+                        fence_after_sync();
+                        const uint32_t w_base = smem_u32(sW + sw * TC_B_BYTES);
+                        const uint32_t x_tap = a_base + (uint32_t)(k * P.d) * 16u;
+#pragma unroll
+                        for (int ks = 0; ks < 4; ++ks) {
+                            const uint64_t wd = sdesc(w_base + (uint32_t)(2 * ks) * lbo_w, lbo_w, 128);
+                            const uint64_t xd = sdesc(x_tap + (uint32_t)(2 * ks) * lbo_a, lbo_a, 128);
+                            mma_f16(d_tmem, wd, xd, idesc, (b > 0 || k > 0 || ks > 0) ? 1u : 0u);
+                        }
+                        mma_commit(bW_empty + 8 * sw);
+                    }
+                    mma_commit(bA_empty + 8 * sa);
+                }
+                if (ok) mma_commit(bAcc_full + 8 * ab);
+            }
+            mma_commit(bDrain);
+            mbar_wait(bDrain, 0, P.err, 19, TC_DRAIN_NS);
+        }
+        __syncwarp();
+    } else {
+        // epilogue warps 2..9: warp w reads TMEM lanes 32 (w % 4) .. (its 32
+        // channels) and the position half (w - 2) / 4 of the tile
+        const int lq = warp & 3;
+        const int ew = warp - 2;
+        const int hsel = ew >> 2;
+        const bool has_res = P.resid != nullptr;
+        uint8_t *blk = sE + ew * 2 * TC_BLK_BYTES;  // STAGED: this warp's two blocks
+        const uint32_t bR = bRes + 8 * 2 * ew;
+        uint32_t it = 0;
+        uint32_t ci = 0, n_res = 0;  // STAGED: blocks done / residual blocks requested
+        bool stop = false;
+        for (int64_t tile = blockIdx.x; tile < n_tiles_total && !stop; tile += gridDim.x, ++it) {
+            const int64_t mt = tile / P.n_oc_tiles;
+            const int n0 = (int)(tile % P.n_oc_tiles) * TC_BN;
+            const int ab = it & 1;
+            const int c_lo = n0 + 32 * lq;                       // first channel of this warp
+            const int64_t pw = mt * TC_BM + hsel * 128;          // first position of this warp
+            if (STAGED && has_res && lane == 0) {
+                // the residual of this tile's first block, requested before the
+                // accumulator is ready
+                bulk_wait_read<0>();
+                mbar_expect_tx(bR + 8 * (ci & 1), TC_BLK_BYTES);
+                tma_load_2d(smem_u32(blk + (ci & 1) * TC_BLK_BYTES), &rmap, bR + 8 * (ci & 1), (int)pw, c_lo);
+                ++n_res;
+            }
+            int ok_lane = 0;
+            if (lane == 0) ok_lane = mbar_wait(bAcc_full + 8 * ab, (it >> 1) & 1, P.err, 15) ? 1 : 0;
+            if (__shfl_sync(0xffffffffu, ok_lane, 0) == 0) break;
+            __syncwarp();
+            fence_after_sync();
+            const int c = c_lo + lane;  // this thread's output channel
+            const bool chan_ok = c < P.OC;
+            const float bias = (P.bias && chan_ok) ? P.bias[c] : 0.f;
+            const uint32_t t_base = tmem + ((uint32_t)(32 * lq) << 16) + (uint32_t)(ab * TC_BM + hsel * 128);
+            for (int cc = 0; cc < 4; ++cc) {
+                uint32_t r[32];  // r[j] = D[c][p0 + j]
+                tmem_ld32(t_base + (uint32_t)(32 * cc), r);
+                const int64_t p0 = pw + 32 * cc;
+                if (STAGED) {
+                    const int s = ci & 1;
+                    uint8_t *buf = blk + s * TC_BLK_BYTES;
+                    if (has_res) {
+                        if (lane == 0 && cc < 3) {
+                            // next block's residual into the other buffer
+                            bulk_wait_read<0>();
+                            mbar_expect_tx(bR + 8 * (s ^ 1), TC_BLK_BYTES);
+                            tma_load_2d(smem_u32(blk + (s ^ 1) * TC_BLK_BYTES), &rmap, bR + 8 * (s ^ 1),
+                                        (int)(p0 + 32), c_lo);
+                            ++n_res;
+                        }
+                        // every lane waits: each reader needs its own acquire of
+                        // the bytes the copy engine wrote
+                        if (!__all_sync(0xffffffffu, mbar_wait(bR + 8 * s, (ci >> 1) & 1, P.err, 20))) {
+                            stop = true;
+                            break;
+                        }
+                    } else {
+                        if (lane == 0) bulk_wait_read<1>();  // this buffer's previous store has read it
+                        __syncwarp();
+                    }
+                    // row `lane` of the block = channel c: 8 chunks of 4 positions
+                    float res[32], old[32];
+                    if (has_res) {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const float4 t = *reinterpret_cast<const float4 *>(buf + swz128(lane, i));
+                            res[4 * i] = t.x, res[4 * i + 1] = t.y, res[4 * i + 2] = t.z, res[4 * i + 3] = t.w;
+                        }
+                    }
+                    if (P.accum && chan_ok && p0 < P.n_pos) {
+                        // n_pos == R_out here, a multiple of 128: the block's 32
+                        // positions exist and the run is 16-byte aligned
+                        const float4 *op = reinterpret_cast<const float4 *>(P.out + (int64_t)c * P.R_out + p0);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const float4 t = op[i];
+                            old[4 * i] = t.x, old[4 * i + 1] = t.y, old[4 * i + 2] = t.z, old[4 * i + 3] = t.w;
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) old[j] = 0.f;
+                    }
+                    float v[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        float x = __uint_as_float(r[j]);
+                        if (P.bias) x = __fadd_rn(x, bias);
+                        if (has_res) x = __fadd_rn(res[j], x);
+                        if (P.scale1 != 1.0f) x = __fmul_rn(x, P.scale1);
+                        if (P.accum) x = __fadd_rn(old[j], x);
+                        if (P.scale2 != 1.0f) x = __fmul_rn(x, P.scale2);
+                        v[j] = x;
+                    }
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        *reinterpret_cast<float4 *>(buf + swz128(lane, i)) =
+                            make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+                    fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0) {
+                        // positions past R_out and channels past OC are clipped by the map
+                        tma_store_2d(&omap, smem_u32(buf), (int)p0, c_lo);
+                        bulk_commit();
+                    }
+                    ++ci;
+                } else {
+                    // memory work only where the channel and rows exist; every
+                    // lane reaches the __syncwarp below before the next TMEM load
+                    if (chan_ok && p0 < P.n_pos) {
+                        float *op = P.out + (int64_t)c * P.R_out + p0;
+                        const float *rp = has_res ? P.resid + (int64_t)c * P.R_resid + p0 : nullptr;
+                        for (int j = 0; j < 32; ++j) {
+                            if (p0 + j >= P.n_pos) break;
+                            float x = __uint_as_float(r[j]);
+                            if (P.bias) x = __fadd_rn(x, bias);
+                            if (has_res) x = __fadd_rn(rp[j], x);
+                            if (P.scale1 != 1.0f) x = __fmul_rn(x, P.scale1);
+                            if (P.accum) x = __fadd_rn(op[j], x);
+                            if (P.scale2 != 1.0f) x = __fmul_rn(x, P.scale2);
+                            op[j] = x;
+                        }
+                    }
+                    __syncwarp();
+                }
+            }
+            if (stop) break;
+            fence_before_sync();
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bAcc_empty + 8 * ab) : "memory");
+        }
+        if (STAGED) {
+            if (lane == 0) {
+                // residual blocks requested but not used (only after an error)
+                for (uint32_t i = ci; i < n_res; ++i)
+                    mbar_wait(bR + 8 * (i & 1), (i >> 1) & 1, P.err, 21, TC_DRAIN_NS);
+                bulk_wait_all();  // every output block written
+            }
+            __syncwarp();
+        }
+    }
+
+    fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        fence_after_sync();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS)
+                     : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 
@@ -574,6 +892,10 @@ cudaError_t conv_tc_init() {
     }
     cudaError_t e = cudaFuncSetAttribute(k_conv_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem(true));
     if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(k_conv_tct<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, tt_smem(true));
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(k_conv_tct<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, tt_smem(false));
+    if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(k_conv_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem(false));
 }
 
@@ -588,6 +910,19 @@ static bool block_map(CUtensorMap *m, const float *base, int64_t R, int C) {
     cuuint32_t estr[2] = {1, 1};
     return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)base, dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The same 32 x 32 blocks with the 128-byte swizzle of the channel-major
+// staging (thread = channel).
+static bool block_map_swz(CUtensorMap *m, const float *base, int64_t R, int C) {
+    if (((uintptr_t)base & 15) || (R & 3)) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)R, (cuuint64_t)C};
+    cuuint64_t strides[1] = {(cuuint64_t)R * 4};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)base, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -629,6 +964,27 @@ cudaError_t conv_tc(const ConvTcArgs &a, cudaStream_t st) {
     P.accum = a.accum;
     P.scale2 = a.scale2;
     P.err = a.err;
+    const int64_t tiles = P.m_tiles * P.n_oc_tiles;
+    const int64_t slots = g_num_sms > 0 ? g_num_sms : 148;
+    const unsigned grid = (unsigned)(tiles < slots ? tiles : slots);
+    // channels x positions kernel where output row = position
+    if (a.omul == 1 && a.oadd == 0 && a.phase_oc == 0 && !a.resid_half && a.OC >= 64 && a.n_pos <= a.R_out &&
+        (!a.resid || a.R_resid >= a.n_pos)) {
+        P.vec = 0;
+        CUtensorMap omap, rmap;
+        memset(&omap, 0, sizeof(omap));
+        memset(&rmap, 0, sizeof(rmap));
+        // staged blocks where every position of the level is written
+        const bool staged = g_encode && a.n_pos == a.R_out && a.R_out % 32 == 0 && (!a.resid || a.R_resid == a.R_out) &&
+                            block_map_swz(&omap, a.out, a.R_out, a.OC) &&
+                            block_map_swz(&rmap, a.resid ? a.resid : a.out, a.R_out, a.OC);
+        if (staged)
+            k_conv_tct<true><<<grid, TC_THREADS, tt_smem(true), st>>>(P, omap, rmap);
+        else
+            k_conv_tct<false><<<grid, TC_THREADS, tt_smem(false), st>>>(P, omap, rmap);
+        return cudaGetLastError();
+    }
+    P.vec = 0;
     // shared-memory epilogue where output row = position over the whole level
     CUtensorMap omap, rmap;
     memset(&omap, 0, sizeof(omap));
@@ -636,9 +992,6 @@ cudaError_t conv_tc(const ConvTcArgs &a, cudaStream_t st) {
     bool tma = g_encode && a.omul == 1 && a.oadd == 0 && a.phase_oc == 0 && a.n_pos == a.R_out && !a.resid_half &&
                a.OC >= 64 && a.OC <= 1024 && (!a.resid || a.R_resid == a.R_out);
     if (tma) tma = block_map(&omap, a.out, a.R_out, a.OC) && block_map(&rmap, a.resid ? a.resid : a.out, a.R_out, a.OC);
-    const int64_t tiles = P.m_tiles * P.n_oc_tiles;
-    const int64_t slots = g_num_sms > 0 ? g_num_sms : 148;
-    const unsigned grid = (unsigned)(tiles < slots ? tiles : slots);
     if (tma)
         k_conv_tc<true><<<grid, TC_THREADS, tc_smem(true), st>>>(P, omap, rmap);
     else

@@ -30,6 +30,7 @@ thread_local std::string g_last_error;
 constexpr float kInvSqrt2 = 0.7071067811865476f;  // KOKOPOP_INV_SQRT2
 constexpr int kDil[3] = {1, 3, 5};                // KOKOPOP_RESBLOCK_DILATIONS
 constexpr int kKs[3] = {3, 7, 11};                // KOKOPOP_RESBLOCK_KERNELS
+constexpr float kThird = 1.0f / 3.0f;             // the branch average
 
 }  // namespace
 
@@ -732,11 +733,16 @@ struct Runner {
         ++c.n_launches;
     }
 
-    void act_only(const float *x, const Op &y, int64_t Rm, int C, int m, int extra, int act, float slope) {
+    // x2 / x3: two more branches averaged in first, ((x + x2) + x3) * sum_scale
+    void act_only(const float *x, const Op &y, int64_t Rm, int C, int m, int extra, int act, float slope,
+                  const float *x2 = nullptr, const float *x3 = nullptr, float sum_scale = 1.f) {
         PrologueArgs a{};
         a.norm = 0;
         a.act = act;
         a.slope = slope;
+        a.x2 = x2;
+        a.x3 = x3;
+        a.sum_scale = sum_scale;
         if (y.h)
             prologue_h(x, y.h, Rm, y.Ry, C, m, extra, B, m * P.maxT + extra, a, st);
         else
@@ -838,6 +844,7 @@ struct Runner {
         const int extra[2] = {0, 1};
         const int64_t R_har = R(60 * gm);
         const float *x = x_in;
+        const float *x2 = nullptr, *x3 = nullptr;  // further branches of x (averaged)
         int C = 512, m_prev = gm;
         Op op_prev = op("op2", gm, 1152);
         const std::string g = "kokopop.decoder.generator.";
@@ -849,8 +856,9 @@ struct Runner {
             const int Cs = (int)ncw.ne[1];
             float *xs = c.buf(("xs" + ss).c_str(), (size_t)Cs * Rm);
             float *xst = c.buf(("xst" + ss).c_str(), (size_t)Cs * Rm);
-            float *acc = c.buf(("acc" + ss).c_str(), (size_t)Cs * Rm);
-            float *xb = c.buf(("xb" + ss).c_str(), (size_t)Cs * Rm);
+            // the three residual blocks' outputs, averaged by the consumer
+            float *br[3] = {c.buf(("acc" + ss).c_str(), (size_t)Cs * Rm), c.buf(("xb" + ss).c_str(), (size_t)Cs * Rm),
+                            c.buf(("xc" + ss).c_str(), (size_t)Cs * Rm)};
             float *tmp = c.buf(("tmp" + ss).c_str(), (size_t)Cs * Rm);
             Op o = op(s == 0 ? "op0" : "op1", m, Cs);
             // noise branch: noise_convs + noise_res (audio_utils.cpp:714-731)
@@ -881,7 +889,7 @@ struct Runner {
             // LeakyReLU(0.1) then ConvTranspose as phase convolutions,
             // + bias, [reflect pad], + noise branch (audio_utils.cpp:687-760)
             const int64_t Rp = R(m_prev);
-            act_only(x, op_prev, Rp, C, m_prev, 0, ACT_LEAKY, 0.1f);
+            act_only(x, op_prev, Rp, C, m_prev, 0, ACT_LEAKY, 0.1f, x2, x3, kThird);
             const DevTensor &uw = c.W(g + "ups." + ss + ".weight");
             const DevTensor &ub = c.W(g + "ups." + ss + ".bias");
             if ((int)uw.ne[1] != Cs || (int)uw.ne[2] != C) throw KKError(KK_ERROR_MODEL, "ups shape mismatch");
@@ -940,11 +948,13 @@ struct Runner {
             ++c.n_launches;
             for (int k = 0; k < 3; ++k) {
                 const std::string pf = g + "resblocks." + std::to_string(s * 3 + k);
-                float *wb = k == 0 ? acc : xb;
-                gen_resblock(pf, kKs[k], xst, wb, acc, k == 0 ? 0 : 1, k == 2 ? 1.0f / 3.0f : 1.f, Cs, m, extra[s],
-                             o, tmp, ms_stage);
+                gen_resblock(pf, kKs[k], xst, br[k], nullptr, 0, 1.f, Cs, m, extra[s], o, tmp, ms_stage);
             }
-            x = acc;
+            // the stage output ((r0 + r1) + r2) / 3 is formed by the next
+            // operand prologue (graph_ops.cpp:1300-1320)
+            x = br[0];
+            x2 = br[1];
+            x3 = br[2];
             C = Cs;
             m_prev = m;
             op_prev = o;
@@ -952,7 +962,7 @@ struct Runner {
         // LeakyReLU(0.01) -> conv_post -> iSTFT (audio_utils.cpp:814-831, :1043)
         const int m = mlev[1];
         const int64_t Rm = R(m);
-        act_only(x, op_prev, Rm, C, m, 1, ACT_LEAKY, 0.01f);
+        act_only(x, op_prev, Rm, C, m, 1, ACT_LEAKY, 0.01f, x2, x3, kThird);
         float *post = c.buf("post", (size_t)22 * Rm);
         conv_w(g + "conv_post.weight", g + "conv_post.bias", op_prev, C, 7, 3, 1, post, Rm, Rm, Epi{},
                sum_len(m, 1));

@@ -160,6 +160,7 @@ __global__ void __launch_bounds__(256) k_prologue(const float *__restrict__ x, f
     }
     for (int64_t t = blockIdx.x * 256 + threadIdx.x; t < len; t += (int64_t)gridDim.x * 256) {
         float v = x[base + t];
+        if (a.x2) v = __fmul_rn(__fadd_rn(__fadd_rn(v, a.x2[base + t]), a.x3[base + t]), a.sum_scale);
         if (a.norm) {
             v = __fmul_rn(__fsub_rn(v, mean), scale);
             v = __fadd_rn(__fmul_rn(v, nw), nb);
@@ -265,6 +266,21 @@ __global__ void __launch_bounds__(256, 3) k_prologue_h(const float *__restrict__
         for (int e = 0; e < 8; ++e)
             v4[e] = e < nc ? *reinterpret_cast<const float4 *>(x + (int64_t)(ch * 8 + e) * R + row)
                            : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (!NORM && a.x2) {
+            // average of the three branches, in the reference's order
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                if (e >= nc) continue;
+                const int64_t o = (int64_t)(ch * 8 + e) * R + row;
+                const float4 b2 = *reinterpret_cast<const float4 *>(a.x2 + o);
+                const float4 b3 = *reinterpret_cast<const float4 *>(a.x3 + o);
+                const float s3 = a.sum_scale;
+                v4[e].x = __fmul_rn(__fadd_rn(__fadd_rn(v4[e].x, b2.x), b3.x), s3);
+                v4[e].y = __fmul_rn(__fadd_rn(__fadd_rn(v4[e].y, b2.y), b3.y), s3);
+                v4[e].z = __fmul_rn(__fadd_rn(__fadd_rn(v4[e].z, b2.z), b3.z), s3);
+                v4[e].w = __fmul_rn(__fadd_rn(__fadd_rn(v4[e].w, b2.w), b3.w), s3);
+            }
+        }
         float v[4][8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {

@@ -26,6 +26,10 @@ struct PrologueArgs {
     float slope;              // LeakyReLU slope
     const float *alpha;       // Snake alpha [C]
     int round16;              // round the result to half (F16 conv operand)
+    // x2, x3 non-null (without norm): the input is ((x + x2) + x3) * sum_scale,
+    // the average of the three residual-block branches (graph_ops.cpp:1300-1320)
+    const float *x2, *x3;
+    float sum_scale;
 };
 
 // Dense convolution over a packed [IC, R_in] operand (zero gaps):
