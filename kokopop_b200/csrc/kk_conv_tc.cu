@@ -57,17 +57,12 @@ constexpr int TC_NSA = 2;                        // A slab stages
 constexpr int TC_EPI_WARPS = 8;
 constexpr int TC_THREADS = 64 + 32 * TC_EPI_WARPS;
 constexpr int TC_TMEM_COLS = 2 * (TC_BM / TC_HM) * TC_BN;  // 512: two accumulators
-constexpr int TC_BLK_BYTES = 32 * 32 * 4;        // one [32 ch][32 rows] F32 epilogue block
-// B tile stages: 8 with the register epilogue, 4 when the shared-memory
-// epilogue blocks (2 per warp) take the rest of the space
-__host__ __device__ constexpr int tc_nsb(bool tma_epi) { return tma_epi ? 4 : 8; }
-__host__ __device__ constexpr int tc_smem(bool tma_epi) {
-    return TC_NSA * TC_A_BYTES + tc_nsb(tma_epi) * TC_B_BYTES + (tma_epi ? TC_EPI_WARPS * 2 * TC_BLK_BYTES : 0) +
-           4096 /*bias*/ + 1024 /*barriers*/ + 1024 /*align*/;
-}
+constexpr int TC_BLK_BYTES = 32 * 32 * 4;        // one [32 ch][32 positions] F32 epilogue block
+constexpr int TC_NSB = 8;                        // weight tile stages of k_conv_tc
+constexpr int TC_SMEM = TC_NSA * TC_A_BYTES + TC_NSB * TC_B_BYTES + 1024 /*barriers*/ + 1024 /*align*/;
 constexpr unsigned long long TC_WAIT_NS = 2000000000ull;   // 2 s
 constexpr unsigned long long TC_DRAIN_NS = 200000000ull;   // 0.2 s
-static_assert(tc_smem(true) <= 227 * 1024 && tc_smem(false) <= 227 * 1024, "shared memory");
+static_assert(TC_SMEM <= 227 * 1024, "shared memory");
 static_assert(TC_SLAB - TC_BM <= kHalfLo + kHalfHi, "slab overhang");
 
 // ---------------------------------------------------------------------------
@@ -230,33 +225,26 @@ struct TcParams {
     int accum;
     float scale2;
     int *err;
-    int vec;  // output / residual rows are 16-byte aligned: float4 accesses allowed
 };
 
-// Persistent: CTA i takes tiles i, i + grid, ... (OC tile fastest, so the
-// CTAs working on one slab of positions run close together and share it in
-// L2). TMA_EPI selects the shared-memory epilogue; omap / rmap are then the
-// 2-D maps of the output and the residual ([OC][R] F32, 32 x 32 boxes).
-template <bool TMA_EPI>
-__global__ void __launch_bounds__(TC_THREADS, 1)
-    k_conv_tc(const __grid_constant__ TcParams P, const __grid_constant__ CUtensorMap omap,
-              const __grid_constant__ CUtensorMap rmap) {
-    constexpr int NSB = tc_nsb(TMA_EPI);
+// Positions x channels, register epilogue (strided row maps). Persistent: CTA
+// i takes tiles i, i + grid, ... (OC tile fastest, so the CTAs working on one
+// slab of positions run close together and share it in L2; the phases of a
+// ConvTranspose tile then write their interleaved rows close in time).
+__global__ void __launch_bounds__(TC_THREADS, 1) k_conv_tc(const __grid_constant__ TcParams P) {
+    constexpr int NSB = TC_NSB;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t *sA = smem;
     uint8_t *sB = smem + TC_NSA * TC_A_BYTES;
-    uint8_t *sE = sB + NSB * TC_B_BYTES;  // epilogue blocks (TMA_EPI)
-    float *sbias = (float *)(sE + (TMA_EPI ? TC_EPI_WARPS * 2 * TC_BLK_BYTES : 0));  // [1024]
-    uint64_t *bars = (uint64_t *)((uint8_t *)sbias + 4096);
+    uint64_t *bars = (uint64_t *)(sB + NSB * TC_B_BYTES);
     // A_full[2] A_empty[2] B_full[NSB] B_empty[NSB] acc_full[2] acc_empty[2]
-    // drain res[8 warps][2] tmem-slot
+    // drain tmem-slot
     const uint32_t bA_full = smem_u32(bars + 0), bA_empty = smem_u32(bars + 2);
     const uint32_t bB_full = smem_u32(bars + 4), bB_empty = smem_u32(bars + 4 + NSB);
     const uint32_t bAcc_full = smem_u32(bars + 4 + 2 * NSB), bAcc_empty = smem_u32(bars + 6 + 2 * NSB);
     const uint32_t bDrain = smem_u32(bars + 8 + 2 * NSB);
-    const uint32_t bRes = smem_u32(bars + 9 + 2 * NSB);
-    uint32_t *tmem_slot = (uint32_t *)(bars + 9 + 2 * NSB + 2 * TC_EPI_WARPS);
+    uint32_t *tmem_slot = (uint32_t *)(bars + 9 + 2 * NSB);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t n_tiles_total = P.m_tiles * P.n_oc_tiles;
@@ -275,7 +263,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             mbar_init(bAcc_empty + 8 * i, TC_EPI_WARPS);  // one arrive per epilogue warp
         }
         mbar_init(bDrain, 1);
-        for (int i = 0; i < 2 * TC_EPI_WARPS; ++i) mbar_init(bRes + 8 * i, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
@@ -283,10 +270,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                      "r"(TC_TMEM_COLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-    }
-    if (TMA_EPI && warp >= 2) {
-        for (int i = threadIdx.x - 64; i < 1024; i += 32 * TC_EPI_WARPS)
-            sbias[i] = (P.bias && i < P.OC) ? P.bias[i] : 0.f;
     }
     fence_before_sync();
     __syncthreads();
@@ -388,13 +371,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int ew = warp - 2;
         const int lg = warp & 3;           // TMEM lane group
         const int half = ew >> 2;          // 128-row half of the tile
-        float *blk = (float *)(sE + ew * 2 * TC_BLK_BYTES);  // TMA_EPI: two blocks of this warp
-        const uint32_t bR = bRes + 8 * 2 * ew;
         const bool has_res = P.resid != nullptr;
         uint32_t it = 0;
-        uint32_t ci = 0, n_res = 0;  // blocks done / residual blocks requested (TMA_EPI)
-        bool stop = false;
-        for (int64_t tile = blockIdx.x; tile < n_tiles_total && !stop; tile += gridDim.x, ++it) {
+        for (int64_t tile = blockIdx.x; tile < n_tiles_total; tile += gridDim.x, ++it) {
             const int64_t mt = tile / P.n_oc_tiles;
             const int n0 = (int)(tile % P.n_oc_tiles) * TC_BN;
             const int ab = it & 1;
@@ -403,14 +382,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             // phase r, whose output rows are q * omul + oadd + r
             const int ph = P.phase_oc > 0 ? n0 / P.phase_oc : 0;
             const int oc0 = n0 - ph * P.phase_oc;
-            if (TMA_EPI && has_res && lane == 0) {
-                // the residual of this tile's first block, requested before the
-                // accumulator is ready
-                bulk_wait_read<0>();
-                mbar_expect_tx(bR + 8 * (ci & 1), TC_BLK_BYTES);
-                tma_load_2d(smem_u32(blk + (ci & 1) * 1024), &rmap, bR + 8 * (ci & 1), (int)qw, n0);
-                ++n_res;
-            }
             int ok_lane = 0;
             if (lane == 0) ok_lane = mbar_wait(bAcc_full + 8 * ab, (it >> 1) & 1, P.err, 15) ? 1 : 0;
             if (__shfl_sync(0xffffffffu, ok_lane, 0) == 0) break;
@@ -427,116 +398,42 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 uint32_t r[32];
                 tmem_ld32(t_base + (uint32_t)c0, r);
                 const int nj = P.OC - (n0 + c0) < 32 ? P.OC - (n0 + c0) : 32;
-                if (TMA_EPI) {
-                    const int s = ci & 1;
-                    float *buf = blk + s * 1024;
-                    if (has_res) {
-                        if (lane == 0 && c0 + 32 < TC_BN && n0 + c0 + 32 < P.OC) {
-                            // request the next block's residual into the other buffer
-                            bulk_wait_read<0>();
-                            mbar_expect_tx(bR + 8 * (s ^ 1), TC_BLK_BYTES);
-                            tma_load_2d(smem_u32(blk + (s ^ 1) * 1024), &rmap, bR + 8 * (s ^ 1), (int)qw,
-                                        n0 + c0 + 32);
-                            ++n_res;
-                        }
-                        // every lane waits: each reader needs its own acquire of
-                        // the bytes the copy engine wrote
-                        if (!__all_sync(0xffffffffu, mbar_wait(bR + 8 * s, (ci >> 1) & 1, P.err, 20))) {
-                            stop = true;
-                            break;
-                        }
-                    } else {
-                        if (lane == 0) bulk_wait_read<1>();  // this buffer's previous store has read it
-                        __syncwarp();
-                    }
-                    // All reads of the block (residual, accumulated output, bias)
-                    // come before the first write of it: the block and the bias
-                    // share one shared-memory array, so interleaved reads and
-                    // writes would run as one serial load -> add -> store chain.
-                    // The bias is one load per lane and a shuffle per column.
-                    const float b_lane = lane < nj ? sbias[n0 + c0 + lane] : 0.f;
-                    // Warp-uniform branch: a per-element (accum && live)
-                    // predicate still costs 32 address computations and
-                    // predicated loads per block when nothing accumulates.
-                    float old[32];
-                    if (P.accum) {
-                        const float *op = P.out + (int64_t)(n0 + c0) * P.R_out + orow;
+                const int64_t rrow = P.resid_half ? (orow >> 1) : orow;
+                const float b_lane = (P.bias && lane < nj) ? __ldg(P.bias + oc0 + c0 + lane) : 0.f;
+                // The residual and the accumulated output may alias the
+                // output (in-place updates): read all of this row's values
+                // first so the loads overlap, then compute and store.
+                float res[32], old[32];
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) old[j] = (row_ok && j < nj) ? op[(int64_t)j * P.R_out] : 0.f;
-                    } else {
+                for (int j = 0; j < 32; ++j) res[j] = old[j] = 0.f;
+                if (has_res) {
+                    const float *rp = P.resid + (int64_t)(oc0 + c0) * P.R_resid + rrow;
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) old[j] = 0.f;
-                    }
-                    float res[32];
+                    for (int j = 0; j < 32; ++j)
+                        if (row_ok && j < nj) res[j] = rp[(int64_t)j * P.R_resid];
+                }
+                if (P.accum) {
+                    const float *op = P.out + (int64_t)(oc0 + c0) * P.R_out + orow;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) res[j] = has_res ? buf[j * 32 + lane] : 0.f;
+                    for (int j = 0; j < 32; ++j)
+                        if (row_ok && j < nj) old[j] = op[(int64_t)j * P.R_out];
+                }
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const float bj = __shfl_sync(0xffffffffu, b_lane, j);
-                        float v = __uint_as_float(r[j]);
-                        if (P.bias) v = __fadd_rn(v, bj);
-                        if (has_res) v = __fadd_rn(res[j], v);
-                        if (P.scale1 != 1.0f) v = __fmul_rn(v, P.scale1);
-                        if (P.accum) v = __fadd_rn(old[j], v);
-                        if (P.scale2 != 1.0f) v = __fmul_rn(v, P.scale2);
-                        buf[j * 32 + lane] = v;
-                    }
-                    fence_proxy_async();
-                    __syncwarp();
-                    if (lane == 0) {
-                        // rows past R_out and channels past OC are clipped by the map
-                        tma_store_2d(&omap, smem_u32(buf), (int)qw, n0 + c0);
-                        bulk_commit();
-                    }
-                    ++ci;
-                } else {
-                    const int64_t rrow = P.resid_half ? (orow >> 1) : orow;
-                    const float b_lane = (P.bias && lane < nj) ? __ldg(P.bias + oc0 + c0 + lane) : 0.f;
-                    // The residual and the accumulated output may alias the
-                    // output (in-place updates): read all of this row's values
-                    // first so the loads overlap, then compute and store.
-                    float res[32], old[32];
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) res[j] = old[j] = 0.f;
-                    if (has_res) {
-                        const float *rp = P.resid + (int64_t)(oc0 + c0) * P.R_resid + rrow;
-#pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (row_ok && j < nj) res[j] = rp[(int64_t)j * P.R_resid];
-                    }
-                    if (P.accum) {
-                        const float *op = P.out + (int64_t)(oc0 + c0) * P.R_out + orow;
-#pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (row_ok && j < nj) old[j] = op[(int64_t)j * P.R_out];
-                    }
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const float bj = __shfl_sync(0xffffffffu, b_lane, j);
-                        float v = __uint_as_float(r[j]);
-                        if (P.bias) v = __fadd_rn(v, bj);
-                        if (has_res) v = __fadd_rn(res[j], v);
-                        if (P.scale1 != 1.0f) v = __fmul_rn(v, P.scale1);
-                        if (P.accum) v = __fadd_rn(old[j], v);
-                        if (P.scale2 != 1.0f) v = __fmul_rn(v, P.scale2);
-                        if (row_ok && j < nj) P.out[(int64_t)(oc0 + c0 + j) * P.R_out + orow] = v;
-                    }
+                for (int j = 0; j < 32; ++j) {
+                    const float bj = __shfl_sync(0xffffffffu, b_lane, j);
+                    float v = __uint_as_float(r[j]);
+                    if (P.bias) v = __fadd_rn(v, bj);
+                    if (has_res) v = __fadd_rn(res[j], v);
+                    if (P.scale1 != 1.0f) v = __fmul_rn(v, P.scale1);
+                    if (P.accum) v = __fadd_rn(old[j], v);
+                    if (P.scale2 != 1.0f) v = __fmul_rn(v, P.scale2);
+                    if (row_ok && j < nj) P.out[(int64_t)(oc0 + c0 + j) * P.R_out + orow] = v;
                 }
             }
-            if (stop) break;
             // hand the accumulator back to the MMA warp
             fence_before_sync();
             __syncwarp();
             if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bAcc_empty + 8 * ab) : "memory");
-        }
-        if (TMA_EPI) {
-            if (lane == 0) {
-                // residual blocks requested but not used (only after an error)
-                for (uint32_t i = ci; i < n_res; ++i)
-                    mbar_wait(bR + 8 * (i & 1), (i >> 1) & 1, P.err, 21, TC_DRAIN_NS);
-                bulk_wait_all();  // every output block written
-            }
-            __syncwarp();
         }
     }
 
@@ -890,31 +787,17 @@ cudaError_t conv_tc_init() {
         if (q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
         g_encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
     }
-    cudaError_t e = cudaFuncSetAttribute(k_conv_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem(true));
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(k_conv_tct<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, tt_smem(true));
+    cudaError_t e = cudaFuncSetAttribute(k_conv_tct<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, tt_smem(true));
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(k_conv_tct<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, tt_smem(false));
     if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(k_conv_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem(false));
+    return cudaFuncSetAttribute(k_conv_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
 }
 
 int conv_tc_max_halo() { return TC_SLAB - TC_BM; }
 
-// 2-D map of an F32 [C][R] tensor in 32 x 32 boxes (x = row, y = channel).
-static bool block_map(CUtensorMap *m, const float *base, int64_t R, int C) {
-    if (((uintptr_t)base & 15) || (R & 3)) return false;
-    cuuint64_t dims[2] = {(cuuint64_t)R, (cuuint64_t)C};
-    cuuint64_t strides[1] = {(cuuint64_t)R * 4};
-    cuuint32_t box[2] = {32, 32};
-    cuuint32_t estr[2] = {1, 1};
-    return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)base, dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-// The same 32 x 32 blocks with the 128-byte swizzle of the channel-major
-// staging (thread = channel).
+// 2-D map of an F32 [C][R] tensor in 32 x 32 boxes (x = position, y =
+// channel) with the 128-byte swizzle of the channel-major staging.
 static bool block_map_swz(CUtensorMap *m, const float *base, int64_t R, int C) {
     if (((uintptr_t)base & 15) || (R & 3)) return false;
     cuuint64_t dims[2] = {(cuuint64_t)R, (cuuint64_t)C};
@@ -970,7 +853,6 @@ cudaError_t conv_tc(const ConvTcArgs &a, cudaStream_t st) {
     // channels x positions kernel where output row = position
     if (a.omul == 1 && a.oadd == 0 && a.phase_oc == 0 && !a.resid_half && a.OC >= 64 && a.n_pos <= a.R_out &&
         (!a.resid || a.R_resid >= a.n_pos)) {
-        P.vec = 0;
         CUtensorMap omap, rmap;
         memset(&omap, 0, sizeof(omap));
         memset(&rmap, 0, sizeof(rmap));
@@ -984,18 +866,7 @@ cudaError_t conv_tc(const ConvTcArgs &a, cudaStream_t st) {
             k_conv_tct<false><<<grid, TC_THREADS, tt_smem(false), st>>>(P, omap, rmap);
         return cudaGetLastError();
     }
-    P.vec = 0;
-    // shared-memory epilogue where output row = position over the whole level
-    CUtensorMap omap, rmap;
-    memset(&omap, 0, sizeof(omap));
-    memset(&rmap, 0, sizeof(rmap));
-    bool tma = g_encode && a.omul == 1 && a.oadd == 0 && a.phase_oc == 0 && a.n_pos == a.R_out && !a.resid_half &&
-               a.OC >= 64 && a.OC <= 1024 && (!a.resid || a.R_resid == a.R_out);
-    if (tma) tma = block_map(&omap, a.out, a.R_out, a.OC) && block_map(&rmap, a.resid ? a.resid : a.out, a.R_out, a.OC);
-    if (tma)
-        k_conv_tc<true><<<grid, TC_THREADS, tc_smem(true), st>>>(P, omap, rmap);
-    else
-        k_conv_tc<false><<<grid, TC_THREADS, tc_smem(false), st>>>(P, omap, rmap);
+    k_conv_tc<<<grid, TC_THREADS, TC_SMEM, st>>>(P);
     return cudaGetLastError();
 }
 
