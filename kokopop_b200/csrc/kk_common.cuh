@@ -55,9 +55,36 @@ __device__ __forceinline__ float snake_sin_small(float x) {
     return fmaf(x * x2, p, x);
 }
 
+// Arguments past the two-constant reduction's range go to the library sinf,
+// out of line so that the unrolled element loops stay small.
+static __device__ __noinline__ float snake_sin_huge(float x) { return sinf(x); }
+
+constexpr float kSnakeReduce = 8192.0f;
+
+// sin(x) for kSnakeSmall < |x| <= kSnakeReduce: Cody-Waite reduction by pi
+// with pi split into two floats (x = k pi + r, |r| <= pi/2, r carrying an
+// absolute error near 1e-7), then the Taylor series of sin to r^13 (its
+// remainder is below 7e-10 on [-pi/2, pi/2]) and the sign (-1)^k.
+__device__ __forceinline__ float snake_sin_reduced(float x) {
+    const float k = rintf(x * 0.31830987f);  // 1 / pi
+    float r = fmaf(-k, 3.14159274f, x);      // float(pi)
+    r = fmaf(-k, -8.74227766e-08f, r);       // pi - float(pi)
+    const float r2 = r * r;
+    float p = 1.60590444e-10f;           // 1/13!
+    p = fmaf(p, r2, -2.50521079e-08f);   // -1/11!
+    p = fmaf(p, r2, 2.75573188e-06f);    // 1/9!
+    p = fmaf(p, r2, -1.98412701e-04f);   // -1/7!
+    p = fmaf(p, r2, 8.33333377e-03f);    // 1/5!
+    p = fmaf(p, r2, -1.66666672e-01f);   // -1/3!
+    const float s = fmaf(r * r2, p, r);
+    return __int_as_float(__float_as_int(s) ^ ((int)k << 31));
+}
+
 __device__ __forceinline__ float snake_sin(float x) {
-    if (fabsf(x) <= kSnakeSmall) return snake_sin_small(x);
-    return sinf(x);
+    const float ax = fabsf(x);
+    if (ax <= kSnakeSmall) return snake_sin_small(x);
+    if (ax <= kSnakeReduce) return snake_sin_reduced(x);
+    return snake_sin_huge(x);
 }
 
 template <typename T>
@@ -65,6 +92,35 @@ __device__ __forceinline__ T warp_sum(T v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     return v;
+}
+
+// Instance-norm terms from the double sums over an utterance's n valid rows,
+// ggml_norm semantics (eps 1e-5): mean = (float)S1 / n; the two-pass variance
+// sum((x - mean)^2) / n with the float mean, expanded as
+// (S2 - 2 mean S1 + n mean^2) / n in double; scale = 1 / sqrtf(var + eps).
+__device__ __forceinline__ float2 norm_from_sums(double s1, double s2, int64_t n) {
+    const float mean = __fdiv_rn((float)s1, (float)n);
+    const double md = (double)mean;
+    double q = s2 - 2.0 * md * s1 + (double)n * md * md;
+    if (q < 0.0) q = 0.0;
+    const float var = (float)(q / (double)n);
+    return make_float2(mean, __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f))));
+}
+
+// The utterance whose slot holds row q of level m: the last u with
+// m * offT[u] <= q, or 0 when q lies before the first utterance (such rows,
+// and the gap rows after an utterance, fall outside that utterance's
+// [m * offT[u], m * offT[u] + m * T[u] + extra) and are not counted).
+__device__ __forceinline__ int utt_of_row(const Batch &b, int m, int64_t q) {
+    int lo = 0, hi = b.n - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if ((int64_t)m * __ldg(b.offT + mid) <= q)
+            lo = mid;
+        else
+            hi = mid - 1;
+    }
+    return lo;
 }
 
 }  // namespace kk

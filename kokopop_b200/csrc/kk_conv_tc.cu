@@ -225,6 +225,9 @@ struct TcParams {
     int accum;
     float scale2;
     int *err;
+    float2 *part;     // non-null: 32-row block partials of the output, [OC][R_out / 32]
+    Batch sb;         // utterances of the output level (each starts on a block boundary)
+    int sm, sextra;   // level multiplier and extra rows of the output level
 };
 
 // Positions x channels, register epilogue (strided row maps). Persistent: CTA
@@ -480,6 +483,76 @@ static_assert(tt_smem(true) <= 227 * 1024 && tt_smem(false) <= 227 * 1024, "shar
 // layout TMA reads and writes with CU_TENSOR_MAP_SWIZZLE_128B).
 __device__ __forceinline__ uint32_t swz128(int r, int i) { return (uint32_t)(r * 128 + ((i ^ (r & 7)) << 4)); }
 
+// Instance-norm partials of one output channel over the 32-position blocks
+// of a tile: (S, M2) with S the sum of the block's k rows that are valid rows
+// of its utterance and M2 = sum (v - S / k)^2, both in FP32; (0, 0) for a
+// block of gap rows. Every utterance starts on a block boundary, so a block
+// belongs to at most one utterance. The utterance and its rows are the same
+// for the 32 lanes of a warp (they share positions and differ in channel).
+struct BlockStats {
+    int u;           // utterance whose slot holds the current block
+    int64_t lo, hi;  // its valid rows
+
+    __device__ __forceinline__ void set_utt(const TcParams &P, int uu) {
+        u = uu;
+        lo = (int64_t)P.sm * __ldg(P.sb.offT + uu);
+        hi = lo + (int64_t)P.sm * __ldg(P.sb.T + uu) + P.sextra;
+    }
+    __device__ __forceinline__ void begin(const TcParams &P, int64_t p) { set_utt(P, utt_of_row(P.sb, P.sm, p)); }
+    // v[j] = output at position p0 + j
+    __device__ __forceinline__ float2 block(const TcParams &P, const float (&v)[32], int64_t p0) {
+        for (int guard = 0; guard < P.sb.n && u + 1 < P.sb.n; ++guard) {
+            if ((int64_t)P.sm * __ldg(P.sb.offT + u + 1) > p0) break;
+            set_utt(P, u + 1);
+        }
+        if (p0 >= lo && p0 + 32 <= hi) {
+            float a[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int j = 0; j < 32; ++j) a[j & 3] += v[j];
+            const float S = (a[0] + a[1]) + (a[2] + a[3]);
+            const float mb = S * (1.0f / 32.0f);
+            float q[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const float dv = v[j] - mb;
+                q[j & 3] = fmaf(dv, dv, q[j & 3]);
+            }
+            return make_float2(S, (q[0] + q[1]) + (q[2] + q[3]));
+        }
+        // the block ends the utterance, or holds gap rows only
+        const int j0 = p0 >= lo ? 0 : (int)(lo - p0 < 32 ? lo - p0 : 32);
+        const int j1 = hi <= p0 ? 0 : (int)(hi - p0 < 32 ? hi - p0 : 32);
+        if (j1 <= j0) return make_float2(0.f, 0.f);
+        float S = 0.f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if (j >= j0 && j < j1) S += v[j];
+        const float mb = __fdiv_rn(S, (float)(j1 - j0));
+        float M2 = 0.f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if (j >= j0 && j < j1) {
+                const float dv = v[j] - mb;
+                M2 = fmaf(dv, dv, M2);
+            }
+        return make_float2(S, M2);
+    }
+};
+
+// Pairs of block partials as one 16-byte store: blocks 2i and 2i + 1 of a
+// thread's four are adjacent in part (the position half of a tile starts on
+// a multiple of 128 rows, and R_out / 32 is a multiple of 4).
+__device__ __forceinline__ void store_part(const TcParams &P, float2 q, float2 &prev, int c, bool chan_ok, int64_t p0,
+                                           int cc) {
+    if (cc & 1) {
+        if (chan_ok && p0 < P.R_out)
+            *reinterpret_cast<float4 *>(P.part + (int64_t)c * (P.R_out >> 5) + (p0 >> 5) - 1) =
+                make_float4(prev.x, prev.y, q.x, q.y);
+    } else {
+        prev = q;
+    }
+}
+
 template <bool STAGED>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     k_conv_tct(const __grid_constant__ TcParams P, const __grid_constant__ CUtensorMap omap,
@@ -631,6 +704,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const int ab = it & 1;
             const int c_lo = n0 + 32 * lq;                       // first channel of this warp
             const int64_t pw = mt * TC_BM + hsel * 128;          // first position of this warp
+            BlockStats bs;
+            float2 prev_part = make_float2(0.f, 0.f);  // the tile's previous block partial
+            if (P.part) bs.begin(P, pw);
             if (STAGED && has_res && lane == 0) {
                 // the residual of this tile's first block, requested before the
                 // accumulator is ready
@@ -719,24 +795,34 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         bulk_commit();
                     }
                     ++ci;
+                    if (P.part) store_part(P, bs.block(P, v, p0), prev_part, c, chan_ok, p0, cc);
                 } else {
                     // memory work only where the channel and rows exist; every
                     // lane reaches the __syncwarp below before the next TMEM load
+                    float v[32];
                     if (chan_ok && p0 < P.n_pos) {
                         float *op = P.out + (int64_t)c * P.R_out + p0;
                         const float *rp = has_res ? P.resid + (int64_t)c * P.R_resid + p0 : nullptr;
+#pragma unroll
                         for (int j = 0; j < 32; ++j) {
-                            if (p0 + j >= P.n_pos) break;
-                            float x = __uint_as_float(r[j]);
-                            if (P.bias) x = __fadd_rn(x, bias);
-                            if (has_res) x = __fadd_rn(rp[j], x);
-                            if (P.scale1 != 1.0f) x = __fmul_rn(x, P.scale1);
-                            if (P.accum) x = __fadd_rn(op[j], x);
-                            if (P.scale2 != 1.0f) x = __fmul_rn(x, P.scale2);
-                            op[j] = x;
+                            float x = 0.f;
+                            if (p0 + j < P.n_pos) {
+                                x = __uint_as_float(r[j]);
+                                if (P.bias) x = __fadd_rn(x, bias);
+                                if (has_res) x = __fadd_rn(rp[j], x);
+                                if (P.scale1 != 1.0f) x = __fmul_rn(x, P.scale1);
+                                if (P.accum) x = __fadd_rn(op[j], x);
+                                if (P.scale2 != 1.0f) x = __fmul_rn(x, P.scale2);
+                                op[j] = x;
+                            }
+                            v[j] = x;
                         }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] = 0.f;
                     }
                     __syncwarp();
+                    if (P.part) store_part(P, bs.block(P, v, p0), prev_part, c, chan_ok, p0, cc);
                 }
             }
             if (stop) break;
@@ -847,6 +933,12 @@ cudaError_t conv_tc(const ConvTcArgs &a, cudaStream_t st) {
     P.accum = a.accum;
     P.scale2 = a.scale2;
     P.err = a.err;
+    P.part = nullptr;
+    P.sb = a.sb;
+    P.sm = a.sm;
+    P.sextra = a.sextra;
+    if (a.stats && (a.sb.n < 1 || a.sm < 1 || a.sextra < 0 || a.omul != 1 || a.oadd != 0 || a.phase_oc != 0))
+        return cudaErrorInvalidValue;
     const int64_t tiles = P.m_tiles * P.n_oc_tiles;
     const int64_t slots = g_num_sms > 0 ? g_num_sms : 148;
     const unsigned grid = (unsigned)(tiles < slots ? tiles : slots);
@@ -860,14 +952,30 @@ cudaError_t conv_tc(const ConvTcArgs &a, cudaStream_t st) {
         const bool staged = g_encode && a.n_pos == a.R_out && a.R_out % 32 == 0 && (!a.resid || a.R_resid == a.R_out) &&
                             block_map_swz(&omap, a.out, a.R_out, a.OC) &&
                             block_map_swz(&rmap, a.resid ? a.resid : a.out, a.R_out, a.OC);
+        // block partials where every position is written and the utterances
+        // start on block boundaries (then R_out is a multiple of 128)
+        const bool fused = a.stats && a.part && a.stats_aligned && a.n_pos == a.R_out && a.R_out % 128 == 0;
+        if (fused) P.part = a.part;
         if (staged)
             k_conv_tct<true><<<grid, TC_THREADS, tt_smem(true), st>>>(P, omap, rmap);
         else
             k_conv_tct<false><<<grid, TC_THREADS, tt_smem(false), st>>>(P, omap, rmap);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess || !a.stats) return e;
+        if (fused)
+            stats_blocks(a.part, a.R_out / 32, a.OC, a.sm, a.sextra, a.sb, a.stats, st);
+        else
+            stats(a.out, a.R_out, a.OC, a.sm, a.sextra, a.sb, a.stats, st);
         return cudaGetLastError();
     }
     k_conv_tc<<<grid, TC_THREADS, TC_SMEM, st>>>(P);
-    return cudaGetLastError();
+    cudaError_t e = cudaGetLastError();
+    // this kernel keeps no partials: a separate pass over the written output
+    if (e == cudaSuccess && a.stats) {
+        stats(a.out, a.R_out, a.OC, a.sm, a.sextra, a.sb, a.stats, st);
+        e = cudaGetLastError();
+    }
+    return e;
 }
 
 }  // namespace kk

@@ -429,14 +429,14 @@ Plan kk::make_plan(const int32_t *lens, int n) {
     P.T.assign(lens, lens + n);
     P.off.resize(n);
     P.cum.resize(n);
-    int64_t off = 4, cum = 0;
+    int64_t off = 8, cum = 0;
     P.maxT = 0;
     for (int u = 0; u < n; ++u) {
         if (lens[u] < 1 || lens[u] > kMaxFrames)
             throw KKError(KK_ERROR_INVALID_ARGUMENT, "utterance length out of range [1, 8192]");
         P.off[u] = off;
         P.cum[u] = cum;
-        off += ((int64_t)lens[u] + 4 + 3) / 4 * 4;
+        off += ((int64_t)lens[u] + 4 + 7) / 8 * 8;
         cum += lens[u];
         if (lens[u] > P.maxT) P.maxT = lens[u];
     }
@@ -509,6 +509,7 @@ struct Runner {
     Batch B{};
     const int64_t *d_cum = nullptr;
     float2 *ms = nullptr;
+    float2 *ms2 = nullptr;  // a second set, for the conv that writes the next AdaIN input
     float *gbase = nullptr, *bbase = nullptr;
     const bool tc;
 
@@ -561,6 +562,7 @@ struct Runner {
         adain_affine((const AdainSite *)c.d_sites.p, (int)c.h_sites.size(), style_dev, P.n, st);
         ++c.n_launches;
         ms = (float2 *)c.buf("stats", n * 1090 * 2);
+        ms2 = (float2 *)c.buf("stats2", n * 1090 * 2);
     }
 
     const AdainSite &site(const std::string &prefix) {
@@ -608,6 +610,10 @@ struct Runner {
         float scale2 = 1.f;
         int64_t omul = 1, oadd = 0;
         int64_t valid = 0;  // valid output positions (algorithmic FLOP count)
+        // non-null: the instance-norm terms (mean, scale) of the output over
+        // the utterances of level (sm, sextra), for the AdaIN that reads it next
+        float2 *stats = nullptr;
+        int sm = 1, sextra = 0;
     };
 
     void timed_begin(cudaEvent_t &e0, cudaEvent_t &e1) {
@@ -683,6 +689,14 @@ struct Runner {
         a.accum = e.accum;
         a.scale2 = e.scale2;
         a.err = (int *)c.d_err.p;
+        a.stats = e.stats;
+        a.sb = B;
+        a.sm = e.sm;
+        a.sextra = e.sextra;
+        if (e.stats) {
+            a.stats_aligned = aligned32(e.sm) ? 1 : 0;
+            a.part = (float2 *)c.buf("stats_part", (size_t)pw.OC * (size_t)(R_out / 32) * 2);
+        }
         cudaEvent_t e0 = nullptr, e1 = nullptr;
         timed_begin(e0, e1);
         check_cuda(conv_tc(a, st), "tensor-core conv launch");
@@ -703,10 +717,22 @@ struct Runner {
             conv_h(it->second, in, K, p, d, out, R_out, n_pos, e);
         } else {
             conv_f32(w.d, w.f16, OC, in.f, in.R, IC, K, 1, p, d, out, R_out, n_pos, e);
+            if (e.stats) {
+                stats(out, R_out, OC, e.sm, e.sextra, B, e.stats, st);
+                ++c.n_launches;
+            }
         }
     }
 
+    // every utterance of level m starts on a 32-row boundary
+    bool aligned32(int m) const {
+        for (int u = 0; u < P.n; ++u)
+            if (((int64_t)m * P.off[u]) % 32 != 0) return false;
+        return true;
+    }
+
     // stats + AdaIN + activation into an operand (or an F32 buffer)
+    // pre: the statistics of x when already known
     void adain_act(const std::string &prefix, const float *x, const Op &y, int64_t Rm, int C, int m, int extra,
                    int act, float slope, const std::string &alpha, const float2 *pre = nullptr) {
         const AdainSite &s = site(prefix);
@@ -808,18 +834,25 @@ struct Runner {
 
     // graph_generator_resblock: x_in -> (3 iterations) -> wb, the last
     // iteration writing final_out (accumulating / scaling) when given.
+    // x_in_stats: the statistics of x_in. A conv whose output feeds an AdaIN
+    // leaves that output's statistics behind (ms after conv1, ms2 after conv2).
     void gen_resblock(const std::string &pf, int K, const float *x_in, float *wb, float *final_out, int accum,
                       float scale2, int C, int m, int extra, const Op &o, float *tmp, const float2 *x_in_stats) {
         const int64_t Rm = R(m);
         const float *cur = x_in;
+        const float2 *cur_stats = x_in_stats;
         for (int i = 0; i < 3; ++i) {
             const std::string is = std::to_string(i);
             const int d = kDil[i];
             adain_act(pf + ".adain1." + is, cur, o, Rm, C, m, extra, ACT_SNAKE, 0.f, pf + ".alpha1." + is,
-                      i == 0 ? x_in_stats : nullptr);
+                      cur_stats);
+            Epi e1;
+            e1.stats = ms;
+            e1.sm = m;
+            e1.sextra = extra;
             conv_w(pf + ".convs1." + is + ".weight", pf + ".convs1." + is + ".bias", o, C, K, (K * d - d) / 2, d, tmp,
-                   Rm, Rm, Epi{}, sum_len(m, extra));
-            adain_act(pf + ".adain2." + is, tmp, o, Rm, C, m, extra, ACT_SNAKE, 0.f, pf + ".alpha2." + is);
+                   Rm, Rm, e1, sum_len(m, extra));
+            adain_act(pf + ".adain2." + is, tmp, o, Rm, C, m, extra, ACT_SNAKE, 0.f, pf + ".alpha2." + is, ms);
             Epi e;
             e.resid = cur;
             e.R_resid = Rm;
@@ -829,9 +862,15 @@ struct Runner {
                 e.accum = accum;
                 e.scale2 = scale2;
             }
+            if (i < 2) {
+                e.stats = ms2;
+                e.sm = m;
+                e.sextra = extra;
+            }
             conv_w(pf + ".convs2." + is + ".weight", pf + ".convs2." + is + ".bias", o, C, K, K / 2, 1, out, Rm, Rm,
                    e, sum_len(m, extra));
             cur = wb;
+            cur_stats = e.stats;
         }
     }
 
@@ -866,6 +905,9 @@ struct Runner {
                 Epi e;
                 e.bias = &c.W(g + "noise_convs." + ss + ".bias");
                 e.valid = sum_len(m, extra[s]);
+                e.stats = ms2;
+                e.sm = m;
+                e.sextra = extra[s];
                 const int K = sp[s].noise_kernel;
                 if (ncw.n != (int64_t)Cs * 22 * K) throw KKError(KK_ERROR_MODEL, "noise_convs shape mismatch");
                 if (tc && s == 0) {
@@ -882,10 +924,12 @@ struct Runner {
                 } else {
                     conv_f32(ncw.d, ncw.f16, Cs, har, R_har, 22, K, sp[s].noise_stride, sp[s].noise_padding, 1, xs,
                              Rm, Rm, e);
+                    stats(xs, Rm, Cs, m, extra[s], B, ms2, st);
+                    ++c.n_launches;
                 }
             }
             gen_resblock(g + "noise_res." + ss, sp[s].kernel, xs, xs, nullptr, 0, 1.f, Cs, m, extra[s], o, tmp,
-                         nullptr);
+                         ms2);
             // LeakyReLU(0.1) then ConvTranspose as phase convolutions,
             // + bias, [reflect pad], + noise branch (audio_utils.cpp:687-760)
             const int64_t Rp = R(m_prev);

@@ -69,9 +69,12 @@ struct SiteInfo {
 };
 
 // Ragged batch plan: utterance u occupies base rows [off[u], off[u] + T[u])
-// inside a slot of round_up(T[u] + 4, 4) rows, after a 4-row lead gap. A
-// level with multiplier m uses rows m * off[u] .. and R(m) rows in total,
-// padded to the 128-row tile.
+// at the start of a slot of round_up(T[u] + 4, 8) rows (at least 4 gap rows
+// follow it), the first slot after an 8-row lead gap. A level with multiplier
+// m uses rows m * off[u] .. and R(m) rows in total, padded to the 128-row
+// tile. Slots on 8-row boundaries put every utterance of the generator's
+// levels (m = 20, 60, 120) on a 32-row boundary, where the convolution keeps
+// per-block statistics.
 struct Plan {
     int n = 0;
     std::vector<int32_t> T;

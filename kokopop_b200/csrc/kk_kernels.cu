@@ -95,11 +95,9 @@ __device__ double block_sum_double(double v, double *red) {
     return red[0];
 }
 
+// One pass: sum and sum of squares in double, then the (mean, scale) pair.
 __global__ void __launch_bounds__(256) k_stats(const float *__restrict__ x, int64_t R, int C, int m,
                                                int extra, Batch b, float2 *__restrict__ ms) {
-    // One pass: sum and sum of squares in double, then the two-pass result of
-    // ggml_norm recovered exactly enough: var = sum((x - mean)^2) / n with the
-    // float mean, expanded as (S2 - 2 mean S1 + n mean^2) / n in double.
     __shared__ double red[32];
     const int c = blockIdx.x, u = blockIdx.y;
     const int64_t len = (int64_t)m * b.T[u] + extra;
@@ -112,20 +110,63 @@ __global__ void __launch_bounds__(256) k_stats(const float *__restrict__ x, int6
     }
     s1 = block_sum_double<256>(s1, red);
     s2 = block_sum_double<256>(s2, red);
-    if (threadIdx.x == 0) {
-        const float mean = __fdiv_rn((float)s1, (float)len);
-        const double md = (double)mean;
-        double q = s2 - 2.0 * md * s1 + (double)len * md * md;
-        if (q < 0.0) q = 0.0;
-        const float var = (float)(q / (double)len);
-        const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-5f)));
-        ms[(int64_t)u * C + c] = make_float2(mean, scale);
-    }
+    if (threadIdx.x == 0) ms[(int64_t)u * C + c] = norm_from_sums(s1, s2, len);
 }
 
 void stats(const float *x, int64_t R, int C, int m, int extra, const Batch &b, float2 *ms,
            cudaStream_t st) {
     k_stats<<<dim3(C, b.n), 256, 0, st>>>(x, R, C, m, extra, b, ms);
+}
+
+// The same terms from 32-row block partials part[c * NB + row / 32] = (S, M2)
+// (S the block's sum over its k valid rows, M2 = sum (v - S / k)^2), written
+// by the tensor-core convolution while it stores the tensor. Every utterance
+// starts on a block boundary, so block i of utterance u holds its rows
+// 32 i .. 32 i + k - 1 whatever the packing, and the fixed summation order
+// below makes the result independent of the batch the utterance is in:
+// S1 = sum S, S2 = sum (M2 + S^2 / k), in double.
+// One warp per (utterance, channel); 8 per block.
+__global__ void __launch_bounds__(256) k_stats_blocks(const float2 *__restrict__ part, int64_t NB, int C, int m,
+                                                      int extra, Batch b, float2 *__restrict__ ms) {
+    const int lane = threadIdx.x & 31;
+    const int c = blockIdx.x * 8 + (threadIdx.x >> 5), u = blockIdx.y;
+    if (c >= C) return;
+    const int64_t len = (int64_t)m * b.T[u] + extra;
+    const int64_t b0 = (int64_t)m * b.offT[u] / 32;
+    const int64_t nb = (len + 31) / 32;
+    const float2 *p = part + (int64_t)c * NB + b0;
+    double s1 = 0.0, s2 = 0.0;
+    if (b0 + nb <= NB) {
+        // full blocks four at a time per lane, then the last (partial) block
+        const int64_t nfull = len / 32;
+        int64_t i = lane;
+        for (; i + 96 < nfull; i += 128) {
+            float2 q[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) q[k] = p[i + 32 * k];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const double S = (double)q[k].x;
+                s1 += S;
+                s2 += (double)q[k].y + S * S * (1.0 / 32.0);
+            }
+        }
+        for (; i < nb; i += 32) {
+            const float2 q = p[i];
+            const int64_t k = len - 32 * i < 32 ? len - 32 * i : 32;
+            const double S = (double)q.x;
+            s1 += S;
+            s2 += (double)q.y + S * S / (double)k;
+        }
+    }
+    s1 = warp_sum(s1);
+    s2 = warp_sum(s2);
+    if (lane == 0) ms[(int64_t)u * C + c] = norm_from_sums(s1, s2, len);
+}
+
+void stats_blocks(const float2 *part, int64_t NB, int C, int m, int extra, const Batch &b, float2 *ms,
+                  cudaStream_t st) {
+    k_stats_blocks<<<dim3((C + 7) / 8, b.n), 256, 0, st>>>(part, NB, C, m, extra, b, ms);
 }
 
 // ---------------------------------------------------------------------------

@@ -97,6 +97,11 @@ void adain_affine(const AdainSite *sites_dev, int n_sites, const float *style, i
                   cudaStream_t st);
 void stats(const float *x, int64_t R, int C, int m, int extra, const Batch &b, float2 *ms,
            cudaStream_t st);
+// stats_blocks: the same terms from the 32-row block partials of a tensor
+// (part[c * NB + row / 32] = (sum, sum of squares about the block mean))
+// whose utterances all start on a 32-row boundary
+void stats_blocks(const float2 *part, int64_t NB, int C, int m, int extra, const Batch &b, float2 *ms,
+                  cudaStream_t st);
 void prologue(const float *x, float *y, int64_t R, int C, int m, int extra, const Batch &b,
               int max_len, const PrologueArgs &a, cudaStream_t st);
 void convt_row0(const ConvTRow0Args &a, const Batch &b, cudaStream_t st);
@@ -157,6 +162,17 @@ struct ConvTcArgs {
     // > 0: the weights are phase-packed (OC = phases x phase_oc, phase-major);
     // channel n writes channel n % phase_oc at rows q * omul + oadd + n / phase_oc
     int phase_oc;
+    // non-null: the instance-norm terms (mean, scale) of the output over each
+    // utterance's valid rows at level (sm, sextra) of batch sb, into
+    // stats[u * OC + c]. With stats_aligned (every utterance of the level
+    // starts on a 32-row boundary) and part (scratch of OC * R_out / 32
+    // float2) the convolution keeps block partials as it writes and a small
+    // pass reduces them; otherwise a separate pass reads the output.
+    float2 *stats;
+    Batch sb;
+    int sm, sextra;
+    int stats_aligned;
+    float2 *part;
 };
 cudaError_t conv_tc_init();
 cudaError_t conv_tc(const ConvTcArgs &a, cudaStream_t st);
