@@ -506,18 +506,18 @@ struct BlockStats {
             set_utt(P, u + 1);
         }
         if (p0 >= lo && p0 + 32 <= hi) {
-            float a[4] = {0.f, 0.f, 0.f, 0.f};
+            float2 a[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-            for (int j = 0; j < 32; ++j) a[j & 3] += v[j];
-            const float S = (a[0] + a[1]) + (a[2] + a[3]);
-            const float mb = S * (1.0f / 32.0f);
-            float q[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int j = 0; j < 32; j += 2) a[(j >> 1) & 1] = f2add(a[(j >> 1) & 1], make_float2(v[j], v[j + 1]));
+            const float S = (a[0].x + a[0].y) + (a[1].x + a[1].y);
+            const float nmb = S * (-1.0f / 32.0f);
+            float2 q[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const float dv = v[j] - mb;
-                q[j & 3] = fmaf(dv, dv, q[j & 3]);
+            for (int j = 0; j < 32; j += 2) {
+                const float2 dv = f2add(make_float2(v[j], v[j + 1]), make_float2(nmb, nmb));
+                q[(j >> 1) & 1] = f2fma(dv, dv, q[(j >> 1) & 1]);
             }
-            return make_float2(S, (q[0] + q[1]) + (q[2] + q[3]));
+            return make_float2(S, (q[0].x + q[0].y) + (q[1].x + q[1].y));
         }
         // the block ends the utterance, or holds gap rows only
         const int j0 = p0 >= lo ? 0 : (int)(lo - p0 < 32 ? lo - p0 : 32);
@@ -773,15 +773,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         for (int j = 0; j < 32; ++j) old[j] = 0.f;
                     }
                     float v[32];
+                    // element pairs in packed FP32: the same roundings as one op each
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        float x = __uint_as_float(r[j]);
-                        if (P.bias) x = __fadd_rn(x, bias);
-                        if (has_res) x = __fadd_rn(res[j], x);
-                        if (P.scale1 != 1.0f) x = __fmul_rn(x, P.scale1);
-                        if (P.accum) x = __fadd_rn(old[j], x);
-                        if (P.scale2 != 1.0f) x = __fmul_rn(x, P.scale2);
-                        v[j] = x;
+                    for (int j = 0; j < 32; j += 2) {
+                        float2 x = make_float2(__uint_as_float(r[j]), __uint_as_float(r[j + 1]));
+                        if (P.bias) x = f2add(x, make_float2(bias, bias));
+                        if (has_res) x = f2add(make_float2(res[j], res[j + 1]), x);
+                        if (P.scale1 != 1.0f) x = f2mul(x, make_float2(P.scale1, P.scale1));
+                        if (P.accum) x = f2add(make_float2(old[j], old[j + 1]), x);
+                        if (P.scale2 != 1.0f) x = f2mul(x, make_float2(P.scale2, P.scale2));
+                        v[j] = x.x;
+                        v[j + 1] = x.y;
                     }
 #pragma unroll
                     for (int i = 0; i < 8; ++i)

@@ -753,7 +753,7 @@ struct Runner {
         a.alpha = alpha.empty() ? nullptr : c.W(alpha).d;
         a.round16 = 0;
         if (y.h)
-            prologue_h(x, y.h, Rm, y.Ry, C, m, extra, B, m * P.maxT + extra, a, st);
+            prologue_h(x, y.h, Rm, y.Ry, C, m, extra, B, (int)(sum_len(m, extra) / P.n), a, st);
         else
             prologue(x, y.f, Rm, C, m, extra, B, m * P.maxT + extra, a, st);
         ++c.n_launches;
@@ -770,7 +770,7 @@ struct Runner {
         a.x3 = x3;
         a.sum_scale = sum_scale;
         if (y.h)
-            prologue_h(x, y.h, Rm, y.Ry, C, m, extra, B, m * P.maxT + extra, a, st);
+            prologue_h(x, y.h, Rm, y.Ry, C, m, extra, B, (int)(sum_len(m, extra) / P.n), a, st);
         else
             prologue(x, y.f, Rm, C, m, extra, B, m * P.maxT + extra, a, st);
         ++c.n_launches;

@@ -378,10 +378,10 @@ __global__ void __launch_bounds__(256, 3) k_prologue_h(const float *__restrict__
 }
 
 void prologue_h(const float *x, __half *y, int64_t R, int64_t Ry, int C, int m, int extra, const Batch &b,
-                int max_len, const PrologueArgs &a, cudaStream_t st) {
-    // about three 1024-row passes per thread over the longest utterance, so
-    // the per-channel set-up of a thread is spread over several passes
-    int bx = (max_len + 3 * 1024 - 1) / (3 * 1024);
+                int mean_len, const PrologueArgs &a, cudaStream_t st) {
+    // about three 1024-row passes per thread over an utterance of the mean
+    // length, so the per-channel set-up of a thread is spread over several
+    int bx = (mean_len + 3 * 1024 - 1) / (3 * 1024);
     if (bx > 64) bx = 64;
     const dim3 grid(bx, (C + 7) / 8, b.n);
     if (a.norm) {

@@ -181,7 +181,7 @@ int conv_tc_max_halo();
 // prologue_h: y[c/8][row][c%8] = half(act(adain(x[c][row]))) on valid rows
 // (x is F32 [C][R]; y a half operand of chunk stride Ry).
 void prologue_h(const float *x, __half *y, int64_t R, int64_t Ry, int C, int m, int extra, const Batch &b,
-                int max_len, const PrologueArgs &a, cudaStream_t st);
+                int mean_len, const PrologueArgs &a, cudaStream_t st);
 // har_s2d: space-to-depth half operand [192/8][R][8] (chunk stride Ry) of the
 // stride-6 noise convolution (132 real channels), all R rows of the stage-0
 // level.
