@@ -228,6 +228,15 @@ struct TcParams {
     float2 *part;     // non-null: 32-row block partials of the output, [OC][R_out / 32]
     Batch sb;         // utterances of the output level (each starts on a block boundary)
     int sm, sextra;   // level multiplier and extra rows of the output level
+    // k_conv_tcf: the operand is half(snake(adain(x))) of the F32 input x
+    // ([IC][R_out], read through a tensor map) on the valid rows of level
+    // (sm, sextra), zero elsewhere
+    int IC;                              // channels of x (a multiple of 64)
+    const float2 *x_ms;                  // [n][IC] (mean, scale)
+    const float *x_nw, *x_nb;            // [IC] norm weight and bias
+    const float *x_gamma, *x_beta;       // [n][IC]
+    const float *x_alpha;                // [IC] Snake alpha
+    float nz;                            // -0.0f, opaque to the compiler (packed products)
 };
 
 // Positions x channels, register epilogue (strided row maps). Persistent: CTA
@@ -779,9 +788,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         float2 x = make_float2(__uint_as_float(r[j]), __uint_as_float(r[j + 1]));
                         if (P.bias) x = f2add(x, make_float2(bias, bias));
                         if (has_res) x = f2add(make_float2(res[j], res[j + 1]), x);
-                        if (P.scale1 != 1.0f) x = f2mul(x, make_float2(P.scale1, P.scale1));
+                        // scalar products: a packed product feeding a packed add may be contracted
+                        if (P.scale1 != 1.0f) x = make_float2(__fmul_rn(x.x, P.scale1), __fmul_rn(x.y, P.scale1));
                         if (P.accum) x = f2add(make_float2(old[j], old[j + 1]), x);
-                        if (P.scale2 != 1.0f) x = f2mul(x, make_float2(P.scale2, P.scale2));
+                        if (P.scale2 != 1.0f) x = make_float2(__fmul_rn(x.x, P.scale2), __fmul_rn(x.y, P.scale2));
                         v[j] = x.x;
                         v[j + 1] = x.y;
                     }
@@ -853,6 +863,484 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------
+// k_conv_tcf: k_conv_tct with the operand prologue inside. The activation
+// slab is formed in shared memory from the F32 input instead of being read
+// from a half operand in HBM:
+//   warp 0 lane 0   copies F32 pieces [64 channels][32 rows] of x (tensor
+//                   map, 128-byte swizzle, rows < 0 or >= R read as zero)
+//                   into a ring of TF_NP pieces;
+//   warp 2 lane 0   copies the weight tiles;
+//   warps 7..14     (transform) turn each piece into half(snake(adain(x)))
+//                   with the k_prologue_h arithmetic (one rounding per
+//                   operation, packed in FP32 pairs), zero on rows that are
+//                   not valid rows of an utterance, and store it into the
+//                   K-major slab: warp t owns channels 8t..8t+7 of the 64;
+//   warp 1          MMAs as in k_conv_tct;
+//   warps 3..6      the staged epilogue of k_conv_tct, each warp over all
+//                   256 positions of its 32 channels.
+// The slab starts at the tile's first input row rounded down to a multiple
+// of 4 (the tensor copy's row coordinate must be 16-byte aligned); the MMA
+// start address skips the 0..3 extra rows.
+// ---------------------------------------------------------------------------
+
+constexpr int TF_EPI_WARPS = 4;
+constexpr int TF_XF_WARPS = 8;
+constexpr int TF_XF_WARP0 = 3 + TF_EPI_WARPS;              // first transform warp
+constexpr int TF_THREADS = 32 * (TF_XF_WARP0 + TF_XF_WARPS);  // 480
+constexpr int TF_NP = 8;                                   // F32 piece stages
+constexpr int TF_PIECE_BYTES = 64 * 32 * 4;                // [64 ch][32 rows] F32
+constexpr int TF_PIECES = TC_SLAB / 32;                    // pieces per slab
+constexpr int TF_NSA = 2;
+constexpr int TF_NSW = 3;
+constexpr int TF_SMEM = TF_NSA * TC_A_BYTES + TF_NSW * TC_B_BYTES + TF_EPI_WARPS * 2 * TC_BLK_BYTES +
+                        TF_NP * TF_PIECE_BYTES + 1024 /*barriers*/ + 1024 /*align*/;
+static_assert(TF_SMEM <= 227 * 1024, "shared memory");
+static_assert(TC_SLAB % 32 == 0, "slab of whole pieces");
+
+// AdaIN + Snake terms of a channel pair for one utterance (k_prologue_h).
+struct XfPrm {
+    float2 nmean, scale, nw, nb, g, be, al, ia;  // nmean = -mean
+};
+
+__device__ __forceinline__ XfPrm xf_load(const TcParams &P, int u, int c) {
+    XfPrm q;
+    const float2 m0 = P.x_ms[(int64_t)u * P.IC + c], m1 = P.x_ms[(int64_t)u * P.IC + c + 1];
+    q.nmean = make_float2(-m0.x, -m1.x);
+    q.scale = make_float2(m0.y, m1.y);
+    q.nw = make_float2(P.x_nw[c], P.x_nw[c + 1]);
+    q.nb = make_float2(P.x_nb[c], P.x_nb[c + 1]);
+    q.g = make_float2(P.x_gamma[(int64_t)u * P.IC + c], P.x_gamma[(int64_t)u * P.IC + c + 1]);
+    q.be = make_float2(P.x_beta[(int64_t)u * P.IC + c], P.x_beta[(int64_t)u * P.IC + c + 1]);
+    q.al = make_float2(P.x_alpha[c], P.x_alpha[c + 1]);
+    q.ia = make_float2(__fdiv_rn(1.0f, q.al.x), __fdiv_rn(1.0f, q.al.y));
+    return q;
+}
+
+__device__ __forceinline__ XfPrm xf_select(bool b, const XfPrm &x, const XfPrm &y) {
+    XfPrm r;
+#define KK_SEL(f) r.f = b ? y.f : x.f
+    KK_SEL(nmean);
+    KK_SEL(scale);
+    KK_SEL(nw);
+    KK_SEL(nb);
+    KK_SEL(g);
+    KK_SEL(be);
+    KK_SEL(al);
+    KK_SEL(ia);
+#undef KK_SEL
+    return r;
+}
+
+// Packed product a * b rounded once, as fma(a, b, z) with z = -0.0f from a
+// kernel parameter: the assembler can neither simplify it back to a multiply
+// nor contract it into the add that follows (it does both for a literal
+// -0 or a packed mul.rn), so every step keeps its own rounding.
+__device__ __forceinline__ float2 f2mul_sep(float2 a, float2 b, float z) {
+    float2 r;
+    asm("{\n .reg .b64 ra, rb, rz, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
+        " mov.b64 rz, {%6, %6};\n fma.rn.f32x2 rd, ra, rb, rz;\n mov.b64 {%0, %1}, rd;\n}"
+        : "=f"(r.x), "=f"(r.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(z));
+    return r;
+}
+
+// x[c][r] of a [64 ch][32 rows] F32 piece in the 128-byte swizzle
+__device__ __forceinline__ float xf_piece(const uint8_t *pc, int c, int r) {
+    return *reinterpret_cast<const float *>(pc + c * 128 + (((r >> 2) ^ (c & 7)) << 4) + (r & 3) * 4);
+}
+
+__device__ __forceinline__ int64_t floor4(int64_t v) { return v - (((v % 4) + 4) % 4); }
+
+// One lane's share of a piece: rows 8 i + rr (i = 0..3) of channels cl and
+// cl + 1 into the slab (dst = the slab's row of the piece's first row, plus
+// the lane's channel-pair offset), as half(snake(adain(x))) with the
+// k_prologue_h expressions, one rounding per operation, in packed FP32
+// pairs; the eight elements run as straight-line code around one warp-wide
+// polynomial test (all 32 lanes call this together). SLOW: the piece holds
+// rows outside [lo, hi) of utterance qa's, or rows from lo_n on, which
+// belong to the next utterance (qb, valid below hi_n); invalid rows are zero.
+template <bool SLOW>
+__device__ __forceinline__ void xf_four(const uint8_t *pc, uint8_t *dst, int cl, int rr, const XfPrm &qa,
+                                        const XfPrm &qb, int64_t g0, int64_t lo, int64_t hi, int64_t lo_n,
+                                        int64_t hi_n, float z) {
+    float2 w[4], al[4], ia[4];
+    bool valid[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int rw = 8 * i + rr;
+        const float2 x = make_float2(xf_piece(pc, cl, rw), xf_piece(pc, cl + 1, rw));
+        XfPrm q = qa;
+        valid[i] = true;
+        if (SLOW) {
+            const int64_t g = g0 + rw;
+            const bool in_n = g >= lo_n;
+            valid[i] = in_n ? g < hi_n : (g >= lo && g < hi);
+            q = xf_select(in_n, qa, qb);
+        }
+        float2 v = f2mul_sep(f2add(x, q.nmean), q.scale, z);
+        v = f2add(f2mul_sep(v, q.nw, z), q.nb);
+        v = f2add(v, f2mul_sep(v, q.g, z));
+        w[i] = f2add(v, q.be);
+        al[i] = q.al;
+        ia[i] = q.ia;
+    }
+    float2 t[4];
+    bool small = true;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        t[i] = f2mul_sep(w[i], al[i], z);
+        small = small && fabsf(t[i].x) <= kSnakeSmall && fabsf(t[i].y) <= kSnakeSmall;
+    }
+    float2 sn[4];
+    if (__all_sync(0xffffffffu, small)) {
+        // snake_sin_small in pairs
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 t2 = f2mul_sep(t[i], t[i], z);
+            float2 p = f2fma(make_float2(2.7557319e-06f, 2.7557319e-06f), t2,
+                             make_float2(-1.9841270e-04f, -1.9841270e-04f));
+            p = f2fma(p, t2, make_float2(8.3333333e-03f, 8.3333333e-03f));
+            p = f2fma(p, t2, make_float2(-1.6666667e-01f, -1.6666667e-01f));
+            sn[i] = f2fma(f2mul_sep(t[i], t2, z), p, t[i]);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sn[i] = make_float2(snake_sin(t[i].x), snake_sin(t[i].y));
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 v = f2add(w[i], f2mul_sep(f2mul_sep(sn[i], sn[i], z), ia[i], z));
+        const __half2 h = __floats2half2_rn(v.x, v.y);
+        const uint32_t hb = *reinterpret_cast<const uint32_t *>(&h);
+        *reinterpret_cast<uint32_t *>(dst + (8 * i + rr) * 16) = valid[i] ? hb : 0u;
+    }
+}
+
+__global__ void __launch_bounds__(TF_THREADS, 1)
+    k_conv_tcf(const __grid_constant__ TcParams P, const __grid_constant__ CUtensorMap omap,
+               const __grid_constant__ CUtensorMap rmap, const __grid_constant__ CUtensorMap xmap) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t *sA = smem;                                   // half slabs
+    uint8_t *sW = sA + TF_NSA * TC_A_BYTES;               // weight tiles
+    uint8_t *sE = sW + TF_NSW * TC_B_BYTES;               // epilogue blocks, two per warp
+    uint8_t *sF = sE + TF_EPI_WARPS * 2 * TC_BLK_BYTES;   // F32 pieces (1 KB aligned)
+    uint64_t *bars = (uint64_t *)(sF + TF_NP * TF_PIECE_BYTES);
+    // F_full[NP] F_empty[NP] A_full[NSA] A_empty[NSA] W_full[NSW] W_empty[NSW]
+    // acc_full[2] acc_empty[2] drain res[4 warps][2] tmem-slot
+    const uint32_t bF_full = smem_u32(bars), bF_empty = smem_u32(bars + TF_NP);
+    const uint32_t bA_full = smem_u32(bars + 2 * TF_NP), bA_empty = smem_u32(bars + 2 * TF_NP + TF_NSA);
+    const uint32_t bW_full = smem_u32(bars + 2 * TF_NP + 2 * TF_NSA);
+    const uint32_t bW_empty = smem_u32(bars + 2 * TF_NP + 2 * TF_NSA + TF_NSW);
+    const uint32_t bAcc_full = smem_u32(bars + 2 * TF_NP + 2 * TF_NSA + 2 * TF_NSW);
+    const uint32_t bAcc_empty = bAcc_full + 16;
+    const uint32_t bDrain = bAcc_full + 32;
+    const uint32_t bRes = bAcc_full + 40;
+    uint32_t *tmem_slot = (uint32_t *)(bars + 2 * TF_NP + 2 * TF_NSA + 2 * TF_NSW + 5 + 2 * TF_EPI_WARPS);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t n_tiles_total = P.m_tiles * P.n_oc_tiles;
+    const int IC_blocks = P.IC / 64;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < TF_NP; ++i) {
+            mbar_init(bF_full + 8 * i, 1);
+            mbar_init(bF_empty + 8 * i, TF_XF_WARPS);
+        }
+        for (int i = 0; i < TF_NSA; ++i) {
+            mbar_init(bA_full + 8 * i, TF_XF_WARPS);
+            mbar_init(bA_empty + 8 * i, 1);
+        }
+        for (int i = 0; i < TF_NSW; ++i) {
+            mbar_init(bW_full + 8 * i, 1);
+            mbar_init(bW_empty + 8 * i, 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(bAcc_full + 8 * i, 1);
+            mbar_init(bAcc_empty + 8 * i, TF_EPI_WARPS);
+        }
+        mbar_init(bDrain, 1);
+        for (int i = 0; i < 2 * TF_EPI_WARPS; ++i) mbar_init(bRes + 8 * i, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TC_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+
+    constexpr uint32_t lbo_a = (uint32_t)TC_SLAB * 16u;  // activation chunk stride
+    constexpr uint32_t lbo_w = (uint32_t)TC_BN * 16u;    // weight chunk stride
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // F32 pieces of x
+            bool ok = true;
+            uint32_t ip = 0;
+            for (int64_t tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x) {
+                const int64_t mt = tile / P.n_oc_tiles;
+                const int64_t r0a = floor4(mt * TC_BM - P.p);
+                for (int b = 0; b < IC_blocks && ok; ++b) {
+                    for (int j = 0; j < TF_PIECES; ++j, ++ip) {
+                        const int sp = ip % TF_NP;
+                        if (ip >= TF_NP) ok = mbar_wait(bF_empty + 8 * sp, ((ip / TF_NP) & 1) ^ 1, P.err, 31);
+                        if (!ok) break;
+                        mbar_expect_tx(bF_full + 8 * sp, TF_PIECE_BYTES);
+                        tma_load_2d(smem_u32(sF + sp * TF_PIECE_BYTES), &xmap, bF_full + 8 * sp, (int)(r0a + 32 * j),
+                                    64 * b);
+                    }
+                }
+            }
+            for (uint32_t i = (ip > TF_NP ? ip - TF_NP : 0); i < ip; ++i)
+                mbar_wait(bF_full + 8 * (i % TF_NP), (i / TF_NP) & 1, P.err, 38, TC_DRAIN_NS);
+        }
+        __syncwarp();
+    } else if (warp == 2) {
+        if (lane == 0) {
+            // weight tiles
+            bool ok = true;
+            uint32_t iw = 0;
+            for (int64_t tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x) {
+                const int nt = (int)(tile % P.n_oc_tiles);
+                for (int b = 0; b < IC_blocks && ok; ++b) {
+                    for (int k = 0; k < P.K; ++k, ++iw) {
+                        const int sw = iw % TF_NSW;
+                        if (iw >= TF_NSW) ok = mbar_wait(bW_empty + 8 * sw, ((iw / TF_NSW) & 1) ^ 1, P.err, 32);
+                        if (!ok) break;
+                        mbar_expect_tx(bW_full + 8 * sw, TC_B_BYTES);
+                        const __half *src =
+                            P.w + ((((size_t)k * IC_blocks + b) * P.n_tiles + nt) * (size_t)(8 * TC_BN * 8));
+                        bulk_load(smem_u32(sW + sw * TC_B_BYTES), src, TC_B_BYTES, bW_full + 8 * sw);
+                    }
+                }
+            }
+            for (uint32_t i = (iw > TF_NSW ? iw - TF_NSW : 0); i < iw; ++i)
+                mbar_wait(bW_full + 8 * (i % TF_NSW), (i / TF_NSW) & 1, P.err, 38, TC_DRAIN_NS);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // MMA issuer: A = weights (M = 128 channels), B = the formed slab (N = 256 positions)
+            const uint32_t idesc = idesc_f16(TC_BN, TC_BM);
+            bool ok = true;
+            uint32_t ia = 0, iw = 0, it = 0;
+            for (int64_t tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x, ++it) {
+                const int64_t mt = tile / P.n_oc_tiles;
+                const int64_t row0 = mt * TC_BM - P.p;
+                const uint32_t shift = (uint32_t)(row0 - floor4(row0));  // 0..3 rows
+                const int ab = it & 1;
+                if (it >= 2) ok = mbar_wait(bAcc_empty + 8 * ab, ((it >> 1) & 1) ^ 1, P.err, 37);
+                if (!ok) break;
+                fence_after_sync();
+                const uint32_t d_tmem = tmem + (uint32_t)(ab * TC_BM);
+                for (int b = 0; b < IC_blocks && ok; ++b, ++ia) {
+                    const int sa = ia % TF_NSA;
+                    ok = mbar_wait(bA_full + 8 * sa, (ia / TF_NSA) & 1, P.err, 33);
+                    if (!ok) break;
+                    fence_after_sync();
+                    const uint32_t a_base = smem_u32(sA + sa * TC_A_BYTES);
+                    for (int k = 0; k < P.K; ++k, ++iw) {
+                        const int sw = iw % TF_NSW;
+                        ok = mbar_wait(bW_full + 8 * sw, (iw / TF_NSW) & 1, P.err, 34);
+                        if (!ok) break;
+                        fence_after_sync();
+                        const uint32_t w_base = smem_u32(sW + sw * TC_B_BYTES);
+                        const uint32_t x_tap = a_base + (shift + (uint32_t)(k * P.d)) * 16u;
+#pragma unroll
+                        for (int ks = 0; ks < 4; ++ks) {
+                            const uint64_t wd = sdesc(w_base + (uint32_t)(2 * ks) * lbo_w, lbo_w, 128);
+                            const uint64_t xd = sdesc(x_tap + (uint32_t)(2 * ks) * lbo_a, lbo_a, 128);
+                            mma_f16(d_tmem, wd, xd, idesc, (b > 0 || k > 0 || ks > 0) ? 1u : 0u);
+                        }
+                        mma_commit(bW_empty + 8 * sw);
+                    }
+                    mma_commit(bA_empty + 8 * sa);
+                }
+                if (ok) mma_commit(bAcc_full + 8 * ab);
+            }
+            mma_commit(bDrain);
+            mbar_wait(bDrain, 0, P.err, 39, TC_DRAIN_NS);
+        }
+        __syncwarp();
+    } else if (warp < TF_XF_WARP0) {
+        // epilogue warps 3..6: warp w reads TMEM lanes 32 (w % 4) .. (its 32
+        // channels) over all 256 positions of the tile
+        const int lq = warp & 3;
+        const int ew = warp - 3;
+        const bool has_res = P.resid != nullptr;
+        uint8_t *blk = sE + ew * 2 * TC_BLK_BYTES;
+        const uint32_t bR = bRes + 8 * 2 * ew;
+        uint32_t it = 0;
+        uint32_t ci = 0, n_res = 0;  // blocks done / residual blocks requested
+        bool stop = false;
+        for (int64_t tile = blockIdx.x; tile < n_tiles_total && !stop; tile += gridDim.x, ++it) {
+            const int64_t mt = tile / P.n_oc_tiles;
+            const int n0 = (int)(tile % P.n_oc_tiles) * TC_BN;
+            const int ab = it & 1;
+            const int c_lo = n0 + 32 * lq;
+            const int64_t pw = mt * TC_BM;
+            BlockStats bs;
+            float2 prev_part = make_float2(0.f, 0.f);
+            if (P.part) bs.begin(P, pw);
+            if (has_res && lane == 0) {
+                bulk_wait_read<0>();
+                mbar_expect_tx(bR + 8 * (ci & 1), TC_BLK_BYTES);
+                tma_load_2d(smem_u32(blk + (ci & 1) * TC_BLK_BYTES), &rmap, bR + 8 * (ci & 1), (int)pw, c_lo);
+                ++n_res;
+            }
+            int ok_lane = 0;
+            if (lane == 0) ok_lane = mbar_wait(bAcc_full + 8 * ab, (it >> 1) & 1, P.err, 35) ? 1 : 0;
+            if (__shfl_sync(0xffffffffu, ok_lane, 0) == 0) break;
+            __syncwarp();
+            fence_after_sync();
+            const int c = c_lo + lane;
+            const bool chan_ok = c < P.OC;
+            const float bias = (P.bias && chan_ok) ? P.bias[c] : 0.f;
+            const uint32_t t_base = tmem + ((uint32_t)(32 * lq) << 16) + (uint32_t)(ab * TC_BM);
+            for (int cc = 0; cc < 8; ++cc) {
+                uint32_t r[32];
+                tmem_ld32(t_base + (uint32_t)(32 * cc), r);
+                const int64_t p0 = pw + 32 * cc;
+                const int s = ci & 1;
+                uint8_t *buf = blk + s * TC_BLK_BYTES;
+                if (has_res) {
+                    if (lane == 0 && cc < 7) {
+                        bulk_wait_read<0>();
+                        mbar_expect_tx(bR + 8 * (s ^ 1), TC_BLK_BYTES);
+                        tma_load_2d(smem_u32(blk + (s ^ 1) * TC_BLK_BYTES), &rmap, bR + 8 * (s ^ 1), (int)(p0 + 32),
+                                    c_lo);
+                        ++n_res;
+                    }
+                    if (!__all_sync(0xffffffffu, mbar_wait(bR + 8 * s, (ci >> 1) & 1, P.err, 36))) {
+                        stop = true;
+                        break;
+                    }
+                } else {
+                    if (lane == 0) bulk_wait_read<1>();
+                    __syncwarp();
+                }
+                float v[32];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    float2 x0 = make_float2(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]));
+                    float2 x1 = make_float2(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+                    if (P.bias) {
+                        x0 = f2add(x0, make_float2(bias, bias));
+                        x1 = f2add(x1, make_float2(bias, bias));
+                    }
+                    if (has_res) {
+                        const float4 t = *reinterpret_cast<const float4 *>(buf + swz128(lane, i));
+                        x0 = f2add(make_float2(t.x, t.y), x0);
+                        x1 = f2add(make_float2(t.z, t.w), x1);
+                    }
+                    v[4 * i] = x0.x, v[4 * i + 1] = x0.y, v[4 * i + 2] = x1.x, v[4 * i + 3] = x1.y;
+                }
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    *reinterpret_cast<float4 *>(buf + swz128(lane, i)) =
+                        make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+                fence_proxy_async();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_2d(&omap, smem_u32(buf), (int)p0, c_lo);
+                    bulk_commit();
+                }
+                ++ci;
+                if (P.part) store_part(P, bs.block(P, v, p0), prev_part, c, chan_ok, p0, cc);
+            }
+            if (stop) break;
+            fence_before_sync();
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bAcc_empty + 8 * ab) : "memory");
+        }
+        if (lane == 0) {
+            for (uint32_t i = ci; i < n_res; ++i) mbar_wait(bR + 8 * (i & 1), (i >> 1) & 1, P.err, 40, TC_DRAIN_NS);
+            bulk_wait_all();
+        }
+        __syncwarp();
+    } else {
+        // transform warps: warp t forms channels 8t..8t+7 of each 64-channel
+        // slab; lane = (row rr = lane / 4 of each 8, channel pair cp = lane % 4)
+        const int tw = warp - TF_XF_WARP0;
+        const int rr = lane >> 2, cp = lane & 3;
+        const int cl = 8 * tw + 2 * cp;  // first of the lane's two channels within the slab
+        uint32_t ip = 0, is = 0;
+        bool ok = true;
+        for (int64_t tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x) {
+            const int64_t mt = tile / P.n_oc_tiles;
+            const int64_t r0a = floor4(mt * TC_BM - P.p);
+            for (int b = 0; b < IC_blocks && ok; ++b, ++is) {
+                const int sa = is % TF_NSA;
+                if (is >= TF_NSA) {
+                    int okl = 1;
+                    if (lane == 0) okl = mbar_wait(bA_empty + 8 * sa, ((is / TF_NSA) & 1) ^ 1, P.err, 41) ? 1 : 0;
+                    ok = __shfl_sync(0xffffffffu, okl, 0) != 0;
+                    if (!ok) break;
+                }
+                const int cg = 64 * b + cl;  // global channel
+                // the utterance whose slot holds the slab's first row, and the next
+                int u = utt_of_row(P.sb, P.sm, r0a > 0 ? r0a : 0);
+                int64_t lo = (int64_t)P.sm * __ldg(P.sb.offT + u);
+                int64_t hi = lo + (int64_t)P.sm * __ldg(P.sb.T + u) + P.sextra;
+                int64_t lo_n = u + 1 < P.sb.n ? (int64_t)P.sm * __ldg(P.sb.offT + u + 1) : INT64_MAX;
+                XfPrm pa = xf_load(P, u, cg);
+                uint8_t *slab = sA + sa * TC_A_BYTES + tw * lbo_a;
+                for (int j = 0; j < TF_PIECES; ++j, ++ip) {
+                    const int sp = ip % TF_NP;
+                    // every lane acquires the bytes the copy wrote
+                    if (!__all_sync(0xffffffffu, mbar_wait(bF_full + 8 * sp, (ip / TF_NP) & 1, P.err, 42))) {
+                        ok = false;
+                        break;
+                    }
+                    const int64_t g0 = r0a + 32 * j;
+                    for (int guard = 0; guard < P.sb.n && g0 >= lo_n; ++guard) {
+                        ++u;
+                        lo = lo_n;
+                        hi = lo + (int64_t)P.sm * __ldg(P.sb.T + u) + P.sextra;
+                        lo_n = u + 1 < P.sb.n ? (int64_t)P.sm * __ldg(P.sb.offT + u + 1) : INT64_MAX;
+                        pa = xf_load(P, u, cg);
+                    }
+                    const uint8_t *pc = sF + sp * TF_PIECE_BYTES;
+                    uint8_t *dst = slab + 32 * j * 16 + cp * 4;
+                    if (g0 >= lo && g0 + 32 <= hi) {
+                        xf_four<false>(pc, dst, cl, rr, pa, pa, g0, lo, hi, INT64_MAX, 0, P.nz);
+                    } else {
+                        // gap rows, an utterance's end, or the next one's start
+                        if (lo_n < g0 + 32) {
+                            const XfPrm pb = xf_load(P, u + 1, cg);
+                            const int64_t hi_n = lo_n + (int64_t)P.sm * __ldg(P.sb.T + u + 1) + P.sextra;
+                            xf_four<true>(pc, dst, cl, rr, pa, pb, g0, lo, hi, lo_n, hi_n, P.nz);
+                        } else {
+                            xf_four<true>(pc, dst, cl, rr, pa, pa, g0, lo, hi, INT64_MAX, 0, P.nz);
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bF_empty + 8 * sp) : "memory");
+                }
+                if (!ok) break;
+                // the slab's generic stores, visible to the tensor cores
+                fence_proxy_async();
+                __syncwarp();
+                if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bA_full + 8 * sa) : "memory");
+            }
+        }
+    }
+
+    fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        fence_after_sync();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS)
+                     : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 
@@ -879,6 +1367,8 @@ cudaError_t conv_tc_init() {
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(k_conv_tct<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, tt_smem(false));
     if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(k_conv_tcf, cudaFuncAttributeMaxDynamicSharedMemorySize, TF_SMEM);
+    if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(k_conv_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
 }
 
@@ -897,7 +1387,88 @@ static bool block_map_swz(CUtensorMap *m, const float *base, int64_t R, int C) {
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 2-D map of the F32 input [C][R] of k_conv_tcf in [64 ch][32 rows] pieces,
+// 128-byte swizzle; rows outside [0, R) read as zero.
+static bool piece_map(CUtensorMap *m, const float *base, int64_t R, int C) {
+    if (((uintptr_t)base & 15) || (R & 3)) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)R, (cuuint64_t)C};
+    cuuint64_t strides[1] = {(cuuint64_t)R * 4};
+    cuuint32_t box[2] = {32, 64};
+    cuuint32_t estr[2] = {1, 1};
+    return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)base, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool conv_tc_fusable(const ConvTcArgs &a) {
+    return g_encode && a.x && a.x_ms && a.x_nw && a.x_nb && a.x_gamma && a.x_beta && a.x_alpha && a.omul == 1 &&
+           a.oadd == 0 && a.phase_oc == 0 && !a.resid_half && a.accum == 0 && a.scale1 == 1.0f &&
+           a.scale2 == 1.0f && a.OC >= 64 && a.OC <= a.n_tiles * TC_BN && a.n_pos == a.R_out &&
+           a.R_out % 128 == 0 && (!a.resid || a.R_resid == a.R_out) && a.IC_pad >= 64 && a.IC_pad % 64 == 0 &&
+           a.K >= 1 && a.d >= 1 && a.p >= 0 && (a.K - 1) * a.d + 3 <= TC_SLAB - TC_BM && a.sb.n >= 1 && a.sm >= 4 &&
+           a.sextra >= 0;
+}
+
+// k_conv_tcf launch: the operand formed from x inside the conv.
+static cudaError_t conv_tc_fused(const ConvTcArgs &a, cudaStream_t st) {
+    if (!conv_tc_fusable(a)) return cudaErrorInvalidValue;
+    TcParams P;
+    memset(&P, 0, sizeof(P));
+    P.IC_blocks = a.IC_pad / 64;
+    P.K = a.K;
+    P.p = a.p;
+    P.d = a.d;
+    P.OC = a.OC;
+    P.n_tiles = a.n_tiles;
+    P.n_oc_tiles = (a.OC + TC_BN - 1) / TC_BN;
+    P.mma_n = TC_BN;
+    P.m_tiles = (a.n_pos + TC_BM - 1) / TC_BM;
+    P.w = a.w;
+    P.out = a.out;
+    P.R_out = a.R_out;
+    P.n_pos = a.n_pos;
+    P.omul = 1;
+    P.bias = a.bias;
+    P.resid = a.resid;
+    P.R_resid = a.R_resid;
+    P.scale1 = 1.0f;
+    P.scale2 = 1.0f;
+    P.err = a.err;
+    P.sb = a.sb;
+    P.sm = a.sm;
+    P.sextra = a.sextra;
+    P.IC = a.IC_pad;
+    P.x_ms = a.x_ms;
+    P.x_nw = a.x_nw;
+    P.x_nb = a.x_nb;
+    P.x_gamma = a.x_gamma;
+    P.x_beta = a.x_beta;
+    P.x_alpha = a.x_alpha;
+    P.nz = -0.0f;
+    const bool fused_stats = a.stats && a.part && a.stats_aligned;
+    P.part = fused_stats ? a.part : nullptr;
+    CUtensorMap omap, rmap, xmap;
+    memset(&omap, 0, sizeof(omap));
+    memset(&rmap, 0, sizeof(rmap));
+    memset(&xmap, 0, sizeof(xmap));
+    if (!block_map_swz(&omap, a.out, a.R_out, a.OC) ||
+        !block_map_swz(&rmap, a.resid ? a.resid : a.out, a.R_out, a.OC) || !piece_map(&xmap, a.x, a.R_out, a.IC_pad))
+        return cudaErrorInvalidValue;
+    const int64_t tiles = P.m_tiles * P.n_oc_tiles;
+    const int64_t slots = g_num_sms > 0 ? g_num_sms : 148;
+    const unsigned grid = (unsigned)(tiles < slots ? tiles : slots);
+    k_conv_tcf<<<grid, TF_THREADS, TF_SMEM, st>>>(P, omap, rmap, xmap);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess || !a.stats) return e;
+    if (fused_stats)
+        stats_blocks(a.part, a.R_out / 32, a.OC, a.sm, a.sextra, a.sb, a.stats, st);
+    else
+        stats(a.out, a.R_out, a.OC, a.sm, a.sextra, a.sb, a.stats, st);
+    return cudaGetLastError();
+}
+
 cudaError_t conv_tc(const ConvTcArgs &a, cudaStream_t st) {
+    if (a.x) return conv_tc_fused(a, st);
     const int halo = (a.K - 1) * a.d;
     if (a.K < 1 || a.d < 1 || a.p < 0 || halo > TC_SLAB - TC_BM || a.p > kHalfLo || a.IC_pad % 64 != 0 ||
         a.OC > a.n_tiles * TC_BN || a.n_pos < 1 || a.R_in < half_stride(0))

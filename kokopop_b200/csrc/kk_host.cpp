@@ -15,6 +15,7 @@
 #include "kk_host.h"
 
 #include <cmath>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <memory>
@@ -295,6 +296,10 @@ void kk_ctx::derive() {
         if (t && !t->f16) tc_mode = false;
         if (!t && cv.first.find("conv1x1") == std::string::npos) tc_mode = false;
     }
+    {
+        const char *f = std::getenv("KOKOPOP_B200_FUSED_OPERAND");
+        fuse_operand = f && f[0] == '1';
+    }
     if (tc_mode) {
         check_cuda(conv_tc_init(), "tensor-core conv init");
         std::vector<float> h;
@@ -510,6 +515,7 @@ struct Runner {
     const int64_t *d_cum = nullptr;
     float2 *ms = nullptr;
     float2 *ms2 = nullptr;  // a second set, for the conv that writes the next AdaIN input
+    float2 *ms3 = nullptr;  // statistics computed just before a fused-operand conv
     float *gbase = nullptr, *bbase = nullptr;
     const bool tc;
 
@@ -563,6 +569,7 @@ struct Runner {
         ++c.n_launches;
         ms = (float2 *)c.buf("stats", n * 1090 * 2);
         ms2 = (float2 *)c.buf("stats2", n * 1090 * 2);
+        ms3 = (float2 *)c.buf("stats3", n * 1090 * 2);
     }
 
     const AdainSite &site(const std::string &prefix) {
@@ -701,6 +708,7 @@ struct Runner {
         timed_begin(e0, e1);
         check_cuda(conv_tc(a, st), "tensor-core conv launch");
         timed_end(e0, e1, 2.0 * pw.OC * (double)pw.IC * K * (double)e.valid);
+        if (e.stats) ++c.n_launches;  // the statistics pass
     }
 
     // Convolution by weight name on an operand of the current path (stride 1).
@@ -834,6 +842,72 @@ struct Runner {
 
     // graph_generator_resblock: x_in -> (3 iterations) -> wb, the last
     // iteration writing final_out (accumulating / scaling) when given.
+    // AdaIN + Snake of x (statistics x_stats, or computed here when null),
+    // then the conv by weight name into out: inside the conv (k_conv_tcf)
+    // where it applies, else the operand prologue into o and the conv.
+    void adain_snake_conv(const std::string &adain, const std::string &alpha, const float *x, const float2 *x_stats,
+                          const Op &o, int C, int m, int extra, const std::string &wname, const std::string &bname,
+                          int K, int p, int d, float *out, Epi e) {
+        const int64_t Rm = R(m);
+        if (tc && c.fuse_operand) {
+            const AdainSite &s = site(adain);
+            if (s.C != C) throw KKError(KK_ERROR_MODEL, "AdaIN channel mismatch: " + adain);
+            auto it = c.packed.find(wname);
+            if (it == c.packed.end()) throw KKError(KK_ERROR_MODEL, "no packed weight for " + wname);
+            const PackedW &pw = it->second;
+            ConvTcArgs a{};
+            a.IC_pad = pw.IC_pad;
+            a.w = (const __half *)pw.buf.p;
+            a.n_tiles = pw.n_tiles;
+            a.OC = pw.OC;
+            a.K = K;
+            a.p = p;
+            a.d = d;
+            a.out = out;
+            a.R_out = Rm;
+            a.n_pos = Rm;
+            a.omul = 1;
+            a.oadd = 0;
+            a.bias = bname.empty() ? nullptr : c.W(bname).d;
+            a.resid = e.resid;
+            a.R_resid = e.R_resid;
+            a.resid_half = e.resid_half;
+            a.scale1 = e.scale1;
+            a.accum = e.accum;
+            a.scale2 = e.scale2;
+            a.err = (int *)c.d_err.p;
+            a.stats = e.stats;
+            a.sb = B;
+            a.sm = m;
+            a.sextra = extra;
+            if (e.stats) {
+                a.stats_aligned = aligned32(m) ? 1 : 0;
+                a.part = (float2 *)c.buf("stats_part", (size_t)pw.OC * (size_t)(Rm / 32) * 2);
+            }
+            a.x = x;
+            a.x_ms = x_stats ? x_stats : ms3;
+            a.x_nw = c.W(adain + ".norm.weight").d;
+            a.x_nb = c.W(adain + ".norm.bias").d;
+            a.x_gamma = s.gamma;
+            a.x_beta = s.beta;
+            a.x_alpha = c.W(alpha).d;
+            if (pw.IC_pad == C && conv_tc_fusable(a)) {
+                if (!x_stats) {
+                    stats(x, Rm, C, m, extra, B, ms3, st);
+                    ++c.n_launches;
+                }
+                cudaEvent_t e0 = nullptr, e1 = nullptr;
+                timed_begin(e0, e1);
+                check_cuda(conv_tc(a, st), "tensor-core conv launch (fused operand)");
+                timed_end(e0, e1, 2.0 * pw.OC * (double)pw.IC * K * (double)sum_len(m, extra));
+                if (e.stats) ++c.n_launches;
+                return;
+            }
+        }
+        adain_act(adain, x, o, Rm, C, m, extra, ACT_SNAKE, 0.f, alpha, x_stats);
+        conv_w(wname, bname, o, C, K, p, d, out, Rm, Rm, e, sum_len(m, extra));
+    }
+
     // x_in_stats: the statistics of x_in. A conv whose output feeds an AdaIN
     // leaves that output's statistics behind (ms after conv1, ms2 after conv2).
     void gen_resblock(const std::string &pf, int K, const float *x_in, float *wb, float *final_out, int accum,
@@ -844,15 +918,13 @@ struct Runner {
         for (int i = 0; i < 3; ++i) {
             const std::string is = std::to_string(i);
             const int d = kDil[i];
-            adain_act(pf + ".adain1." + is, cur, o, Rm, C, m, extra, ACT_SNAKE, 0.f, pf + ".alpha1." + is,
-                      cur_stats);
             Epi e1;
             e1.stats = ms;
             e1.sm = m;
             e1.sextra = extra;
-            conv_w(pf + ".convs1." + is + ".weight", pf + ".convs1." + is + ".bias", o, C, K, (K * d - d) / 2, d, tmp,
-                   Rm, Rm, e1, sum_len(m, extra));
-            adain_act(pf + ".adain2." + is, tmp, o, Rm, C, m, extra, ACT_SNAKE, 0.f, pf + ".alpha2." + is, ms);
+            adain_snake_conv(pf + ".adain1." + is, pf + ".alpha1." + is, cur, cur_stats, o, C, m, extra,
+                             pf + ".convs1." + is + ".weight", pf + ".convs1." + is + ".bias", K, (K * d - d) / 2, d,
+                             tmp, e1);
             Epi e;
             e.resid = cur;
             e.R_resid = Rm;
@@ -867,8 +939,8 @@ struct Runner {
                 e.sm = m;
                 e.sextra = extra;
             }
-            conv_w(pf + ".convs2." + is + ".weight", pf + ".convs2." + is + ".bias", o, C, K, K / 2, 1, out, Rm, Rm,
-                   e, sum_len(m, extra));
+            adain_snake_conv(pf + ".adain2." + is, pf + ".alpha2." + is, tmp, ms, o, C, m, extra,
+                             pf + ".convs2." + is + ".weight", pf + ".convs2." + is + ".bias", K, K / 2, 1, out, e);
             cur = wb;
             cur_stats = e.stats;
         }

@@ -106,6 +106,10 @@ struct kk_ctx {
     bool convt_f16[2] = {false, false};
     // tensor-core path: every convolution weight is F16
     bool tc_mode = false;
+    // KOKOPOP_B200_FUSED_OPERAND=1 at upload: the residual-block convs form
+    // their AdaIN + Snake operand inside the conv (k_conv_tcf, bit-identical
+    // to the separate operand pass, slower than it on B200 so far)
+    bool fuse_operand = false;
     std::unordered_map<std::string, kk::PackedW> packed;
     std::unordered_map<std::string, kk::DevBuf> adain_t;  // fc weights transposed to [128][C]
     kk::DevBuf d_err;  // device-side error code of the tensor-core kernel

@@ -173,9 +173,19 @@ struct ConvTcArgs {
     int sm, sextra;
     int stats_aligned;
     float2 *part;
+    // x non-null: the operand is formed inside the conv from the F32 tensor
+    // x [IC_pad][R_out] (the output's level) as half(snake(adain(x))) on the
+    // valid rows of level (sm, sextra), zero elsewhere: the k_prologue_h
+    // arithmetic with (mean, scale) x_ms [n][IC], norm weight/bias [IC],
+    // gamma/beta [n][IC] and Snake alpha [IC]; in / R_in are unused. Only
+    // where conv_tc_fusable holds.
+    const float *x;
+    const float2 *x_ms;
+    const float *x_nw, *x_nb, *x_gamma, *x_beta, *x_alpha;
 };
 cudaError_t conv_tc_init();
 cudaError_t conv_tc(const ConvTcArgs &a, cudaStream_t st);
+bool conv_tc_fusable(const ConvTcArgs &a);
 int conv_tc_max_halo();
 
 // prologue_h: y[c/8][row][c%8] = half(act(adain(x[c][row]))) on valid rows

@@ -118,6 +118,30 @@ def test_ragged_batch_equals_single_calls(ctx, w16):
         np.testing.assert_array_equal(ctx.decoder_forward([u])[0], b)
 
 
+def test_fused_operand_equals_separate_pass(ctx, w16, monkeypatch):
+    """With KOKOPOP_B200_FUSED_OPERAND=1 the residual-block convs form their
+    AdaIN + Snake operand inside the conv (k_conv_tcf) with the arithmetic of
+    the separate operand pass: the two paths agree bit for bit, and the fused
+    one launches fewer kernels."""
+    rng = np.random.default_rng(11)
+    utts = [W.make_utterance(rng, t) for t in (37, 5, 90, 1)]
+    runs = {}
+    for flag in ("1", "0"):
+        monkeypatch.setenv("KOKOPOP_B200_FUSED_OPERAND", flag)
+        ctx.upload(w16)
+        ctx.profile_enable(True)
+        ctx.profile_read(reset=True)
+        out = ctx.decoder_forward(utts)
+        runs[flag] = (out, ctx.profile_read(reset=True)["launches"])
+        ctx.profile_enable(False)
+    monkeypatch.delenv("KOKOPOP_B200_FUSED_OPERAND")
+    ctx.upload(w16)
+    for a, b in zip(runs["1"][0], runs["0"][0]):
+        np.testing.assert_array_equal(a, b)
+    # 24 operand passes per generator stage are gone
+    assert runs["1"][1] <= runs["0"][1] - 48
+
+
 def test_unvoiced_everywhere(ctx, w32, o32):
     ctx.upload(w32)
     u = W.make_utterance(np.random.default_rng(4), 6)
