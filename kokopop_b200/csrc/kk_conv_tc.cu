@@ -197,6 +197,20 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// The same load into floats (the accumulator values), for in-place epilogues.
+__device__ __forceinline__ void tmem_ld32f(uint32_t taddr, float (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+        "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=f"(r[0]), "=f"(r[1]), "=f"(r[2]), "=f"(r[3]), "=f"(r[4]), "=f"(r[5]), "=f"(r[6]), "=f"(r[7]),
+          "=f"(r[8]), "=f"(r[9]), "=f"(r[10]), "=f"(r[11]), "=f"(r[12]), "=f"(r[13]), "=f"(r[14]), "=f"(r[15]),
+          "=f"(r[16]), "=f"(r[17]), "=f"(r[18]), "=f"(r[19]), "=f"(r[20]), "=f"(r[21]), "=f"(r[22]),
+          "=f"(r[23]), "=f"(r[24]), "=f"(r[25]), "=f"(r[26]), "=f"(r[27]), "=f"(r[28]), "=f"(r[29]),
+          "=f"(r[30]), "=f"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
 // ---------------------------------------------------------------------------
 // kernel
 // ---------------------------------------------------------------------------
@@ -237,6 +251,7 @@ struct TcParams {
     const float *x_gamma, *x_beta;       // [n][IC]
     const float *x_alpha;                // [IC] Snake alpha
     float nz;                            // -0.0f, opaque to the compiler (packed products)
+    unsigned long long nz2;              // two packed -0.0f, the same
 };
 
 // Positions x channels, register epilogue (strided row maps). Persistent: CTA
@@ -916,20 +931,6 @@ __device__ __forceinline__ XfPrm xf_load(const TcParams &P, int u, int c) {
     return q;
 }
 
-__device__ __forceinline__ XfPrm xf_select(bool b, const XfPrm &x, const XfPrm &y) {
-    XfPrm r;
-#define KK_SEL(f) r.f = b ? y.f : x.f
-    KK_SEL(nmean);
-    KK_SEL(scale);
-    KK_SEL(nw);
-    KK_SEL(nb);
-    KK_SEL(g);
-    KK_SEL(be);
-    KK_SEL(al);
-    KK_SEL(ia);
-#undef KK_SEL
-    return r;
-}
 
 // Packed product a * b rounded once, as fma(a, b, z) with z = -0.0f from a
 // kernel parameter: the assembler can neither simplify it back to a multiply
@@ -951,49 +952,34 @@ __device__ __forceinline__ float xf_piece(const uint8_t *pc, int c, int r) {
 
 __device__ __forceinline__ int64_t floor4(int64_t v) { return v - (((v % 4) + 4) % 4); }
 
-// One lane's share of a piece: rows 8 i + rr (i = 0..3) of channels cl and
-// cl + 1 into the slab (dst = the slab's row of the piece's first row, plus
-// the lane's channel-pair offset), as half(snake(adain(x))) with the
-// k_prologue_h expressions, one rounding per operation, in packed FP32
-// pairs; the eight elements run as straight-line code around one warp-wide
-// polynomial test (all 32 lanes call this together). SLOW: the piece holds
-// rows outside [lo, hi) of utterance qa's, or rows from lo_n on, which
-// belong to the next utterance (qb, valid below hi_n); invalid rows are zero.
-template <bool SLOW>
-__device__ __forceinline__ void xf_four(const uint8_t *pc, uint8_t *dst, int cl, int rr, const XfPrm &qa,
-                                        const XfPrm &qb, int64_t g0, int64_t lo, int64_t hi, int64_t lo_n,
-                                        int64_t hi_n, float z) {
-    float2 w[4], al[4], ia[4];
-    bool valid[4];
+// One lane's share of an edge piece: rows 8 i + rr (i = 0..3) of channels
+// cl and cl + 1, as half(snake(adain(x))) with the terms q of one utterance,
+// written for the rows g with sel_lo <= g < sel_hi: the value where
+// lo <= g < hi, else zero. The k_prologue_h expressions with one rounding
+// per operation, in packed FP32 pairs; all 32 lanes call this together (one
+// warp-wide polynomial test). dst = the slab chunk at the piece's first row
+// plus the lane's channel-pair offset.
+__device__ __forceinline__ void xf_edge(const uint8_t *pc, uint8_t *dst, int cl, int rr, const XfPrm &q, int64_t g0,
+                                        int64_t lo, int64_t hi, int64_t sel_lo, int64_t sel_hi, float z) {
+    float2 w[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const int rw = 8 * i + rr;
         const float2 x = make_float2(xf_piece(pc, cl, rw), xf_piece(pc, cl + 1, rw));
-        XfPrm q = qa;
-        valid[i] = true;
-        if (SLOW) {
-            const int64_t g = g0 + rw;
-            const bool in_n = g >= lo_n;
-            valid[i] = in_n ? g < hi_n : (g >= lo && g < hi);
-            q = xf_select(in_n, qa, qb);
-        }
         float2 v = f2mul_sep(f2add(x, q.nmean), q.scale, z);
         v = f2add(f2mul_sep(v, q.nw, z), q.nb);
         v = f2add(v, f2mul_sep(v, q.g, z));
         w[i] = f2add(v, q.be);
-        al[i] = q.al;
-        ia[i] = q.ia;
     }
     float2 t[4];
     bool small = true;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        t[i] = f2mul_sep(w[i], al[i], z);
+        t[i] = f2mul_sep(w[i], q.al, z);
         small = small && fabsf(t[i].x) <= kSnakeSmall && fabsf(t[i].y) <= kSnakeSmall;
     }
     float2 sn[4];
     if (__all_sync(0xffffffffu, small)) {
-        // snake_sin_small in pairs
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const float2 t2 = f2mul_sep(t[i], t[i], z);
@@ -1009,10 +995,126 @@ __device__ __forceinline__ void xf_four(const uint8_t *pc, uint8_t *dst, int cl,
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const float2 v = f2add(w[i], f2mul_sep(f2mul_sep(sn[i], sn[i], z), ia[i], z));
+        const int64_t g = g0 + 8 * i + rr;
+        const float2 v = f2add(w[i], f2mul_sep(f2mul_sep(sn[i], sn[i], z), q.ia, z));
         const __half2 h = __floats2half2_rn(v.x, v.y);
         const uint32_t hb = *reinterpret_cast<const uint32_t *>(&h);
-        *reinterpret_cast<uint32_t *>(dst + (8 * i + rr) * 16) = valid[i] ? hb : 0u;
+        if (g >= sel_lo && g < sel_hi)
+            *reinterpret_cast<uint32_t *>(dst + (8 * i + rr) * 16) = (g >= lo && g < hi) ? hb : 0u;
+    }
+}
+
+// FP32 pairs held in one 64-bit register from load to store (no packing
+// moves between operations); products as fma(a, b, z) with z a packed -0
+// from a kernel parameter, so each step keeps its own rounding.
+typedef unsigned long long p2_t;
+__device__ __forceinline__ p2_t p2_bc(float v) {
+    p2_t d;
+    asm("mov.b64 %0, {%1, %1};" : "=l"(d) : "f"(v));
+    return d;
+}
+__device__ __forceinline__ p2_t p2_pack(float lo, float hi) {
+    p2_t d;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+    return d;
+}
+__device__ __forceinline__ float2 p2_unpack(p2_t a) {
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(a));
+    return r;
+}
+__device__ __forceinline__ p2_t p2_add(p2_t a, p2_t b) {
+    p2_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ p2_t p2_fma(p2_t a, p2_t b, p2_t c) {
+    p2_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
+// One channel's AdaIN + Snake terms as loaded (prefetched a slab ahead)...
+struct XfRaw {
+    float2 ms;
+    float nw, nb, g, be, al;
+};
+__device__ __forceinline__ XfRaw xf_raw(const TcParams &P, int u, int c) {
+    XfRaw r;
+    r.ms = P.x_ms[(int64_t)u * P.IC + c];
+    r.nw = P.x_nw[c];
+    r.nb = P.x_nb[c];
+    r.g = P.x_gamma[(int64_t)u * P.IC + c];
+    r.be = P.x_beta[(int64_t)u * P.IC + c];
+    r.al = P.x_alpha[c];
+    return r;
+}
+// ... and each broadcast to both halves of a pair (nmean = -mean)
+struct XfP {
+    p2_t nmean, scale, nw, nb, g, be, al, ia;
+};
+__device__ __forceinline__ XfP xf_bc(const XfRaw &r) {
+    XfP q;
+    q.nmean = p2_bc(-r.ms.x);
+    q.scale = p2_bc(r.ms.y);
+    q.nw = p2_bc(r.nw);
+    q.nb = p2_bc(r.nb);
+    q.g = p2_bc(r.g);
+    q.be = p2_bc(r.be);
+    q.al = p2_bc(r.al);
+    q.ia = p2_bc(__fdiv_rn(1.0f, r.al));
+    return q;
+}
+
+// A piece whose 32 rows are all valid rows of one utterance: lane = ch +
+// 8 q owns channel c (= 8 t + ch of the slab) at rows 8 i + 2 q and the row
+// after (i = 0..3), one 8-byte load per pair; the k_prologue_h expressions
+// with one rounding per operation; one warp-wide polynomial test for the
+// piece (all 32 lanes call this together). dst = the warp's slab chunk at
+// the piece's first row.
+__device__ __forceinline__ void xf_rows(const uint8_t *pc, uint8_t *dst, int c, int ch, int q, const XfP &p, p2_t z) {
+    p2_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int r = 8 * i + 2 * q;
+        const p2_t x = *reinterpret_cast<const p2_t *>(pc + c * 128 + (((r >> 2) ^ (c & 7)) << 4) + (r & 3) * 4);
+        p2_t v = p2_fma(p2_add(x, p.nmean), p.scale, z);
+        v = p2_add(p2_fma(v, p.nw, z), p.nb);
+        v = p2_add(v, p2_fma(v, p.g, z));
+        w[i] = p2_add(v, p.be);
+    }
+    p2_t t[4];
+    bool small = true;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        t[i] = p2_fma(w[i], p.al, z);
+        const float2 tf = p2_unpack(t[i]);
+        small = small && fabsf(tf.x) <= kSnakeSmall && fabsf(tf.y) <= kSnakeSmall;
+    }
+    p2_t sn[4];
+    if (__all_sync(0xffffffffu, small)) {
+        // snake_sin_small in pairs
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const p2_t t2 = p2_fma(t[i], t[i], z);
+            p2_t pp = p2_fma(p2_bc(2.7557319e-06f), t2, p2_bc(-1.9841270e-04f));
+            pp = p2_fma(pp, t2, p2_bc(8.3333333e-03f));
+            pp = p2_fma(pp, t2, p2_bc(-1.6666667e-01f));
+            sn[i] = p2_fma(p2_fma(t[i], t2, z), pp, t[i]);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 tf = p2_unpack(t[i]);
+            sn[i] = p2_pack(snake_sin(tf.x), snake_sin(tf.y));
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 v = p2_unpack(p2_add(w[i], p2_fma(p2_fma(sn[i], sn[i], z), p.ia, z)));
+        const int r = 8 * i + 2 * q;
+        *reinterpret_cast<__half *>(dst + r * 16 + ch * 2) = __float2half_rn(v.x);
+        *reinterpret_cast<__half *>(dst + (r + 1) * 16 + ch * 2) = __float2half_rn(v.y);
     }
 }
 
@@ -1203,8 +1305,8 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
             const float bias = (P.bias && chan_ok) ? P.bias[c] : 0.f;
             const uint32_t t_base = tmem + ((uint32_t)(32 * lq) << 16) + (uint32_t)(ab * TC_BM);
             for (int cc = 0; cc < 8; ++cc) {
-                uint32_t r[32];
-                tmem_ld32(t_base + (uint32_t)(32 * cc), r);
+                float v[32];  // the accumulator, then the output, in place
+                tmem_ld32f(t_base + (uint32_t)(32 * cc), v);
                 const int64_t p0 = pw + 32 * cc;
                 const int s = ci & 1;
                 uint8_t *buf = blk + s * TC_BLK_BYTES;
@@ -1224,11 +1326,10 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
                     if (lane == 0) bulk_wait_read<1>();
                     __syncwarp();
                 }
-                float v[32];
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
-                    float2 x0 = make_float2(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]));
-                    float2 x1 = make_float2(__uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+                    float2 x0 = make_float2(v[4 * i], v[4 * i + 1]);
+                    float2 x1 = make_float2(v[4 * i + 2], v[4 * i + 3]);
                     if (P.bias) {
                         x0 = f2add(x0, make_float2(bias, bias));
                         x1 = f2add(x1, make_float2(bias, bias));
@@ -1239,11 +1340,8 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
                         x1 = f2add(make_float2(t.z, t.w), x1);
                     }
                     v[4 * i] = x0.x, v[4 * i + 1] = x0.y, v[4 * i + 2] = x1.x, v[4 * i + 3] = x1.y;
+                    *reinterpret_cast<float4 *>(buf + swz128(lane, i)) = make_float4(x0.x, x0.y, x1.x, x1.y);
                 }
-#pragma unroll
-                for (int i = 0; i < 8; ++i)
-                    *reinterpret_cast<float4 *>(buf + swz128(lane, i)) =
-                        make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
                 fence_proxy_async();
                 __syncwarp();
                 if (lane == 0) {
@@ -1265,69 +1363,98 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
         __syncwarp();
     } else {
         // transform warps: warp t forms channels 8t..8t+7 of each 64-channel
-        // slab; lane = (row rr = lane / 4 of each 8, channel pair cp = lane % 4)
-        const int tw = warp - TF_XF_WARP0;
+        // slab. Whole-utterance pieces: lane = ch + 8 q (xf_rows); pieces at
+        // utterance edges: lane = (row rr = lane / 4, channel pair cp = lane
+        // % 4) (xf_edge). The next slab's terms are loaded while this one is
+        // formed.
+        const int tw = warp - TF_XF_WARP0;  // channel chunk
         const int rr = lane >> 2, cp = lane & 3;
-        const int cl = 8 * tw + 2 * cp;  // first of the lane's two channels within the slab
+        const int ch = lane & 7, q8 = lane >> 3;
+        const int cl = 8 * tw + 2 * cp;  // edge pieces: the lane's first channel within the slab
+        const int c1 = 8 * tw + ch;      // whole pieces: the lane's channel within the slab
         uint32_t ip = 0, is = 0;
         bool ok = true;
-        for (int64_t tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x) {
+        int64_t tile = blockIdx.x;
+        int b = 0;
+        int u_cur = 0;
+        XfRaw raw_cur{};
+        if (tile < n_tiles_total) {
+            const int64_t r0 = floor4((tile / P.n_oc_tiles) * TC_BM - P.p);
+            u_cur = utt_of_row(P.sb, P.sm, r0 > 0 ? r0 : 0);
+            raw_cur = xf_raw(P, u_cur, c1);
+        }
+        while (tile < n_tiles_total && ok) {
             const int64_t mt = tile / P.n_oc_tiles;
             const int64_t r0a = floor4(mt * TC_BM - P.p);
-            for (int b = 0; b < IC_blocks && ok; ++b, ++is) {
-                const int sa = is % TF_NSA;
-                if (is >= TF_NSA) {
-                    int okl = 1;
-                    if (lane == 0) okl = mbar_wait(bA_empty + 8 * sa, ((is / TF_NSA) & 1) ^ 1, P.err, 41) ? 1 : 0;
-                    ok = __shfl_sync(0xffffffffu, okl, 0) != 0;
-                    if (!ok) break;
-                }
-                const int cg = 64 * b + cl;  // global channel
-                // the utterance whose slot holds the slab's first row, and the next
-                int u = utt_of_row(P.sb, P.sm, r0a > 0 ? r0a : 0);
-                int64_t lo = (int64_t)P.sm * __ldg(P.sb.offT + u);
-                int64_t hi = lo + (int64_t)P.sm * __ldg(P.sb.T + u) + P.sextra;
-                int64_t lo_n = u + 1 < P.sb.n ? (int64_t)P.sm * __ldg(P.sb.offT + u + 1) : INT64_MAX;
-                XfPrm pa = xf_load(P, u, cg);
-                uint8_t *slab = sA + sa * TC_A_BYTES + tw * lbo_a;
-                for (int j = 0; j < TF_PIECES; ++j, ++ip) {
-                    const int sp = ip % TF_NP;
-                    // every lane acquires the bytes the copy wrote
-                    if (!__all_sync(0xffffffffu, mbar_wait(bF_full + 8 * sp, (ip / TF_NP) & 1, P.err, 42))) {
-                        ok = false;
-                        break;
-                    }
-                    const int64_t g0 = r0a + 32 * j;
-                    for (int guard = 0; guard < P.sb.n && g0 >= lo_n; ++guard) {
-                        ++u;
-                        lo = lo_n;
-                        hi = lo + (int64_t)P.sm * __ldg(P.sb.T + u) + P.sextra;
-                        lo_n = u + 1 < P.sb.n ? (int64_t)P.sm * __ldg(P.sb.offT + u + 1) : INT64_MAX;
-                        pa = xf_load(P, u, cg);
-                    }
-                    const uint8_t *pc = sF + sp * TF_PIECE_BYTES;
-                    uint8_t *dst = slab + 32 * j * 16 + cp * 4;
-                    if (g0 >= lo && g0 + 32 <= hi) {
-                        xf_four<false>(pc, dst, cl, rr, pa, pa, g0, lo, hi, INT64_MAX, 0, P.nz);
-                    } else {
-                        // gap rows, an utterance's end, or the next one's start
-                        if (lo_n < g0 + 32) {
-                            const XfPrm pb = xf_load(P, u + 1, cg);
-                            const int64_t hi_n = lo_n + (int64_t)P.sm * __ldg(P.sb.T + u + 1) + P.sextra;
-                            xf_four<true>(pc, dst, cl, rr, pa, pb, g0, lo, hi, lo_n, hi_n, P.nz);
-                        } else {
-                            xf_four<true>(pc, dst, cl, rr, pa, pa, g0, lo, hi, INT64_MAX, 0, P.nz);
-                        }
-                    }
-                    __syncwarp();
-                    if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bF_empty + 8 * sp) : "memory");
-                }
-                if (!ok) break;
-                // the slab's generic stores, visible to the tensor cores
-                fence_proxy_async();
-                __syncwarp();
-                if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bA_full + 8 * sa) : "memory");
+            // the slab after this one, and its terms
+            int64_t tile_n = tile;
+            int b_n = b + 1;
+            if (b_n == IC_blocks) {
+                b_n = 0;
+                tile_n += gridDim.x;
             }
+            int u_next = 0;
+            XfRaw raw_next{};
+            if (tile_n < n_tiles_total) {
+                const int64_t r0n = floor4((tile_n / P.n_oc_tiles) * TC_BM - P.p);
+                u_next = utt_of_row(P.sb, P.sm, r0n > 0 ? r0n : 0);
+                raw_next = xf_raw(P, u_next, 64 * b_n + c1);
+            }
+            const int sa = is % TF_NSA;
+            if (is >= TF_NSA) {
+                int okl = 1;
+                if (lane == 0) okl = mbar_wait(bA_empty + 8 * sa, ((is / TF_NSA) & 1) ^ 1, P.err, 41) ? 1 : 0;
+                ok = __shfl_sync(0xffffffffu, okl, 0) != 0;
+                if (!ok) break;
+            }
+            const int cg = 64 * b + cl;  // edge pieces: global channel
+            int u = u_cur;
+            int64_t lo = (int64_t)P.sm * __ldg(P.sb.offT + u);
+            int64_t hi = lo + (int64_t)P.sm * __ldg(P.sb.T + u) + P.sextra;
+            int64_t lo_n = u + 1 < P.sb.n ? (int64_t)P.sm * __ldg(P.sb.offT + u + 1) : INT64_MAX;
+            XfP pf = xf_bc(raw_cur);
+            uint8_t *slab = sA + sa * TC_A_BYTES + tw * lbo_a;
+            for (int j = 0; j < TF_PIECES; ++j, ++ip) {
+                const int sp = ip % TF_NP;
+                // every lane acquires the bytes the copy wrote
+                if (!__all_sync(0xffffffffu, mbar_wait(bF_full + 8 * sp, (ip / TF_NP) & 1, P.err, 42))) {
+                    ok = false;
+                    break;
+                }
+                const int64_t g0 = r0a + 32 * j;
+                for (int guard = 0; guard < P.sb.n && g0 >= lo_n; ++guard) {
+                    ++u;
+                    lo = lo_n;
+                    hi = lo + (int64_t)P.sm * __ldg(P.sb.T + u) + P.sextra;
+                    lo_n = u + 1 < P.sb.n ? (int64_t)P.sm * __ldg(P.sb.offT + u + 1) : INT64_MAX;
+                    pf = xf_bc(xf_raw(P, u, 64 * b + c1));
+                }
+                const uint8_t *pc = sF + sp * TF_PIECE_BYTES;
+                if (g0 >= lo && g0 + 32 <= hi) {
+                    xf_rows(pc, slab + 32 * j * 16, c1, ch, q8, pf, P.nz2);
+                } else {
+                    // gap rows, an utterance's end, or the next one's start
+                    // (rows of this utterance's slot, then the next one's)
+                    uint8_t *dst = slab + 32 * j * 16 + cp * 4;
+                    xf_edge(pc, dst, cl, rr, xf_load(P, u, cg), g0, lo, hi, INT64_MIN, lo_n, P.nz);
+                    if (lo_n < g0 + 32) {
+                        const int64_t hi_n = lo_n + (int64_t)P.sm * __ldg(P.sb.T + u + 1) + P.sextra;
+                        xf_edge(pc, dst, cl, rr, xf_load(P, u + 1, cg), g0, lo_n, hi_n, lo_n, INT64_MAX, P.nz);
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bF_empty + 8 * sp) : "memory");
+            }
+            if (!ok) break;
+            // the slab's generic stores, visible to the tensor cores
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bA_full + 8 * sa) : "memory");
+            ++is;
+            raw_cur = raw_next;
+            u_cur = u_next;
+            tile = tile_n;
+            b = b_n;
         }
     }
 
@@ -1445,6 +1572,7 @@ static cudaError_t conv_tc_fused(const ConvTcArgs &a, cudaStream_t st) {
     P.x_beta = a.x_beta;
     P.x_alpha = a.x_alpha;
     P.nz = -0.0f;
+    P.nz2 = 0x8000000080000000ull;
     const bool fused_stats = a.stats && a.part && a.stats_aligned;
     P.part = fused_stats ? a.part : nullptr;
     CUtensorMap omap, rmap, xmap;
