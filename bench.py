@@ -348,8 +348,10 @@ def main():
     ev1 = torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
     secs = 0.0
+    th0 = time.perf_counter()
     for k in range(args.steps):
         secs += step_device(args.warmup + k)
+    host_enqueue_ms = (time.perf_counter() - th0) * 1e3 / max(1, args.steps)
     ev1.record(stream)
     torch.cuda.synchronize()
     barrier()
@@ -437,6 +439,7 @@ def main():
                      "conv_share_of_step": (prof["conv_ms"] / 1e3) / elapsed if elapsed else None},
         "cpu_baseline": cpu,
         "clocks": clk,
+        "host_enqueue_ms_per_step": round(host_enqueue_ms, 2),
         "gpu_launches": prof["launches"],
         "ttfa_p50_ms": ttfa,
         "lstm": lstm,
