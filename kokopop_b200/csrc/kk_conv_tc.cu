@@ -1004,36 +1004,6 @@ __device__ __forceinline__ void xf_edge(const uint8_t *pc, uint8_t *dst, int cl,
     }
 }
 
-// FP32 pairs held in one 64-bit register from load to store (no packing
-// moves between operations); products as fma(a, b, z) with z a packed -0
-// from a kernel parameter, so each step keeps its own rounding.
-typedef unsigned long long p2_t;
-__device__ __forceinline__ p2_t p2_bc(float v) {
-    p2_t d;
-    asm("mov.b64 %0, {%1, %1};" : "=l"(d) : "f"(v));
-    return d;
-}
-__device__ __forceinline__ p2_t p2_pack(float lo, float hi) {
-    p2_t d;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
-    return d;
-}
-__device__ __forceinline__ float2 p2_unpack(p2_t a) {
-    float2 r;
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(a));
-    return r;
-}
-__device__ __forceinline__ p2_t p2_add(p2_t a, p2_t b) {
-    p2_t d;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ p2_t p2_fma(p2_t a, p2_t b, p2_t c) {
-    p2_t d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
-
 // One channel's AdaIN + Snake terms as loaded (prefetched a slab ahead)...
 struct XfRaw {
     float2 ms;
