@@ -227,6 +227,42 @@ def bench_lstm(kb, W, device, runs):
     return out
 
 
+def bench_prosody(kb, W, device, runs, pool, batch):
+    """The prosody predictor's F0 / N chain (biLSTM 640 -> 2x256, then per
+    branch 3 x AdainResBlk1d and the 1x1 projection) over one batch of the
+    pool's lengths as aligned frames, seed-2 F16 weights (config 2's draw),
+    inputs N(0, 1) / style N(0, 0.1), device-resident, timed with CUDA
+    events on the launch stream: ms per call and frames/s."""
+    import torch
+    lens = np.array([u.T for u in pool[:batch]], np.int32)
+    c = kb.Context(device)
+    c.upload(W.prosody_weights(f16=True))
+    g = torch.Generator(device="cuda").manual_seed(102)
+    rows = int(lens.sum())
+    en = torch.randn(rows, 640, device="cuda", generator=g)
+    st = 0.1 * torch.randn(len(lens), 128, device="cuda", generator=g)
+    f0 = torch.empty(2 * rows, device="cuda")
+    nn = torch.empty(2 * rows, device="cuda")
+    stream = torch.cuda.Stream()
+    call = lambda: c.prosody_f0n_device(lens, en.data_ptr(), st.data_ptr(), f0.data_ptr(), nn.data_ptr(),
+                                        stream.cuda_stream)
+    for _ in range(2):
+        call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(runs):
+        call()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / runs
+    c.close()
+    return {"workload": f"prosody F0/N chain: biLSTM 640->2x256 + 2 x (3 AdainResBlk1d + 1x1 proj), "
+                        f"batch {len(lens)} utterances T~U[40,800] frames, F16 weights seed 2",
+            "frames": rows, "ms_per_call": ms, "frames_per_s": rows / (ms / 1e3),
+            "audio_s_per_s": rows / 40.0 / (ms / 1e3)}
+
+
 def config_dict(batch=BATCH):
     return {
         "workload": "Kokoro-82M decoder (AdainResBlk1d encode/decode) + ISTFTNet generator + iSTFT; "
@@ -247,6 +283,7 @@ def main():
     ap.add_argument("--batch", type=int, default=BATCH, help="utterances per GPU step (profiling cases)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg (profiling cases)")
     ap.add_argument("--lstm-runs", type=int, default=5, help="timed calls per LSTM-stack case (0 skips)")
+    ap.add_argument("--prosody-runs", type=int, default=3, help="timed calls of the prosody F0/N chain (0 skips)")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
@@ -411,6 +448,9 @@ def main():
     lstm = None
     if rank == 0 and args.lstm_runs > 0:
         lstm = bench_lstm(kb, W, local, args.lstm_runs)
+    prosody = None
+    if rank == 0 and args.prosody_runs > 0:
+        prosody = bench_prosody(kb, W, local, args.prosody_runs, pool, args.batch)
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
             sample = cpu_sample(pool)
@@ -443,6 +483,7 @@ def main():
         "gpu_launches": prof["launches"],
         "ttfa_p50_ms": ttfa,
         "lstm": lstm,
+        "prosody": prosody,
         "pipeline_tflops": value / world * algorithmic_flop_per_asr_frame() * 40.0 / 1e12,
     }
     if rank == 0:

@@ -134,6 +134,27 @@ int kk_duration_encoder_forward(kk_ctx *ctx, int32_t n_seqs, const int32_t *n_st
 int kk_duration_encoder_forward_device(kk_ctx *ctx, int32_t n_seqs, const int32_t *n_steps, const float *x,
                                        const float *style, float *out, void *stream);
 
+/* The prosody predictor's F0 / N chain (src/arch/kokoro/kokoro.cpp:669-708,
+ * replacing the ggml sub-graph from the aligned `en` to f0_curve / n_curve):
+ * the biLSTM kokopop.predictor.shared (640 -> 2 x 256) over the T_b frames,
+ * then for each of F0 and N three adain_resblk1d
+ * kokopop.predictor.{F0,N}.{0,1,2} (graph_ops.cpp:996-1065; the second
+ * upsamples x2) with the prosody style, and the 1x1 conv {F0,N}_proj + bias.
+ * Ragged batch; per utterance b:
+ *   n_frames[b] = T_b, at most 8192
+ *   en    : [T_b, 640], frame-major (the aligned duration-encoder output,
+ *           as kk_align_durations writes it)
+ *   style : [128] (the prosody half of the voice row)
+ *   f0, n : [2 T_b]
+ * Host buffers. */
+int kk_prosody_f0n(kk_ctx *ctx, int32_t n_utts, const int32_t *n_frames, const float *en, const float *style,
+                   float *f0, float *n);
+
+/* Same with device-resident en, style, f0 and n (lengths on the host).
+ * Asynchronous on `stream` (NULL = the context's stream). */
+int kk_prosody_f0n_device(kk_ctx *ctx, int32_t n_utts, const int32_t *n_frames, const float *en,
+                          const float *style, float *f0, float *n, void *stream);
+
 /* Durations -> frames and the alignment (duration_to_frames,
  * src/arch/kokoro/kokoro.cpp:181-193; build_duration_mask :115-152 and
  * en = d . mask :669-674): frames[i] = clamp(int(lrint(d[i] / speed)), 1, 50)

@@ -78,6 +78,8 @@ def load_library():
     L.kk_bilstm_forward.argtypes = [vp, ctypes.c_char_p, ctypes.c_int32, _i32p, ctypes.c_int64, _f32p, _f32p]
     L.kk_duration_encoder_forward.argtypes = [vp, ctypes.c_int32, _i32p, _f32p, _f32p, _f32p]
     L.kk_duration_encoder_forward_device.argtypes = [vp, ctypes.c_int32, _i32p, vp, vp, vp, vp]
+    L.kk_prosody_f0n.argtypes = [vp, ctypes.c_int32, _i32p, _f32p, _f32p, _f32p, _f32p]
+    L.kk_prosody_f0n_device.argtypes = [vp, ctypes.c_int32, _i32p, vp, vp, vp, vp, vp]
     L.kk_align_durations.argtypes = [vp, ctypes.c_int64, _f32p, ctypes.c_float, _i32p,
                                      ctypes.POINTER(ctypes.c_int64), _f32p, ctypes.c_int64, _f32p, ctypes.c_int64]
     L.kk_profile_enable.argtypes = [vp, ctypes.c_int]
@@ -223,6 +225,26 @@ class Context:
         self._check(self.L.kk_duration_encoder_forward(self.h, len(xs), _ptr(lens, _i32p), _ptr(x), _ptr(st),
                                                        _ptr(out)))
         return np.split(out, np.cumsum(lens)[:-1])
+
+    def prosody_f0n(self, ens: Sequence[np.ndarray], styles: Sequence[np.ndarray]):
+        """kk_prosody_f0n: ens[b] [T_b, 640] (aligned duration-encoder
+        output), styles[b] [128] -> (f0 [2 T_b], n [2 T_b]) per utterance."""
+        ens = [np.ascontiguousarray(e, np.float32) for e in ens]
+        lens = np.array([e.shape[0] for e in ens], np.int32)
+        en = np.concatenate(ens, axis=0)
+        st = np.ascontiguousarray(np.stack(styles), np.float32)
+        f0 = np.zeros(2 * int(lens.sum()), np.float32)
+        nn = np.zeros(2 * int(lens.sum()), np.float32)
+        self._check(self.L.kk_prosody_f0n(self.h, len(ens), _ptr(lens, _i32p), _ptr(en), _ptr(st), _ptr(f0),
+                                          _ptr(nn)))
+        cuts = np.cumsum(2 * lens)[:-1]
+        return list(zip(np.split(f0, cuts), np.split(nn, cuts)))
+
+    def prosody_f0n_device(self, lens: np.ndarray, en_ptr: int, style_ptr: int, f0_ptr: int, n_ptr: int,
+                           stream: int = 0) -> None:
+        lens = np.ascontiguousarray(lens, np.int32)
+        self._check(self.L.kk_prosody_f0n_device(self.h, len(lens), _ptr(lens, _i32p), en_ptr, style_ptr, f0_ptr,
+                                                 n_ptr, stream))
 
     def duration_encoder_device(self, lens: np.ndarray, x_ptr: int, style_ptr: int, out_ptr: int,
                                 stream: int = 0) -> None:

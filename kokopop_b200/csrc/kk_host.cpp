@@ -195,6 +195,33 @@ static std::vector<std::string> adain_site_prefixes() {
     return v;
 }
 
+// The prosody predictor's F0 / N chain (kokoro.cpp:669-708): its AdaIN sites
+// and convolutions, used when a weight set carries them.
+static std::vector<std::string> prosody_site_prefixes() {
+    std::vector<std::string> v;
+    for (const char *br : {"F0", "N"})
+        for (int i = 0; i < 3; ++i) {
+            const std::string p = std::string("kokopop.predictor.") + br + "." + std::to_string(i);
+            v.push_back(p + ".norm1");
+            v.push_back(p + ".norm2");
+        }
+    return v;
+}
+
+static std::vector<std::pair<std::string, int>> prosody_convs() {
+    std::vector<std::pair<std::string, int>> v;
+    for (const char *br : {"F0", "N"}) {
+        for (int i = 0; i < 3; ++i) {
+            const std::string p = std::string("kokopop.predictor.") + br + "." + std::to_string(i);
+            v.push_back({p + ".conv1.weight", 3});
+            v.push_back({p + ".conv2.weight", 3});
+            v.push_back({p + ".conv1x1.weight", 1});
+        }
+        v.push_back({std::string("kokopop.predictor.") + br + "_proj.weight", 1});
+    }
+    return v;
+}
+
 // Packs a convolution weight W[oc, ic, k] (via `get`) into the tensor-core
 // kernel's shared-memory images: half [K][IC_pad/64][n_tiles][8][128][8],
 // zero in the channel padding. The values are F16 already, so the
@@ -303,7 +330,12 @@ void kk_ctx::derive() {
     if (tc_mode) {
         check_cuda(conv_tc_init(), "tensor-core conv init");
         std::vector<float> h;
-        for (const auto &cv : tc_convs()) {
+        std::vector<std::pair<std::string, int>> convs = tc_convs();
+        for (const auto &cv : prosody_convs()) {
+            const DevTensor *t = Wopt(cv.first);
+            if (t && t->f16) convs.push_back(cv);
+        }
+        for (const auto &cv : convs) {
             const DevTensor *t = Wopt(cv.first);
             if (!t) continue;
             const int K = cv.second, OC = (int)t->ne[1], IC = (int)(t->ne[0] / K);
@@ -355,12 +387,18 @@ void kk_ctx::derive() {
     // AdaIN sites
     sites.clear();
     site_total_C = 0;
-    for (const auto &p : adain_site_prefixes()) {
+    std::vector<std::string> site_list = adain_site_prefixes();
+    const size_t n_required_sites = site_list.size();
+    for (const auto &p : prosody_site_prefixes()) site_list.push_back(p);
+    for (size_t si_i = 0; si_i < site_list.size(); ++si_i) {
+        const std::string &p = site_list[si_i];
         const DevTensor *gw = Wopt(p + ".fc.gamma.weight"), *gb = Wopt(p + ".fc.gamma.bias");
         const DevTensor *bw = Wopt(p + ".fc.beta.weight"), *bb = Wopt(p + ".fc.beta.bias");
         if (!gw || !gb || !bw || !bb || !Wopt(p + ".norm.weight") || !Wopt(p + ".norm.bias")) {
-            if (missing.empty()) missing = p + ".fc/norm";
-            ok = false;
+            if (si_i < n_required_sites) {
+                if (missing.empty()) missing = p + ".fc/norm";
+                ok = false;
+            }
             continue;
         }
         SiteInfo si;
@@ -414,6 +452,32 @@ void kk_ctx::derive() {
                           "kokopop.decoder.decode.3.pool.weight"})
         dok = need(n) && dok;
     decoder_ready = dok;
+    // prosody predictor F0 / N chain (optional)
+    {
+        bool pok = true;
+        missing_prosody.clear();
+        auto needp = [&](const std::string &n) {
+            if (!Wopt(n)) {
+                if (missing_prosody.empty()) missing_prosody = n;
+                pok = false;
+            }
+        };
+        for (const char *sfx : {"", "_reverse"})
+            for (const char *w : {"weight_ih_l0", "weight_hh_l0", "bias_ih_l0", "bias_hh_l0"})
+                needp(std::string("kokopop.predictor.shared.") + w + sfx);
+        for (const char *br : {"F0", "N"}) {
+            for (int i = 0; i < 3; ++i) {
+                const std::string p = std::string("kokopop.predictor.") + br + "." + std::to_string(i);
+                for (const char *w : {".conv1.weight", ".conv1.bias", ".conv2.weight", ".conv2.bias"}) needp(p + w);
+                for (const char *nm : {".norm1", ".norm2"})
+                    if (site_index.find(p + nm) == site_index.end()) needp(p + nm + ".fc.gamma.weight");
+            }
+            needp(std::string("kokopop.predictor.") + br + ".1.pool.weight");
+            needp(std::string("kokopop.predictor.") + br + "_proj.weight");
+            needp(std::string("kokopop.predictor.") + br + "_proj.bias");
+        }
+        prosody_ready = pok;
+    }
     // tables
     StftTables stt;
     IstftTables ist;
@@ -838,6 +902,41 @@ struct Runner {
         // AdaIN(norm2) -> LeakyReLU(0.2) -> conv2, + shortcut, * 1/sqrt(2)
         adain_act(pf + ".norm2", tmp, opL, Rc, Cout, m, 0, ACT_LEAKY, 0.2f, "");
         conv_w(pf + ".conv2.weight", pf + ".conv2.bias", opL, Cout, 3, 1, 1, out, Rc, Rc, e2, sum_len(m, 0));
+    }
+
+    // The prosody predictor's F0 and N chains after the shared biLSTM
+    // (kokoro.cpp:682-708): x [512][R(1)] on the frame level -> three
+    // adain_resblk1d kokopop.predictor.{F0,N}.{0,1,2} (the second upsamples
+    // x2) -> the 1x1 projection {F0,N}_proj with bias -> f0p / np [1][R(2)].
+    void prosody_chains(const float *x, int Cx, float *f0p, float *np) {
+        const int64_t R1 = R(1), R2 = R(2);
+        if (tc) {
+            zero(op("opT", 1, 1152), 1152);
+            zero(op("op2", 2, 1152), 1152);
+        }
+        float *y0 = c.buf("pr_y0", 1024 * (size_t)R1);
+        float *y1 = c.buf("pr_y1", 512 * (size_t)R2);
+        float *y2 = c.buf("pr_y2", 512 * (size_t)R2);
+        for (int br = 0; br < 2; ++br) {
+            const std::string p = std::string("kokopop.predictor.") + (br ? "N" : "F0");
+            const int C0 = (int)c.W(p + ".0.conv1.weight").ne[1];
+            const int C1 = (int)c.W(p + ".1.conv1.weight").ne[1];
+            const int C2 = (int)c.W(p + ".2.conv1.weight").ne[1];
+            if (C0 > 1024 || C1 > 512 || C2 > 512) throw KKError(KK_ERROR_MODEL, "prosody block too wide: " + p);
+            adain_resblk(p + ".0", x, Cx, false, y0);
+            adain_resblk(p + ".1", y0, C0, true, y1);
+            adain_resblk(p + ".2", y1, C1, false, y2);
+            Op in;
+            if (tc) {
+                in = op("op2", 2, 1152);
+                act_only(y2, in, R2, C2, 2, 0, ACT_NONE, 0.f);
+            } else {
+                in.f = y2;
+                in.R = R2;
+            }
+            conv_w(p + "_proj.weight", p + "_proj.bias", in, C2, 1, 0, 1, br ? np : f0p, R2, R2, Epi{},
+                   sum_len(2, 0));
+        }
     }
 
     // graph_generator_resblock: x_in -> (3 iterations) -> wb, the last
@@ -1582,6 +1681,40 @@ void duration_encoder_device(kk_ctx &c, int32_t n_seqs, const int32_t *n_steps, 
     check_cuda(cudaGetLastError(), "kernel launch");
 }
 
+// The prosody predictor's F0 / N chain (kokoro.cpp:669-708) from the aligned
+// duration-encoder output: the biLSTM kokopop.predictor.shared over the
+// frames, then the F0 and N chains on the packed frame level.
+void prosody_device(kk_ctx &c, int32_t n_utts, const int32_t *n_frames, const float *en, const float *style,
+                    float *f0, float *nn, cudaStream_t st) {
+    if (!c.prosody_ready) throw KKError(KK_ERROR_MODEL, "prosody weights incomplete, first missing: " + c.missing_prosody);
+    const LstmLayer &L = c.lstm_layer("kokopop.predictor.shared");
+    if (L.in_dim != 640 || L.H != 256) throw KKError(KK_ERROR_MODEL, "predictor.shared must be a biLSTM 640 -> 2 x 256");
+    Runner::Seqs q = lstm_seqs(c, n_utts, n_frames, st);
+    Plan Pl = lstm_plan(n_utts, q.max_len);
+    Runner rl(c, Pl, st);
+    rl.setup_batch();
+    const int64_t Rr = Pl.R(1);
+    float *X = c.buf("lstm_X", (size_t)640 * Rr);
+    check_cuda(cudaMemsetAsync(X, 0, (size_t)640 * Rr * 4, st), "memset");
+    lstm_pack(en, 640, nullptr, 0, X, Rr, q.d_len, q.d_cum, n_utts, q.max_len, st);
+    float *hout = c.buf("lstm_h", (size_t)512 * Rr);
+    rl.bilstm(L, X, hout, q);
+    // the frame level of a ragged plan (kMaxFrames per utterance)
+    Plan P = make_plan(n_frames, n_utts);
+    Runner r(c, P, st);
+    r.setup_batch();
+    r.setup_adain(style);
+    const int64_t R1 = P.R(1), R2 = P.R(2);
+    float *x = c.buf("pr_x", (size_t)512 * R1);
+    lstm_to_level(hout, Rr, 512, n_utts, q.d_len, q.max_len, x, R1, r.B.offT, 1, st);
+    float *f0p = c.buf("pr_f0", (size_t)R2), *np = c.buf("pr_n", (size_t)R2);
+    r.prosody_chains(x, 512, f0p, np);
+    gather(f0p, f0, R2, 1, 2, 0, r.B, r.d_cum, 2 * P.maxT, st);
+    gather(np, nn, R2, 1, 2, 0, r.B, r.d_cum, 2 * P.maxT, st);
+    c.n_launches += 3 + 1 + 2;
+    check_cuda(cudaGetLastError(), "kernel launch");
+}
+
 int64_t total_steps(int32_t n_seqs, const int32_t *n_steps) {
     int64_t rows = 0;
     for (int b = 0; b < n_seqs; ++b) rows += n_steps[b];
@@ -1623,6 +1756,50 @@ int kk_duration_encoder_forward_device(kk_ctx *ctx, int32_t n_seqs, const int32_
         use_device(ctx);
         cudaStream_t st = stream ? (cudaStream_t)stream : ctx->st;
         duration_encoder_device(*ctx, n_seqs, n_steps, x, style, out, st);
+        return KK_OK;
+    });
+}
+
+int kk_prosody_f0n(kk_ctx *ctx, int32_t n_utts, const int32_t *n_frames, const float *en, const float *style,
+                   float *f0, float *n) {
+    return guarded([&] {
+        if (!ctx || !n_frames || !en || !style || !f0 || !n || n_utts < 1)
+            throw KKError(KK_ERROR_INVALID_ARGUMENT, "null argument");
+        use_device(ctx);
+        kk_ctx &c = *ctx;
+        cudaStream_t st = c.st;
+        int64_t rows = 0;
+        for (int b = 0; b < n_utts; ++b) {
+            if (n_frames[b] < 1 || n_frames[b] > kMaxFrames)
+                throw KKError(KK_ERROR_INVALID_ARGUMENT, "utterance length out of range [1, 8192]");
+            rows += n_frames[b];
+        }
+        float *d_en = c.buf("pr_en", (size_t)rows * 640);
+        float *d_style = c.buf("pr_style", (size_t)n_utts * 128);
+        float *d_f0 = c.buf("pr_f0_out", (size_t)rows * 2), *d_n = c.buf("pr_n_out", (size_t)rows * 2);
+        check_cuda(cudaMemcpyAsync(d_en, en, (size_t)rows * 640 * 4, cudaMemcpyHostToDevice, st), "upload en");
+        check_cuda(cudaMemcpyAsync(d_style, style, (size_t)n_utts * 128 * 4, cudaMemcpyHostToDevice, st),
+                   "upload style");
+        prosody_device(c, n_utts, n_frames, d_en, d_style, d_f0, d_n, st);
+        check_cuda(cudaMemcpyAsync(f0, d_f0, (size_t)rows * 2 * 4, cudaMemcpyDeviceToHost, st), "D2H");
+        check_cuda(cudaMemcpyAsync(n, d_n, (size_t)rows * 2 * 4, cudaMemcpyDeviceToHost, st), "D2H");
+        check_cuda(cudaStreamSynchronize(st), "prosody F0 / N");
+        check_device_error(ctx);
+        return KK_OK;
+    });
+}
+
+int kk_prosody_f0n_device(kk_ctx *ctx, int32_t n_utts, const int32_t *n_frames, const float *en,
+                          const float *style, float *f0, float *n, void *stream) {
+    return guarded([&] {
+        if (!ctx || !n_frames || !en || !style || !f0 || !n || n_utts < 1)
+            throw KKError(KK_ERROR_INVALID_ARGUMENT, "null argument");
+        for (int b = 0; b < n_utts; ++b)
+            if (n_frames[b] < 1 || n_frames[b] > kMaxFrames)
+                throw KKError(KK_ERROR_INVALID_ARGUMENT, "utterance length out of range [1, 8192]");
+        use_device(ctx);
+        cudaStream_t st = stream ? (cudaStream_t)stream : ctx->st;
+        prosody_device(*ctx, n_utts, n_frames, en, style, f0, n, st);
         return KK_OK;
     });
 }

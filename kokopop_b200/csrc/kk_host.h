@@ -102,6 +102,8 @@ struct kk_ctx {
     // derived from the weights
     bool decoder_ready = false, generator_ready = false;
     std::string missing;
+    bool prosody_ready = false;  // the prosody predictor's F0 / N chain
+    std::string missing_prosody;
     kk::DevBuf convt_phase[2];
     bool convt_f16[2] = {false, false};
     // tensor-core path: every convolution weight is F16

@@ -37,6 +37,26 @@ void scatter(const float *src, float *dst, int64_t R, int C, int m, int extra, c
     k_scatter<<<grid, 256, 0, st>>>(src, dst, R, C, m, extra, b, cumT);
 }
 
+// The inverse of k_scatter: the packed [C, R] rows of each utterance back to
+// per-utterance [C, m*T + extra] tensors, concatenated.
+__global__ void k_gather(const float *__restrict__ src, float *__restrict__ dst, int64_t R, int C, int m,
+                         int extra, Batch b, const int64_t *__restrict__ cumT) {
+    const int u = blockIdx.z;
+    const int c = blockIdx.y;
+    const int64_t len = (int64_t)m * b.T[u] + extra;
+    const float *s = src + (int64_t)c * R + (int64_t)m * b.offT[u];
+    float *d = dst + (int64_t)C * ((int64_t)m * cumT[u] + (int64_t)extra * u) + (int64_t)c * len;
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < len;
+         t += (int64_t)gridDim.x * blockDim.x)
+        d[t] = s[t];
+}
+
+void gather(const float *src, float *dst, int64_t R, int C, int m, int extra, const Batch &b,
+            const int64_t *cumT, int max_len, cudaStream_t st) {
+    dim3 grid((unsigned)((max_len + 255) / 256 < 64 ? (max_len + 255) / 256 : 64), C, b.n);
+    k_gather<<<grid, 256, 0, st>>>(src, dst, R, C, m, extra, b, cumT);
+}
+
 // ---------------------------------------------------------------------------
 // AdaIN affine terms: gamma = Wg . style + bg, beta = Wb . style + bb
 // (linear(), graph_ops.cpp:636-654). Sequential F32 sum over the 128 style

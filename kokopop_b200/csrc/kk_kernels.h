@@ -93,6 +93,9 @@ struct IstftTables {
 
 void scatter(const float *src, float *dst, int64_t R, int C, int m, int extra, const Batch &b,
              const int64_t *cumT, int max_len, cudaStream_t st);
+// gather: the inverse of scatter (packed [C, R] -> per-utterance tensors)
+void gather(const float *src, float *dst, int64_t R, int C, int m, int extra, const Batch &b,
+            const int64_t *cumT, int max_len, cudaStream_t st);
 void adain_affine(const AdainSite *sites_dev, int n_sites, const float *style, int n_utts,
                   cudaStream_t st);
 void stats(const float *x, int64_t R, int C, int m, int extra, const Batch &b, float2 *ms,
@@ -218,6 +221,9 @@ size_t lstm_rec_smem(int Bc);
 cudaError_t lstm_recurrence(const LstmRecArgs &a, cudaStream_t st);  // H = 256
 void lstm_pack(const float *x, int D, const float *style, int Ds, float *X, int64_t R, const int32_t *len,
                const int64_t *cum, int B, int max_len, cudaStream_t st);
+// X [C][R] in the LSTM layout -> rows m * offT[b] + t of a packed level
+void lstm_to_level(const float *X, int64_t R, int C, int B, const int32_t *len, int max_len, float *dst,
+                   int64_t R_dst, const int64_t *offT, int m, cudaStream_t st);
 void lstm_unpack(const float *X, int64_t R, int C, float *out, const int32_t *len, const int64_t *cum, int B,
                  int max_len, cudaStream_t st);
 void style_linear(const float *w, const float *bias, int f16, const float *style, int Ds, int C, int B, float *out,

@@ -225,6 +225,25 @@ __global__ void k_lstm_unpack(const float *__restrict__ X, int64_t R, int C, flo
     }
 }
 
+// X [C][R] in the LSTM layout (row t * B + b) -> dst [C][R_dst] at rows
+// m * offT[b] + t of a packed ragged level (t < len[b]); other rows untouched.
+__global__ void k_lstm_to_level(const float *__restrict__ X, int64_t R, int B, const int32_t *__restrict__ len,
+                                float *__restrict__ dst, int64_t R_dst, const int64_t *__restrict__ offT, int m) {
+    const int b = blockIdx.y, c = blockIdx.z;
+    const int L = len[b];
+    const int64_t o = (int64_t)m * offT[b];
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < L; t += gridDim.x * blockDim.x)
+        dst[(int64_t)c * R_dst + o + t] = X[(int64_t)c * R + (int64_t)t * B + b];
+}
+
+void lstm_to_level(const float *X, int64_t R, int C, int B, const int32_t *len, int max_len, float *dst,
+                   int64_t R_dst, const int64_t *offT, int m, cudaStream_t st) {
+    int bx = (max_len + 255) / 256;
+    if (bx > 64) bx = 64;
+    if (bx < 1) bx = 1;
+    k_lstm_to_level<<<dim3(bx, B, C), 256, 0, st>>>(X, R, B, len, dst, R_dst, offT, m);
+}
+
 void lstm_pack(const float *x, int D, const float *style, int Ds, float *X, int64_t R, const int32_t *len,
                const int64_t *cum, int B, int max_len, cudaStream_t st) {
     int bx = (int)(((int64_t)max_len * (D + Ds) + 255) / 256);

@@ -154,6 +154,26 @@ def duration_encoder_spec() -> List[Tuple[str, Tuple[int, ...]]]:
     return spec
 
 
+def prosody_spec() -> List[Tuple[str, Tuple[int, ...]]]:
+    """The prosody predictor's F0 / N chain (kokoro.cpp:669-708): the shared
+    biLSTM 640 -> 2 x 256, then per branch AdainResBlk1d(512, 512),
+    (512, 256, x2 upsample), (256, 256) and the 1x1 projection 256 -> 1."""
+    p = "kokopop.predictor"
+    spec: List[Tuple[str, Tuple[int, ...]]] = lstm_spec(f"{p}.shared", HIDDEN + STYLE_DIM)
+    for br in ("F0", "N"):
+        spec += _adain_resblk(f"{p}.{br}.0", HIDDEN, HIDDEN, False)
+        spec += _adain_resblk(f"{p}.{br}.1", HIDDEN, HIDDEN // 2, True)
+        spec += _adain_resblk(f"{p}.{br}.2", HIDDEN // 2, HIDDEN // 2, False)
+        spec += [(f"{p}.{br}_proj.weight", (HIDDEN // 2, 1)), (f"{p}.{br}_proj.bias", (1,))]
+    return spec
+
+
+def prosody_weights(f16: bool = False) -> Dict[str, Tensor]:
+    """Prosody F0 / N chain weights: seed 2, N(0, 0.02) (config 2's
+    draw), F16 under the converter's policy when f16, else F32."""
+    return make_weights(prosody_spec(), seed=2, dist="normal", scale=0.02, f16=f16)
+
+
 def _is_f16_under_converter_policy(name: str, ne: Sequence[int]) -> bool:
     """_target_type (tools/convert_kokoro_to_gguf.py:140-177) for these tensors."""
     if len(ne) <= 1:

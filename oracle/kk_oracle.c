@@ -1055,6 +1055,63 @@ int kko_bilstm(kko_model *m, const char *prefix, int64_t N, int64_t in_dim, cons
     return rc;
 }
 
+/* The prosody predictor's F0 / N chain (kokoro.cpp:669-708): the biLSTM
+ * kokopop.predictor.shared over the frames (cur = [2H, T] after the
+ * transpose), then per branch three adain_resblk1d
+ * kokopop.predictor.{F0,N}.{0,1,2} (the second with the x2 upsample), the
+ * 1x1 conv {F0,N}_proj and its channel bias (add_channel_bias), viewed as a
+ * 1-D curve of 2T values. */
+int kko_prosody_f0n(kko_model *m, int64_t T, const float *en, const float *style, float *f0,
+                    float *nout) {
+    g_err[0] = 0;
+    const ko_tensor *whh = req(m, "kokopop.predictor.shared.weight_hh_l0");
+    if (!whh) return -1;
+    const int64_t H2 = 2 * whh->ne[0];
+    float *h = fbuf((size_t)(T * H2));
+    int rc = kko_bilstm(m, "kokopop.predictor.shared", T, 640, en, h);
+    if (rc != 0) {
+        free(h);
+        return rc;
+    }
+    float *x = fbuf((size_t)(H2 * T));
+    for (int64_t t = 0; t < T; ++t)
+        for (int64_t c = 0; c < H2; ++c) x[c * T + t] = h[t * H2 + c];
+    free(h);
+    for (int br = 0; br < 2 && rc == 0; ++br) {
+        const char *name = br ? "N" : "F0";
+        const float *cur = x;
+        int64_t C = H2, L = T;
+        float *bufs[3] = {NULL, NULL, NULL};
+        char key[256];
+        for (int i = 0; i < 3 && rc == 0; ++i) {
+            char pfx[128];
+            snprintf(pfx, sizeof pfx, "kokopop.predictor.%s.%d", name, i);
+            snprintf(key, sizeof key, "%s.conv1.weight", pfx);
+            const ko_tensor *c1w = req(m, key);
+            if (!c1w) {
+                rc = -1;
+                break;
+            }
+            const int64_t L2 = i == 1 ? 2 * L : L;
+            bufs[i] = fbuf((size_t)(c1w->ne[1] * L2));
+            rc = adain_resblk(m, pfx, cur, C, L, style, i == 1, bufs[i], &C);
+            L = L2;
+            cur = bufs[i];
+        }
+        if (rc == 0) {
+            snprintf(key, sizeof key, "kokopop.predictor.%s_proj.weight", name);
+            const ko_tensor *pw = req(m, key);
+            snprintf(key, sizeof key, "kokopop.predictor.%s_proj.bias", name);
+            const ko_tensor *pb = req(m, key);
+            int64_t ol;
+            rc = (pw && pb) ? conv1d(pw, pb, cur, C, L, 1, 0, 1, 1, br ? nout : f0, &ol) : -1;
+        }
+        for (int i = 0; i < 3; ++i) free(bufs[i]);
+    }
+    free(x);
+    return rc;
+}
+
 /* ada_layer_norm (graph_ops.cpp:865-886): ggml_norm over features per step,
  * then (normed + normed * gamma) + beta. */
 static int ada_layer_norm(kko_model *m, const char *prefix, float *x, int64_t D, int64_t N,

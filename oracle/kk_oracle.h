@@ -94,6 +94,12 @@ int kko_bilstm(kko_model *m, const char *prefix, int64_t N, int64_t in_dim,
 int kko_duration_encoder(kko_model *m, int64_t N, const float *x,
                          const float *style, float *out);
 
+/* ---- prosody predictor F0 / N chain (kokoro.cpp:669-708) ----
+ * en: [T, 640] (the aligned duration-encoder output, frame-major);
+ * style: [128] (prosody half); f0, n: [2T]. */
+int kko_prosody_f0n(kko_model *m, int64_t T, const float *en, const float *style,
+                    float *f0, float *n);
+
 /* ---- R11: durations -> frames and the alignment (kokoro.cpp:115-193, :669-674)
  * frames[i] = clamp(lrint(d[i] / speed), 1, 50); *total = sum(frames).
  * If hidden != NULL: en[f, :] = hidden[token(f), :] for every frame f

@@ -175,6 +175,17 @@ class OracleModel:
         return out
 
 
+    def prosody_f0n(self, en: np.ndarray, style: np.ndarray):
+        """kko_prosody_f0n: en [T, 640], style [128] -> (f0 [2T], n [2T])."""
+        en = np.ascontiguousarray(en, dtype=np.float32)
+        T = en.shape[0]
+        f0 = np.zeros(2 * T, np.float32)
+        nn = np.zeros(2 * T, np.float32)
+        self._check(self.L.kko_prosody_f0n(ctypes.c_void_p(self.h), ctypes.c_int64(T), _ptr(en),
+                                           _ptr(np.ascontiguousarray(style, np.float32)), _ptr(f0), _ptr(nn)))
+        return f0, nn
+
+
 def istft(post: np.ndarray) -> np.ndarray:
     post = np.ascontiguousarray(post, dtype=np.float32)
     n = post.shape[1]

@@ -219,3 +219,19 @@ def test_duration_encoder_f16_input_sensitivity():
     b = m.duration_encoder(np.nextafter(x, np.float32(np.inf)).astype(np.float32), s)
     d = float(np.abs(a - b).max())
     assert 2e-4 < d < 3e-3
+
+
+def test_prosody_chain_shapes_and_determinism():
+    """The oracle's prosody F0 / N chain (kokoro.cpp:669-708): [T, 640] ->
+    two curves of 2T values, finite and identical on a second call."""
+    w = W.prosody_weights(f16=False)
+    m = O.OracleModel(w)
+    rng = np.random.default_rng(7)
+    for T in (1, 9):
+        en = rng.normal(0.0, 1.0, size=(T, 640)).astype(np.float32)
+        st = rng.normal(0.0, 0.1, size=128).astype(np.float32)
+        f0, n = m.prosody_f0n(en, st)
+        assert f0.shape == (2 * T,) and n.shape == (2 * T,)
+        assert np.all(np.isfinite(f0)) and np.all(np.isfinite(n))
+        f0b, nb = m.prosody_f0n(en, st)
+        assert np.array_equal(f0, f0b) and np.array_equal(n, nb)
