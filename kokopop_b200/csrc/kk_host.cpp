@@ -848,33 +848,36 @@ struct Runner {
         ++c.n_launches;
     }
 
-    // adain_resblk1d (graph_ops.cpp:996-1065) on the T level.
-    void adain_resblk(const std::string &pf, const float *x, int Cin, bool up, float *out) {
-        const int64_t R1 = R(1), R2 = R(2);
+    // adain_resblk1d (graph_ops.cpp:996-1065) with its input on level mi (1 or
+    // 2; upsampling blocks take level 1 to level 2).
+    void adain_resblk(const std::string &pf, const float *x, int Cin, bool up, float *out, int mi = 1) {
+        if (mi != 1 && (mi != 2 || up)) throw KKError(KK_ERROR_INFERENCE, "unsupported resblock level");
+        const int64_t Ri = R(mi);
         const DevTensor &c1 = c.W(pf + ".conv1.weight");
         const int Cout = (int)c1.ne[1];
-        const int m = up ? 2 : 1;
-        const int64_t Rc = up ? R2 : R1;
-        Op opT = op("opT", 1, 1152);
-        Op opL = up ? op("op2", 2, 1152) : opT;
-        float *tmp = up ? c.buf("tmp2", 512 * (size_t)R2) : c.buf("tmpT", 1024 * (size_t)R1);
+        const int m = up ? 2 : mi;
+        const int64_t Rc = R(m);
+        Op opI = mi == 1 ? op("opT", 1, 1152) : op("op2", 2, 1152);
+        Op opL = up ? op("op2", 2, 1152) : opI;
+        float *tmp = m == 2 ? c.buf("tmp2", 512 * (size_t)R(2)) : c.buf("tmpT", 1024 * (size_t)R(1));
+        if (Cout > (m == 2 ? 512 : 1024)) throw KKError(KK_ERROR_MODEL, "resblock too wide: " + pf);
         // shortcut: nearest x2 upsample (folded into the epilogue's row map)
         // then the bias-free 1x1 conv, on the raw input
         Epi e2;
         e2.scale1 = kInvSqrt2;
         e2.resid_half = up ? 1 : 0;
-        e2.R_resid = R1;
+        e2.R_resid = Ri;
         if (c.Wopt(pf + ".conv1x1.weight")) {
-            float *sc = c.buf("scT", 1024 * (size_t)R1);
+            float *sc = c.buf("scT", 1024 * (size_t)Ri);
             Op xin;
             if (tc) {
-                act_only(x, opT, R1, Cin, 1, 0, ACT_NONE, 0.f);
-                xin = opT;
+                act_only(x, opI, Ri, Cin, mi, 0, ACT_NONE, 0.f);
+                xin = opI;
             } else {
                 xin.f = const_cast<float *>(x);
-                xin.R = R1;
+                xin.R = Ri;
             }
-            conv_w(pf + ".conv1x1.weight", "", xin, Cin, 1, 0, 1, sc, R1, R1, Epi{}, sum_len(1, 0));
+            conv_w(pf + ".conv1x1.weight", "", xin, Cin, 1, 0, 1, sc, Ri, Ri, Epi{}, sum_len(mi, 0));
             e2.resid = sc;
         } else {
             if (Cin != Cout) throw KKError(KK_ERROR_MODEL, "missing conv1x1 for " + pf);
@@ -886,6 +889,7 @@ struct Runner {
             if (pw.ne[0] != 3 || pw.ne[1] != 1 || pw.ne[2] != Cin)
                 throw KKError(KK_ERROR_MODEL, "invalid depthwise upsample pool shape: " + pf);
             // the pool reads F32 activations (the reference's dense F32 kernel)
+            const int64_t R1 = R(1), R2 = R(2);
             Op pf32;
             pf32.f = c.buf("pfT", 1090 * (size_t)R1);
             pf32.R = R1;
@@ -896,7 +900,7 @@ struct Runner {
                 pool_up(pf32.f, opL.f, R1, R2, Cin, pw.d, pb.d, B, P.maxT, 0, st);
             ++c.n_launches;
         } else {
-            adain_act(pf + ".norm1", x, opT, R1, Cin, 1, 0, ACT_LEAKY, 0.2f, "");
+            adain_act(pf + ".norm1", x, opI, Ri, Cin, mi, 0, ACT_LEAKY, 0.2f, "");
         }
         conv_w(pf + ".conv1.weight", pf + ".conv1.bias", opL, Cin, 3, 1, 1, tmp, Rc, Rc, Epi{}, sum_len(m, 0));
         // AdaIN(norm2) -> LeakyReLU(0.2) -> conv2, + shortcut, * 1/sqrt(2)
@@ -925,7 +929,7 @@ struct Runner {
             if (C0 > 1024 || C1 > 512 || C2 > 512) throw KKError(KK_ERROR_MODEL, "prosody block too wide: " + p);
             adain_resblk(p + ".0", x, Cx, false, y0);
             adain_resblk(p + ".1", y0, C0, true, y1);
-            adain_resblk(p + ".2", y1, C1, false, y2);
+            adain_resblk(p + ".2", y1, C1, false, y2, 2);
             Op in;
             if (tc) {
                 in = op("op2", 2, 1152);
