@@ -914,10 +914,10 @@ struct Runner {
     // x2) -> the 1x1 projection {F0,N}_proj with bias -> f0p / np [1][R(2)].
     void prosody_chains(const float *x, int Cx, float *f0p, float *np) {
         const int64_t R1 = R(1), R2 = R(2);
-        if (tc) {
-            zero(op("opT", 1, 1152), 1152);
-            zero(op("op2", 2, 1152), 1152);
-        }
+        // operand gaps must read as zero (half operands on the tensor-core
+        // path, F32 ones on the CUDA-core path)
+        zero(op("opT", 1, 1152), 1152);
+        zero(op("op2", 2, 1152), 1152);
         float *y0 = c.buf("pr_y0", 1024 * (size_t)R1);
         float *y1 = c.buf("pr_y1", 512 * (size_t)R2);
         float *y2 = c.buf("pr_y2", 512 * (size_t)R2);
