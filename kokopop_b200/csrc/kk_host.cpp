@@ -327,6 +327,28 @@ void kk_ctx::derive() {
         const char *f = std::getenv("KOKOPOP_B200_FUSED_OPERAND");
         fuse_operand = f && f[0] == '1';
     }
+    // the prosody chain's convolutions on the tensor cores when they are all
+    // F16, whatever the rest of the weight set
+    prosody_tc = true;
+    for (const auto &cv : prosody_convs()) {
+        const DevTensor *t = Wopt(cv.first);
+        if (t ? !t->f16 : cv.first.find("conv1x1") == std::string::npos) prosody_tc = false;
+    }
+    if (prosody_tc && !tc_mode) {
+        check_cuda(conv_tc_init(), "tensor-core conv init");
+        std::vector<float> h;
+        for (const auto &cv : prosody_convs()) {
+            const DevTensor *t = Wopt(cv.first);
+            if (!t) continue;
+            const int K = cv.second, OC = (int)t->ne[1], IC = (int)(t->ne[0] / K);
+            h.resize((size_t)t->n);
+            check_cuda(cudaMemcpy(h.data(), t->d, h.size() * 4, cudaMemcpyDeviceToHost), "read conv weight");
+            pack_tc(packed[cv.first], OC, IC, K,
+                    [&](int oc, int ic, int k) { return h[((size_t)oc * IC + ic) * K + k]; });
+        }
+    }
+    d_err.ensure(sizeof(int));
+    check_cuda(cudaMemset(d_err.p, 0, sizeof(int)), "clear error");
     if (tc_mode) {
         check_cuda(conv_tc_init(), "tensor-core conv init");
         std::vector<float> h;
@@ -381,8 +403,6 @@ void kk_ctx::derive() {
                             [&](int oc, int ic, int k) { return ph[(((size_t)r * OC + oc) * IC + ic) * 2 + k]; });
             }
         }
-        d_err.ensure(sizeof(int));
-        check_cuda(cudaMemset(d_err.p, 0, sizeof(int)), "clear error");
     }
     // AdaIN sites
     sites.clear();
@@ -583,7 +603,9 @@ struct Runner {
     float *gbase = nullptr, *bbase = nullptr;
     const bool tc;
 
-    Runner(kk_ctx &ctx, const Plan &plan, cudaStream_t s) : c(ctx), P(plan), st(s), tc(ctx.tc_mode) {}
+    // tc_path: the tensor-core path (default: the context's tc_mode)
+    Runner(kk_ctx &ctx, const Plan &plan, cudaStream_t s, int tc_path = -1)
+        : c(ctx), P(plan), st(s), tc(tc_path < 0 ? ctx.tc_mode : tc_path != 0) {}
 
     int64_t R(int m) const { return P.R(m); }
 
@@ -1705,7 +1727,7 @@ void prosody_device(kk_ctx &c, int32_t n_utts, const int32_t *n_frames, const fl
     rl.bilstm(L, X, hout, q);
     // the frame level of a ragged plan (kMaxFrames per utterance)
     Plan P = make_plan(n_frames, n_utts);
-    Runner r(c, P, st);
+    Runner r(c, P, st, c.prosody_tc ? 1 : 0);
     r.setup_batch();
     r.setup_adain(style);
     const int64_t R1 = P.R(1), R2 = P.R(2);

@@ -103,6 +103,7 @@ struct kk_ctx {
     bool decoder_ready = false, generator_ready = false;
     std::string missing;
     bool prosody_ready = false;  // the prosody predictor's F0 / N chain
+    bool prosody_tc = false;     // its convolutions all F16: the tensor-core path
     std::string missing_prosody;
     kk::DevBuf convt_phase[2];
     bool convt_f16[2] = {false, false};
