@@ -34,9 +34,9 @@ POOL = 256
 BATCH = 64
 FLOP_PER_AUDIO_S = None  # filled from the model dimensions below
 # DRAM bytes of all tensor-core conv launches per audio second, from one ncu
-# capture of the batch-8 step (dram__bytes_read.sum + dram__bytes_write.sum;
-# profiles/conv_dram_batch8.md); traffic grows with the rows processed.
-CONV_DRAM_BYTES_PER_AUDIO_S = 1.436e8
+# capture of the batch-8 step (dram__bytes_read.sum + dram__bytes_write.sum of
+# one forward); traffic grows with the rows processed.
+CONV_DRAM_BYTES_PER_AUDIO_S = 1.483e8
 
 
 def algorithmic_flop_per_asr_frame() -> float:
