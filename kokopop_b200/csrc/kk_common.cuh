@@ -152,6 +152,15 @@ __device__ __forceinline__ p2_t p2_fma(p2_t a, p2_t b, p2_t c) {
     return d;
 }
 
+// Split F32 operands for the half tensor cores: v = hi + lo with hi = half(v)
+// and lo = half(v - hi) (the difference is exact in F32). A product of two
+// splits summed as hi*hi' + hi*lo' + lo*hi' carries about 22 significant
+// bits; the omitted lo*lo' is below 2^-22 of |v v'| (less where lo falls in
+// the half subnormal range, below 2^-14, where its absolute error is 2^-25).
+__device__ __forceinline__ __half split_lo(float v, __half hi) {
+    return __float2half_rn(__fsub_rn(v, __half2float(hi)));
+}
+
 template <typename T>
 __device__ __forceinline__ T warp_sum(T v) {
 #pragma unroll

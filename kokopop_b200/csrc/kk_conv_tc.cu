@@ -226,6 +226,7 @@ struct TcParams {
     int64_t m_tiles;  // position tiles of 256
     const __half *a;  // half operand, row 0 of chunk 0
     int64_t R_a;      // chunk stride (rows)
+    int a_wrap;       // > 0: K block b >= a_wrap reads operand block b - a_wrap
     const __half *w;  // packed [K][IC_blocks][n_tiles][8][128][8]
     float *out;
     int64_t R_out;
@@ -321,9 +322,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_conv_tc(const __grid_constant
                     if (!ok) break;
                     mbar_expect_tx(bA_full + 8 * sa, TC_A_BYTES);
                     const uint32_t dst = smem_u32(sA + sa * TC_A_BYTES);
+                    const int bo = (P.a_wrap > 0 && b >= P.a_wrap) ? b - P.a_wrap : b;
 #pragma unroll
                     for (int c = 0; c < 8; ++c) {
-                        const __half *src = P.a + ((int64_t)(8 * b + c) * P.R_a + row0) * 8;
+                        const __half *src = P.a + ((int64_t)(8 * bo + c) * P.R_a + row0) * 8;
                         bulk_load(dst + (uint32_t)c * lbo_a, src, lbo_a, bA_full + 8 * sa);
                     }
                     for (int k = 0; k < P.K; ++k, ++ib) {
@@ -647,9 +649,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     if (!ok) break;
                     mbar_expect_tx(bA_full + 8 * sa, TC_A_BYTES);
                     const uint32_t dst = smem_u32(sA + sa * TC_A_BYTES);
+                    const int bo = (P.a_wrap > 0 && b >= P.a_wrap) ? b - P.a_wrap : b;
 #pragma unroll
                     for (int c = 0; c < 8; ++c) {
-                        const __half *src = P.a + ((int64_t)(8 * b + c) * P.R_a + row0) * 8;
+                        const __half *src = P.a + ((int64_t)(8 * bo + c) * P.R_a + row0) * 8;
                         bulk_load(dst + (uint32_t)c * lbo_a, src, lbo_a, bA_full + 8 * sa);
                     }
                     for (int k = 0; k < P.K; ++k, ++iw) {
@@ -1503,7 +1506,7 @@ bool conv_tc_fusable(const ConvTcArgs &a) {
            a.scale2 == 1.0f && a.OC >= 64 && a.OC <= a.n_tiles * TC_BN && a.n_pos == a.R_out &&
            a.R_out % 128 == 0 && (!a.resid || a.R_resid == a.R_out) && a.IC_pad >= 64 && a.IC_pad % 64 == 0 &&
            a.K >= 1 && a.d >= 1 && a.p >= 0 && (a.K - 1) * a.d + 3 <= TC_SLAB - TC_BM && a.sb.n >= 1 && a.sm >= 4 &&
-           a.sextra >= 0;
+           a.sextra >= 0 && a.a_wrap == 0;
 }
 
 // k_conv_tcf launch: the operand formed from x inside the conv.
@@ -1569,7 +1572,8 @@ cudaError_t conv_tc(const ConvTcArgs &a, cudaStream_t st) {
     if (a.x) return conv_tc_fused(a, st);
     const int halo = (a.K - 1) * a.d;
     if (a.K < 1 || a.d < 1 || a.p < 0 || halo > TC_SLAB - TC_BM || a.p > kHalfLo || a.IC_pad % 64 != 0 ||
-        a.OC > a.n_tiles * TC_BN || a.n_pos < 1 || a.R_in < half_stride(0))
+        a.OC > a.n_tiles * TC_BN || a.n_pos < 1 || a.R_in < half_stride(0) || a.a_wrap < 0 ||
+        a.a_wrap >= a.IC_pad / 64)
         return cudaErrorInvalidValue;
     TcParams P;
     P.IC_blocks = a.IC_pad / 64;
@@ -1590,6 +1594,7 @@ cudaError_t conv_tc(const ConvTcArgs &a, cudaStream_t st) {
     if (a.n_pos > rows || (P.m_tiles - 1) * TC_BM - a.p + TC_SLAB > rows + kHalfHi) return cudaErrorInvalidValue;
     P.a = a.in;
     P.R_a = a.R_in;
+    P.a_wrap = a.a_wrap;
     P.w = a.w;
     P.out = a.out;
     P.R_out = a.R_out;

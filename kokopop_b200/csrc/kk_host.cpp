@@ -18,6 +18,7 @@
 #include <cstdlib>
 #include <cstdio>
 #include <cstring>
+#include <functional>
 #include <memory>
 #include <stdexcept>
 #include <string>
@@ -246,6 +247,25 @@ static void pack_tc(PackedW &pw, int OC, int IC, int K, Get get) {
     check_cuda(cudaMemcpy(pw.buf.p, h.data(), h.size() * sizeof(__half), cudaMemcpyHostToDevice), "upload packed");
 }
 
+// Split-F32 packing: the F32 weight as [W_hi | W_hi | W_lo] over 3 blocks of
+// IC rounded to 64 virtual channels (hi = half(w), lo = half(w - hi)),
+// against the operand [x_hi | x_lo] whose hi blocks the kernel reads again
+// for the third (a_wrap), so that one GEMM with F32 accumulation sums
+// W_hi x_hi + W_hi x_lo + W_lo x_hi.
+template <typename Get>
+static void pack_tc_split(PackedW &pw, int OC, int IC, int K, Get get) {
+    const int ICp = (IC + 63) / 64 * 64;
+    pack_tc(pw, OC, 3 * ICp, K, [&](int oc, int v, int k) {
+        const int part = v / ICp, ic = v % ICp;
+        if (ic >= IC) return 0.f;
+        const float w = get(oc, ic, k);
+        const float hi = __half2float(__float2half_rn(w));
+        return part < 2 ? hi : __half2float(__float2half_rn(w - hi));
+    });
+    pw.IC = IC;
+    pw.a_wrap = 2 * ICp / 64;
+}
+
 // The convolutions that run on the tensor cores, with their tap counts.
 static std::vector<std::pair<std::string, int>> tc_convs() {
     std::vector<std::pair<std::string, int>> v;
@@ -317,12 +337,25 @@ void kk_ctx::derive() {
         kv.second.bih_buf.release();
     }
     lstm.clear();
-    tc_mode = ok && convt_f16[0] && convt_f16[1];
-    for (const auto &cv : tc_convs()) {
-        const DevTensor *t = Wopt(cv.first);
-        if (t && !t->f16) tc_mode = false;
-        if (!t && cv.first.find("conv1x1") == std::string::npos) tc_mode = false;
+    bool all16 = ok && convt_f16[0] && convt_f16[1], all32 = ok && !convt_f16[0] && !convt_f16[1];
+    {
+        std::vector<std::pair<std::string, int>> convs = tc_convs();
+        convs.push_back({"kokopop.decoder.generator.noise_convs.0.weight", 12});
+        convs.push_back({"kokopop.decoder.generator.noise_convs.1.weight", 1});
+        for (const auto &cv : convs) {
+            const DevTensor *t = Wopt(cv.first);
+            if (t) {
+                all16 = all16 && t->f16;
+                all32 = all32 && !t->f16;
+            } else if (cv.first.find("conv1x1") == std::string::npos) {
+                all16 = all32 = false;
+            }
+        }
+        const char *f = std::getenv("KOKOPOP_B200_F32_SPLIT");
+        if (f && f[0] == '0') all32 = false;
     }
+    tc_mode = all16 || all32;
+    split_mode = all32;
     {
         const char *f = std::getenv("KOKOPOP_B200_FUSED_OPERAND");
         fuse_operand = f && f[0] == '1';
@@ -334,7 +367,7 @@ void kk_ctx::derive() {
         const DevTensor *t = Wopt(cv.first);
         if (t ? !t->f16 : cv.first.find("conv1x1") == std::string::npos) prosody_tc = false;
     }
-    if (prosody_tc && !tc_mode) {
+    if (prosody_tc && (!tc_mode || split_mode)) {
         check_cuda(conv_tc_init(), "tensor-core conv init");
         std::vector<float> h;
         for (const auto &cv : prosody_convs()) {
@@ -351,11 +384,18 @@ void kk_ctx::derive() {
     check_cuda(cudaMemset(d_err.p, 0, sizeof(int)), "clear error");
     if (tc_mode) {
         check_cuda(conv_tc_init(), "tensor-core conv init");
+        // F16 weights pack as they are; F32 ones split (split_mode)
+        auto pack = [&](PackedW &pw, int OC, int IC, int K, const std::function<float(int, int, int)> &get) {
+            if (split_mode)
+                pack_tc_split(pw, OC, IC, K, get);
+            else
+                pack_tc(pw, OC, IC, K, get);
+        };
         std::vector<float> h;
         std::vector<std::pair<std::string, int>> convs = tc_convs();
         for (const auto &cv : prosody_convs()) {
             const DevTensor *t = Wopt(cv.first);
-            if (t && t->f16) convs.push_back(cv);
+            if (t && t->f16 && !split_mode) convs.push_back(cv);
         }
         for (const auto &cv : convs) {
             const DevTensor *t = Wopt(cv.first);
@@ -363,8 +403,8 @@ void kk_ctx::derive() {
             const int K = cv.second, OC = (int)t->ne[1], IC = (int)(t->ne[0] / K);
             h.resize((size_t)t->n);
             check_cuda(cudaMemcpy(h.data(), t->d, h.size() * 4, cudaMemcpyDeviceToHost), "read conv weight");
-            pack_tc(packed[cv.first], OC, IC, K,
-                    [&](int oc, int ic, int k) { return h[((size_t)oc * IC + ic) * K + k]; });
+            pack(packed[cv.first], OC, IC, K,
+                 [&](int oc, int ic, int k) { return h[((size_t)oc * IC + ic) * K + k]; });
         }
         // noise_convs.1: 1x1 over the 22 har channels
         {
@@ -372,7 +412,7 @@ void kk_ctx::derive() {
             const int OC = (int)t.ne[1], IC = (int)t.ne[0];
             h.resize((size_t)t.n);
             check_cuda(cudaMemcpy(h.data(), t.d, h.size() * 4, cudaMemcpyDeviceToHost), "read noise conv");
-            pack_tc(packed["noise_convs.1"], OC, IC, 1, [&](int oc, int ic, int) { return h[(size_t)oc * IC + ic]; });
+            pack(packed["noise_convs.1"], OC, IC, 1, [&](int oc, int ic, int) { return h[(size_t)oc * IC + ic]; });
         }
         // noise_convs.0 (k=12, stride 6, pad 3) as 2 taps over the
         // space-to-depth operand: channel r*22+ic, tap j <- W[oc][ic][6j + r]
@@ -382,7 +422,7 @@ void kk_ctx::derive() {
             if (IC * K != (int)t.ne[0] || IC != 22) throw KKError(KK_ERROR_MODEL, "noise_convs.0 shape mismatch");
             h.resize((size_t)t.n);
             check_cuda(cudaMemcpy(h.data(), t.d, h.size() * 4, cudaMemcpyDeviceToHost), "read noise conv");
-            pack_tc(packed["noise_convs.0.s2d"], OC, 6 * IC, 2, [&](int oc, int c6, int j) {
+            pack(packed["noise_convs.0.s2d"], OC, 6 * IC, 2, [&](int oc, int c6, int j) {
                 const int r = c6 / IC, ic = c6 % IC;
                 return h[((size_t)oc * IC + ic) * K + 6 * j + r];
             });
@@ -395,12 +435,12 @@ void kk_ctx::derive() {
                 // all phases as one convolution, phase-major output channels
                 // n = r * OC + oc, so the CTAs writing the interleaved rows of
                 // one position tile run together
-                pack_tc(packed["ups." + std::to_string(s) + ".phases"], S * OC, IC, 2,
-                        [&](int n, int ic, int k) { return ph[((size_t)n * IC + ic) * 2 + k]; });
+                pack(packed["ups." + std::to_string(s) + ".phases"], S * OC, IC, 2,
+                     [&](int n, int ic, int k) { return ph[((size_t)n * IC + ic) * 2 + k]; });
             } else {
                 for (int r = 0; r < S; ++r)
-                    pack_tc(packed["ups." + std::to_string(s) + ".phase." + std::to_string(r)], OC, IC, 2,
-                            [&](int oc, int ic, int k) { return ph[(((size_t)r * OC + oc) * IC + ic) * 2 + k]; });
+                    pack(packed["ups." + std::to_string(s) + ".phase." + std::to_string(r)], OC, IC, 2,
+                         [&](int oc, int ic, int k) { return ph[(((size_t)r * OC + oc) * IC + ic) * 2 + k]; });
             }
         }
     }
@@ -589,6 +629,9 @@ struct Op {
     __half *h = nullptr;
     int64_t R = 0;
     int64_t Ry = 0;
+    bool split = false;  // half operand of split F32: lo chunks after the hi ones
+    // element offset of the lo half of a C-channel split operand (0: none)
+    int64_t lo(int C) const { return split ? (int64_t)((C + 63) / 64 * 64) * Ry : 0; }
 };
 
 struct Runner {
@@ -602,10 +645,13 @@ struct Runner {
     float2 *ms3 = nullptr;  // statistics computed just before a fused-operand conv
     float *gbase = nullptr, *bbase = nullptr;
     const bool tc;
+    const bool split;  // F32 weights split over the half tensor cores
 
-    // tc_path: the tensor-core path (default: the context's tc_mode)
+    // tc_path: the tensor-core path on F16 weights (default: the context's
+    // mode, split F32 included)
     Runner(kk_ctx &ctx, const Plan &plan, cudaStream_t s, int tc_path = -1)
-        : c(ctx), P(plan), st(s), tc(tc_path < 0 ? ctx.tc_mode : tc_path != 0) {}
+        : c(ctx), P(plan), st(s), tc(tc_path < 0 ? ctx.tc_mode : tc_path != 0),
+          split(tc_path < 0 && ctx.tc_mode && ctx.split_mode) {}
 
     int64_t R(int m) const { return P.R(m); }
 
@@ -668,17 +714,19 @@ struct Runner {
     int64_t sum_len(int m, int extra) const { return (int64_t)m * P.total + (int64_t)extra * P.n; }
 
     // The operand buffer of a level (multiplier m) with room for C channels.
-    Op op(const char *name, int m, int C) { return op(name, m, C, tc); }
+    Op op(const char *name, int m, int C) { return op(name, m, C, tc, split); }
 
-    // half == true: the tensor-core operand whatever the context's mode
-    Op op(const char *name, int m, int C, bool half) {
+    // half == true: the tensor-core operand whatever the context's mode;
+    // split: with room for the lo halves of split F32
+    Op op(const char *name, int m, int C, bool half, bool sp = false) {
         Op o;
         o.R = R(m);
         o.Ry = o.R;
         if (half) {
-            const int cpad = (C + 63) / 64 * 64;
+            const int cpad = (C + 63) / 64 * 64 * (sp ? 2 : 1);
             o.Ry = half_stride(o.R);
             o.h = (__half *)c.buf(name, ((size_t)cpad * o.Ry + 1) / 2) + kHalfLo * 8;
+            o.split = sp;
         } else {
             o.f = c.buf(name, (size_t)C * o.R);
         }
@@ -687,7 +735,8 @@ struct Runner {
 
     void zero(const Op &o, int C) {
         if (o.h)
-            check_cuda(cudaMemsetAsync(o.h - kHalfLo * 8, 0, (size_t)((C + 63) / 64 * 64) * o.Ry * sizeof(__half), st),
+            check_cuda(cudaMemsetAsync(o.h - kHalfLo * 8, 0,
+                                       (size_t)((C + 63) / 64 * 64) * (o.split ? 2 : 1) * o.Ry * sizeof(__half), st),
                        "memset");
         else
             check_cuda(cudaMemsetAsync(o.f, 0, (size_t)C * o.R * sizeof(float), st), "memset");
@@ -758,11 +807,14 @@ struct Runner {
     // Tensor-core convolution on a half chunk-major operand.
     void conv_h(const PackedW &pw, const Op &in, int K, int p, int d, float *out, int64_t R_out, int64_t n_pos,
                 const Epi &e, int phase_oc = 0) {
+        if (in.split != (pw.a_wrap > 0))
+            throw KKError(KK_ERROR_INFERENCE, "operand and weight packing disagree on the F32 split");
         ConvTcArgs a{};
         a.phase_oc = phase_oc;
         a.in = in.h;
         a.R_in = in.Ry;
         a.IC_pad = pw.IC_pad;
+        a.a_wrap = pw.a_wrap;
         a.w = (const __half *)pw.buf.p;
         a.n_tiles = pw.n_tiles;
         a.OC = pw.OC;
@@ -846,6 +898,7 @@ struct Runner {
         a.slope = slope;
         a.alpha = alpha.empty() ? nullptr : c.W(alpha).d;
         a.round16 = 0;
+        a.lo_off = y.lo(C);
         if (y.h)
             prologue_h(x, y.h, Rm, y.Ry, C, m, extra, B, (int)(sum_len(m, extra) / P.n), a, st);
         else
@@ -863,6 +916,7 @@ struct Runner {
         a.x2 = x2;
         a.x3 = x3;
         a.sum_scale = sum_scale;
+        a.lo_off = y.lo(C);
         if (y.h)
             prologue_h(x, y.h, Rm, y.Ry, C, m, extra, B, (int)(sum_len(m, extra) / P.n), a, st);
         else
@@ -917,7 +971,7 @@ struct Runner {
             pf32.R = R1;
             adain_act(pf + ".norm1", x, pf32, R1, Cin, 1, 0, ACT_LEAKY, 0.2f, "");
             if (tc)
-                pool_up_h(pf32.f, opL.h, R1, opL.Ry, Cin, pw.d, pb.d, B, P.maxT, st);
+                pool_up_h(pf32.f, opL.h, R1, opL.Ry, Cin, pw.d, pb.d, B, P.maxT, opL.lo(Cin), st);
             else
                 pool_up(pf32.f, opL.f, R1, R2, Cin, pw.d, pb.d, B, P.maxT, 0, st);
             ++c.n_launches;
@@ -974,7 +1028,7 @@ struct Runner {
                           const Op &o, int C, int m, int extra, const std::string &wname, const std::string &bname,
                           int K, int p, int d, float *out, Epi e) {
         const int64_t Rm = R(m);
-        if (tc && c.fuse_operand) {
+        if (tc && !split && c.fuse_operand) {
             const AdainSite &s = site(adain);
             if (s.C != C) throw KKError(KK_ERROR_MODEL, "AdaIN channel mismatch: " + adain);
             auto it = c.packed.find(wname);
@@ -1110,7 +1164,7 @@ struct Runner {
                 if (tc && s == 0) {
                     // stride 6 as 2 taps over the space-to-depth operand
                     Op sd = op("s2d", m, 192);
-                    har_s2d(har, R_har, sd.h, Rm, sd.Ry, st);
+                    har_s2d(har, R_har, sd.h, Rm, sd.Ry, sd.lo(192), st);
                     ++c.n_launches;
                     e.valid = sum_len(m, extra[s]);
                     conv_h(c.packed.at("noise_convs.0.s2d"), sd, 2, 0, 1, xs, Rm, Rm, e);
@@ -1166,6 +1220,7 @@ struct Runner {
                 ConvTRow0Args a{};
                 a.in = op_prev.f;
                 a.in_h = op_prev.h;
+                a.lo_off = op_prev.lo(C);
                 a.R_in = op_prev.h ? op_prev.Ry : Rp;
                 a.IC = C;
                 a.m_in = m_prev;

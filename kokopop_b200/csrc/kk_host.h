@@ -44,6 +44,10 @@ struct DevBuf {
 struct PackedW {
     DevBuf buf;
     int IC = 0, IC_pad = 0, OC = 0, K = 0, n_tiles = 0;
+    // > 0: split-F32 packing over 3 * (IC rounded to 64) virtual channels
+    // [W_hi | W_hi | W_lo]; K blocks from a_wrap on read the operand's hi
+    // blocks again (ConvTcArgs::a_wrap)
+    int a_wrap = 0;
 };
 
 // One bidirectional LSTM layer (prefix.weight_ih_l0[_reverse], ...), derived
@@ -107,8 +111,14 @@ struct kk_ctx {
     std::string missing_prosody;
     kk::DevBuf convt_phase[2];
     bool convt_f16[2] = {false, false};
-    // tensor-core path: every convolution weight is F16
+    // tensor-core path: every convolution weight is F16, or every one is F32
+    // (split_mode) unless KOKOPOP_B200_F32_SPLIT=0 at upload
     bool tc_mode = false;
+    // F32 weights on the half tensor cores: weights and operands split as
+    // hi + lo halves, one GEMM over 3x the input channels (W_hi x_hi +
+    // W_hi x_lo + W_lo x_hi, F32 accumulation); mixed F16 / F32 weight sets
+    // keep the CUDA-core path
+    bool split_mode = false;
     // KOKOPOP_B200_FUSED_OPERAND=1 at upload: the residual-block convs form
     // their AdaIN + Snake operand inside the conv (k_conv_tcf, bit-identical
     // to the separate operand pass, slower than it on B200 so far)

@@ -266,7 +266,9 @@ __global__ void k_convt_row0(ConvTRow0Args a, Batch b) {
     for (int ic = 0; ic < a.IC; ++ic) {
         float x;
         if (a.in_h) {
-            x = __half2float(a.in_h[(((int64_t)(ic >> 3)) * a.R_in + in_row) * 8 + (ic & 7)]);
+            const int64_t o = (((int64_t)(ic >> 3)) * a.R_in + in_row) * 8 + (ic & 7);
+            x = __half2float(a.in_h[o]);
+            if (a.lo_off > 0) x = __fadd_rn(x, __half2float(a.in_h[o + a.lo_off]));
         } else {
             x = a.in[(int64_t)ic * a.R_in + in_row];
             if (a.round16) x = round_f16(x);
@@ -292,8 +294,8 @@ void convt_row0(const ConvTRow0Args &a, const Batch &b, cudaStream_t st) {
 // fall past the utterance are written as zero (they are gap rows). The
 // normalisation and the activation are template parameters so that each
 // variant keeps only the registers it needs (3 blocks per SM).
-template <bool NORM, int ACT>
-__global__ void __launch_bounds__(256, 3) k_prologue_h(const float *__restrict__ x, __half *__restrict__ y,
+template <bool NORM, int ACT, bool SPLIT>
+__global__ void __launch_bounds__(256, SPLIT ? 2 : 3) k_prologue_h(const float *__restrict__ x, __half *__restrict__ y,
                                                        int64_t R, int64_t Ry, int C, int m, int extra, Batch b,
                                                        PrologueArgs a) {
     const int u = blockIdx.z, ch = blockIdx.y;
@@ -386,14 +388,51 @@ __global__ void __launch_bounds__(256, 3) k_prologue_h(const float *__restrict__
                     }
             }
         }
-        __align__(16) __half h[4][8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) h[i][e] = __float2half_rn((e >= nc || t + i >= len) ? 0.f : v[i][e]);
         uint4 *dst = reinterpret_cast<uint4 *>(y + ((int64_t)ch * Ry + row) * 8);
+        if (SPLIT) {
+            // hi and lo halves of each row: [hi chunks | lo chunks]
+            uint4 *dlo = reinterpret_cast<uint4 *>(y + ((int64_t)ch * Ry + row) * 8 + a.lo_off);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) dst[i] = *reinterpret_cast<const uint4 *>(h[i]);
+            for (int i = 0; i < 4; ++i) {
+                __align__(16) __half hh[8], ll[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const float w = (e >= nc || t + i >= len) ? 0.f : v[i][e];
+                    hh[e] = __float2half_rn(w);
+                    ll[e] = split_lo(w, hh[e]);
+                }
+                dst[i] = *reinterpret_cast<const uint4 *>(hh);
+                dlo[i] = *reinterpret_cast<const uint4 *>(ll);
+            }
+        } else {
+            __align__(16) __half h[4][8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) h[i][e] = __float2half_rn((e >= nc || t + i >= len) ? 0.f : v[i][e]);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) dst[i] = *reinterpret_cast<const uint4 *>(h[i]);
+        }
+    }
+}
+
+template <bool SPLIT>
+static void prologue_h_launch(dim3 grid, const float *x, __half *y, int64_t R, int64_t Ry, int C, int m, int extra,
+                              const Batch &b, const PrologueArgs &a, cudaStream_t st) {
+    if (a.norm) {
+        if (a.act == ACT_SNAKE)
+            k_prologue_h<true, ACT_SNAKE, SPLIT><<<grid, 256, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
+        else if (a.act == ACT_LEAKY)
+            k_prologue_h<true, ACT_LEAKY, SPLIT><<<grid, 256, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
+        else
+            k_prologue_h<true, ACT_NONE, SPLIT><<<grid, 256, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
+    } else {
+        if (a.act == ACT_SNAKE)
+            k_prologue_h<false, ACT_SNAKE, SPLIT><<<grid, 256, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
+        else if (a.act == ACT_LEAKY)
+            k_prologue_h<false, ACT_LEAKY, SPLIT><<<grid, 256, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
+        else
+            k_prologue_h<false, ACT_NONE, SPLIT><<<grid, 256, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
     }
 }
 
@@ -404,33 +443,23 @@ void prologue_h(const float *x, __half *y, int64_t R, int64_t Ry, int C, int m, 
     int bx = (mean_len + 3 * 1024 - 1) / (3 * 1024);
     if (bx > 64) bx = 64;
     const dim3 grid(bx, (C + 7) / 8, b.n);
-    if (a.norm) {
-        if (a.act == ACT_SNAKE)
-            k_prologue_h<true, ACT_SNAKE><<<grid, 256, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
-        else if (a.act == ACT_LEAKY)
-            k_prologue_h<true, ACT_LEAKY><<<grid, 256, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
-        else
-            k_prologue_h<true, ACT_NONE><<<grid, 256, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
-    } else {
-        if (a.act == ACT_SNAKE)
-            k_prologue_h<false, ACT_SNAKE><<<grid, 256, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
-        else if (a.act == ACT_LEAKY)
-            k_prologue_h<false, ACT_LEAKY><<<grid, 256, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
-        else
-            k_prologue_h<false, ACT_NONE><<<grid, 256, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
-    }
+    if (a.lo_off > 0)
+        prologue_h_launch<true>(grid, x, y, R, Ry, C, m, extra, b, a, st);
+    else
+        prologue_h_launch<false>(grid, x, y, R, Ry, C, m, extra, b, a, st);
 }
 
 // Depthwise x2 pool (see k_pool_up) written as the half chunk-major operand
 // of the following F16 convolution (its input is rounded to half there).
 __global__ void k_pool_up_h(const float *__restrict__ x, __half *__restrict__ y, int64_t R_in, int64_t Ry_out,
-                            int C, const float *__restrict__ w, const float *__restrict__ bias, Batch b) {
+                            int C, const float *__restrict__ w, const float *__restrict__ bias, Batch b,
+                            int64_t lo_off) {
     const int u = blockIdx.z, ch = blockIdx.y;
     const int64_t L = b.T[u];
     for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < 2 * L;
          t += (int64_t)gridDim.x * blockDim.x) {
         const int64_t j = t + 1;
-        __align__(16) __half h[8];
+        __align__(16) __half h[8], l[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
             const int c = ch * 8 + e;
@@ -448,17 +477,19 @@ __global__ void k_pool_up_h(const float *__restrict__ x, __half *__restrict__ y,
                 v = __fadd_rn(acc, bias[c]);
             }
             h[e] = __float2half_rn(v);
+            l[e] = split_lo(v, h[e]);
         }
-        *reinterpret_cast<uint4 *>(y + ((int64_t)ch * Ry_out + 2 * b.offT[u] + t) * 8) =
-            *reinterpret_cast<const uint4 *>(h);
+        __half *dst = y + ((int64_t)ch * Ry_out + 2 * b.offT[u] + t) * 8;
+        *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(h);
+        if (lo_off > 0) *reinterpret_cast<uint4 *>(dst + lo_off) = *reinterpret_cast<const uint4 *>(l);
     }
 }
 
 void pool_up_h(const float *x, __half *y, int64_t R_in, int64_t Ry_out, int C, const float *w, const float *bias,
-               const Batch &b, int max_T, cudaStream_t st) {
+               const Batch &b, int max_T, int64_t lo_off, cudaStream_t st) {
     int bx = (2 * max_T + 255) / 256;
     if (bx > 16) bx = 16;
-    k_pool_up_h<<<dim3(bx, (C + 7) / 8, b.n), 256, 0, st>>>(x, y, R_in, Ry_out, C, w, bias, b);
+    k_pool_up_h<<<dim3(bx, (C + 7) / 8, b.n), 256, 0, st>>>(x, y, R_in, Ry_out, C, w, bias, b, lo_off);
 }
 
 // Space-to-depth operand of the stride-6 noise convolution: every packed row
@@ -467,10 +498,10 @@ void pool_up_h(const float *x, __half *y, int64_t R_in, int64_t Ry_out, int C, c
 // convolution becomes a stride-1 convolution with 2 taps. All rows are
 // written: outside an utterance they read the zero gaps of har.
 __global__ void k_har_s2d(const float *__restrict__ har, int64_t R_har, __half *__restrict__ y, int64_t R,
-                          int64_t Ry) {
+                          int64_t Ry, int64_t lo_off) {
     const int ch = blockIdx.y;  // output chunk of 8 (24 chunks = 192 padded channels)
     for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < R; t += (int64_t)gridDim.x * blockDim.x) {
-        __align__(16) __half h[8];
+        __align__(16) __half h[8], l[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
             const int c6 = ch * 8 + e;
@@ -481,15 +512,18 @@ __global__ void k_har_s2d(const float *__restrict__ har, int64_t R_har, __half *
                 if (row >= 0 && row < R_har) v = har[(int64_t)ic * R_har + row];
             }
             h[e] = __float2half_rn(v);
+            l[e] = split_lo(v, h[e]);
         }
-        *reinterpret_cast<uint4 *>(y + ((int64_t)ch * Ry + t) * 8) = *reinterpret_cast<const uint4 *>(h);
+        __half *dst = y + ((int64_t)ch * Ry + t) * 8;
+        *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(h);
+        if (lo_off > 0) *reinterpret_cast<uint4 *>(dst + lo_off) = *reinterpret_cast<const uint4 *>(l);
     }
 }
 
-void har_s2d(const float *har, int64_t R_har, __half *y, int64_t R, int64_t Ry, cudaStream_t st) {
+void har_s2d(const float *har, int64_t R_har, __half *y, int64_t R, int64_t Ry, int64_t lo_off, cudaStream_t st) {
     int bx = (int)((R + 255) / 256);
     if (bx > 2048) bx = 2048;
-    k_har_s2d<<<dim3(bx, 24), 256, 0, st>>>(har, R_har, y, R, Ry);
+    k_har_s2d<<<dim3(bx, 24), 256, 0, st>>>(har, R_har, y, R, Ry, lo_off);
 }
 
 // ---------------------------------------------------------------------------

@@ -30,6 +30,9 @@ struct PrologueArgs {
     // the average of the three residual-block branches (graph_ops.cpp:1300-1320)
     const float *x2, *x3;
     float sum_scale;
+    // > 0 (half operands): also write lo = half(v - half(v)) lo_off halves
+    // after each hi value, the split-F32 operand [hi chunks | lo chunks]
+    int64_t lo_off;
 };
 
 // Dense convolution over a packed [IC, R_in] operand (zero gaps):
@@ -64,6 +67,7 @@ struct ConvArgs {
 struct ConvTRow0Args {
     const float *in;      // F32 [C][R] operand, or
     const __half *in_h;   // half chunk-major operand (when non-null)
+    int64_t lo_off;       // > 0: in_h is split F32, value = hi + the half lo_off further
     int64_t R_in;         // row stride of `in`, or the chunk stride of `in_h`
     int IC, m_in;
     const float *w;  // ggml [K, OC, IC]
@@ -147,6 +151,9 @@ struct ConvTcArgs {
     const __half *in;
     int64_t R_in;
     int IC_pad;
+    // > 0: the K blocks of 64 channels past a_wrap read operand block
+    // b - a_wrap again (the split-F32 GEMM's third term reuses the hi part)
+    int a_wrap;
     const __half *w;
     int n_tiles;
     int OC, K, p, d;
@@ -198,11 +205,12 @@ void prologue_h(const float *x, __half *y, int64_t R, int64_t Ry, int C, int m, 
 // har_s2d: space-to-depth half operand [192/8][R][8] (chunk stride Ry) of the
 // stride-6 noise convolution (132 real channels), all R rows of the stage-0
 // level.
-void har_s2d(const float *har, int64_t R_har, __half *y, int64_t R, int64_t Ry, cudaStream_t st);
+void har_s2d(const float *har, int64_t R_har, __half *y, int64_t R, int64_t Ry, int64_t lo_off, cudaStream_t st);
 // pool_up_h: the depthwise x2 pool written as a half operand of chunk stride
-// Ry_out.
+// Ry_out. lo_off > 0 on har_s2d and pool_up_h: the split-F32 operand, as
+// PrologueArgs::lo_off.
 void pool_up_h(const float *x, __half *y, int64_t R_in, int64_t Ry_out, int C, const float *w, const float *bias,
-               const Batch &b, int max_T, cudaStream_t st);
+               const Batch &b, int max_T, int64_t lo_off, cudaStream_t st);
 
 // kk_lstm.cu: bidirectional LSTM stack and the duration alignment.
 // Sequences are packed time-major: row = t * B + b of a [C][R] activation.

@@ -167,3 +167,31 @@ def test_missing_weights_is_model_error():
         assert e.value.code == kb.KK_ERROR_MODEL
     finally:
         c.close()
+
+
+def test_f32_weights_split_and_cuda_core_paths(ctx, w32, o32, monkeypatch):
+    """F32 weights run on the half tensor cores as split GEMMs (hi + lo
+    halves, the default) or on the CUDA cores (KOKOPOP_B200_F32_SPLIT=0).
+    Both stay within the waveform tolerance of the oracle, the two launch
+    different kernel sequences, and the split path packs ragged batches
+    bit-exactly like single calls."""
+    rng = np.random.default_rng(12)
+    utts = [W.make_utterance(rng, t) for t in (33, 1, 70)]
+    want = [o32.decoder_forward(u.asr, u.f0, u.noise, u.style) for u in utts]
+    launches = {}
+    for flag in ("1", "0"):
+        monkeypatch.setenv("KOKOPOP_B200_F32_SPLIT", flag)
+        ctx.upload(w32)
+        ctx.profile_enable(True)
+        ctx.profile_read(reset=True)
+        out = ctx.decoder_forward(utts)
+        launches[flag] = ctx.profile_read(reset=True)["launches"]
+        ctx.profile_enable(False)
+        for g_, w_ in zip(out, want):
+            _check(g_, w_)
+        if flag == "1":
+            for u, b in zip(utts, out):
+                np.testing.assert_array_equal(ctx.decoder_forward([u])[0], b)
+    monkeypatch.delenv("KOKOPOP_B200_F32_SPLIT")
+    ctx.upload(w32)
+    assert launches["1"] != launches["0"]
