@@ -219,7 +219,7 @@ def bench_lstm(kb, W, device, runs):
         gemm_tf = prof["conv_flop"] / (prof["conv_ms"] / 1e3) / 1e12 if prof["conv_ms"] > 0 else None
         out["cases"].append({
             "batch": B, "steps": L, "weights": "f16" if f16 else "f32",
-            "wih_path": "tcgen05 f16" if f16 else "fp32 cuda cores",
+            "wih_path": "tcgen05 f16" if f16 else "tcgen05 split f32 (hi + lo halves, 3 products)",
             "ms_per_call": ms, "us_per_step": 1e3 * ms / (3 * L), "tokens_per_s": B * L / (ms / 1e3),
             "wih_gemm_tflops": gemm_tf, "wih_share": (prof["conv_ms"] / runs) / ms if ms > 0 else None,
         })

@@ -227,6 +227,7 @@ struct TcParams {
     const __half *a;  // half operand, row 0 of chunk 0
     int64_t R_a;      // chunk stride (rows)
     int a_wrap;       // > 0: K block b >= a_wrap reads operand block b - a_wrap
+    float acc_scale;  // the accumulator times this power of two first (1: none)
     const __half *w;  // packed [K][IC_blocks][n_tiles][8][128][8]
     float *out;
     int64_t R_out;
@@ -451,6 +452,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_conv_tc(const __grid_constant
                 for (int j = 0; j < 32; ++j) {
                     const float bj = __shfl_sync(0xffffffffu, b_lane, j);
                     float v = __uint_as_float(r[j]);
+                    if (P.acc_scale != 1.0f) v = __fmul_rn(v, P.acc_scale);
                     if (P.bias) v = __fadd_rn(v, bj);
                     if (has_res) v = __fadd_rn(res[j], v);
                     if (P.scale1 != 1.0f) v = __fmul_rn(v, P.scale1);
@@ -804,6 +806,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < 32; j += 2) {
                         float2 x = make_float2(__uint_as_float(r[j]), __uint_as_float(r[j + 1]));
+                        // a power of two: exact, contracted or not
+                        if (P.acc_scale != 1.0f) x = f2mul(x, make_float2(P.acc_scale, P.acc_scale));
                         if (P.bias) x = f2add(x, make_float2(bias, bias));
                         if (has_res) x = f2add(make_float2(res[j], res[j + 1]), x);
                         // scalar products: a packed product feeding a packed add may be contracted
@@ -838,6 +842,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                             float x = 0.f;
                             if (p0 + j < P.n_pos) {
                                 x = __uint_as_float(r[j]);
+                                if (P.acc_scale != 1.0f) x = __fmul_rn(x, P.acc_scale);
                                 if (P.bias) x = __fadd_rn(x, bias);
                                 if (has_res) x = __fadd_rn(rp[j], x);
                                 if (P.scale1 != 1.0f) x = __fmul_rn(x, P.scale1);
@@ -1506,7 +1511,7 @@ bool conv_tc_fusable(const ConvTcArgs &a) {
            a.scale2 == 1.0f && a.OC >= 64 && a.OC <= a.n_tiles * TC_BN && a.n_pos == a.R_out &&
            a.R_out % 128 == 0 && (!a.resid || a.R_resid == a.R_out) && a.IC_pad >= 64 && a.IC_pad % 64 == 0 &&
            a.K >= 1 && a.d >= 1 && a.p >= 0 && (a.K - 1) * a.d + 3 <= TC_SLAB - TC_BM && a.sb.n >= 1 && a.sm >= 4 &&
-           a.sextra >= 0 && a.a_wrap == 0;
+           a.sextra >= 0 && a.a_wrap == 0 && (a.acc_scale == 0.0f || a.acc_scale == 1.0f);
 }
 
 // k_conv_tcf launch: the operand formed from x inside the conv.
@@ -1595,6 +1600,7 @@ cudaError_t conv_tc(const ConvTcArgs &a, cudaStream_t st) {
     P.a = a.in;
     P.R_a = a.R_in;
     P.a_wrap = a.a_wrap;
+    P.acc_scale = a.acc_scale == 0.0f ? 1.0f : a.acc_scale;
     P.w = a.w;
     P.out = a.out;
     P.R_out = a.R_out;

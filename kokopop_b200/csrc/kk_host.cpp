@@ -14,6 +14,7 @@
 #include "kk_kernels.h"
 #include "kk_host.h"
 
+#include <algorithm>
 #include <cmath>
 #include <cstdlib>
 #include <cstdio>
@@ -247,23 +248,41 @@ static void pack_tc(PackedW &pw, int OC, int IC, int K, Get get) {
     check_cuda(cudaMemcpy(pw.buf.p, h.data(), h.size() * sizeof(__half), cudaMemcpyHostToDevice), "upload packed");
 }
 
-// Split-F32 packing: the F32 weight as [W_hi | W_hi | W_lo] over 3 blocks of
+// Split-F32 packing: the F32 weight as [W_lo | W_hi | W_hi] over 3 blocks of
 // IC rounded to 64 virtual channels (hi = half(w), lo = half(w - hi)),
 // against the operand [x_hi | x_lo] whose hi blocks the kernel reads again
 // for the third (a_wrap), so that one GEMM with F32 accumulation sums
-// W_hi x_hi + W_hi x_lo + W_lo x_hi.
+// W_lo x_hi + W_hi x_lo + W_hi x_hi. The two small correction terms come
+// first, into a small accumulator: the tensor cores' accumulation error then
+// stays near that of the W_hi x_hi GEMM alone.
+// The weights are scaled by 2^s, s the largest with max |w| 2^s <= 2^14,
+// before the split (a lo half then sits in the half subnormal range, with
+// its coarser absolute spacing, only for |w| below 2^-3 of the largest),
+// and the conv takes acc_scale = 2^-s back, exactly.
 template <typename Get>
 static void pack_tc_split(PackedW &pw, int OC, int IC, int K, Get get) {
     const int ICp = (IC + 63) / 64 * 64;
+    float amax = 0.f;
+    for (int k = 0; k < K; ++k)
+        for (int oc = 0; oc < OC; ++oc)
+            for (int ic = 0; ic < IC; ++ic) amax = std::fmax(amax, std::fabs(get(oc, ic, k)));
+    int s = 0;
+    if (amax > 0.f && std::isfinite(amax)) {
+        int e = 0;
+        std::frexp(amax, &e);  // amax < 2^e
+        s = std::min(std::max(14 - e, -100), 100);
+    }
+    const float up = std::ldexp(1.0f, s);
     pack_tc(pw, OC, 3 * ICp, K, [&](int oc, int v, int k) {
         const int part = v / ICp, ic = v % ICp;
         if (ic >= IC) return 0.f;
-        const float w = get(oc, ic, k);
+        const float w = get(oc, ic, k) * up;
         const float hi = __half2float(__float2half_rn(w));
-        return part < 2 ? hi : __half2float(__float2half_rn(w - hi));
+        return part > 0 ? hi : __half2float(__float2half_rn(w - hi));
     });
     pw.IC = IC;
     pw.a_wrap = 2 * ICp / 64;
+    pw.acc_scale = std::ldexp(1.0f, -s);
 }
 
 // The convolutions that run on the tensor cores, with their tap counts.
@@ -352,7 +371,8 @@ void kk_ctx::derive() {
             }
         }
         const char *f = std::getenv("KOKOPOP_B200_F32_SPLIT");
-        if (f && f[0] == '0') all32 = false;
+        f32_split = !(f && f[0] == '0');
+        all32 = all32 && f32_split;
     }
     tc_mode = all16 || all32;
     split_mode = all32;
@@ -601,11 +621,16 @@ const LstmLayer &kk_ctx::lstm_layer(const std::string &prefix) {
     L.bih.d = (float *)L.bih_buf.p;
     L.bih.ne[0] = 2 * H4;
     L.bih.n = 2 * H4;
-    if (L.f16) {
+    if (L.f16 || f32_split) {
+        // F16: the weights as they are; F32: split hi + lo (pack_tc_split)
         check_cuda(conv_tc_init(), "tensor-core conv init");
         std::vector<float> h(2 * nw);
         check_cuda(cudaMemcpy(h.data(), L.wih.p, h.size() * 4, cudaMemcpyDeviceToHost), "read W_ih");
-        pack_tc(L.wih_tc, (int)(2 * H4), (int)in, 1, [&](int oc, int ic, int) { return h[(size_t)oc * in + ic]; });
+        auto get = [&](int oc, int ic, int) { return h[(size_t)oc * in + ic]; };
+        if (L.f16)
+            pack_tc(L.wih_tc, (int)(2 * H4), (int)in, 1, get);
+        else
+            pack_tc_split(L.wih_tc, (int)(2 * H4), (int)in, 1, get);
     }
     L.whh[0] = hf.d;
     L.whh[1] = hb.d;
@@ -815,6 +840,7 @@ struct Runner {
         a.R_in = in.Ry;
         a.IC_pad = pw.IC_pad;
         a.a_wrap = pw.a_wrap;
+        a.acc_scale = pw.acc_scale;
         a.w = (const __half *)pw.buf.p;
         a.n_tiles = pw.n_tiles;
         a.OC = pw.OC;
@@ -1286,8 +1312,8 @@ struct Runner {
         Epi e;
         e.bias = &L.bih;
         e.valid = q.rows;
-        if (L.f16 && L.wih_tc.buf.p) {
-            Op xh = op("lstm_xh", 1, L.in_dim, true);
+        if (L.wih_tc.buf.p) {
+            Op xh = op("lstm_xh", 1, L.in_dim, true, L.wih_tc.a_wrap > 0);
             zero(xh, L.in_dim);
             act_only(X, xh, Rr, L.in_dim, 1, 0, ACT_NONE, 0.f);
             conv_h(L.wih_tc, xh, 1, 0, 1, pre, Rr, Rr, e);

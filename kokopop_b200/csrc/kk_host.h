@@ -45,9 +45,13 @@ struct PackedW {
     DevBuf buf;
     int IC = 0, IC_pad = 0, OC = 0, K = 0, n_tiles = 0;
     // > 0: split-F32 packing over 3 * (IC rounded to 64) virtual channels
-    // [W_hi | W_hi | W_lo]; K blocks from a_wrap on read the operand's hi
+    // [W_lo | W_hi | W_hi]; K blocks from a_wrap on read the operand's hi
     // blocks again (ConvTcArgs::a_wrap)
     int a_wrap = 0;
+    // split packing: the weights are packed times 2^s (the hi and lo halves
+    // of small weights stay in the normal half range); the conv multiplies
+    // its accumulator by acc_scale = 2^-s, exactly
+    float acc_scale = 1.f;
 };
 
 // One bidirectional LSTM layer (prefix.weight_ih_l0[_reverse], ...), derived
@@ -57,7 +61,7 @@ struct LstmLayer {
     int in_dim = 0, H = 0;
     bool f16 = false;   // W_ih stored as F16: ggml rounds the input to half
     DevBuf wih;         // F32 values [8H][in_dim]
-    PackedW wih_tc;     // tensor-core packing of wih (F16 weights)
+    PackedW wih_tc;     // tensor-core packing of wih (F16 weights, or split F32)
     DevBuf bih_buf;     // [8H]
     DevTensor bih;      // view of bih_buf
     const float *whh[2] = {nullptr, nullptr};  // rowwise [4H][H] (the uploaded tensors)
@@ -119,6 +123,9 @@ struct kk_ctx {
     // W_hi x_lo + W_lo x_hi, F32 accumulation); mixed F16 / F32 weight sets
     // keep the CUDA-core path
     bool split_mode = false;
+    // KOKOPOP_B200_F32_SPLIT is not 0: F32 weights may take the split path
+    // (the decoder when all its convolutions are F32, each F32 LSTM W_ih)
+    bool f32_split = true;
     // KOKOPOP_B200_FUSED_OPERAND=1 at upload: the residual-block convs form
     // their AdaIN + Snake operand inside the conv (k_conv_tcf, bit-identical
     // to the separate operand pass, slower than it on B200 so far)

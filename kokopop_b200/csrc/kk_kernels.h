@@ -154,6 +154,9 @@ struct ConvTcArgs {
     // > 0: the K blocks of 64 channels past a_wrap read operand block
     // b - a_wrap again (the split-F32 GEMM's third term reuses the hi part)
     int a_wrap;
+    // non-zero and not 1: the accumulator is multiplied by this power of two
+    // before the epilogue (split weights packed scaled by its inverse)
+    float acc_scale;
     const __half *w;
     int n_tiles;
     int OC, K, p, d;

@@ -108,6 +108,24 @@ def test_bilstm_f16_weights_tensor_cores_match_oracle(f16_setup):
     assert err < TOL_LAYER
 
 
+def test_bilstm_f32_cuda_core_projection_matches_oracle(monkeypatch):
+    """KOKOPOP_B200_F32_SPLIT=0: the F32 W_ih projection on the CUDA cores
+    instead of the split hi + lo tensor-core GEMM (the default above)."""
+    monkeypatch.setenv("KOKOPOP_B200_F32_SPLIT", "0")
+    wts = W.config1_weights(f16=False)
+    c = kb.Context(0)
+    try:
+        c.upload(wts)
+        xs = _seqs(np.random.default_rng(11), [17, 5, 40], 640)
+        got = c.bilstm(PFX, xs)
+    finally:
+        c.close()
+    m = O.OracleModel(wts)
+    err = _max_err(got, [m.bilstm(PFX, x) for x in xs])
+    print(f"bilstm f32 cuda-core projection: max abs err {err:.3g}")
+    assert err < TOL_LAYER
+
+
 @pytest.mark.parametrize("lens", [[33], [33, 12, 50]])
 def test_duration_encoder_matches_oracle(f32_setup, lens):
     c, m = f32_setup
