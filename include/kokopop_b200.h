@@ -155,6 +155,48 @@ int kk_prosody_f0n(kk_ctx *ctx, int32_t n_utts, const int32_t *n_frames, const f
 int kk_prosody_f0n_device(kk_ctx *ctx, int32_t n_utts, const int32_t *n_frames, const float *en,
                           const float *style, float *f0, float *n, void *stream);
 
+/* The text encoder up to its biLSTM (text_encoder,
+ * src/arch/kokoro/graph_ops.cpp:1578-1624, replacing the ggml sub-graph from
+ * the token ids to the biLSTM output that the duration mask then multiplies):
+ * the embedding lookup, three times conv1d_chfirst k = 5 (pad 2) + bias ->
+ * LayerNorm over the 512 channels (eps 1e-5) * gamma + beta -> LeakyReLU
+ * 0.2, then the biLSTM kokopop.text_encoder.lstm (512 -> 2 x 256). Ragged
+ * batch; per sequence b:
+ *   n_tokens[b] = N_b, at most 8192
+ *   ids : int32 [N_b], concatenated over the sequences, 0 <= id < vocab
+ *   out : [N_b, 512], token-major (forward half first)
+ * Host buffers; an id out of range is KK_ERROR_INVALID_ARGUMENT. */
+int kk_text_encoder_forward(kk_ctx *ctx, int32_t n_seqs, const int32_t *n_tokens, const int32_t *ids, float *out);
+
+/* Same with device-resident ids and out (lengths on the host). Asynchronous
+ * on `stream` (NULL = the context's stream); an id out of range gives a zero
+ * embedding row and is reported (KK_ERROR_INVALID_ARGUMENT) by the next call
+ * of this context that synchronises. */
+int kk_text_encoder_forward_device(kk_ctx *ctx, int32_t n_seqs, const int32_t *n_tokens, const int32_t *ids,
+                                   float *out, void *stream);
+
+/* The duration head (src/arch/kokoro/kokoro.cpp:343-355 and :469-516,
+ * replacing the predictor.lstm graph node and the host loop over the
+ * duration_proj buckets): the biLSTM kokopop.predictor.lstm (640 -> 2 x 256)
+ * over the duration encoder output, then per token
+ *   durations[t] = (float) sum over buckets n of sigmoid((float) acc_n),
+ *   acc_n = bias[n] + sum over k of w[n][k] h[k]
+ * in double, as the reference computes it on the host. Ragged batch;
+ * per sequence b: n_tokens[b] = N_b (at most 65536), d: [N_b, 640]
+ * token-major, durations: [N_b]. Host buffers. */
+int kk_duration_head_forward(kk_ctx *ctx, int32_t n_seqs, const int32_t *n_tokens, const float *d,
+                             float *durations);
+
+/* Same with device-resident d and durations (lengths on the host).
+ * Asynchronous on `stream` (NULL = the context's stream). */
+int kk_duration_head_forward_device(kk_ctx *ctx, int32_t n_seqs, const int32_t *n_tokens, const float *d,
+                                    float *durations, void *stream);
+
+/* The duration head's projection and bucket sum alone (kokoro.cpp:469-516),
+ * from the predictor biLSTM output h: [n_rows, 512] token-major, durations:
+ * [n_rows]; at most 65536 rows. Host buffers. */
+int kk_duration_proj(kk_ctx *ctx, int64_t n_rows, const float *h, float *durations);
+
 /* Durations -> frames and the alignment (duration_to_frames,
  * src/arch/kokoro/kokoro.cpp:181-193; build_duration_mask :115-152 and
  * en = d . mask :669-674): frames[i] = clamp(int(lrint(d[i] / speed)), 1, 50)

@@ -80,6 +80,11 @@ def load_library():
     L.kk_duration_encoder_forward_device.argtypes = [vp, ctypes.c_int32, _i32p, vp, vp, vp, vp]
     L.kk_prosody_f0n.argtypes = [vp, ctypes.c_int32, _i32p, _f32p, _f32p, _f32p, _f32p]
     L.kk_prosody_f0n_device.argtypes = [vp, ctypes.c_int32, _i32p, vp, vp, vp, vp, vp]
+    L.kk_text_encoder_forward.argtypes = [vp, ctypes.c_int32, _i32p, _i32p, _f32p]
+    L.kk_text_encoder_forward_device.argtypes = [vp, ctypes.c_int32, _i32p, vp, vp, vp]
+    L.kk_duration_head_forward.argtypes = [vp, ctypes.c_int32, _i32p, _f32p, _f32p]
+    L.kk_duration_head_forward_device.argtypes = [vp, ctypes.c_int32, _i32p, vp, vp, vp]
+    L.kk_duration_proj.argtypes = [vp, ctypes.c_int64, _f32p, _f32p]
     L.kk_align_durations.argtypes = [vp, ctypes.c_int64, _f32p, ctypes.c_float, _i32p,
                                      ctypes.POINTER(ctypes.c_int64), _f32p, ctypes.c_int64, _f32p, ctypes.c_int64]
     L.kk_profile_enable.argtypes = [vp, ctypes.c_int]
@@ -252,6 +257,44 @@ class Context:
         lens = np.ascontiguousarray(lens, np.int32)
         self._check(self.L.kk_duration_encoder_forward_device(self.h, len(lens), _ptr(lens, _i32p), x_ptr,
                                                               style_ptr, out_ptr, stream or None))
+
+    def text_encoder(self, ids: Sequence[np.ndarray]) -> List[np.ndarray]:
+        """kk_text_encoder_forward: ids[b] int32 [N_b] -> [N_b, 512] each
+        (the text encoder's biLSTM output)."""
+        ids = [np.ascontiguousarray(i, np.int32) for i in ids]
+        lens = np.array([len(i) for i in ids], np.int32)
+        flat = np.concatenate(ids) if ids else np.zeros(0, np.int32)
+        out = np.zeros((int(lens.sum()), 512), np.float32)
+        self._check(self.L.kk_text_encoder_forward(self.h, len(ids), _ptr(lens, _i32p), _ptr(flat, _i32p),
+                                                   _ptr(out)))
+        return np.split(out, np.cumsum(lens)[:-1])
+
+    def text_encoder_device(self, lens: np.ndarray, ids_ptr: int, out_ptr: int, stream: int = 0) -> None:
+        lens = np.ascontiguousarray(lens, np.int32)
+        self._check(self.L.kk_text_encoder_forward_device(self.h, len(lens), _ptr(lens, _i32p), ids_ptr, out_ptr,
+                                                          stream))
+
+    def duration_head(self, ds: Sequence[np.ndarray]) -> List[np.ndarray]:
+        """kk_duration_head_forward: ds[b] [N_b, 640] (duration encoder
+        output) -> durations [N_b] each."""
+        ds = [np.ascontiguousarray(d, np.float32) for d in ds]
+        lens = np.array([d.shape[0] for d in ds], np.int32)
+        out = np.zeros(int(lens.sum()), np.float32)
+        self._check(self.L.kk_duration_head_forward(self.h, len(ds), _ptr(lens, _i32p), _ptr(np.concatenate(ds)),
+                                                    _ptr(out)))
+        return np.split(out, np.cumsum(lens)[:-1])
+
+    def duration_head_device(self, lens: np.ndarray, d_ptr: int, out_ptr: int, stream: int = 0) -> None:
+        lens = np.ascontiguousarray(lens, np.int32)
+        self._check(self.L.kk_duration_head_forward_device(self.h, len(lens), _ptr(lens, _i32p), d_ptr, out_ptr,
+                                                           stream))
+
+    def duration_proj(self, h: np.ndarray) -> np.ndarray:
+        """kk_duration_proj: the predictor biLSTM output [N, 512] -> durations [N]."""
+        h = np.ascontiguousarray(h, np.float32)
+        out = np.zeros(h.shape[0], np.float32)
+        self._check(self.L.kk_duration_proj(self.h, h.shape[0], _ptr(h), _ptr(out)))
+        return out
 
     def align_durations(self, durations: np.ndarray, speed: float, hidden: Optional[np.ndarray] = None):
         """kk_align_durations: (frames int32 [n], total, en [total, D] or None)."""

@@ -224,6 +224,13 @@ static std::vector<std::pair<std::string, int>> prosody_convs() {
     return v;
 }
 
+// The text encoder's three k = 5 convolutions (graph_ops.cpp:1593-1611).
+static std::vector<std::string> text_convs() {
+    std::vector<std::string> v;
+    for (int i = 0; i < 3; ++i) v.push_back("kokopop.text_encoder.cnn." + std::to_string(i) + ".0.weight");
+    return v;
+}
+
 // Packs a convolution weight W[oc, ic, k] (via `get`) into the tensor-core
 // kernel's shared-memory images: half [K][IC_pad/64][n_tiles][8][128][8],
 // zero in the channel padding. The values are F16 already, so the
@@ -400,6 +407,36 @@ void kk_ctx::derive() {
                     [&](int oc, int ic, int k) { return h[((size_t)oc * IC + ic) * K + k]; });
         }
     }
+    // the text encoder's convs: tensor cores when all F16, split when all F32
+    {
+        bool t16 = true, t32 = true, any = false;
+        for (const auto &n : text_convs()) {
+            const DevTensor *t = Wopt(n);
+            if (!t) {
+                t16 = t32 = false;
+                continue;
+            }
+            any = true;
+            t16 = t16 && t->f16;
+            t32 = t32 && !t->f16;
+        }
+        text_mode = !any ? 0 : t16 ? 1 : (t32 && f32_split) ? 2 : 0;
+        if (text_mode) {
+            check_cuda(conv_tc_init(), "tensor-core conv init");
+            std::vector<float> h;
+            for (const auto &n : text_convs()) {
+                const DevTensor *t = Wopt(n);
+                const int K = 5, OC = (int)t->ne[1], IC = (int)(t->ne[0] / K);
+                h.resize((size_t)t->n);
+                check_cuda(cudaMemcpy(h.data(), t->d, h.size() * 4, cudaMemcpyDeviceToHost), "read conv weight");
+                auto get = [&](int oc, int ic, int k) { return h[((size_t)oc * IC + ic) * K + k]; };
+                if (text_mode == 1)
+                    pack_tc(packed[n], OC, IC, K, get);
+                else
+                    pack_tc_split(packed[n], OC, IC, K, get);
+            }
+        }
+    }
     d_err.ensure(sizeof(int));
     check_cuda(cudaMemset(d_err.p, 0, sizeof(int)), "clear error");
     if (tc_mode) {
@@ -558,6 +595,22 @@ void kk_ctx::derive() {
         }
         prosody_ready = pok;
     }
+    // text encoder (optional)
+    {
+        missing_text.clear();
+        auto needt = [&](const std::string &n) {
+            if (!Wopt(n) && missing_text.empty()) missing_text = n;
+        };
+        needt("kokopop.text_encoder.embedding.weight");
+        for (int i = 0; i < 3; ++i) {
+            const std::string p = "kokopop.text_encoder.cnn." + std::to_string(i);
+            for (const char *w : {".0.weight", ".0.bias", ".1.gamma", ".1.beta"}) needt(p + w);
+        }
+        for (const char *sfx : {"", "_reverse"})
+            for (const char *w : {"weight_ih_l0", "weight_hh_l0", "bias_ih_l0", "bias_hh_l0"})
+                needt(std::string("kokopop.text_encoder.lstm.") + w + sfx);
+        text_ready = missing_text.empty();
+    }
     // tables
     StftTables stt;
     IstftTables ist;
@@ -672,11 +725,11 @@ struct Runner {
     const bool tc;
     const bool split;  // F32 weights split over the half tensor cores
 
-    // tc_path: the tensor-core path on F16 weights (default: the context's
-    // mode, split F32 included)
-    Runner(kk_ctx &ctx, const Plan &plan, cudaStream_t s, int tc_path = -1)
+    // tc_path: the tensor-core path (default: the context's mode, split F32
+    // included); split_path: with tc_path set, its operands split F32
+    Runner(kk_ctx &ctx, const Plan &plan, cudaStream_t s, int tc_path = -1, bool split_path = false)
         : c(ctx), P(plan), st(s), tc(tc_path < 0 ? ctx.tc_mode : tc_path != 0),
-          split(tc_path < 0 && ctx.tc_mode && ctx.split_mode) {}
+          split(tc_path < 0 ? ctx.tc_mode && ctx.split_mode : tc_path != 0 && split_path) {}
 
     int64_t R(int m) const { return P.R(m); }
 
@@ -1454,6 +1507,7 @@ void check_device_error(kk_ctx *ctx) {
     check_cuda(cudaMemcpy(&e, ctx->d_err.p, sizeof e, cudaMemcpyDeviceToHost), "read device status");
     if (e != 0) {
         cudaMemset(ctx->d_err.p, 0, sizeof(int));
+        if (e == kErrTokenId) throw KKError(KK_ERROR_INVALID_ARGUMENT, "token id out of range (device input)");
         throw KKError(KK_ERROR_INFERENCE, "tensor-core convolution timed out waiting (code " + std::to_string(e) + ")");
     }
 }
@@ -1822,6 +1876,93 @@ void prosody_device(kk_ctx &c, int32_t n_utts, const int32_t *n_frames, const fl
     check_cuda(cudaGetLastError(), "kernel launch");
 }
 
+// text_encoder (graph_ops.cpp:1578-1624) up to its biLSTM, for n sequences
+// of token ids (device, concatenated) -> out [sum n_tokens][512] (device).
+// The CNN runs on a ragged plan (tokens as level 1); the last LayerNorm
+// writes the LSTM layout (rows t * n + s) directly.
+void text_encoder_device(kk_ctx &c, int32_t n, const int32_t *n_tokens, const int32_t *ids, float *out,
+                         cudaStream_t st) {
+    if (!c.text_ready) throw KKError(KK_ERROR_MODEL, "text encoder weights incomplete, first missing: " + c.missing_text);
+    const DevTensor &emb = c.W("kokopop.text_encoder.embedding.weight");
+    const int C = (int)emb.ne[0], vocab = (int)emb.ne[1];
+    const LstmLayer &L = c.lstm_layer("kokopop.text_encoder.lstm");
+    if (C != 512 || L.in_dim != C || L.H != 256)
+        throw KKError(KK_ERROR_MODEL, "text encoder must be 512 channels into a biLSTM 512 -> 2 x 256");
+    Plan P = make_plan(n_tokens, n);
+    Runner r(c, P, st, c.text_mode != 0 ? 1 : 0, c.text_mode == 2);
+    r.setup_batch();
+    const int64_t R1 = P.R(1);
+    float *X = c.buf("te_x", (size_t)C * R1);
+    float *Y = c.buf("te_y", (size_t)C * R1);
+    embed(emb.d, C, vocab, ids, r.d_cum, r.B, X, R1, (int *)c.d_err.p, st);
+    ++c.n_launches;
+    // the biLSTM's input in its own layout
+    Runner::Seqs q = lstm_seqs(c, n, n_tokens, st);
+    Plan Pl = lstm_plan(n, q.max_len);
+    const int64_t Rr = Pl.R(1);
+    float *Xl = c.buf("lstm_X", (size_t)C * Rr);
+    check_cuda(cudaMemsetAsync(Xl, 0, (size_t)C * Rr * 4, st), "memset");
+    Op in;
+    if (r.tc) {
+        in = r.op("opT", 1, C);
+        r.zero(in, C);
+    } else {
+        in.f = X;
+        in.R = R1;
+    }
+    for (int i = 0; i < 3; ++i) {
+        const std::string p = "kokopop.text_encoder.cnn." + std::to_string(i);
+        if (r.tc) r.act_only(X, in, R1, C, 1, 0, ACT_NONE, 0.f);
+        r.conv_w(p + ".0.weight", p + ".0.bias", in, C, 5, 2, 1, Y, R1, R1, Runner::Epi{}, r.sum_len(1, 0));
+        const bool last = i == 2;
+        layer_norm_ch(Y, R1, C, c.W(p + ".1.gamma").d, c.W(p + ".1.beta").d, 0.2f, r.B, last ? Xl : X,
+                      last ? Rr : R1, last ? n : 0, st);
+        ++c.n_launches;
+    }
+    Runner rl(c, Pl, st);
+    rl.setup_batch();
+    float *hout = c.buf("lstm_h", (size_t)512 * Rr);
+    rl.bilstm(L, Xl, hout, q);
+    lstm_unpack(hout, Rr, 512, out, q.d_len, q.d_cum, n, q.max_len, st);
+    ++c.n_launches;
+    check_cuda(cudaGetLastError(), "kernel launch");
+}
+
+// The duration projection's weights, checked against the predictor biLSTM.
+static void duration_proj_weights(kk_ctx &c, const DevTensor *&w, const DevTensor *&b) {
+    const std::string p = "kokopop.predictor.duration_proj.linear_layer.";
+    if (!c.Wopt(p + "weight") || !c.Wopt(p + "bias")) throw KKError(KK_ERROR_MODEL, "missing " + p + "weight / bias");
+    w = &c.W(p + "weight");
+    b = &c.W(p + "bias");
+    if (w->ne[0] != 512 || w->ne[1] < 1 || w->ne[1] > 64 || b->n != w->ne[1])
+        throw KKError(KK_ERROR_MODEL, "duration_proj must be 512 -> 1..64 buckets");
+}
+
+// predictor.lstm over the duration encoder output d [sum n][640] (device),
+// then the projection and bucket sum (kokoro.cpp:343-355, :469-516) into
+// durations [sum n] (device).
+void duration_head_device(kk_ctx &c, int32_t n, const int32_t *n_tokens, const float *d, float *durations,
+                          cudaStream_t st) {
+    const DevTensor *w = nullptr, *b = nullptr;
+    duration_proj_weights(c, w, b);
+    const LstmLayer &L = c.lstm_layer("kokopop.predictor.lstm");
+    if (L.in_dim != 640 || L.H != 256) throw KKError(KK_ERROR_MODEL, "predictor.lstm must be a biLSTM 640 -> 2 x 256");
+    Runner::Seqs q = lstm_seqs(c, n, n_tokens, st);
+    Plan Pl = lstm_plan(n, q.max_len);
+    Runner rl(c, Pl, st);
+    rl.setup_batch();
+    const int64_t Rr = Pl.R(1);
+    float *X = c.buf("lstm_X", (size_t)640 * Rr);
+    check_cuda(cudaMemsetAsync(X, 0, (size_t)640 * Rr * 4, st), "memset");
+    lstm_pack(d, 640, nullptr, 0, X, Rr, q.d_len, q.d_cum, n, q.max_len, st);
+    float *hout = c.buf("lstm_h", (size_t)512 * Rr);
+    rl.bilstm(L, X, hout, q);
+    check_cuda(duration_proj(hout, 1, Rr, 512, w->d, b->d, (int)w->ne[1], q.d_len, q.d_cum, n,
+                             (int64_t)q.max_len * n, durations, st),
+               "duration projection launch");
+    c.n_launches += 2;
+}
+
 int64_t total_steps(int32_t n_seqs, const int32_t *n_steps) {
     int64_t rows = 0;
     for (int b = 0; b < n_seqs; ++b) rows += n_steps[b];
@@ -1907,6 +2048,111 @@ int kk_prosody_f0n_device(kk_ctx *ctx, int32_t n_utts, const int32_t *n_frames, 
         use_device(ctx);
         cudaStream_t st = stream ? (cudaStream_t)stream : ctx->st;
         prosody_device(*ctx, n_utts, n_frames, en, style, f0, n, st);
+        return KK_OK;
+    });
+}
+
+namespace {
+// total tokens of a ragged batch of 1..kMaxFrames tokens per sequence
+int64_t token_rows(int32_t n_seqs, const int32_t *n_tokens) {
+    int64_t rows = 0;
+    for (int b = 0; b < n_seqs; ++b) {
+        if (n_tokens[b] < 1 || n_tokens[b] > kMaxFrames)
+            throw KKError(KK_ERROR_INVALID_ARGUMENT, "sequence length out of range [1, 8192]");
+        rows += n_tokens[b];
+    }
+    return rows;
+}
+}  // namespace
+
+int kk_text_encoder_forward(kk_ctx *ctx, int32_t n_seqs, const int32_t *n_tokens, const int32_t *ids, float *out) {
+    return guarded([&] {
+        if (!ctx || !n_tokens || !ids || !out || n_seqs < 1) throw KKError(KK_ERROR_INVALID_ARGUMENT, "null argument");
+        use_device(ctx);
+        kk_ctx &c = *ctx;
+        const int64_t rows = token_rows(n_seqs, n_tokens);
+        if (!c.text_ready) throw KKError(KK_ERROR_MODEL, "text encoder weights incomplete, first missing: " + c.missing_text);
+        const int64_t vocab = c.W("kokopop.text_encoder.embedding.weight").ne[1];
+        for (int64_t i = 0; i < rows; ++i)
+            if (ids[i] < 0 || ids[i] >= vocab) throw KKError(KK_ERROR_INVALID_ARGUMENT, "token id out of range");
+        cudaStream_t st = c.st;
+        int32_t *d_ids = (int32_t *)c.buf("te_ids", (size_t)rows);
+        float *d_out = c.buf("te_out", (size_t)rows * 512);
+        check_cuda(cudaMemcpyAsync(d_ids, ids, (size_t)rows * 4, cudaMemcpyHostToDevice, st), "upload ids");
+        text_encoder_device(c, n_seqs, n_tokens, d_ids, d_out, st);
+        check_cuda(cudaMemcpyAsync(out, d_out, (size_t)rows * 512 * 4, cudaMemcpyDeviceToHost, st), "D2H");
+        check_cuda(cudaStreamSynchronize(st), "text encoder");
+        check_device_error(ctx);
+        return KK_OK;
+    });
+}
+
+int kk_text_encoder_forward_device(kk_ctx *ctx, int32_t n_seqs, const int32_t *n_tokens, const int32_t *ids,
+                                   float *out, void *stream) {
+    return guarded([&] {
+        if (!ctx || !n_tokens || !ids || !out || n_seqs < 1) throw KKError(KK_ERROR_INVALID_ARGUMENT, "null argument");
+        token_rows(n_seqs, n_tokens);
+        use_device(ctx);
+        cudaStream_t st = stream ? (cudaStream_t)stream : ctx->st;
+        text_encoder_device(*ctx, n_seqs, n_tokens, ids, out, st);
+        return KK_OK;
+    });
+}
+
+int kk_duration_head_forward(kk_ctx *ctx, int32_t n_seqs, const int32_t *n_tokens, const float *d,
+                             float *durations) {
+    return guarded([&] {
+        if (!ctx || !n_tokens || !d || !durations || n_seqs < 1)
+            throw KKError(KK_ERROR_INVALID_ARGUMENT, "null argument");
+        use_device(ctx);
+        kk_ctx &c = *ctx;
+        cudaStream_t st = c.st;
+        for (int b = 0; b < n_seqs; ++b)
+            if (n_tokens[b] < 1 || n_tokens[b] > kMaxSteps)
+                throw KKError(KK_ERROR_INVALID_ARGUMENT, "sequence length out of range [1, 65536]");
+        const int64_t rows = total_steps(n_seqs, n_tokens);
+        float *d_in = c.buf("dh_in", (size_t)rows * 640);
+        float *d_out = c.buf("dh_out", (size_t)rows);
+        check_cuda(cudaMemcpyAsync(d_in, d, (size_t)rows * 640 * 4, cudaMemcpyHostToDevice, st), "upload d");
+        duration_head_device(c, n_seqs, n_tokens, d_in, d_out, st);
+        check_cuda(cudaMemcpyAsync(durations, d_out, (size_t)rows * 4, cudaMemcpyDeviceToHost, st), "D2H");
+        check_cuda(cudaStreamSynchronize(st), "duration head");
+        check_device_error(ctx);
+        return KK_OK;
+    });
+}
+
+int kk_duration_head_forward_device(kk_ctx *ctx, int32_t n_seqs, const int32_t *n_tokens, const float *d,
+                                    float *durations, void *stream) {
+    return guarded([&] {
+        if (!ctx || !n_tokens || !d || !durations || n_seqs < 1)
+            throw KKError(KK_ERROR_INVALID_ARGUMENT, "null argument");
+        use_device(ctx);
+        cudaStream_t st = stream ? (cudaStream_t)stream : ctx->st;
+        duration_head_device(*ctx, n_seqs, n_tokens, d, durations, st);
+        return KK_OK;
+    });
+}
+
+int kk_duration_proj(kk_ctx *ctx, int64_t n_rows, const float *h, float *durations) {
+    return guarded([&] {
+        if (!ctx || !h || !durations || n_rows < 1 || n_rows > kMaxSteps)
+            throw KKError(KK_ERROR_INVALID_ARGUMENT, "null argument or n_rows out of range [1, 65536]");
+        use_device(ctx);
+        kk_ctx &c = *ctx;
+        cudaStream_t st = c.st;
+        const DevTensor *w = nullptr, *b = nullptr;
+        duration_proj_weights(c, w, b);
+        const int32_t n = (int32_t)n_rows;
+        Runner::Seqs q = lstm_seqs(c, 1, &n, st);
+        float *d_h = c.buf("dh_h", (size_t)n_rows * 512);
+        float *d_out = c.buf("dh_out", (size_t)n_rows);
+        check_cuda(cudaMemcpyAsync(d_h, h, (size_t)n_rows * 512 * 4, cudaMemcpyHostToDevice, st), "upload h");
+        check_cuda(duration_proj(d_h, 512, 1, 512, w->d, b->d, (int)w->ne[1], q.d_len, q.d_cum, 1, n_rows, d_out, st),
+                   "duration projection launch");
+        ++c.n_launches;
+        check_cuda(cudaMemcpyAsync(durations, d_out, (size_t)n_rows * 4, cudaMemcpyDeviceToHost, st), "D2H");
+        check_cuda(cudaStreamSynchronize(st), "duration projection");
         return KK_OK;
     });
 }

@@ -113,6 +113,11 @@ struct kk_ctx {
     bool prosody_ready = false;  // the prosody predictor's F0 / N chain
     bool prosody_tc = false;     // its convolutions all F16: the tensor-core path
     std::string missing_prosody;
+    bool text_ready = false;  // the text encoder up to its biLSTM
+    std::string missing_text;
+    // its k = 5 convs: 0 CUDA cores (mixed types, or F32 without the split),
+    // 1 tensor cores on F16 weights, 2 split F32 on the tensor cores
+    int text_mode = 0;
     kk::DevBuf convt_phase[2];
     bool convt_f16[2] = {false, false};
     // tensor-core path: every convolution weight is F16, or every one is F32

@@ -215,6 +215,21 @@ void har_s2d(const float *har, int64_t R_har, __half *y, int64_t R, int64_t Ry, 
 void pool_up_h(const float *x, __half *y, int64_t R_in, int64_t Ry_out, int C, const float *w, const float *bias,
                const Batch &b, int max_T, int64_t lo_off, cudaStream_t st);
 
+// kk_frontend.cu: the text encoder's embedding and LayerNorm, the duration
+// projection.
+constexpr int kErrTokenId = 31;  // device error word: a token id out of range
+void embed(const float *emb, int C, int vocab, const int32_t *ids, const int64_t *cum, const Batch &b, float *X,
+           int64_t R, int *err, cudaStream_t st);
+// LayerNorm over C channels per token row + gamma / beta + LeakyReLU(slope);
+// lstm_B > 0 writes row t * lstm_B + u (the LSTM layout) instead of row q.
+void layer_norm_ch(const float *x, int64_t R, int C, const float *gamma, const float *beta, float slope,
+                   const Batch &b, float *y, int64_t R_out, int lstm_B, cudaStream_t st);
+// durations[cum[s] + t] from h(r, k) = h[r * s_row + k * s_k], r = t * B + s
+// (P <= 1024 inputs, NB <= 64 buckets)
+cudaError_t duration_proj(const float *h, int64_t s_row, int64_t s_k, int P, const float *w, const float *bias,
+                          int NB, const int32_t *len, const int64_t *cum, int B, int64_t n_rows, float *out,
+                          cudaStream_t st);
+
 // kk_lstm.cu: bidirectional LSTM stack and the duration alignment.
 // Sequences are packed time-major: row = t * B + b of a [C][R] activation.
 struct LstmRecArgs {

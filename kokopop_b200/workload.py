@@ -168,6 +168,48 @@ def prosody_spec() -> List[Tuple[str, Tuple[int, ...]]]:
     return spec
 
 
+VOCAB = 178  # Kokoro's token vocabulary (pad 0, phonemes 1..177)
+
+
+def text_encoder_spec() -> List[Tuple[str, Tuple[int, ...]]]:
+    """The text encoder up to its biLSTM (graph_ops.cpp:1578-1624): the
+    embedding [512, vocab], three k = 5 convs 512 -> 512 (weights stored 2-D,
+    innermost IC * K, as the converter writes them) with their LayerNorm
+    gamma / beta, and the biLSTM 512 -> 2 x 256."""
+    p = "kokopop.text_encoder"
+    spec: List[Tuple[str, Tuple[int, ...]]] = [(f"{p}.embedding.weight", (HIDDEN, VOCAB))]
+    for i in range(3):
+        spec += [
+            (f"{p}.cnn.{i}.0.weight", (HIDDEN * 5, HIDDEN)),
+            (f"{p}.cnn.{i}.0.bias", (HIDDEN,)),
+            (f"{p}.cnn.{i}.1.gamma", (HIDDEN,)),
+            (f"{p}.cnn.{i}.1.beta", (HIDDEN,)),
+        ]
+    spec += lstm_spec(f"{p}.lstm", HIDDEN)
+    return spec
+
+
+def duration_head_spec() -> List[Tuple[str, Tuple[int, ...]]]:
+    """predictor.lstm (biLSTM 640 -> 2 x 256) and the duration projection
+    512 -> 50 buckets (kokoro.cpp:343-355, :469-516)."""
+    p = "kokopop.predictor"
+    return lstm_spec(f"{p}.lstm", HIDDEN + STYLE_DIM) + [
+        (f"{p}.duration_proj.linear_layer.weight", (HIDDEN, 50)),
+        (f"{p}.duration_proj.linear_layer.bias", (50,)),
+    ]
+
+
+def frontend_weights(f16: bool = False) -> Dict[str, Tensor]:
+    """Text encoder + duration head weights: seed 2, N(0, 0.02) (config 2's
+    draw), F16 under the converter's policy when f16, else F32."""
+    return make_weights(text_encoder_spec() + duration_head_spec(), seed=2, dist="normal", scale=0.02, f16=f16)
+
+
+def token_ids(rng: np.random.Generator, n: int) -> np.ndarray:
+    """n phoneme ids uniform over 1..177 wrapped in the pad id 0 (n + 2 ids)."""
+    return np.concatenate([[0], rng.integers(1, VOCAB, size=n), [0]]).astype(np.int32)
+
+
 def prosody_weights(f16: bool = False) -> Dict[str, Tensor]:
     """Prosody F0 / N chain weights: seed 2, N(0, 0.02) (config 2's
     draw), F16 under the converter's policy when f16, else F32."""
@@ -179,6 +221,9 @@ def _is_f16_under_converter_policy(name: str, ne: Sequence[int]) -> bool:
     if len(ne) <= 1:
         return False
     if ".alpha" in name and ".weight" not in name:
+        return False
+    # embedding lookup tables stay F32 (indexed, never multiplied)
+    if name.endswith(".weight") and (".embeddings." in name or ".embedding.weight" in name):
         return False
     return True
 

@@ -1173,6 +1173,109 @@ int kko_duration_encoder(kko_model *m, int64_t N, const float *x, const float *s
 /* ------------------------------------------------------------------------ */
 
 /* duration_to_frames (kokoro.cpp:181-193). */
+/* text_encoder (graph_ops.cpp:1578-1624): ggml_get_rows of the embedding
+ * [C, vocab] (ne[0] = C) -> [C, N]; three times: the transpose to [N, C]
+ * time-fastest, conv1d_chfirst k = 5, pad 2 (the conv1d arithmetic: F16
+ * weights round the input to half) + the channel bias, then per token
+ * ggml_norm over the C channels (eps 1e-5), * gamma, + beta, LeakyReLU 0.2;
+ * then the biLSTM over the N tokens. */
+int kko_text_encoder(kko_model *m, int64_t N, const int32_t *ids, float *out) {
+    g_err[0] = 0;
+    const ko_tensor *emb = req(m, "kokopop.text_encoder.embedding.weight");
+    if (!emb) return -1;
+    const int64_t C = emb->ne[0], V = emb->ne[1];
+    if (N < 1) return fail("text encoder needs at least one token%s", "");
+    for (int64_t t = 0; t < N; ++t)
+        if (ids[t] < 0 || ids[t] >= V) return fail("token id out of range%s", "");
+    float *x = fbuf((size_t)(C * N)), *y = fbuf((size_t)(C * N));
+    float *tok = fbuf((size_t)C), *nrm = fbuf((size_t)C);
+    int rc = 0;
+    /* x [N, C] time-fastest: x[c * N + t] */
+    for (int64_t t = 0; t < N; ++t)
+        for (int64_t c = 0; c < C; ++c) x[c * N + t] = emb->data[(int64_t)ids[t] * C + c];
+    for (int i = 0; i < 3 && rc == 0; ++i) {
+        char k[256];
+        const ko_tensor *w, *b, *g, *be;
+        snprintf(k, sizeof k, "kokopop.text_encoder.cnn.%d.0.weight", i);
+        w = req(m, k);
+        snprintf(k, sizeof k, "kokopop.text_encoder.cnn.%d.0.bias", i);
+        b = req(m, k);
+        snprintf(k, sizeof k, "kokopop.text_encoder.cnn.%d.1.gamma", i);
+        g = req(m, k);
+        snprintf(k, sizeof k, "kokopop.text_encoder.cnn.%d.1.beta", i);
+        be = req(m, k);
+        if (!w || !b || !g || !be) {
+            rc = -1;
+            break;
+        }
+        int64_t OL = 0;
+        rc = conv1d(w, b, x, C, N, 1, 2, 1, 5, y, &OL);
+        if (rc == 0 && (OL != N || (w->ne[2] > 1 ? w->ne[2] : w->ne[1]) != C))
+            rc = fail("text encoder conv shape mismatch: %s", w->name);
+        if (rc != 0) break;
+        for (int64_t t = 0; t < N; ++t) {
+            for (int64_t c = 0; c < C; ++c) tok[c] = y[c * N + t];
+            kko_norm_time(tok, 1, C, 1e-5f, nrm);
+            for (int64_t c = 0; c < C; ++c) {
+                float v = nrm[c] * g->data[c];
+                v = v + be->data[c];
+                tok[c] = v;
+            }
+            leaky_relu(tok, tok, (size_t)C, 0.2f);
+            for (int64_t c = 0; c < C; ++c) x[c * N + t] = tok[c];
+        }
+    }
+    if (rc == 0) {
+        /* the biLSTM reads [N, C] feature-fastest */
+        for (int64_t t = 0; t < N; ++t)
+            for (int64_t c = 0; c < C; ++c) y[t * C + c] = x[c * N + t];
+        rc = kko_bilstm(m, "kokopop.text_encoder.lstm", N, C, y, out);
+    }
+    free(x);
+    free(y);
+    free(tok);
+    free(nrm);
+    return rc;
+}
+
+/* The duration projection and bucket sum (kokoro.cpp:469-516), on the host in
+ * double: per token and bucket n, acc = b[n] + sum over k ascending of
+ * w[n][k] * h[k] (separate double multiply and add), x = (float)acc, then the
+ * logistic function in double by the branch that avoids overflow, summed over
+ * n ascending; the duration is (float)sum. */
+int kko_duration_proj(kko_model *m, int64_t N, const float *h, float *durations) {
+    g_err[0] = 0;
+    const ko_tensor *w = req(m, "kokopop.predictor.duration_proj.linear_layer.weight");
+    const ko_tensor *b = req(m, "kokopop.predictor.duration_proj.linear_layer.bias");
+    if (!w || !b) return -1;
+    const int64_t P = w->ne[0], NB = w->ne[1];
+    for (int64_t t = 0; t < N; ++t) {
+        const float *ht = h + t * P;
+        double sum = 0.0;
+        for (int64_t n = 0; n < NB; ++n) {
+            const float *wr = w->data + n * P;
+            double acc = (double)b->data[n];
+            for (int64_t k = 0; k < P; ++k) acc += (double)wr[k] * (double)ht[k];
+            const double x = (double)(float)acc;
+            sum += x >= 0.0 ? 1.0 / (1.0 + exp(-x)) : exp(x) / (1.0 + exp(x));
+        }
+        durations[t] = (float)sum;
+    }
+    return 0;
+}
+
+/* predictor.lstm over the duration encoder output, then the projection. */
+int kko_duration_head(kko_model *m, int64_t N, const float *d, float *durations) {
+    g_err[0] = 0;
+    const ko_tensor *w = req(m, "kokopop.predictor.duration_proj.linear_layer.weight");
+    if (!w) return -1;
+    float *h = fbuf((size_t)(N * w->ne[0]));
+    int rc = kko_bilstm(m, "kokopop.predictor.lstm", N, 640, d, h);
+    if (rc == 0) rc = kko_duration_proj(m, N, h, durations);
+    free(h);
+    return rc;
+}
+
 static int duration_to_frames(float value, float speed) {
     if (!isfinite(speed) || speed <= 0.0f) speed = 1.0f;
     const float v = value / speed;

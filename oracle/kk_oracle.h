@@ -108,6 +108,22 @@ int kko_align_durations(const float *durations, int64_t n_tokens, float speed,
                         int32_t *frames, int64_t *total, const float *hidden,
                         int64_t hidden_dim, float *en, int64_t en_capacity);
 
+/* ---- text encoder (graph_ops.cpp:1578-1624, up to the biLSTM) ----
+ * ids: [N] token ids, 0 <= id < vocab; out: [N, 512] feature-fastest (the
+ * biLSTM kokopop.text_encoder.lstm, forward half first), the t_en that the
+ * duration alignment multiplies by the one-hot mask. */
+int kko_text_encoder(kko_model *m, int64_t N, const int32_t *ids, float *out);
+
+/* ---- duration head (kokoro.cpp:343-355, :469-516) ----
+ * d: [N, 640] (the duration encoder output) -> the biLSTM
+ * kokopop.predictor.lstm -> per token the sum over the projection buckets of
+ * sigmoid(linear), in double; durations: [N]. */
+int kko_duration_head(kko_model *m, int64_t N, const float *d, float *durations);
+
+/* The duration head's last step alone, from the biLSTM output h [N, P]
+ * (P = the projection's input size). */
+int kko_duration_proj(kko_model *m, int64_t N, const float *h, float *durations);
+
 /* Single-op entry points used by the unit tests. */
 void kko_norm_time(const float *x, int64_t C, int64_t L, float eps, float *y);
 float kko_round_f16(float x);

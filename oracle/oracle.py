@@ -185,6 +185,31 @@ class OracleModel:
                                            _ptr(np.ascontiguousarray(style, np.float32)), _ptr(f0), _ptr(nn)))
         return f0, nn
 
+    def text_encoder(self, ids: np.ndarray):
+        """kko_text_encoder: token ids [N] -> [N, 512] (the biLSTM output)."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        N = len(ids)
+        out = np.zeros((N, 512), np.float32)
+        self._check(self.L.kko_text_encoder(ctypes.c_void_p(self.h), ctypes.c_int64(N),
+                                            ids.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), _ptr(out)))
+        return out
+
+    def duration_head(self, d: np.ndarray):
+        """kko_duration_head: the duration encoder output [N, 640] -> durations [N]."""
+        d = np.ascontiguousarray(d, dtype=np.float32)
+        out = np.zeros(d.shape[0], np.float32)
+        self._check(self.L.kko_duration_head(ctypes.c_void_p(self.h), ctypes.c_int64(d.shape[0]), _ptr(d),
+                                             _ptr(out)))
+        return out
+
+    def duration_proj(self, h: np.ndarray):
+        """kko_duration_proj: the predictor biLSTM output [N, 512] -> durations [N]."""
+        h = np.ascontiguousarray(h, dtype=np.float32)
+        out = np.zeros(h.shape[0], np.float32)
+        self._check(self.L.kko_duration_proj(ctypes.c_void_p(self.h), ctypes.c_int64(h.shape[0]), _ptr(h),
+                                             _ptr(out)))
+        return out
+
 
 def istft(post: np.ndarray) -> np.ndarray:
     post = np.ascontiguousarray(post, dtype=np.float32)

@@ -235,3 +235,20 @@ def test_prosody_chain_shapes_and_determinism():
         assert np.all(np.isfinite(f0)) and np.all(np.isfinite(n))
         f0b, nb = m.prosody_f0n(en, st)
         assert np.array_equal(f0, f0b) and np.array_equal(n, nb)
+
+
+def test_text_encoder_and_duration_head_shapes_and_determinism():
+    """The front-end restatements run, give finite values of the documented
+    shapes, and repeat bit for bit."""
+    from kokopop_b200 import workload as W
+    from oracle import oracle as O
+    m = O.OracleModel(W.frontend_weights(f16=False))
+    ids = W.token_ids(np.random.default_rng(1), 30)
+    a, b = m.text_encoder(ids), m.text_encoder(ids)
+    assert a.shape == (32, 512) and np.isfinite(a).all()
+    np.testing.assert_array_equal(a, b)
+    d = np.random.default_rng(2).normal(0, 1, (32, 640)).astype(np.float32)
+    du = m.duration_head(d)
+    assert du.shape == (32,) and np.all((du > 0) & (du < 50))
+    with pytest.raises(RuntimeError):
+        m.text_encoder(np.array([0, 178], np.int32))
