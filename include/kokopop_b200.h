@@ -175,6 +175,24 @@ int kk_text_encoder_forward(kk_ctx *ctx, int32_t n_seqs, const int32_t *n_tokens
 int kk_text_encoder_forward_device(kk_ctx *ctx, int32_t n_seqs, const int32_t *n_tokens, const int32_t *ids,
                                    float *out, void *stream);
 
+/* ALBERT and bert_encoder (src/arch/kokoro/kokoro.cpp:279-337, replacing the
+ * frontend graph from the token ids to `cur = linear(enc_w, enc_b, cur)`):
+ * word + position (0..N_b - 1) + token-type-0 embeddings, LayerNorm (eps
+ * 1e-12), the 128 -> 768 mapping, twelve passes of the shared layer (12
+ * heads of 64, softmax(q k / 8) v, dense + residual -> LayerNorm, ffn ->
+ * GELU -> ffn_output + residual -> LayerNorm), then bert_encoder 768 -> 512.
+ * Ragged batch; per sequence b: n_tokens[b] = N_b, at most 512 (the position
+ * table); ids int32 [N_b] concatenated; out [N_b, 512] token-major (the
+ * duration encoder's input). Host buffers; an id out of range is
+ * KK_ERROR_INVALID_ARGUMENT. */
+int kk_albert_forward(kk_ctx *ctx, int32_t n_seqs, const int32_t *n_tokens, const int32_t *ids, float *out);
+
+/* Same with device-resident ids and out (lengths on the host), asynchronous
+ * on `stream` (NULL = the context's stream); a bad id as in
+ * kk_text_encoder_forward_device. */
+int kk_albert_forward_device(kk_ctx *ctx, int32_t n_seqs, const int32_t *n_tokens, const int32_t *ids, float *out,
+                             void *stream);
+
 /* The duration head (src/arch/kokoro/kokoro.cpp:343-355 and :469-516,
  * replacing the predictor.lstm graph node and the host loop over the
  * duration_proj buckets): the biLSTM kokopop.predictor.lstm (640 -> 2 x 256)

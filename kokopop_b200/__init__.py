@@ -82,6 +82,8 @@ def load_library():
     L.kk_prosody_f0n_device.argtypes = [vp, ctypes.c_int32, _i32p, vp, vp, vp, vp, vp]
     L.kk_text_encoder_forward.argtypes = [vp, ctypes.c_int32, _i32p, _i32p, _f32p]
     L.kk_text_encoder_forward_device.argtypes = [vp, ctypes.c_int32, _i32p, vp, vp, vp]
+    L.kk_albert_forward.argtypes = [vp, ctypes.c_int32, _i32p, _i32p, _f32p]
+    L.kk_albert_forward_device.argtypes = [vp, ctypes.c_int32, _i32p, vp, vp, vp]
     L.kk_duration_head_forward.argtypes = [vp, ctypes.c_int32, _i32p, _f32p, _f32p]
     L.kk_duration_head_forward_device.argtypes = [vp, ctypes.c_int32, _i32p, vp, vp, vp]
     L.kk_duration_proj.argtypes = [vp, ctypes.c_int64, _f32p, _f32p]
@@ -273,6 +275,20 @@ class Context:
         lens = np.ascontiguousarray(lens, np.int32)
         self._check(self.L.kk_text_encoder_forward_device(self.h, len(lens), _ptr(lens, _i32p), ids_ptr, out_ptr,
                                                           stream))
+
+    def albert(self, ids: Sequence[np.ndarray]) -> List[np.ndarray]:
+        """kk_albert_forward: ids[b] int32 [N_b] -> [N_b, 512] each (ALBERT +
+        bert_encoder, the duration encoder's input)."""
+        ids = [np.ascontiguousarray(i, np.int32) for i in ids]
+        lens = np.array([len(i) for i in ids], np.int32)
+        out = np.zeros((int(lens.sum()), 512), np.float32)
+        self._check(self.L.kk_albert_forward(self.h, len(ids), _ptr(lens, _i32p), _ptr(np.concatenate(ids), _i32p),
+                                             _ptr(out)))
+        return np.split(out, np.cumsum(lens)[:-1])
+
+    def albert_device(self, lens: np.ndarray, ids_ptr: int, out_ptr: int, stream: int = 0) -> None:
+        lens = np.ascontiguousarray(lens, np.int32)
+        self._check(self.L.kk_albert_forward_device(self.h, len(lens), _ptr(lens, _i32p), ids_ptr, out_ptr, stream))
 
     def duration_head(self, ds: Sequence[np.ndarray]) -> List[np.ndarray]:
         """kk_duration_head_forward: ds[b] [N_b, 640] (duration encoder

@@ -224,6 +224,17 @@ static std::vector<std::pair<std::string, int>> prosody_convs() {
     return v;
 }
 
+// ALBERT's linear layers (kokoro.cpp:52-81, :297-337) and bert_encoder.
+static const char *kAlbertLayer = "kokopop.albert.encoder.albert_layer_groups.0.albert_layers.0.";
+static std::vector<std::string> albert_linears() {
+    std::vector<std::string> v = {"kokopop.albert.encoder.embedding_hidden_mapping_in.weight",
+                                  "kokopop.bert_encoder.weight"};
+    for (const char *n : {"attention.query.weight", "attention.key.weight", "attention.value.weight",
+                          "attention.dense.weight", "ffn.weight", "ffn_output.weight"})
+        v.push_back(std::string(kAlbertLayer) + n);
+    return v;
+}
+
 // The text encoder's three k = 5 convolutions (graph_ops.cpp:1593-1611).
 static std::vector<std::string> text_convs() {
     std::vector<std::string> v;
@@ -437,6 +448,35 @@ void kk_ctx::derive() {
             }
         }
     }
+    // ALBERT's linears: the same rule as the text encoder's convs
+    {
+        bool t16 = true, t32 = true, all = true;
+        for (const auto &n : albert_linears()) {
+            const DevTensor *t = Wopt(n);
+            if (!t) {
+                all = false;
+                continue;
+            }
+            t16 = t16 && t->f16;
+            t32 = t32 && !t->f16;
+        }
+        albert_mode = !all ? 0 : t16 ? 1 : (t32 && f32_split) ? 2 : 0;
+        if (albert_mode) {
+            check_cuda(conv_tc_init(), "tensor-core conv init");
+            std::vector<float> h;
+            for (const auto &n : albert_linears()) {
+                const DevTensor *t = Wopt(n);
+                const int OC = (int)t->ne[1], IC = (int)t->ne[0];
+                h.resize((size_t)t->n);
+                check_cuda(cudaMemcpy(h.data(), t->d, h.size() * 4, cudaMemcpyDeviceToHost), "read linear weight");
+                auto get = [&](int oc, int ic, int) { return h[(size_t)oc * IC + ic]; };
+                if (albert_mode == 1)
+                    pack_tc(packed[n], OC, IC, 1, get);
+                else
+                    pack_tc_split(packed[n], OC, IC, 1, get);
+            }
+        }
+    }
     d_err.ensure(sizeof(int));
     check_cuda(cudaMemset(d_err.p, 0, sizeof(int)), "clear error");
     if (tc_mode) {
@@ -610,6 +650,24 @@ void kk_ctx::derive() {
             for (const char *w : {"weight_ih_l0", "weight_hh_l0", "bias_ih_l0", "bias_hh_l0"})
                 needt(std::string("kokopop.text_encoder.lstm.") + w + sfx);
         text_ready = missing_text.empty();
+    }
+    // ALBERT + bert_encoder (optional)
+    {
+        missing_albert.clear();
+        auto needa = [&](const std::string &n) {
+            if (!Wopt(n) && missing_albert.empty()) missing_albert = n;
+        };
+        for (const char *n : {"word_embeddings.weight", "position_embeddings.weight", "token_type_embeddings.weight",
+                              "LayerNorm.weight", "LayerNorm.bias"})
+            needa(std::string("kokopop.albert.embeddings.") + n);
+        for (const auto &n : albert_linears()) {
+            needa(n);
+            needa(n.substr(0, n.size() - 6) + "bias");
+        }
+        for (const char *n : {"attention.LayerNorm.weight", "attention.LayerNorm.bias",
+                              "full_layer_layer_norm.weight", "full_layer_layer_norm.bias"})
+            needa(std::string(kAlbertLayer) + n);
+        albert_ready = missing_albert.empty();
     }
     // tables
     StftTables stt;
@@ -1915,8 +1973,9 @@ void text_encoder_device(kk_ctx &c, int32_t n, const int32_t *n_tokens, const in
         if (r.tc) r.act_only(X, in, R1, C, 1, 0, ACT_NONE, 0.f);
         r.conv_w(p + ".0.weight", p + ".0.bias", in, C, 5, 2, 1, Y, R1, R1, Runner::Epi{}, r.sum_len(1, 0));
         const bool last = i == 2;
-        layer_norm_ch(Y, R1, C, c.W(p + ".1.gamma").d, c.W(p + ".1.beta").d, 0.2f, r.B, last ? Xl : X,
-                      last ? Rr : R1, last ? n : 0, st);
+        check_cuda(layer_norm_ch(Y, R1, C, c.W(p + ".1.gamma").d, c.W(p + ".1.beta").d, 1, 0.2f, 1e-5f, r.B,
+                                 last ? Xl : X, last ? Rr : R1, last ? n : 0, st),
+                   "layer norm launch");
         ++c.n_launches;
     }
     Runner rl(c, Pl, st);
@@ -1924,6 +1983,92 @@ void text_encoder_device(kk_ctx &c, int32_t n, const int32_t *n_tokens, const in
     float *hout = c.buf("lstm_h", (size_t)512 * Rr);
     rl.bilstm(L, Xl, hout, q);
     lstm_unpack(hout, Rr, 512, out, q.d_len, q.d_cum, n, q.max_len, st);
+    ++c.n_launches;
+    check_cuda(cudaGetLastError(), "kernel launch");
+}
+
+// ALBERT + bert_encoder (kokoro.cpp:279-337) for n sequences of token ids
+// (device, concatenated; positions 0..N-1, token type 0) -> out [sum
+// n_tokens][512] (device), the duration encoder's input. Tokens are level 1
+// of a ragged plan; every linear is a K = 1 conv on the operand path of the
+// weights' type; the attention, GELU and LayerNorms are kk_frontend.cu.
+void albert_device(kk_ctx &c, int32_t n, const int32_t *n_tokens, const int32_t *ids, float *out,
+                   cudaStream_t st) {
+    if (!c.albert_ready) throw KKError(KK_ERROR_MODEL, "ALBERT weights incomplete, first missing: " + c.missing_albert);
+    const std::string e = "kokopop.albert.embeddings.", L = kAlbertLayer;
+    const DevTensor &word = c.W(e + "word_embeddings.weight"), &pos = c.W(e + "position_embeddings.weight");
+    const DevTensor &type = c.W(e + "token_type_embeddings.weight");
+    const int E = (int)word.ne[0], vocab = (int)word.ne[1];
+    const DevTensor &mapw = c.W("kokopop.albert.encoder.embedding_hidden_mapping_in.weight");
+    const DevTensor &ffw = c.W(L + "ffn.weight"), &encw = c.W("kokopop.bert_encoder.weight");
+    const int H = (int)mapw.ne[1], F = (int)ffw.ne[1], D = (int)encw.ne[1];
+    if (pos.ne[0] != E || type.ne[0] != E || mapw.ne[0] != E || H != 768 || ffw.ne[0] != H || encw.ne[0] != H)
+        throw KKError(KK_ERROR_MODEL, "ALBERT shapes: embeddings E, hidden 768 (12 heads of 64)");
+    int max_len = 0;
+    for (int b = 0; b < n; ++b) {
+        if (n_tokens[b] > pos.ne[1] || n_tokens[b] > 512)
+            throw KKError(KK_ERROR_INVALID_ARGUMENT, "sequence longer than the position table");
+        max_len = std::max(max_len, (int)n_tokens[b]);
+    }
+    Plan P = make_plan(n_tokens, n);
+    Runner r(c, P, st, c.albert_mode != 0 ? 1 : 0, c.albert_mode == 2);
+    r.setup_batch();
+    const int64_t R1 = P.R(1);
+    float *x = c.buf("al_x", (size_t)E * R1);
+    float *cur = c.buf("al_cur", (size_t)H * R1);
+    float *qkv = c.buf("al_qkv", (size_t)3 * H * R1);
+    float *att = c.buf("al_att", (size_t)H * R1);
+    float *tmp = c.buf("al_tmp", (size_t)H * R1);
+    float *ff = c.buf("al_ff", (size_t)F * R1);
+    embed(word.d, E, vocab, ids, r.d_cum, r.B, x, R1, (int *)c.d_err.p, st, pos.d, type.d);
+    check_cuda(layer_norm_ch(x, R1, E, c.W(e + "LayerNorm.weight").d, c.W(e + "LayerNorm.bias").d, 0, 0.f, 1e-12f,
+                             r.B, x, R1, 0, st),
+               "layer norm launch");
+    c.n_launches += 2;
+    const int Cmax = std::max(std::max(E, H), F);
+    Op op;
+    if (r.tc) {
+        op = r.op("opA", 1, Cmax);
+        r.zero(op, Cmax);
+    }
+    // linear(w, b, in [C][R1]) -> o [OC][R1] (+ resid)
+    auto linear = [&](const std::string &w, const float *in, int C, float *o, const float *resid) {
+        Op src;
+        if (r.tc) {
+            r.act_only(in, op, R1, C, 1, 0, ACT_NONE, 0.f);
+            src = op;
+        } else {
+            src.f = const_cast<float *>(in);
+            src.R = R1;
+        }
+        Runner::Epi ep;
+        if (resid) {
+            ep.resid = resid;
+            ep.R_resid = R1;
+        }
+        r.conv_w(w, w.substr(0, w.size() - 6) + "bias", src, C, 1, 0, 1, o, R1, R1, ep, r.sum_len(1, 0));
+    };
+    linear("kokopop.albert.encoder.embedding_hidden_mapping_in.weight", x, E, cur, nullptr);
+    for (int layer = 0; layer < 12; ++layer) {
+        linear(L + "attention.query.weight", cur, H, qkv, nullptr);
+        linear(L + "attention.key.weight", cur, H, qkv + (size_t)H * R1, nullptr);
+        linear(L + "attention.value.weight", cur, H, qkv + (size_t)2 * H * R1, nullptr);
+        check_cuda(attention(qkv, R1, H, 12, max_len, r.B, 0.125f, att, st), "attention launch");
+        linear(L + "attention.dense.weight", att, H, tmp, cur);
+        check_cuda(layer_norm_ch(tmp, R1, H, c.W(L + "attention.LayerNorm.weight").d,
+                                 c.W(L + "attention.LayerNorm.bias").d, 0, 0.f, 1e-12f, r.B, cur, R1, 0, st),
+                   "layer norm launch");
+        linear(L + "ffn.weight", cur, H, ff, nullptr);
+        gelu(ff, (int64_t)F * R1, st);
+        linear(L + "ffn_output.weight", ff, F, tmp, cur);
+        check_cuda(layer_norm_ch(tmp, R1, H, c.W(L + "full_layer_layer_norm.weight").d,
+                                 c.W(L + "full_layer_layer_norm.bias").d, 0, 0.f, 1e-12f, r.B, cur, R1, 0, st),
+                   "layer norm launch");
+        c.n_launches += 4;
+    }
+    float *y = c.buf("al_y", (size_t)D * R1);
+    linear("kokopop.bert_encoder.weight", cur, H, y, nullptr);
+    rows_out(y, R1, D, r.B, r.d_cum, max_len, out, st);
     ++c.n_launches;
     check_cuda(cudaGetLastError(), "kernel launch");
 }
@@ -2095,6 +2240,41 @@ int kk_text_encoder_forward_device(kk_ctx *ctx, int32_t n_seqs, const int32_t *n
         use_device(ctx);
         cudaStream_t st = stream ? (cudaStream_t)stream : ctx->st;
         text_encoder_device(*ctx, n_seqs, n_tokens, ids, out, st);
+        return KK_OK;
+    });
+}
+
+int kk_albert_forward(kk_ctx *ctx, int32_t n_seqs, const int32_t *n_tokens, const int32_t *ids, float *out) {
+    return guarded([&] {
+        if (!ctx || !n_tokens || !ids || !out || n_seqs < 1) throw KKError(KK_ERROR_INVALID_ARGUMENT, "null argument");
+        use_device(ctx);
+        kk_ctx &c = *ctx;
+        const int64_t rows = token_rows(n_seqs, n_tokens);
+        if (!c.albert_ready) throw KKError(KK_ERROR_MODEL, "ALBERT weights incomplete, first missing: " + c.missing_albert);
+        const int64_t vocab = c.W("kokopop.albert.embeddings.word_embeddings.weight").ne[1];
+        for (int64_t i = 0; i < rows; ++i)
+            if (ids[i] < 0 || ids[i] >= vocab) throw KKError(KK_ERROR_INVALID_ARGUMENT, "token id out of range");
+        const int D = (int)c.W("kokopop.bert_encoder.weight").ne[1];
+        cudaStream_t st = c.st;
+        int32_t *d_ids = (int32_t *)c.buf("al_ids", (size_t)rows);
+        float *d_out = c.buf("al_out", (size_t)rows * D);
+        check_cuda(cudaMemcpyAsync(d_ids, ids, (size_t)rows * 4, cudaMemcpyHostToDevice, st), "upload ids");
+        albert_device(c, n_seqs, n_tokens, d_ids, d_out, st);
+        check_cuda(cudaMemcpyAsync(out, d_out, (size_t)rows * D * 4, cudaMemcpyDeviceToHost, st), "D2H");
+        check_cuda(cudaStreamSynchronize(st), "ALBERT");
+        check_device_error(ctx);
+        return KK_OK;
+    });
+}
+
+int kk_albert_forward_device(kk_ctx *ctx, int32_t n_seqs, const int32_t *n_tokens, const int32_t *ids, float *out,
+                             void *stream) {
+    return guarded([&] {
+        if (!ctx || !n_tokens || !ids || !out || n_seqs < 1) throw KKError(KK_ERROR_INVALID_ARGUMENT, "null argument");
+        token_rows(n_seqs, n_tokens);
+        use_device(ctx);
+        cudaStream_t st = stream ? (cudaStream_t)stream : ctx->st;
+        albert_device(*ctx, n_seqs, n_tokens, ids, out, st);
         return KK_OK;
     });
 }

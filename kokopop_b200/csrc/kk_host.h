@@ -118,6 +118,9 @@ struct kk_ctx {
     // its k = 5 convs: 0 CUDA cores (mixed types, or F32 without the split),
     // 1 tensor cores on F16 weights, 2 split F32 on the tensor cores
     int text_mode = 0;
+    bool albert_ready = false;  // ALBERT + bert_encoder
+    std::string missing_albert;
+    int albert_mode = 0;  // its linears, as text_mode
     kk::DevBuf convt_phase[2];
     bool convt_f16[2] = {false, false};
     // tensor-core path: every convolution weight is F16, or every one is F32

@@ -218,12 +218,24 @@ void pool_up_h(const float *x, __half *y, int64_t R_in, int64_t Ry_out, int C, c
 // kk_frontend.cu: the text encoder's embedding and LayerNorm, the duration
 // projection.
 constexpr int kErrTokenId = 31;  // device error word: a token id out of range
+// pos / type non-null (ALBERT): + the position row t and the token type row 0
 void embed(const float *emb, int C, int vocab, const int32_t *ids, const int64_t *cum, const Batch &b, float *X,
-           int64_t R, int *err, cudaStream_t st);
-// LayerNorm over C channels per token row + gamma / beta + LeakyReLU(slope);
-// lstm_B > 0 writes row t * lstm_B + u (the LSTM layout) instead of row q.
-void layer_norm_ch(const float *x, int64_t R, int C, const float *gamma, const float *beta, float slope,
-                   const Batch &b, float *y, int64_t R_out, int lstm_B, cudaStream_t st);
+           int64_t R, int *err, cudaStream_t st, const float *pos = nullptr, const float *type = nullptr);
+// LayerNorm (eps) over C channels per token row + gamma / beta, then
+// LeakyReLU(slope) when leaky_on; lstm_B > 0 writes row t * lstm_B + u (the
+// LSTM layout) instead of row q. y may be x.
+// (C <= 1024)
+cudaError_t layer_norm_ch(const float *x, int64_t R, int C, const float *gamma, const float *beta, int leaky_on,
+                          float slope, float eps, const Batch &b, float *y, int64_t R_out, int lstm_B,
+                          cudaStream_t st);
+// ALBERT self-attention: qkv [3 H][R] -> out [H][R], heads of 64, at most
+// 512 tokens per sequence
+cudaError_t attention(const float *qkv, int64_t R, int H, int n_heads, int max_len, const Batch &b, float scale,
+                      float *out, cudaStream_t st);
+void gelu(float *x, int64_t n, cudaStream_t st);
+// packed level-1 [C][R] -> token-major [sum T][C]
+void rows_out(const float *x, int64_t R, int C, const Batch &b, const int64_t *cum, int max_len, float *out,
+              cudaStream_t st);
 // durations[cum[s] + t] from h(r, k) = h[r * s_row + k * s_k], r = t * B + s
 // (P <= 1024 inputs, NB <= 64 buckets)
 cudaError_t duration_proj(const float *h, int64_t s_row, int64_t s_k, int P, const float *w, const float *bias,

@@ -199,6 +199,50 @@ def duration_head_spec() -> List[Tuple[str, Tuple[int, ...]]]:
     ]
 
 
+ALBERT_EMBED = 128
+ALBERT_HIDDEN = 768
+ALBERT_FFN = 2048
+ALBERT_POSITIONS = 512
+
+
+def albert_spec() -> List[Tuple[str, Tuple[int, ...]]]:
+    """ALBERT (embed 128, hidden 768, one shared layer of 12 heads, FFN 2048)
+    and bert_encoder 768 -> 512 (kokoro.cpp:52-81, :213-224)."""
+    e = "kokopop.albert.embeddings"
+    lay = "kokopop.albert.encoder.albert_layer_groups.0.albert_layers.0"
+    E, H, F = ALBERT_EMBED, ALBERT_HIDDEN, ALBERT_FFN
+    spec: List[Tuple[str, Tuple[int, ...]]] = [
+        (f"{e}.word_embeddings.weight", (E, VOCAB)),
+        (f"{e}.position_embeddings.weight", (E, ALBERT_POSITIONS)),
+        (f"{e}.token_type_embeddings.weight", (E, 2)),
+        (f"{e}.LayerNorm.weight", (E,)),
+        (f"{e}.LayerNorm.bias", (E,)),
+        ("kokopop.albert.encoder.embedding_hidden_mapping_in.weight", (E, H)),
+        ("kokopop.albert.encoder.embedding_hidden_mapping_in.bias", (H,)),
+        ("kokopop.bert_encoder.weight", (H, HIDDEN)),
+        ("kokopop.bert_encoder.bias", (HIDDEN,)),
+    ]
+    for n in ("query", "key", "value", "dense"):
+        spec += [(f"{lay}.attention.{n}.weight", (H, H)), (f"{lay}.attention.{n}.bias", (H,))]
+    spec += [
+        (f"{lay}.attention.LayerNorm.weight", (H,)),
+        (f"{lay}.attention.LayerNorm.bias", (H,)),
+        (f"{lay}.ffn.weight", (H, F)),
+        (f"{lay}.ffn.bias", (F,)),
+        (f"{lay}.ffn_output.weight", (F, H)),
+        (f"{lay}.ffn_output.bias", (H,)),
+        (f"{lay}.full_layer_layer_norm.weight", (H,)),
+        (f"{lay}.full_layer_layer_norm.bias", (H,)),
+    ]
+    return spec
+
+
+def albert_weights(f16: bool = False) -> Dict[str, Tensor]:
+    """ALBERT + bert_encoder weights: seed 2, N(0, 0.02) (config 2's draw),
+    F16 under the converter's policy when f16, else F32."""
+    return make_weights(albert_spec(), seed=2, dist="normal", scale=0.02, f16=f16)
+
+
 def frontend_weights(f16: bool = False) -> Dict[str, Tensor]:
     """Text encoder + duration head weights: seed 2, N(0, 0.02) (config 2's
     draw), F16 under the converter's policy when f16, else F32."""

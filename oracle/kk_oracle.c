@@ -1276,6 +1276,155 @@ int kko_duration_head(kko_model *m, int64_t N, const float *d, float *durations)
     return rc;
 }
 
+/* ---- ALBERT (kokoro.cpp:279-337) ---- */
+
+/* layer_norm (graph_ops.cpp:622-634): ggml_norm over the D features of each
+ * of the N rows of x [N, D] (feature-fastest), * w, + b, in place. */
+static void layer_norm_rows(float *x, int64_t N, int64_t D, const ko_tensor *w, const ko_tensor *b, float eps) {
+    float *y = fbuf((size_t)D);
+    for (int64_t t = 0; t < N; ++t) {
+        float *r = x + t * D;
+        kko_norm_time(r, 1, D, eps, y);
+        for (int64_t c = 0; c < D; ++c) {
+            float v = y[c] * w->data[c];
+            r[c] = v + b->data[c];
+        }
+    }
+    free(y);
+}
+
+/* ggml semantics, ggml_gelu on F32 (ggml-cpu, GGML_GELU_FP16): 0 for
+ * x <= -10, x for x >= 10, else the F16 table entry of half(x): the tanh
+ * approximation 0.5 x (1 + tanh(sqrt(2/pi) x (1 + 0.044715 x^2))) of the
+ * half value, rounded to half. tanh is taken correctly rounded here (ggml's
+ * table holds the build machine's tanhf; the two differ at most in the
+ * table's last bit for a few entries). */
+static float gelu_ggml(float x) {
+    if (x <= -10.0f) return 0.0f;
+    if (x >= 10.0f) return x;
+    const float h = kko_round_f16(x);
+    const float a = 0.79788456080286535587989211986876f * h;
+    const float inner = a * (1.0f + (0.044715f * h) * h);
+    const float g = (0.5f * h) * (1.0f + cr_tanhf(inner));
+    return kko_round_f16(g);
+}
+
+/* ggml semantics, ggml_soft_max_ext(x, NULL, scale, 0) on one row of n:
+ * w = x * scale, m = max w, e = exp(w - m) with the sum in double, then
+ * e * (float)(1 / sum). exp is taken correctly rounded (ggml's CPU path uses
+ * its own vectorised exp approximation). */
+static void softmax_row(float *x, int64_t n, float scale) {
+    float mx = -INFINITY;
+    for (int64_t i = 0; i < n; ++i) {
+        x[i] = x[i] * scale;
+        if (x[i] > mx) mx = x[i];
+    }
+    double sum = 0.0;
+    for (int64_t i = 0; i < n; ++i) {
+        x[i] = (float)exp((double)(x[i] - mx));
+        sum += (double)x[i];
+    }
+    const float inv = (float)(1.0 / sum);
+    for (int64_t i = 0; i < n; ++i) x[i] *= inv;
+}
+
+static const ko_tensor *albert_req(kko_model *m, const char *suffix) {
+    char k[256];
+    snprintf(k, sizeof k, "kokopop.albert.encoder.albert_layer_groups.0.albert_layers.0.%s", suffix);
+    return req(m, k);
+}
+
+/* Embeddings (word + position, + token type 0), LayerNorm (eps 1e-12), the
+ * 128 -> 768 mapping, twelve passes of the shared layer (12 heads of 64,
+ * scores k . q in F32 scaled by 1/8, softmax over the keys, the weighted sum
+ * of v, dense + residual -> LayerNorm, ffn -> GELU -> ffn_output + residual
+ * -> LayerNorm), then bert_encoder 768 -> 512. Every linear rounds its input
+ * to half for an F16 weight (linear_vec); the attention products are F32. */
+int kko_albert(kko_model *m, int64_t N, const int32_t *ids, float *out) {
+    g_err[0] = 0;
+    const ko_tensor *word = req(m, "kokopop.albert.embeddings.word_embeddings.weight");
+    const ko_tensor *pos = req(m, "kokopop.albert.embeddings.position_embeddings.weight");
+    const ko_tensor *type = req(m, "kokopop.albert.embeddings.token_type_embeddings.weight");
+    const ko_tensor *enw = req(m, "kokopop.albert.embeddings.LayerNorm.weight");
+    const ko_tensor *enb = req(m, "kokopop.albert.embeddings.LayerNorm.bias");
+    const ko_tensor *mapw = req(m, "kokopop.albert.encoder.embedding_hidden_mapping_in.weight");
+    const ko_tensor *mapb = req(m, "kokopop.albert.encoder.embedding_hidden_mapping_in.bias");
+    const ko_tensor *encw = req(m, "kokopop.bert_encoder.weight");
+    const ko_tensor *encb = req(m, "kokopop.bert_encoder.bias");
+    const ko_tensor *qw = albert_req(m, "attention.query.weight"), *qb = albert_req(m, "attention.query.bias");
+    const ko_tensor *kw = albert_req(m, "attention.key.weight"), *kb = albert_req(m, "attention.key.bias");
+    const ko_tensor *vw = albert_req(m, "attention.value.weight"), *vb = albert_req(m, "attention.value.bias");
+    const ko_tensor *ow = albert_req(m, "attention.dense.weight"), *ob = albert_req(m, "attention.dense.bias");
+    const ko_tensor *anw = albert_req(m, "attention.LayerNorm.weight");
+    const ko_tensor *anb = albert_req(m, "attention.LayerNorm.bias");
+    const ko_tensor *fw = albert_req(m, "ffn.weight"), *fb = albert_req(m, "ffn.bias");
+    const ko_tensor *f2w = albert_req(m, "ffn_output.weight"), *f2b = albert_req(m, "ffn_output.bias");
+    const ko_tensor *onw = albert_req(m, "full_layer_layer_norm.weight");
+    const ko_tensor *onb = albert_req(m, "full_layer_layer_norm.bias");
+    if (!word || !pos || !type || !enw || !enb || !mapw || !mapb || !encw || !encb || !qw || !qb || !kw || !kb ||
+        !vw || !vb || !ow || !ob || !anw || !anb || !fw || !fb || !f2w || !f2b || !onw || !onb)
+        return -1;
+    const int64_t E = word->ne[0], V = word->ne[1], H = mapw->ne[1], F = fw->ne[1], D = encw->ne[1];
+    const int64_t NH = 12, HS = H / NH;
+    if (N < 1 || N > pos->ne[1]) return fail("ALBERT sequence length out of range%s", "");
+    for (int64_t t = 0; t < N; ++t)
+        if (ids[t] < 0 || ids[t] >= V) return fail("token id out of range%s", "");
+    float *e = fbuf((size_t)(N * E)), *cur = fbuf((size_t)(N * H)), *q = fbuf((size_t)(N * H));
+    float *k = fbuf((size_t)(N * H)), *v = fbuf((size_t)(N * H)), *att = fbuf((size_t)(N * H));
+    float *o = fbuf((size_t)(N * H)), *ff = fbuf((size_t)(N * F)), *sc = fbuf((size_t)N);
+    for (int64_t t = 0; t < N; ++t)
+        for (int64_t c = 0; c < E; ++c) {
+            const float a = word->data[(int64_t)ids[t] * E + c] + pos->data[t * E + c];
+            e[t * E + c] = a + type->data[c];
+        }
+    layer_norm_rows(e, N, E, enw, enb, 1e-12f);
+    for (int64_t t = 0; t < N; ++t) linear_vec(mapw, mapb, e + t * E, cur + t * H);
+    for (int r = 0; r < 12; ++r) {
+        for (int64_t t = 0; t < N; ++t) {
+            linear_vec(qw, qb, cur + t * H, q + t * H);
+            linear_vec(kw, kb, cur + t * H, k + t * H);
+            linear_vec(vw, vb, cur + t * H, v + t * H);
+        }
+        for (int64_t h = 0; h < NH; ++h)
+            for (int64_t qi = 0; qi < N; ++qi) {
+                for (int64_t ki = 0; ki < N; ++ki) {
+                    float acc = 0.f;
+                    for (int64_t d = 0; d < HS; ++d) acc += k[ki * H + h * HS + d] * q[qi * H + h * HS + d];
+                    sc[ki] = acc;
+                }
+                softmax_row(sc, N, 0.125f);
+                for (int64_t d = 0; d < HS; ++d) {
+                    float acc = 0.f;
+                    for (int64_t ki = 0; ki < N; ++ki) acc += sc[ki] * v[ki * H + h * HS + d];
+                    att[qi * H + h * HS + d] = acc;
+                }
+            }
+        for (int64_t t = 0; t < N; ++t) {
+            linear_vec(ow, ob, att + t * H, o + t * H);
+            for (int64_t c = 0; c < H; ++c) cur[t * H + c] = o[t * H + c] + cur[t * H + c];
+        }
+        layer_norm_rows(cur, N, H, anw, anb, 1e-12f);
+        for (int64_t t = 0; t < N; ++t) {
+            linear_vec(fw, fb, cur + t * H, ff + t * F);
+            for (int64_t c = 0; c < F; ++c) ff[t * F + c] = gelu_ggml(ff[t * F + c]);
+            linear_vec(f2w, f2b, ff + t * F, o + t * H);
+            for (int64_t c = 0; c < H; ++c) cur[t * H + c] = o[t * H + c] + cur[t * H + c];
+        }
+        layer_norm_rows(cur, N, H, onw, onb, 1e-12f);
+    }
+    for (int64_t t = 0; t < N; ++t) linear_vec(encw, encb, cur + t * H, out + t * D);
+    free(e);
+    free(cur);
+    free(q);
+    free(k);
+    free(v);
+    free(att);
+    free(o);
+    free(ff);
+    free(sc);
+    return 0;
+}
+
 static int duration_to_frames(float value, float speed) {
     if (!isfinite(speed) || speed <= 0.0f) speed = 1.0f;
     const float v = value / speed;

@@ -124,6 +124,14 @@ int kko_duration_head(kko_model *m, int64_t N, const float *d, float *durations)
  * (P = the projection's input size). */
 int kko_duration_proj(kko_model *m, int64_t N, const float *h, float *durations);
 
+/* ---- ALBERT + bert_encoder (kokoro.cpp:279-337) ----
+ * ids: [N] token ids (positions 0..N-1, token type 0); out: [N, 512]
+ * feature-fastest, the bert_encoder output that the duration encoder
+ * reads. PARITY UNPINNED: ggml_gelu, ggml_soft_max_ext and ggml_norm are
+ * restated from the public ggml CPU source (v0.28.0, not in the reference
+ * tree); exp and tanh are taken correctly rounded (see kk_oracle.c). */
+int kko_albert(kko_model *m, int64_t N, const int32_t *ids, float *out);
+
 /* Single-op entry points used by the unit tests. */
 void kko_norm_time(const float *x, int64_t C, int64_t L, float eps, float *y);
 float kko_round_f16(float x);

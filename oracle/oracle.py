@@ -194,6 +194,14 @@ class OracleModel:
                                             ids.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), _ptr(out)))
         return out
 
+    def albert(self, ids: np.ndarray):
+        """kko_albert: token ids [N] -> [N, 512] (ALBERT + bert_encoder)."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        out = np.zeros((len(ids), 512), np.float32)
+        self._check(self.L.kko_albert(ctypes.c_void_p(self.h), ctypes.c_int64(len(ids)),
+                                      ids.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), _ptr(out)))
+        return out
+
     def duration_head(self, d: np.ndarray):
         """kko_duration_head: the duration encoder output [N, 640] -> durations [N]."""
         d = np.ascontiguousarray(d, dtype=np.float32)

@@ -252,3 +252,15 @@ def test_text_encoder_and_duration_head_shapes_and_determinism():
     assert du.shape == (32,) and np.all((du > 0) & (du < 50))
     with pytest.raises(RuntimeError):
         m.text_encoder(np.array([0, 178], np.int32))
+
+
+def test_albert_restatement_runs():
+    """ALBERT + bert_encoder: finite [N, 512] output, deterministic, bad ids
+    rejected (the restatement is unpinned: no reference fixtures exist)."""
+    m = O.OracleModel(W.albert_weights(f16=True))
+    ids = W.token_ids(np.random.default_rng(4), 6)
+    a, b = m.albert(ids), m.albert(ids)
+    assert a.shape == (8, 512) and np.isfinite(a).all()
+    np.testing.assert_array_equal(a, b)
+    with pytest.raises(RuntimeError):
+        m.albert(np.array([0, 500], np.int32))
