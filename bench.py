@@ -263,6 +263,57 @@ def bench_prosody(kb, W, device, runs, pool, batch):
             "audio_s_per_s": rows / 40.0 / (ms / 1e3)}
 
 
+def bench_frontend(kb, W, device, runs):
+    """Config 2's front end for one utterance of 128 phoneme ids (130 with the
+    pads), F16 weights seed 2, device-resident, each stage timed with CUDA
+    events on the launch stream: ALBERT + bert_encoder, the duration encoder,
+    the duration head (predictor biLSTM + projection), the text encoder; ms
+    per call (median of `runs`)."""
+    import statistics
+    import torch
+    c = kb.Context(device)
+    c.upload(W.config2_frontend_weights())
+    ids = W.token_ids(np.random.default_rng(7), 128)
+    lens = np.array([len(ids)], np.int32)
+    n = int(lens[0])
+    g = torch.Generator(device="cuda").manual_seed(103)
+    d_ids = torch.from_numpy(ids).cuda()
+    style = 0.1 * torch.randn(1, 128, device="cuda", generator=g)
+    bert = torch.empty(n, 512, device="cuda")
+    d = torch.empty(n, 640, device="cuda")
+    dur = torch.empty(n, device="cuda")
+    ten = torch.empty(n, 512, device="cuda")
+    stream = torch.cuda.Stream()
+    stages = {
+        "albert_ms": lambda: c.albert_device(lens, d_ids.data_ptr(), bert.data_ptr(), stream.cuda_stream),
+        "duration_encoder_ms": lambda: c.duration_encoder_device(lens, bert.data_ptr(), style.data_ptr(),
+                                                                 d.data_ptr(), stream.cuda_stream),
+        "duration_head_ms": lambda: c.duration_head_device(lens, d.data_ptr(), dur.data_ptr(), stream.cuda_stream),
+        "text_encoder_ms": lambda: c.text_encoder_device(lens, d_ids.data_ptr(), ten.data_ptr(), stream.cuda_stream),
+    }
+    for f in stages.values():
+        f()
+        f()
+    torch.cuda.synchronize()
+    out = {"workload": "config-2 front end, one utterance of 128 phoneme ids + 2 pads, F16 weights seed 2",
+           "tokens": n}
+    total = 0.0
+    for k, f in stages.items():
+        ts = []
+        for _ in range(runs):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            f()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        out[k] = statistics.median(ts)
+        total += out[k]
+    out["total_ms"] = total
+    c.close()
+    return out
+
+
 def config_dict(batch=BATCH):
     return {
         "workload": "Kokoro-82M decoder (AdainResBlk1d encode/decode) + ISTFTNet generator + iSTFT; "
@@ -284,6 +335,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg (profiling cases)")
     ap.add_argument("--lstm-runs", type=int, default=5, help="timed calls per LSTM-stack case (0 skips)")
     ap.add_argument("--prosody-runs", type=int, default=3, help="timed calls of the prosody F0/N chain (0 skips)")
+    ap.add_argument("--frontend-runs", type=int, default=5, help="timed calls per front-end stage (0 skips)")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
@@ -451,6 +503,9 @@ def main():
     prosody = None
     if rank == 0 and args.prosody_runs > 0:
         prosody = bench_prosody(kb, W, local, args.prosody_runs, pool, args.batch)
+    frontend = None
+    if rank == 0 and args.frontend_runs > 0:
+        frontend = bench_frontend(kb, W, local, args.frontend_runs)
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
             sample = cpu_sample(pool)
@@ -484,6 +539,7 @@ def main():
         "ttfa_p50_ms": ttfa,
         "lstm": lstm,
         "prosody": prosody,
+        "frontend": frontend,
         "pipeline_tflops": value / world * algorithmic_flop_per_asr_frame() * 40.0 / 1e12,
     }
     if rank == 0:

@@ -249,6 +249,14 @@ def frontend_weights(f16: bool = False) -> Dict[str, Tensor]:
     return make_weights(text_encoder_spec() + duration_head_spec(), seed=2, dist="normal", scale=0.02, f16=f16)
 
 
+def config2_frontend_weights() -> Dict[str, Tensor]:
+    """Config 2's front end up to the durations and t_en: ALBERT +
+    bert_encoder, the duration encoder, the duration head and the text
+    encoder, seed 2, N(0, 0.02), F16 under the converter's policy."""
+    spec = albert_spec() + duration_encoder_spec() + duration_head_spec() + text_encoder_spec()
+    return make_weights(spec, seed=2, dist="normal", scale=0.02, f16=True)
+
+
 def token_ids(rng: np.random.Generator, n: int) -> np.ndarray:
     """n phoneme ids uniform over 1..177 wrapped in the pad id 0 (n + 2 ids)."""
     return np.concatenate([[0], rng.integers(1, VOCAB, size=n), [0]]).astype(np.int32)
