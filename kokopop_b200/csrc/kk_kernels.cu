@@ -607,71 +607,86 @@ void f0n_conv(const float *in, int64_t R_in, float *out0, float *out1, int64_t R
 // path). tanh, sin and cos are the correctly rounded float values (double
 // evaluation, rounded once): the generator output depends on the last bit of
 // the source through the phases of near-silent STFT bins, and only the
-// correctly rounded values are reproducible across implementations. Per utterance one warp: lanes 0..8 each carry one harmonic's phasor
-// sequentially through all voiced segments (rotation by (cos d, sin d) with
-// each product rounded separately), stage the 300 new sines of a segment in
-// shared memory, then all 32 lanes form merged = b + sum_h w_h * 0.1 * sin_h
-// in harmonic order and tanh it. Unvoiced segments (f0 <= 10) hold
-// tanh(b) (computed once on the host) and leave the phases untouched. The phasors are renormalised every 16 voiced
-// segments.
+// correctly rounded values are reproducible across implementations. Lanes
+// 0..8 each carry one harmonic's phasor sequentially through all voiced
+// segments (rotation by (cos d, sin d) with each product rounded
+// separately) and stage the 300 new sines of a segment in shared memory;
+// merged = b + sum_h w_h * 0.1 * sin_h is formed in harmonic order and
+// tanh'd. Unvoiced segments (f0 <= 10) hold tanh(b) (computed once on the
+// host) and leave the phases untouched. The phasors are renormalised after
+// every voiced segment whose index + 1 is a multiple of 16.
 // ---------------------------------------------------------------------------
 
-__global__ void __launch_bounds__(32) k_sinegen(const float *__restrict__ f0, int mf,
-                                                float *__restrict__ source, Batch b,
-                                                const int64_t *__restrict__ cumT, SineArgs a) {
-    __shared__ float sbuf[kHarmonics][kUpsample];
+// One block of 4 warps per utterance, the segments pipelined: in step s,
+// warp 0 carries the 9 phasors (lanes 0..8) through segment s into one half
+// of a double buffer while warps 1..3 merge segment s - 1 from the other
+// half; one block barrier per step. The arithmetic and its order are those
+// of a single warp doing both in turn.
+constexpr int kSineThreads = 128;
+
+__global__ void __launch_bounds__(kSineThreads) k_sinegen(const float *__restrict__ f0, int mf,
+                                                          float *__restrict__ source, Batch b,
+                                                          const int64_t *__restrict__ cumT, SineArgs a) {
+    __shared__ float sbuf[2][kHarmonics][kUpsample];
     const int u = blockIdx.x;
-    const int lane = threadIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t nseg = (int64_t)mf * b.T[u];
     const float *fp = f0 + (int64_t)mf * b.offT[u];
     float *src = source + (int64_t)kUpsample * mf * cumT[u];
     float ps = 0.f, pc = 1.f;
-    const bool chain = lane < kHarmonics;
-    const float mws = chain ? a.mw_scaled[lane] : 0.f;
-    for (int64_t seg = 0; seg < nseg; ++seg) {
-        const float base_f0 = fp[seg];
-        float *out = src + seg * kUpsample;
-        if (base_f0 > 10.0f) {
-            if (chain) {
-                // delta = (float)(2 pi f0 (h+1) / 24000) evaluated in double
-                const float delta = (float)(2.0 * 3.14159265358979323846 * (double)base_f0 *
-                                            (double)(lane + 1) / 24000.0);
-                const float sd = (float)sin((double)delta);
-                const float cd = (float)cos((double)delta);
-                for (int j = 0; j < kUpsample; ++j) {
-                    const float ns = __fadd_rn(__fmul_rn(ps, cd), __fmul_rn(pc, sd));
-                    const float nc = __fsub_rn(__fmul_rn(pc, cd), __fmul_rn(ps, sd));
-                    ps = ns;
-                    pc = nc;
-                    sbuf[lane][j] = ns;
-                }
-                if ((seg + 1) % 16 == 0) {
-                    const float norm = __fsqrt_rn(__fadd_rn(__fmul_rn(ps, ps), __fmul_rn(pc, pc)));
-                    if (norm > 0.0f) {
-                        ps = __fdiv_rn(ps, norm);
-                        pc = __fdiv_rn(pc, norm);
+    const bool chain = warp == 0 && lane < kHarmonics;
+    for (int64_t step = 0; step <= nseg; ++step) {
+        if (warp == 0) {
+            // the phasors through segment `step`
+            if (step < nseg && chain) {
+                const float base_f0 = fp[step];
+                if (base_f0 > 10.0f) {
+                    // delta = (float)(2 pi f0 (h+1) / 24000) evaluated in double
+                    const float delta = (float)(2.0 * 3.14159265358979323846 * (double)base_f0 *
+                                                (double)(lane + 1) / 24000.0);
+                    const float sd = (float)sin((double)delta);
+                    const float cd = (float)cos((double)delta);
+                    float *row = sbuf[step & 1][lane];
+                    for (int j = 0; j < kUpsample; ++j) {
+                        const float ns = __fadd_rn(__fmul_rn(ps, cd), __fmul_rn(pc, sd));
+                        const float nc = __fsub_rn(__fmul_rn(pc, cd), __fmul_rn(ps, sd));
+                        ps = ns;
+                        pc = nc;
+                        row[j] = ns;
+                    }
+                    if ((step + 1) % 16 == 0) {
+                        const float norm = __fsqrt_rn(__fadd_rn(__fmul_rn(ps, ps), __fmul_rn(pc, pc)));
+                        if (norm > 0.0f) {
+                            ps = __fdiv_rn(ps, norm);
+                            pc = __fdiv_rn(pc, norm);
+                        }
                     }
                 }
             }
-            __syncwarp();
-            for (int j = lane; j < kUpsample; j += 32) {
-                float merged = a.mb;
+        } else if (step > 0) {
+            // segment step - 1: merged = b + sum_h w_h * 0.1 * sin_h in
+            // harmonic order, tanh; unvoiced segments hold tanh(b)
+            const int64_t seg = step - 1;
+            float *out = src + seg * kUpsample;
+            if (fp[seg] > 10.0f) {
+                const float(*sb)[kUpsample] = sbuf[seg & 1];
+                for (int j = tid - 32; j < kUpsample; j += kSineThreads - 32) {
+                    float merged = a.mb;
 #pragma unroll
-                for (int h = 0; h < kHarmonics; ++h)
-                    merged = __fadd_rn(merged, __fmul_rn(a.mw_scaled[h], sbuf[h][j]));
-                out[j] = (float)tanh((double)merged);
+                    for (int h = 0; h < kHarmonics; ++h) merged = __fadd_rn(merged, __fmul_rn(a.mw_scaled[h], sb[h][j]));
+                    out[j] = (float)tanh((double)merged);
+                }
+            } else {
+                for (int j = tid - 32; j < kUpsample; j += kSineThreads - 32) out[j] = a.unvoiced;
             }
-            __syncwarp();
-        } else {
-            for (int j = lane; j < kUpsample; j += 32) out[j] = a.unvoiced;
         }
+        __syncthreads();
     }
-    (void)mws;
 }
 
 void sinegen(const float *f0, int mf, float *source, const Batch &b, const int64_t *cumT,
              const SineArgs &a, cudaStream_t st) {
-    k_sinegen<<<b.n, 32, 0, st>>>(f0, mf, source, b, cumT, a);
+    k_sinegen<<<b.n, kSineThreads, 0, st>>>(f0, mf, source, b, cumT, a);
 }
 
 // Forward STFT of the source (audio_utils.cpp:381-419): Hann-20 window, hop
