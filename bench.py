@@ -314,6 +314,31 @@ def bench_frontend(kb, W, device, runs):
     return out
 
 
+def bench_queue(kb, device, weights, pool, batch):
+    """The rank's pool through the batching queue (one worker on a second
+    context of this GPU, max_batch = the bench batch, 2 ms batching wait): all
+    chunks submitted at once from the host, wall time until the last result is
+    in host memory; audio-s/s and the batches formed."""
+    ctx = kb.Context(device)
+    ctx.upload(weights)
+    q = kb.Queue(contexts=[ctx], max_batch=batch, max_batch_frames=batch * 800, max_wait_us=2000)
+    try:
+        t0 = time.perf_counter()
+        tickets = [q.submit(i, u) for i, u in enumerate(pool)]
+        for t in tickets:
+            rc, _ = q.wait(t, 600000)
+            if rc != 0:
+                raise RuntimeError(f"queue result {rc}")
+        wall = time.perf_counter() - t0
+        st = q.stats()
+    finally:
+        q.close()
+        ctx.close()
+    secs = sum(u.T for u in pool) / 40.0
+    return {"workload": f"{len(pool)} utterances of the pool submitted at once, one worker, max batch {batch}",
+            "value": secs / wall, "unit": UNIT, "wall_s": wall, "batches": st["batches"], "max_batch": st["max_batch"]}
+
+
 def config_dict(batch=BATCH):
     return {
         "workload": "Kokoro-82M decoder (AdainResBlk1d encode/decode) + ISTFTNet generator + iSTFT; "
@@ -336,6 +361,7 @@ def main():
     ap.add_argument("--lstm-runs", type=int, default=5, help="timed calls per LSTM-stack case (0 skips)")
     ap.add_argument("--prosody-runs", type=int, default=3, help="timed calls of the prosody F0/N chain (0 skips)")
     ap.add_argument("--frontend-runs", type=int, default=5, help="timed calls per front-end stage (0 skips)")
+    ap.add_argument("--no-queue", action="store_true", help="skip the batching-queue leg")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
@@ -503,6 +529,9 @@ def main():
     prosody = None
     if rank == 0 and args.prosody_runs > 0:
         prosody = bench_prosody(kb, W, local, args.prosody_runs, pool, args.batch)
+    queue = None
+    if rank == 0 and not args.no_queue:
+        queue = bench_queue(kb, local, weights, [pool[i] for idx in batches for i in idx], args.batch)
     frontend = None
     if rank == 0 and args.frontend_runs > 0:
         frontend = bench_frontend(kb, W, local, args.frontend_runs)
@@ -540,6 +569,7 @@ def main():
         "lstm": lstm,
         "prosody": prosody,
         "frontend": frontend,
+        "queue": queue,
         "pipeline_tflops": value / world * algorithmic_flop_per_asr_frame() * 40.0 / 1e12,
     }
     if rank == 0:

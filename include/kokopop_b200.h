@@ -215,6 +215,64 @@ int kk_duration_head_forward_device(kk_ctx *ctx, int32_t n_seqs, const int32_t *
  * [n_rows]; at most 65536 rows. Host buffers. */
 int kk_duration_proj(kk_ctx *ctx, int64_t n_rows, const float *h, float *durations);
 
+/* ---- Batching request queue (the per-GPU counterpart of the reference's
+ * SynthesisScheduler, src/http/synthesis_scheduler.cpp:15-209, which runs
+ * one chunk of one request at a time, round-robin over the requests) ----
+ * Workers (one per GPU context, or per caller executor) each run a ragged
+ * batch per call: the oldest pending chunk of each request, in arrival
+ * order, at most max_batch chunks and max_batch_frames frames, after waiting
+ * up to max_wait_us from the oldest chunk's arrival for the batch to fill. A
+ * request has at most one chunk dispatched at a time, so its chunks finish
+ * in submission order. Results: KK_* statuses, or these. */
+enum { KK_QUEUE_PENDING = -1, KK_QUEUE_CANCELLED = -2 };
+
+typedef struct kk_queue kk_queue;
+
+/* A batch executor with the arguments of kk_decoder_forward (host buffers);
+ * returns a KK_* status. Called from the queue's worker threads. */
+typedef int (*kk_queue_exec_fn)(void *user, int32_t n_utts, const int32_t *n_frames, const float *asr,
+                                const float *f0, const float *noise, const float *style, float *audio);
+
+/* One worker per context (each with the decoder weights uploaded, used by
+ * that worker only while the queue lives). The worker stages a batch in
+ * pinned memory and runs it with kk_decoder_forward_device on its own
+ * stream, packing the next batch while the GPU runs. */
+int kk_queue_create(kk_ctx *const *ctxs, int32_t n_ctx, int32_t max_batch, int64_t max_batch_frames,
+                    int32_t max_wait_us, kk_queue **out);
+
+/* One worker per users[i] (NULL users: n_workers workers with user NULL),
+ * each calling fn(users[i], ...) for its batches. */
+int kk_queue_create_exec(kk_queue_exec_fn fn, void *const *users, int32_t n_workers, int32_t max_batch,
+                         int64_t max_batch_frames, int32_t max_wait_us, kk_queue **out);
+
+/* Queues one decoder chunk of request `request` (any caller-chosen id):
+ * asr [T, 512], f0 / noise [2 T], style [128], audio [600 T], as for
+ * kk_decoder_forward; the buffers stay the caller's and must stay valid
+ * until the ticket's result is returned. 1 <= T <= min(8192,
+ * max_batch_frames). Thread-safe. */
+int kk_queue_submit(kk_queue *q, uint64_t request, int32_t n_frames, const float *asr, const float *f0,
+                    const float *noise, const float *style, float *audio, uint64_t *ticket);
+
+/* Waits up to timeout_ms (< 0: without limit) for a ticket. Returns
+ * KK_QUEUE_PENDING on timeout; otherwise the chunk's result (KK_OK, a
+ * KK_ERROR_*, or KK_QUEUE_CANCELLED), after which the ticket is forgotten
+ * (waiting on it again is KK_ERROR_INVALID_ARGUMENT). Thread-safe. */
+int kk_queue_wait(kk_queue *q, uint64_t ticket, int32_t timeout_ms);
+
+/* Cancels the chunks of `request` not yet dispatched (the reference's
+ * cancelled flag); *n_cancelled (optional) = how many. */
+int kk_queue_cancel(kk_queue *q, uint64_t request, int32_t *n_cancelled);
+
+/* Batches and chunks run so far, and the largest batch. */
+int kk_queue_stats(kk_queue *q, uint64_t *batches, uint64_t *jobs, uint64_t *max_batch_seen);
+
+/* Message of the last failed kk_queue_* call on this thread. */
+const char *kk_queue_last_error(void);
+
+/* Cancels the pending chunks, lets the dispatched batches finish and stops
+ * the workers. Call it once every kk_queue_wait has returned. */
+void kk_queue_destroy(kk_queue *q);
+
 /* Durations -> frames and the alignment (duration_to_frames,
  * src/arch/kokoro/kokoro.cpp:181-193; build_duration_mask :115-152 and
  * en = d . mask :669-674): frames[i] = clamp(int(lrint(d[i] / speed)), 1, 50)

@@ -8,6 +8,7 @@ fallback: without the library, or without a B200, every call raises.
 from __future__ import annotations
 
 import ctypes
+import threading
 import os
 from typing import Dict, List, Optional, Sequence
 
@@ -89,6 +90,19 @@ def load_library():
     L.kk_duration_proj.argtypes = [vp, ctypes.c_int64, _f32p, _f32p]
     L.kk_align_durations.argtypes = [vp, ctypes.c_int64, _f32p, ctypes.c_float, _i32p,
                                      ctypes.POINTER(ctypes.c_int64), _f32p, ctypes.c_int64, _f32p, ctypes.c_int64]
+    L.kk_queue_create.argtypes = [ctypes.POINTER(vp), ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, ctypes.c_int32,
+                                  ctypes.POINTER(vp)]
+    L.kk_queue_create_exec.argtypes = [QUEUE_EXEC_FN, ctypes.POINTER(vp), ctypes.c_int32, ctypes.c_int32,
+                                       ctypes.c_int64, ctypes.c_int32, ctypes.POINTER(vp)]
+    L.kk_queue_submit.argtypes = [vp, ctypes.c_uint64, ctypes.c_int32, _f32p, _f32p, _f32p, _f32p, _f32p,
+                                  ctypes.POINTER(ctypes.c_uint64)]
+    L.kk_queue_wait.argtypes = [vp, ctypes.c_uint64, ctypes.c_int32]
+    L.kk_queue_cancel.argtypes = [vp, ctypes.c_uint64, ctypes.POINTER(ctypes.c_int32)]
+    L.kk_queue_stats.argtypes = [vp, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64),
+                                 ctypes.POINTER(ctypes.c_uint64)]
+    L.kk_queue_last_error.restype = ctypes.c_char_p
+    L.kk_queue_destroy.argtypes = [vp]
+    L.kk_queue_destroy.restype = None
     L.kk_profile_enable.argtypes = [vp, ctypes.c_int]
     L.kk_profile_read.argtypes = [vp, ctypes.POINTER(Profile), ctypes.c_int]
     _lib = L
@@ -100,6 +114,15 @@ def declared_symbols() -> List[str]:
     import re
     src = open(HEADER).read()
     return sorted(set(re.findall(r"\b(kk_[a-z0-9_]+)\s*\(", src)))
+
+
+# kk_queue_exec_fn
+QUEUE_EXEC_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_int32, ctypes.POINTER(ctypes.c_int32),
+                                 ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_float),
+                                 ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_float),
+                                 ctypes.POINTER(ctypes.c_float))
+QUEUE_PENDING = -1
+QUEUE_CANCELLED = -2
 
 
 def _ptr(a: Optional[np.ndarray], t=_f32p):
@@ -328,3 +351,80 @@ class Context:
         self._check(self.L.kk_align_durations(self.h, n, _ptr(d), speed, _ptr(frames, _i32p), ctypes.byref(total),
                                               _ptr(hidden), hidden.shape[1], _ptr(en), cap))
         return frames[:n], total.value, en[: total.value]
+
+
+class Queue:
+    """kk_queue: batches decoder chunks from any number of threads onto the
+    workers (one per Context, or `n_workers` calling `executor`). A chunk is
+    a workload.Utterance-like object (asr [T, 512] time-fastest as in
+    workload.pack, f0, noise, style); results come back by ticket."""
+
+    def __init__(self, contexts: Optional[Sequence["Context"]] = None, executor=None, n_workers: int = 1,
+                 max_batch: int = 64, max_batch_frames: int = 64 * 800, max_wait_us: int = 2000):
+        self.L = load_library()
+        self.h = ctypes.c_void_p()
+        self._keep = {}
+        self._lock = threading.Lock()
+        if contexts is not None:
+            arr = (ctypes.c_void_p * len(contexts))(*[c.h.value for c in contexts])
+            rc = self.L.kk_queue_create(arr, len(contexts), max_batch, max_batch_frames, max_wait_us,
+                                        ctypes.byref(self.h))
+        else:
+            def call(user, n, T, asr, f0, noise, style, audio):
+                try:
+                    t = np.ctypeslib.as_array(T, shape=(n,)).copy()
+                    fr = int(t.sum())
+                    return int(executor(t, np.ctypeslib.as_array(asr, shape=(fr * 512,)),
+                                        np.ctypeslib.as_array(f0, shape=(2 * fr,)),
+                                        np.ctypeslib.as_array(noise, shape=(2 * fr,)),
+                                        np.ctypeslib.as_array(style, shape=(n * 128,)),
+                                        np.ctypeslib.as_array(audio, shape=(600 * fr,))))
+                except Exception:
+                    return 5
+            self._fn = QUEUE_EXEC_FN(call)
+            rc = self.L.kk_queue_create_exec(self._fn, None, n_workers, max_batch, max_batch_frames, max_wait_us,
+                                             ctypes.byref(self.h))
+        if rc != 0:
+            raise KKError(rc, self.L.kk_queue_last_error().decode())
+
+    def submit(self, request: int, u) -> int:
+        asr = np.ascontiguousarray(u.asr, np.float32)
+        f0 = np.ascontiguousarray(u.f0, np.float32)
+        noise = np.ascontiguousarray(u.noise, np.float32)
+        style = np.ascontiguousarray(u.style, np.float32)
+        audio = np.zeros(600 * int(u.T), np.float32)
+        ticket = ctypes.c_uint64()
+        with self._lock:
+            rc = self.L.kk_queue_submit(self.h, request, int(u.T), _ptr(asr), _ptr(f0), _ptr(noise), _ptr(style),
+                                        _ptr(audio), ctypes.byref(ticket))
+            if rc != 0:
+                raise KKError(rc, self.L.kk_queue_last_error().decode())
+            self._keep[ticket.value] = (asr, f0, noise, style, audio)
+        return ticket.value
+
+    def wait(self, ticket: int, timeout_ms: int = -1):
+        """(result, audio): result 0 (audio valid), a KK_ERROR_* code,
+        QUEUE_CANCELLED, or QUEUE_PENDING on timeout (audio None)."""
+        rc = self.L.kk_queue_wait(self.h, ticket, timeout_ms)
+        if rc == QUEUE_PENDING:
+            return rc, None
+        with self._lock:
+            bufs = self._keep.pop(ticket, None)
+        if rc == 1 and bufs is None:
+            raise KKError(rc, self.L.kk_queue_last_error().decode())
+        return rc, (bufs[4] if bufs is not None and rc == 0 else None)
+
+    def cancel(self, request: int) -> int:
+        n = ctypes.c_int32()
+        self.L.kk_queue_cancel(self.h, request, ctypes.byref(n))
+        return n.value
+
+    def stats(self):
+        b, j, m = ctypes.c_uint64(), ctypes.c_uint64(), ctypes.c_uint64()
+        self.L.kk_queue_stats(self.h, ctypes.byref(b), ctypes.byref(j), ctypes.byref(m))
+        return {"batches": b.value, "jobs": j.value, "max_batch": m.value}
+
+    def close(self):
+        if self.h:
+            self.L.kk_queue_destroy(self.h)
+            self.h = ctypes.c_void_p()
