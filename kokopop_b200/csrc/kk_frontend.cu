@@ -7,6 +7,8 @@
 #include "kk_common.cuh"
 #include "kk_kernels.h"
 
+#include <atomic>
+
 namespace kk {
 
 // ggml_get_rows of the embedding [C, vocab] into the packed level-1 layout:
@@ -118,17 +120,17 @@ __global__ void __launch_bounds__(128) k_layer_norm_ch(const float *x, int64_t R
 cudaError_t layer_norm_ch(const float *x, int64_t R, int C, const float *gamma, const float *beta, int leaky_on,
                           float slope, float eps, const Batch &b, float *y, int64_t R_out, int lstm_B,
                           cudaStream_t st) {
-    static bool attr[64] = {};
+    static std::atomic<bool> attr[64];
     int dev = 0;
     if (C < 1 || C > kLnMaxC) return cudaErrorInvalidValue;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (!attr[dev]) {
+    if (!attr[dev].load(std::memory_order_acquire)) {
         e = cudaFuncSetAttribute(k_layer_norm_ch, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)(kLnMaxC * 32 * sizeof(float)));
         if (e != cudaSuccess) return e;
-        attr[dev] = true;
+        attr[dev].store(true, std::memory_order_release);
     }
     const size_t smem = (size_t)C * 32 * sizeof(float);
     k_layer_norm_ch<<<(unsigned)((R + 31) / 32), 128, smem, st>>>(x, R, C, gamma, beta, leaky_on, slope, b, y, R_out,
@@ -237,15 +239,15 @@ __global__ void __launch_bounds__(256) k_attention(const float *__restrict__ qkv
 cudaError_t attention(const float *qkv, int64_t R, int H, int n_heads, int max_len, const Batch &b, float scale,
                       float *out, cudaStream_t st) {
     if (H != n_heads * kAttHS || max_len < 1 || max_len > kAttMaxN) return cudaErrorInvalidValue;
-    static bool attr[64] = {};
+    static std::atomic<bool> attr[64];
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    if (!attr[dev]) {
+    if (!attr[dev].load(std::memory_order_acquire)) {
         e = cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kAttSmem);
         if (e != cudaSuccess) return e;
-        attr[dev] = true;
+        attr[dev].store(true, std::memory_order_release);
     }
     const dim3 grid((unsigned)((max_len + kAttQ - 1) / kAttQ), (unsigned)n_heads, (unsigned)b.n);
     k_attention<<<grid, 256, kAttSmem, st>>>(qkv, R, H, b, scale, out);
