@@ -139,19 +139,24 @@ __global__ void __cluster_dims__(kLstmCl, 1, 1) __launch_bounds__(kLstmThreads, 
                     gb[(rb * RPT + i) * Bc + sb * SPT + jj] = __fadd_rn(__fadd_rn(bias[i], pg[i][jj]), acc[i][jj]);
         }
         __syncthreads();
+        // the four gate activations of every live cell, spread over the
+        // threads (in place: i, f, o logistic, g tanh)
+        for (int idx = threadIdx.x; idx < kLstmRows * Bc; idx += kLstmThreads) {
+            const int lr = idx / Bc, bl = idx % Bc, b = b0 + bl;
+            if (b >= a.B || s >= a.len[b]) continue;
+            const float x = sanitize(gb[idx], 80.0f);
+            gb[idx] = lr / kLstmUnits == 2 ? tanh_cr(x) : sigmoid_stable(x);
+        }
+        __syncthreads();
         for (int idx = threadIdx.x; idx < kLstmUnits * Bc; idx += kLstmThreads) {
             const int uu = idx / Bc, bl = idx % Bc, b = b0 + bl;
             if (b >= a.B) continue;
             const int L = a.len[b];
             if (s >= L) continue;
-            const float xi = sanitize(gb[(0 * kLstmUnits + uu) * Bc + bl], 80.0f);
-            const float xf = sanitize(gb[(1 * kLstmUnits + uu) * Bc + bl], 80.0f);
-            const float xg = sanitize(gb[(2 * kLstmUnits + uu) * Bc + bl], 80.0f);
-            const float xo = sanitize(gb[(3 * kLstmUnits + uu) * Bc + bl], 80.0f);
-            const float ig = sigmoid_stable(xi);
-            const float fg = sigmoid_stable(xf);
-            const float gg = tanh_cr(xg);
-            const float og = sigmoid_stable(xo);
+            const float ig = gb[(0 * kLstmUnits + uu) * Bc + bl];
+            const float fg = gb[(1 * kLstmUnits + uu) * Bc + bl];
+            const float gg = gb[(2 * kLstmUnits + uu) * Bc + bl];
+            const float og = gb[(3 * kLstmUnits + uu) * Bc + bl];
             const float cn = sanitize(__fadd_rn(__fmul_rn(fg, cs[uu * Bc + bl]), __fmul_rn(ig, gg)), 50.0f);
             cs[uu * Bc + bl] = cn;
             float hv = __fmul_rn(og, tanh_cr(cn));
