@@ -475,6 +475,37 @@ void kk_ctx::derive() {
                 else
                     pack_tc_split(packed[n], OC, IC, 1, get);
             }
+            // query | key | value along the output channels
+            const std::string L = kAlbertLayer;
+            const DevTensor *qkv[3] = {Wopt(L + "attention.query.weight"), Wopt(L + "attention.key.weight"),
+                                       Wopt(L + "attention.value.weight")};
+            const DevTensor *qkvb[3] = {Wopt(L + "attention.query.bias"), Wopt(L + "attention.key.bias"),
+                                        Wopt(L + "attention.value.bias")};
+            const int H = (int)qkv[0]->ne[1], IC = (int)qkv[0]->ne[0];
+            bool same = true;
+            for (int i = 0; i < 3; ++i)
+                same = same && qkv[i]->ne[0] == IC && qkv[i]->ne[1] == H && qkvb[i] && qkvb[i]->n == H;
+            if (same) {
+                std::vector<float> hw((size_t)3 * H * IC), hb((size_t)3 * H);
+                for (int i = 0; i < 3; ++i) {
+                    check_cuda(cudaMemcpy(hw.data() + (size_t)i * H * IC, qkv[i]->d, (size_t)H * IC * 4,
+                                          cudaMemcpyDeviceToHost),
+                               "read qkv weight");
+                    check_cuda(cudaMemcpy(hb.data() + (size_t)i * H, qkvb[i]->d, (size_t)H * 4, cudaMemcpyDeviceToHost),
+                               "read qkv bias");
+                }
+                auto get = [&](int oc, int ic, int) { return hw[(size_t)oc * IC + ic]; };
+                if (albert_mode == 1)
+                    pack_tc(packed["albert.qkv"], 3 * H, IC, 1, get);
+                else
+                    pack_tc_split(packed["albert.qkv"], 3 * H, IC, 1, get);
+                albert_qkv_bbuf.ensure(hb.size() * 4);
+                check_cuda(cudaMemcpy(albert_qkv_bbuf.p, hb.data(), hb.size() * 4, cudaMemcpyHostToDevice),
+                           "upload qkv bias");
+                albert_qkv_b.d = (float *)albert_qkv_bbuf.p;
+                albert_qkv_b.ne[0] = 3 * H;
+                albert_qkv_b.n = 3 * H;
+            }
         }
     }
     d_err.ensure(sizeof(int));
@@ -2050,9 +2081,19 @@ void albert_device(kk_ctx &c, int32_t n, const int32_t *n_tokens, const int32_t 
     };
     linear("kokopop.albert.encoder.embedding_hidden_mapping_in.weight", x, E, cur, nullptr);
     for (int layer = 0; layer < 12; ++layer) {
-        linear(L + "attention.query.weight", cur, H, qkv, nullptr);
-        linear(L + "attention.key.weight", cur, H, qkv + (size_t)H * R1, nullptr);
-        linear(L + "attention.value.weight", cur, H, qkv + (size_t)2 * H * R1, nullptr);
+        auto fused = c.packed.find("albert.qkv");
+        if (r.tc && fused != c.packed.end()) {
+            // one GEMM for query | key | value (each channel's sum as in the separate ones)
+            r.act_only(cur, op, R1, H, 1, 0, ACT_NONE, 0.f);
+            Runner::Epi ep;
+            ep.bias = &c.albert_qkv_b;
+            ep.valid = r.sum_len(1, 0);
+            r.conv_h(fused->second, op, 1, 0, 1, qkv, R1, R1, ep);
+        } else {
+            linear(L + "attention.query.weight", cur, H, qkv, nullptr);
+            linear(L + "attention.key.weight", cur, H, qkv + (size_t)H * R1, nullptr);
+            linear(L + "attention.value.weight", cur, H, qkv + (size_t)2 * H * R1, nullptr);
+        }
         check_cuda(attention(qkv, R1, H, 12, max_len, r.B, 0.125f, att, st), "attention launch");
         linear(L + "attention.dense.weight", att, H, tmp, cur);
         check_cuda(layer_norm_ch(tmp, R1, H, c.W(L + "attention.LayerNorm.weight").d,

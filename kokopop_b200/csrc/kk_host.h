@@ -121,6 +121,10 @@ struct kk_ctx {
     bool albert_ready = false;  // ALBERT + bert_encoder
     std::string missing_albert;
     int albert_mode = 0;  // its linears, as text_mode
+    // tensor-core modes: query | key | value as one packed weight
+    // ("albert.qkv", 3 x 768 output channels) with its bias
+    kk::DevBuf albert_qkv_bbuf;
+    kk::DevTensor albert_qkv_b;
     kk::DevBuf convt_phase[2];
     bool convt_f16[2] = {false, false};
     // tensor-core path: every convolution weight is F16, or every one is F32
