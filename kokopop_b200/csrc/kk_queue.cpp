@@ -271,6 +271,31 @@ int q_fail(int code, const char *msg) {
     return code;
 }
 
+// No C++ exception crosses the C ABI: thread creation and allocation
+// failures become KK_ERROR_INFERENCE with a message.
+template <typename F>
+int q_guard(F &&f) noexcept {
+    try {
+        return f();
+    } catch (const std::exception &e) {
+        return q_fail(KK_ERROR_INFERENCE, e.what());
+    } catch (...) {
+        return q_fail(KK_ERROR_INFERENCE, "unknown C++ exception");
+    }
+}
+
+// Stops and joins the workers started so far (creation failed part way).
+void q_abort(kk_queue *q) {
+    {
+        std::lock_guard<std::mutex> lk(q->m);
+        q->stop = true;
+        q->cv_work.notify_all();
+    }
+    for (std::thread &t : q->workers)
+        if (t.joinable()) t.join();
+    delete q;
+}
+
 int q_config(kk_queue *q, int32_t max_batch, int64_t max_batch_frames, int32_t max_wait_us) {
     if (max_batch < 1 || max_batch > 4096 || max_batch_frames < 1 || max_batch_frames > ((int64_t)1 << 24) ||
         max_wait_us < 0)
@@ -290,31 +315,46 @@ int kk_queue_create(kk_ctx *const *ctxs, int32_t n_ctx, int32_t max_batch, int64
     if (!ctxs || n_ctx < 1 || !out) return q_fail(KK_ERROR_INVALID_ARGUMENT, "null argument");
     for (int i = 0; i < n_ctx; ++i)
         if (!ctxs[i]) return q_fail(KK_ERROR_INVALID_ARGUMENT, "null context");
-    kk_queue *q = new kk_queue();
-    const int rc = q_config(q, max_batch, max_batch_frames, max_wait_us);
-    if (rc != KK_OK) {
-        delete q;
-        return rc;
-    }
-    if (max_batch_frames > kk::kMaxFrames * (int64_t)max_batch) q->max_frames = kk::kMaxFrames * (int64_t)max_batch;
-    for (int i = 0; i < n_ctx; ++i) q->workers.emplace_back(worker_ctx, q, ctxs[i]);
-    *out = q;
-    return KK_OK;
+    return q_guard([&] {
+        kk_queue *q = new kk_queue();
+        const int rc = q_config(q, max_batch, max_batch_frames, max_wait_us);
+        if (rc != KK_OK) {
+            delete q;
+            return rc;
+        }
+        if (max_batch_frames > kk::kMaxFrames * (int64_t)max_batch)
+            q->max_frames = kk::kMaxFrames * (int64_t)max_batch;
+        try {
+            for (int i = 0; i < n_ctx; ++i) q->workers.emplace_back(worker_ctx, q, ctxs[i]);
+        } catch (...) {
+            q_abort(q);
+            throw;
+        }
+        *out = q;
+        return (int)KK_OK;
+    });
 }
 
 int kk_queue_create_exec(kk_queue_exec_fn fn, void *const *users, int32_t n_workers, int32_t max_batch,
                          int64_t max_batch_frames, int32_t max_wait_us, kk_queue **out) {
     if (!fn || n_workers < 1 || !out) return q_fail(KK_ERROR_INVALID_ARGUMENT, "null argument");
-    kk_queue *q = new kk_queue();
-    const int rc = q_config(q, max_batch, max_batch_frames, max_wait_us);
-    if (rc != KK_OK) {
-        delete q;
-        return rc;
-    }
-    q->fn = fn;
-    for (int i = 0; i < n_workers; ++i) q->workers.emplace_back(worker_fn, q, users ? users[i] : nullptr);
-    *out = q;
-    return KK_OK;
+    return q_guard([&] {
+        kk_queue *q = new kk_queue();
+        const int rc = q_config(q, max_batch, max_batch_frames, max_wait_us);
+        if (rc != KK_OK) {
+            delete q;
+            return rc;
+        }
+        q->fn = fn;
+        try {
+            for (int i = 0; i < n_workers; ++i) q->workers.emplace_back(worker_fn, q, users ? users[i] : nullptr);
+        } catch (...) {
+            q_abort(q);
+            throw;
+        }
+        *out = q;
+        return (int)KK_OK;
+    });
 }
 
 int kk_queue_submit(kk_queue *q, uint64_t request, int32_t n_frames, const float *asr, const float *f0,
@@ -323,23 +363,30 @@ int kk_queue_submit(kk_queue *q, uint64_t request, int32_t n_frames, const float
         return q_fail(KK_ERROR_INVALID_ARGUMENT, "null argument");
     if (n_frames < 1 || n_frames > kk::kMaxFrames || n_frames > q->max_frames)
         return q_fail(KK_ERROR_INVALID_ARGUMENT, "chunk length out of range");
-    std::lock_guard<std::mutex> lk(q->m);
-    if (q->stop) return q_fail(KK_ERROR_INVALID_ARGUMENT, "queue stopped");
-    QJob j;
-    j.ticket = q->next_ticket++;
-    j.request = request;
-    j.T = n_frames;
-    j.asr = asr;
-    j.f0 = f0;
-    j.noise = noise;
-    j.style = style;
-    j.audio = audio;
-    j.t0 = Clock::now();
-    q->pending.push_back(j);
-    q->live.insert(j.ticket);
-    *ticket = j.ticket;
-    q->cv_work.notify_all();
-    return KK_OK;
+    return q_guard([&] {
+        std::lock_guard<std::mutex> lk(q->m);
+        if (q->stop) return q_fail(KK_ERROR_INVALID_ARGUMENT, "queue stopped");
+        QJob j;
+        j.ticket = q->next_ticket++;
+        j.request = request;
+        j.T = n_frames;
+        j.asr = asr;
+        j.f0 = f0;
+        j.noise = noise;
+        j.style = style;
+        j.audio = audio;
+        j.t0 = Clock::now();
+        q->pending.push_back(j);
+        try {
+            q->live.insert(j.ticket);
+        } catch (...) {
+            q->pending.pop_back();
+            throw;
+        }
+        *ticket = j.ticket;
+        q->cv_work.notify_all();
+        return (int)KK_OK;
+    });
 }
 
 int kk_queue_wait(kk_queue *q, uint64_t ticket, int32_t timeout_ms) {
