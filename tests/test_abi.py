@@ -53,3 +53,45 @@ def test_error_slot_is_thread_local():
     t.join()
     assert seen["msg"] == ""
     assert L.kk_last_error().decode() != ""
+
+
+def test_front_end_and_queue_entry_points_reject_bad_arguments():
+    """The front-end entry points and the queue validate their arguments
+    before touching a device."""
+    L = kb.load_library()
+    n = np.array([4], np.int32)
+    ids = np.zeros(4, np.int32)
+    z = np.zeros(4096, np.float32)
+    f = ctypes.POINTER(ctypes.c_float)
+    i32p = ctypes.POINTER(ctypes.c_int32)
+    ip, fp = n.ctypes.data_as(i32p), z.ctypes.data_as(f)
+    idp = ids.ctypes.data_as(i32p)
+    E = kb.KK_ERROR_INVALID_ARGUMENT
+    assert L.kk_text_encoder_forward(None, 1, ip, idp, fp) == E
+    assert L.kk_albert_forward(None, 1, ip, idp, fp) == E
+    assert L.kk_duration_head_forward(None, 1, ip, fp, fp) == E
+    assert L.kk_duration_proj(None, 4, fp, fp) == E
+    assert L.kk_prosody_f0n(None, 1, ip, fp, fp, fp, fp) == E
+    q = ctypes.c_void_p()
+    assert L.kk_queue_create(None, 1, 64, 1000, 0, ctypes.byref(q)) == E
+    assert L.kk_queue_create_exec(kb.QUEUE_EXEC_FN(0), None, 1, 64, 1000, 0, ctypes.byref(q)) == E
+    assert L.kk_queue_last_error().decode()
+    t = ctypes.c_uint64()
+    assert L.kk_queue_submit(None, 0, 4, fp, fp, fp, fp, fp, ctypes.byref(t)) == E
+    assert L.kk_queue_wait(None, 1, 0) == E
+    L.kk_queue_destroy(None)  # no-op
+
+
+def test_queue_rejects_out_of_range_chunks_and_limits():
+    ok = kb.Queue(executor=lambda *a: 0, max_batch=2, max_batch_frames=100, max_wait_us=0)
+    try:
+        from types import SimpleNamespace
+        big = SimpleNamespace(T=101, asr=np.zeros((512, 101), np.float32), f0=np.zeros(202, np.float32),
+                              noise=np.zeros(202, np.float32), style=np.zeros(128, np.float32))
+        with pytest.raises(kb.KKError):
+            ok.submit(1, big)
+    finally:
+        ok.close()
+    for kw in ({"max_batch": 0}, {"max_batch_frames": 0}, {"max_wait_us": -1}):
+        with pytest.raises(kb.KKError):
+            kb.Queue(executor=lambda *a: 0, **kw)
