@@ -1,9 +1,11 @@
-// Text encoder and duration head of the Kokoro-82M front end (sm_100a):
-// the embedding lookup and the per-token LayerNorm of the text encoder's CNN
-// (text_encoder, src/arch/kokoro/graph_ops.cpp:1578-1624; its k = 5 convs
-// run on the conv kernels of kk_conv_tc.cu / kk_conv_simt.cu and its biLSTM
-// on kk_lstm.cu), and the duration projection with the bucket sum that the
-// reference runs on the host in double (src/arch/kokoro/kokoro.cpp:469-516).
+// Kernels of the Kokoro-82M front end (sm_100a): the embedding lookups and
+// the per-token LayerNorm (the text encoder's CNN, text_encoder,
+// src/arch/kokoro/graph_ops.cpp:1578-1624; ALBERT's embeddings and layers,
+// src/arch/kokoro/kokoro.cpp:279-337), ALBERT's self-attention and GELU, the
+// token-major output gather, and the duration projection with the bucket
+// sum that the reference runs on the host in double (kokoro.cpp:469-516).
+// The convolutions and linears run on the conv kernels of kk_conv_tc.cu /
+// kk_conv_simt.cu, the biLSTMs on kk_lstm.cu.
 #include "kk_common.cuh"
 #include "kk_kernels.h"
 
