@@ -60,13 +60,16 @@ void embed(const float *emb, int C, int vocab, const int32_t *ids, const int64_t
 // threads write the result; the tile is read whole before anything is
 // written, so y may be x. Gap rows are written as zero. lstm_B > 0: row t of
 // utterance u goes to row t * lstm_B + u of y (the LSTM layout, rows beyond
-// the utterances untouched).
+// the utterances untouched). yh (level layout only): the result also as the
+// half chunk-major operand of the next linear (chunk stride Ryh, with the lo
+// halves lo_off further when lo_off > 0), valid rows only.
 constexpr int kLnMaxC = 1024;
 
 __global__ void __launch_bounds__(128) k_layer_norm_ch(const float *x, int64_t R, int C,
                                                        const float *__restrict__ gamma,
                                                        const float *__restrict__ beta, int leaky_on, float slope,
-                                                       Batch b, float *y, int64_t R_out, int lstm_B, float eps) {
+                                                       Batch b, float *y, int64_t R_out, int lstm_B, float eps,
+                                                       __half *yh, int64_t Ryh, int64_t lo_off) {
     extern __shared__ float tile[];  // [C][32]
     __shared__ float stat[2][32];
     __shared__ int64_t orow_s[32];
@@ -106,22 +109,40 @@ __global__ void __launch_bounds__(128) k_layer_norm_ch(const float *x, int64_t R
         stat[1][lane] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
     }
     __syncthreads();
-    for (int i = tid; i < C * 32; i += 128) {
-        const int c = i >> 5, r = i & 31;
+    // thread = (chunk of 8 channels, row): the F32 values, and with yh the
+    // chunk's 8 halves of the row as one 16-byte store
+    const int nch = (C + 7) / 8;
+    for (int i = tid; i < nch * 32; i += 128) {
+        const int ck = i >> 5, r = i & 31;
         if (q0 + r >= R) continue;
-        if (!live_s[r]) {
-            if (lstm_B == 0) y[(int64_t)c * R_out + q0 + r] = 0.0f;
-            continue;
+        const bool lv = live_s[r] != 0;
+        if (!lv && lstm_B > 0) continue;
+        __align__(16) __half hh[8], ll[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const int c = ck * 8 + e;
+            float v = 0.0f;
+            if (c < C && lv) {
+                v = __fmul_rn(__fsub_rn(tile[c * 32 + r], stat[0][r]), stat[1][r]);
+                v = __fadd_rn(__fmul_rn(v, gamma[c]), beta[c]);
+                if (leaky_on) v = leaky(v, slope);
+            }
+            if (c < C) y[(int64_t)c * R_out + (lv ? orow_s[r] : q0 + r)] = v;
+            hh[e] = __float2half_rn(v);
+            ll[e] = split_lo(v, hh[e]);
         }
-        float v = __fmul_rn(__fsub_rn(tile[i], stat[0][r]), stat[1][r]);
-        v = __fadd_rn(__fmul_rn(v, gamma[c]), beta[c]);
-        y[(int64_t)c * R_out + orow_s[r]] = leaky_on ? leaky(v, slope) : v;
+        if (yh && lv) {
+            __half *dst = yh + ((int64_t)ck * Ryh + q0 + r) * 8;
+            *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(hh);
+            if (lo_off > 0) *reinterpret_cast<uint4 *>(dst + lo_off) = *reinterpret_cast<const uint4 *>(ll);
+        }
     }
 }
 
 cudaError_t layer_norm_ch(const float *x, int64_t R, int C, const float *gamma, const float *beta, int leaky_on,
                           float slope, float eps, const Batch &b, float *y, int64_t R_out, int lstm_B,
-                          cudaStream_t st) {
+                          cudaStream_t st, __half *yh, int64_t Ryh, int64_t lo_off) {
+    if (yh && lstm_B > 0) return cudaErrorInvalidValue;
     static std::atomic<bool> attr[64];
     int dev = 0;
     if (C < 1 || C > kLnMaxC) return cudaErrorInvalidValue;
@@ -136,7 +157,7 @@ cudaError_t layer_norm_ch(const float *x, int64_t R, int C, const float *gamma, 
     }
     const size_t smem = (size_t)C * 32 * sizeof(float);
     k_layer_norm_ch<<<(unsigned)((R + 31) / 32), 128, smem, st>>>(x, R, C, gamma, beta, leaky_on, slope, b, y, R_out,
-                                                                  lstm_B, eps);
+                                                                  lstm_B, eps, yh, Ryh, lo_off);
     return cudaGetLastError();
 }
 

@@ -2001,11 +2001,15 @@ void text_encoder_device(kk_ctx &c, int32_t n, const int32_t *n_tokens, const in
     }
     for (int i = 0; i < 3; ++i) {
         const std::string p = "kokopop.text_encoder.cnn." + std::to_string(i);
-        if (r.tc) r.act_only(X, in, R1, C, 1, 0, ACT_NONE, 0.f);
+        // the first conv's operand from the embeddings; the others' from
+        // the LayerNorm before them
+        if (r.tc && i == 0) r.act_only(X, in, R1, C, 1, 0, ACT_NONE, 0.f);
         r.conv_w(p + ".0.weight", p + ".0.bias", in, C, 5, 2, 1, Y, R1, R1, Runner::Epi{}, r.sum_len(1, 0));
         const bool last = i == 2;
+        const bool to_op = r.tc && !last;
         check_cuda(layer_norm_ch(Y, R1, C, c.W(p + ".1.gamma").d, c.W(p + ".1.beta").d, 1, 0.2f, 1e-5f, r.B,
-                                 last ? Xl : X, last ? Rr : R1, last ? n : 0, st),
+                                 last ? Xl : X, last ? Rr : R1, last ? n : 0, st, to_op ? in.h : nullptr, in.Ry,
+                                 to_op ? in.lo(C) : 0),
                    "layer norm launch");
         ++c.n_launches;
     }
@@ -2052,9 +2056,6 @@ void albert_device(kk_ctx &c, int32_t n, const int32_t *n_tokens, const int32_t 
     float *tmp = c.buf("al_tmp", (size_t)H * R1);
     float *ff = c.buf("al_ff", (size_t)F * R1);
     embed(word.d, E, vocab, ids, r.d_cum, r.B, x, R1, (int *)c.d_err.p, st, pos.d, type.d);
-    check_cuda(layer_norm_ch(x, R1, E, c.W(e + "LayerNorm.weight").d, c.W(e + "LayerNorm.bias").d, 0, 0.f, 1e-12f,
-                             r.B, x, R1, 0, st),
-               "layer norm launch");
     c.n_launches += 2;
     const int Cmax = std::max(std::max(E, H), F);
     Op op;
@@ -2062,11 +2063,21 @@ void albert_device(kk_ctx &c, int32_t n, const int32_t *n_tokens, const int32_t 
         op = r.op("opA", 1, Cmax);
         r.zero(op, Cmax);
     }
-    // linear(w, b, in [C][R1]) -> o [OC][R1] (+ resid)
-    auto linear = [&](const std::string &w, const float *in, int C, float *o, const float *resid) {
+    // LayerNorm (eps 1e-12) of x into y, and on the tensor-core path the
+    // operand of the next linear
+    auto norm = [&](const float *xin, int C, const std::string &wn, float *yout) {
+        check_cuda(layer_norm_ch(xin, R1, C, c.W(wn + ".weight").d, c.W(wn + ".bias").d, 0, 0.f, 1e-12f, r.B, yout,
+                                 R1, 0, st, r.tc ? op.h : nullptr, op.Ry, r.tc ? op.lo(C) : 0),
+                   "layer norm launch");
+    };
+    norm(x, E, e + "LayerNorm", x);
+    // linear(w, b, in [C][R1]) -> o [OC][R1] (+ resid); ready: the operand of
+    // `in` is in `op` already (written by the LayerNorm that produced it)
+    auto linear = [&](const std::string &w, const float *in, int C, float *o, const float *resid,
+                      bool ready = false) {
         Op src;
         if (r.tc) {
-            r.act_only(in, op, R1, C, 1, 0, ACT_NONE, 0.f);
+            if (!ready) r.act_only(in, op, R1, C, 1, 0, ACT_NONE, 0.f);
             src = op;
         } else {
             src.f = const_cast<float *>(in);
@@ -2079,12 +2090,13 @@ void albert_device(kk_ctx &c, int32_t n, const int32_t *n_tokens, const int32_t 
         }
         r.conv_w(w, w.substr(0, w.size() - 6) + "bias", src, C, 1, 0, 1, o, R1, R1, ep, r.sum_len(1, 0));
     };
-    linear("kokopop.albert.encoder.embedding_hidden_mapping_in.weight", x, E, cur, nullptr);
+    linear("kokopop.albert.encoder.embedding_hidden_mapping_in.weight", x, E, cur, nullptr, true);
     for (int layer = 0; layer < 12; ++layer) {
         auto fused = c.packed.find("albert.qkv");
         if (r.tc && fused != c.packed.end()) {
-            // one GEMM for query | key | value (each channel's sum as in the separate ones)
-            r.act_only(cur, op, R1, H, 1, 0, ACT_NONE, 0.f);
+            // one GEMM for query | key | value (each channel's sum as in the
+            // separate ones); from layer 1 on its operand is the LayerNorm's
+            if (layer == 0) r.act_only(cur, op, R1, H, 1, 0, ACT_NONE, 0.f);
             Runner::Epi ep;
             ep.bias = &c.albert_qkv_b;
             ep.valid = r.sum_len(1, 0);
@@ -2096,19 +2108,15 @@ void albert_device(kk_ctx &c, int32_t n, const int32_t *n_tokens, const int32_t 
         }
         check_cuda(attention(qkv, R1, H, 12, max_len, r.B, 0.125f, att, st), "attention launch");
         linear(L + "attention.dense.weight", att, H, tmp, cur);
-        check_cuda(layer_norm_ch(tmp, R1, H, c.W(L + "attention.LayerNorm.weight").d,
-                                 c.W(L + "attention.LayerNorm.bias").d, 0, 0.f, 1e-12f, r.B, cur, R1, 0, st),
-                   "layer norm launch");
-        linear(L + "ffn.weight", cur, H, ff, nullptr);
+        norm(tmp, H, L + "attention.LayerNorm", cur);
+        linear(L + "ffn.weight", cur, H, ff, nullptr, true);
         gelu(ff, (int64_t)F * R1, st);
         linear(L + "ffn_output.weight", ff, F, tmp, cur);
-        check_cuda(layer_norm_ch(tmp, R1, H, c.W(L + "full_layer_layer_norm.weight").d,
-                                 c.W(L + "full_layer_layer_norm.bias").d, 0, 0.f, 1e-12f, r.B, cur, R1, 0, st),
-                   "layer norm launch");
+        norm(tmp, H, L + "full_layer_layer_norm", cur);
         c.n_launches += 4;
     }
     float *y = c.buf("al_y", (size_t)D * R1);
-    linear("kokopop.bert_encoder.weight", cur, H, y, nullptr);
+    linear("kokopop.bert_encoder.weight", cur, H, y, nullptr, true);
     rows_out(y, R1, D, r.B, r.d_cum, max_len, out, st);
     ++c.n_launches;
     check_cuda(cudaGetLastError(), "kernel launch");

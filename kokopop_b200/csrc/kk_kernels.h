@@ -225,9 +225,10 @@ void embed(const float *emb, int C, int vocab, const int32_t *ids, const int64_t
 // LeakyReLU(slope) when leaky_on; lstm_B > 0 writes row t * lstm_B + u (the
 // LSTM layout) instead of row q. y may be x.
 // (C <= 1024)
+// yh non-null: also the half operand of the next linear (see kk_frontend.cu)
 cudaError_t layer_norm_ch(const float *x, int64_t R, int C, const float *gamma, const float *beta, int leaky_on,
                           float slope, float eps, const Batch &b, float *y, int64_t R_out, int lstm_B,
-                          cudaStream_t st);
+                          cudaStream_t st, __half *yh = nullptr, int64_t Ryh = 0, int64_t lo_off = 0);
 // ALBERT self-attention: qkv [3 H][R] -> out [H][R], heads of 64, at most
 // 512 tokens per sequence
 cudaError_t attention(const float *qkv, int64_t R, int H, int n_heads, int max_len, const Batch &b, float scale,
