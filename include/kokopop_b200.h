@@ -14,7 +14,13 @@
  *     thread-safe, exactly like a kokopop_model (docs/c-api.md:284-286);
  *   - pointers are plain host pointers unless the name ends in _device, in
  *     which case they are device pointers on the context's device and the
- *     call is asynchronous on `stream` (NULL = the context's own stream).
+ *     call is asynchronous on `stream` (NULL = the context's own stream):
+ *     it stages its small tables in pinned memory and returns without
+ *     waiting for the GPU;
+ *   - calls on one context reuse its workspaces, so the device runs them in
+ *     the order they were made, also when they name different streams: a
+ *     call waits (on the device, not the host) for the previous call of the
+ *     context to finish. Calls on different contexts are independent.
  *
  * Layouts follow ggml (ne[0] fastest). Per utterance, an activation written
  * "[L, C]" is time-fastest: x[c * L + t] (src/arch/kokoro/kokoro.h:200-212).
@@ -286,21 +292,28 @@ int kk_align_durations(kk_ctx *ctx, int64_t n_tokens, const float *durations, fl
 /* kk_istft without any device allocation (no counterpart in the reference,
  * whose iSTFT runs on the host). Same arguments and results as kk_istft, but
  * no kk_ctx: input, output, tables and descriptor are staged in one static
- * device array of the library (about 3.5 MB per device, reserved when the
- * library's device code loads), so the call never allocates or frees device
- * memory. For callers that cannot allocate mid-run: a real-time audio thread
- * (cudaMalloc / cudaFree can synchronise the whole device) or a process that
- * fixes its device-memory budget up front.
- *   device   CUDA device to run on (made current for the call, then restored)
+ * device array of the library (about 3.5 MB per device), so the call never
+ * allocates or frees device memory itself. For callers that cannot allocate
+ * mid-run: a real-time audio thread (cudaMalloc / cudaFree can synchronise
+ * the whole device) or a process that fixes its device-memory budget up
+ * front.
+ *   device   CUDA device to run on (made current for the call, then
+ *            restored); an index past the device count is
+ *            KK_ERROR_INVALID_ARGUMENT
  *   stream   a stream of that device, or NULL for its legacy default stream;
  *            the call returns after the stream has finished the copy back
  *   n_frames at most KK_ISTFT_STATIC_MAX_FRAMES; larger inputs are rejected
  *            with KK_ERROR_INVALID_ARGUMENT (use kk_istft for them)
- * The first call on each device looks up the array's address and uploads the
- * tables (synchronous): make it before any stream capture starts. Nothing in
- * the array has to start at zero. Calls that overlap in time on one device
- * (from several threads, or on several streams) share the array and
- * overwrite each other's data: serialise them. */
+ * Set-up: with CUDA's default lazy module loading, the array's memory is
+ * reserved when the first call on a device looks up its address, so that
+ * first call can fail for lack of device memory or stall while the module
+ * loads. Make one call with n_frames = 0 (or 1) on each device at start-up,
+ * before any stream capture: it does that set-up and nothing else. (With
+ * CUDA_MODULE_LOADING=EAGER the array is reserved when the context is
+ * created.) The device then holds the array until the process exits.
+ * Nothing in the array has to start at zero. Calls that overlap in time on
+ * one device (from several threads, or on several streams) share the array
+ * and overwrite each other's data: serialise them. */
 #define KK_ISTFT_STATIC_MAX_FRAMES 32768
 int kk_istft_static(int device, int64_t n_frames, const float *post, float *audio, void *stream);
 
@@ -319,6 +332,11 @@ typedef struct kk_profile {
 int kk_profile_enable(kk_ctx *ctx, int enable);
 /* Reads (after synchronising the context's work) and optionally resets. */
 int kk_profile_read(kk_ctx *ctx, kk_profile *out, int reset);
+
+/* How many device or pinned-host allocations the library has made in this
+ * process, over all contexts and queues (no counterpart in the reference).
+ * Lets a caller check that a path allocates nothing once warm. */
+int kk_allocation_count(uint64_t *out);
 
 #ifdef __cplusplus
 }

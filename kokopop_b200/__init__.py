@@ -105,6 +105,7 @@ def load_library():
     L.kk_queue_destroy.restype = None
     L.kk_profile_enable.argtypes = [vp, ctypes.c_int]
     L.kk_profile_read.argtypes = [vp, ctypes.POINTER(Profile), ctypes.c_int]
+    L.kk_allocation_count.argtypes = [ctypes.POINTER(ctypes.c_uint64)]
     _lib = L
     return L
 

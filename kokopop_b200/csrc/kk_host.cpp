@@ -15,6 +15,7 @@
 #include "kk_host.h"
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdlib>
 #include <cstdio>
@@ -46,12 +47,24 @@ void check_cuda(cudaError_t e, const char *what) {
         throw KKError(KK_ERROR_INFERENCE, std::string(what) + ": " + cudaGetErrorString(e));
 }
 
+static std::atomic<uint64_t> g_allocations{0};
+
+cudaError_t device_malloc(void **p, size_t bytes) {
+    g_allocations.fetch_add(1, std::memory_order_relaxed);
+    return cudaMalloc(p, bytes);
+}
+
+cudaError_t pinned_malloc(void **p, size_t bytes) {
+    g_allocations.fetch_add(1, std::memory_order_relaxed);
+    return cudaMallocHost(p, bytes);
+}
+
 void DevBuf::ensure(size_t b) {
     if (b <= bytes) return;
     if (p) cudaFree(p);
     p = nullptr;
     bytes = 0;
-    check_cuda(cudaMalloc(&p, b), "cudaMalloc workspace");
+    check_cuda(device_malloc(&p, b), "cudaMalloc workspace");
     bytes = b;
 }
 
@@ -114,6 +127,12 @@ kk_ctx::~kk_ctx() {
     d_sites.release();
     d_tables.release();
     d_batch.release();
+    for (auto &s : stage) {
+        if (s.ev) cudaEventDestroy(s.ev);
+        if (s.p) cudaFreeHost(s.p);
+        for (char *r : s.retired) cudaFreeHost(r);
+    }
+    if (ev_done) cudaEventDestroy(ev_done);
     if (ev_inputs) cudaEventDestroy(ev_inputs);
     if (ev_src) cudaEventDestroy(ev_src);
     if (st2) cudaStreamDestroy(st2);
@@ -146,6 +165,46 @@ float *kk_ctx::buf(const char *name, size_t floats) {
     DevBuf &b = ws[name];
     b.ensure(floats * sizeof(float));
     return (float *)b.p;
+}
+
+void kk_ctx::stage_begin() {
+    stage_k ^= 1;
+    StageSlot &s = stage[stage_k];
+    if (s.pending) {
+        check_cuda(cudaEventSynchronize(s.ev), "staging slot reuse");
+        s.pending = false;
+    }
+    for (char *r : s.retired) cudaFreeHost(r);
+    s.retired.clear();
+    s.used = 0;
+}
+
+void kk_ctx::upload(void *dst, const void *src, size_t bytes, cudaStream_t st, const char *what) {
+    if (!bytes) return;
+    StageSlot &s = stage[stage_k];
+    size_t at = (s.used + 63) / 64 * 64;
+    if (at + bytes > s.cap) {
+        // earlier uploads of this call may still read the old buffer: keep it
+        // until the slot's event has passed
+        if (s.p) s.retired.push_back(s.p);
+        s.p = nullptr;
+        s.cap = 0;
+        const size_t cap = std::max<size_t>(bytes, 64 * 1024) * 2;
+        check_cuda(pinned_malloc((void **)&s.p, cap), "cudaMallocHost staging");
+        s.cap = cap;
+        at = 0;
+    }
+    std::memcpy(s.p + at, src, bytes);
+    s.used = at + bytes;
+    check_cuda(cudaMemcpyAsync(dst, s.p + at, bytes, cudaMemcpyHostToDevice, st), what);
+}
+
+void kk_ctx::stage_end(cudaStream_t st) {
+    StageSlot &s = stage[stage_k];
+    if (cudaEventRecord(s.ev, st) == cudaSuccess)
+        s.pending = true;
+    else
+        cudaStreamSynchronize(st);  // no event: make sure no copy still reads the slot
 }
 
 // Host tables, computed with the C library exactly as the reference does.
@@ -835,7 +894,7 @@ struct Runner {
         }
         const size_t bytes = (size_t)((char *)(hcum + n) - (char *)hT);
         c.d_batch.ensure(bytes);
-        check_cuda(cudaMemcpyAsync(c.d_batch.p, hT, bytes, cudaMemcpyHostToDevice, st), "upload batch");
+        c.upload(c.d_batch.p, hT, bytes, st, "upload batch");
         char *base = (char *)c.d_batch.p;
         B.n = P.n;
         B.T = (const int32_t *)base;
@@ -861,9 +920,7 @@ struct Runner {
             a.beta = bbase + n * (size_t)s.off;
         }
         c.d_sites.ensure(c.h_sites.size() * sizeof(AdainSite));
-        check_cuda(cudaMemcpyAsync(c.d_sites.p, c.h_sites.data(), c.h_sites.size() * sizeof(AdainSite),
-                                   cudaMemcpyHostToDevice, st),
-                   "upload adain sites");
+        c.upload(c.d_sites.p, c.h_sites.data(), c.h_sites.size() * sizeof(AdainSite), st, "upload adain sites");
         adain_affine((const AdainSite *)c.d_sites.p, (int)c.h_sites.size(), style_dev, P.n, st);
         ++c.n_launches;
         ms = (float2 *)c.buf("stats", n * 1090 * 2);
@@ -1588,6 +1645,25 @@ int guarded(F &&f) noexcept {
 
 void use_device(kk_ctx *ctx) { check_cuda(cudaSetDevice(ctx->device), "cudaSetDevice"); }
 
+// Brackets one entry point's work on `st`: orders it after the context's
+// previous call, which may have run on another stream and whose workspaces
+// this call reuses, and opens a pinned staging slot for its small uploads.
+struct CallScope {
+    kk_ctx &c;
+    cudaStream_t st;
+    CallScope(kk_ctx &ctx, cudaStream_t s) : c(ctx), st(s) {
+        if (c.done_recorded) check_cuda(cudaStreamWaitEvent(st, c.ev_done, 0), "order after the previous call");
+        c.stage_begin();
+    }
+    ~CallScope() {
+        c.stage_end(st);
+        c.done_recorded = cudaEventRecord(c.ev_done, st) == cudaSuccess;
+        if (!c.done_recorded) cudaStreamSynchronize(st);  // nothing to wait for next time
+    }
+    CallScope(const CallScope &) = delete;
+    CallScope &operator=(const CallScope &) = delete;
+};
+
 // After a synchronising call: surfaces a bounded-wait expiry recorded by the
 // tensor-core kernel (and clears it).
 void check_device_error(kk_ctx *ctx) {
@@ -1629,6 +1705,8 @@ int kk_ctx_create(int device, kk_ctx **out) {
         check_cuda(cudaStreamCreateWithFlags(&c->st2, cudaStreamNonBlocking), "stream");
         check_cuda(cudaEventCreateWithFlags(&c->ev_inputs, cudaEventDisableTiming), "event");
         check_cuda(cudaEventCreateWithFlags(&c->ev_src, cudaEventDisableTiming), "event");
+        check_cuda(cudaEventCreateWithFlags(&c->ev_done, cudaEventDisableTiming), "event");
+        for (auto &s : c->stage) check_cuda(cudaEventCreateWithFlags(&s.ev, cudaEventDisableTiming), "event");
         check_cuda(conv_simt_init(), "conv init");
         *out = c.release();
         return KK_OK;
@@ -1638,6 +1716,7 @@ int kk_ctx_create(int device, kk_ctx **out) {
 void kk_ctx_destroy(kk_ctx *ctx) {
     if (!ctx) return;
     cudaSetDevice(ctx->device);
+    if (ctx->done_recorded) cudaEventSynchronize(ctx->ev_done);  // a call on the caller's stream
     cudaStreamSynchronize(ctx->st);
     cudaStreamSynchronize(ctx->st2);
     delete ctx;
@@ -1647,6 +1726,8 @@ int kk_weights_upload(kk_ctx *ctx, const kk_tensor_desc *descs, size_t n) {
     return guarded([&] {
         if (!ctx || (!descs && n)) throw KKError(KK_ERROR_INVALID_ARGUMENT, "null argument");
         use_device(ctx);
+        // the packed weights may be rewritten below: let every earlier call finish
+        if (ctx->done_recorded) check_cuda(cudaEventSynchronize(ctx->ev_done), "sync");
         check_cuda(cudaStreamSynchronize(ctx->st), "sync");
         std::vector<float> tmp;
         for (size_t i = 0; i < n; ++i) {
@@ -1677,7 +1758,7 @@ int kk_weights_upload(kk_ctx *ctx, const kk_tensor_desc *descs, size_t n) {
                 cudaFree(it->second.d);
                 ctx->w.erase(it);
             }
-            check_cuda(cudaMalloc(&t.d, (size_t)cnt * 4), "cudaMalloc weight");
+            check_cuda(device_malloc((void **)&t.d, (size_t)cnt * 4), "cudaMalloc weight");
             check_cuda(cudaMemcpy(t.d, tmp.data(), (size_t)cnt * 4, cudaMemcpyHostToDevice), "upload weight");
             ctx->w.emplace(d.name, std::move(t));
         }
@@ -1702,6 +1783,7 @@ int kk_decoder_forward_device(kk_ctx *ctx, int32_t n_utts, const int32_t *n_fram
         check_ready(ctx, true);
         const Plan P = make_plan(n_frames, n_utts);
         cudaStream_t st = stream ? (cudaStream_t)stream : ctx->st;
+        CallScope call_scope(*ctx, st);
         Runner r(*ctx, P, st);
         r.decoder_forward(asr, f0, noise, style, audio);
         check_cuda(cudaGetLastError(), "kernel launch");
@@ -1725,6 +1807,7 @@ int kk_decoder_forward(kk_ctx *ctx, int32_t n_utts, const int32_t *n_frames, con
         float *d_style = ctx->buf("in_style", (size_t)kStyle * n_utts);
         float *d_audio = ctx->buf("out_audio", 600 * tot);
         cudaStream_t st = ctx->st;
+        CallScope call_scope(*ctx, st);
         check_cuda(cudaMemcpyAsync(d_asr, asr, 512 * tot * 4, cudaMemcpyHostToDevice, st), "H2D");
         check_cuda(cudaMemcpyAsync(d_f0, f0, 2 * tot * 4, cudaMemcpyHostToDevice, st), "H2D");
         check_cuda(cudaMemcpyAsync(d_n, noise, 2 * tot * 4, cudaMemcpyHostToDevice, st), "H2D");
@@ -1754,6 +1837,7 @@ int kk_generator_forward(kk_ctx *ctx, int32_t n_utts, const int32_t *n_decoder_f
         float *d_style = ctx->buf("in_style", (size_t)kStyle * n_utts);
         float *d_audio = ctx->buf("out_audio", 300 * tot);
         cudaStream_t st = ctx->st;
+        CallScope call_scope(*ctx, st);
         check_cuda(cudaMemcpyAsync(d_dec, decoder, 512 * tot * 4, cudaMemcpyHostToDevice, st), "H2D");
         check_cuda(cudaMemcpyAsync(d_f0, f0, tot * 4, cudaMemcpyHostToDevice, st), "H2D");
         check_cuda(cudaMemcpyAsync(d_style, style, (size_t)kStyle * n_utts * 4, cudaMemcpyHostToDevice, st), "H2D");
@@ -1784,6 +1868,7 @@ int kk_istft(kk_ctx *ctx, int64_t n_frames, const float *post, float *audio) {
                        "tables");
         }
         cudaStream_t st = ctx->st;
+        CallScope call_scope(*ctx, st);
         // one utterance with base length n_frames - 1 and a_nf = 1:
         // frames = T + 1, samples = 5 T, offsets 0
         const int32_t T = (int32_t)(n_frames - 1);
@@ -1850,7 +1935,7 @@ Runner::Seqs lstm_seqs(kk_ctx &c, int32_t n_seqs, const int32_t *n_steps, cudaSt
     if ((int64_t)q.max_len * n_seqs > INT32_MAX) throw KKError(KK_ERROR_INVALID_ARGUMENT, "batch too large");
     const size_t bytes = (size_t)((char *)(hc + n_seqs) - (char *)h.data());
     float *d = c.buf("lstm_seq", (bytes + 3) / 4);
-    check_cuda(cudaMemcpyAsync(d, h.data(), bytes, cudaMemcpyHostToDevice, st), "upload lengths");
+    c.upload(d, h.data(), bytes, st, "upload lengths");
     q.d_len = (const int32_t *)d;
     q.d_cum = (const int64_t *)((char *)d + ((char *)hc - (char *)h.data()));
     return q;
@@ -1867,6 +1952,7 @@ int kk_bilstm_forward(kk_ctx *ctx, const char *prefix, int32_t n_seqs, const int
         const LstmLayer &L = c.lstm_layer(prefix);
         if (in_dim != L.in_dim) throw KKError(KK_ERROR_INVALID_ARGUMENT, "in_dim does not match the weights");
         cudaStream_t st = c.st;
+        CallScope call_scope(*ctx, st);
         Runner::Seqs q = lstm_seqs(c, n_seqs, n_steps, st);
         Plan P = lstm_plan(n_seqs, q.max_len);
         Runner r(c, P, st);
@@ -2173,6 +2259,7 @@ int kk_duration_encoder_forward(kk_ctx *ctx, int32_t n_seqs, const int32_t *n_st
         use_device(ctx);
         kk_ctx &c = *ctx;
         cudaStream_t st = c.st;
+        CallScope call_scope(*ctx, st);
         for (int b = 0; b < n_seqs; ++b)
             if (n_steps[b] < 1 || n_steps[b] > kMaxSteps)
                 throw KKError(KK_ERROR_INVALID_ARGUMENT, "sequence length out of range [1, 65536]");
@@ -2197,6 +2284,7 @@ int kk_duration_encoder_forward_device(kk_ctx *ctx, int32_t n_seqs, const int32_
             throw KKError(KK_ERROR_INVALID_ARGUMENT, "null argument");
         use_device(ctx);
         cudaStream_t st = stream ? (cudaStream_t)stream : ctx->st;
+        CallScope call_scope(*ctx, st);
         duration_encoder_device(*ctx, n_seqs, n_steps, x, style, out, st);
         return KK_OK;
     });
@@ -2210,6 +2298,7 @@ int kk_prosody_f0n(kk_ctx *ctx, int32_t n_utts, const int32_t *n_frames, const f
         use_device(ctx);
         kk_ctx &c = *ctx;
         cudaStream_t st = c.st;
+        CallScope call_scope(*ctx, st);
         int64_t rows = 0;
         for (int b = 0; b < n_utts; ++b) {
             if (n_frames[b] < 1 || n_frames[b] > kMaxFrames)
@@ -2241,6 +2330,7 @@ int kk_prosody_f0n_device(kk_ctx *ctx, int32_t n_utts, const int32_t *n_frames, 
                 throw KKError(KK_ERROR_INVALID_ARGUMENT, "utterance length out of range [1, 8192]");
         use_device(ctx);
         cudaStream_t st = stream ? (cudaStream_t)stream : ctx->st;
+        CallScope call_scope(*ctx, st);
         prosody_device(*ctx, n_utts, n_frames, en, style, f0, n, st);
         return KK_OK;
     });
@@ -2270,6 +2360,7 @@ int kk_text_encoder_forward(kk_ctx *ctx, int32_t n_seqs, const int32_t *n_tokens
         for (int64_t i = 0; i < rows; ++i)
             if (ids[i] < 0 || ids[i] >= vocab) throw KKError(KK_ERROR_INVALID_ARGUMENT, "token id out of range");
         cudaStream_t st = c.st;
+        CallScope call_scope(*ctx, st);
         int32_t *d_ids = (int32_t *)c.buf("te_ids", (size_t)rows);
         float *d_out = c.buf("te_out", (size_t)rows * 512);
         check_cuda(cudaMemcpyAsync(d_ids, ids, (size_t)rows * 4, cudaMemcpyHostToDevice, st), "upload ids");
@@ -2288,6 +2379,7 @@ int kk_text_encoder_forward_device(kk_ctx *ctx, int32_t n_seqs, const int32_t *n
         token_rows(n_seqs, n_tokens);
         use_device(ctx);
         cudaStream_t st = stream ? (cudaStream_t)stream : ctx->st;
+        CallScope call_scope(*ctx, st);
         text_encoder_device(*ctx, n_seqs, n_tokens, ids, out, st);
         return KK_OK;
     });
@@ -2305,6 +2397,7 @@ int kk_albert_forward(kk_ctx *ctx, int32_t n_seqs, const int32_t *n_tokens, cons
             if (ids[i] < 0 || ids[i] >= vocab) throw KKError(KK_ERROR_INVALID_ARGUMENT, "token id out of range");
         const int D = (int)c.W("kokopop.bert_encoder.weight").ne[1];
         cudaStream_t st = c.st;
+        CallScope call_scope(*ctx, st);
         int32_t *d_ids = (int32_t *)c.buf("al_ids", (size_t)rows);
         float *d_out = c.buf("al_out", (size_t)rows * D);
         check_cuda(cudaMemcpyAsync(d_ids, ids, (size_t)rows * 4, cudaMemcpyHostToDevice, st), "upload ids");
@@ -2323,6 +2416,7 @@ int kk_albert_forward_device(kk_ctx *ctx, int32_t n_seqs, const int32_t *n_token
         token_rows(n_seqs, n_tokens);
         use_device(ctx);
         cudaStream_t st = stream ? (cudaStream_t)stream : ctx->st;
+        CallScope call_scope(*ctx, st);
         albert_device(*ctx, n_seqs, n_tokens, ids, out, st);
         return KK_OK;
     });
@@ -2336,6 +2430,7 @@ int kk_duration_head_forward(kk_ctx *ctx, int32_t n_seqs, const int32_t *n_token
         use_device(ctx);
         kk_ctx &c = *ctx;
         cudaStream_t st = c.st;
+        CallScope call_scope(*ctx, st);
         for (int b = 0; b < n_seqs; ++b)
             if (n_tokens[b] < 1 || n_tokens[b] > kMaxSteps)
                 throw KKError(KK_ERROR_INVALID_ARGUMENT, "sequence length out of range [1, 65536]");
@@ -2358,6 +2453,7 @@ int kk_duration_head_forward_device(kk_ctx *ctx, int32_t n_seqs, const int32_t *
             throw KKError(KK_ERROR_INVALID_ARGUMENT, "null argument");
         use_device(ctx);
         cudaStream_t st = stream ? (cudaStream_t)stream : ctx->st;
+        CallScope call_scope(*ctx, st);
         duration_head_device(*ctx, n_seqs, n_tokens, d, durations, st);
         return KK_OK;
     });
@@ -2370,6 +2466,7 @@ int kk_duration_proj(kk_ctx *ctx, int64_t n_rows, const float *h, float *duratio
         use_device(ctx);
         kk_ctx &c = *ctx;
         cudaStream_t st = c.st;
+        CallScope call_scope(*ctx, st);
         const DevTensor *w = nullptr, *b = nullptr;
         duration_proj_weights(c, w, b);
         const int32_t n = (int32_t)n_rows;
@@ -2398,6 +2495,7 @@ int kk_align_durations(kk_ctx *ctx, int64_t n_tokens, const float *durations, fl
         use_device(ctx);
         kk_ctx &c = *ctx;
         cudaStream_t st = c.st;
+        CallScope call_scope(*ctx, st);
         // duration_to_frames (kokoro.cpp:181-193): a non-finite or
         // non-positive speed counts as 1
         if (!std::isfinite(speed) || speed <= 0.0f) speed = 1.0f;
@@ -2461,6 +2559,15 @@ int kk_profile_read(kk_ctx *ctx, kk_profile *out, int reset) {
         }
         return KK_OK;
     });
+}
+
+int kk_allocation_count(uint64_t *out) {
+    if (!out) {
+        g_last_error = "kk_allocation_count: out is null";
+        return KK_ERROR_INVALID_ARGUMENT;
+    }
+    *out = g_allocations.load(std::memory_order_relaxed);
+    return KK_OK;
 }
 
 }  // extern "C"

@@ -21,6 +21,11 @@ struct KKError : std::runtime_error {
 void check_cuda(cudaError_t e, const char *what);
 float half_to_float(uint16_t h);
 
+// Every device and pinned-host allocation of the library goes through these
+// two, which count it (kk_allocation_count).
+cudaError_t device_malloc(void **p, size_t bytes);
+cudaError_t pinned_malloc(void **p, size_t bytes);
+
 // A weight as F32 values on the device (F16 tensors are widened exactly);
 // `f16` records the stored type because it selects ggml's F16 arithmetic.
 struct DevTensor {
@@ -150,6 +155,31 @@ struct kk_ctx {
     std::unordered_map<std::string, int> site_index;
     int64_t site_total_C = 0;
     kk::DevBuf d_tables;
+    // Pinned staging of each call's small host-built tables (batch
+    // descriptors, AdaIN site tables, sequence lengths), so that their
+    // uploads are asynchronous: a copy from pageable memory would first wait
+    // for the stream. Two slots serve alternate calls; a slot is written
+    // again only after the copies of the call that last used it have
+    // finished (its event).
+    struct StageSlot {
+        char *p = nullptr;
+        size_t cap = 0, used = 0;
+        cudaEvent_t ev = nullptr;
+        bool pending = false;
+        std::vector<char *> retired;  // outgrown buffers, freed once `ev` has passed
+    };
+    StageSlot stage[2];
+    int stage_k = 0;
+    void stage_begin();
+    // copies `bytes` of host data into the current slot and queues their
+    // upload to `dst` on `st`
+    void upload(void *dst, const void *src, size_t bytes, cudaStream_t st, const char *what);
+    void stage_end(cudaStream_t st);
+    // Calls on one context share its workspaces, so each call is ordered
+    // after the previous one even when they run on different streams: a call
+    // waits (on the device) for the event the previous call recorded.
+    cudaEvent_t ev_done = nullptr;
+    bool done_recorded = false;
     // per-forward staging
     std::vector<kk::AdainSite> h_sites;
     kk::DevBuf d_sites;

@@ -7,22 +7,28 @@
 // cudaFree may synchronise the whole device and stall it), or a serving
 // process that fixes its device-memory budget at start-up (an allocation can
 // fail later, mid-request). This entry point needs no context and allocates
-// nothing: everything it stages lives in one file-scope device array, sized
-// for KK_ISTFT_STATIC_MAX_FRAMES frames and reserved when the library's
-// device code is loaded. The arithmetic is the same kernel as kk_istft.
+// nothing itself: everything it stages lives in one file-scope device array,
+// sized for KK_ISTFT_STATIC_MAX_FRAMES frames. The arithmetic is the same
+// kernel as kk_istft.
+//
+// When the array's memory is reserved: with CUDA's default lazy module
+// loading, the module that holds the array is loaded (and the array's memory
+// reserved) the first time host code looks up its address on a device, i.e.
+// on the first call of this entry point on that device. A call with
+// n_frames = 0 or 1 does that and nothing else, so a caller makes one such
+// call per device at start-up (or runs with CUDA_MODULE_LOADING=EAGER, which
+// loads every module when the context is created).
 //
 // Scratch layout (bytes from the start of the array):
-//   [0, 4096)                 iSTFT tables (written once per device)
+//   [0, 4096)                 iSTFT tables (uploaded by every call)
 //   [4096, 4352)              batch descriptor of this call (T, row offset,
 //                             output offset)
 //   [4352, ...)               post, 22 x n_frames F32 (this call's input)
 //   [audio_off(n_frames), ...) audio, 5 (n_frames - 1) F32 (this call's output)
-// Nothing in it has to start at zero: the tables are written before their
-// first use, and every call writes its descriptor, its whole input and every
-// output sample before reading them.
+// Nothing in it has to start at zero: every call writes the tables, its
+// descriptor, its whole input and every output sample before reading them.
 #include "kk_host.h"
 
-#include <mutex>
 #include <string>
 
 namespace {
@@ -48,25 +54,24 @@ struct Desc {
 };
 static_assert(sizeof(Desc) <= kPostOff - kDescOff, "descriptor does not fit its slot");
 
-constexpr int kMaxDevices = 64;
-std::mutex g_init_mu;
-unsigned char *g_base[kMaxDevices] = {};  // device address of the scratch, per device
-
-// First call on a device (that device current): look up the array's device
-// address and upload the tables. Synchronous.
-unsigned char *scratch_for(int device) {
-    std::lock_guard<std::mutex> lk(g_init_mu);
-    if (!g_base[device]) {
-        void *p = nullptr;
-        kk::check_cuda(cudaGetSymbolAddress(&p, g_istft_scratch), "cudaGetSymbolAddress (iSTFT scratch)");
+// The iSTFT tables in host memory, computed once per process.
+const kk::IstftTables &host_tables() {
+    static const kk::IstftTables t = [] {
         kk::StftTables stt;
         kk::IstftTables ist;
         kk::fill_tables(stt, ist);
-        kk::check_cuda(cudaMemcpy((unsigned char *)p + kTabOff, &ist, sizeof ist, cudaMemcpyHostToDevice),
-                       "upload iSTFT tables");
-        g_base[device] = (unsigned char *)p;
-    }
-    return g_base[device];
+        return ist;
+    }();
+    return t;
+}
+
+// The array's device address on the current device. Looked up on every call
+// (the lookup allocates nothing once the module is loaded), so nothing goes
+// stale if the caller resets the device or recreates its primary context.
+unsigned char *scratch_base() {
+    void *p = nullptr;
+    kk::check_cuda(cudaGetSymbolAddress(&p, g_istft_scratch), "cudaGetSymbolAddress (iSTFT scratch)");
+    return (unsigned char *)p;
 }
 
 // Makes `device` current for the call and restores the caller's device.
@@ -92,11 +97,20 @@ extern "C" int kk_istft_static(int device, int64_t n_frames, const float *post, 
                           "kk_istft_static: n_frames = " + std::to_string(n_frames) +
                               " exceeds the static scratch, which holds at most " + std::to_string(kMaxFrames) +
                               " frames (use kk_istft for longer inputs)");
-        if (device < 0 || device >= kMaxDevices)
-            throw KKError(KK_ERROR_INVALID_ARGUMENT, "kk_istft_static: device index out of range");
-        if (n_frames <= 1) return KK_OK;  // (frames - 1) * hop = 0 samples
+        if (device < 0) throw KKError(KK_ERROR_INVALID_ARGUMENT, "kk_istft_static: negative device index");
+        int n_dev = 0;
+        if (cudaGetDeviceCount(&n_dev) != cudaSuccess) {
+            cudaGetLastError();  // leave no error pending on this thread
+            n_dev = 0;
+        }
+        if (device >= n_dev)
+            throw KKError(KK_ERROR_INVALID_ARGUMENT, "kk_istft_static: device " + std::to_string(device) +
+                                                         " out of range (" + std::to_string(n_dev) +
+                                                         " CUDA devices)");
         DeviceScope scope(device);
-        unsigned char *base = scratch_for(device);
+        cudaGetLastError();  // an error left pending by earlier runtime calls is not this call's
+        unsigned char *base = scratch_base();  // the first call on a device loads the module here
+        if (n_frames <= 1) return KK_OK;       // (frames - 1) * hop = 0 samples
         cudaStream_t st = (cudaStream_t)stream;
         const int32_t T = (int32_t)(n_frames - 1);
         const Desc h{T, 0, 0, 0};
@@ -104,6 +118,9 @@ extern "C" int kk_istft_static(int device, int64_t n_frames, const float *post, 
         float *d_post = (float *)(base + kPostOff);
         float *d_audio = (float *)(base + audio_off(n_frames));
         // pageable sources: each copy has read its host bytes when it returns
+        kk::check_cuda(cudaMemcpyAsync(base + kTabOff, &host_tables(), sizeof(kk::IstftTables),
+                                       cudaMemcpyHostToDevice, st),
+                       "upload iSTFT tables");
         kk::check_cuda(cudaMemcpyAsync(d_desc, &h, sizeof h, cudaMemcpyHostToDevice, st), "upload descriptor");
         kk::check_cuda(cudaMemcpyAsync(d_post, post, 22 * (size_t)n_frames * sizeof(float), cudaMemcpyHostToDevice, st),
                        "upload post");

@@ -195,9 +195,10 @@ void worker_ctx(kk_queue *q, kk_ctx *ctx) {
     bool ok = cudaSetDevice(ctx->device) == cudaSuccess && cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) ==
                                                                 cudaSuccess;
     for (int i = 0; i < 2 && ok; ++i)
-        ok = cudaMallocHost(&s[i].h_in, n_in * 4) == cudaSuccess && cudaMallocHost(&s[i].h_out, n_out * 4) ==
-                                                                        cudaSuccess &&
-             cudaMalloc(&s[i].d_in, n_in * 4) == cudaSuccess && cudaMalloc(&s[i].d_out, n_out * 4) == cudaSuccess &&
+        ok = kk::pinned_malloc((void **)&s[i].h_in, n_in * 4) == cudaSuccess &&
+             kk::pinned_malloc((void **)&s[i].h_out, n_out * 4) == cudaSuccess &&
+             kk::device_malloc((void **)&s[i].d_in, n_in * 4) == cudaSuccess &&
+             kk::device_malloc((void **)&s[i].d_out, n_out * 4) == cudaSuccess &&
              cudaEventCreateWithFlags(&s[i].ev, cudaEventDisableTiming) == cudaSuccess;
     int k = 0;
     bool busy = false;  // slot k ^ 1 holds a batch in flight
@@ -313,8 +314,12 @@ extern "C" {
 int kk_queue_create(kk_ctx *const *ctxs, int32_t n_ctx, int32_t max_batch, int64_t max_batch_frames,
                     int32_t max_wait_us, kk_queue **out) {
     if (!ctxs || n_ctx < 1 || !out) return q_fail(KK_ERROR_INVALID_ARGUMENT, "null argument");
-    for (int i = 0; i < n_ctx; ++i)
+    for (int i = 0; i < n_ctx; ++i) {
         if (!ctxs[i]) return q_fail(KK_ERROR_INVALID_ARGUMENT, "null context");
+        // two workers on one context would share its workspaces without a lock
+        for (int j = 0; j < i; ++j)
+            if (ctxs[j] == ctxs[i]) return q_fail(KK_ERROR_INVALID_ARGUMENT, "the same context appears twice");
+    }
     return q_guard([&] {
         kk_queue *q = new kk_queue();
         const int rc = q_config(q, max_batch, max_batch_frames, max_wait_us);

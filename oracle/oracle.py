@@ -32,7 +32,14 @@ class TensorDesc(ctypes.Structure):
 
 
 def build() -> None:
-    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    """Builds the oracle and, where the reference checkout exists (the
+    KOKOPOP_REFERENCE environment variable, else /root/reference), the
+    reference's own host-side sources into _ref/."""
+    ref = os.environ.get("KOKOPOP_REFERENCE", "/root/reference")
+    args = ["make", "-s", "-C", HERE]
+    if os.path.isdir(os.path.join(ref, "src")):
+        args.append(f"REF={ref}")
+    subprocess.run(args, check=True)
 
 
 def _ptr(a: np.ndarray):
@@ -282,8 +289,44 @@ def ref():
         R = ctypes.CDLL(REF_PATH)
         R.kkref_istft_kokoro.argtypes = [_f32p, ctypes.c_int64, _f32p, ctypes.POINTER(ctypes.c_int64)]
         R.kkref_lstm_direction.argtypes = [_f32p, _f32p, _f32p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, _f32p]
+        R.kkref_harmonic_stft.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int64, _f32p, ctypes.c_float, _f32p, _f32p]
+        R.kkref_duration_to_frames.argtypes = [ctypes.c_float, ctypes.c_float]
+        R.kkref_duration_mask.argtypes = [ctypes.POINTER(ctypes.c_int32), ctypes.c_int64, ctypes.c_int64, _f32p]
         _ref = R
     return _ref
+
+
+def ref_harmonic_stft(f0: np.ndarray, target_frames: int, merge_w: np.ndarray, merge_b: float):
+    """The reference's fill_harmonic_stft (audio_utils.cpp:120-422, compiled
+    unchanged): har [22, target_frames] and the sine source [300 len(f0)]."""
+    f0 = np.ascontiguousarray(f0, np.float32)
+    mw = np.ascontiguousarray(np.asarray(merge_w, np.float32).ravel())
+    har = np.zeros((22, target_frames), np.float32)
+    src = np.zeros(300 * len(f0), np.float32)
+    if ref().kkref_harmonic_stft(_ptr(f0), len(f0), target_frames, _ptr(mw), float(merge_b), _ptr(har),
+                                 _ptr(src)) != 0:
+        raise RuntimeError("reference fill_harmonic_stft failed")
+    return har, src
+
+
+def ref_duration_frames(durations: np.ndarray, speed: float) -> np.ndarray:
+    """The reference's duration_to_frames(value, speed) (kokoro.cpp:181-193)
+    per token."""
+    R = ref()
+    return np.array([R.kkref_duration_to_frames(float(v), float(speed)) for v in
+                     np.asarray(durations, np.float32)], np.int32)
+
+
+def ref_duration_mask(frames: np.ndarray) -> np.ndarray:
+    """The reference's build_duration_mask (kokoro.cpp:115-152): [tokens,
+    total frames], 1 where a frame belongs to the token."""
+    fr = np.ascontiguousarray(frames, np.int32)
+    total = int(fr.sum())
+    mask = np.zeros((len(fr), total), np.float32)
+    if ref().kkref_duration_mask(fr.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), len(fr), total,
+                                 _ptr(mask)) != 0:
+        raise RuntimeError("reference build_duration_mask failed")
+    return mask
 
 
 def ref_istft(post: np.ndarray) -> np.ndarray:

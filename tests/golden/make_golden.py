@@ -7,6 +7,14 @@
   lstm_ref.npz    the deterministic inputs of tests/test_lstm_fused.cpp:64-73
                   (H=33, N=9, forward and reverse) plus a seeded H=64 case,
                   with outputs of the reference's own lstm_fused.cpp
+  harmonic_ref.npz  seeded F0 curves (voiced, unvoiced spans, all unvoiced)
+                  with the harmonic source and its STFT from the reference's
+                  own fill_harmonic_stft (src/arch/kokoro/audio_utils.cpp,
+                  compiled unchanged), which calls the C library's float
+                  sin / cos / tanh / atan2
+  align_ref.npz   edge-case durations at several speeds with the frame counts
+                  of the reference's duration_to_frames and the mask of its
+                  build_duration_mask (src/arch/kokoro/kokoro.cpp)
   oracle_small.npz  regression vectors of the oracle itself (decoder + generator
                   at T=3 for the F32 and F16 weight sets); these are NOT
                   reference outputs (the reference's generator needs ggml,
@@ -68,6 +76,32 @@ def main():
     ls["h64_out_0"] = O.ref_lstm_direction(pre, w, b, False)
     ls["h64_out_1"] = O.ref_lstm_direction(pre, w, b, True)
     np.savez_compressed(os.path.join(OUT, "lstm_ref.npz"), **ls)
+
+    wts = W.config0_weights()
+    mw = wts["kokopop.decoder.generator.m_source.l_linear.weight"].data.astype(np.float32).ravel()
+    mb = float(wts["kokopop.decoder.generator.m_source.l_linear.bias"].data.ravel()[0])
+    hs = {"merge_w": mw, "merge_b": np.float32(mb)}
+    curves = {
+        "voiced": W.make_utterance(np.random.default_rng(31), 8).f0,
+        "gaps": np.array([0, 0, 180, 181.5, 0, 95, 300, 300, 12, 0, 250, 251], np.float32),
+        "unvoiced": np.zeros(6, np.float32),
+    }
+    for k, f0 in curves.items():
+        f0 = np.ascontiguousarray(f0, np.float32)
+        har, src = O.ref_harmonic_stft(f0, 60 * len(f0) + 1, mw, mb)
+        hs[f"f0_{k}"], hs[f"har_{k}"], hs[f"src_{k}"] = f0, har, src
+    np.savez_compressed(os.path.join(OUT, "harmonic_ref.npz"), **hs)
+
+    edge = np.array([0.0, 0.4, 0.5, 1.5, 2.5, 2.5000002, 3.49, 49.5, 50.5, 1e9, np.inf, -np.inf, np.nan, -3.0,
+                     3e9, 1e30, -1e30, 0.49999997, 7.5, 8.5], np.float32)
+    dur = np.concatenate([edge, np.random.default_rng(17).uniform(0.0, 30.0, 60).astype(np.float32)])
+    al = {"durations": dur}
+    for i, sp in enumerate((1.0, 2.0, 0.7, -1.0, float("nan"), float("inf"), 0.0)):
+        al[f"speed_{i}"] = np.float32(sp)
+        al[f"frames_{i}"] = O.ref_duration_frames(dur, sp)
+    al["mask_frames"] = al["frames_0"][:24]
+    al["mask"] = O.ref_duration_mask(al["mask_frames"])
+    np.savez_compressed(os.path.join(OUT, "align_ref.npz"), **al)
 
     sm = {}
     u = W.make_utterance(np.random.default_rng(11), 3)

@@ -80,6 +80,15 @@ def test_front_end_and_queue_entry_points_reject_bad_arguments():
     assert L.kk_queue_submit(None, 0, 4, fp, fp, fp, fp, fp, ctypes.byref(t)) == E
     assert L.kk_queue_wait(None, 1, 0) == E
     L.kk_queue_destroy(None)  # no-op
+    # one context listed twice would give two workers the same workspaces;
+    # the check runs before any context is touched, so any non-null handle serves
+    fake = ctypes.c_void_p(0x1000)
+    ctxs = (ctypes.c_void_p * 2)(fake, fake)
+    assert L.kk_queue_create(ctxs, 2, 64, 1000, 0, ctypes.byref(q)) == E
+    assert "twice" in L.kk_queue_last_error().decode()
+    n = ctypes.c_uint64(0)
+    assert L.kk_allocation_count(ctypes.byref(n)) == kb.KK_OK
+    assert L.kk_allocation_count(None) == E
 
 
 def test_queue_rejects_out_of_range_chunks_and_limits():

@@ -147,7 +147,82 @@ def test_duration_speed_and_alignment_copies_rows():
     np.testing.assert_array_equal(en, expect)
 
 
+def test_duration_frames_and_mask_match_reference_golden_bit_exact():
+    """duration_to_frames and build_duration_mask of the reference's own
+    kokoro.cpp (compiled unchanged into oracle/_ref/): the oracle's frame
+    counts at every speed, and the frames its alignment assigns to each
+    token, equal them exactly."""
+    z = g("align_ref.npz")
+    i = 0
+    while f"frames_{i}" in z.files:
+        frames, total, _ = O.align_durations(z["durations"], float(z[f"speed_{i}"]))
+        np.testing.assert_array_equal(frames, z[f"frames_{i}"])
+        assert total == int(z[f"frames_{i}"].sum())
+        i += 1
+    assert i == 7
+    fr = z["mask_frames"]
+    hidden = np.arange(len(fr), dtype=np.float32)[:, None] * np.ones((1, 3), np.float32)
+    _, total, en = O.align_durations(fr.astype(np.float32), 1.0, hidden)
+    mask = z["mask"]
+    assert mask.shape == (len(fr), total)
+    # the mask is one-hot per frame; en = mask^T . hidden copies that token's row
+    np.testing.assert_array_equal(mask.sum(0), np.ones(total, np.float32))
+    np.testing.assert_array_equal(en[:, 0], mask.argmax(0).astype(np.float32))
+
+
+@pytest.mark.skipif(not O.ref_available(), reason="oracle/_ref not built")
+def test_duration_frames_match_reference_library_on_random_values():
+    rng = np.random.default_rng(23)
+    d = np.concatenate([rng.uniform(-5, 60, 4000), rng.normal(0, 1e6, 500)]).astype(np.float32)
+    d[::97] = np.nextafter(np.round(d[::97]) + np.float32(0.5), np.float32(0)).astype(np.float32)
+    for sp in (1.0, 1.3, 0.25):
+        frames, _, _ = O.align_durations(d, sp)
+        np.testing.assert_array_equal(frames, O.ref_duration_frames(d, sp))
+
+
 # --- R1 harmonic source -----------------------------------------------------
+
+def _merge(wts):
+    mw = wts["kokopop.decoder.generator.m_source.l_linear.weight"].data.astype(np.float32).ravel()
+    mb = float(wts["kokopop.decoder.generator.m_source.l_linear.bias"].data.ravel()[0])
+    return mw, mb
+
+
+def test_harmonic_source_matches_reference_golden_bit_exact():
+    """fill_harmonic_stft of the reference's own audio_utils.cpp (compiled
+    unchanged; the C library's float sin / cos / tanh / atan2): the oracle in
+    its C-library mode reproduces the sine source and every har value (STFT
+    magnitudes and atan2 phases) exactly, for voiced curves, unvoiced gaps
+    and an all-unvoiced curve."""
+    z = g("harmonic_ref.npz")
+    wts = W.config0_weights()
+    mw, mb = _merge(wts)
+    np.testing.assert_array_equal(mw, z["merge_w"])
+    assert np.float32(mb) == z["merge_b"]
+    m = O.OracleModel(wts)
+    m.set_source_libm(True)
+    for k in ("voiced", "gaps", "unvoiced"):
+        f0 = z[f"f0_{k}"]
+        har, src = m.harmonic_stft(f0, 60 * len(f0) + 1)
+        np.testing.assert_array_equal(src, z[f"src_{k}"])
+        np.testing.assert_array_equal(har, z[f"har_{k}"])
+
+
+@pytest.mark.skipif(not O.ref_available(), reason="oracle/_ref not built")
+@pytest.mark.parametrize("T", [1, 40, 200, 800])
+def test_harmonic_source_matches_reference_library(T):
+    """The same against the live reference build, up to the longest
+    utterance of the benchmark pool (T = 800 asr frames, 480 000 samples,
+    i.e. 30 000 renormalisations of the phase recurrence)."""
+    wts = W.config0_weights()
+    mw, mb = _merge(wts)
+    m = O.OracleModel(wts)
+    m.set_source_libm(True)
+    f0 = W.make_utterance(np.random.default_rng(300 + T), T).f0
+    har, src = m.harmonic_stft(f0, 60 * len(f0) + 1)
+    rh, rs = O.ref_harmonic_stft(f0, 60 * len(f0) + 1, mw, mb)
+    np.testing.assert_array_equal(src, rs)
+    np.testing.assert_array_equal(har, rh)
 
 def test_harmonic_source_unvoiced_is_constant_and_phase_held():
     wts = W.config0_weights()
