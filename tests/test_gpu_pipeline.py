@@ -48,3 +48,85 @@ def test_front_end_to_audio():
         assert np.all(np.isfinite(audio)) and np.abs(audio).max() <= 1.0
     finally:
         c.close()
+
+
+def _err(a, b):
+    d = np.abs(np.asarray(a, np.float64) - np.asarray(b, np.float64))
+    return float(d.max()), float(d.mean())
+
+
+def test_ids_to_audio_against_oracle_composition():
+    """Config 2 end to end (F16 weights seed 2, 128 phoneme ids wrapped in
+    pads, seeded U[2, 10] duration override): the device chain from the token
+    ids to the waveform against the oracle's chain of the same stages
+    (kokoro.cpp:199-541 and :669-763).
+
+    Anchored: every device stage is compared with the oracle's stage run on
+    the device's own input to that stage, under that stage's tolerance
+    (ALBERT 2e-3 max / 1e-4 mean, duration encoder 3e-3 / 1e-4, duration
+    head 1e-4, text encoder 1e-4, prosody 1e-4, waveform 1e-3), so every
+    hand-over between stages is checked at the configuration's sizes; frames
+    and the alignment are bit-exact. Free-running: the oracle's own chain
+    from the ids gives F0 / N curves and audio that are printed beside the
+    device's (the differences of the half-rounded stages compound through
+    the F0 curve into the harmonic source's phase)."""
+    weights = {}
+    weights.update(W.config2_frontend_weights())
+    weights.update(W.prosody_weights(f16=True))
+    weights.update(W.config2_weights())
+    rng = np.random.default_rng(52)
+    ids = W.token_ids(rng, 128)
+    n = len(ids)
+    voice = rng.normal(0, 0.1, 256).astype(np.float32)
+    style_d, style_p = voice[:128].copy(), voice[128:].copy()
+    override = rng.integers(2, 11, size=n).astype(np.float32)
+    m = O.OracleModel(weights)
+    c = kb.Context(0)
+    try:
+        c.upload(weights)
+        # anchored stage by stage
+        bert = c.albert([ids])[0]
+        e = _err(bert, m.albert(ids))
+        print(f"ALBERT: {e[0]:.3g} max, {e[1]:.3g} mean")
+        assert e[0] < 2e-3 and e[1] < 1e-4
+        d = c.duration_encoder([bert], [style_p])[0]
+        e = _err(d, m.duration_encoder(bert, style_p))
+        print(f"duration encoder: {e[0]:.3g} max, {e[1]:.3g} mean")
+        assert e[0] < 3e-3 and e[1] < 1e-4
+        dur = c.duration_head([d])[0]
+        e = _err(dur, m.duration_head(d))
+        print(f"duration head: {e[0]:.3g} max")
+        assert e[0] < 1e-4
+        frames, total, en = c.align_durations(override, 1.0, d)
+        f_or, t_or, en_or = O.align_durations(override, 1.0, d)
+        np.testing.assert_array_equal(frames, f_or)
+        assert total == t_or == int(override.sum())
+        np.testing.assert_array_equal(en, en_or)
+        (f0, nn), = c.prosody_f0n([en], [style_p])
+        wf0, wn = m.prosody_f0n(en, style_p)
+        e0, en_e = _err(f0, wf0), _err(nn, wn)
+        print(f"prosody F0 {e0[0]:.3g}, N {en_e[0]:.3g} max")
+        assert e0[0] < 1e-4 and en_e[0] < 1e-4
+        t_en = c.text_encoder([ids])[0]
+        e = _err(t_en, m.text_encoder(ids))
+        print(f"text encoder: {e[0]:.3g} max")
+        assert e[0] < 1e-4
+        _, _, asr_fm = c.align_durations(override, 1.0, t_en)
+        u = W.Utterance(T=int(total), asr=np.ascontiguousarray(asr_fm.T), f0=f0, noise=nn, style=style_d)
+        audio = c.decoder_forward([u])[0]
+        want = m.decoder_forward(u.asr, u.f0, u.noise, u.style)
+        e = _err(audio, want)
+        print(f"decoder (T = {total}): {e[0]:.3g} max, {e[1]:.3g} mean")
+        assert audio.shape == (600 * total,) and e[0] < 1e-3
+        # free-running: the oracle's own chain from the ids
+        d_o = m.duration_encoder(m.albert(ids), style_p)
+        _, _, en_o = O.align_durations(override, 1.0, d_o)
+        f0_o, n_o = m.prosody_f0n(en_o, style_p)
+        _, _, asr_o = O.align_durations(override, 1.0, m.text_encoder(ids))
+        audio_o = m.decoder_forward(np.ascontiguousarray(asr_o.T), f0_o, n_o, style_d)
+        ef, ea = _err(f0, f0_o), _err(audio, audio_o)
+        print(f"free-running: F0 {ef[0]:.3g} max (|F0| up to {float(np.abs(f0_o).max()):.3g}), "
+              f"audio {ea[0]:.3g} max, {ea[1]:.3g} mean")
+        assert np.all(np.isfinite(audio_o)) and audio_o.shape == audio.shape
+    finally:
+        c.close()
