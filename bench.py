@@ -37,6 +37,9 @@ FLOP_PER_AUDIO_S = None  # filled from the model dimensions below
 # capture of the batch-8 step (dram__bytes_read.sum + dram__bytes_write.sum of
 # one forward); traffic grows with the rows processed.
 CONV_DRAM_BYTES_PER_AUDIO_S = 1.483e8
+# DRAM bytes measured by ncu per algorithmic byte for the tensor-bound
+# convolutions (per-shape captures of single launches); None until measured.
+CONV_TENSOR_DRAM_PER_ALGO_BYTE = None
 
 
 def algorithmic_flop_per_asr_frame() -> float:
@@ -58,6 +61,56 @@ def algorithmic_flop_per_asr_frame() -> float:
     mac += 120 * 6 * 128 * 128 * (11 + 3 + 7 + 11)     # noise_res.1 (k11) + resblocks
     mac += 120 * 128 * 22 * 7                          # conv_post
     return 2.0 * mac
+
+
+def roofline_classes(records, steps, step_ms, pk, pk_kind):
+    """Groups the timed launches of the timed region (kk_profile_records) by
+    class and sets each class against its roofline: convolutions whose
+    arithmetic intensity (algorithmic FLOP per algorithmic DRAM byte) reaches
+    the ridge point of the measured peaks are tensor-bound (TFLOP/s against
+    the sustained dense bf16 peak), the others HBM-bound (GB/s against the
+    measured copy bandwidth), like every memory pass. The LSTM recurrence is
+    bound by its sequential steps, not by a pipe. Per step: launches, device
+    ms and its share of the step (the source runs on a side stream,
+    overlapped with the decoder)."""
+    hbm = float(pk["hbm_gbs"])
+    tf = float(pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")))
+    ridge = tf * 1e12 / (hbm * 1e9)
+    names = {"operand": "operand pass (AdaIN + Snake / LeakyReLU -> half operand)",
+             "stats": "instance-norm statistics pass", "istft": "conv_post -> iSTFT",
+             "source": "harmonic source + STFT (side stream)", "lstm": "LSTM recurrence",
+             "other": "packing, upsampling, ConvTranspose edge row",
+             "conv_tensor": "dense conv, tensor-bound (k >= 7 and the 1024-channel decoder convs)",
+             "conv_hbm": "dense conv, HBM-bound (k = 3 at 128 / 256 channels, 1x1, ConvTranspose phases)"}
+    agg = {}
+    for r in records:
+        k = r["kind"]
+        if k == "conv":
+            k = "conv_tensor" if r["bytes"] > 0 and r["flop"] / r["bytes"] >= ridge else "conv_hbm"
+        a = agg.setdefault(k, {"launches": 0, "ms": 0.0, "flop": 0.0, "bytes": 0.0})
+        a["launches"] += 1
+        a["ms"] += r["ms"]
+        a["flop"] += r["flop"]
+        a["bytes"] += r["bytes"]
+    out = {}
+    for k, a in agg.items():
+        s = a["ms"] / 1e3
+        c = {"what": names.get(k, k), "launches_per_step": a["launches"] / steps, "ms_per_step": a["ms"] / steps,
+             "share_of_step": (a["ms"] / steps) / step_ms if step_ms else None}
+        if k == "conv_tensor":
+            c.update(bound="tensor", achieved=a["flop"] / s / 1e12 if s else None, peak=tf, unit="TFLOP/s")
+        elif k == "lstm":
+            c.update(bound="latency (sequential steps)", achieved=a["flop"] / s / 1e12 if s else None,
+                     peak=None, unit="TFLOP/s")
+        else:
+            c.update(bound="hbm", achieved=a["bytes"] / s / 1e9 if s else None, peak=hbm, unit="GB/s")
+        c["frac"] = c["achieved"] / c["peak"] if c.get("peak") and c.get("achieved") is not None else None
+        c["algorithmic_flop_per_step"] = a["flop"] / steps
+        c["algorithmic_bytes_per_step"] = a["bytes"] / steps
+        out[k] = c
+    out["ridge_flop_per_byte"] = ridge
+    out["peak_source"] = f"{pk_kind}: copy {hbm:.0f} GB/s, bf16 dense sustained {tf:.0f} TFLOP/s"
+    return out
 
 
 def peaks():
@@ -175,12 +228,47 @@ def reference_arm(args):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
         "config": config_dict(),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": "one utterance (T<=240 asr frames) of the pool per step, oracle port of the "
-                                   "reference's ggml CPU path"},
+                         "sample": "one utterance per step, cycling over the pool's utterances with T<=240 asr "
+                                   "frames (not the pool's U[40,800] length mix); the oracle port of the "
+                                   "reference's ggml CPU path (C, -O3 without -march: scalar, no SIMD, like the "
+                                   "reference's own flags), OpenMP over output channels"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+def parity_vs_c_library(kb, W, device, pool):
+    """The device waveform against the oracle in its two modes for the
+    harmonic source's sin / cos / tanh / atan2: correctly rounded (what the
+    kernels compute) and the C library's float functions (what the
+    reference's compiled fill_harmonic_stft calls; the oracle's C-library
+    mode equals it bit for bit). Cases: config 0 (T = 200, F32 weights seed
+    0) and the pool's first utterance with T <= 240 (F16 weights seed 2).
+    The two oracle modes differ from each other by about as much as the
+    device differs from the C-library mode: near-silent STFT bins feed atan2,
+    whose branch flips with the last bit of the source."""
+    from oracle import oracle as O
+    out = {"cases": []}
+    u3 = next(u for u in pool if u.T <= 240)
+    for name, w, u in (("config 0: T=200, F32 weights seed 0", W.config0_weights(), W.config0_inputs(200)),
+                       (f"pool utterance T={u3.T}, F16 weights seed 2", W.config2_weights(), u3)):
+        c = kb.Context(device)
+        c.upload(w)
+        got = c.decoder_forward([u])[0]
+        c.close()
+        m = O.OracleModel(w)
+        cr = m.decoder_forward(u.asr, u.f0, u.noise, u.style)
+        m.set_source_libm(True)
+        lm = m.decoder_forward(u.asr, u.f0, u.noise, u.style)
+        out["cases"].append({
+            "case": name,
+            "max_abs_vs_oracle_correctly_rounded": float(np.abs(got - cr).max()),
+            "max_abs_vs_oracle_c_library": float(np.abs(got - lm).max()),
+            "mean_abs_vs_oracle_c_library": float(np.abs(got - lm).mean()),
+            "oracle_modes_max_abs": float(np.abs(cr - lm).max()),
+        })
+    return out
 
 
 def bench_lstm(kb, W, device, runs):
@@ -357,6 +445,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the device-vs-C-library-mode parity key")
     ap.add_argument("--ttfa-runs", type=int, default=50, help="0 skips the TTFA measurement")
     ap.add_argument("--batch", type=int, default=BATCH, help="utterances per GPU step (profiling cases)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer leg (profiling cases)")
@@ -482,6 +571,7 @@ def main():
         uuid = None
     clk = clocks.stop(uuid) if rank == 0 else None
     ctx.profile_enable(False)
+    records = ctx.profile_records()
     prof = ctx.profile_read(reset=True)
     t_max = max_over_ranks(elapsed)
     secs_all = sum_over_ranks(secs)
@@ -509,6 +599,7 @@ def main():
 
     ttfa = None
     cpu = None
+    parity = None
     if rank == 0 and args.ttfa_runs > 0:
         # p50 time to first audio: one config-0 utterance (T=200, F32 weights
         # seed 0), submitted alone on an idle GPU, until its samples are in
@@ -542,12 +633,19 @@ def main():
             sample = cpu_sample(pool)
             s_audio, s_wall, thr = run_cpu_oracle(weights, sample)
             cpu = {"value": s_audio / s_wall, "unit": UNIT, "cores": thr, "kind": "port",
-                   "sample": f"{len(sample)} pool utterances with T<=240 ({s_audio:.1f} s of audio), oracle port "
-                             f"of the reference's ggml CPU path, OpenMP over output channels"}
+                   "sample": f"the first {len(sample)} pool utterances with T<=240 ({s_audio:.1f} s of audio; not "
+                             f"the pool's U[40,800] length mix); the oracle port of the reference's ggml CPU path "
+                             f"(C, -O3 without -march: scalar, no SIMD, like the reference's own flags), OpenMP "
+                             f"over output channels"}
+        if world == 1 and not args.no_parity:
+            parity = parity_vs_c_library(kb, W, local, pool)
 
     pk, pk_kind = peaks()
-    achieved = prof["conv_flop"] / (prof["conv_ms"] / 1e3) / 1e12 if prof["conv_ms"] > 0 else 0.0
+    achieved_all = prof["conv_flop"] / (prof["conv_ms"] / 1e3) / 1e12 if prof["conv_ms"] > 0 else 0.0
     peak = float(pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")))
+    classes = roofline_classes(records, args.steps, 1e3 * elapsed / args.steps, pk, pk_kind)
+    ct = classes.get("conv_tensor", {})
+    ct_launches = ct.get("launches_per_step") or 0
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * t_max / args.steps, "higher_is_better": True,
@@ -556,13 +654,24 @@ def main():
         "e2e": ({"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                  "step_ms": e2e_steps_ms}
                 if e2e_value is not None else None),
-        "roofline": {"bound": "tensor", "kernel": "dense conv (all conv launches of a step)",
-                     "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": achieved / peak if peak else None,
-                     "traffic": CONV_DRAM_BYTES_PER_AUDIO_S * secs_all / world / args.steps,
-                     "traffic_unit": "DRAM bytes per step, all conv launches (ncu, batch 8, scaled by audio s)",
+        # the dominant kernel class: the tensor-bound convolutions (CUDA
+        # events around each launch in the timed region); per launch
+        "roofline": {"bound": "tensor", "kernel": "k_conv_tct / k_conv_tc launches at or above the ridge point",
+                     "achieved": ct.get("achieved"), "peak": peak, "unit": "TFLOP/s", "frac": ct.get("frac"),
+                     "traffic": (CONV_TENSOR_DRAM_PER_ALGO_BYTE * ct["algorithmic_bytes_per_step"] / ct_launches
+                                 if ct_launches and CONV_TENSOR_DRAM_PER_ALGO_BYTE else None),
+                     "traffic_unit": "DRAM bytes per launch (ncu per-shape captures: measured / algorithmic bytes, "
+                                     "applied to this class's algorithmic bytes)",
+                     "algorithmic_bytes_per_launch": (ct["algorithmic_bytes_per_step"] / ct_launches
+                                                      if ct_launches else None),
+                     "share_of_step": ct.get("share_of_step"),
                      "peak_source": f"{pk_kind} bf16 dense, sustained",
-                     "conv_share_of_step": (prof["conv_ms"] / 1e3) / elapsed if elapsed else None},
+                     "all_conv": {"achieved": achieved_all, "unit": "TFLOP/s",
+                                  "frac": achieved_all / peak if peak else None,
+                                  "share_of_step": (prof["conv_ms"] / 1e3) / elapsed if elapsed else None,
+                                  "dram_bytes_per_step": CONV_DRAM_BYTES_PER_AUDIO_S * secs_all / world / args.steps,
+                                  "dram_source": "ncu, batch-8 step, all conv launches, scaled by audio seconds"}},
+        "roofline_classes": classes,
         "cpu_baseline": cpu,
         "clocks": clk,
         "host_enqueue_ms_per_step": round(host_enqueue_ms, 2),
@@ -572,6 +681,7 @@ def main():
         "prosody": prosody,
         "frontend": frontend,
         "queue": queue,
+        "parity_vs_c_library": parity,
         "pipeline_tflops": value / world * algorithmic_flop_per_asr_frame() * 40.0 / 1e12,
     }
     if rank == 0:

@@ -327,11 +327,38 @@ typedef struct kk_profile {
     double conv_flop;        /* their algorithmic FLOPs: 2*OC*IC*K per valid position */
 } kk_profile;
 
-/* When enabled, every dense-convolution launch is bracketed by CUDA events
- * on its stream. */
+/* When enabled, every launch of the kinds below is bracketed by CUDA events
+ * on its stream and recorded with its algorithmic work. */
 int kk_profile_enable(kk_ctx *ctx, int enable);
-/* Reads (after synchronising the context's work) and optionally resets. */
+/* Reads (after synchronising the context's work) and optionally resets the
+ * counters and the records. */
 int kk_profile_read(kk_ctx *ctx, kk_profile *out, int reset);
+
+/* Kinds of timed launches. */
+enum {
+    KK_PROF_CONV = 0,     /* dense convolution (tensor or CUDA cores), its statistics epilogue included */
+    KK_PROF_OPERAND = 1,  /* AdaIN / activation operand pass (instance norm applied, Snake or LeakyReLU) */
+    KK_PROF_STATS = 2,    /* instance-norm statistics pass over an activation */
+    KK_PROF_ISTFT = 3,    /* conv_post magnitude / phase -> inverse DFT -> overlap-add */
+    KK_PROF_SOURCE = 4,   /* harmonic source and its STFT (side stream) */
+    KK_PROF_LSTM = 5,     /* LSTM recurrence */
+    KK_PROF_OTHER = 6     /* packing, upsampling, the ConvTranspose edge row */
+};
+
+/* One timed launch: its kind, the convolution's taps (0 for other kinds),
+ * its device time and its algorithmic work: FLOPs (2 per multiply-add) and
+ * DRAM bytes (every input element read once, every output written once). */
+typedef struct kk_profile_record {
+    int32_t kind;
+    int32_t taps;
+    double ms;
+    double flop;
+    double bytes;
+} kk_profile_record;
+
+/* The records since the last reset, in launch order per stream (after
+ * synchronising): copies min(cap, *n) of them to out; *n = how many exist. */
+int kk_profile_records(kk_ctx *ctx, kk_profile_record *out, size_t cap, size_t *n);
 
 /* How many device or pinned-host allocations the library has made in this
  * process, over all contexts and queues (no counterpart in the reference).

@@ -47,6 +47,20 @@ class Profile(ctypes.Structure):
     ]
 
 
+class ProfileRecord(ctypes.Structure):
+    _fields_ = [
+        ("kind", ctypes.c_int32),
+        ("taps", ctypes.c_int32),
+        ("ms", ctypes.c_double),
+        ("flop", ctypes.c_double),
+        ("bytes", ctypes.c_double),
+    ]
+
+
+# kinds of timed launches (KK_PROF_*)
+PROF_KINDS = ["conv", "operand", "stats", "istft", "source", "lstm", "other"]
+
+
 class KKError(RuntimeError):
     def __init__(self, code: int, msg: str):
         super().__init__(f"[{code}] {msg}")
@@ -106,6 +120,8 @@ def load_library():
     L.kk_profile_enable.argtypes = [vp, ctypes.c_int]
     L.kk_profile_read.argtypes = [vp, ctypes.POINTER(Profile), ctypes.c_int]
     L.kk_allocation_count.argtypes = [ctypes.POINTER(ctypes.c_uint64)]
+    L.kk_profile_records.argtypes = [vp, ctypes.POINTER(ProfileRecord), ctypes.c_size_t,
+                                     ctypes.POINTER(ctypes.c_size_t)]
     _lib = L
     return L
 
@@ -224,6 +240,16 @@ class Context:
         self._check(self.L.kk_profile_read(self.h, ctypes.byref(p), 1 if reset else 0))
         return {"launches": int(p.launches), "conv_launches": int(p.conv_launches),
                 "conv_ms": float(p.conv_ms), "conv_flop": float(p.conv_flop)}
+
+    def profile_records(self) -> List[Dict[str, float]]:
+        """The timed launches since the last reset: kind (PROF_KINDS), taps,
+        device ms, algorithmic FLOPs and DRAM bytes."""
+        n = ctypes.c_size_t(0)
+        self._check(self.L.kk_profile_records(self.h, None, 0, ctypes.byref(n)))
+        arr = (ProfileRecord * max(1, n.value))()
+        self._check(self.L.kk_profile_records(self.h, arr, n.value, ctypes.byref(n)))
+        return [{"kind": PROF_KINDS[r.kind], "taps": int(r.taps), "ms": float(r.ms), "flop": float(r.flop),
+                 "bytes": float(r.bytes)} for r in arr[: n.value]]
 
     def istft(self, post: np.ndarray) -> np.ndarray:
         post = np.ascontiguousarray(post, np.float32)

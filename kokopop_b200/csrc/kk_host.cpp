@@ -167,6 +167,25 @@ float *kk_ctx::buf(const char *name, size_t floats) {
     return (float *)b.p;
 }
 
+// Waits for the timed launches' end events and turns them into records (and
+// the convolution counters of kk_profile).
+void kk_ctx::resolve_timed() {
+    for (auto &t : timed) {
+        check_cuda(cudaEventSynchronize(t.b), "profile sync");
+        float ms = 0.f;
+        check_cuda(cudaEventElapsedTime(&ms, t.a, t.b), "profile elapsed");
+        if (t.kind == KK_PROF_CONV) {
+            conv_ms += ms;
+            conv_flop += t.flop;
+            conv_launches += 1;
+        }
+        records.push_back(kk_profile_record{t.kind, t.taps, (double)ms, t.flop, t.bytes});
+        event_pool.push_back(t.a);
+        event_pool.push_back(t.b);
+    }
+    timed.clear();
+}
+
 void kk_ctx::stage_begin() {
     stage_k ^= 1;
     StageSlot &s = stage[stage_k];
@@ -197,10 +216,9 @@ void kk_ctx::upload(void *dst, const void *src, size_t bytes, cudaStream_t st, c
     std::memcpy(s.p + at, src, bytes);
     s.used = at + bytes;
     check_cuda(cudaMemcpyAsync(dst, s.p + at, bytes, cudaMemcpyHostToDevice, st), what);
-}
-
-void kk_ctx::stage_end(cudaStream_t st) {
-    StageSlot &s = stage[stage_k];
+    // the slot is free again once its last copy has run (early in the call's
+    // work on the device), not when the whole call has finished
+    s.pending = false;
     if (cudaEventRecord(s.ev, st) == cudaSuccess)
         s.pending = true;
     else
@@ -982,18 +1000,36 @@ struct Runner {
         int sm = 1, sextra = 0;
     };
 
-    void timed_begin(cudaEvent_t &e0, cudaEvent_t &e1) {
+    void timed_begin(cudaEvent_t &e0, cudaEvent_t &e1, cudaStream_t s = nullptr) {
         if (!c.profiling) return;
         e0 = c.take_event();
         e1 = c.take_event();
-        check_cuda(cudaEventRecord(e0, st), "event");
+        check_cuda(cudaEventRecord(e0, s ? s : st), "event");
     }
 
-    void timed_end(cudaEvent_t e0, cudaEvent_t e1, double flop) {
+    void timed_end(cudaEvent_t e0, cudaEvent_t e1, int kind, int taps, double flop, double bytes,
+                   cudaStream_t s = nullptr) {
         ++c.n_launches;
         if (!c.profiling) return;
-        check_cuda(cudaEventRecord(e1, st), "event");
-        c.timed.push_back({e0, e1, flop});
+        check_cuda(cudaEventRecord(e1, s ? s : st), "event");
+        c.timed.push_back({e0, e1, kind, taps, flop, bytes});
+    }
+
+    // One launch of `kind` (f enqueues it on s, default the runner's
+    // stream), timed when profiling, with its algorithmic work.
+    template <class F>
+    void launch(int kind, double flop, double bytes, F &&f, cudaStream_t s = nullptr) {
+        cudaEvent_t e0 = nullptr, e1 = nullptr;
+        timed_begin(e0, e1, s);
+        f();
+        timed_end(e0, e1, kind, 0, flop, bytes, s);
+    }
+
+    // algorithmic DRAM bytes of a convolution over `valid` output rows:
+    // the operand read once (ebytes per input element), the output written
+    // once, the residual and an accumulated output read once
+    static double conv_bytes(int IC, int OC, double ebytes, int64_t valid, const Epi &e) {
+        return (double)valid * ((double)IC * ebytes + 4.0 * OC * (1 + (e.resid ? 1 : 0) + (e.accum ? 1 : 0)));
     }
 
     // CUDA-core convolution on an F32 operand.
@@ -1025,7 +1061,8 @@ struct Runner {
         cudaEvent_t e0 = nullptr, e1 = nullptr;
         timed_begin(e0, e1);
         conv_simt(a, st);
-        timed_end(e0, e1, 2.0 * OC * (double)IC * K * (double)e.valid);
+        timed_end(e0, e1, KK_PROF_CONV, K, 2.0 * OC * (double)IC * K * (double)e.valid,
+                  conv_bytes(IC, OC, 4.0, e.valid, e));
     }
 
     // Tensor-core convolution on a half chunk-major operand.
@@ -1070,7 +1107,9 @@ struct Runner {
         cudaEvent_t e0 = nullptr, e1 = nullptr;
         timed_begin(e0, e1);
         check_cuda(conv_tc(a, st), "tensor-core conv launch");
-        timed_end(e0, e1, 2.0 * pw.OC * (double)pw.IC * K * (double)e.valid);
+        // split F32 operands carry hi and lo halves: 4 bytes per input element
+        timed_end(e0, e1, KK_PROF_CONV, K, 2.0 * pw.OC * (double)pw.IC * K * (double)e.valid,
+                  conv_bytes(pw.IC, pw.OC, in.split ? 4.0 : 2.0, e.valid, e));
         if (e.stats) ++c.n_launches;  // the statistics pass
     }
 
@@ -1088,10 +1127,7 @@ struct Runner {
             conv_h(it->second, in, K, p, d, out, R_out, n_pos, e);
         } else {
             conv_f32(w.d, w.f16, OC, in.f, in.R, IC, K, 1, p, d, out, R_out, n_pos, e);
-            if (e.stats) {
-                stats(out, R_out, OC, e.sm, e.sextra, B, e.stats, st);
-                ++c.n_launches;
-            }
+            if (e.stats) stats_pass(out, R_out, OC, e.sm, e.sextra, e.stats);
         }
     }
 
@@ -1108,10 +1144,7 @@ struct Runner {
                    int act, float slope, const std::string &alpha, const float2 *pre = nullptr) {
         const AdainSite &s = site(prefix);
         if (s.C != C) throw KKError(KK_ERROR_MODEL, "AdaIN channel mismatch: " + prefix);
-        if (!pre) {
-            stats(x, Rm, C, m, extra, B, ms, st);
-            ++c.n_launches;
-        }
+        if (!pre) stats_pass(x, Rm, C, m, extra, ms);
         PrologueArgs a{};
         a.norm = 1;
         a.ms = pre ? pre : ms;
@@ -1124,11 +1157,7 @@ struct Runner {
         a.alpha = alpha.empty() ? nullptr : c.W(alpha).d;
         a.round16 = 0;
         a.lo_off = y.lo(C);
-        if (y.h)
-            prologue_h(x, y.h, Rm, y.Ry, C, m, extra, B, (int)(sum_len(m, extra) / P.n), a, st);
-        else
-            prologue(x, y.f, Rm, C, m, extra, B, m * P.maxT + extra, a, st);
-        ++c.n_launches;
+        operand_pass(x, y, Rm, C, m, extra, a);
     }
 
     // x2 / x3: two more branches averaged in first, ((x + x2) + x3) * sum_scale
@@ -1142,11 +1171,28 @@ struct Runner {
         a.x3 = x3;
         a.sum_scale = sum_scale;
         a.lo_off = y.lo(C);
-        if (y.h)
-            prologue_h(x, y.h, Rm, y.Ry, C, m, extra, B, (int)(sum_len(m, extra) / P.n), a, st);
-        else
-            prologue(x, y.f, Rm, C, m, extra, B, m * P.maxT + extra, a, st);
-        ++c.n_launches;
+        operand_pass(x, y, Rm, C, m, extra, a);
+    }
+
+    // The operand pass of one activation: F32 reads of x (and of the other
+    // branches averaged in), the operand written once (half, hi + lo halves
+    // for split F32, or F32 on the CUDA-core path).
+    void operand_pass(const float *x, const Op &y, int64_t Rm, int C, int m, int extra, const PrologueArgs &a) {
+        const double elems = (double)C * (double)sum_len(m, extra);
+        const double in_b = 4.0 * (1 + (a.x2 ? 1 : 0) + (a.x3 ? 1 : 0));
+        const double out_b = y.h ? (y.split ? 4.0 : 2.0) : 4.0;
+        launch(KK_PROF_OPERAND, 0.0, elems * (in_b + out_b), [&] {
+            if (y.h)
+                prologue_h(x, y.h, Rm, y.Ry, C, m, extra, B, (int)(sum_len(m, extra) / P.n), a, st);
+            else
+                prologue(x, y.f, Rm, C, m, extra, B, m * P.maxT + extra, a, st);
+        });
+    }
+
+    // Instance-norm statistics of x over the utterances of level (m, extra).
+    void stats_pass(const float *x, int64_t Rm, int C, int m, int extra, float2 *out) {
+        launch(KK_PROF_STATS, 0.0, 4.0 * C * (double)sum_len(m, extra),
+               [&] { stats(x, Rm, C, m, extra, B, out, st); });
     }
 
     // adain_resblk1d (graph_ops.cpp:996-1065) with its input on level mi (1 or
@@ -1195,11 +1241,14 @@ struct Runner {
             pf32.f = c.buf("pfT", 1090 * (size_t)R1);
             pf32.R = R1;
             adain_act(pf + ".norm1", x, pf32, R1, Cin, 1, 0, ACT_LEAKY, 0.2f, "");
-            if (tc)
-                pool_up_h(pf32.f, opL.h, R1, opL.Ry, Cin, pw.d, pb.d, B, P.maxT, opL.lo(Cin), st);
-            else
-                pool_up(pf32.f, opL.f, R1, R2, Cin, pw.d, pb.d, B, P.maxT, 0, st);
-            ++c.n_launches;
+            // reads the frame level once, writes the doubled level
+            const double el = (double)Cin * (double)sum_len(1, 0);
+            launch(KK_PROF_OTHER, 0.0, el * (4.0 + 2.0 * (tc ? (opL.split ? 4.0 : 2.0) : 4.0)), [&] {
+                if (tc)
+                    pool_up_h(pf32.f, opL.h, R1, opL.Ry, Cin, pw.d, pb.d, B, P.maxT, opL.lo(Cin), st);
+                else
+                    pool_up(pf32.f, opL.f, R1, R2, Cin, pw.d, pb.d, B, P.maxT, 0, st);
+            });
         } else {
             adain_act(pf + ".norm1", x, opI, Ri, Cin, mi, 0, ACT_LEAKY, 0.2f, "");
         }
@@ -1296,14 +1345,13 @@ struct Runner {
             a.x_beta = s.beta;
             a.x_alpha = c.W(alpha).d;
             if (pw.IC_pad == C && conv_tc_fusable(a)) {
-                if (!x_stats) {
-                    stats(x, Rm, C, m, extra, B, ms3, st);
-                    ++c.n_launches;
-                }
+                if (!x_stats) stats_pass(x, Rm, C, m, extra, ms3);
                 cudaEvent_t e0 = nullptr, e1 = nullptr;
                 timed_begin(e0, e1);
                 check_cuda(conv_tc(a, st), "tensor-core conv launch (fused operand)");
-                timed_end(e0, e1, 2.0 * pw.OC * (double)pw.IC * K * (double)sum_len(m, extra));
+                // the operand is read as F32 activations
+                timed_end(e0, e1, KK_PROF_CONV, K, 2.0 * pw.OC * (double)pw.IC * K * (double)sum_len(m, extra),
+                          conv_bytes(pw.IC, pw.OC, 4.0, sum_len(m, extra), e));
                 if (e.stats) ++c.n_launches;
                 return;
             }
@@ -1389,8 +1437,8 @@ struct Runner {
                 if (tc && s == 0) {
                     // stride 6 as 2 taps over the space-to-depth operand
                     Op sd = op("s2d", m, 192);
-                    har_s2d(har, R_har, sd.h, Rm, sd.Ry, sd.lo(192), st);
-                    ++c.n_launches;
+                    launch(KK_PROF_OTHER, 0.0, (double)sum_len(60 * gm, 1) * 22 * (4.0 + (sd.split ? 4.0 : 2.0)),
+                           [&] { har_s2d(har, R_har, sd.h, Rm, sd.Ry, sd.lo(192), st); });
                     e.valid = sum_len(m, extra[s]);
                     conv_h(c.packed.at("noise_convs.0.s2d"), sd, 2, 0, 1, xs, Rm, Rm, e);
                 } else if (tc) {
@@ -1400,8 +1448,7 @@ struct Runner {
                 } else {
                     conv_f32(ncw.d, ncw.f16, Cs, har, R_har, 22, K, sp[s].noise_stride, sp[s].noise_padding, 1, xs,
                              Rm, Rm, e);
-                    stats(xs, Rm, Cs, m, extra[s], B, ms2, st);
-                    ++c.n_launches;
+                    stats_pass(xs, Rm, Cs, m, extra[s], ms2);
                 }
             }
             gen_resblock(g + "noise_res." + ss, sp[s].kernel, xs, xs, nullptr, 0, 1.f, Cs, m, extra[s], o, tmp,
@@ -1459,14 +1506,12 @@ struct Runner {
                 a.out = xst;
                 a.R_out = Rm;
                 a.round16 = uw.f16 ? 1 : 0;
-                convt_row0(a, B, st);
-                ++c.n_launches;
+                launch(KK_PROF_OTHER, 0.0, 8.0 * Cs * P.n, [&] { convt_row0(a, B, st); });
             }
             // three main resblocks, averaged (graph_ops.cpp:1300-1320); they
             // share the input, so its statistics are computed once
             float2 *ms_stage = (float2 *)c.buf("stats_stage", (size_t)P.n * 1090 * 2);
-            stats(xst, Rm, Cs, m, extra[s], B, ms_stage, st);
-            ++c.n_launches;
+            stats_pass(xst, Rm, Cs, m, extra[s], ms_stage);
             for (int k = 0; k < 3; ++k) {
                 const std::string pf = g + "resblocks." + std::to_string(s * 3 + k);
                 gen_resblock(pf, kKs[k], xst, br[k], nullptr, 0, 1.f, Cs, m, extra[s], o, tmp, ms_stage);
@@ -1488,8 +1533,10 @@ struct Runner {
         conv_w(g + "conv_post.weight", g + "conv_post.bias", op_prev, C, 7, 3, 1, post, Rm, Rm, Epi{},
                sum_len(m, 1));
         const IstftTables *it = (const IstftTables *)((char *)c.d_tables.p + sizeof(StftTables));
-        istft(post, Rm, 60 * gm, audio, B, d_cum, it, P.maxT, st);
-        ++c.n_launches;
+        // 22 post values read per frame, 5 samples written per frame
+        const double frames = (double)sum_len(m, 1);
+        launch(KK_PROF_ISTFT, 0.0, 88.0 * frames + 20.0 * (frames - P.n),
+               [&] { istft(post, Rm, 60 * gm, audio, B, d_cum, it, P.maxT, st); });
     }
 
     // ---- LSTM stack: the plan is one "utterance" of R rows (rows t * B + b) ----
@@ -1537,8 +1584,11 @@ struct Runner {
                 a.Bc = bc;
                 break;
             }
-        check_cuda(lstm_recurrence(a, st), "LSTM recurrence launch");
-        ++c.n_launches;
+        // per row and direction: the 4H pre-gates read, H outputs written,
+        // 4H x H multiply-adds with W_hh (read from shared memory)
+        const double rows = (double)q.rows, H = L.H;
+        launch(KK_PROF_LSTM, 2.0 * 2.0 * 4.0 * H * H * rows, 2.0 * rows * (16.0 * H + 4.0 * H),
+               [&] { check_cuda(lstm_recurrence(a, st), "LSTM recurrence launch"); });
     }
 
     // zero every operand buffer whose gaps must read as zero
@@ -1558,11 +1608,13 @@ struct Runner {
         check_cuda(cudaEventRecord(c.ev_inputs, st), "event");
         check_cuda(cudaStreamWaitEvent(c.st2, c.ev_inputs, 0), "wait");
         check_cuda(cudaMemsetAsync(har, 0, (size_t)22 * Rh * sizeof(float), c.st2), "memset har");
-        sinegen(f0p, mf, src, B, d_cum, c.sine, c.st2);
-        ++c.n_launches;
+        // the source writes 300 mf samples per base frame; the STFT reads
+        // them and writes 22 values per frame of 5 samples (+1 per utterance)
+        const double samples = (double)kUpsample * mf * (double)P.total;
+        launch(KK_PROF_SOURCE, 0.0, 4.0 * samples, [&] { sinegen(f0p, mf, src, B, d_cum, c.sine, c.st2); }, c.st2);
         const StftTables *tab = (const StftTables *)c.d_tables.p;
-        stft(src, har, Rh, mf, B, d_cum, tab, P.maxT, c.st2);
-        ++c.n_launches;
+        launch(KK_PROF_SOURCE, 0.0, 4.0 * samples + 88.0 * (samples / 5.0 + P.n),
+               [&] { stft(src, har, Rh, mf, B, d_cum, tab, P.maxT, c.st2); }, c.st2);
         check_cuda(cudaEventRecord(c.ev_src, c.st2), "event");
         return har;
     }
@@ -1656,7 +1708,6 @@ struct CallScope {
         c.stage_begin();
     }
     ~CallScope() {
-        c.stage_end(st);
         c.done_recorded = cudaEventRecord(c.ev_done, st) == cudaSuccess;
         if (!c.done_recorded) cudaStreamSynchronize(st);  // nothing to wait for next time
     }
@@ -2536,17 +2587,7 @@ int kk_profile_read(kk_ctx *ctx, kk_profile *out, int reset) {
     return guarded([&] {
         if (!ctx || !out) throw KKError(KK_ERROR_INVALID_ARGUMENT, "null argument");
         use_device(ctx);
-        for (auto &t : ctx->timed) {
-            check_cuda(cudaEventSynchronize(t.b), "profile sync");
-            float ms = 0.f;
-            check_cuda(cudaEventElapsedTime(&ms, t.a, t.b), "profile elapsed");
-            ctx->conv_ms += ms;
-            ctx->conv_flop += t.flop;
-            ctx->conv_launches += 1;
-            ctx->event_pool.push_back(t.a);
-            ctx->event_pool.push_back(t.b);
-        }
-        ctx->timed.clear();
+        ctx->resolve_timed();
         out->launches = ctx->n_launches;
         out->conv_launches = ctx->conv_launches;
         out->conv_ms = ctx->conv_ms;
@@ -2556,7 +2597,19 @@ int kk_profile_read(kk_ctx *ctx, kk_profile *out, int reset) {
             ctx->conv_launches = 0;
             ctx->conv_ms = 0.0;
             ctx->conv_flop = 0.0;
+            ctx->records.clear();
         }
+        return KK_OK;
+    });
+}
+
+int kk_profile_records(kk_ctx *ctx, kk_profile_record *out, size_t cap, size_t *n) {
+    return guarded([&] {
+        if (!ctx || !n || (cap && !out)) throw KKError(KK_ERROR_INVALID_ARGUMENT, "null argument");
+        use_device(ctx);
+        ctx->resolve_timed();
+        *n = ctx->records.size();
+        std::copy(ctx->records.begin(), ctx->records.begin() + std::min(cap, ctx->records.size()), out);
         return KK_OK;
     });
 }

@@ -159,8 +159,8 @@ struct kk_ctx {
     // descriptors, AdaIN site tables, sequence lengths), so that their
     // uploads are asynchronous: a copy from pageable memory would first wait
     // for the stream. Two slots serve alternate calls; a slot is written
-    // again only after the copies of the call that last used it have
-    // finished (its event).
+    // again only after the copies of the call that last used it have run
+    // (its event, recorded after each upload).
     struct StageSlot {
         char *p = nullptr;
         size_t cap = 0, used = 0;
@@ -172,9 +172,8 @@ struct kk_ctx {
     int stage_k = 0;
     void stage_begin();
     // copies `bytes` of host data into the current slot and queues their
-    // upload to `dst` on `st`
+    // upload to `dst` on `st` (the slot's event follows the last upload)
     void upload(void *dst, const void *src, size_t bytes, cudaStream_t st, const char *what);
-    void stage_end(cudaStream_t st);
     // Calls on one context share its workspaces, so each call is ordered
     // after the previous one even when they run on different streams: a call
     // waits (on the device) for the event the previous call recorded.
@@ -190,11 +189,14 @@ struct kk_ctx {
     // measurement
     uint64_t n_launches = 0;
     bool profiling = false;
-    struct TimedConv {
+    struct TimedLaunch {
         cudaEvent_t a, b;
-        double flop;
+        int kind, taps;
+        double flop, bytes;
     };
-    std::vector<TimedConv> timed;
+    std::vector<TimedLaunch> timed;         // events not read yet
+    std::vector<kk_profile_record> records;  // read, since the last reset
+    void resolve_timed();
     std::vector<cudaEvent_t> event_pool;
     uint64_t conv_launches = 0;
     double conv_ms = 0.0, conv_flop = 0.0;

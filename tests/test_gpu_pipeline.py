@@ -67,9 +67,9 @@ def test_ids_to_audio_against_oracle_composition():
     head 1e-4, text encoder 1e-4, prosody 1e-4, waveform 1e-3), so every
     hand-over between stages is checked at the configuration's sizes; frames
     and the alignment are bit-exact. Free-running: the oracle's own chain
-    from the ids gives F0 / N curves and audio that are printed beside the
-    device's (the differences of the half-rounded stages compound through
-    the F0 curve into the harmonic source's phase)."""
+    from the ids gives F0 / N curves and audio that the device's must match
+    at 1e-3 max-abs, the waveform bar (measured on B200: audio 9.2e-5, F0
+    3.8e-5; the half-rounded stages' differences shrink through the chain)."""
     weights = {}
     weights.update(W.config2_frontend_weights())
     weights.update(W.prosody_weights(f16=True))
@@ -124,9 +124,11 @@ def test_ids_to_audio_against_oracle_composition():
         f0_o, n_o = m.prosody_f0n(en_o, style_p)
         _, _, asr_o = O.align_durations(override, 1.0, m.text_encoder(ids))
         audio_o = m.decoder_forward(np.ascontiguousarray(asr_o.T), f0_o, n_o, style_d)
-        ef, ea = _err(f0, f0_o), _err(audio, audio_o)
-        print(f"free-running: F0 {ef[0]:.3g} max (|F0| up to {float(np.abs(f0_o).max()):.3g}), "
+        ef, en_f, ea = _err(f0, f0_o), _err(nn, n_o), _err(audio, audio_o)
+        print(f"free-running: F0 {ef[0]:.3g} max (|F0| up to {float(np.abs(f0_o).max()):.3g}), N {en_f[0]:.3g}, "
               f"audio {ea[0]:.3g} max, {ea[1]:.3g} mean")
         assert np.all(np.isfinite(audio_o)) and audio_o.shape == audio.shape
+        # ids -> audio, each side on its own chain: the waveform bar holds
+        assert ef[0] < 1e-3 and en_f[0] < 1e-3 and ea[0] < 1e-3
     finally:
         c.close()
