@@ -289,6 +289,39 @@ void kk_queue_destroy(kk_queue *q);
 int kk_align_durations(kk_ctx *ctx, int64_t n_tokens, const float *durations, float speed, int32_t *frames,
                        int64_t *total, const float *hidden, int64_t hidden_dim, float *en, int64_t en_capacity);
 
+/* ---- sanoTTS Vocos decoder ----
+ * The hyper-parameters of one voice's decoder: its GGUF keys dec.dim,
+ * dec.blocks, dec.pw_hidden, dec.dw_kernel, dec.embed_kernel, dec.noise_ch,
+ * dec.mels, dec.n_fft, dec.hop, dec.dc_pole, dec.mag_clip
+ * (src/arch/sanotts/sano_arch.cpp:1081-1096; dec.bins = n_fft / 2 + 1). */
+typedef struct kk_vocos_params {
+    int32_t dim, blocks, pw_hidden, dw_kernel, embed_kernel, noise_ch, mels, n_fft, hop;
+    float dc_pole, mag_clip;
+} kk_vocos_params;
+
+/* sano_run_vocos (src/arch/sanotts/sano_vocos.cpp:94-230) for a ragged batch
+ * of chunks of one voice: the two 7-tap stem convs (mel, noise), LayerNorm,
+ * `blocks` ConvNeXt1D blocks (depthwise conv, LayerNorm, pw0, exact GELU,
+ * pw1, layer scale, residual), LayerNorm, the magnitude / phase head, the
+ * iSTFT (n_fft, hop, centred) and the DC blocker. Weights are read under
+ * `prefix` (e.g. "kokopop.sanotts.voice.0." + "dec.embed.weight"); the
+ * pointwise / stem / head weights all F16 or all F32. The noise input is the
+ * caller's (sano::seeded_noise in the reference). Per chunk u:
+ *   n_frames[u] = F_u frames, 2 <= F_u <= 8192
+ *   mel   : [F_u, mels]      (time-fastest: mel[c * F_u + t])
+ *   noise : [F_u, noise_ch]  (time-fastest)
+ *   audio : [hop (F_u - 1)] samples
+ * n_fft must be a power of two in [64, 4096], dim and pw_hidden at most
+ * 1024, the kernels odd. Host buffers. */
+int kk_vocos_forward(kk_ctx *ctx, const char *prefix, const kk_vocos_params *params, int32_t n_chunks,
+                     const int32_t *n_frames, const float *mel, const float *noise, float *audio);
+
+/* Same with device-resident mel, noise and audio (lengths on the host).
+ * Asynchronous on `stream` (NULL = the context's stream). */
+int kk_vocos_forward_device(kk_ctx *ctx, const char *prefix, const kk_vocos_params *params, int32_t n_chunks,
+                            const int32_t *n_frames, const float *mel, const float *noise, float *audio,
+                            void *stream);
+
 /* kk_istft without any device allocation (no counterpart in the reference,
  * whose iSTFT runs on the host). Same arguments and results as kk_istft, but
  * no kk_ctx: input, output, tables and descriptor are staged in one static

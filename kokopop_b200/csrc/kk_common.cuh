@@ -39,6 +39,15 @@ __device__ __forceinline__ float leaky(float x, float slope) {
     return __fadd_rn(x > 0.f ? x : 0.f, __fmul_rn(slope, x < 0.f ? x : 0.f));
 }
 
+// Exact GELU as ggml_vec_gelu_erf_f32 evaluates it, left to right:
+// (0.5f * x) * (1.0f + erff(x * SQRT_2_INV)), each operation rounded once,
+// with erf correctly rounded (from the double-precision erf).
+__device__ __forceinline__ float gelu_erf(float x) {
+    const float t = __fmul_rn(x, 0.70710678118654752440f);
+    const float e = __double2float_rn(erf((double)t));
+    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, e));
+}
+
 // sin for the Snake activation. Its arguments v * alpha are small in
 // practice, where the odd Taylor polynomial of sin to x^9 (Horner in x^2)
 // is accurate to float rounding: the first omitted term x^11/11! is below

@@ -237,6 +237,7 @@ struct TcParams {
     const float *resid;
     int64_t R_resid;
     int resid_half;
+    const float *chscale;  // non-null: per output channel, after bias and residual
     float scale1;
     int accum;
     float scale2;
@@ -430,6 +431,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_conv_tc(const __grid_constant
                 const int nj = P.OC - (n0 + c0) < 32 ? P.OC - (n0 + c0) : 32;
                 const int64_t rrow = P.resid_half ? (orow >> 1) : orow;
                 const float b_lane = (P.bias && lane < nj) ? __ldg(P.bias + oc0 + c0 + lane) : 0.f;
+                const float s_lane = (P.chscale && lane < nj) ? __ldg(P.chscale + oc0 + c0 + lane) : 1.f;
                 // The residual and the accumulated output may alias the
                 // output (in-place updates): read all of this row's values
                 // first so the loads overlap, then compute and store.
@@ -451,10 +453,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_conv_tc(const __grid_constant
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     const float bj = __shfl_sync(0xffffffffu, b_lane, j);
+                    const float sj = __shfl_sync(0xffffffffu, s_lane, j);
                     float v = __uint_as_float(r[j]);
                     if (P.acc_scale != 1.0f) v = __fmul_rn(v, P.acc_scale);
                     if (P.bias) v = __fadd_rn(v, bj);
                     if (has_res) v = __fadd_rn(res[j], v);
+                    if (P.chscale) v = __fmul_rn(v, sj);
                     if (P.scale1 != 1.0f) v = __fmul_rn(v, P.scale1);
                     if (P.accum) v = __fadd_rn(old[j], v);
                     if (P.scale2 != 1.0f) v = __fmul_rn(v, P.scale2);
@@ -752,6 +756,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const int c = c_lo + lane;  // this thread's output channel
             const bool chan_ok = c < P.OC;
             const float bias = (P.bias && chan_ok) ? P.bias[c] : 0.f;
+            const float chs = (P.chscale && chan_ok) ? P.chscale[c] : 1.f;
             const uint32_t t_base = tmem + ((uint32_t)(32 * lq) << 16) + (uint32_t)(ab * TC_BM + hsel * 128);
             for (int cc = 0; cc < 4; ++cc) {
                 uint32_t r[32];  // r[j] = D[c][p0 + j]
@@ -811,6 +816,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         if (P.bias) x = f2add(x, make_float2(bias, bias));
                         if (has_res) x = f2add(make_float2(res[j], res[j + 1]), x);
                         // scalar products: a packed product feeding a packed add may be contracted
+                        if (P.chscale) x = make_float2(__fmul_rn(x.x, chs), __fmul_rn(x.y, chs));
                         if (P.scale1 != 1.0f) x = make_float2(__fmul_rn(x.x, P.scale1), __fmul_rn(x.y, P.scale1));
                         if (P.accum) x = f2add(make_float2(old[j], old[j + 1]), x);
                         if (P.scale2 != 1.0f) x = make_float2(__fmul_rn(x.x, P.scale2), __fmul_rn(x.y, P.scale2));
@@ -845,6 +851,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                                 if (P.acc_scale != 1.0f) x = __fmul_rn(x, P.acc_scale);
                                 if (P.bias) x = __fadd_rn(x, bias);
                                 if (has_res) x = __fadd_rn(rp[j], x);
+                                if (P.chscale) x = __fmul_rn(x, chs);
                                 if (P.scale1 != 1.0f) x = __fmul_rn(x, P.scale1);
                                 if (P.accum) x = __fadd_rn(op[j], x);
                                 if (P.scale2 != 1.0f) x = __fmul_rn(x, P.scale2);
@@ -1511,7 +1518,7 @@ bool conv_tc_fusable(const ConvTcArgs &a) {
            a.scale2 == 1.0f && a.OC >= 64 && a.OC <= a.n_tiles * TC_BN && a.n_pos == a.R_out &&
            a.R_out % 128 == 0 && (!a.resid || a.R_resid == a.R_out) && a.IC_pad >= 64 && a.IC_pad % 64 == 0 &&
            a.K >= 1 && a.d >= 1 && a.p >= 0 && (a.K - 1) * a.d + 3 <= TC_SLAB - TC_BM && a.sb.n >= 1 && a.sm >= 4 &&
-           a.sextra >= 0 && a.a_wrap == 0 && (a.acc_scale == 0.0f || a.acc_scale == 1.0f);
+           a.sextra >= 0 && a.a_wrap == 0 && (a.acc_scale == 0.0f || a.acc_scale == 1.0f) && !a.chscale;
 }
 
 // k_conv_tcf launch: the operand formed from x inside the conv.
@@ -1611,6 +1618,7 @@ cudaError_t conv_tc(const ConvTcArgs &a, cudaStream_t st) {
     P.resid = a.resid;
     P.R_resid = a.R_resid;
     P.resid_half = a.resid_half;
+    P.chscale = a.chscale;
     P.scale1 = a.scale1;
     P.accum = a.accum;
     P.scale2 = a.scale2;

@@ -451,6 +451,16 @@ void kk_ctx::derive() {
         kv.second.bih_buf.release();
     }
     lstm.clear();
+    for (auto &kv : vocos) {
+        VocosNet &v = kv.second;
+        v.embed.buf.release();
+        v.noise.buf.release();
+        v.head.buf.release();
+        for (auto &p : v.pw0) p.buf.release();
+        for (auto &p : v.pw1) p.buf.release();
+        v.tables.release();
+    }
+    vocos.clear();
     bool all16 = ok && convt_f16[0] && convt_f16[1], all32 = ok && !convt_f16[0] && !convt_f16[1];
     {
         std::vector<std::pair<std::string, int>> convs = tc_convs();
@@ -858,6 +868,140 @@ const LstmLayer &kk_ctx::lstm_layer(const std::string &prefix) {
     return lstm.emplace(prefix, std::move(L)).first->second;
 }
 
+// load_vocos (src/arch/sanotts/sano_arch.cpp:1081-1180): the range checks of
+// the voice's decoder hyper-parameters, the tensor shapes, then the
+// packings and the inverse-FFT tables.
+const VocosNet &kk_ctx::vocos_net(const std::string &prefix, const kk_vocos_params &p) {
+    auto it = vocos.find(prefix);
+    if (it != vocos.end() && std::memcmp(&it->second.p, &p, sizeof p) == 0) return it->second;
+    const auto bad = [&](const char *what) { throw KKError(KK_ERROR_INVALID_ARGUMENT, std::string("vocos: ") + what); };
+    if (p.dim < 1 || p.dim > 1024 || p.pw_hidden < 1 || p.pw_hidden > 1024) bad("dim and pw_hidden must be in [1, 1024]");
+    if (p.blocks < 0 || p.blocks > 64) bad("blocks out of range");
+    if (p.dw_kernel < 1 || p.dw_kernel % 2 == 0 || p.embed_kernel < 1 || p.embed_kernel % 2 == 0 || p.dw_kernel > 63 ||
+        p.embed_kernel > 63)
+        bad("kernels must be odd (at most 63)");
+    if (p.mels < 1 || p.mels > 1024 || p.noise_ch < 1 || p.noise_ch > 1024) bad("mels / noise_ch out of range");
+    if (p.n_fft < 64 || p.n_fft > 4096 || (p.n_fft & (p.n_fft - 1))) bad("n_fft must be a power of two in [64, 4096]");
+    if (p.hop < 1 || p.hop > p.n_fft) bad("hop must lie in (0, n_fft]");
+    if (!std::isfinite(p.dc_pole) || std::fabs(p.dc_pole) >= 1.0f) bad("dc_pole must be a stable pole in (-1, 1)");
+    if (!std::isfinite(p.mag_clip) || p.mag_clip <= 0.0f) bad("mag_clip must be finite and positive");
+    if (it != vocos.end()) {
+        VocosNet &v = it->second;
+        v.embed.buf.release();
+        v.noise.buf.release();
+        v.head.buf.release();
+        for (auto &q : v.pw0) q.buf.release();
+        for (auto &q : v.pw1) q.buf.release();
+        v.tables.release();
+        vocos.erase(it);
+    }
+    const int64_t D = p.dim, Hd = p.pw_hidden, bins = p.n_fft / 2 + 1;
+    const auto get = [&](const std::string &suffix, int64_t ne0, int64_t ne1) -> const DevTensor & {
+        const DevTensor &t = W(prefix + suffix);
+        if (t.ne[0] != ne0 || t.ne[1] != ne1 || t.ne[2] != 1 || t.ne[3] != 1)
+            throw KKError(KK_ERROR_MODEL, "vocos: tensor " + prefix + suffix + " has the wrong shape");
+        return t;
+    };
+    VocosNet v;
+    v.p = p;
+    const DevTensor &ew = get("dec.embed.weight", (int64_t)p.mels * p.embed_kernel, D);
+    const DevTensor &nw = get("dec.noise.weight", (int64_t)p.noise_ch * p.embed_kernel, D);
+    const DevTensor &hw = get("dec.head.weight", D, 2 * bins);
+    v.embed_b = &get("dec.embed.bias", D, 1);
+    v.noise_b = &get("dec.noise.bias", D, 1);
+    v.norm_w = &get("dec.norm.weight", D, 1);
+    v.norm_b = &get("dec.norm.bias", D, 1);
+    v.final_w = &get("dec.final_norm.weight", D, 1);
+    v.final_b = &get("dec.final_norm.bias", D, 1);
+    v.head_b = &get("dec.head.bias", 2 * bins, 1);
+    std::vector<const DevTensor *> pw0w, pw1w;
+    for (int i = 0; i < p.blocks; ++i) {
+        const std::string b = "dec.blocks." + std::to_string(i) + ".";
+        v.dw_w.push_back(&get(b + "dw.weight", p.dw_kernel, D));
+        v.dw_b.push_back(&get(b + "dw.bias", D, 1));
+        v.ln_w.push_back(&get(b + "norm.weight", D, 1));
+        v.ln_b.push_back(&get(b + "norm.bias", D, 1));
+        pw0w.push_back(&get(b + "pw0.weight", D, Hd));
+        v.pw0_b.push_back(&get(b + "pw0.bias", Hd, 1));
+        pw1w.push_back(&get(b + "pw1.weight", Hd, D));
+        v.pw1_b.push_back(&get(b + "pw1.bias", D, 1));
+        v.gamma.push_back(&get(b + "gamma", D, 1));
+    }
+    // one tensor-core packing for all the linears: F16 as stored, F32 split
+    std::vector<const DevTensor *> lin = {&ew, &nw, &hw};
+    lin.insert(lin.end(), pw0w.begin(), pw0w.end());
+    lin.insert(lin.end(), pw1w.begin(), pw1w.end());
+    const bool f16 = ew.f16;
+    for (const DevTensor *t : lin)
+        if (t->f16 != f16) throw KKError(KK_ERROR_MODEL, "vocos: the stem, pointwise and head weights mix F16 and F32");
+    if (!f16 && !f32_split)
+        throw KKError(KK_ERROR_MODEL, "vocos: F32 weights need the split tensor-core path (KOKOPOP_B200_F32_SPLIT)");
+    check_cuda(conv_tc_init(), "tensor-core conv init");
+    const auto pack = [&](PackedW &pw, const DevTensor &t, int OC, int IC, int K) {
+        std::vector<float> h((size_t)t.n);
+        check_cuda(cudaMemcpy(h.data(), t.d, h.size() * 4, cudaMemcpyDeviceToHost), "read vocos weight");
+        // ggml [IC * K, OC] (im2col order ic * K + k), or [IC, OC] for K = 1
+        auto g = [&](int oc, int ic, int k) { return h[((size_t)oc * IC + ic) * K + k]; };
+        if (f16)
+            pack_tc(pw, OC, IC, K, g);
+        else
+            pack_tc_split(pw, OC, IC, K, g);
+    };
+    pack(v.embed, ew, (int)D, p.mels, p.embed_kernel);
+    pack(v.noise, nw, (int)D, p.noise_ch, p.embed_kernel);
+    pack(v.head, hw, (int)(2 * bins), (int)D, 1);
+    v.pw0.resize(p.blocks);
+    v.pw1.resize(p.blocks);
+    for (int i = 0; i < p.blocks; ++i) {
+        pack(v.pw0[i], *pw0w[i], (int)Hd, (int)D, 1);
+        pack(v.pw1[i], *pw1w[i], (int)D, (int)Hd, 1);
+    }
+    // istft()'s RealRadix2 plan tables (src/audio/istft.cpp:82-162), each
+    // value computed in double and rounded once
+    const int n = p.n_fft, half = n / 2;
+    std::vector<float> fl((size_t)2 * n + 2 * half + 2 * half, 0.f);
+    float *win = fl.data(), *wsq = win + n, *stc = wsq + n, *sts = stc + half, *spc = sts + half, *sps = spc + half;
+    for (int i = 0; i < n; ++i) {
+        win[i] = (float)(0.5 - 0.5 * std::cos(2.0 * M_PI * (double)i / (double)n));
+        wsq[i] = win[i] * win[i];
+    }
+    for (int h = 1; h < half; h <<= 1) {
+        const int step = half / (2 * h);
+        for (int k = 0; k < h; ++k) {
+            const double a = 2.0 * M_PI * (double)(k * step) / (double)half;
+            stc[h - 1 + k] = (float)std::cos(a);
+            sts[h - 1 + k] = (float)std::sin(a);
+        }
+    }
+    for (int k = 0; k < half; ++k) {
+        const double a = 2.0 * M_PI * (double)k / (double)n;
+        spc[k] = (float)std::cos(a);
+        sps[k] = (float)std::sin(a);
+    }
+    int lg = 0;
+    while ((1 << lg) < half) ++lg;
+    std::vector<int> rev((size_t)half);
+    for (int i = 0; i < half; ++i) {
+        int r = 0;
+        for (int b = 0; b < lg; ++b) r = (r << 1) | ((i >> b) & 1);
+        rev[(size_t)i] = r;
+    }
+    const size_t fb = fl.size() * sizeof(float);
+    v.tables.ensure(fb + rev.size() * sizeof(int));
+    check_cuda(cudaMemcpy(v.tables.p, fl.data(), fb, cudaMemcpyHostToDevice), "upload vocos tables");
+    check_cuda(cudaMemcpy((char *)v.tables.p + fb, rev.data(), rev.size() * sizeof(int), cudaMemcpyHostToDevice),
+               "upload vocos tables");
+    const float *d = (const float *)v.tables.p;
+    v.tab.window = d;
+    v.tab.window_sq = d + n;
+    v.tab.stage_cos = d + 2 * n;
+    v.tab.stage_sin = d + 2 * n + half;
+    v.tab.split_cos = d + 2 * n + 2 * half;
+    v.tab.split_sin = d + 2 * n + 3 * half;
+    v.tab.rev = (const int *)((const char *)v.tables.p + fb);
+    return vocos.emplace(prefix, std::move(v)).first->second;
+}
+
 // ---------------------------------------------------------------------------
 // the forward pass
 // ---------------------------------------------------------------------------
@@ -994,6 +1138,7 @@ struct Runner {
         float scale2 = 1.f;
         int64_t omul = 1, oadd = 0;
         int64_t valid = 0;  // valid output positions (algorithmic FLOP count)
+        const float *chscale = nullptr;  // per output channel, after bias and residual (tensor-core path)
         // non-null: the instance-norm terms (mean, scale) of the output over
         // the utterances of level (sm, sextra), for the AdaIN that reads it next
         float2 *stats = nullptr;
@@ -1092,6 +1237,7 @@ struct Runner {
         a.resid = e.resid;
         a.R_resid = e.R_resid;
         a.resid_half = e.resid_half;
+        a.chscale = e.chscale;
         a.scale1 = e.scale1;
         a.accum = e.accum;
         a.scale2 = e.scale2;
@@ -1661,6 +1807,101 @@ struct Runner {
         generator(2, dec, har, audio);
     }
 
+    // sano_run_vocos (sano_vocos.cpp:94-230) over the chunks of the plan
+    // (level 1 = frames): mel / noise per chunk [C][F_u] back to back ->
+    // audio per chunk [hop (F_u - 1)] back to back. The residual stream x
+    // [dim][R] stays F32; every linear reads a half operand (hi + lo halves
+    // with F32 weights) written by the pass before it.
+    void vocos_forward(const VocosNet &v, const float *mel, const float *noise, float *audio) {
+        const kk_vocos_params &p = v.p;
+        setup_batch();
+        const int64_t R1 = R(1);
+        const int D = p.dim, Hd = p.pw_hidden, n = p.n_fft, bins = n / 2 + 1;
+        float *xm = c.buf("vo_xm", (size_t)p.mels * R1);
+        float *xn = c.buf("vo_xn", (size_t)p.noise_ch * R1);
+        float *x = c.buf("vo_x", (size_t)D * R1);
+        float *hid = c.buf("vo_hid", (size_t)Hd * R1);
+        float *hd = c.buf("vo_head", (size_t)2 * bins * R1);
+        float *fr = c.buf("vo_frames", (size_t)n * R1);
+        check_cuda(cudaMemsetAsync(xm, 0, (size_t)p.mels * R1 * 4, st), "memset");
+        check_cuda(cudaMemsetAsync(xn, 0, (size_t)p.noise_ch * R1 * 4, st), "memset");
+        Op om = op("vo_om", 1, p.mels), on = op("vo_on", 1, p.noise_ch), od = op("vo_od", 1, D),
+           oh = op("vo_oh", 1, Hd);
+        zero(om, p.mels);
+        zero(on, p.noise_ch);
+        zero(od, D);
+        zero(oh, Hd);
+        launch(KK_PROF_OTHER, 0.0, 8.0 * (p.mels + p.noise_ch) * (double)P.total, [&] {
+            scatter(mel, xm, R1, p.mels, 1, 0, B, d_cum, P.maxT, st);
+            scatter(noise, xn, R1, p.noise_ch, 1, 0, B, d_cum, P.maxT, st);
+        });
+        ++c.n_launches;
+        act_only(xm, om, R1, p.mels, 1, 0, ACT_NONE, 0.f);
+        act_only(xn, on, R1, p.noise_ch, 1, 0, ACT_NONE, 0.f);
+        const int64_t valid = sum_len(1, 0);
+        // stem: x = (conv(mel) + b) + (conv(noise) + b), then LayerNorm
+        Epi e;
+        e.bias = v.embed_b;
+        e.valid = valid;
+        conv_h(v.embed, om, p.embed_kernel, p.embed_kernel / 2, 1, x, R1, R1, e);
+        Epi e2;
+        e2.bias = v.noise_b;
+        e2.accum = 1;
+        e2.valid = valid;
+        conv_h(v.noise, on, p.embed_kernel, p.embed_kernel / 2, 1, x, R1, R1, e2);
+        const double el = (double)D * (double)valid;
+        launch(KK_PROF_OTHER, 0.0, 8.0 * el, [&] {
+            check_cuda(layer_norm_ch(x, R1, D, v.norm_w->d, v.norm_b->d, 0, 0.f, 1e-6f, B, x, R1, 0, st),
+                       "layer norm launch");
+        });
+        for (int i = 0; i < p.blocks; ++i) {
+            launch(KK_PROF_OPERAND, 0.0, el * (4.0 + (od.split ? 4.0 : 2.0)), [&] {
+                check_cuda(dw_layer_norm(x, R1, D, p.dw_kernel, v.dw_w[i]->d, v.dw_b[i]->d, v.ln_w[i]->d,
+                                         v.ln_b[i]->d, 1e-6f, B, od.h, od.Ry, od.lo(D), st),
+                           "depthwise conv + layer norm launch");
+            });
+            Epi e0;
+            e0.bias = v.pw0_b[i];
+            e0.valid = valid;
+            conv_h(v.pw0[i], od, 1, 0, 1, hid, R1, R1, e0);
+            act_only(hid, oh, R1, Hd, 1, 0, ACT_GELU, 0.f);
+            Epi e1;
+            e1.bias = v.pw1_b[i];
+            e1.chscale = v.gamma[i]->d;
+            e1.accum = 1;
+            e1.valid = valid;
+            conv_h(v.pw1[i], oh, 1, 0, 1, x, R1, R1, e1);
+        }
+        launch(KK_PROF_OPERAND, 0.0, el * (8.0 + (od.split ? 4.0 : 2.0)), [&] {
+            check_cuda(layer_norm_ch(x, R1, D, v.final_w->d, v.final_b->d, 0, 0.f, 1e-6f, B, x, R1, 0, st, od.h,
+                                     od.Ry, od.lo(D)),
+                       "layer norm launch");
+        });
+        Epi eh;
+        eh.bias = v.head_b;
+        eh.valid = valid;
+        conv_h(v.head, od, 1, 0, 1, hd, R1, R1, eh);
+        // per chunk: audio offsets and lengths (hop (F_u - 1) samples)
+        std::vector<int64_t> ol((size_t)2 * P.n);
+        int64_t acc = 0, max_len = 0;
+        for (int u = 0; u < P.n; ++u) {
+            const int64_t len = (int64_t)p.hop * (P.T[u] - 1);
+            ol[(size_t)u] = acc;
+            ol[(size_t)P.n + u] = len;
+            acc += len;
+            max_len = std::max(max_len, len);
+        }
+        int64_t *d_ol = (int64_t *)c.buf("vo_ol", (size_t)4 * P.n);
+        c.upload(d_ol, ol.data(), ol.size() * sizeof(int64_t), st, "upload audio offsets");
+        launch(KK_PROF_ISTFT, 0.0, 4.0 * (2.0 * bins + n) * (double)valid, [&] {
+            check_cuda(vocos_spectrum(hd, R1, n, p.mag_clip, B, v.tab, fr, st), "vocos spectrum launch");
+        });
+        launch(KK_PROF_ISTFT, 0.0, 4.0 * (double)n * valid + 4.0 * (double)acc,
+               [&] { vocos_ola(fr, n, p.hop, B, d_ol, v.tab.window_sq, max_len, audio, st); });
+        launch(KK_PROF_OTHER, 0.0, 8.0 * (double)acc,
+               [&] { dc_block(audio, d_ol, d_ol + P.n, P.n, p.dc_pole, st); });
+    }
+
     // ggml_generator seam: decoder output given per utterance.
     void generator_forward(const float *decoder, const float *f0, const float *style, float *audio) {
         setup_batch();
@@ -1941,6 +2182,66 @@ int kk_istft(kk_ctx *ctx, int64_t n_frames, const float *post, float *audio) {
         check_cuda(cudaGetLastError(), "kernel launch");
         check_cuda(cudaMemcpyAsync(audio, d_audio, 5 * (size_t)T * 4, cudaMemcpyDeviceToHost, st), "D2H");
         check_cuda(cudaStreamSynchronize(st), "istft");
+        return KK_OK;
+    });
+}
+
+// ---------------------------------------------------------------------------
+// sanoTTS Vocos decoder
+// ---------------------------------------------------------------------------
+
+static void vocos_args(kk_ctx *ctx, const char *prefix, const kk_vocos_params *params, int32_t n_chunks,
+                       const int32_t *n_frames, const void *mel, const void *noise, const void *audio) {
+    if (!ctx || !prefix || !params || n_chunks < 0 || (n_chunks && (!n_frames || !mel || !noise || !audio)))
+        throw KKError(KK_ERROR_INVALID_ARGUMENT, "null argument");
+    for (int32_t u = 0; u < n_chunks; ++u)
+        if (n_frames[u] < 2 || n_frames[u] > kMaxFrames)
+            throw KKError(KK_ERROR_INVALID_ARGUMENT, "vocos: a chunk needs 2 to 8192 frames");
+}
+
+int kk_vocos_forward_device(kk_ctx *ctx, const char *prefix, const kk_vocos_params *params, int32_t n_chunks,
+                            const int32_t *n_frames, const float *mel, const float *noise, float *audio,
+                            void *stream) {
+    return guarded([&] {
+        vocos_args(ctx, prefix, params, n_chunks, n_frames, mel, noise, audio);
+        if (n_chunks == 0) return KK_OK;
+        use_device(ctx);
+        const VocosNet &v = ctx->vocos_net(prefix, *params);
+        const Plan P = make_plan(n_frames, n_chunks);
+        cudaStream_t st = stream ? (cudaStream_t)stream : ctx->st;
+        CallScope call_scope(*ctx, st);
+        Runner r(*ctx, P, st, 1, v.embed.a_wrap > 0);
+        r.vocos_forward(v, mel, noise, audio);
+        check_cuda(cudaGetLastError(), "kernel launch");
+        return KK_OK;
+    });
+}
+
+int kk_vocos_forward(kk_ctx *ctx, const char *prefix, const kk_vocos_params *params, int32_t n_chunks,
+                     const int32_t *n_frames, const float *mel, const float *noise, float *audio) {
+    return guarded([&] {
+        vocos_args(ctx, prefix, params, n_chunks, n_frames, mel, noise, audio);
+        if (n_chunks == 0) return KK_OK;
+        use_device(ctx);
+        const VocosNet &v = ctx->vocos_net(prefix, *params);
+        const Plan P = make_plan(n_frames, n_chunks);
+        int64_t samples = 0;
+        for (int32_t u = 0; u < n_chunks; ++u) samples += (int64_t)params->hop * (n_frames[u] - 1);
+        const size_t tot = (size_t)P.total;
+        float *d_mel = ctx->buf("vo_in_mel", (size_t)params->mels * tot);
+        float *d_noise = ctx->buf("vo_in_noise", (size_t)params->noise_ch * tot);
+        float *d_audio = ctx->buf("vo_out_audio", (size_t)samples);
+        cudaStream_t st = ctx->st;
+        CallScope call_scope(*ctx, st);
+        check_cuda(cudaMemcpyAsync(d_mel, mel, (size_t)params->mels * tot * 4, cudaMemcpyHostToDevice, st), "H2D");
+        check_cuda(cudaMemcpyAsync(d_noise, noise, (size_t)params->noise_ch * tot * 4, cudaMemcpyHostToDevice, st),
+                   "H2D");
+        Runner r(*ctx, P, st, 1, v.embed.a_wrap > 0);
+        r.vocos_forward(v, d_mel, d_noise, d_audio);
+        check_cuda(cudaGetLastError(), "kernel launch");
+        check_cuda(cudaMemcpyAsync(audio, d_audio, (size_t)samples * 4, cudaMemcpyDeviceToHost, st), "D2H");
+        check_cuda(cudaStreamSynchronize(st), "vocos forward");
+        check_device_error(ctx);
         return KK_OK;
     });
 }

@@ -73,6 +73,22 @@ struct LstmLayer {
     const float *bhh[2] = {nullptr, nullptr};
 };
 
+// A sanoTTS Vocos decoder of one voice (its tensor prefix), derived on first
+// use from the uploaded weights and the voice's hyper-parameters: the
+// tensor-core packings of its two stem convolutions, its pointwise linears
+// and its head (F16 weights as they are, F32 weights split hi + lo), the
+// F32 vectors it reads, and the tables of its inverse FFT.
+struct VocosNet {
+    kk_vocos_params p{};
+    PackedW embed, noise, head;
+    std::vector<PackedW> pw0, pw1;
+    const DevTensor *embed_b = nullptr, *noise_b = nullptr, *norm_w = nullptr, *norm_b = nullptr;
+    const DevTensor *final_w = nullptr, *final_b = nullptr, *head_b = nullptr;
+    std::vector<const DevTensor *> dw_w, dw_b, ln_w, ln_b, pw0_b, pw1_b, gamma;
+    DevBuf tables;
+    R2Tables tab{};
+};
+
 struct SiteInfo {
     std::string prefix;
     int C = 0;
@@ -186,6 +202,7 @@ struct kk_ctx {
     kk::DevBuf d_batch;
     std::unordered_map<std::string, kk::DevBuf> ws;
     std::unordered_map<std::string, kk::LstmLayer> lstm;
+    std::unordered_map<std::string, kk::VocosNet> vocos;
     // measurement
     uint64_t n_launches = 0;
     bool profiling = false;
@@ -208,4 +225,5 @@ struct kk_ctx {
     float *buf(const char *name, size_t floats);
     void derive();
     const kk::LstmLayer &lstm_layer(const std::string &prefix);
+    const kk::VocosNet &vocos_net(const std::string &prefix, const kk_vocos_params &p);
 };

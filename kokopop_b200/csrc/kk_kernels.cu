@@ -358,6 +358,7 @@ __global__ void __launch_bounds__(256, SPLIT ? 2 : 3) k_prologue_h(const float *
                     w = __fadd_rn(w, be[e]);
                 }
                 if (ACT == ACT_LEAKY) w = leaky(w, a.slope);
+                if (ACT == ACT_GELU) w = gelu_erf(w);
                 v[i][e] = w;
             }
         }
@@ -431,6 +432,8 @@ static void prologue_h_launch(dim3 grid, const float *x, __half *y, int64_t R, i
             k_prologue_h<false, ACT_SNAKE, SPLIT><<<grid, 256, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
         else if (a.act == ACT_LEAKY)
             k_prologue_h<false, ACT_LEAKY, SPLIT><<<grid, 256, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
+        else if (a.act == ACT_GELU)
+            k_prologue_h<false, ACT_GELU, SPLIT><<<grid, 256, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
         else
             k_prologue_h<false, ACT_NONE, SPLIT><<<grid, 256, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
     }

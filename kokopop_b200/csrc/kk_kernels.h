@@ -6,7 +6,7 @@
 
 namespace kk {
 
-enum { ACT_NONE = 0, ACT_LEAKY = 1, ACT_SNAKE = 2 };
+enum { ACT_NONE = 0, ACT_LEAKY = 1, ACT_SNAKE = 2, ACT_GELU = 3 };
 
 // One AdaIN site (adain_1d / ada_layer_norm): fc weights transposed to
 // [128, C] (F32 values), and per-utterance outputs gamma/beta [n_utts, C].
@@ -168,6 +168,9 @@ struct ConvTcArgs {
     const float *resid;
     int64_t R_resid;
     int resid_half;
+    // non-null: per output channel, multiplies the value after the bias and
+    // the residual, before scale1 (the Vocos layer scale)
+    const float *chscale;
     float scale1;
     int accum;
     float scale2;
@@ -229,6 +232,34 @@ void embed(const float *emb, int C, int vocab, const int32_t *ids, const int64_t
 cudaError_t layer_norm_ch(const float *x, int64_t R, int C, const float *gamma, const float *beta, int leaky_on,
                           float slope, float eps, const Batch &b, float *y, int64_t R_out, int lstm_B,
                           cudaStream_t st, __half *yh = nullptr, int64_t Ryh = 0, int64_t lo_off = 0);
+// ---- sanoTTS Vocos (kk_vocos.cu) ----
+// The tables of istft()'s RealRadix2 plan (src/audio/istft.cpp:96-168) for
+// one n_fft, each computed in double and rounded once: the periodic Hann
+// window and its squares [n], the stage twiddles [half - 1] (entry h - 1 + k
+// for stage h), the split factors [half], and the bit-reversal map [half].
+struct R2Tables {
+    const float *window, *window_sq;
+    const float *stage_cos, *stage_sin;
+    const float *split_cos, *split_sin;
+    const int *rev;
+};
+// depthwise conv (K taps, zero padding per utterance) + bias, then
+// LayerNorm over the C channels (eps) * gamma + beta, into the half operand
+// yh (chunk stride Ryh, lo halves at lo_off when > 0) on the valid rows of
+// level 1 (C <= 1024)
+cudaError_t dw_layer_norm(const float *x, int64_t R, int C, int K, const float *dw_w, const float *dw_b,
+                          const float *gamma, const float *beta, float eps, const Batch &b, __half *yh, int64_t Ryh,
+                          int64_t lo_off, cudaStream_t st);
+// the head output h [2 (n/2 + 1)][R] -> windowed inverse-FFT frames
+// fr [R][n] on the valid rows (n a power of two, 64 .. 4096)
+cudaError_t vocos_spectrum(const float *h, int64_t R, int n, float mag_clip, const Batch &b, const R2Tables &tab,
+                           float *fr, cudaStream_t st);
+// overlap-add of fr into audio + cum[u]: hop (T_u - 1) samples per utterance
+void vocos_ola(const float *fr, int n, int hop, const Batch &b, const int64_t *cum, const float *window_sq,
+               int64_t max_len, float *audio, cudaStream_t st);
+// DC blocker in place over audio + cum[u], len[u] samples each
+void dc_block(float *audio, const int64_t *cum, const int64_t *len, int n_utts, float pole, cudaStream_t st);
+
 // ALBERT self-attention: qkv [3 H][R] -> out [H][R], heads of 64, at most
 // 512 tokens per sequence
 cudaError_t attention(const float *qkv, int64_t R, int H, int n_heads, int max_len, const Batch &b, float scale,

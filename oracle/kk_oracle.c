@@ -1455,3 +1455,264 @@ int kko_align_durations(const float *durations, int64_t n_tokens, float speed, i
     }
     return 0;
 }
+
+/* ------------------------------------------------------------------------ */
+/* sanoTTS Vocos decoder (src/arch/sanotts/sano_vocos.cpp:94-230)           */
+/* ------------------------------------------------------------------------ */
+
+/* The RealRadix2 path of istft (src/audio/istft.cpp:96-168 plan,
+ * :186-375 transform; scalar kernels of src/audio/istft_kernels.h:45-151)
+ * for a power-of-two n_fft >= 64 with center = true. The spectrum is
+ * frame-major (re[f * bins + k], the view sano_run_vocos hands over);
+ * audio gets hop * (frames - 1) samples; no clamp. */
+int kko_istft_r2(const float *re, const float *im, int64_t frames, int n_fft, int hop, float *audio,
+                 int64_t *n_out) {
+    const int n = n_fft, half = n_fft / 2, bins = n_fft / 2 + 1;
+    if (n < 64 || (n & (n - 1)) || hop <= 0 || hop > n) return fail("istft_r2: bad n_fft / hop%s", "");
+    if (n_out) *n_out = 0;
+    if (frames <= 0) return 0;
+    const int64_t padded = (int64_t)hop * (frames - 1) + n;
+    const int64_t out_len = padded - n;
+    float *window = fbuf((size_t)n), *window_sq = fbuf((size_t)n);
+    for (int i = 0; i < n; ++i) {
+        window[i] = (float)(0.5 - 0.5 * cos(2.0 * M_PI * (double)i / (double)n));
+        window_sq[i] = window[i] * window[i];
+    }
+    int log2_half = 0;
+    while ((1 << log2_half) < half) ++log2_half;
+    int *rev = (int *)calloc((size_t)half, sizeof(int));
+    for (int i = 0; i < half; ++i) {
+        int r = 0;
+        for (int b = 0; b < log2_half; ++b) r = (r << 1) | ((i >> b) & 1);
+        rev[i] = r;
+    }
+    float *twc = fbuf((size_t)half), *tws = fbuf((size_t)half);
+    for (int h = 1; h < half; h <<= 1) {
+        const int step = half / (2 * h);
+        for (int k = 0; k < h; ++k) {
+            const double a = 2.0 * M_PI * (double)(k * step) / (double)half;
+            twc[h - 1 + k] = (float)cos(a);
+            tws[h - 1 + k] = (float)sin(a);
+        }
+    }
+    float *scos = fbuf((size_t)half), *ssin = fbuf((size_t)half);
+    for (int k = 0; k < half; ++k) {
+        const double a = 2.0 * M_PI * (double)k / (double)n;
+        scos[k] = (float)cos(a);
+        ssin[k] = (float)sin(a);
+    }
+    float *zr = fbuf((size_t)half), *zi = fbuf((size_t)half), *frame = fbuf((size_t)n);
+    float *ola = fbuf((size_t)padded), *env = fbuf((size_t)padded);
+    const float scale = 0.5f / (float)half;
+    for (int64_t f = 0; f < frames; ++f) {
+        const float *xr = re + f * bins, *xi = im + f * bins;
+        /* hermitian_split */
+        for (int k = 0; k < half; ++k) {
+            const float ar = xr[k], ai = xi[k], mr = xr[half - k], mi = xi[half - k];
+            const float er = scale * (ar + mr), ei = scale * (ai - mi);
+            const float dr = scale * (ar - mr), di = scale * (ai + mi);
+            const float sc = scos[k], ss = ssin[k];
+            zr[k] = er - (dr * ss + di * sc);
+            zi[k] = ei + (dr * sc - di * ss);
+        }
+        /* bit-reversal swaps (each pair once) */
+        for (int i = 0; i < half; ++i)
+            if (rev[i] > i) {
+                const int j = rev[i];
+                float t = zr[i]; zr[i] = zr[j]; zr[j] = t;
+                t = zi[i]; zi[i] = zi[j]; zi[j] = t;
+            }
+        /* fft_stage_pairs then fft_stage for h = 2, 4, ..., half / 2 */
+        for (int i = 0; i < half; i += 2) {
+            const float ar = zr[i], ai = zi[i], br = zr[i + 1], bi = zi[i + 1];
+            zr[i] = ar + br;
+            zi[i] = ai + bi;
+            zr[i + 1] = ar - br;
+            zi[i + 1] = ai - bi;
+        }
+        for (int h = 2; h < half; h <<= 1) {
+            const float *wc = twc + (h - 1), *ws = tws + (h - 1);
+            for (int base = 0; base < half; base += 2 * h)
+                for (int k = 0; k < h; ++k) {
+                    const int a = base + k, b = a + h;
+                    const float brr = zr[b] * wc[k] - zi[b] * ws[k];
+                    const float bii = zr[b] * ws[k] + zi[b] * wc[k];
+                    zr[b] = zr[a] - brr;
+                    zi[b] = zi[a] - bii;
+                    zr[a] = zr[a] + brr;
+                    zi[a] = zi[a] + bii;
+                }
+        }
+        /* interleave_windowed */
+        for (int mm = 0; mm < half; ++mm) {
+            frame[2 * mm] = zr[mm] * window[2 * mm];
+            frame[2 * mm + 1] = zi[mm] * window[2 * mm + 1];
+        }
+        const int64_t base = (int64_t)hop * f;
+        for (int i = 0; i < n; ++i) {
+            ola[base + i] += frame[i];
+            env[base + i] += window_sq[i];
+        }
+    }
+    const int64_t trim = n / 2;
+    for (int64_t j = 0; j < out_len; ++j) {
+        const float e = env[trim + j];
+        audio[j] = e > 1e-8f ? ola[trim + j] / e : 0.0f;
+    }
+    if (n_out) *n_out = out_len;
+    free(window); free(window_sq); free(rev); free(twc); free(tws); free(scos); free(ssin);
+    free(zr); free(zi); free(frame); free(ola); free(env);
+    return 0;
+}
+
+/* ggml semantics, ggml_gelu_erf on F32 (ggml-cpu vec.h):
+ * y = 0.5f * x * (1.0f + erff(x * SQRT_2_INV)), evaluated left to right;
+ * erf taken correctly rounded (the C library's erff differs in the last bit
+ * for some arguments). */
+static float gelu_erf(float x) {
+    const float t = x * 0.70710678118654752440f;
+    const float e = (float)erf((double)t);
+    return (0.5f * x) * (1.0f + e);
+}
+
+/* sano_run_vocos (src/arch/sanotts/sano_vocos.cpp:94-230) for one chunk of
+ * `frames` frames: mel [mels][frames] and noise [noise_ch][frames] (ggml
+ * [frames, C], time-fastest) -> audio [hop * (frames - 1)]. Weight names
+ * under `prefix` ("...dec.embed.weight" etc., sano_arch.cpp:1138-1177).
+ * The trunk runs frame-major [frames][dim] as the reference's [C, T]:
+ *   stem   x = conv_k(mel) + b + conv_k(noise) + b (F32 im2col + mul_mat,
+ *          sano_graph.cpp:35-56), LayerNorm over channels (eps 1e-6)
+ *   block  r = depthwise conv_k(x) + dw_b (:58-71), LayerNorm,
+ *          h = gelu_erf(pw0 r + b0), x = x + (pw1 h + b1) * gamma
+ *   head   LayerNorm, head x + b -> [2 bins]; magnitude
+ *          min(exp(clamp(lm, +-60)), mag_clip) with the DC and Nyquist bins
+ *          zeroed, real = mag cos(phase), imag = mag sin(phase)
+ *   iSTFT  (kko_istft_r2), then the DC blocker (sano_vocos.cpp:81-92).
+ * Dot products are summed in ascending index order; exp / cos / sin are
+ * correctly rounded. */
+int kko_vocos(kko_model *m, const char *prefix, const kko_vocos_dims *d, int64_t frames, const float *mel,
+              const float *noise, float *audio, int64_t *n_out) {
+    g_err[0] = 0;
+    if (frames < 2) return fail("vocos: a chunk needs at least two frames%s", "");
+    const int64_t T = frames, D = d->dim, Hd = d->pw_hidden, bins = d->n_fft / 2 + 1;
+    char k[320];
+#define VREQ(var, suffix)                                   \
+    snprintf(k, sizeof k, "%s%s", prefix, suffix);         \
+    const ko_tensor *var = req(m, k);                       \
+    if (!var) return -1;
+    VREQ(ew, "dec.embed.weight") VREQ(eb, "dec.embed.bias") VREQ(nw, "dec.noise.weight")
+    VREQ(nb, "dec.noise.bias") VREQ(n0w, "dec.norm.weight") VREQ(n0b, "dec.norm.bias")
+    VREQ(fnw, "dec.final_norm.weight") VREQ(fnb, "dec.final_norm.bias") VREQ(hw, "dec.head.weight")
+    VREQ(hb, "dec.head.bias")
+    if (ew->n != D * d->mels * d->embed_kernel || nw->n != D * d->noise_ch * d->embed_kernel ||
+        hw->n != D * 2 * bins)
+        return fail("vocos: weight shapes disagree with the dimensions (%s)", prefix);
+    /* stem: conv outputs are [D][T] (channel-major) */
+    float *s1 = fbuf((size_t)(D * T)), *s2 = fbuf((size_t)(D * T));
+    int64_t ol = 0;
+    if (conv1d(ew, eb, mel, d->mels, T, 1, d->embed_kernel / 2, 1, d->embed_kernel, s1, &ol) != 0 ||
+        conv1d(nw, nb, noise, d->noise_ch, T, 1, d->embed_kernel / 2, 1, d->embed_kernel, s2, &ol) != 0) {
+        free(s1); free(s2);
+        return -1;
+    }
+    float *x = fbuf((size_t)(T * D));
+    for (int64_t c = 0; c < D; ++c)
+        for (int64_t t = 0; t < T; ++t) x[t * D + c] = s1[c * T + t] + s2[c * T + t];
+    free(s1); free(s2);
+    layer_norm_rows(x, T, D, n0w, n0b, 1e-6f);
+    float *r = fbuf((size_t)(T * D)), *h = fbuf((size_t)(T * Hd));
+    const int K = d->dw_kernel, pad = K / 2;
+    for (int bi = 0; bi < d->blocks; ++bi) {
+        char base[200];
+        snprintf(base, sizeof base, "dec.blocks.%d.", bi);
+        char nm[260];
+#define BREQ(var, suffix)                                           \
+        snprintf(nm, sizeof nm, "%s%s", base, suffix);             \
+        snprintf(k, sizeof k, "%s%s", prefix, nm);                 \
+        const ko_tensor *var = req(m, k);                           \
+        if (!var) { free(x); free(r); free(h); return -1; }
+        BREQ(dww, "dw.weight") BREQ(dwb, "dw.bias") BREQ(lnw, "norm.weight") BREQ(lnb, "norm.bias")
+        BREQ(p0w, "pw0.weight") BREQ(p0b, "pw0.bias") BREQ(p1w, "pw1.weight") BREQ(p1b, "pw1.bias")
+        BREQ(gam, "gamma")
+        /* depthwise conv over time, zero padded, + bias */
+        for (int64_t t = 0; t < T; ++t)
+            for (int64_t c = 0; c < D; ++c) {
+                float acc = 0.f;
+                for (int kk = 0; kk < K; ++kk) {
+                    const int64_t tt = t - pad + kk;
+                    if (tt >= 0 && tt < T) acc += x[tt * D + c] * dww->data[c * K + kk];
+                }
+                r[t * D + c] = acc + dwb->data[c];
+            }
+        layer_norm_rows(r, T, D, lnw, lnb, 1e-6f);
+#pragma omp parallel for schedule(static)
+        for (int64_t t = 0; t < T; ++t) {
+            const float *rt = r + t * D;
+            float *ht = h + t * Hd;
+            for (int64_t j = 0; j < Hd; ++j) {
+                const float *wj = p0w->data + j * D;
+                float acc = 0.f;
+                for (int64_t c = 0; c < D; ++c) acc += wj[c] * rt[c];
+                ht[j] = gelu_erf(acc + p0b->data[j]);
+            }
+            float *xt = x + t * D;
+            for (int64_t c = 0; c < D; ++c) {
+                const float *wc = p1w->data + c * Hd;
+                float acc = 0.f;
+                for (int64_t j = 0; j < Hd; ++j) acc += wc[j] * ht[j];
+                const float o = acc + p1b->data[c];
+                xt[c] = xt[c] + o * gam->data[c];
+            }
+        }
+#undef BREQ
+    }
+    free(r);
+    free(h);
+    layer_norm_rows(x, T, D, fnw, fnb, 1e-6f);
+    float *re = fbuf((size_t)(T * bins)), *im = fbuf((size_t)(T * bins));
+    const float clip = d->mag_clip;
+#pragma omp parallel for schedule(static)
+    for (int64_t t = 0; t < T; ++t) {
+        const float *xt = x + t * D;
+        for (int64_t kb = 0; kb < bins; ++kb) {
+            float lm = 0.f, ph = 0.f;
+            for (int pass = 0; pass < 2; ++pass) {
+                const int64_t o = pass * bins + kb;
+                const float *wo = hw->data + o * D;
+                float acc = 0.f;
+                for (int64_t c = 0; c < D; ++c) acc += wo[c] * xt[c];
+                if (pass == 0) lm = acc + hb->data[o];
+                else ph = acc + hb->data[o];
+            }
+            float v = lm < -60.0f ? -60.0f : (lm > 60.0f ? 60.0f : lm);
+            float mag = (float)exp((double)v);
+            mag = mag < 0.0f ? 0.0f : (mag > clip ? clip : mag);
+            if (kb == 0 || kb == bins - 1) mag = mag * 0.0f;
+            re[t * bins + kb] = mag * (float)cos((double)ph);
+            im[t * bins + kb] = mag * (float)sin((double)ph);
+        }
+    }
+    free(x);
+    int64_t n = 0;
+    const int rc = kko_istft_r2(re, im, T, d->n_fft, d->hop, audio, &n);
+    free(re);
+    free(im);
+    if (rc != 0) return rc;
+    kko_dc_block(audio, n, d->dc_pole);
+    if (n_out) *n_out = n;
+    return 0;
+#undef VREQ
+}
+
+/* The first-order DC blocker of sano_vocos.cpp:81-92, in sample order:
+ * y[n] = x[n] - x[n - 1] + pole * y[n - 1], from zero state. */
+void kko_dc_block(float *audio, int64_t n, float pole) {
+    float prev_in = 0.0f, prev_out = 0.0f;
+    for (int64_t i = 0; i < n; ++i) {
+        const float input = audio[i];
+        const float output = input - prev_in + pole * prev_out;
+        prev_in = input;
+        prev_out = output;
+        audio[i] = output;
+    }
+}

@@ -132,6 +132,29 @@ int kko_duration_proj(kko_model *m, int64_t N, const float *h, float *durations)
  * tree); exp and tanh are taken correctly rounded (see kk_oracle.c). */
 int kko_albert(kko_model *m, int64_t N, const int32_t *ids, float *out);
 
+/* ---- sanoTTS Vocos decoder (src/arch/sanotts/sano_vocos.cpp:94-230) ----
+ * The voice's decoder hyper-parameters (its GGUF dec.* keys,
+ * src/arch/sanotts/sano_arch.cpp:1081-1096). */
+typedef struct kko_vocos_dims {
+    int32_t dim, blocks, pw_hidden, dw_kernel, embed_kernel, noise_ch, mels, n_fft, hop;
+    float dc_pole, mag_clip;
+} kko_vocos_dims;
+
+/* mel [mels][frames], noise [noise_ch][frames] (time-fastest) -> audio
+ * [hop * (frames - 1)]; weights "<prefix>dec.embed.weight", ... PARITY
+ * UNPINNED for the trunk (ggml ops); the iSTFT restatement is pinned
+ * against the reference's compiled istft.cpp. */
+int kko_vocos(kko_model *m, const char *prefix, const kko_vocos_dims *d, int64_t frames, const float *mel,
+              const float *noise, float *audio, int64_t *n_out);
+
+/* The RealRadix2 iSTFT (power-of-two n_fft >= 64, center): re / im
+ * frame-major [frames][n_fft / 2 + 1] -> audio [hop * (frames - 1)]. */
+int kko_istft_r2(const float *re, const float *im, int64_t frames, int n_fft, int hop, float *audio,
+                 int64_t *n_out);
+
+/* The DC blocker y[n] = x[n] - x[n-1] + pole y[n-1], in place. */
+void kko_dc_block(float *audio, int64_t n, float pole);
+
 /* Single-op entry points used by the unit tests. */
 void kko_norm_time(const float *x, int64_t C, int64_t L, float eps, float *y);
 float kko_round_f16(float x);

@@ -87,6 +87,12 @@ struct ggml_tensor *ggml_add(struct ggml_context *ctx, struct ggml_tensor *a, st
 struct ggml_tensor *ggml_repeat(struct ggml_context *ctx, struct ggml_tensor *a, struct ggml_tensor *b);
 struct ggml_tensor *ggml_concat(struct ggml_context *ctx, struct ggml_tensor *a, struct ggml_tensor *b, int dim);
 struct ggml_tensor *ggml_mul_mat(struct ggml_context *ctx, struct ggml_tensor *a, struct ggml_tensor *b);
+struct ggml_tensor *ggml_mul(struct ggml_context *ctx, struct ggml_tensor *a, struct ggml_tensor *b);
+struct ggml_tensor *ggml_exp(struct ggml_context *ctx, struct ggml_tensor *a);
+struct ggml_tensor *ggml_sin(struct ggml_context *ctx, struct ggml_tensor *a);
+struct ggml_tensor *ggml_cos(struct ggml_context *ctx, struct ggml_tensor *a);
+struct ggml_tensor *ggml_clamp(struct ggml_context *ctx, struct ggml_tensor *a, float min, float max);
+struct ggml_tensor *ggml_gelu_erf(struct ggml_context *ctx, struct ggml_tensor *a);
 struct ggml_tensor *ggml_get_rows(struct ggml_context *ctx, struct ggml_tensor *a, struct ggml_tensor *b);
 struct ggml_tensor *ggml_gelu(struct ggml_context *ctx, struct ggml_tensor *a);
 struct ggml_tensor *ggml_soft_max_ext(struct ggml_context *ctx, struct ggml_tensor *a, struct ggml_tensor *mask,
