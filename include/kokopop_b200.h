@@ -311,7 +311,7 @@ typedef struct kk_vocos_params {
  *   mel   : [F_u, mels]      (time-fastest: mel[c * F_u + t])
  *   noise : [F_u, noise_ch]  (time-fastest)
  *   audio : [hop (F_u - 1)] samples
- * n_fft must be a power of two in [64, 4096], dim and pw_hidden at most
+ * n_fft must be a power of two in [64, 2048], dim and pw_hidden at most
  * 1024, the kernels odd. Host buffers. */
 int kk_vocos_forward(kk_ctx *ctx, const char *prefix, const kk_vocos_params *params, int32_t n_chunks,
                      const int32_t *n_frames, const float *mel, const float *noise, float *audio);

@@ -47,6 +47,18 @@ class Profile(ctypes.Structure):
     ]
 
 
+class VocosParams(ctypes.Structure):
+    """kk_vocos_params."""
+    _fields_ = [(n, ctypes.c_int32) for n in ("dim", "blocks", "pw_hidden", "dw_kernel", "embed_kernel",
+                                                 "noise_ch", "mels", "n_fft", "hop")] + \
+               [("dc_pole", ctypes.c_float), ("mag_clip", ctypes.c_float)]
+
+    @classmethod
+    def of(cls, d: Dict) -> "VocosParams":
+        return cls(*(int(d[n]) for n in ("dim", "blocks", "pw_hidden", "dw_kernel", "embed_kernel", "noise_ch",
+                                         "mels", "n_fft", "hop")), float(d["dc_pole"]), float(d["mag_clip"]))
+
+
 class ProfileRecord(ctypes.Structure):
     _fields_ = [
         ("kind", ctypes.c_int32),
@@ -120,6 +132,10 @@ def load_library():
     L.kk_profile_enable.argtypes = [vp, ctypes.c_int]
     L.kk_profile_read.argtypes = [vp, ctypes.POINTER(Profile), ctypes.c_int]
     L.kk_allocation_count.argtypes = [ctypes.POINTER(ctypes.c_uint64)]
+    L.kk_vocos_forward.argtypes = [vp, ctypes.c_char_p, ctypes.POINTER(VocosParams), ctypes.c_int32, _i32p, _f32p,
+                                   _f32p, _f32p]
+    L.kk_vocos_forward_device.argtypes = [vp, ctypes.c_char_p, ctypes.POINTER(VocosParams), ctypes.c_int32, _i32p,
+                                          vp, vp, vp, vp]
     L.kk_profile_records.argtypes = [vp, ctypes.POINTER(ProfileRecord), ctypes.c_size_t,
                                      ctypes.POINTER(ctypes.c_size_t)]
     _lib = L
@@ -240,6 +256,32 @@ class Context:
         self._check(self.L.kk_profile_read(self.h, ctypes.byref(p), 1 if reset else 0))
         return {"launches": int(p.launches), "conv_launches": int(p.conv_launches),
                 "conv_ms": float(p.conv_ms), "conv_flop": float(p.conv_flop)}
+
+    def vocos_forward(self, prefix: str, dims: Dict, mels: Sequence[np.ndarray],
+                      noises: Sequence[np.ndarray]) -> List[np.ndarray]:
+        """kk_vocos_forward over chunks: mels[u] [mels, F_u], noises[u]
+        [noise_ch, F_u] (time-fastest) -> audio [hop (F_u - 1)] each."""
+        p = VocosParams.of(dims)
+        lens = np.array([m.shape[1] for m in mels], np.int32)
+        mel = np.concatenate([np.ascontiguousarray(m, np.float32).reshape(-1) for m in mels])
+        noise = np.concatenate([np.ascontiguousarray(z, np.float32).reshape(-1) for z in noises])
+        hop = int(dims["hop"])
+        audio = np.zeros(max(1, int((hop * (lens - 1)).sum())), np.float32)
+        self._check(self.L.kk_vocos_forward(self.h, prefix.encode(), ctypes.byref(p), len(lens), _ptr(lens, _i32p),
+                                            _ptr(mel), _ptr(noise), _ptr(audio)))
+        out, o = [], 0
+        for f in lens:
+            n = hop * (int(f) - 1)
+            out.append(audio[o:o + n])
+            o += n
+        return out
+
+    def vocos_forward_device(self, prefix: str, dims: Dict, lens: np.ndarray, mel_ptr: int, noise_ptr: int,
+                             audio_ptr: int, stream: int = 0) -> None:
+        p = VocosParams.of(dims)
+        lens = np.ascontiguousarray(lens, np.int32)
+        self._check(self.L.kk_vocos_forward_device(self.h, prefix.encode(), ctypes.byref(p), len(lens),
+                                                   _ptr(lens, _i32p), mel_ptr, noise_ptr, audio_ptr, stream or None))
 
     def profile_records(self) -> List[Dict[str, float]]:
         """The timed launches since the last reset: kind (PROF_KINDS), taps,

@@ -881,7 +881,7 @@ const VocosNet &kk_ctx::vocos_net(const std::string &prefix, const kk_vocos_para
         p.embed_kernel > 63)
         bad("kernels must be odd (at most 63)");
     if (p.mels < 1 || p.mels > 1024 || p.noise_ch < 1 || p.noise_ch > 1024) bad("mels / noise_ch out of range");
-    if (p.n_fft < 64 || p.n_fft > 4096 || (p.n_fft & (p.n_fft - 1))) bad("n_fft must be a power of two in [64, 4096]");
+    if (p.n_fft < 64 || p.n_fft > 2048 || (p.n_fft & (p.n_fft - 1))) bad("n_fft must be a power of two in [64, 2048]");
     if (p.hop < 1 || p.hop > p.n_fft) bad("hop must lie in (0, n_fft]");
     if (!std::isfinite(p.dc_pole) || std::fabs(p.dc_pole) >= 1.0f) bad("dc_pole must be a stable pole in (-1, 1)");
     if (!std::isfinite(p.mag_clip) || p.mag_clip <= 0.0f) bad("mag_clip must be finite and positive");

@@ -251,7 +251,7 @@ cudaError_t dw_layer_norm(const float *x, int64_t R, int C, int K, const float *
                           const float *gamma, const float *beta, float eps, const Batch &b, __half *yh, int64_t Ryh,
                           int64_t lo_off, cudaStream_t st);
 // the head output h [2 (n/2 + 1)][R] -> windowed inverse-FFT frames
-// fr [R][n] on the valid rows (n a power of two, 64 .. 4096)
+// fr [R][n] on the valid rows (n a power of two, 64 .. 2048)
 cudaError_t vocos_spectrum(const float *h, int64_t R, int n, float mag_clip, const Batch &b, const R2Tables &tab,
                            float *fr, cudaStream_t st);
 // overlap-add of fr into audio + cum[u]: hop (T_u - 1) samples per utterance

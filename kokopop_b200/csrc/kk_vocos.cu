@@ -231,9 +231,11 @@ __global__ void __launch_bounds__(256) k_vocos_spectrum(const float *__restrict_
         out[m] = make_float2(__fmul_rn(zr[m], tab.window[2 * m]), __fmul_rn(zi[m], tab.window[2 * m + 1]));
 }
 
+constexpr int kSpecMaxN = 2048;  // 8 frames of spectrum + FFT buffers: 131 KB of shared memory
+
 cudaError_t vocos_spectrum(const float *h, int64_t R, int n, float mag_clip, const Batch &b, const R2Tables &tab,
                            float *fr, cudaStream_t st) {
-    if (n < 64 || n > 4096 || (n & (n - 1))) return cudaErrorInvalidValue;
+    if (n < 64 || n > kSpecMaxN || (n & (n - 1))) return cudaErrorInvalidValue;
     static std::atomic<bool> attr[64];
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -242,7 +244,7 @@ cudaError_t vocos_spectrum(const float *h, int64_t R, int n, float mag_clip, con
     const size_t smem = (size_t)kSpecFrames * (2 * (n / 2 + 1) + n) * sizeof(float);
     if (!attr[dev].load(std::memory_order_acquire)) {
         e = cudaFuncSetAttribute(k_vocos_spectrum, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)(kSpecFrames * (2 * (4096 / 2 + 1) + 4096) * sizeof(float)));
+                                 (int)(kSpecFrames * (2 * (kSpecMaxN / 2 + 1) + kSpecMaxN) * sizeof(float)));
         if (e != cudaSuccess) return e;
         attr[dev].store(true, std::memory_order_release);
     }

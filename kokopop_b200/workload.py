@@ -268,6 +268,61 @@ def prosody_weights(f16: bool = False) -> Dict[str, Tensor]:
     return make_weights(prosody_spec(), seed=2, dist="normal", scale=0.02, f16=f16)
 
 
+# --------------------------------------------------------------------------
+# sanoTTS Vocos decoder
+# --------------------------------------------------------------------------
+
+# Tensor prefix of voice 0 in a sanoTTS GGUF (sano_arch.cpp:47).
+VOCOS_PREFIX = "kokopop.sanotts.voice.0."
+
+# The `heart` voice's decoder dimensions come from an upstream header
+# (nano_q8_meta.h, read by tools/convert_sanotts_to_gguf.py:2226-2291) that
+# is not available here; these stand in for them. n_fft 1024 / hop 256, the
+# DC pole 0.9973 and mag_clip 100 are the converter's own values
+# (:2362-2381), four noise channels the noise adapter's (sano_noise.h).
+VOCOS_DIMS = dict(dim=256, blocks=8, pw_hidden=768, dw_kernel=7, embed_kernel=7, noise_ch=4, mels=80,
+                  n_fft=1024, hop=256, dc_pole=0.9973, mag_clip=100.0)
+
+
+def vocos_spec(prefix: str = VOCOS_PREFIX, dims: Dict = VOCOS_DIMS) -> List[Tuple[str, Tuple[int, ...]]]:
+    """Tensor names and ggml shapes the loader expects (load_vocos,
+    sano_arch.cpp:1138-1177)."""
+    d = dims
+    D, H, bins = d["dim"], d["pw_hidden"], d["n_fft"] // 2 + 1
+    p = prefix + "dec."
+    spec = [(p + "embed.weight", (d["mels"] * d["embed_kernel"], D)), (p + "embed.bias", (D,)),
+            (p + "noise.weight", (d["noise_ch"] * d["embed_kernel"], D)), (p + "noise.bias", (D,)),
+            (p + "norm.weight", (D,)), (p + "norm.bias", (D,)),
+            (p + "final_norm.weight", (D,)), (p + "final_norm.bias", (D,)),
+            (p + "head.weight", (D, 2 * bins)), (p + "head.bias", (2 * bins,))]
+    for i in range(d["blocks"]):
+        b = f"{p}blocks.{i}."
+        spec += [(b + "dw.weight", (d["dw_kernel"], D)), (b + "dw.bias", (D,)), (b + "norm.weight", (D,)),
+                 (b + "norm.bias", (D,)), (b + "pw0.weight", (D, H)), (b + "pw0.bias", (H,)),
+                 (b + "pw1.weight", (H, D)), (b + "pw1.bias", (D,)), (b + "gamma", (D,))]
+    return spec
+
+
+def vocos_weights(f16: bool = False, seed: int = 3, prefix: str = VOCOS_PREFIX, dims: Dict = VOCOS_DIMS):
+    """The Vocos decoder: seed 3, N(0, 0.02); the LayerNorm weights drawn
+    around 1 (N(1, 0.02)) so that the normalised activations keep their
+    scale. F32 (the configuration's), or F16 for the multi-dimensional
+    tensors."""
+    w = make_weights(vocos_spec(prefix, dims), seed=seed, dist="normal", scale=0.02, f16=f16)
+    for name, t in w.items():
+        if name.endswith("norm.weight"):
+            t.data[...] = (t.data.astype(np.float32) + np.float32(1.0)).astype(t.data.dtype)
+    return w
+
+
+def vocos_inputs(rng: np.random.Generator, frames: int, dims: Dict = VOCOS_DIMS):
+    """One chunk's mel features [mels, frames] ~ N(0, 1) and noise
+    [noise_ch, frames] ~ N(0, 1) (time-fastest, the ggml [frames, C])."""
+    mel = rng.normal(0.0, 1.0, size=(dims["mels"], frames)).astype(np.float32)
+    noise = rng.normal(0.0, 1.0, size=(dims["noise_ch"], frames)).astype(np.float32)
+    return mel, noise
+
+
 def _is_f16_under_converter_policy(name: str, ne: Sequence[int]) -> bool:
     """_target_type (tools/convert_kokoro_to_gguf.py:140-177) for these tensors."""
     if len(ne) <= 1:

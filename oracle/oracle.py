@@ -85,6 +85,37 @@ def lib():
     return _lib
 
 
+class VocosDims(ctypes.Structure):
+    """kko_vocos_dims."""
+    _int_names = ("dim", "blocks", "pw_hidden", "dw_kernel", "embed_kernel", "noise_ch", "mels", "n_fft", "hop")
+    _fields_ = [(n, ctypes.c_int32) for n in _int_names] + [("dc_pole", ctypes.c_float),
+                                                              ("mag_clip", ctypes.c_float)]
+
+
+def istft_r2(re: np.ndarray, im: np.ndarray, n_fft: int, hop: int) -> np.ndarray:
+    """kko_istft_r2: frame-major re / im [F, n_fft/2 + 1] -> audio [hop (F - 1)]."""
+    re = np.ascontiguousarray(re, np.float32)
+    im = np.ascontiguousarray(im, np.float32)
+    F = re.shape[0]
+    audio = np.zeros(max(1, hop * (F - 1)), np.float32)
+    n = ctypes.c_int64(0)
+    L = lib()
+    L.kko_istft_r2.argtypes = [_f32p, _f32p, ctypes.c_int64, ctypes.c_int, ctypes.c_int, _f32p,
+                               ctypes.POINTER(ctypes.c_int64)]
+    if L.kko_istft_r2(_ptr(re), _ptr(im), F, n_fft, hop, _ptr(audio), ctypes.byref(n)) != 0:
+        raise RuntimeError(L.kko_last_error().decode())
+    return audio[: n.value]
+
+
+def dc_block(audio: np.ndarray, pole: float) -> np.ndarray:
+    a = np.array(audio, np.float32, copy=True)
+    L = lib()
+    L.kko_dc_block.argtypes = [_f32p, ctypes.c_int64, ctypes.c_float]
+    L.kko_dc_block.restype = None
+    L.kko_dc_block(_ptr(a), len(a), ctypes.c_float(pole))
+    return a
+
+
 TAP_FN = ctypes.CFUNCTYPE(None, ctypes.c_char_p, _f32p, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p)
 
 
@@ -217,6 +248,19 @@ class OracleModel:
                                              _ptr(out)))
         return out
 
+    def vocos(self, prefix: str, dims, mel: np.ndarray, noise: np.ndarray) -> np.ndarray:
+        """kko_vocos: mel [mels, F], noise [noise_ch, F] -> audio [hop (F - 1)]."""
+        d = VocosDims(*(int(dims[n]) for n in VocosDims._int_names), float(dims["dc_pole"]),
+                      float(dims["mag_clip"]))
+        mel = np.ascontiguousarray(mel, np.float32)
+        noise = np.ascontiguousarray(noise, np.float32)
+        F = mel.shape[1]
+        audio = np.zeros(max(1, int(dims["hop"]) * (F - 1)), np.float32)
+        n = ctypes.c_int64(0)
+        self._check(self.L.kko_vocos(ctypes.c_void_p(self.h), prefix.encode(), ctypes.byref(d), ctypes.c_int64(F),
+                                     _ptr(mel), _ptr(noise), _ptr(audio), ctypes.byref(n)))
+        return audio[: n.value]
+
     def duration_proj(self, h: np.ndarray):
         """kko_duration_proj: the predictor biLSTM output [N, 512] -> durations [N]."""
         h = np.ascontiguousarray(h, dtype=np.float32)
@@ -292,8 +336,49 @@ def ref():
         R.kkref_harmonic_stft.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int64, _f32p, ctypes.c_float, _f32p, _f32p]
         R.kkref_duration_to_frames.argtypes = [ctypes.c_float, ctypes.c_float]
         R.kkref_duration_mask.argtypes = [ctypes.POINTER(ctypes.c_int32), ctypes.c_int64, ctypes.c_int64, _f32p]
+        R.kkref_istft_complex.argtypes = [_f32p, _f32p, ctypes.c_int64, ctypes.c_int, ctypes.c_int, _f32p,
+                                          ctypes.POINTER(ctypes.c_int64)]
+        R.kkref_dc_block.argtypes = [_f32p, ctypes.c_int64, ctypes.c_float]
+        R.kkref_dc_block.restype = None
+        R.kkref_bin_mask.argtypes = [ctypes.c_uint32, _f32p]
+        R.kkref_bin_mask.restype = None
+        R.kkref_sano_noise.argtypes = [ctypes.c_uint64, ctypes.c_int64, ctypes.c_int64, _f32p]
         _ref = R
     return _ref
+
+
+def ref_istft_complex(re: np.ndarray, im: np.ndarray, n_fft: int, hop: int) -> np.ndarray:
+    """The reference's istft() (src/audio/istft.cpp) on a frame-major
+    spectrum [F, n_fft/2 + 1], centred."""
+    re = np.ascontiguousarray(re, np.float32)
+    im = np.ascontiguousarray(im, np.float32)
+    F = re.shape[0]
+    audio = np.zeros(max(1, hop * (F - 1)), np.float32)
+    n = ctypes.c_int64(0)
+    if ref().kkref_istft_complex(_ptr(re), _ptr(im), F, n_fft, hop, _ptr(audio), ctypes.byref(n)) != 0:
+        raise RuntimeError("reference istft failed")
+    return audio[: n.value]
+
+
+def ref_dc_block(audio: np.ndarray, pole: float) -> np.ndarray:
+    """The reference's dc_block (src/arch/sanotts/sano_vocos.cpp:81-92)."""
+    a = np.array(audio, np.float32, copy=True)
+    ref().kkref_dc_block(_ptr(a), len(a), ctypes.c_float(pole))
+    return a
+
+
+def ref_bin_mask(bins: int) -> np.ndarray:
+    m = np.zeros(bins, np.float32)
+    ref().kkref_bin_mask(bins, _ptr(m))
+    return m
+
+
+def ref_sano_noise(seed: int, channels: int, frames: int) -> np.ndarray:
+    """The reference's sano::seeded_noise: [channels, frames]."""
+    out = np.zeros((channels, frames), np.float32)
+    if ref().kkref_sano_noise(seed, channels, frames, _ptr(out)) != 0:
+        raise RuntimeError("reference seeded_noise failed")
+    return out
 
 
 def ref_harmonic_stft(f0: np.ndarray, target_frames: int, merge_w: np.ndarray, merge_b: float):

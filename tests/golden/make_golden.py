@@ -15,6 +15,11 @@
   align_ref.npz   edge-case durations at several speeds with the frame counts
                   of the reference's duration_to_frames and the mask of its
                   build_duration_mask (src/arch/kokoro/kokoro.cpp)
+  vocos_ref.npz   seeded frame-major spectra with the output of the
+                  reference's istft() (its radix-2 path at n_fft 1024 / hop
+                  256, and n_fft 64), the reference's DC blocker
+                  (src/arch/sanotts/sano_vocos.cpp) on a seeded signal, and
+                  its DC / Nyquist bin mask
   oracle_small.npz  regression vectors of the oracle itself (decoder + generator
                   at T=3 for the F32 and F16 weight sets); these are NOT
                   reference outputs (the reference's generator needs ggml,
@@ -102,6 +107,19 @@ def main():
     al["mask_frames"] = al["frames_0"][:24]
     al["mask"] = O.ref_duration_mask(al["mask_frames"])
     np.savez_compressed(os.path.join(OUT, "align_ref.npz"), **al)
+
+    vs = {}
+    for F, n, hop in ((5, 1024, 256), (3, 64, 16)):
+        bins = n // 2 + 1
+        re = rng.normal(0.0, 1.0, size=(F, bins)).astype(np.float32)
+        im = rng.normal(0.0, 1.0, size=(F, bins)).astype(np.float32)
+        vs[f"re_{n}"], vs[f"im_{n}"] = re, im
+        vs[f"hop_{n}"] = np.int32(hop)
+        vs[f"audio_{n}"] = O.ref_istft_complex(re, im, n, hop)
+    x = rng.normal(0.0, 1.0, size=3000).astype(np.float32)
+    vs["dc_in"], vs["dc_out"] = x, O.ref_dc_block(x, 0.9973)
+    vs["mask_513"] = O.ref_bin_mask(513)
+    np.savez_compressed(os.path.join(OUT, "vocos_ref.npz"), **vs)
 
     sm = {}
     u = W.make_utterance(np.random.default_rng(11), 3)

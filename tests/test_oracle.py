@@ -260,6 +260,45 @@ def test_source_last_bit_sensitivity_is_why_the_source_is_correctly_rounded():
     assert np.abs(cr - pert).max() < 1e-4
 
 
+# --- sanoTTS Vocos: iSTFT (radix-2 path) and DC blocker ---------------------
+
+def test_vocos_istft_and_dc_block_match_reference_golden_bit_exact():
+    """istft() at n_fft 1024 / hop 256 (its RealRadix2 path) and at n_fft 64,
+    dc_block and bin_mask of the reference's own sources (compiled unchanged
+    into oracle/_ref/): the oracle's restatement equals them exactly."""
+    z = g("vocos_ref.npz")
+    for n in (1024, 64):
+        got = O.istft_r2(z[f"re_{n}"], z[f"im_{n}"], n, int(z[f"hop_{n}"]))
+        np.testing.assert_array_equal(got, z[f"audio_{n}"])
+    np.testing.assert_array_equal(O.dc_block(z["dc_in"], 0.9973), z["dc_out"])
+    mask = z["mask_513"]
+    assert mask[0] == 0 and mask[-1] == 0 and np.all(mask[1:-1] == 1)
+
+
+@pytest.mark.skipif(not O.ref_available(), reason="oracle/_ref not built")
+@pytest.mark.parametrize("F,n,hop", [(2, 1024, 256), (938, 1024, 256), (40, 2048, 512), (25, 128, 128)])
+def test_vocos_istft_matches_reference_library(F, n, hop):
+    rng = np.random.default_rng(F + n)
+    bins = n // 2 + 1
+    re = rng.normal(0.0, 2.0, size=(F, bins)).astype(np.float32)
+    im = rng.normal(0.0, 2.0, size=(F, bins)).astype(np.float32)
+    np.testing.assert_array_equal(O.istft_r2(re, im, n, hop), O.ref_istft_complex(re, im, n, hop))
+
+
+def test_vocos_restatement_shapes_and_determinism():
+    """The oracle's Vocos decoder (unpinned trunk: ggml ops): hop (F - 1)
+    samples, finite, repeatable; a chunk of one frame is rejected like the
+    reference (sano_vocos.cpp:105-108)."""
+    d = W.VOCOS_DIMS
+    m = O.OracleModel(W.vocos_weights())
+    mel, noise = W.vocos_inputs(np.random.default_rng(8), 12)
+    a, b = m.vocos(W.VOCOS_PREFIX, d, mel, noise), m.vocos(W.VOCOS_PREFIX, d, mel, noise)
+    assert a.shape == (d["hop"] * 11,) and np.all(np.isfinite(a))
+    np.testing.assert_array_equal(a, b)
+    with pytest.raises(RuntimeError):
+        m.vocos(W.VOCOS_PREFIX, d, mel[:, :1], noise[:, :1])
+
+
 def test_oracle_regression_small():
     z = g("oracle_small.npz")
     for tag, wts in (("f32", W.config0_weights()), ("f16", W.config2_weights())):
