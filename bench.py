@@ -351,6 +351,63 @@ def bench_prosody(kb, W, device, runs, pool, batch):
             "audio_s_per_s": rows / 40.0 / (ms / 1e3)}
 
 
+def bench_vocos(kb, W, device, runs, batch=64):
+    """The sanoTTS Vocos decoder: `batch` chunks of 10 s (938 frames at hop
+    256), F32 weights seed 3 at the stand-in dimensions of
+    workload.VOCOS_DIMS, inputs N(0, 1), device-resident, timed with CUDA
+    events on the launch stream (the median of `runs` calls): ms per call,
+    audio-s/s, and the tensor-core linears' TFLOP/s from the profile
+    records of one call."""
+    import statistics
+    import torch
+    d = W.VOCOS_DIMS
+    frames = 938
+    c = kb.Context(device)
+    c.upload(W.vocos_weights(f16=False))
+    g = torch.Generator(device="cuda").manual_seed(104)
+    lens = np.full(batch, frames, np.int32)
+    mel = torch.randn(batch * d["mels"] * frames, device="cuda", generator=g)
+    noise = torch.randn(batch * d["noise_ch"] * frames, device="cuda", generator=g)
+    out = torch.empty(batch * d["hop"] * (frames - 1), device="cuda")
+    stream = torch.cuda.Stream()
+    call = lambda: c.vocos_forward_device(W.VOCOS_PREFIX, d, lens, mel.data_ptr(), noise.data_ptr(), out.data_ptr(),
+                                          stream.cuda_stream)
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(runs):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        call()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    c.profile_read(reset=True)
+    c.profile_enable(True)
+    call()
+    torch.cuda.synchronize()
+    c.profile_enable(False)
+    recs = c.profile_records()
+    c.profile_read(reset=True)
+    c.close()
+    ms = statistics.median(ts)
+    secs = batch * d["hop"] * (frames - 1) / 24000.0
+    kinds = {}
+    for r in recs:
+        k = kinds.setdefault(r["kind"], {"ms": 0.0, "flop": 0.0, "bytes": 0.0, "launches": 0})
+        k["ms"] += r["ms"]
+        k["flop"] += r["flop"]
+        k["bytes"] += r["bytes"]
+        k["launches"] += 1
+    conv = kinds.get("conv", {"ms": 0.0, "flop": 0.0})
+    return {"workload": f"sanoTTS Vocos decoder, {batch} chunks of {frames} frames (10 s each), F32 weights seed 3, "
+                        f"dims {d} (stand-ins: the heart voice's are not available)",
+            "ms_per_call": ms, "audio_s_per_s": secs / (ms / 1e3),
+            "linears_tflops": conv["flop"] / (conv["ms"] / 1e3) / 1e12 if conv["ms"] else None,
+            "ms_by_kind": {k: round(v["ms"], 4) for k, v in kinds.items()}}
+
+
 def bench_frontend(kb, W, device, runs):
     """Config 2's front end for one utterance of 128 phoneme ids (130 with the
     pads), F16 weights seed 2, device-resident, each stage timed with CUDA
@@ -452,6 +509,7 @@ def main():
     ap.add_argument("--lstm-runs", type=int, default=5, help="timed calls per LSTM-stack case (0 skips)")
     ap.add_argument("--prosody-runs", type=int, default=3, help="timed calls of the prosody F0/N chain (0 skips)")
     ap.add_argument("--frontend-runs", type=int, default=5, help="timed calls per front-end stage (0 skips)")
+    ap.add_argument("--vocos-runs", type=int, default=5, help="timed calls of the Vocos decoder (0 skips)")
     ap.add_argument("--no-queue", action="store_true", help="skip the batching-queue leg")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -577,6 +635,17 @@ def main():
     secs_all = sum_over_ranks(secs)
     value = secs_all / t_max
 
+    # Host cost of enqueueing, from an idle GPU: two device-buffer steps in a
+    # row. A call that waited for the stream would take a whole step here
+    # (the loop above also includes the launch queue's back-pressure once
+    # the host runs a few steps ahead).
+    torch.cuda.synchronize()
+    th0 = time.perf_counter()
+    step_device(0)
+    step_device(1)
+    enqueue_idle_ms = (time.perf_counter() - th0) * 1e3 / 2
+    torch.cuda.synchronize()
+
     # ---- end to end through the host-buffer C ABI (pinned host memory) ----
     e2e_value = None
     if not args.no_e2e:
@@ -628,6 +697,9 @@ def main():
     frontend = None
     if rank == 0 and args.frontend_runs > 0:
         frontend = bench_frontend(kb, W, local, args.frontend_runs)
+    vocos = None
+    if rank == 0 and args.vocos_runs > 0:
+        vocos = bench_vocos(kb, W, local, args.vocos_runs)
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
             sample = cpu_sample(pool)
@@ -675,11 +747,13 @@ def main():
         "cpu_baseline": cpu,
         "clocks": clk,
         "host_enqueue_ms_per_step": round(host_enqueue_ms, 2),
+        "host_enqueue_ms_from_idle": round(enqueue_idle_ms, 3),
         "gpu_launches": prof["launches"],
         "ttfa_p50_ms": ttfa,
         "lstm": lstm,
         "prosody": prosody,
         "frontend": frontend,
+        "vocos": vocos,
         "queue": queue,
         "parity_vs_c_library": parity,
         "pipeline_tflops": value / world * algorithmic_flop_per_asr_frame() * 40.0 / 1e12,
