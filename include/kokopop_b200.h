@@ -87,13 +87,19 @@ const char *kk_last_error(void);
  *   noise : per utterance [2 T_u]      (N curve)
  *   style : per utterance [128]        (decoder half of the voice row)
  *   audio : per utterance [600 T_u]    samples at 24 kHz, clamped to +-1
+ * Like the reference (all_finite, src/arch/kokoro/kokoro.cpp:91-99,
+ * :933-940), a non-finite f0, noise or asr value, decoder output or style
+ * value is KK_ERROR_INFERENCE with "non-finite Kokoro <name> value at index
+ * <i>" (the first such tensor in that order, its smallest index; inputs are
+ * indexed as passed). The context stays usable.
  */
 int kk_decoder_forward(kk_ctx *ctx, int32_t n_utts, const int32_t *n_frames,
                        const float *asr, const float *f0, const float *noise,
                        const float *style, float *audio);
 
 /* Same as kk_decoder_forward with device-resident inputs and output; the
- * lengths stay on the host. Asynchronous on `stream`. */
+ * lengths stay on the host. Asynchronous on `stream`; a non-finite value is
+ * reported by the next call of this context that synchronises. */
 int kk_decoder_forward_device(kk_ctx *ctx, int32_t n_utts, const int32_t *n_frames,
                               const float *asr, const float *f0,
                               const float *noise, const float *style,
@@ -397,6 +403,20 @@ int kk_profile_records(kk_ctx *ctx, kk_profile_record *out, size_t cap, size_t *
  * process, over all contexts and queues (no counterpart in the reference).
  * Lets a caller check that a path allocates nothing once warm. */
 int kk_allocation_count(uint64_t *out);
+
+/* ---- failure injection and self-tests (no counterpart in the reference) ----
+ * The next n device or pinned-host allocations of the library fail as out of
+ * memory (0 clears), so that a caller can test its handling of
+ * KK_ERROR_INFERENCE from a workspace that cannot grow. A call that fails
+ * this way leaves its context usable: the next call allocates again. */
+int kk_inject_allocation_failures(int32_t n);
+
+/* Runs the bounded wait of the tensor-core kernels on an mbarrier that
+ * nothing arrives at, for limit_us microseconds (at most 2 s), on the
+ * context's stream. Returns KK_ERROR_INFERENCE with the wait's code in
+ * kk_last_error(): the path a real expiry takes (the kernel gives up and
+ * returns, the host reports it); the context stays usable. */
+int kk_wait_selftest(kk_ctx *ctx, int64_t limit_us);
 
 #ifdef __cplusplus
 }

@@ -132,6 +132,8 @@ def load_library():
     L.kk_profile_enable.argtypes = [vp, ctypes.c_int]
     L.kk_profile_read.argtypes = [vp, ctypes.POINTER(Profile), ctypes.c_int]
     L.kk_allocation_count.argtypes = [ctypes.POINTER(ctypes.c_uint64)]
+    L.kk_inject_allocation_failures.argtypes = [ctypes.c_int32]
+    L.kk_wait_selftest.argtypes = [vp, ctypes.c_int64]
     L.kk_vocos_forward.argtypes = [vp, ctypes.c_char_p, ctypes.POINTER(VocosParams), ctypes.c_int32, _i32p, _f32p,
                                    _f32p, _f32p]
     L.kk_vocos_forward_device.argtypes = [vp, ctypes.c_char_p, ctypes.POINTER(VocosParams), ctypes.c_int32, _i32p,

@@ -1668,4 +1668,24 @@ cudaError_t conv_tc(const ConvTcArgs &a, cudaStream_t st) {
     return e;
 }
 
+// The bounded wait of the convolution kernels, made to run out: one thread
+// initialises an mbarrier that expects one arrival, which nothing makes, and
+// waits on it with mbar_wait. After limit_ns the wait records
+// kErrWaitSelftest in *err and returns false, and the kernel ends; the
+// context stays usable and the host reads the status as for a real expiry.
+__global__ void k_wait_selftest(int *err, unsigned long long limit_ns) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x != 0) return;
+    const uint32_t b = smem_u32(&bar);
+    mbar_init(b, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    mbar_wait(b, 0, err, kErrWaitSelftest, limit_ns);
+}
+
+cudaError_t wait_selftest(int *err, unsigned long long limit_ns, cudaStream_t st) {
+    if (limit_ns > TC_WAIT_NS) return cudaErrorInvalidValue;
+    k_wait_selftest<<<1, 32, 0, st>>>(err, limit_ns);
+    return cudaGetLastError();
+}
+
 }  // namespace kk

@@ -19,6 +19,7 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstdio>
+#include <cstddef>
 #include <cstring>
 #include <functional>
 #include <memory>
@@ -48,14 +49,24 @@ void check_cuda(cudaError_t e, const char *what) {
 }
 
 static std::atomic<uint64_t> g_allocations{0};
+static std::atomic<int32_t> g_fail_next{0};  // allocations still to fail (kk_inject_allocation_failures)
+
+static bool injected_failure() {
+    int32_t n = g_fail_next.load(std::memory_order_relaxed);
+    while (n > 0)
+        if (g_fail_next.compare_exchange_weak(n, n - 1, std::memory_order_relaxed)) return true;
+    return false;
+}
 
 cudaError_t device_malloc(void **p, size_t bytes) {
     g_allocations.fetch_add(1, std::memory_order_relaxed);
+    if (injected_failure()) return cudaErrorMemoryAllocation;
     return cudaMalloc(p, bytes);
 }
 
 cudaError_t pinned_malloc(void **p, size_t bytes) {
     g_allocations.fetch_add(1, std::memory_order_relaxed);
+    if (injected_failure()) return cudaErrorMemoryAllocation;
     return cudaMallocHost(p, bytes);
 }
 
@@ -165,6 +176,14 @@ float *kk_ctx::buf(const char *name, size_t floats) {
     DevBuf &b = ws[name];
     b.ensure(floats * sizeof(float));
     return (float *)b.p;
+}
+
+// The device status block: error word 0, no non-finite index recorded.
+void kk_ctx::reset_status() {
+    d_err.ensure(sizeof(DevStatus));
+    check_cuda(cudaMemset(d_err.p, 0, offsetof(DevStatus, first)), "clear status");
+    check_cuda(cudaMemset((char *)d_err.p + offsetof(DevStatus, first), 0xff, sizeof(DevStatus::first)),
+               "clear status");
 }
 
 // Waits for the timed launches' end events and turns them into records (and
@@ -595,8 +614,7 @@ void kk_ctx::derive() {
             }
         }
     }
-    d_err.ensure(sizeof(int));
-    check_cuda(cudaMemset(d_err.p, 0, sizeof(int)), "clear error");
+    reset_status();
     if (tc_mode) {
         check_cuda(conv_tc_init(), "tensor-core conv init");
         // F16 weights pack as they are; F32 ones split (split_mode)
@@ -1769,6 +1787,15 @@ struct Runner {
     void decoder_forward(const float *asr, const float *f0, const float *noise, const float *style, float *audio) {
         setup_batch();
         const int64_t R1 = R(1), R2 = R(2);
+        // all_finite on the inputs, in the reference's order (kokoro.cpp:933-940);
+        // indices are into the caller's arrays
+        DevStatus *status = (DevStatus *)c.d_err.p;
+        launch(KK_PROF_OTHER, 0.0, 4.0 * (516.0 * P.total), [&] {
+            check_finite(f0, 2 * P.total, kFiniteF0, status, st);
+            check_finite(noise, 2 * P.total, kFiniteNoise, status, st);
+            check_finite(asr, 512 * P.total, kFiniteAsr, status, st);
+        });
+        c.n_launches += 2;
         float *Xenc = c.buf("Xenc", 514 * (size_t)R1);
         float *Xdec = c.buf("Xdec", 1090 * (size_t)R1);
         float *f0p = c.buf("f0p", (size_t)R2);
@@ -1803,6 +1830,12 @@ struct Runner {
         for (int i = 0; i < 3; ++i) adain_resblk(d + "decode." + std::to_string(i), Xdec, 1090, false, Xdec);
         float *dec = c.buf("dec_out", 512 * (size_t)R2);
         adain_resblk(d + "decode.3", Xdec, 1090, true, dec);
+        // the decoder output (packed rows; gap rows are zero) and the style
+        launch(KK_PROF_OTHER, 0.0, 4.0 * (512.0 * R2 + 128.0 * P.n), [&] {
+            check_finite(dec, 512 * R2, kFiniteDecoder, status, st);
+            check_finite(style, (int64_t)kStyle * P.n, kFiniteStyle, status, st);
+        });
+        ++c.n_launches;
         check_cuda(cudaStreamWaitEvent(st, c.ev_src, 0), "wait source");
         generator(2, dec, har, audio);
     }
@@ -1956,17 +1989,27 @@ struct CallScope {
     CallScope &operator=(const CallScope &) = delete;
 };
 
-// After a synchronising call: surfaces a bounded-wait expiry recorded by the
-// tensor-core kernel (and clears it).
+// After a synchronising call: surfaces what the device status block
+// recorded since the last check (and clears it): a non-finite input or
+// intermediate (the reference's all_finite, kokoro.cpp:91-99, :933-940), a
+// token id out of range, or a bounded wait that ran out.
 void check_device_error(kk_ctx *ctx) {
     if (!ctx->d_err.p) return;
-    int e = 0;
-    check_cuda(cudaMemcpy(&e, ctx->d_err.p, sizeof e, cudaMemcpyDeviceToHost), "read device status");
-    if (e != 0) {
-        cudaMemset(ctx->d_err.p, 0, sizeof(int));
-        if (e == kErrTokenId) throw KKError(KK_ERROR_INVALID_ARGUMENT, "token id out of range (device input)");
-        throw KKError(KK_ERROR_INFERENCE, "tensor-core convolution timed out waiting (code " + std::to_string(e) + ")");
+    DevStatus s;
+    check_cuda(cudaMemcpy(&s, ctx->d_err.p, sizeof s, cudaMemcpyDeviceToHost), "read device status");
+    if (s.code == 0) return;
+    ctx->reset_status();
+    const int e = s.code;
+    if (e >= kErrNonFinite && e < kErrNonFinite + kFiniteLabels) {
+        static const char *labels[kFiniteLabels] = {"f0", "noise", "asr", "decoder", "decoder style"};
+        const int l = e - kErrNonFinite;
+        throw KKError(KK_ERROR_INFERENCE, std::string("non-finite Kokoro ") + labels[l] + " value at index " +
+                                              std::to_string(s.first[l]));
     }
+    if (e == kErrTokenId) throw KKError(KK_ERROR_INVALID_ARGUMENT, "token id out of range (device input)");
+    if (e == kErrWaitSelftest)
+        throw KKError(KK_ERROR_INFERENCE, "bounded wait ran out (self-test, code " + std::to_string(e) + ")");
+    throw KKError(KK_ERROR_INFERENCE, "tensor-core convolution timed out waiting (code " + std::to_string(e) + ")");
 }
 
 }  // namespace
@@ -2000,6 +2043,7 @@ int kk_ctx_create(int device, kk_ctx **out) {
         check_cuda(cudaEventCreateWithFlags(&c->ev_done, cudaEventDisableTiming), "event");
         for (auto &s : c->stage) check_cuda(cudaEventCreateWithFlags(&s.ev, cudaEventDisableTiming), "event");
         check_cuda(conv_simt_init(), "conv init");
+        c->reset_status();
         *out = c.release();
         return KK_OK;
     });
@@ -2911,6 +2955,28 @@ int kk_profile_records(kk_ctx *ctx, kk_profile_record *out, size_t cap, size_t *
         ctx->resolve_timed();
         *n = ctx->records.size();
         std::copy(ctx->records.begin(), ctx->records.begin() + std::min(cap, ctx->records.size()), out);
+        return KK_OK;
+    });
+}
+
+int kk_inject_allocation_failures(int32_t n) {
+    if (n < 0) {
+        g_last_error = "kk_inject_allocation_failures: negative count";
+        return KK_ERROR_INVALID_ARGUMENT;
+    }
+    g_fail_next.store(n, std::memory_order_relaxed);
+    return KK_OK;
+}
+
+int kk_wait_selftest(kk_ctx *ctx, int64_t limit_us) {
+    return guarded([&] {
+        if (!ctx || limit_us < 1 || limit_us > 2000000) throw KKError(KK_ERROR_INVALID_ARGUMENT, "bad argument");
+        use_device(ctx);
+        CallScope call_scope(*ctx, ctx->st);
+        check_cuda(wait_selftest((int *)ctx->d_err.p, (unsigned long long)limit_us * 1000ull, ctx->st),
+                   "wait self-test launch");
+        check_cuda(cudaStreamSynchronize(ctx->st), "wait self-test");
+        check_device_error(ctx);
         return KK_OK;
     });
 }

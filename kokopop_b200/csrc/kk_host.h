@@ -165,7 +165,8 @@ struct kk_ctx {
     bool fuse_operand = false;
     std::unordered_map<std::string, kk::PackedW> packed;
     std::unordered_map<std::string, kk::DevBuf> adain_t;  // fc weights transposed to [128][C]
-    kk::DevBuf d_err;  // device-side error code of the tensor-core kernel
+    kk::DevBuf d_err;  // device status block (kk::DevStatus): error word, non-finite indices
+    void reset_status();
     kk::SineArgs sine{};
     std::vector<kk::SiteInfo> sites;
     std::unordered_map<std::string, int> site_index;

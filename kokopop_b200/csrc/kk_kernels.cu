@@ -31,6 +31,24 @@ __global__ void k_scatter(const float *__restrict__ src, float *__restrict__ dst
         d[t] = s[t];
 }
 
+// all_finite (src/arch/kokoro/kokoro.cpp:91-99) on the device: the smallest
+// index of a non-finite value, and the error word if nothing set it before.
+__global__ void k_check_finite(const float *__restrict__ x, int64_t n, int label, DevStatus *status) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        if (!isfinite(x[i])) {
+            atomicMin(&status->first[label], (unsigned long long)i);
+            atomicCAS(&status->code, 0, kErrNonFinite + label);
+        }
+    }
+}
+
+void check_finite(const float *x, int64_t n, int label, DevStatus *status, cudaStream_t st) {
+    if (n <= 0) return;
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > 1184) blocks = 1184;  // 8 per SM
+    k_check_finite<<<(unsigned)blocks, 256, 0, st>>>(x, n, label, status);
+}
+
 void scatter(const float *src, float *dst, int64_t R, int C, int m, int extra, const Batch &b,
              const int64_t *cumT, int max_len, cudaStream_t st) {
     dim3 grid((unsigned)((max_len + 255) / 256 < 64 ? (max_len + 255) / 256 : 64), C, b.n);

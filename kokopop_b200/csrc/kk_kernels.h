@@ -221,6 +221,24 @@ void pool_up_h(const float *x, __half *y, int64_t R_in, int64_t Ry_out, int C, c
 // kk_frontend.cu: the text encoder's embedding and LayerNorm, the duration
 // projection.
 constexpr int kErrTokenId = 31;  // device error word: a token id out of range
+
+// The device status block of a context: the error word (0 = none; the first
+// error wins) and, per checked tensor, the smallest index of a non-finite
+// value (all bits set = none).
+enum { kFiniteF0 = 0, kFiniteNoise, kFiniteAsr, kFiniteDecoder, kFiniteStyle, kFiniteLabels };
+constexpr int kErrNonFinite = 60;  // + label
+struct DevStatus {
+    int code;
+    int pad;
+    unsigned long long first[kFiniteLabels];
+};
+// Records a non-finite value of x[0, n) (label's smallest index, and the
+// error word kErrNonFinite + label if it is still 0).
+void check_finite(const float *x, int64_t n, int label, DevStatus *status, cudaStream_t st);
+// A bounded wait on an mbarrier that nothing arrives at: after limit_ns the
+// waiting thread sets *err to kErrWaitSelftest (if 0) and the kernel returns.
+constexpr int kErrWaitSelftest = 77;
+cudaError_t wait_selftest(int *err, unsigned long long limit_ns, cudaStream_t st);
 // pos / type non-null (ALBERT): + the position row t and the token type row 0
 void embed(const float *emb, int C, int vocab, const int32_t *ids, const int64_t *cum, const Batch &b, float *X,
            int64_t R, int *err, cudaStream_t st, const float *pos = nullptr, const float *type = nullptr);

@@ -89,6 +89,13 @@ def test_front_end_and_queue_entry_points_reject_bad_arguments():
     n = ctypes.c_uint64(0)
     assert L.kk_allocation_count(ctypes.byref(n)) == kb.KK_OK
     assert L.kk_allocation_count(None) == E
+    # failure injection and the wait self-test validate before any CUDA call
+    assert L.kk_inject_allocation_failures(-1) == E
+    assert L.kk_inject_allocation_failures(0) == kb.KK_OK
+    assert L.kk_wait_selftest(None, 1000) == E
+    pv = kb.VocosParams.of(dict(dim=8, blocks=1, pw_hidden=8, dw_kernel=7, embed_kernel=7, noise_ch=4, mels=8,
+                                n_fft=64, hop=16, dc_pole=0.9, mag_clip=100.0))
+    assert L.kk_vocos_forward(None, b"p", ctypes.byref(pv), 1, ip, fp, fp, fp) == E
 
 
 def test_queue_rejects_out_of_range_chunks_and_limits():
