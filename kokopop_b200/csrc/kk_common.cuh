@@ -40,11 +40,12 @@ __device__ __forceinline__ float leaky(float x, float slope) {
 }
 
 // Exact GELU as ggml_vec_gelu_erf_f32 evaluates it, left to right:
-// (0.5f * x) * (1.0f + erff(x * SQRT_2_INV)), each operation rounded once,
-// with erf correctly rounded (from the double-precision erf).
+// (0.5f * x) * (1.0f + erff(x * SQRT_2_INV)), each operation rounded once.
+// erff is CUDA's single-precision erf (at most 2 ulp from the exact value,
+// like a C library's); the oracle takes it correctly rounded.
 __device__ __forceinline__ float gelu_erf(float x) {
     const float t = __fmul_rn(x, 0.70710678118654752440f);
-    const float e = __double2float_rn(erf((double)t));
+    const float e = erff(t);
     return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, e));
 }
 
