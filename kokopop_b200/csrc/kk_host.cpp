@@ -1741,13 +1741,17 @@ struct Runner {
         a.len = q.d_len;
         a.B = q.B;
         a.max_len = q.max_len;
-        // smallest group that keeps the clusters (2 per group) within one wave
+        a.err = (int *)c.d_err.p;
+        // smallest group that keeps the clusters (2 per group) within one
+        // wave of the device's co-resident clusters (16 when unknown)
         a.Bc = 32;
-        for (int bc : {1, 2, 4, 8, 16, 32})
-            if ((q.B + bc - 1) / bc <= 8) {
+        for (int bc : {1, 2, 4, 8, 16, 32}) {
+            const int fit = lstm_max_clusters(bc);
+            if (2 * ((q.B + bc - 1) / bc) <= (fit > 0 ? fit : 16)) {
                 a.Bc = bc;
                 break;
             }
+        }
         // per row and direction: the 4H pre-gates read, H outputs written,
         // 4H x H multiply-adds with W_hh (read from shared memory)
         const double rows = (double)q.rows, H = L.H;
@@ -2009,6 +2013,9 @@ void check_device_error(kk_ctx *ctx) {
     if (e == kErrTokenId) throw KKError(KK_ERROR_INVALID_ARGUMENT, "token id out of range (device input)");
     if (e == kErrWaitSelftest)
         throw KKError(KK_ERROR_INFERENCE, "bounded wait ran out (self-test, code " + std::to_string(e) + ")");
+    if (e == kErrLstmWait)
+        throw KKError(KK_ERROR_INFERENCE, "LSTM recurrence timed out waiting for a step's hidden state (code " +
+                                              std::to_string(e) + ")");
     throw KKError(KK_ERROR_INFERENCE, "tensor-core convolution timed out waiting (code " + std::to_string(e) + ")");
 }
 

@@ -238,6 +238,8 @@ void check_finite(const float *x, int64_t n, int label, DevStatus *status, cudaS
 // A bounded wait on an mbarrier that nothing arrives at: after limit_ns the
 // waiting thread sets *err to kErrWaitSelftest (if 0) and the kernel returns.
 constexpr int kErrWaitSelftest = 77;
+// The LSTM recurrence's wait for a step's hidden state ran out (1 s).
+constexpr int kErrLstmWait = 45;
 cudaError_t wait_selftest(int *err, unsigned long long limit_ns, cudaStream_t st);
 // pos / type non-null (ALBERT): + the position row t and the token type row 0
 void embed(const float *emb, int C, int vocab, const int32_t *ids, const int64_t *cum, const Batch &b, float *X,
@@ -304,8 +306,12 @@ struct LstmRecArgs {
     int B;                 // sequences
     int Bc;                // sequences per cluster: 1, 2, 4, 8, 16 or 32
     int max_len;           // max over len
+    int *err;              // device error word: set when a bounded wait runs out
 };
 size_t lstm_rec_smem(int Bc);
+// Clusters of the recurrence kernel for group size Bc that the current device
+// runs at once (cudaOccupancyMaxActiveClusters; cached per device), 0 if unknown.
+int lstm_max_clusters(int Bc);
 cudaError_t lstm_recurrence(const LstmRecArgs &a, cudaStream_t st);  // H = 256
 void lstm_pack(const float *x, int D, const float *style, int Ds, float *X, int64_t R, const int32_t *len,
                const int64_t *cum, int B, int max_len, cudaStream_t st);

@@ -10,14 +10,30 @@
 // Recurrence (cpu_lstm_contiguous, src/arch/kokoro/lstm_fused.cpp:200-247):
 // one thread-block cluster of 8 CTAs per (direction, group of Bc sequences).
 // CTA r of the cluster owns hidden units [32 r, 32 r + 32) and their four
-// gate rows of W_hh (128 rows x 256, F32, 128 KB) in shared memory for the
-// whole sequence. Per step every CTA computes its 128 gate rows for the
-// group's sequences, updates its 32 cells, and writes the new h values into
-// the h buffer of every CTA of the cluster (distributed shared memory); one
-// cluster barrier per step publishes them. The dot products keep the
-// reference's scalar order (k ascending, separate multiply and add), and the
-// gate sum is (b_hh + pre) + dot as in the reference.
+// gate rows of W_hh (128 rows x 256, F32, 130 KB padded) in shared memory
+// for the whole sequence. Local row lr = 4 u + q holds gate q (i, f, g, o) of
+// local unit u, so warp w owns units 4w .. 4w + 3 with all their gates.
+// Per step:
+//   * every CTA waits on its own mbarrier for the previous h of all 256
+//     units (the cluster's stores, below), bounded in time;
+//   * two threads per gate row each sum one half of the 256-term dot
+//     (fixed order: interleaved FMA partial sums, then their pairwise sum,
+//     then the two halves); the reference's AVX2 build reorders this sum
+//     too (lstm_fused.cpp:93-123), and the parity bound covers it;
+//   * the gate sum is (b_hh + pre) + dot as in the reference, the pre-gates
+//     having been loaded from global memory one step ahead; the gate's
+//     activation is applied by its own thread;
+//   * the warp's lanes update the cells of its 4 units (c stays in
+//     registers) after a __syncwarp, write h to global memory, and store it
+//     into the h buffer of every CTA of the cluster with st.async, each
+//     store completing bytes on the receiving CTA's mbarrier.
+// No block-wide or cluster-wide barrier runs inside the step loop: a CTA's
+// buffer for step s + 2 is written only after every CTA has sent its h for
+// step s + 1, which each sends after finishing its dot of step s + 1 that
+// read the other buffer, so the double buffer needs no further fence.
 #include "kk_kernels.h"
+
+#include <atomic>
 
 #include <cooperative_groups.h>
 
@@ -29,25 +45,68 @@ constexpr int kLstmH = 256;        // hidden units per direction
 constexpr int kLstmCl = 8;         // CTAs per cluster
 constexpr int kLstmUnits = 32;     // hidden units per CTA
 constexpr int kLstmRows = 128;     // gate rows per CTA (4 gates x 32 units)
-constexpr int kLstmThreads = 256;
+constexpr int kLstmThreads = 256;  // two threads per gate row
+constexpr int kLstmHalf = kLstmH / 2;    // terms of the dot per thread
+constexpr int kWStride = kLstmH + 8;     // W row stride in shared memory (floats): conflict-free 16-byte loads
+constexpr unsigned long long kLstmWaitNs = 1000000000ull;  // 1 s per wait, then kErrLstmWait
 
 size_t lstm_rec_smem(int Bc) {
-    return sizeof(float) * ((size_t)kLstmH * kLstmRows + 2 * (size_t)kLstmH * Bc + (size_t)kLstmRows * Bc +
-                            (size_t)kLstmUnits * Bc);
+    return sizeof(float) * ((size_t)kLstmRows * kWStride + 2 * (size_t)Bc * kLstmH + (size_t)kLstmRows * Bc);
 }
 
-// exp / tanh correctly rounded to float (through double)
-__device__ __forceinline__ float exp_cr(float x) { return (float)exp((double)x); }
-__device__ __forceinline__ float tanh_cr(float x) { return (float)tanh((double)x); }
-
-// lstm_fused.cpp:60-68: branch-stable logistic
+// lstm_fused.cpp:60-68: branch-stable logistic, with CUDA's single-precision
+// expf (the reference calls the C library's; both are within a few ulp)
 __device__ __forceinline__ float sigmoid_stable(float x) {
     if (x >= 0.0f) {
-        const float z = exp_cr(-x);
+        const float z = expf(-x);
         return __fdiv_rn(1.0f, __fadd_rn(1.0f, z));
     }
-    const float z = exp_cr(x);
+    const float z = expf(x);
     return __fdiv_rn(z, __fadd_rn(1.0f, z));
+}
+
+__device__ __forceinline__ uint32_t lstm_smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ uint64_t lstm_clock_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Waits for the phase of parity `parity` of the mbarrier at `bar`; false
+// after kLstmWaitNs.
+__device__ __forceinline__ bool lstm_wait(uint32_t bar, uint32_t parity) {
+    const uint64_t t0 = lstm_clock_ns();
+    while (true) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        if (ok) return true;
+        if (lstm_clock_ns() - t0 > kLstmWaitNs) return false;
+    }
+}
+
+// this CTA's shared address `local` as seen in the shared memory of CTA
+// `rank` of the cluster
+__device__ __forceinline__ uint32_t lstm_mapa(uint32_t local, int rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+    return r;
+}
+
+// 4-byte store into another CTA's shared memory that completes its bytes on
+// that CTA's mbarrier
+__device__ __forceinline__ void lstm_st_async(uint32_t remote, float v, uint32_t remote_bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(remote),
+                 "r"(__float_as_uint(v)), "r"(remote_bar)
+                 : "memory");
 }
 
 // non-finite -> 0, clamp to +-lim
@@ -56,143 +115,244 @@ __device__ __forceinline__ float sanitize(float x, float lim) {
     return fminf(fmaxf(x, -lim), lim);
 }
 
-template <int RPT, int SPT>
+// Pre-gates of step s for the sequences jj = part, part + 2, ... of the
+// group (the ones this thread adds into its gate values), 0 past a sequence.
+template <int BC>
+__device__ __forceinline__ void lstm_load_pre(float (&p)[(BC + 1) / 2], const float *pre, int64_t B, int b0,
+                                              const int *lens, int d, int s, int part) {
+#pragma unroll
+    for (int i = 0; i < (BC + 1) / 2; ++i) {
+        const int jj = 2 * i + part;
+        float v = 0.0f;
+        if (jj < BC) {
+            const int L = lens[jj];
+            if (s < L) {
+                const int t = d ? L - 1 - s : s;
+                v = pre[(int64_t)t * B + b0 + jj];
+            }
+        }
+        p[i] = v;
+    }
+}
+
+template <int BC>
 __global__ void __cluster_dims__(kLstmCl, 1, 1) __launch_bounds__(kLstmThreads, 1)
     k_lstm_rec(const LstmRecArgs a) {
+    constexpr int NA = BC >= 4 ? 1 : 4 / BC;  // interleaved partial sums per sequence
+    constexpr int NP = (4 * BC + 31) / 32;    // (unit, sequence) cells per lane
+    constexpr int NH = (BC + 1) / 2;          // sequences whose pre-gates a thread adds
+    constexpr uint32_t kBytes = (uint32_t)kLstmH * BC * 4;  // h of one step, all units
     cg::cluster_group cluster = cg::this_cluster();
     const int cr = (int)cluster.block_rank();
     const int cid = blockIdx.x / kLstmCl;
     const int d = cid & 1, grp = cid >> 1;
-    const int Bc = a.Bc;
-    const int b0 = grp * Bc;
+    const int b0 = grp * BC;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     extern __shared__ __align__(16) float sm[];
-    float *Wt = sm;                                  // [256 k][128 local rows]
-    float *hb = Wt + kLstmH * kLstmRows;             // [2][256][Bc]
-    float *gb = hb + 2 * kLstmH * Bc;                // [128][Bc]
-    float *cs = gb + kLstmRows * Bc;                 // [32][Bc]
+    float *W = sm;                          // [128 local rows][kWStride]
+    float *hb = W + kLstmRows * kWStride;   // [2][BC][256]: h of the previous step, double-buffered
+    float *gb = hb + 2 * BC * kLstmH;       // [128 local rows][BC]: activated gates
+    __shared__ __align__(8) uint64_t bar[2];
+    __shared__ int lens[BC];
     const float *whh = d ? a.whh[1] : a.whh[0];
     const float *bhh = d ? a.bhh[1] : a.bhh[0];
-    // local row lr = q * 32 + uu <-> gate row j = q * 256 + 32 cr + uu
-    for (int idx = threadIdx.x; idx < kLstmRows * kLstmH; idx += kLstmThreads) {
+    // local row lr = 4 u + q <-> gate row j = q * 256 + 32 cr + u, in natural
+    // k order; the two threads of a row take alternate 16-byte chunks, and
+    // the 264-float stride (8 banks apart) puts the 8 threads of each
+    // quarter-warp's 16-byte loads on 32 distinct banks
+    for (int idx = tid; idx < kLstmRows * kLstmH; idx += kLstmThreads) {
         const int lr = idx / kLstmH, k = idx % kLstmH;
-        const int j = (lr / kLstmUnits) * kLstmH + kLstmUnits * cr + (lr % kLstmUnits);
-        Wt[k * kLstmRows + lr] = whh[(int64_t)j * kLstmH + k];
+        const int j = (lr & 3) * kLstmH + kLstmUnits * cr + (lr >> 2);
+        W[lr * kWStride + k] = whh[(int64_t)j * kLstmH + k];
     }
-    for (int idx = threadIdx.x; idx < kLstmH * Bc; idx += kLstmThreads) hb[idx] = 0.0f;
-    for (int idx = threadIdx.x; idx < kLstmUnits * Bc; idx += kLstmThreads) cs[idx] = 0.0f;
-    cluster.sync();
+    for (int idx = tid; idx < BC * kLstmH; idx += kLstmThreads) hb[idx] = 0.0f;  // h(-1) = 0
+    if (tid < BC) lens[tid] = b0 + tid < a.B ? a.len[b0 + tid] : 0;
+    const uint32_t bar0 = lstm_smem_u32(&bar[0]);
+    if (tid == 0) {
+        // one arrival per phase (the expect below); the phase completes when
+        // all kBytes of a step's h have been stored by the cluster
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0) : "memory");
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0 + 8) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int b = 0; b < 2; ++b)
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar0 + 8 * b), "r"(kBytes)
+                         : "memory");
+    }
+    cluster.sync();  // every CTA's barriers are armed before any store reaches them
 
-    constexpr int NRB = kLstmRows / RPT;
-    const int rb = threadIdx.x % NRB, sb = threadIdx.x / NRB;
-    const bool active = sb * SPT < Bc;
-    int jg[RPT];
-    float bias[RPT];
+    const int lr = tid >> 1, part = tid & 1;  // gate row and dot half of this thread
+    const int q = lr & 3;
+    const int jrow = q * kLstmH + kLstmUnits * cr + (lr >> 2);
+    const float bias = bhh[jrow];
+    const float *pre = a.pre + ((int64_t)d * 4 * kLstmH + jrow) * a.R;
+    const float *wrow = W + lr * kWStride + 4 * part;
+    float pcur[NH], pnext[NH];
+    lstm_load_pre<BC>(pcur, pre, a.B, b0, lens, d, 0, part);
+    float c[NP];
 #pragma unroll
-    for (int i = 0; i < RPT; ++i) {
-        const int lr = rb * RPT + i;
-        jg[i] = (lr / kLstmUnits) * kLstmH + kLstmUnits * cr + (lr % kLstmUnits);
-        bias[i] = bhh[jg[i]];
-    }
-    int len[SPT];
-#pragma unroll
-    for (int jj = 0; jj < SPT; ++jj) {
-        const int b = b0 + sb * SPT + jj;
-        len[jj] = (active && b < a.B) ? a.len[b] : 0;
-    }
-    const float *pre = a.pre + (int64_t)d * 4 * kLstmH * a.R;
+    for (int j = 0; j < NP; ++j) c[j] = 0.0f;
 
+    bool ok = true;
     for (int s = 0; s < a.max_len; ++s) {
-        const float *hp = hb + (s & 1) * kLstmH * Bc;
-        float *hn = hb + ((s + 1) & 1) * kLstmH * Bc;
-        if (active) {
-            float pg[RPT][SPT];
-#pragma unroll
-            for (int jj = 0; jj < SPT; ++jj) {
-                const int b = b0 + sb * SPT + jj;
-                const bool live = s < len[jj];
-                const int t = d ? len[jj] - 1 - s : s;
-                const int64_t row = (int64_t)t * a.B + b;
-#pragma unroll
-                for (int i = 0; i < RPT; ++i) pg[i][jj] = live ? pre[(int64_t)jg[i] * a.R + row] : 0.0f;
+        const int cb = s & 1, nb = cb ^ 1;
+        if (s > 0) {
+            ok = __all_sync(0xffffffffu, lstm_wait(bar0 + 8 * cb, ((s - 1) >> 1) & 1));
+            if (!ok) {
+                if (lane == 0) atomicCAS(a.err, 0, kErrLstmWait);
+                break;
             }
-            float acc[RPT][SPT];
+            // the next phase of this buffer (step s + 2's h) can only start
+            // after this CTA has sent step s + 1's, later than this
+            if (tid == 0)
+                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar0 + 8 * cb),
+                             "r"(kBytes)
+                             : "memory");
+        }
+        // next step's pre-gates, a step ahead of their use
+        lstm_load_pre<BC>(pnext, pre, a.B, b0, lens, d, s + 1, part);
+        // dot products: this thread's 32 chunks of 4 terms (half of 256)
+        const float *hp = hb + cb * BC * kLstmH + 4 * part;
+        float acc[BC][NA];
 #pragma unroll
-            for (int i = 0; i < RPT; ++i)
+        for (int jj = 0; jj < BC; ++jj)
 #pragma unroll
-                for (int jj = 0; jj < SPT; ++jj) acc[i][jj] = 0.0f;
+            for (int i = 0; i < NA; ++i) acc[jj][i] = 0.0f;
 #pragma unroll 4
-            for (int k = 0; k < kLstmH; ++k) {
-                float w[RPT], h[SPT];
+        for (int ch = 0; ch < kLstmHalf / 4; ++ch) {
+            const float4 w4 = *reinterpret_cast<const float4 *>(wrow + 8 * ch);
 #pragma unroll
-                for (int i = 0; i < RPT; ++i) w[i] = Wt[k * kLstmRows + rb * RPT + i];
-#pragma unroll
-                for (int jj = 0; jj < SPT; ++jj) h[jj] = hp[k * Bc + sb * SPT + jj];
-#pragma unroll
-                for (int i = 0; i < RPT; ++i)
-#pragma unroll
-                    for (int jj = 0; jj < SPT; ++jj) acc[i][jj] = __fadd_rn(acc[i][jj], __fmul_rn(w[i], h[jj]));
+            for (int jj = 0; jj < BC; ++jj) {
+                const float4 h4 = *reinterpret_cast<const float4 *>(hp + jj * kLstmH + 8 * ch);
+                if (NA == 4) {
+                    acc[jj][0] = fmaf(w4.x, h4.x, acc[jj][0]);
+                    acc[jj][1 % NA] = fmaf(w4.y, h4.y, acc[jj][1 % NA]);
+                    acc[jj][2 % NA] = fmaf(w4.z, h4.z, acc[jj][2 % NA]);
+                    acc[jj][3 % NA] = fmaf(w4.w, h4.w, acc[jj][3 % NA]);
+                } else {
+                    acc[jj][0] = fmaf(w4.x, h4.x, acc[jj][0]);
+                    acc[jj][1 % NA] = fmaf(w4.y, h4.y, acc[jj][1 % NA]);
+                    acc[jj][0] = fmaf(w4.z, h4.z, acc[jj][0]);
+                    acc[jj][1 % NA] = fmaf(w4.w, h4.w, acc[jj][1 % NA]);
+                }
             }
-#pragma unroll
-            for (int i = 0; i < RPT; ++i)
-#pragma unroll
-                for (int jj = 0; jj < SPT; ++jj)
-                    gb[(rb * RPT + i) * Bc + sb * SPT + jj] = __fadd_rn(__fadd_rn(bias[i], pg[i][jj]), acc[i][jj]);
         }
-        __syncthreads();
-        // the four gate activations of every live cell, spread over the
-        // threads (in place: i, f, o logistic, g tanh)
-        for (int idx = threadIdx.x; idx < kLstmRows * Bc; idx += kLstmThreads) {
-            const int lr = idx / Bc, bl = idx % Bc, b = b0 + bl;
-            if (b >= a.B || s >= a.len[b]) continue;
-            const float x = sanitize(gb[idx], 80.0f);
-            gb[idx] = lr / kLstmUnits == 2 ? tanh_cr(x) : sigmoid_stable(x);
-        }
-        __syncthreads();
-        for (int idx = threadIdx.x; idx < kLstmUnits * Bc; idx += kLstmThreads) {
-            const int uu = idx / Bc, bl = idx % Bc, b = b0 + bl;
-            if (b >= a.B) continue;
-            const int L = a.len[b];
-            if (s >= L) continue;
-            const float ig = gb[(0 * kLstmUnits + uu) * Bc + bl];
-            const float fg = gb[(1 * kLstmUnits + uu) * Bc + bl];
-            const float gg = gb[(2 * kLstmUnits + uu) * Bc + bl];
-            const float og = gb[(3 * kLstmUnits + uu) * Bc + bl];
-            const float cn = sanitize(__fadd_rn(__fmul_rn(fg, cs[uu * Bc + bl]), __fmul_rn(ig, gg)), 50.0f);
-            cs[uu * Bc + bl] = cn;
-            float hv = __fmul_rn(og, tanh_cr(cn));
-            if (!isfinite(hv)) hv = 0.0f;
-            const int t = d ? L - 1 - s : s;
-            const int unit = kLstmUnits * cr + uu;
-            a.hout[(int64_t)(d * kLstmH + unit) * a.R + (int64_t)t * a.B + b] = hv;
-            float *dst = hn + unit * Bc + bl;
+        // gate values: the partial sums in a fixed order, the two halves
+        // (lower half first on both threads), then (b_hh + pre) + dot
 #pragma unroll
-            for (int r = 0; r < kLstmCl; ++r) *cluster.map_shared_rank(dst, r) = hv;
+        for (int jj = 0; jj < BC; ++jj) {
+            float sum = acc[jj][0];
+            if (NA == 2) sum = __fadd_rn(acc[jj][0], acc[jj][1 % NA]);
+            if (NA == 4) sum = __fadd_rn(__fadd_rn(acc[jj][0], acc[jj][1 % NA]), __fadd_rn(acc[jj][2 % NA], acc[jj][3 % NA]));
+            const float other = __shfl_xor_sync(0xffffffffu, sum, 1);
+            const float dot = part == 0 ? __fadd_rn(sum, other) : __fadd_rn(other, sum);
+            if ((jj & 1) == part) {
+                const float x = sanitize(__fadd_rn(__fadd_rn(bias, pcur[jj >> 1]), dot), 80.0f);
+                gb[lr * BC + jj] = q == 2 ? tanhf(x) : sigmoid_stable(x);
+            }
         }
-        cluster.sync();
+        __syncwarp();
+        // cells of the warp's 4 units: cell p = lane + 32 j is unit
+        // 4 warp + p / BC of sequence p % BC
+#pragma unroll
+        for (int j = 0; j < NP; ++j) {
+            const int p = lane + 32 * j;
+            if (p < 4 * BC) {
+                const int ul = 4 * warp + p / BC, jj = p % BC;
+                const float *g4 = gb + (4 * ul) * BC + jj;
+                const float ig = g4[0], fg = g4[BC], gg = g4[2 * BC], og = g4[3 * BC];
+                const int L = lens[jj];
+                const bool live = s < L;
+                const float cn = sanitize(__fadd_rn(__fmul_rn(fg, c[j]), __fmul_rn(ig, gg)), 50.0f);
+                float hv = __fmul_rn(og, tanhf(cn));
+                if (!isfinite(hv)) hv = 0.0f;
+                if (!live) hv = 0.0f;
+                else c[j] = cn;
+                const int unit = kLstmUnits * cr + ul;
+                if (live) {
+                    const int t = d ? L - 1 - s : s;
+                    a.hout[(int64_t)(d * kLstmH + unit) * a.R + (int64_t)t * a.B + b0 + jj] = hv;
+                }
+                // every CTA of the cluster, this one included, gets the value
+                const uint32_t dst = lstm_smem_u32(hb + nb * BC * kLstmH + jj * kLstmH + unit);
+#pragma unroll
+                for (int r = 0; r < kLstmCl; ++r) lstm_st_async(lstm_mapa(dst, r), hv, lstm_mapa(bar0 + 8 * nb, r));
+            }
+        }
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < NH; ++i) pcur[i] = pnext[i];
     }
+    // the last step's stores into this CTA complete before it leaves the
+    // cluster
+    if (ok) {
+        const int s = a.max_len;
+        if (!__all_sync(0xffffffffu, lstm_wait(bar0 + 8 * (s & 1), ((s - 1) >> 1) & 1)) && lane == 0)
+            atomicCAS(a.err, 0, kErrLstmWait);
+    }
+    cluster.sync();
 }
 
-template <int RPT, int SPT>
+template <int BC>
 static cudaError_t launch_rec(const LstmRecArgs &a, int n_clusters, cudaStream_t st) {
-    const size_t smem = lstm_rec_smem(a.Bc);
-    cudaError_t e = cudaFuncSetAttribute(k_lstm_rec<RPT, SPT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const size_t smem = lstm_rec_smem(BC);
+    cudaError_t e = cudaFuncSetAttribute(k_lstm_rec<BC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    k_lstm_rec<RPT, SPT><<<n_clusters * kLstmCl, kLstmThreads, smem, st>>>(a);
+    k_lstm_rec<BC><<<n_clusters * kLstmCl, kLstmThreads, smem, st>>>(a);
     return cudaGetLastError();
+}
+
+template <int BC>
+static int max_clusters_of() {
+    const size_t smem = lstm_rec_smem(BC);
+    if (cudaFuncSetAttribute(k_lstm_rec<BC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return 0;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(kLstmCl * 64);
+    cfg.blockDim = dim3(kLstmThreads);
+    cfg.dynamicSmemBytes = smem;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, k_lstm_rec<BC>, &cfg) != cudaSuccess) n = 0;
+    return n;
+}
+
+int lstm_max_clusters(int Bc) {
+    constexpr int kDev = 64;
+    static std::atomic<int> cache[kDev][6];  // 0 = not yet asked; -1 = query failed
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    const int i = Bc == 1 ? 0 : Bc == 2 ? 1 : Bc == 4 ? 2 : Bc == 8 ? 3 : Bc == 16 ? 4 : Bc == 32 ? 5 : -1;
+    if (i < 0) return 0;
+    if (dev >= 0 && dev < kDev) {
+        const int v = cache[dev][i].load(std::memory_order_relaxed);
+        if (v != 0) return v < 0 ? 0 : v;
+    }
+    int n = 0;
+    switch (Bc) {
+        case 1: n = max_clusters_of<1>(); break;
+        case 2: n = max_clusters_of<2>(); break;
+        case 4: n = max_clusters_of<4>(); break;
+        case 8: n = max_clusters_of<8>(); break;
+        case 16: n = max_clusters_of<16>(); break;
+        default: n = max_clusters_of<32>(); break;
+    }
+    cudaGetLastError();  // a failed query leaves no sticky error behind
+    if (dev >= 0 && dev < kDev) cache[dev][i].store(n > 0 ? n : -1, std::memory_order_relaxed);
+    return n;
 }
 
 cudaError_t lstm_recurrence(const LstmRecArgs &a, cudaStream_t st) {
     if (a.B < 1 || a.max_len < 1) return cudaSuccess;
-    if (!(a.Bc == 1 || a.Bc == 2 || a.Bc == 4 || a.Bc == 8 || a.Bc == 16 || a.Bc == 32)) return cudaErrorInvalidValue;
+    if (!a.err) return cudaErrorInvalidValue;
     const int groups = (a.B + a.Bc - 1) / a.Bc;
     const int n_clusters = 2 * groups;
     switch (a.Bc) {
-        case 1:
-        case 2: return launch_rec<1, 1>(a, n_clusters, st);
-        case 4: return launch_rec<2, 1>(a, n_clusters, st);
-        case 8: return launch_rec<4, 1>(a, n_clusters, st);
-        case 16: return launch_rec<4, 2>(a, n_clusters, st);
-        default: return launch_rec<4, 4>(a, n_clusters, st);
+        case 1: return launch_rec<1>(a, n_clusters, st);
+        case 2: return launch_rec<2>(a, n_clusters, st);
+        case 4: return launch_rec<4>(a, n_clusters, st);
+        case 8: return launch_rec<8>(a, n_clusters, st);
+        case 16: return launch_rec<16>(a, n_clusters, st);
+        case 32: return launch_rec<32>(a, n_clusters, st);
+        default: return cudaErrorInvalidValue;
     }
 }
 

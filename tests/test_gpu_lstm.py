@@ -1,13 +1,15 @@
 """GPU parity of the LSTM stack and the duration alignment, through the C ABI,
 against the oracle on the same seeded inputs.
 
-Tolerances: the recurrence keeps the reference's scalar dot order, but the
-input projection accumulates in a different order (tensor cores / CUDA-core
-tiles) and the GPU evaluates exp / tanh correctly rounded where the reference
-calls the C library's expf / tanhf, so h differs from the oracle in the last
-bits. The bound for one layer is 5e-6 max-abs on h in [-1, 1] (measured
-~5e-7; the reference's own fused-vs-scalar LSTM test allows 2e-5 on the
-recurrence alone, tests/test_lstm_fused.cpp:114-118); the duration encoder
+Tolerances: the recurrence sums its 256-term dots as two interleaved halves of
+fused multiply-adds (the reference's AVX2 build reorders this sum too,
+src/arch/kokoro/lstm_fused.cpp:93-123), the input projection accumulates in a
+different order (tensor cores / CUDA-core tiles), and the GPU's expf / tanhf
+are CUDA's (within a few ulp) where the oracle's are correctly rounded, so h
+differs from the oracle in the last bits. The bound for one layer is 5e-6
+max-abs on h in [-1, 1] (measured ~2e-6 over 512 steps; the reference's own
+fused-vs-scalar LSTM test allows 2e-5 on the recurrence alone,
+tests/test_lstm_fused.cpp:114-118); the duration encoder
 renormalises h three times (AdaLayerNorm divides by the per-step spread of
 h), so its bound is 1e-4 on outputs of order 1 (measured ~1e-5). With F16
 weights every layer input is rounded to half, so a last-bit difference can
