@@ -255,6 +255,9 @@ struct TcParams {
     const float *x_alpha;                // [IC] Snake alpha
     float nz;                            // -0.0f, opaque to the compiler (packed products)
     unsigned long long nz2;              // two packed -0.0f, the same
+    // k_convt_tc: channels per phase in one tile (the tile's MMA N is
+    // omul * phase_nc, its rows phase-major)
+    int phase_nc;
 };
 
 // Positions x channels, register epilogue (strided row maps). Persistent: CTA
@@ -1453,6 +1456,380 @@ __global__ void __launch_bounds__(TF_THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------
+// kernel, transposed convolution with row-contiguous output
+// ---------------------------------------------------------------------------
+//
+// ConvTranspose1d with stride S as S phase convolutions of 2 taps over the
+// input (phase r writes output rows S q + oadd + r), all S phases of NC
+// channels in one tile: D[q][r NC + c] = one M = 128 positions x N = S NC MMA
+// per 16-channel step, the activation slab as operand A and the phase-major
+// weight rows as operand B. The S phases of a position are adjacent output
+// rows, so an epilogue warp (32 positions, NC / 2 channels) holds, per
+// channel, the 32 S consecutive output rows [S q0 + oadd, S q0 + oadd + 32 S)
+// of its positions. The residual of those rows arrives by bulk copies (a
+// 16-byte aligned superset of the run) in a shared run buffer, the
+// accumulator and bias are added into it in row order, and the run is
+// written out as whole 128-byte stores, where the per-phase register
+// epilogue of k_conv_tc writes every S-th float (partial L2 sectors).
+//
+// With two taps the MMA work per tile is small and the tile pipeline sets
+// the pace: at batch 64 the stride-6 upsampler took 0.52 ms with no MMA and
+// no stores (operand copies and the epilogue's TMEM reads and run staging
+// alone), 0.79 ms complete. Where the weights of one channel group fit in
+// shared memory next to the slabs (stride 6: NC = 16, N = 96, 2 taps x 256
+// channels = 96 KB) they stay resident: the grid is a multiple of the
+// channel groups, so every tile of a CTA has the same group and only the
+// slabs stream. More epilogue warps (16: more runs in flight) took it from
+// 0.80 to 0.73 ms; an L2 prefetch of the residual two tiles ahead made it
+// slower (0.88 ms).
+//
+// Roles (64 + 32 EW threads): warp 0 lane 0 copies, warp 1 lane 0 issues the
+// MMAs into two accumulators of up to 256 columns, warps 2 .. EW + 1 run the
+// epilogue, EW / 4 of them per TMEM lane group (warp w: lanes 32 (w % 4) ..,
+// channel part (w - 2) / 4 of the tile).
+constexpr int CT_BM = 128;                          // positions per tile
+constexpr int CT_SLAB = 136;                        // slab rows: 128 + the taps' halo, rounded to 8
+constexpr int CT_A_BYTES = 8 * CT_SLAB * 16;        // 17 KB
+
+// One instance: S phases, NC channels per phase in a tile (MMA N = S NC), G
+// channels per epilogue pass, NRB run buffers per epilogue warp (2: the next
+// pass's residual lands while this one is written out; 1: after it), RES:
+// resident weights (at most CT_RES_TILES (tap, 64-channel block) tiles),
+// else NSW streamed weight stages; EW epilogue warps.
+constexpr int CT_RES_TILES = 8;
+template <int S_, int NC_, int G_, int NRB_, bool RES_, int NSA_, int NSW_, int EW_>
+struct CtCfg {
+    static constexpr int S = S_, NC = NC_, G = G_, NRB = NRB_, NSA = NSA_, NSW = NSW_, EW = EW_;
+    static constexpr bool RES = RES_;
+    static constexpr int N = S * NC;
+    static constexpr int NCW = NC / (EW / 4);  // channels of one epilogue warp
+    static constexpr int THREADS = 64 + 32 * EW;
+    static constexpr int BX = 32 * S + 4;  // rows of a run buffer: a run and its 16-byte alignment
+    static constexpr int RUN = G * BX;     // floats per run buffer
+    static constexpr int W_TILE = N * 128;
+    static constexpr int W_SLOTS = RES ? CT_RES_TILES : NSW;
+    static constexpr int SMEM = NSA * CT_A_BYTES + W_SLOTS * W_TILE + EW * NRB * RUN * 4 + 1024 /*barriers*/ +
+                                1024 /*align*/;
+    static_assert(S % 2 == 0 && G * S <= 48 && EW % 4 == 0 && NC % (EW / 4) == 0 && NCW % G == 0 && N % 16 == 0 &&
+                      N <= 256,
+                  "shape");
+    static_assert(SMEM <= 227 * 1024, "shared memory");
+};
+using CtCfg6 = CtCfg<6, 16, 4, 1, true, 3, 0, 16>;    // stride 6, weights resident: N = 96
+using CtCfg6s = CtCfg<6, 16, 4, 2, false, 2, 4, 16>;   // stride 6, streamed (split F32: 3x the blocks)
+using CtCfg10 = CtCfg<10, 16, 4, 2, false, 2, 4, 8>;  // stride 10 (256 x 512 weights): N = 160, streamed
+
+// tcgen05.ld 32x32b of N consecutive columns, without the wait
+template <int N>
+__device__ __forceinline__ void tmem_ld_nowait(uint32_t taddr, float (&r)[N]);
+template <>
+__device__ __forceinline__ void tmem_ld_nowait<4>(uint32_t taddr, float (&r)[4]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(r[0]), "=f"(r[1]), "=f"(r[2]), "=f"(r[3])
+                 : "r"(taddr));
+}
+template <>
+__device__ __forceinline__ void tmem_ld_nowait<8>(uint32_t taddr, float (&r)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=f"(r[0]), "=f"(r[1]), "=f"(r[2]), "=f"(r[3]), "=f"(r[4]), "=f"(r[5]), "=f"(r[6]), "=f"(r[7])
+                 : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+template <class C>
+__global__ void __launch_bounds__(C::THREADS, 1) k_convt_tc(const __grid_constant__ TcParams P) {
+    constexpr int S = C::S, NC = C::NC, N = C::N, G = C::G, BX = C::BX, NRB = C::NRB;
+    constexpr int NSA = C::NSA, NWB = C::RES ? 1 : C::NSW;  // weight barriers
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t *sA = smem;
+    uint8_t *sW = sA + NSA * CT_A_BYTES;
+    float *sE = (float *)(sW + C::W_SLOTS * C::W_TILE);
+    uint64_t *bars = (uint64_t *)(sE + C::EW * NRB * C::RUN);
+    // A_full[NSA] A_empty[NSA] W_full[NWB] W_empty[NWB] acc_full[2] acc_empty[2] drain
+    // res[EW warps][NRB] tmem-slot
+    const uint32_t bA_full = smem_u32(bars), bA_empty = smem_u32(bars + NSA);
+    const uint32_t bW_full = smem_u32(bars + 2 * NSA), bW_empty = smem_u32(bars + 2 * NSA + NWB);
+    const uint32_t bAcc_full = smem_u32(bars + 2 * NSA + 2 * NWB);
+    const uint32_t bAcc_empty = smem_u32(bars + 2 * NSA + 2 * NWB + 2);
+    const uint32_t bDrain = smem_u32(bars + 2 * NSA + 2 * NWB + 4);
+    const uint32_t bRes = smem_u32(bars + 2 * NSA + 2 * NWB + 5);
+    uint32_t *tmem_slot = (uint32_t *)(bars + 2 * NSA + 2 * NWB + 5 + NRB * C::EW);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t n_tiles_total = P.m_tiles * P.n_oc_tiles;
+    const int n_wt = P.K * P.IC_blocks;  // weight tiles of a channel group
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < NSA; ++i) {
+            mbar_init(bA_full + 8 * i, 1);
+            mbar_init(bA_empty + 8 * i, 1);
+        }
+        for (int i = 0; i < NWB; ++i) {
+            mbar_init(bW_full + 8 * i, 1);
+            mbar_init(bW_empty + 8 * i, 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(bAcc_full + 8 * i, 1);
+            mbar_init(bAcc_empty + 8 * i, C::EW);
+        }
+        mbar_init(bDrain, 1);
+        for (int i = 0; i < NRB * C::EW; ++i) mbar_init(bRes + 8 * i, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TC_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+
+    constexpr uint32_t lbo_a = (uint32_t)CT_SLAB * 16u;  // slab chunk stride
+    constexpr uint32_t lbo_w = (uint32_t)N * 16u;        // weight chunk stride
+    constexpr uint32_t w_bytes = (uint32_t)C::W_TILE;    // one weight tile
+    // packed weight tile (tap k, block b) of channel group nt
+    auto w_src = [&](int k, int b, int nt) {
+        return P.w + (((size_t)k * P.IC_blocks + b) * P.n_tiles + nt) * (size_t)N * 64;
+    };
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // producer
+            bool ok = true;
+            uint32_t ia = 0, iw = 0;
+            if (C::RES && (int64_t)blockIdx.x < n_tiles_total) {
+                // every tile of this CTA has channel group blockIdx.x % n_oc_tiles
+                const int nt = (int)(blockIdx.x % P.n_oc_tiles);
+                mbar_expect_tx(bW_full, w_bytes * (uint32_t)n_wt);
+                for (int b = 0; b < P.IC_blocks; ++b)
+                    for (int k = 0; k < P.K; ++k)
+                        bulk_load(smem_u32(sW + (b * P.K + k) * C::W_TILE), w_src(k, b, nt), w_bytes, bW_full);
+                iw = 1;
+            }
+            for (int64_t tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x) {
+                const int64_t mt = tile / P.n_oc_tiles;
+                const int nt = (int)(tile % P.n_oc_tiles);
+                const int64_t row0 = mt * CT_BM - P.p;  // >= -kHalfLo (checked on the host)
+                for (int b = 0; b < P.IC_blocks && ok; ++b, ++ia) {
+                    const int sa = ia % NSA;
+                    if (ia >= NSA) ok = mbar_wait(bA_empty + 8 * sa, ((ia / NSA) & 1) ^ 1, P.err, 11);
+                    if (!ok) break;
+                    mbar_expect_tx(bA_full + 8 * sa, CT_A_BYTES);
+                    const uint32_t dst = smem_u32(sA + sa * CT_A_BYTES);
+                    const int bo = (P.a_wrap > 0 && b >= P.a_wrap) ? b - P.a_wrap : b;
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        const __half *src = P.a + ((int64_t)(8 * bo + c) * P.R_a + row0) * 8;
+                        bulk_load(dst + (uint32_t)c * lbo_a, src, lbo_a, bA_full + 8 * sa);
+                    }
+                    if (!C::RES) {
+                        for (int k = 0; k < P.K; ++k, ++iw) {
+                            const int sw = iw % NWB;
+                            if (iw >= NWB) ok = mbar_wait(bW_empty + 8 * sw, ((iw / NWB) & 1) ^ 1, P.err, 12);
+                            if (!ok) break;
+                            mbar_expect_tx(bW_full + 8 * sw, w_bytes);
+                            bulk_load(smem_u32(sW + sw * C::W_TILE), w_src(k, b, nt), w_bytes, bW_full + 8 * sw);
+                        }
+                    }
+                }
+            }
+            for (uint32_t i = (ia > NSA ? ia - NSA : 0); i < ia; ++i)
+                mbar_wait(bA_full + 8 * (i % NSA), (i / NSA) & 1, P.err, 18, TC_DRAIN_NS);
+            for (uint32_t i = (iw > NWB ? iw - NWB : 0); i < iw; ++i)
+                mbar_wait(bW_full + 8 * (i % NWB), (i / NWB) & 1, P.err, 18, TC_DRAIN_NS);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // MMA issuer: A = activations (M = 128 positions), B = weights (N = S NC phase rows)
+            const uint32_t idesc = idesc_f16(CT_BM, N);
+            bool ok = true;
+            uint32_t ia = 0, iw = 0, it = 0;
+            if (C::RES && (int64_t)blockIdx.x < n_tiles_total) ok = mbar_wait(bW_full, 0, P.err, 14);
+            for (int64_t tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x, ++it) {
+                const int ab = it & 1;
+                if (it >= 2) ok = mbar_wait(bAcc_empty + 8 * ab, ((it >> 1) & 1) ^ 1, P.err, 17);
+                if (!ok) break;
+                fence_after_sync();
+                const uint32_t d_tmem = tmem + (uint32_t)(ab * 256);
+                for (int b = 0; b < P.IC_blocks && ok; ++b, ++ia) {
+                    const int sa = ia % NSA;
+                    ok = mbar_wait(bA_full + 8 * sa, (ia / NSA) & 1, P.err, 13);
+                    if (!ok) break;
+                    fence_after_sync();
+                    const uint32_t a_base = smem_u32(sA + sa * CT_A_BYTES);
+                    for (int k = 0; k < P.K; ++k) {
+                        uint32_t w_base;
+                        int sw = 0;
+                        if (C::RES) {
+                            w_base = smem_u32(sW + (b * P.K + k) * C::W_TILE);
+                        } else {
+                            sw = iw % NWB;
+                            ok = mbar_wait(bW_full + 8 * sw, (iw / NWB) & 1, P.err, 14);
+                            if (!ok) break;
+                            fence_after_sync();
+                            w_base = smem_u32(sW + sw * C::W_TILE);
+                        }
+                        const uint32_t a_tap = a_base + (uint32_t)(k * P.d) * 16u;
+#pragma unroll
+                        for (int ks = 0; ks < 4; ++ks) {
+                            const uint64_t ad = sdesc(a_tap + (uint32_t)(2 * ks) * lbo_a, lbo_a, 128);
+                            const uint64_t wd = sdesc(w_base + (uint32_t)(2 * ks) * lbo_w, lbo_w, 128);
+                            mma_f16(d_tmem, ad, wd, idesc, (b > 0 || k > 0 || ks > 0) ? 1u : 0u);
+                        }
+                        if (!C::RES) {
+                            mma_commit(bW_empty + 8 * sw);
+                            ++iw;
+                        }
+                    }
+                    mma_commit(bA_empty + 8 * sa);
+                }
+                if (ok) mma_commit(bAcc_full + 8 * ab);
+            }
+            mma_commit(bDrain);
+            mbar_wait(bDrain, 0, P.err, 19, TC_DRAIN_NS);
+        }
+        __syncwarp();
+    } else {
+        // epilogue warps 2 .. EW + 1
+        const int lg = warp & 3;            // TMEM lane group: positions 32 lg .. of the tile
+        const int hsel = (warp - 2) >> 2;   // channel part of the tile
+        constexpr int ncw = C::NCW;         // channels of this warp
+        constexpr int n_pass = ncw / G;
+        const int ew = warp - 2;
+        // NRB run buffers [G][BX]; a run of 32 S output rows starts d0 < 4
+        // floats into its buffer, at the 16-byte boundary below it. Item n
+        // (a tile's pass) uses buffer n % NRB.
+        float *runs = sE + ew * NRB * C::RUN;
+        const uint32_t bR = bRes + 8 * NRB * ew;  // their barriers
+        const bool has_res = P.resid != nullptr;
+        // lane 0: the residual of item (tile, pass g) into buffer s: channels
+        // c_lo + g G + j, rows [x0, x0 + BX) clipped to [0, R_resid) (the
+        // clipped rows are no output rows of the run), one bulk copy each
+        uint32_t n_issued = 0;
+        auto fetch = [&](int64_t tile, int g, int s) {
+            const int64_t mt = tile / P.n_oc_tiles;
+            const int nt = (int)(tile % P.n_oc_tiles);
+            const int64_t x0 = ((mt * CT_BM + 32 * lg) * S + P.oadd) & ~(int64_t)3;
+            const int64_t lo = x0 > 0 ? x0 : 0;
+            const int64_t hi = x0 + BX < P.R_resid ? x0 + BX : P.R_resid;
+            const uint32_t bytes = hi > lo ? (uint32_t)(hi - lo) * 4u : 0u;
+            fence_proxy_async();  // this buffer's earlier reads and writes come first
+            mbar_expect_tx(bR + 8 * s, bytes * G);
+            if (bytes) {
+                const int c0 = nt * NC + hsel * ncw + g * G;
+                const uint32_t dst = smem_u32(runs + s * C::RUN + (lo - x0));
+                for (int j = 0; j < G; ++j)
+                    bulk_load(dst + (uint32_t)(j * BX * 4), P.resid + (int64_t)(c0 + j) * P.R_resid + lo, bytes,
+                              bR + 8 * s);
+            }
+            ++n_issued;
+        };
+        // lane 0: the residual of the item after (tile, g) into buffer s
+        auto fetch_next = [&](int64_t tile, int g, int s) {
+            if (g + 1 < n_pass)
+                fetch(tile, g + 1, s);
+            else if (tile + gridDim.x < n_tiles_total)
+                fetch(tile + gridDim.x, 0, s);
+        };
+        if (has_res && lane == 0 && (int64_t)blockIdx.x < n_tiles_total) fetch(blockIdx.x, 0, 0);
+        uint32_t it = 0, n = 0;  // tiles and items (tile, pass) done
+        bool stop = false;
+        for (int64_t tile = blockIdx.x; tile < n_tiles_total && !stop; tile += gridDim.x, ++it) {
+            const int64_t mt = tile / P.n_oc_tiles;
+            const int nt = (int)(tile % P.n_oc_tiles);
+            const int ab = it & 1;
+            const int64_t pw = mt * CT_BM + 32 * lg;  // first position of this warp
+            const int64_t orow0 = pw * S + P.oadd;    // its first output row
+            const int d0 = (int)(orow0 - (orow0 & ~(int64_t)3));
+            const int c_lo = nt * NC + hsel * ncw;    // its first output channel
+            int ok_lane = 0;
+            if (lane == 0) ok_lane = mbar_wait(bAcc_full + 8 * ab, (it >> 1) & 1, P.err, 15) ? 1 : 0;
+            if (__shfl_sync(0xffffffffu, ok_lane, 0) == 0) break;
+            __syncwarp();
+            fence_after_sync();
+            // row lane + 32 k of the run: position pw + (lane + 32 k) / S, phase (lane + 32 k) % S
+            bool row_ok[S];
+#pragma unroll
+            for (int k = 0; k < S; ++k) {
+                const int i = lane + 32 * k;
+                const int64_t o = orow0 + i;
+                row_ok[k] = pw + i / S < P.n_pos && o >= 0 && o < P.R_out;
+            }
+            const uint32_t t_base = tmem + ((uint32_t)(32 * lg) << 16) + (uint32_t)(ab * 256 + hsel * ncw);
+            for (int g = 0; g < n_pass; ++g, ++n) {
+                const int s = (int)(n % NRB);
+                float *run = runs + s * C::RUN + d0;
+                // with two buffers, the next item's residual into the other
+                // one (its reads ended at the previous item's last __syncwarp)
+                if (NRB == 2 && has_res && lane == 0) fetch_next(tile, g, s ^ 1);
+                float v[S][G];  // v[r][j] = D[position pw + lane][phase r, channel c_lo + g G + j]
+#pragma unroll
+                for (int r = 0; r < S; ++r) tmem_ld_nowait<G>(t_base + (uint32_t)(r * NC + g * G), v[r]);
+                tmem_ld_wait();
+                if (g == n_pass - 1) {
+                    // the tile's accumulator values are all in registers: hand it back
+                    fence_before_sync();
+                    __syncwarp();
+                    if (lane == 0)
+                        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bAcc_empty + 8 * ab) : "memory");
+                }
+                // every lane waits: each reader needs its own acquire of the
+                // bytes the copies wrote
+                if (has_res && !__all_sync(0xffffffffu, mbar_wait(bR + 8 * s, (n / NRB) & 1, P.err, 20))) {
+                    stop = true;
+                    break;
+                }
+                // accumulator (+ bias) into the run, row S lane + r of channel
+                // j: residual + value, or the value alone
+#pragma unroll
+                for (int j = 0; j < G; ++j) {
+                    const float bj = P.bias ? __ldg(P.bias + c_lo + g * G + j) : 0.f;
+                    float *rj = run + j * BX + S * lane;
+#pragma unroll
+                    for (int r = 0; r < S; ++r) {
+                        float x = v[r][j];
+                        if (P.acc_scale != 1.0f) x = __fmul_rn(x, P.acc_scale);
+                        if (P.bias) x = __fadd_rn(x, bj);
+                        rj[r] = has_res ? __fadd_rn(rj[r], x) : x;
+                    }
+                }
+                __syncwarp();
+                // whole 128-byte runs of each channel's output row
+#pragma unroll
+                for (int j = 0; j < G; ++j) {
+                    float *op = P.out + (int64_t)(c_lo + g * G + j) * P.R_out + orow0 + lane;
+                    const float *rj = run + j * BX + lane;
+#pragma unroll
+                    for (int k = 0; k < S; ++k)
+                        if (row_ok[k]) op[32 * k] = rj[32 * k];
+                }
+                __syncwarp();  // the run is read before this buffer's next copy or write
+                // with one buffer, the next item's residual into it now
+                if (NRB == 1 && has_res && lane == 0) fetch_next(tile, g, s);
+            }
+        }
+        // a copy issued for an item that never ran (a wait that ran out) lands
+        // before the CTA ends
+        if (has_res && lane == 0)
+            for (uint32_t i = n; i < n_issued; ++i)
+                mbar_wait(bR + 8 * (i % NRB), (i / NRB) & 1, P.err, 18, TC_DRAIN_NS);
+    }
+
+    fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        fence_after_sync();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS)
+                     : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 
@@ -1481,10 +1858,85 @@ cudaError_t conv_tc_init() {
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(k_conv_tcf, cudaFuncAttributeMaxDynamicSharedMemorySize, TF_SMEM);
     if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(k_convt_tc<CtCfg6>, cudaFuncAttributeMaxDynamicSharedMemorySize, CtCfg6::SMEM);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(k_convt_tc<CtCfg6s>, cudaFuncAttributeMaxDynamicSharedMemorySize, CtCfg6s::SMEM);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(k_convt_tc<CtCfg10>, cudaFuncAttributeMaxDynamicSharedMemorySize, CtCfg10::SMEM);
+    if (e != cudaSuccess) return e;
     return cudaFuncSetAttribute(k_conv_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
 }
 
 int conv_tc_max_halo() { return TC_SLAB - TC_BM; }
+
+// The instances of k_convt_tc: 16 channels per phase in a tile for strides 6
+// (N = 96) and 10 (N = 160).
+int convt_phase_nc(int S, int OC) {
+    const int nc = (S == 6 || S == 10) ? 16 : 0;
+    return nc > 0 && OC % nc == 0 ? nc : 0;
+}
+
+template <class C>
+static void launch_convt(const TcParams &P, int64_t tiles, cudaStream_t st) {
+    const int64_t slots = g_num_sms > 0 ? g_num_sms : 148;
+    int64_t grid = tiles < slots ? tiles : slots;
+    // resident weights: a grid of whole channel-group rounds keeps every tile
+    // of a CTA in one group (tiles is a multiple of n_oc_tiles)
+    if (C::RES) grid = grid / P.n_oc_tiles * P.n_oc_tiles;
+    k_convt_tc<C><<<(unsigned)grid, C::THREADS, C::SMEM, st>>>(P);
+}
+
+// k_convt_tc launch (ConvTcArgs::phase_nc > 0).
+static cudaError_t conv_tc_transposed(const ConvTcArgs &a, cudaStream_t st) {
+    const int S = (int)a.omul, NC = a.phase_nc;
+    if (NC != convt_phase_nc(S, a.OC) || a.n_tiles != a.OC / NC || a.K < 1 || a.d < 1 || a.p < 0 ||
+        a.p > kHalfLo || (a.K - 1) * a.d > CT_SLAB - CT_BM || a.IC_pad % 64 != 0 || a.n_pos < 1 ||
+        a.R_in < half_stride(0) || a.a_wrap < 0 || a.a_wrap >= a.IC_pad / 64 || a.phase_oc != 0 || a.resid_half ||
+        a.accum || a.scale1 != 1.0f || a.scale2 != 1.0f || a.chscale || a.stats || a.x)
+        return cudaErrorInvalidValue;
+    // the residual arrives by bulk copies of 16-byte aligned row runs
+    if (a.resid && (a.R_resid < a.R_out || a.R_resid % 4 != 0 || ((uintptr_t)a.resid & 15)))
+        return cudaErrorInvalidValue;
+    TcParams P;
+    memset(&P, 0, sizeof(P));
+    P.IC_blocks = a.IC_pad / 64;
+    P.K = a.K;
+    P.p = a.p;
+    P.d = a.d;
+    P.OC = a.OC;
+    P.n_tiles = a.n_tiles;
+    P.n_oc_tiles = a.n_tiles;
+    P.mma_n = S * NC;
+    P.phase_nc = NC;
+    P.m_tiles = (a.n_pos + CT_BM - 1) / CT_BM;
+    // the last slab stays inside the operand's chunk (rows < R + kHalfHi)
+    const int64_t rows = a.R_in - kHalfLo - kHalfHi;
+    if (a.n_pos > rows || (P.m_tiles - 1) * CT_BM - a.p + CT_SLAB > rows + kHalfHi) return cudaErrorInvalidValue;
+    P.a = a.in;
+    P.R_a = a.R_in;
+    P.a_wrap = a.a_wrap;
+    P.acc_scale = a.acc_scale == 0.0f ? 1.0f : a.acc_scale;
+    P.w = a.w;
+    P.out = a.out;
+    P.R_out = a.R_out;
+    P.n_pos = a.n_pos;
+    P.omul = a.omul;
+    P.oadd = a.oadd;
+    P.bias = a.bias;
+    P.resid = a.resid;
+    P.R_resid = a.R_resid;
+    P.scale1 = 1.0f;
+    P.scale2 = 1.0f;
+    P.err = a.err;
+    const int64_t tiles = P.m_tiles * P.n_oc_tiles;
+    if (S == 6 && a.K * P.IC_blocks <= CT_RES_TILES && P.n_oc_tiles <= (g_num_sms > 0 ? g_num_sms : 148))
+        launch_convt<CtCfg6>(P, tiles, st);
+    else if (S == 6)
+        launch_convt<CtCfg6s>(P, tiles, st);
+    else
+        launch_convt<CtCfg10>(P, tiles, st);
+    return cudaGetLastError();
+}
 
 // 2-D map of an F32 [C][R] tensor in 32 x 32 boxes (x = position, y =
 // channel) with the 128-byte swizzle of the channel-major staging.
@@ -1582,12 +2034,14 @@ static cudaError_t conv_tc_fused(const ConvTcArgs &a, cudaStream_t st) {
 
 cudaError_t conv_tc(const ConvTcArgs &a, cudaStream_t st) {
     if (a.x) return conv_tc_fused(a, st);
+    if (a.phase_nc > 0) return conv_tc_transposed(a, st);
     const int halo = (a.K - 1) * a.d;
     if (a.K < 1 || a.d < 1 || a.p < 0 || halo > TC_SLAB - TC_BM || a.p > kHalfLo || a.IC_pad % 64 != 0 ||
         a.OC > a.n_tiles * TC_BN || a.n_pos < 1 || a.R_in < half_stride(0) || a.a_wrap < 0 ||
         a.a_wrap >= a.IC_pad / 64)
         return cudaErrorInvalidValue;
     TcParams P;
+    memset(&P, 0, sizeof(P));
     P.IC_blocks = a.IC_pad / 64;
     P.K = a.K;
     P.p = a.p;

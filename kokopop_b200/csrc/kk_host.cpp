@@ -339,23 +339,25 @@ static std::vector<std::string> text_convs() {
 }
 
 // Packs a convolution weight W[oc, ic, k] (via `get`) into the tensor-core
-// kernel's shared-memory images: half [K][IC_pad/64][n_tiles][8][128][8],
-// zero in the channel padding. The values are F16 already, so the
-// conversion is exact.
+// kernel's shared-memory images: half [K][IC_pad/64][n_tiles][8][tile_n][8]
+// (tiles of tile_n output rows, 128 unless a kernel asks otherwise), zero in
+// the channel padding. The values are F16 already, so the conversion is
+// exact.
 template <typename Get>
-static void pack_tc(PackedW &pw, int OC, int IC, int K, Get get) {
+static void pack_tc(PackedW &pw, int OC, int IC, int K, Get get, int tile_n = 128) {
     pw.IC = IC;
     pw.OC = OC;
     pw.K = K;
     pw.IC_pad = (IC + 63) / 64 * 64;
-    pw.n_tiles = (OC + 127) / 128;
+    pw.n_tiles = (OC + tile_n - 1) / tile_n;
     const int NB = pw.IC_pad / 64;
-    std::vector<__half> h((size_t)K * NB * pw.n_tiles * 8 * 128 * 8, __float2half_rn(0.f));
+    std::vector<__half> h((size_t)K * NB * pw.n_tiles * 8 * tile_n * 8, __float2half_rn(0.f));
     for (int k = 0; k < K; ++k)
         for (int oc = 0; oc < OC; ++oc)
             for (int ic = 0; ic < IC; ++ic) {
-                const int b = ic / 64, c = (ic % 64) / 8, e = ic % 8, nt = oc / 128, n = oc % 128;
-                const size_t idx = ((((size_t)k * NB + b) * pw.n_tiles + nt) * 8 + c) * (128 * 8) + (size_t)n * 8 + e;
+                const int b = ic / 64, c = (ic % 64) / 8, e = ic % 8, nt = oc / tile_n, n = oc % tile_n;
+                const size_t idx =
+                    ((((size_t)k * NB + b) * pw.n_tiles + nt) * 8 + c) * ((size_t)tile_n * 8) + (size_t)n * 8 + e;
                 h[idx] = __float2half_rn(get(oc, ic, k));
             }
     pw.buf.ensure(h.size() * sizeof(__half));
@@ -374,7 +376,7 @@ static void pack_tc(PackedW &pw, int OC, int IC, int K, Get get) {
 // its coarser absolute spacing, only for |w| below 2^-3 of the largest),
 // and the conv takes acc_scale = 2^-s back, exactly.
 template <typename Get>
-static void pack_tc_split(PackedW &pw, int OC, int IC, int K, Get get) {
+static void pack_tc_split(PackedW &pw, int OC, int IC, int K, Get get, int tile_n = 128) {
     const int ICp = (IC + 63) / 64 * 64;
     float amax = 0.f;
     for (int k = 0; k < K; ++k)
@@ -393,7 +395,7 @@ static void pack_tc_split(PackedW &pw, int OC, int IC, int K, Get get) {
         const float w = get(oc, ic, k) * up;
         const float hi = __half2float(__float2half_rn(w));
         return part > 0 ? hi : __half2float(__float2half_rn(w - hi));
-    });
+    }, tile_n);
     pw.IC = IC;
     pw.a_wrap = 2 * ICp / 64;
     pw.acc_scale = std::ldexp(1.0f, -s);
@@ -503,6 +505,10 @@ void kk_ctx::derive() {
     {
         const char *f = std::getenv("KOKOPOP_B200_FUSED_OPERAND");
         fuse_operand = f && f[0] == '1';
+        // the ConvTranspose as phase-major 128-channel tiles on k_conv_tc
+        // (every S-th output row per store) instead of k_convt_tc
+        const char *g = std::getenv("KOKOPOP_B200_CONVT_PHASES");
+        convt_phases = g && g[0] == '1';
     }
     // the prosody chain's convolutions on the tensor cores when they are all
     // F16, whatever the rest of the weight set
@@ -618,11 +624,12 @@ void kk_ctx::derive() {
     if (tc_mode) {
         check_cuda(conv_tc_init(), "tensor-core conv init");
         // F16 weights pack as they are; F32 ones split (split_mode)
-        auto pack = [&](PackedW &pw, int OC, int IC, int K, const std::function<float(int, int, int)> &get) {
+        auto pack = [&](PackedW &pw, int OC, int IC, int K, const std::function<float(int, int, int)> &get,
+                        int tile_n = 128) {
             if (split_mode)
-                pack_tc_split(pw, OC, IC, K, get);
+                pack_tc_split(pw, OC, IC, K, get, tile_n);
             else
-                pack_tc(pw, OC, IC, K, get);
+                pack_tc(pw, OC, IC, K, get, tile_n);
         };
         std::vector<float> h;
         std::vector<std::pair<std::string, int>> convs = tc_convs();
@@ -664,7 +671,19 @@ void kk_ctx::derive() {
             const DevTensor &t = W("kokopop.decoder.generator.ups." + std::to_string(s) + ".weight");
             const int OC = (int)t.ne[1], IC = (int)t.ne[2], S = strides[s];
             const std::vector<float> &ph = phase_host[s];
-            if (OC % 128 == 0) {
+            const int NC = convt_phase_nc(S, OC);
+            if (NC > 0 && !convt_phases) {
+                // k_convt_tc: tile nt holds the S phases of channels
+                // [nt NC, nt NC + NC), row n = r NC + c (phase r, channel c)
+                const int N = S * NC;
+                pack(
+                    packed["ups." + std::to_string(s) + ".inter"], OC / NC * N, IC, 2,
+                    [&](int v, int ic, int k) {
+                        const int nt = v / N, r = (v % N) / NC, oc = nt * NC + (v % N) % NC;
+                        return ph[(((size_t)r * OC + oc) * IC + ic) * 2 + k];
+                    },
+                    N);
+            } else if (OC % 128 == 0) {
                 // all phases as one convolution, phase-major output channels
                 // n = r * OC + oc, so the CTAs writing the interleaved rows of
                 // one position tile run together
@@ -1230,11 +1249,12 @@ struct Runner {
 
     // Tensor-core convolution on a half chunk-major operand.
     void conv_h(const PackedW &pw, const Op &in, int K, int p, int d, float *out, int64_t R_out, int64_t n_pos,
-                const Epi &e, int phase_oc = 0) {
+                const Epi &e, int phase_oc = 0, int phase_nc = 0) {
         if (in.split != (pw.a_wrap > 0))
             throw KKError(KK_ERROR_INFERENCE, "operand and weight packing disagree on the F32 split");
         ConvTcArgs a{};
         a.phase_oc = phase_oc;
+        a.phase_nc = phase_nc;
         a.in = in.h;
         a.R_in = in.Ry;
         a.IC_pad = pw.IC_pad;
@@ -1242,7 +1262,8 @@ struct Runner {
         a.acc_scale = pw.acc_scale;
         a.w = (const __half *)pw.buf.p;
         a.n_tiles = pw.n_tiles;
-        a.OC = pw.OC;
+        // phase-interleaved packing: pw.OC counts the rows of all phases
+        a.OC = phase_nc > 0 ? pw.OC / (int)e.omul : pw.OC;
         a.K = K;
         a.p = p;
         a.d = d;
@@ -1625,7 +1646,8 @@ struct Runner {
             const DevTensor &ub = c.W(g + "ups." + ss + ".bias");
             if ((int)uw.ne[1] != Cs || (int)uw.ne[2] != C) throw KKError(KK_ERROR_MODEL, "ups shape mismatch");
             const int S = sp[s].up_stride, crop = sp[s].up_padding, pad = s == 1 ? 1 : 0;
-            auto all_phases = c.packed.find("ups." + ss + ".phases");
+            auto inter = c.packed.find("ups." + ss + ".inter");
+            auto all_phases = inter != c.packed.end() ? inter : c.packed.find("ups." + ss + ".phases");
             if (tc && all_phases != c.packed.end()) {
                 Epi e;
                 e.bias = &ub;
@@ -1634,7 +1656,10 @@ struct Runner {
                 e.omul = S;
                 e.oadd = -crop + pad;
                 e.valid = sum_len(m_prev, 0);
-                conv_h(all_phases->second, op_prev, 2, 1, 1, xst, Rm, Rp, e, Cs);
+                if (inter != c.packed.end())
+                    conv_h(inter->second, op_prev, 2, 1, 1, xst, Rm, Rp, e, 0, convt_phase_nc(S, Cs));
+                else
+                    conv_h(all_phases->second, op_prev, 2, 1, 1, xst, Rm, Rp, e, Cs);
             }
             for (int r = 0; r < S && !(tc && all_phases != c.packed.end()); ++r) {
                 Epi e;

@@ -178,6 +178,12 @@ struct ConvTcArgs {
     // > 0: the weights are phase-packed (OC = phases x phase_oc, phase-major);
     // channel n writes channel n % phase_oc at rows q * omul + oadd + n / phase_oc
     int phase_oc;
+    // > 0: a transposed convolution with stride omul on k_convt_tc. The
+    // weights are packed in tiles of omul * phase_nc rows (phase r, channel c
+    // at row r * phase_nc + c; OC real channels per phase), and channel c of
+    // phase r at input position q writes output row q * omul + oadd + r.
+    // Epilogue: bias and residual only.
+    int phase_nc;
     // non-null: the instance-norm terms (mean, scale) of the output over each
     // utterance's valid rows at level (sm, sextra) of batch sb, into
     // stats[u * OC + c]. With stats_aligned (every utterance of the level
@@ -203,6 +209,9 @@ cudaError_t conv_tc_init();
 cudaError_t conv_tc(const ConvTcArgs &a, cudaStream_t st);
 bool conv_tc_fusable(const ConvTcArgs &a);
 int conv_tc_max_halo();
+// Channels per phase of k_convt_tc's tiles for stride S and OC channels per
+// phase (0: no instance of the kernel serves this shape).
+int convt_phase_nc(int S, int OC);
 
 // prologue_h: y[c/8][row][c%8] = half(act(adain(x[c][row]))) on valid rows
 // (x is F32 [C][R]; y a half operand of chunk stride Ry).

@@ -142,6 +142,28 @@ def test_fused_operand_equals_separate_pass(ctx, w16, monkeypatch):
     assert runs["1"][1] <= runs["0"][1] - 48
 
 
+@pytest.mark.parametrize("wname", ["w16", "w32"])
+def test_convt_row_runs_equal_phase_tiles(ctx, wname, request, monkeypatch):
+    """The ConvTranspose upsamplers on k_convt_tc (all stride phases of a
+    channel group in one tile, output written in whole row runs) equal the
+    phase-tile path of k_conv_tc (KOKOPOP_B200_CONVT_PHASES=1) bit for bit,
+    F16 weights and split F32 alike: the same products summed in the same
+    order, the same epilogue operations."""
+    w = request.getfixturevalue(wname)
+    rng = np.random.default_rng(12)
+    utts = [W.make_utterance(rng, t) for t in (37, 5, 90, 1, 64)]
+    runs = {}
+    for flag in ("1", "0"):
+        monkeypatch.setenv("KOKOPOP_B200_CONVT_PHASES", flag)
+        ctx.upload(w)
+        runs[flag] = ctx.decoder_forward(utts)
+    monkeypatch.delenv("KOKOPOP_B200_CONVT_PHASES")
+    ctx.upload(w)
+    for a, b in zip(runs["1"], runs["0"]):
+        print(f"{wname}: max abs diff {float(np.abs(a - b).max()):.3g}")
+        np.testing.assert_array_equal(a, b)
+
+
 def test_unvoiced_everywhere(ctx, w32, o32):
     ctx.upload(w32)
     u = W.make_utterance(np.random.default_rng(4), 6)
