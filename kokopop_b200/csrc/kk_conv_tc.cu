@@ -845,7 +845,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     float v[32];
                     if (chan_ok && p0 < P.n_pos) {
                         float *op = P.out + (int64_t)c * P.R_out + p0;
-                        const float *rp = has_res ? P.resid + (int64_t)c * P.R_resid + p0 : nullptr;
+                        // resid_half: the nearest x2 upsample of the residual,
+                        // row p / 2 (p0 is even)
+                        const int rs = P.resid_half ? 1 : 0;
+                        const float *rp = has_res ? P.resid + (int64_t)c * P.R_resid + (p0 >> rs) : nullptr;
 #pragma unroll
                         for (int j = 0; j < 32; ++j) {
                             float x = 0.f;
@@ -853,7 +856,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                                 x = __uint_as_float(r[j]);
                                 if (P.acc_scale != 1.0f) x = __fmul_rn(x, P.acc_scale);
                                 if (P.bias) x = __fadd_rn(x, bias);
-                                if (has_res) x = __fadd_rn(rp[j], x);
+                                if (has_res) x = __fadd_rn(rp[j >> rs], x);
                                 if (P.chscale) x = __fmul_rn(x, chs);
                                 if (P.scale1 != 1.0f) x = __fmul_rn(x, P.scale1);
                                 if (P.accum) x = __fadd_rn(op[j], x);
@@ -2087,13 +2090,16 @@ cudaError_t conv_tc(const ConvTcArgs &a, cudaStream_t st) {
     const int64_t slots = g_num_sms > 0 ? g_num_sms : 148;
     const unsigned grid = (unsigned)(tiles < slots ? tiles : slots);
     // channels x positions kernel where output row = position
-    if (a.omul == 1 && a.oadd == 0 && a.phase_oc == 0 && !a.resid_half && a.OC >= 64 && a.n_pos <= a.R_out &&
-        (!a.resid || a.R_resid >= a.n_pos)) {
+    // (a residual upsampled x2 by resid_half only on the unstaged epilogue;
+    // its rows up to n_pos / 2 exist)
+    if (a.omul == 1 && a.oadd == 0 && a.phase_oc == 0 && a.OC >= 64 && a.n_pos <= a.R_out &&
+        (!a.resid || (a.resid_half ? 2 * a.R_resid >= a.n_pos : a.R_resid >= a.n_pos))) {
         CUtensorMap omap, rmap;
         memset(&omap, 0, sizeof(omap));
         memset(&rmap, 0, sizeof(rmap));
         // staged blocks where every position of the level is written
-        const bool staged = g_encode && a.n_pos == a.R_out && a.R_out % 32 == 0 && (!a.resid || a.R_resid == a.R_out) &&
+        const bool staged = g_encode && !a.resid_half && a.n_pos == a.R_out && a.R_out % 32 == 0 &&
+                            (!a.resid || a.R_resid == a.R_out) &&
                             block_map_swz(&omap, a.out, a.R_out, a.OC) &&
                             block_map_swz(&rmap, a.resid ? a.resid : a.out, a.R_out, a.OC);
         // block partials where every position is written and the utterances

@@ -1422,18 +1422,33 @@ struct Runner {
                 throw KKError(KK_ERROR_MODEL, "invalid depthwise upsample pool shape: " + pf);
             // the pool reads F32 activations (the reference's dense F32 kernel)
             const int64_t R1 = R(1), R2 = R(2);
-            Op pf32;
-            pf32.f = c.buf("pfT", 1090 * (size_t)R1);
-            pf32.R = R1;
-            adain_act(pf + ".norm1", x, pf32, R1, Cin, 1, 0, ACT_LEAKY, 0.2f, "");
-            // reads the frame level once, writes the doubled level
             const double el = (double)Cin * (double)sum_len(1, 0);
-            launch(KK_PROF_OTHER, 0.0, el * (4.0 + 2.0 * (tc ? (opL.split ? 4.0 : 2.0) : 4.0)), [&] {
-                if (tc)
-                    pool_up_h(pf32.f, opL.h, R1, opL.Ry, Cin, pw.d, pb.d, B, P.maxT, opL.lo(Cin), st);
-                else
-                    pool_up(pf32.f, opL.f, R1, R2, Cin, pw.d, pb.d, B, P.maxT, 0, st);
-            });
+            if (tc) {
+                // AdaIN + LeakyReLU applied by the pool as it reads x: reads
+                // the frame level once, writes the doubled level
+                const AdainSite &s = site(pf + ".norm1");
+                if (s.C != Cin) throw KKError(KK_ERROR_MODEL, "AdaIN channel mismatch: " + pf + ".norm1");
+                stats_pass(x, R1, Cin, 1, 0, ms);
+                PrologueArgs a{};
+                a.norm = 1;
+                a.ms = ms;
+                a.norm_w = c.W(pf + ".norm1.norm.weight").d;
+                a.norm_b = c.W(pf + ".norm1.norm.bias").d;
+                a.gamma = s.gamma;
+                a.beta = s.beta;
+                a.act = ACT_LEAKY;
+                a.slope = 0.2f;
+                launch(KK_PROF_OPERAND, 0.0, el * (4.0 + 2.0 * (opL.split ? 4.0 : 2.0)), [&] {
+                    pool_up_adain_h(x, opL.h, R1, opL.Ry, Cin, pw.d, pb.d, B, P.maxT, opL.lo(Cin), a, st);
+                });
+            } else {
+                Op pf32;
+                pf32.f = c.buf("pfT", 1090 * (size_t)R1);
+                pf32.R = R1;
+                adain_act(pf + ".norm1", x, pf32, R1, Cin, 1, 0, ACT_LEAKY, 0.2f, "");
+                launch(KK_PROF_OTHER, 0.0, el * (4.0 + 2.0 * 4.0),
+                       [&] { pool_up(pf32.f, opL.f, R1, R2, Cin, pw.d, pb.d, B, P.maxT, 0, st); });
+            }
         } else {
             adain_act(pf + ".norm1", x, opI, Ri, Cin, mi, 0, ACT_LEAKY, 0.2f, "");
         }

@@ -151,9 +151,35 @@ __global__ void __launch_bounds__(256) k_stats(const float *__restrict__ x, int6
     if (threadIdx.x == 0) ms[(int64_t)u * C + c] = norm_from_sums(s1, s2, len);
 }
 
+// One warp per (channel, utterance), for the decoder levels (m <= 2) where an
+// utterance has a few hundred to ~1600 rows and a block per pair would wait
+// on its barriers: lane l sums rows l, l + 32, ... in double, then the lanes
+// combine in a fixed butterfly. The order depends only on the length, never
+// on the rest of the batch.
+__global__ void __launch_bounds__(256) k_stats_w(const float *__restrict__ x, int64_t R, int C, int m, int extra,
+                                                 Batch b, float2 *__restrict__ ms) {
+    const int c = blockIdx.x * 8 + (threadIdx.x >> 5), u = blockIdx.y, lane = threadIdx.x & 31;
+    if (c >= C) return;  // the whole warp
+    const int64_t len = (int64_t)m * b.T[u] + extra;
+    const float *p = x + (int64_t)c * R + (int64_t)m * b.offT[u];
+    double s1 = 0.0, s2 = 0.0;
+#pragma unroll 4
+    for (int64_t t = lane; t < len; t += 32) {
+        const double v = (double)p[t];
+        s1 += v;
+        s2 += v * v;
+    }
+    s1 = warp_sum(s1);
+    s2 = warp_sum(s2);
+    if (lane == 0) ms[(int64_t)u * C + c] = norm_from_sums(s1, s2, len);
+}
+
 void stats(const float *x, int64_t R, int C, int m, int extra, const Batch &b, float2 *ms,
            cudaStream_t st) {
-    k_stats<<<dim3(C, b.n), 256, 0, st>>>(x, R, C, m, extra, b, ms);
+    if (m <= 2)
+        k_stats_w<<<dim3((C + 7) / 8, b.n), 256, 0, st>>>(x, R, C, m, extra, b, ms);
+    else
+        k_stats<<<dim3(C, b.n), 256, 0, st>>>(x, R, C, m, extra, b, ms);
 }
 
 // The same terms from 32-row block partials part[c * NB + row / 32] = (S, M2)
@@ -340,7 +366,8 @@ __global__ void __launch_bounds__(256, SPLIT ? 2 : 3) k_prologue_h(const float *
         }
     }
     const int nc = C - ch * 8 < 8 ? C - ch * 8 : 8;
-    for (int64_t t = (blockIdx.x * 256 + threadIdx.x) * 4; t < len; t += (int64_t)gridDim.x * 256 * 4) {
+    for (int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4; t < len;
+         t += (int64_t)gridDim.x * blockDim.x * 4) {
         const int64_t row = row0 + t;
         float4 v4[8];
 #pragma unroll
@@ -436,38 +463,42 @@ __global__ void __launch_bounds__(256, SPLIT ? 2 : 3) k_prologue_h(const float *
 }
 
 template <bool SPLIT>
-static void prologue_h_launch(dim3 grid, const float *x, __half *y, int64_t R, int64_t Ry, int C, int m, int extra,
-                              const Batch &b, const PrologueArgs &a, cudaStream_t st) {
+static void prologue_h_launch(dim3 grid, int nt, const float *x, __half *y, int64_t R, int64_t Ry, int C, int m,
+                              int extra, const Batch &b, const PrologueArgs &a, cudaStream_t st) {
     if (a.norm) {
         if (a.act == ACT_SNAKE)
-            k_prologue_h<true, ACT_SNAKE, SPLIT><<<grid, 256, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
+            k_prologue_h<true, ACT_SNAKE, SPLIT><<<grid, nt, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
         else if (a.act == ACT_LEAKY)
-            k_prologue_h<true, ACT_LEAKY, SPLIT><<<grid, 256, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
+            k_prologue_h<true, ACT_LEAKY, SPLIT><<<grid, nt, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
         else
-            k_prologue_h<true, ACT_NONE, SPLIT><<<grid, 256, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
+            k_prologue_h<true, ACT_NONE, SPLIT><<<grid, nt, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
     } else {
         if (a.act == ACT_SNAKE)
-            k_prologue_h<false, ACT_SNAKE, SPLIT><<<grid, 256, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
+            k_prologue_h<false, ACT_SNAKE, SPLIT><<<grid, nt, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
         else if (a.act == ACT_LEAKY)
-            k_prologue_h<false, ACT_LEAKY, SPLIT><<<grid, 256, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
+            k_prologue_h<false, ACT_LEAKY, SPLIT><<<grid, nt, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
         else if (a.act == ACT_GELU)
-            k_prologue_h<false, ACT_GELU, SPLIT><<<grid, 256, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
+            k_prologue_h<false, ACT_GELU, SPLIT><<<grid, nt, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
         else
-            k_prologue_h<false, ACT_NONE, SPLIT><<<grid, 256, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
+            k_prologue_h<false, ACT_NONE, SPLIT><<<grid, nt, 0, st>>>(x, y, R, Ry, C, m, extra, b, a);
     }
 }
 
 void prologue_h(const float *x, __half *y, int64_t R, int64_t Ry, int C, int m, int extra, const Batch &b,
                 int mean_len, const PrologueArgs &a, cudaStream_t st) {
-    // about three 1024-row passes per thread over an utterance of the mean
-    // length, so the per-channel set-up of a thread is spread over several
-    int bx = (mean_len + 3 * 1024 - 1) / (3 * 1024);
+    // about three passes per thread over an utterance of the mean length, so
+    // the per-channel set-up of a thread is spread over several; blocks of
+    // 64 threads (256 rows a pass) where utterances are short (the decoder
+    // levels), else 256 (1024 rows)
+    const int nt = mean_len < 2048 ? 64 : 256;
+    int bx = (mean_len + 3 * 4 * nt - 1) / (3 * 4 * nt);
     if (bx > 64) bx = 64;
+    if (bx < 1) bx = 1;
     const dim3 grid(bx, (C + 7) / 8, b.n);
     if (a.lo_off > 0)
-        prologue_h_launch<true>(grid, x, y, R, Ry, C, m, extra, b, a, st);
+        prologue_h_launch<true>(grid, nt, x, y, R, Ry, C, m, extra, b, a, st);
     else
-        prologue_h_launch<false>(grid, x, y, R, Ry, C, m, extra, b, a, st);
+        prologue_h_launch<false>(grid, nt, x, y, R, Ry, C, m, extra, b, a, st);
 }
 
 // Depthwise x2 pool (see k_pool_up) written as the half chunk-major operand
@@ -511,6 +542,102 @@ void pool_up_h(const float *x, __half *y, int64_t R_in, int64_t Ry_out, int C, c
     int bx = (2 * max_T + 255) / 256;
     if (bx > 16) bx = 16;
     k_pool_up_h<<<dim3(bx, (C + 7) / 8, b.n), 256, 0, st>>>(x, y, R_in, Ry_out, C, w, bias, b, lo_off);
+}
+
+// The same pool of LeakyReLU(AdaIN(x)): the AdaIN + LeakyReLU of k_prologue
+// (the same operations and roundings) applied to each input value as it is
+// read, in place of a separate F32 pass over the frame level. A thread takes
+// input rows q0 .. q0 + 3 of 8 channels (one float4 each, plus row q0 + 4)
+// and writes the output rows 2 q0 .. 2 q0 + 7 they produce: 128 contiguous
+// bytes of the half chunk-major operand. Input row q gives output row 2 q
+// (w1 x[q]) and 2 q + 1 (w2 x[q], then + w0 x[q + 1] when q + 1 < T), each
+// summed from +0 in that order and + bias, as in k_pool_up_h.
+__global__ void __launch_bounds__(64) k_pool_up_adain_h(const float *__restrict__ x, __half *__restrict__ y,
+                                                        int64_t R_in, int64_t Ry_out, int C,
+                                                        const float *__restrict__ w, const float *__restrict__ bias,
+                                                        Batch b, int64_t lo_off, PrologueArgs a) {
+    const int u = blockIdx.z, ch = blockIdx.y;
+    const int64_t L = b.T[u];
+    const int64_t off = b.offT[u];  // a multiple of 4
+    float mean[8], scale[8], nw[8], nb[8], g[8], be[8], w0[8], w1[8], w2[8], bs[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        const int c = ch * 8 + e;
+        mean[e] = 0.f, scale[e] = 1.f, nw[e] = 1.f, nb[e] = 0.f, g[e] = 0.f, be[e] = 0.f;
+        w0[e] = w1[e] = w2[e] = bs[e] = 0.f;
+        if (c >= C) continue;
+        const float2 s = a.ms[(int64_t)u * C + c];
+        mean[e] = s.x;
+        scale[e] = s.y;
+        nw[e] = a.norm_w[c];
+        nb[e] = a.norm_b[c];
+        g[e] = a.gamma[(int64_t)u * C + c];
+        be[e] = a.beta[(int64_t)u * C + c];
+        w0[e] = w[c * 3 + 0];
+        w1[e] = w[c * 3 + 1];
+        w2[e] = w[c * 3 + 2];
+        bs[e] = bias[c];
+    }
+    const int nc = C - ch * 8 < 8 ? C - ch * 8 : 8;
+    auto act = [&](float v, int e) {
+        v = __fmul_rn(__fsub_rn(v, mean[e]), scale[e]);
+        v = __fadd_rn(__fmul_rn(v, nw[e]), nb[e]);
+        v = __fadd_rn(v, __fmul_rn(v, g[e]));
+        v = __fadd_rn(v, be[e]);
+        return leaky(v, a.slope);
+    };
+    for (int64_t q0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4; q0 < L;
+         q0 += (int64_t)gridDim.x * blockDim.x * 4) {
+        float av[5][8];  // activations of input rows q0 .. q0 + 4 (0 past T, never used)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            if (e < nc) {
+                const float *xp = x + (int64_t)(ch * 8 + e) * R_in + off + q0;
+                const float4 v = *reinterpret_cast<const float4 *>(xp);
+                av[0][e] = act(v.x, e), av[1][e] = act(v.y, e), av[2][e] = act(v.z, e), av[3][e] = act(v.w, e);
+                av[4][e] = q0 + 4 < L ? act(xp[4], e) : 0.f;
+            } else {
+#pragma unroll
+                for (int i = 0; i < 5; ++i) av[i][e] = 0.f;
+            }
+        }
+        __half *dst = y + ((int64_t)ch * Ry_out + 2 * off + 2 * q0) * 8;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            if (q0 + i >= L) break;
+            __align__(16) __half h0[8], l0[8], h1[8], l1[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                float v0 = 0.f, v1 = 0.f;
+                if (e < nc) {
+                    v0 = __fadd_rn(__fadd_rn(0.f, __fmul_rn(w1[e], av[i][e])), bs[e]);
+                    float acc = __fadd_rn(0.f, __fmul_rn(w2[e], av[i][e]));
+                    if (q0 + i + 1 < L) acc = __fadd_rn(acc, __fmul_rn(w0[e], av[i + 1][e]));
+                    v1 = __fadd_rn(acc, bs[e]);
+                }
+                h0[e] = __float2half_rn(v0);
+                l0[e] = split_lo(v0, h0[e]);
+                h1[e] = __float2half_rn(v1);
+                l1[e] = split_lo(v1, h1[e]);
+            }
+            *reinterpret_cast<uint4 *>(dst + 16 * i) = *reinterpret_cast<const uint4 *>(h0);
+            *reinterpret_cast<uint4 *>(dst + 16 * i + 8) = *reinterpret_cast<const uint4 *>(h1);
+            if (lo_off > 0) {
+                *reinterpret_cast<uint4 *>(dst + 16 * i + lo_off) = *reinterpret_cast<const uint4 *>(l0);
+                *reinterpret_cast<uint4 *>(dst + 16 * i + 8 + lo_off) = *reinterpret_cast<const uint4 *>(l1);
+            }
+        }
+    }
+}
+
+void pool_up_adain_h(const float *x, __half *y, int64_t R_in, int64_t Ry_out, int C, const float *w,
+                     const float *bias, const Batch &b, int max_T, int64_t lo_off, const PrologueArgs &a,
+                     cudaStream_t st) {
+    // 64 threads cover 256 input rows
+    int bx = (max_T + 255) / 256;
+    if (bx > 16) bx = 16;
+    if (bx < 1) bx = 1;
+    k_pool_up_adain_h<<<dim3(bx, (C + 7) / 8, b.n), 64, 0, st>>>(x, y, R_in, Ry_out, C, w, bias, b, lo_off, a);
 }
 
 // Space-to-depth operand of the stride-6 noise convolution: every packed row
@@ -643,6 +770,9 @@ void f0n_conv(const float *in, int64_t R_in, float *out0, float *out1, int64_t R
 // of a double buffer while warps 1..3 merge segment s - 1 from the other
 // half; one block barrier per step. The arithmetic and its order are those
 // of a single warp doing both in turn.
+// (Half segments, 10.8 KB of shared memory so that a block shares an SM with
+// a persistent conv CTA, made the batch-64 forward 2.3 ms slower: the source
+// then runs longer beside the decoder and the generator waits for it.)
 constexpr int kSineThreads = 128;
 
 __global__ void __launch_bounds__(kSineThreads) k_sinegen(const float *__restrict__ f0, int mf,

@@ -226,6 +226,11 @@ void har_s2d(const float *har, int64_t R_har, __half *y, int64_t R, int64_t Ry, 
 // PrologueArgs::lo_off.
 void pool_up_h(const float *x, __half *y, int64_t R_in, int64_t Ry_out, int C, const float *w, const float *bias,
                const Batch &b, int max_T, int64_t lo_off, cudaStream_t st);
+// pool_up_h of LeakyReLU(AdaIN(x)) (norm terms, gamma / beta and slope of a,
+// the arithmetic of prologue), without the F32 intermediate
+void pool_up_adain_h(const float *x, __half *y, int64_t R_in, int64_t Ry_out, int C, const float *w,
+                     const float *bias, const Batch &b, int max_T, int64_t lo_off, const PrologueArgs &a,
+                     cudaStream_t st);
 
 // kk_frontend.cu: the text encoder's embedding and LayerNorm, the duration
 // projection.
