@@ -486,6 +486,47 @@ def bench_queue(kb, device, weights, pool, batch):
             "value": secs / wall, "unit": UNIT, "wall_s": wall, "batches": st["batches"], "max_batch": st["max_batch"]}
 
 
+def bench_stream(kb, W, device, weights, runs):
+    """First audio through a streaming session (kk_stream over a one-worker
+    GPU queue, adaptative preset): a request of four chunks (T = 40, 120,
+    120, 120 asr frames: a short first chunk, as the reference's adaptative
+    chunker makes it) pushed at once on an idle GPU; wall time from the
+    push to the first post-processed chunk in host memory (kk_stream_next),
+    and to the last. p50 over `runs` requests after two untimed ones."""
+    ctx = kb.Context(device)
+    ctx.upload(weights)
+    q = kb.Queue(contexts=[ctx], max_batch=8, max_batch_frames=8 * 800, max_wait_us=0)
+    rng = np.random.default_rng(77)
+    chunks = [W.make_utterance(rng, t) for t in (40, 120, 120, 120)]
+    first, total = [], []
+    try:
+        for r in range(runs + 2):
+            s = kb.Stream(q, kb.StreamConfig.preset(0))
+            t0 = time.perf_counter()
+            for i, u in enumerate(chunks):
+                s.push(u, kb.BOUNDARY_CLAUSE_WEAK, i == len(chunks) - 1)
+            t_first = None
+            while True:
+                rc, _, _ = s.next(60000)
+                if rc == kb.STREAM_END:
+                    break
+                if rc != 0:
+                    raise RuntimeError(f"stream result {rc}")
+                if t_first is None:
+                    t_first = time.perf_counter() - t0
+            t_all = time.perf_counter() - t0
+            s.close()
+            if r >= 2:
+                first.append(1e3 * t_first)
+                total.append(1e3 * t_all)
+    finally:
+        q.close()
+        ctx.close()
+    return {"workload": "one request of 4 chunks (T = 40, 120, 120, 120), idle GPU, adaptative preset",
+            "ttfa_p50_ms": statistics.median(first), "all_chunks_p50_ms": statistics.median(total),
+            "runs": runs, "audio_s": sum(u.T for u in chunks) / 40.0}
+
+
 def config_dict(batch=BATCH):
     return {
         "workload": "Kokoro-82M decoder (AdainResBlk1d encode/decode) + ISTFTNet generator + iSTFT; "
@@ -511,6 +552,7 @@ def main():
     ap.add_argument("--frontend-runs", type=int, default=5, help="timed calls per front-end stage (0 skips)")
     ap.add_argument("--vocos-runs", type=int, default=5, help="timed calls of the Vocos decoder (0 skips)")
     ap.add_argument("--no-queue", action="store_true", help="skip the batching-queue leg")
+    ap.add_argument("--stream-runs", type=int, default=20, help="timed requests of the streaming-session leg (0 skips)")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
@@ -694,6 +736,9 @@ def main():
     queue = None
     if rank == 0 and not args.no_queue:
         queue = bench_queue(kb, local, weights, [pool[i] for idx in batches for i in idx], args.batch)
+    stream = None
+    if rank == 0 and args.stream_runs > 0:
+        stream = bench_stream(kb, W, local, weights, args.stream_runs)
     frontend = None
     if rank == 0 and args.frontend_runs > 0:
         frontend = bench_frontend(kb, W, local, args.frontend_runs)
@@ -755,6 +800,7 @@ def main():
         "frontend": frontend,
         "vocos": vocos,
         "queue": queue,
+        "stream": stream,
         "parity_vs_c_library": parity,
         "pipeline_tflops": value / world * algorithmic_flop_per_asr_frame() * 40.0 / 1e12,
     }

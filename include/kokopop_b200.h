@@ -285,6 +285,90 @@ const char *kk_queue_last_error(void);
  * the workers. Call it once every kk_queue_wait has returned. */
 void kk_queue_destroy(kk_queue *q);
 
+/* ---- Streaming sessions over the queue ----
+ * The reference streams a request chunk by chunk (stream_synthesize,
+ * src/streaming/streaming.cpp:252-360): each chunk's raw audio is
+ * post-processed (postprocess_chunk_audio, src/audio/audio_postprocess.cpp:
+ * 260-307: silence trim and the boundary pause) and crossfaded onto the
+ * previous chunk's tail (postprocess_and_crossfade, streaming.cpp:26-60;
+ * apply_crossfade_smart, audio_postprocess.cpp:94-202), then handed to the
+ * caller in order. A kk_stream does the same over a kk_queue: kk_stream_push
+ * submits a chunk's decoder inputs at once (so the chunks of many sessions
+ * share GPU batches), kk_stream_next returns the chunks in push order, each
+ * post-processed and crossfaded as the reference does. The chunker and the
+ * phonemizer stay outside (their outputs are the pushed inputs). */
+
+/* Chunk boundaries (Boundary, src/synthesis/chunker/chunker.h:14-21). */
+enum {
+    KK_BOUNDARY_NONE = 0,
+    KK_BOUNDARY_CLAUSE_WEAK = 1,
+    KK_BOUNDARY_CLAUSE_STRONG = 2,
+    KK_BOUNDARY_SENTENCE = 3,
+    KK_BOUNDARY_NEWLINE = 4,
+    KK_BOUNDARY_PARAGRAPH = 5
+};
+
+/* kk_stream_next after the last chunk has been returned. */
+enum { KK_STREAM_END = -3 };
+
+/* The post-processing fields of ChunkConfig (chunker.h:26-51). */
+typedef struct kk_stream_config {
+    int32_t comma_pause_ms;
+    int32_t sentence_pause_ms;
+    int32_t paragraph_pause_ms;
+    int32_t crossfade_ms;
+    int32_t trim_silence;        /* 0 or 1 */
+    int32_t max_silence_trim_ms;
+    int32_t sample_rate;         /* 24000 for Kokoro */
+} kk_stream_config;
+
+/* The reference's presets (make_adaptative_config / make_long_form_config,
+ * src/synthesis/chunker/chunker.cpp:16-48): mode 0 adaptative, 1 long-form;
+ * sample_rate 24000. */
+int kk_stream_preset(int32_t mode, kk_stream_config *out);
+
+/* postprocess_chunk_audio on a host buffer: out gets at most `capacity`
+ * samples, *n_out the processed length (also when capacity is too small,
+ * then KK_ERROR_INVALID_ARGUMENT). Bit-exact with the reference. */
+int kk_postprocess_chunk(const kk_stream_config *cfg, const float *audio, int64_t n, int32_t boundary_after,
+                         int32_t is_first, int32_t is_last, float *out, int64_t capacity, int64_t *n_out);
+
+/* apply_crossfade_smart(prev, next, boundary, crossfade_ms, sample_rate) on
+ * host buffers, the same capacity rule. Bit-exact with the reference. */
+int kk_crossfade(const kk_stream_config *cfg, const float *prev, int64_t n_prev, const float *next, int64_t n_next,
+                 int32_t boundary, float *out, int64_t capacity, int64_t *n_out);
+
+typedef struct kk_stream kk_stream;
+
+/* A session on q (its own request id); the config is copied. */
+int kk_stream_create(kk_queue *q, const kk_stream_config *cfg, kk_stream **out);
+
+/* Queues the next chunk (inputs as for kk_queue_submit; they are copied, so
+ * the caller may reuse them on return). is_last marks the final chunk: no
+ * pause after it, and kk_stream_next returns KK_STREAM_END once it has been
+ * returned. No push after is_last. */
+int kk_stream_push(kk_stream *s, int32_t n_frames, const float *asr, const float *f0, const float *noise,
+                   const float *style, int32_t boundary_after, int32_t is_last);
+
+/* The next chunk in push order, waiting up to timeout_ms (< 0: without
+ * limit): KK_OK with *samples / *n_samples (owned by the session, valid
+ * until the next call) and *chunk_index; KK_QUEUE_PENDING on timeout, or
+ * when nothing has been pushed yet; KK_STREAM_END after the last chunk. A
+ * chunk that failed returns its status with no samples, and the next chunk
+ * is not crossfaded onto the tail from before it (streaming.cpp:325-333);
+ * a cancelled chunk returns KK_QUEUE_CANCELLED. Not thread-safe per
+ * session; sessions are independent. */
+int kk_stream_next(kk_stream *s, int32_t timeout_ms, const float **samples, int64_t *n_samples,
+                   int32_t *chunk_index);
+
+/* Cancels the session's chunks not yet dispatched (the reference's stopped
+ * flag); the dispatched ones finish and are still returned by
+ * kk_stream_next. */
+int kk_stream_cancel(kk_stream *s);
+
+/* Waits for the session's chunks in flight, then frees it. */
+void kk_stream_destroy(kk_stream *s);
+
 /* Durations -> frames and the alignment (duration_to_frames,
  * src/arch/kokoro/kokoro.cpp:181-193; build_duration_mask :115-152 and
  * en = d . mask :669-674): frames[i] = clamp(int(lrint(d[i] / speed)), 1, 50)

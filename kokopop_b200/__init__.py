@@ -140,6 +140,19 @@ def load_library():
                                           vp, vp, vp, vp]
     L.kk_profile_records.argtypes = [vp, ctypes.POINTER(ProfileRecord), ctypes.c_size_t,
                                      ctypes.POINTER(ctypes.c_size_t)]
+    i64p = ctypes.POINTER(ctypes.c_int64)
+    cfgp = ctypes.POINTER(StreamConfig)
+    L.kk_stream_preset.argtypes = [ctypes.c_int32, cfgp]
+    L.kk_postprocess_chunk.argtypes = [cfgp, _f32p, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                       _f32p, ctypes.c_int64, i64p]
+    L.kk_crossfade.argtypes = [cfgp, _f32p, ctypes.c_int64, _f32p, ctypes.c_int64, ctypes.c_int32, _f32p,
+                               ctypes.c_int64, i64p]
+    L.kk_stream_create.argtypes = [vp, cfgp, ctypes.POINTER(vp)]
+    L.kk_stream_push.argtypes = [vp, ctypes.c_int32, _f32p, _f32p, _f32p, _f32p, ctypes.c_int32, ctypes.c_int32]
+    L.kk_stream_next.argtypes = [vp, ctypes.c_int32, ctypes.POINTER(_f32p), i64p, ctypes.POINTER(ctypes.c_int32)]
+    L.kk_stream_cancel.argtypes = [vp]
+    L.kk_stream_destroy.argtypes = [vp]
+    L.kk_stream_destroy.restype = None
     _lib = L
     return L
 
@@ -158,6 +171,65 @@ QUEUE_EXEC_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_int32, 
                                  ctypes.POINTER(ctypes.c_float))
 QUEUE_PENDING = -1
 QUEUE_CANCELLED = -2
+STREAM_END = -3
+
+# chunk boundaries (KK_BOUNDARY_*)
+BOUNDARY_NONE, BOUNDARY_CLAUSE_WEAK, BOUNDARY_CLAUSE_STRONG, BOUNDARY_SENTENCE, BOUNDARY_NEWLINE, \
+    BOUNDARY_PARAGRAPH = range(6)
+
+
+class StreamConfig(ctypes.Structure):
+    """kk_stream_config: the post-processing fields of the reference's
+    ChunkConfig. preset(0) is the adaptative preset, preset(1) long-form."""
+    _fields_ = [
+        ("comma_pause_ms", ctypes.c_int32),
+        ("sentence_pause_ms", ctypes.c_int32),
+        ("paragraph_pause_ms", ctypes.c_int32),
+        ("crossfade_ms", ctypes.c_int32),
+        ("trim_silence", ctypes.c_int32),
+        ("max_silence_trim_ms", ctypes.c_int32),
+        ("sample_rate", ctypes.c_int32),
+    ]
+
+    @classmethod
+    def preset(cls, mode: int = 0) -> "StreamConfig":
+        c = cls()
+        L = load_library()
+        rc = L.kk_stream_preset(mode, ctypes.byref(c))
+        if rc != 0:
+            raise KKError(rc, L.kk_queue_last_error().decode())
+        return c
+
+
+def postprocess_chunk(cfg: StreamConfig, audio: np.ndarray, boundary_after: int, is_first: bool,
+                      is_last: bool) -> np.ndarray:
+    """kk_postprocess_chunk (the reference's postprocess_chunk_audio)."""
+    L = load_library()
+    a = np.ascontiguousarray(audio, np.float32)
+    longest_pause_ms = max(cfg.paragraph_pause_ms, cfg.sentence_pause_ms, cfg.comma_pause_ms, 0)
+    cap = len(a) + longest_pause_ms * cfg.sample_rate // 1000 + 1
+    out = np.zeros(cap, np.float32)
+    n = ctypes.c_int64()
+    rc = L.kk_postprocess_chunk(ctypes.byref(cfg), _ptr(a), len(a), boundary_after, int(is_first), int(is_last),
+                                _ptr(out), cap, ctypes.byref(n))
+    if rc != 0:
+        raise KKError(rc, L.kk_queue_last_error().decode())
+    return out[:n.value].copy()
+
+
+def crossfade(cfg: StreamConfig, prev: np.ndarray, nxt: np.ndarray, boundary: int) -> np.ndarray:
+    """kk_crossfade (the reference's apply_crossfade_smart)."""
+    L = load_library()
+    p = np.ascontiguousarray(prev, np.float32)
+    q = np.ascontiguousarray(nxt, np.float32)
+    cap = len(p) + len(q)
+    out = np.zeros(max(cap, 1), np.float32)
+    n = ctypes.c_int64()
+    rc = L.kk_crossfade(ctypes.byref(cfg), _ptr(p), len(p), _ptr(q), len(q), boundary, _ptr(out), cap,
+                        ctypes.byref(n))
+    if rc != 0:
+        raise KKError(rc, L.kk_queue_last_error().decode())
+    return out[:n.value].copy()
 
 
 def _ptr(a: Optional[np.ndarray], t=_f32p):
@@ -498,4 +570,46 @@ class Queue:
     def close(self):
         if self.h:
             self.L.kk_queue_destroy(self.h)
+            self.h = ctypes.c_void_p()
+
+
+class Stream:
+    """kk_stream: one request's chunks through a Queue, returned in order,
+    post-processed and crossfaded as the reference's stream_synthesize
+    does. push() takes a workload.Utterance-like chunk; next() returns
+    (status, samples or None, chunk index)."""
+
+    def __init__(self, queue: "Queue", cfg: Optional[StreamConfig] = None):
+        self.L = load_library()
+        self.q = queue
+        self.cfg = cfg if cfg is not None else StreamConfig.preset(0)
+        self.h = ctypes.c_void_p()
+        rc = self.L.kk_stream_create(queue.h, ctypes.byref(self.cfg), ctypes.byref(self.h))
+        if rc != 0:
+            raise KKError(rc, self.L.kk_queue_last_error().decode())
+
+    def push(self, u, boundary_after: int = BOUNDARY_NONE, is_last: bool = False) -> None:
+        a = [np.ascontiguousarray(x, np.float32) for x in (u.asr, u.f0, u.noise, u.style)]
+        rc = self.L.kk_stream_push(self.h, int(u.T), *[_ptr(x) for x in a], boundary_after, int(is_last))
+        if rc != 0:
+            raise KKError(rc, self.L.kk_queue_last_error().decode())
+
+    def next(self, timeout_ms: int = -1):
+        p = _f32p()
+        n = ctypes.c_int64()
+        idx = ctypes.c_int32()
+        rc = self.L.kk_stream_next(self.h, timeout_ms, ctypes.byref(p), ctypes.byref(n), ctypes.byref(idx))
+        if rc == 0:
+            out = np.ctypeslib.as_array(p, shape=(n.value,)).copy() if n.value else np.zeros(0, np.float32)
+            return rc, out, idx.value
+        if rc == 1:
+            raise KKError(rc, self.L.kk_queue_last_error().decode())
+        return rc, None, idx.value
+
+    def cancel(self) -> None:
+        self.L.kk_stream_cancel(self.h)
+
+    def close(self) -> None:
+        if self.h:
+            self.L.kk_stream_destroy(self.h)
             self.h = ctypes.c_void_p()

@@ -17,7 +17,7 @@ LIB = os.path.join(HERE, "libkokopop_b200.so")
 
 CU_SOURCES = ["kk_kernels.cu", "kk_conv_simt.cu", "kk_conv_tc.cu", "kk_istft_static.cu", "kk_lstm.cu", "kk_frontend.cu",
               "kk_vocos.cu"]
-CXX_SOURCES = ["kk_host.cpp", "kk_queue.cpp"]
+CXX_SOURCES = ["kk_host.cpp", "kk_queue.cpp", "kk_stream.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr"] + ARCH
 

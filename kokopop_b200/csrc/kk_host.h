@@ -26,6 +26,10 @@ float half_to_float(uint16_t h);
 cudaError_t device_malloc(void **p, size_t bytes);
 cudaError_t pinned_malloc(void **p, size_t bytes);
 
+// kk_queue.cpp: sets the message of kk_queue_last_error on this thread;
+// returns code.
+int queue_error(int code, const char *msg);
+
 // A weight as F32 values on the device (F16 tensors are widened exactly);
 // `f16` records the stored type because it selects ggml's F16 arithmetic.
 struct DevTensor {

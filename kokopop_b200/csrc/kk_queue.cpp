@@ -309,6 +309,12 @@ int q_config(kk_queue *q, int32_t max_batch, int64_t max_batch_frames, int32_t m
 
 }  // namespace
 
+namespace kk {
+// Sets the message kk_queue_last_error returns on this thread (the
+// streaming sessions of kk_stream.cpp report through it too); returns code.
+int queue_error(int code, const char *msg) { return q_fail(code, msg); }
+}  // namespace kk
+
 extern "C" {
 
 int kk_queue_create(kk_ctx *const *ctxs, int32_t n_ctx, int32_t max_batch, int64_t max_batch_frames,

@@ -336,6 +336,11 @@ def ref():
         R.kkref_harmonic_stft.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int64, _f32p, ctypes.c_float, _f32p, _f32p]
         R.kkref_duration_to_frames.argtypes = [ctypes.c_float, ctypes.c_float]
         R.kkref_duration_mask.argtypes = [ctypes.POINTER(ctypes.c_int32), ctypes.c_int64, ctypes.c_int64, _f32p]
+        R.kkref_postprocess_chunk.argtypes = [_f32p, ctypes.c_int64] + [ctypes.c_int] * 10 + [_f32p, ctypes.c_int64]
+        R.kkref_postprocess_chunk.restype = ctypes.c_int64
+        R.kkref_crossfade_smart.argtypes = [_f32p, ctypes.c_int64, _f32p, ctypes.c_int64, ctypes.c_int, ctypes.c_int,
+                                            ctypes.c_int, _f32p, ctypes.c_int64]
+        R.kkref_crossfade_smart.restype = ctypes.c_int64
         R.kkref_istft_complex.argtypes = [_f32p, _f32p, ctypes.c_int64, ctypes.c_int, ctypes.c_int, _f32p,
                                           ctypes.POINTER(ctypes.c_int64)]
         R.kkref_dc_block.argtypes = [_f32p, ctypes.c_int64, ctypes.c_float]
@@ -365,6 +370,51 @@ def ref_dc_block(audio: np.ndarray, pole: float) -> np.ndarray:
     a = np.array(audio, np.float32, copy=True)
     ref().kkref_dc_block(_ptr(a), len(a), ctypes.c_float(pole))
     return a
+
+
+def ref_postprocess_chunk(audio: np.ndarray, boundary: int, is_first: bool, is_last: bool, cfg) -> np.ndarray:
+    """The reference's postprocess_chunk_audio (src/audio/audio_postprocess.cpp:
+    260-307) with cfg's post-processing fields (a kokopop_b200.StreamConfig
+    or any object with those attributes)."""
+    R = ref()
+    a = np.ascontiguousarray(audio, np.float32)
+    cap = len(a) + max(cfg.paragraph_pause_ms, cfg.sentence_pause_ms, cfg.comma_pause_ms, 0) * cfg.sample_rate // 1000 + 1
+    out = np.zeros(cap, np.float32)
+    n = R.kkref_postprocess_chunk(_ptr(a), len(a), boundary, int(is_first), int(is_last), cfg.comma_pause_ms,
+                                  cfg.sentence_pause_ms, cfg.paragraph_pause_ms, cfg.crossfade_ms,
+                                  int(cfg.trim_silence), cfg.max_silence_trim_ms, cfg.sample_rate, _ptr(out), cap)
+    assert n <= cap
+    return out[:n].copy()
+
+
+def ref_crossfade_smart(prev: np.ndarray, nxt: np.ndarray, boundary: int, crossfade_ms: int,
+                        sample_rate: int) -> np.ndarray:
+    """The reference's apply_crossfade_smart (audio_postprocess.cpp:94-202)."""
+    R = ref()
+    p = np.ascontiguousarray(prev, np.float32)
+    q = np.ascontiguousarray(nxt, np.float32)
+    cap = len(p) + len(q)
+    out = np.zeros(max(cap, 1), np.float32)
+    n = R.kkref_crossfade_smart(_ptr(p), len(p), _ptr(q), len(q), boundary, crossfade_ms, sample_rate, _ptr(out),
+                                cap)
+    assert n <= cap
+    return out[:n].copy()
+
+
+def ref_stream(raw_chunks, boundaries, cfg):
+    """postprocess_and_crossfade (src/streaming/streaming.cpp:26-60) over a
+    request's raw chunk audio, in order, with the reference's own functions:
+    the list of post-processed, crossfaded chunks it hands to its callback."""
+    out, tail = [], np.zeros(0, np.float32)
+    n = len(raw_chunks)
+    ncf = cfg.crossfade_ms * cfg.sample_rate // 1000 if cfg.crossfade_ms > 0 else 0
+    for i, (raw, b) in enumerate(zip(raw_chunks, boundaries)):
+        p = ref_postprocess_chunk(raw, b, i == 0, i == n - 1, cfg)
+        if len(tail) and len(p):
+            p = ref_crossfade_smart(tail, p, b, cfg.crossfade_ms, cfg.sample_rate)
+        tail = p[max(0, len(p) - ncf):].copy() if len(p) and ncf > 0 else np.zeros(0, np.float32)
+        out.append(p)
+    return out
 
 
 def ref_bin_mask(bins: int) -> np.ndarray:

@@ -121,6 +121,28 @@ def main():
     vs["mask_513"] = O.ref_bin_mask(513)
     np.savez_compressed(os.path.join(OUT, "vocos_ref.npz"), **vs)
 
+    # streaming: raw chunks (a tone between near-silent stretches) through
+    # the reference's postprocess_chunk_audio + apply_crossfade_smart, as
+    # postprocess_and_crossfade composes them, for both presets
+    import kokopop_b200 as kb
+    srng = np.random.default_rng(23)
+    lens = [600 * T for T in (4, 2, 6, 3, 5)]
+    raws = []
+    for n in lens:
+        lead, trail = int(srng.integers(0, n // 3)), int(srng.integers(0, n // 3))
+        body = n - lead - trail
+        tone = (0.3 * np.sin(0.013 * np.arange(body)) * (0.5 + 0.5 * srng.random(body))).astype(np.float32)
+        quiet = lambda k: (0.009 * (srng.random(k) * 2 - 1)).astype(np.float32)
+        raws.append(np.concatenate([quiet(lead), tone, quiet(trail)]).astype(np.float32))
+    bounds = np.array([1, 0, 3, 2, 5], np.int32)
+    st = {"raw": np.concatenate(raws), "lens": np.array(lens, np.int64), "bounds": bounds}
+    for mode in (0, 1):
+        cfg = kb.StreamConfig.preset(mode)
+        outs = O.ref_stream(raws, [int(b) for b in bounds], cfg)
+        st[f"out_{mode}"] = np.concatenate(outs)
+        st[f"out_lens_{mode}"] = np.array([len(o) for o in outs], np.int64)
+    np.savez_compressed(os.path.join(OUT, "stream_ref.npz"), **st)
+
     sm = {}
     u = W.make_utterance(np.random.default_rng(11), 3)
     sm["asr"], sm["f0"], sm["noise"], sm["style"] = u.asr, u.f0, u.noise, u.style
