@@ -711,7 +711,13 @@ def main():
     ttfa = None
     cpu = None
     parity = None
-    if rank == 0 and args.ttfa_runs > 0:
+    # The single-GPU legs below (TTFA, LSTM stack, prosody, queue, stream,
+    # front end, Vocos) run at N = 1 only: at N > 1 the other ranks have left
+    # by then while this rank's NCCL communicator lives on, which slowed the
+    # host-driven legs (the queue leg measured 457 audio-s/s at N = 2 against
+    # 8066 at N = 1), and their single-GPU figures are those of the N = 1 run.
+    single = rank == 0 and world == 1
+    if single and args.ttfa_runs > 0:
         # p50 time to first audio: one config-0 utterance (T=200, F32 weights
         # seed 0), submitted alone on an idle GPU, until its samples are in
         # host memory; the whole utterance is returned in one piece.
@@ -728,22 +734,22 @@ def main():
         ttfa = 1e3 * statistics.median(lat)
         c0.close()
     lstm = None
-    if rank == 0 and args.lstm_runs > 0:
+    if single and args.lstm_runs > 0:
         lstm = bench_lstm(kb, W, local, args.lstm_runs)
     prosody = None
-    if rank == 0 and args.prosody_runs > 0:
+    if single and args.prosody_runs > 0:
         prosody = bench_prosody(kb, W, local, args.prosody_runs, pool, args.batch)
     queue = None
-    if rank == 0 and not args.no_queue:
+    if single and not args.no_queue:
         queue = bench_queue(kb, local, weights, [pool[i] for idx in batches for i in idx], args.batch)
     stream = None
-    if rank == 0 and args.stream_runs > 0:
+    if single and args.stream_runs > 0:
         stream = bench_stream(kb, W, local, weights, args.stream_runs)
     frontend = None
-    if rank == 0 and args.frontend_runs > 0:
+    if single and args.frontend_runs > 0:
         frontend = bench_frontend(kb, W, local, args.frontend_runs)
     vocos = None
-    if rank == 0 and args.vocos_runs > 0:
+    if single and args.vocos_runs > 0:
         vocos = bench_vocos(kb, W, local, args.vocos_runs)
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
@@ -802,6 +808,8 @@ def main():
         "queue": queue,
         "stream": stream,
         "parity_vs_c_library": parity,
+        "single_gpu_legs": "measured" if world == 1 else "N = 1 only (ttfa, lstm, prosody, queue, stream, frontend, "
+                                                         "vocos, cpu_baseline, parity: see the N = 1 line)",
         "pipeline_tflops": value / world * algorithmic_flop_per_asr_frame() * 40.0 / 1e12,
     }
     if rank == 0:
