@@ -2087,7 +2087,8 @@ cudaError_t conv_tc(const ConvTcArgs &a, cudaStream_t st) {
     if (a.stats && (a.sb.n < 1 || a.sm < 1 || a.sextra < 0 || a.omul != 1 || a.oadd != 0 || a.phase_oc != 0))
         return cudaErrorInvalidValue;
     const int64_t tiles = P.m_tiles * P.n_oc_tiles;
-    const int64_t slots = g_num_sms > 0 ? g_num_sms : 148;
+    int64_t slots = g_num_sms > 0 ? g_num_sms : 148;
+    if (a.max_ctas > 0 && a.max_ctas < slots) slots = a.max_ctas;
     const unsigned grid = (unsigned)(tiles < slots ? tiles : slots);
     // channels x positions kernel where output row = position
     // (a residual upsampled x2 by resid_half only on the unstaged epilogue;

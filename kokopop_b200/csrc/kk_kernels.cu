@@ -773,14 +773,28 @@ void f0n_conv(const float *in, int64_t R_in, float *out0, float *out1, int64_t R
 // (Half segments, 10.8 KB of shared memory so that a block shares an SM with
 // a persistent conv CTA, made the batch-64 forward 2.3 ms slower: the source
 // then runs longer beside the decoder and the generator waits for it.)
-constexpr int kSineThreads = 128;
+// A block carries kSineGroups utterances, one group of 4 warps each with its
+// own named barrier and buffer, so the source occupies n / kSineGroups SMs
+// while it runs beside the decoder (sinegen_blocks), not one per utterance:
+// the decoder's persistent convolutions keep the other SMs. Measured at
+// batch 64 (whole forwards): one utterance per block 62.2-63.0 ms, two
+// 60.9-61.3 ms, four 63.2-63.9 ms (the source itself slower), against
+// 62.1 ms with one per block and no cap on the conv grids.
+constexpr int kSineThreads = 128;  // per utterance
+constexpr int kSineGroups = 2;
+constexpr int kSineSmem = kSineGroups * 2 * kHarmonics * kUpsample * 4;
 
-__global__ void __launch_bounds__(kSineThreads) k_sinegen(const float *__restrict__ f0, int mf,
-                                                          float *__restrict__ source, Batch b,
-                                                          const int64_t *__restrict__ cumT, SineArgs a) {
-    __shared__ float sbuf[2][kHarmonics][kUpsample];
-    const int u = blockIdx.x;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+__global__ void __launch_bounds__(kSineThreads *kSineGroups) k_sinegen(const float *__restrict__ f0, int mf,
+                                                                       float *__restrict__ source, Batch b,
+                                                                       const int64_t *__restrict__ cumT,
+                                                                       SineArgs a) {
+    extern __shared__ float sine_smem[];
+    const int grp = threadIdx.x / kSineThreads;
+    const int u = blockIdx.x * kSineGroups + grp;
+    if (u >= b.n) return;  // the whole group (it syncs on its own barrier only)
+    float(*sbuf)[kHarmonics][kUpsample] =
+        reinterpret_cast<float(*)[kHarmonics][kUpsample]>(sine_smem + grp * 2 * kHarmonics * kUpsample);
+    const int tid = threadIdx.x % kSineThreads, lane = tid & 31, warp = tid >> 5;
     const int64_t nseg = (int64_t)mf * b.T[u];
     const float *fp = f0 + (int64_t)mf * b.offT[u];
     float *src = source + (int64_t)kUpsample * mf * cumT[u];
@@ -831,13 +845,23 @@ __global__ void __launch_bounds__(kSineThreads) k_sinegen(const float *__restric
                 for (int j = tid - 32; j < kUpsample; j += kSineThreads - 32) out[j] = a.unvoiced;
             }
         }
-        __syncthreads();
+        // this group's barrier (ids 1 .. kSineGroups; 0 is __syncthreads)
+        asm volatile("bar.sync %0, %1;" ::"r"(grp + 1), "r"(kSineThreads) : "memory");
     }
 }
 
+int sinegen_blocks(int n_utts) { return (n_utts + kSineGroups - 1) / kSineGroups; }
+
 void sinegen(const float *f0, int mf, float *source, const Batch &b, const int64_t *cumT,
              const SineArgs &a, cudaStream_t st) {
-    k_sinegen<<<b.n, kSineThreads, 0, st>>>(f0, mf, source, b, cumT, a);
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+        cudaFuncSetAttribute(k_sinegen, cudaFuncAttributeMaxDynamicSharedMemorySize, kSineSmem);
+        if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
+    k_sinegen<<<sinegen_blocks(b.n), kSineThreads * kSineGroups, kSineSmem, st>>>(f0, mf, source, b, cumT, a);
 }
 
 // Forward STFT of the source (audio_utils.cpp:381-419): Hann-20 window, hop

@@ -121,6 +121,9 @@ void f0n_conv(const float *in, int64_t R_in, float *out0, float *out1, int64_t R
 // units), the source 300 mf T samples, the STFT 60 mf T + 1 frames.
 void sinegen(const float *f0, int mf, float *source, const Batch &b, const int64_t *cumT,
              const SineArgs &a, cudaStream_t st);
+// Thread blocks (one SM each at most) the harmonic source of n utterances
+// occupies while it runs.
+int sinegen_blocks(int n_utts);
 void stft(const float *source, float *har, int64_t R, int mf, const Batch &b, const int64_t *cumT,
           const StftTables *tab, int max_T, cudaStream_t st);
 // post has a_nf * T + 1 frames per utterance at rows a_nf * offT; audio is
@@ -184,6 +187,10 @@ struct ConvTcArgs {
     // phase r at input position q writes output row q * omul + oadd + r.
     // Epilogue: bias and residual only.
     int phase_nc;
+    // > 0: at most this many persistent CTAs (the SMs left while another
+    // stream's kernel holds the rest; a static tile split over CTAs that
+    // cannot all be resident would wait for that kernel)
+    int max_ctas;
     // non-null: the instance-norm terms (mean, scale) of the output over each
     // utterance's valid rows at level (sm, sextra) of batch sb, into
     // stats[u * OC + c]. With stats_aligned (every utterance of the level
