@@ -503,8 +503,12 @@ void kk_ctx::derive() {
     tc_mode = all16 || all32;
     split_mode = all32;
     {
+        // the operand formed inside the conv (k_conv_tcf) for the residual
+        // blocks' convs with at least this many taps: "1" all of them, "7"
+        // the k = 7 and k = 11 ones; unset or "0": none
         const char *f = std::getenv("KOKOPOP_B200_FUSED_OPERAND");
-        fuse_operand = f && f[0] == '1';
+        fuse_min_taps = f ? std::atoi(f) : 0;
+        fuse_operand = fuse_min_taps > 0;
         // the ConvTranspose as phase-major 128-channel tiles on k_conv_tc
         // (every S-th output row per store) instead of k_convt_tc
         const char *g = std::getenv("KOKOPOP_B200_CONVT_PHASES");
@@ -1506,7 +1510,7 @@ struct Runner {
                           const Op &o, int C, int m, int extra, const std::string &wname, const std::string &bname,
                           int K, int p, int d, float *out, Epi e) {
         const int64_t Rm = R(m);
-        if (tc && !split && c.fuse_operand) {
+        if (tc && !split && c.fuse_operand && K >= c.fuse_min_taps) {
             const AdainSite &s = site(adain);
             if (s.C != C) throw KKError(KK_ERROR_MODEL, "AdaIN channel mismatch: " + adain);
             auto it = c.packed.find(wname);

@@ -167,6 +167,7 @@ struct kk_ctx {
     // their AdaIN + Snake operand inside the conv (k_conv_tcf, bit-identical
     // to the separate operand pass, slower than it on B200 so far)
     bool fuse_operand = false;
+    int fuse_min_taps = 0;  // fuse_operand: only convs with at least this many taps
     bool convt_phases = false;  // ConvTranspose on k_conv_tc phase tiles instead of k_convt_tc
     std::unordered_map<std::string, kk::PackedW> packed;
     std::unordered_map<std::string, kk::DevBuf> adain_t;  // fc weights transposed to [128][C]
