@@ -464,14 +464,19 @@ def bench_queue(kb, device, weights, pool, batch):
     context of this GPU, max_batch = the bench batch, 2 ms batching wait): all
     chunks submitted at once from the host, wall time until the last result is
     in host memory (the second of two passes); audio-s/s and the batches
-    formed over both passes."""
+    formed over both passes. The output buffers are the caller's, allocated
+    and touched once before both passes (as a C caller of kk_queue_submit
+    passes its own)."""
     ctx = kb.Context(device)
     ctx.upload(weights)
     q = kb.Queue(contexts=[ctx], max_batch=batch, max_batch_frames=batch * 800, max_wait_us=2000)
+    outs = [np.zeros(600 * int(u.T), np.float32) for u in pool]
+    for o in outs:
+        o.fill(0.0)
     try:
         for timed in (False, True):  # one untimed pass: workspace and staging allocated
             t0 = time.perf_counter()
-            tickets = [q.submit(i, u) for i, u in enumerate(pool)]
+            tickets = [q.submit(i, u, outs[i]) for i, u in enumerate(pool)]
             for t in tickets:
                 rc, _ = q.wait(t, 600000)
                 if rc != 0:

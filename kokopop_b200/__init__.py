@@ -530,12 +530,19 @@ class Queue:
         if rc != 0:
             raise KKError(rc, self.L.kk_queue_last_error().decode())
 
-    def submit(self, request: int, u) -> int:
+    def submit(self, request: int, u, out: Optional[np.ndarray] = None) -> int:
+        """Queues chunk u; `out` (float32, 600 T samples) receives its audio,
+        a new array when not given."""
         asr = np.ascontiguousarray(u.asr, np.float32)
         f0 = np.ascontiguousarray(u.f0, np.float32)
         noise = np.ascontiguousarray(u.noise, np.float32)
         style = np.ascontiguousarray(u.style, np.float32)
-        audio = np.zeros(600 * int(u.T), np.float32)
+        if out is not None:
+            if out.dtype != np.float32 or not out.flags.c_contiguous or out.size != 600 * int(u.T):
+                raise KKError(KK_ERROR_INVALID_ARGUMENT, "out must be contiguous float32 of 600 T samples")
+            audio = out
+        else:
+            audio = np.zeros(600 * int(u.T), np.float32)
         ticket = ctypes.c_uint64()
         with self._lock:
             rc = self.L.kk_queue_submit(self.h, request, int(u.T), _ptr(asr), _ptr(f0), _ptr(noise), _ptr(style),
