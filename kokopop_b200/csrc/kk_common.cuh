@@ -49,52 +49,53 @@ __device__ __forceinline__ float gelu_erf(float x) {
     return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, e));
 }
 
-// sin for the Snake activation. Its arguments v * alpha are small in
-// practice, where the odd Taylor polynomial of sin to x^9 (Horner in x^2)
-// is accurate to float rounding: the first omitted term x^11/11! is below
-// 3e-9 relative for |x| <= pi/4. Larger arguments take the library sinf.
-constexpr float kSnakeSmall = 0.78539816f;  // pi / 4: the polynomial's range
+// sin^2 for the Snake activation v + sin^2(v alpha) / alpha. sin^2 has
+// period pi: with k the integer nearest y * 2/pi and r = y - k pi/2
+// (|r| <= pi/4), sin^2 y = sin^2 r for even k and cos^2 r = 1 - sin^2 r for
+// odd k. sin^2 r is its Taylor series
+//   sum_{n >= 1} (-1)^(n+1) 2^(2n-1) r^(2n) / (2n)!  =  r^2 P(r^2),
+// P to the r^10 term (Horner); the first omitted term is below 6e-9 of the
+// value on |r| <= pi/4. The reduction is Cody-Waite with pi/2 split into two
+// floats (r exact to about 2e-11 for |y| <= kSnakeReduce); k is rounded by
+// the 1.5 * 2^23 addend, whose low mantissa bit is k's parity. Against
+// sin^2 in double precision: within 2 ulp for |y| <= 0.78, within 3.6 ulp
+// (or 1.1e-7 absolute near the zeros) up to kSnakeReduce, 0.38-0.46 ulp on
+// average (a C library's sinf, squared and rounded, averages 0.52-0.57).
+// Larger arguments take the library sinf, squared.
+constexpr float kSnakeFast = 0.77f;       // |y| < kSnakeFast: k = 0 and r = y
+constexpr float kSnakeReduce = 8192.0f;  // the two-constant reduction's range
 
-// The polynomial alone, for |x| <= kSnakeSmall.
-__device__ __forceinline__ float snake_sin_small(float x) {
-    const float x2 = x * x;
-    float p = 2.7557319e-06f;         // 1/9!
-    p = fmaf(p, x2, -1.9841270e-04f);  // -1/7!
-    p = fmaf(p, x2, 8.3333333e-03f);   // 1/5!
-    p = fmaf(p, x2, -1.6666667e-01f);  // -1/3!
-    return fmaf(x * x2, p, x);
+// r^2 P(r^2) given r2 = r * r.
+__device__ __forceinline__ float snake_p(float r2) {
+    float p = -4.2755596e-06f;          // -2 / 467775     (n = 6)
+    p = fmaf(p, r2, 1.4109348e-04f);    //  2 / 14175      (n = 5)
+    p = fmaf(p, r2, -3.1746032e-03f);   // -1 / 315        (n = 4)
+    p = fmaf(p, r2, 4.4444446e-02f);    //  2 / 45         (n = 3)
+    p = fmaf(p, r2, -3.3333334e-01f);   // -1 / 3          (n = 2)
+    p = fmaf(p, r2, 1.0f);              //  1              (n = 1)
+    return __fmul_rn(r2, p);
 }
 
-// Arguments past the two-constant reduction's range go to the library sinf,
-// out of line so that the unrolled element loops stay small.
-static __device__ __noinline__ float snake_sin_huge(float x) { return sinf(x); }
-
-constexpr float kSnakeReduce = 8192.0f;
-
-// sin(x) for kSnakeSmall < |x| <= kSnakeReduce: Cody-Waite reduction by pi
-// with pi split into two floats (x = k pi + r, |r| <= pi/2, r carrying an
-// absolute error near 1e-7), then the Taylor series of sin to r^13 (its
-// remainder is below 7e-10 on [-pi/2, pi/2]) and the sign (-1)^k.
-__device__ __forceinline__ float snake_sin_reduced(float x) {
-    const float k = rintf(x * 0.31830987f);  // 1 / pi
-    float r = fmaf(-k, 3.14159274f, x);      // float(pi)
-    r = fmaf(-k, -8.74227766e-08f, r);       // pi - float(pi)
-    const float r2 = r * r;
-    float p = 1.60590444e-10f;           // 1/13!
-    p = fmaf(p, r2, -2.50521079e-08f);   // -1/11!
-    p = fmaf(p, r2, 2.75573188e-06f);    // 1/9!
-    p = fmaf(p, r2, -1.98412701e-04f);   // -1/7!
-    p = fmaf(p, r2, 8.33333377e-03f);    // 1/5!
-    p = fmaf(p, r2, -1.66666672e-01f);   // -1/3!
-    const float s = fmaf(r * r2, p, r);
-    return __int_as_float(__float_as_int(s) ^ ((int)k << 31));
+// |y| <= kSnakeReduce. For |y| < kSnakeFast this is snake_p(y * y) bit for
+// bit (k = +0: both fmas return y unchanged, and the parity bit is 0).
+__device__ __forceinline__ float snake_sin2_reduced(float y) {
+    const float t = fmaf(y, 0.63661975f, 12582912.0f);  // 2/pi; 1.5 * 2^23
+    const float k = __fsub_rn(t, 12582912.0f);
+    float r = fmaf(-k, 1.5707964f, y);    // float(pi/2)
+    r = fmaf(-k, -4.371139e-08f, r);      // pi/2 - float(pi/2)
+    const float s2 = snake_p(__fmul_rn(r, r));
+    return (__float_as_int(t) & 1) ? __fsub_rn(1.0f, s2) : s2;
 }
 
-__device__ __forceinline__ float snake_sin(float x) {
-    const float ax = fabsf(x);
-    if (ax <= kSnakeSmall) return snake_sin_small(x);
-    if (ax <= kSnakeReduce) return snake_sin_reduced(x);
-    return snake_sin_huge(x);
+// Arguments past the reduction's range (and non-finite ones), out of line so
+// that the unrolled element loops stay small.
+static __device__ __noinline__ float snake_sin2_huge(float y) {
+    const float s = sinf(y);
+    return __fmul_rn(s, s);
+}
+
+__device__ __forceinline__ float snake_sin2(float y) {
+    return fabsf(y) <= kSnakeReduce ? snake_sin2_reduced(y) : snake_sin2_huge(y);
 }
 
 // Packed FP32 pairs (sm_100 f32x2): two lanes of IEEE round-to-nearest

@@ -997,27 +997,30 @@ __device__ __forceinline__ void xf_edge(const uint8_t *pc, uint8_t *dst, int cl,
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         t[i] = f2mul_sep(w[i], q.al, z);
-        small = small && fabsf(t[i].x) <= kSnakeSmall && fabsf(t[i].y) <= kSnakeSmall;
+        small = small && fabsf(t[i].x) < kSnakeFast && fabsf(t[i].y) < kSnakeFast;
     }
-    float2 sn[4];
+    float2 s2[4];
     if (__all_sync(0xffffffffu, small)) {
+        // snake_p in pairs
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            const float2 t2 = f2mul_sep(t[i], t[i], z);
-            float2 p = f2fma(make_float2(2.7557319e-06f, 2.7557319e-06f), t2,
-                             make_float2(-1.9841270e-04f, -1.9841270e-04f));
-            p = f2fma(p, t2, make_float2(8.3333333e-03f, 8.3333333e-03f));
-            p = f2fma(p, t2, make_float2(-1.6666667e-01f, -1.6666667e-01f));
-            sn[i] = f2fma(f2mul_sep(t[i], t2, z), p, t[i]);
+            const float2 r2 = f2mul_sep(t[i], t[i], z);
+            float2 p = f2fma(make_float2(-4.2755596e-06f, -4.2755596e-06f), r2,
+                             make_float2(1.4109348e-04f, 1.4109348e-04f));
+            p = f2fma(p, r2, make_float2(-3.1746032e-03f, -3.1746032e-03f));
+            p = f2fma(p, r2, make_float2(4.4444446e-02f, 4.4444446e-02f));
+            p = f2fma(p, r2, make_float2(-3.3333334e-01f, -3.3333334e-01f));
+            p = f2fma(p, r2, make_float2(1.0f, 1.0f));
+            s2[i] = f2mul_sep(r2, p, z);
         }
     } else {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) sn[i] = make_float2(snake_sin(t[i].x), snake_sin(t[i].y));
+        for (int i = 0; i < 4; ++i) s2[i] = make_float2(snake_sin2(t[i].x), snake_sin2(t[i].y));
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const int64_t g = g0 + 8 * i + rr;
-        const float2 v = f2add(w[i], f2mul_sep(f2mul_sep(sn[i], sn[i], z), q.ia, z));
+        const float2 v = f2add(w[i], f2mul_sep(s2[i], q.ia, z));
         const __half2 h = __floats2half2_rn(v.x, v.y);
         const uint32_t hb = *reinterpret_cast<const uint32_t *>(&h);
         if (g >= sel_lo && g < sel_hi)
@@ -1080,29 +1083,31 @@ __device__ __forceinline__ void xf_rows(const uint8_t *pc, uint8_t *dst, int c, 
     for (int i = 0; i < 4; ++i) {
         t[i] = p2_fma(w[i], p.al, z);
         const float2 tf = p2_unpack(t[i]);
-        small = small && fabsf(tf.x) <= kSnakeSmall && fabsf(tf.y) <= kSnakeSmall;
+        small = small && fabsf(tf.x) < kSnakeFast && fabsf(tf.y) < kSnakeFast;
     }
-    p2_t sn[4];
+    p2_t s2[4];
     if (__all_sync(0xffffffffu, small)) {
-        // snake_sin_small in pairs
+        // snake_p in pairs
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            const p2_t t2 = p2_fma(t[i], t[i], z);
-            p2_t pp = p2_fma(p2_bc(2.7557319e-06f), t2, p2_bc(-1.9841270e-04f));
-            pp = p2_fma(pp, t2, p2_bc(8.3333333e-03f));
-            pp = p2_fma(pp, t2, p2_bc(-1.6666667e-01f));
-            sn[i] = p2_fma(p2_fma(t[i], t2, z), pp, t[i]);
+            const p2_t r2 = p2_fma(t[i], t[i], z);
+            p2_t pp = p2_fma(p2_bc(-4.2755596e-06f), r2, p2_bc(1.4109348e-04f));
+            pp = p2_fma(pp, r2, p2_bc(-3.1746032e-03f));
+            pp = p2_fma(pp, r2, p2_bc(4.4444446e-02f));
+            pp = p2_fma(pp, r2, p2_bc(-3.3333334e-01f));
+            pp = p2_fma(pp, r2, p2_bc(1.0f));
+            s2[i] = p2_fma(r2, pp, z);
         }
     } else {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const float2 tf = p2_unpack(t[i]);
-            sn[i] = p2_pack(snake_sin(tf.x), snake_sin(tf.y));
+            s2[i] = p2_pack(snake_sin2(tf.x), snake_sin2(tf.y));
         }
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const float2 v = p2_unpack(p2_add(w[i], p2_fma(p2_fma(sn[i], sn[i], z), p.ia, z)));
+        const float2 v = p2_unpack(p2_add(w[i], p2_fma(s2[i], p.ia, z)));
         const int r = 8 * i + 2 * q;
         *reinterpret_cast<__half *>(dst + r * 16 + ch * 2) = __float2half_rn(v.x);
         *reinterpret_cast<__half *>(dst + (r + 1) * 16 + ch * 2) = __float2half_rn(v.y);

@@ -275,8 +275,7 @@ __global__ void __launch_bounds__(256) k_prologue(const float *__restrict__ x, f
         if (a.act == ACT_LEAKY) {
             v = leaky(v, a.slope);
         } else if (a.act == ACT_SNAKE) {
-            const float s = snake_sin(__fmul_rn(v, alpha));
-            v = __fadd_rn(v, __fmul_rn(__fmul_rn(s, s), inv_a));
+            v = __fadd_rn(v, __fmul_rn(snake_sin2(__fmul_rn(v, alpha)), inv_a));
         }
         if (a.round16) v = round_f16(v);
         y[base + t] = v;
@@ -335,51 +334,64 @@ void convt_row0(const ConvTRow0Args &a, const Batch &b, cudaStream_t st) {
 // A thread produces 4 consecutive rows x 8 channels: eight 16-byte loads
 // (one float4 per channel) and four contiguous 16-byte stores, so enough
 // bytes are in flight to stream at HBM rate. Rows of the 4-row group that
-// fall past the utterance are written as zero (they are gap rows). The
-// normalisation and the activation are template parameters so that each
-// variant keeps only the registers it needs (3 blocks per SM).
+// fall past the utterance are written as zero (they are gap rows); channels
+// past C take the neutral terms below, which give zero. The normalisation
+// and the activation are template parameters so that each variant keeps
+// only the registers it needs (3 blocks per SM).
+//
+// The pass is bound by instruction issue as much as by HBM, so the work per
+// element is kept to the arithmetic itself: the block's 8 channel terms are
+// formed once in shared memory (1/alpha included) and read from there each
+// pass, and one warp-wide test selects straight-line code for the common
+// cases (all Snake arguments in the polynomial's k = 0 range; no row past
+// the utterance).
 template <bool NORM, int ACT, bool SPLIT>
 __global__ void __launch_bounds__(256, SPLIT ? 2 : 3) k_prologue_h(const float *__restrict__ x, __half *__restrict__ y,
                                                        int64_t R, int64_t Ry, int C, int m, int extra, Batch b,
                                                        PrologueArgs a) {
+    // per channel e: {mean, scale, norm_w, norm_b}, {gamma, beta, alpha,
+    // 1/alpha}, and lim: |v| < lim keeps |v * alpha| below kSnakeFast
+    __shared__ float4 prm0[8], prm1[8];
+    __shared__ float lim[8];
     const int u = blockIdx.z, ch = blockIdx.y;
+    if (threadIdx.x < 8) {
+        const int e = threadIdx.x, c = ch * 8 + e;
+        float4 p0 = make_float4(0.f, 1.f, 1.f, 0.f), p1 = make_float4(0.f, 0.f, 0.f, 0.f);
+        float l = INFINITY;
+        if (c < C) {
+            if (NORM) {
+                const float2 s = a.ms[(int64_t)u * C + c];
+                p0 = make_float4(s.x, s.y, a.norm_w[c], a.norm_b[c]);
+                p1.x = a.gamma[(int64_t)u * C + c];
+                p1.y = a.beta[(int64_t)u * C + c];
+            }
+            if (ACT == ACT_SNAKE) {
+                p1.z = a.alpha[c];
+                p1.w = __fdiv_rn(1.0f, p1.z);
+                l = __fdiv_rz(kSnakeFast, fabsf(p1.z));
+            }
+        }
+        prm0[e] = p0;
+        prm1[e] = p1;
+        lim[e] = l;
+    }
+    __syncthreads();
     const int64_t len = (int64_t)m * b.T[u] + extra;
     const int64_t row0 = (int64_t)m * b.offT[u];  // a multiple of 4
-    float mean[8], scale[8], nw[8], nb[8], g[8], be[8], al[8], ia[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-        const int c = ch * 8 + e;
-        mean[e] = 0.f, scale[e] = 1.f, nw[e] = 1.f, nb[e] = 0.f, g[e] = 0.f, be[e] = 0.f, al[e] = 0.f, ia[e] = 0.f;
-        if (c >= C) continue;
-        if (NORM) {
-            const float2 s = a.ms[(int64_t)u * C + c];
-            mean[e] = s.x;
-            scale[e] = s.y;
-            nw[e] = a.norm_w[c];
-            nb[e] = a.norm_b[c];
-            g[e] = a.gamma[(int64_t)u * C + c];
-            be[e] = a.beta[(int64_t)u * C + c];
-        }
-        if (ACT == ACT_SNAKE) {
-            al[e] = a.alpha[c];
-            ia[e] = __fdiv_rn(1.0f, al[e]);
-        }
-    }
+    const float *xc = x + (int64_t)ch * 8 * R + row0;
     const int nc = C - ch * 8 < 8 ? C - ch * 8 : 8;
     for (int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4; t < len;
          t += (int64_t)gridDim.x * blockDim.x * 4) {
-        const int64_t row = row0 + t;
         float4 v4[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e)
-            v4[e] = e < nc ? *reinterpret_cast<const float4 *>(x + (int64_t)(ch * 8 + e) * R + row)
-                           : make_float4(0.f, 0.f, 0.f, 0.f);
+            v4[e] = e < nc ? *reinterpret_cast<const float4 *>(xc + e * R + t) : make_float4(0.f, 0.f, 0.f, 0.f);
         if (!NORM && a.x2) {
             // average of the three branches, in the reference's order
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
                 if (e >= nc) continue;
-                const int64_t o = (int64_t)(ch * 8 + e) * R + row;
+                const int64_t o = (int64_t)(ch * 8 + e) * R + row0 + t;
                 const float4 b2 = *reinterpret_cast<const float4 *>(a.x2 + o);
                 const float4 b3 = *reinterpret_cast<const float4 *>(a.x3 + o);
                 const float s3 = a.sum_scale;
@@ -393,14 +405,15 @@ __global__ void __launch_bounds__(256, SPLIT ? 2 : 3) k_prologue_h(const float *
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
             const float in[4] = {v4[e].x, v4[e].y, v4[e].z, v4[e].w};
+            const float4 p0 = prm0[e], p1 = prm1[e];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 float w = in[i];
                 if (NORM) {
-                    w = __fmul_rn(__fsub_rn(w, mean[e]), scale[e]);
-                    w = __fadd_rn(__fmul_rn(w, nw[e]), nb[e]);
-                    w = __fadd_rn(w, __fmul_rn(w, g[e]));
-                    w = __fadd_rn(w, be[e]);
+                    w = __fmul_rn(__fsub_rn(w, p0.x), p0.y);
+                    w = __fadd_rn(__fmul_rn(w, p0.z), p0.w);
+                    w = __fadd_rn(w, __fmul_rn(w, p1.x));
+                    w = __fadd_rn(w, p1.y);
                 }
                 if (ACT == ACT_LEAKY) w = leaky(w, a.slope);
                 if (ACT == ACT_GELU) w = gelu_erf(w);
@@ -409,55 +422,69 @@ __global__ void __launch_bounds__(256, SPLIT ? 2 : 3) k_prologue_h(const float *
         }
         if (ACT == ACT_SNAKE) {
             // One warp-wide test instead of a branch per element: when every
-            // argument is in the polynomial's range the 32 elements run as
-            // straight-line code (the general path gives the same values).
-            bool small = true;
+            // argument is in the k = 0 range the 32 elements run as
+            // straight-line polynomials (snake_sin2 gives the same values).
+            bool fast = true;
 #pragma unroll
-            for (int e = 0; e < 8; ++e)
+            for (int e = 0; e < 8; ++e) {
+                const float l = lim[e];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) small = small && fabsf(__fmul_rn(v[i][e], al[e])) <= kSnakeSmall;
-            if (__all_sync(__activemask(), small)) {
+                for (int i = 0; i < 4; ++i) fast = fast && fabsf(v[i][e]) < l;
+            }
+            if (__all_sync(__activemask(), fast)) {
 #pragma unroll
-                for (int e = 0; e < 8; ++e)
+                for (int e = 0; e < 8; ++e) {
+                    const float4 p1 = prm1[e];
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
-                        const float sn = snake_sin_small(__fmul_rn(v[i][e], al[e]));
-                        v[i][e] = __fadd_rn(v[i][e], __fmul_rn(__fmul_rn(sn, sn), ia[e]));
+                        const float yv = __fmul_rn(v[i][e], p1.z);
+                        v[i][e] = __fadd_rn(v[i][e], __fmul_rn(snake_p(__fmul_rn(yv, yv)), p1.w));
                     }
+                }
             } else {
 #pragma unroll
-                for (int e = 0; e < 8; ++e)
+                for (int e = 0; e < 8; ++e) {
+                    const float4 p1 = prm1[e];
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const float sn = snake_sin(__fmul_rn(v[i][e], al[e]));
-                        v[i][e] = __fadd_rn(v[i][e], __fmul_rn(__fmul_rn(sn, sn), ia[e]));
-                    }
+                    for (int i = 0; i < 4; ++i)
+                        v[i][e] = __fadd_rn(v[i][e], __fmul_rn(snake_sin2(__fmul_rn(v[i][e], p1.z)), p1.w));
+                }
             }
         }
-        uint4 *dst = reinterpret_cast<uint4 *>(y + ((int64_t)ch * Ry + row) * 8);
+        const int64_t off = ((int64_t)ch * Ry + row0 + t) * 8;
+        uint4 *dst = reinterpret_cast<uint4 *>(y + off);
+        const bool whole = t + 4 <= len;
         if (SPLIT) {
             // hi and lo halves of each row: [hi chunks | lo chunks]
-            uint4 *dlo = reinterpret_cast<uint4 *>(y + ((int64_t)ch * Ry + row) * 8 + a.lo_off);
+            uint4 *dlo = reinterpret_cast<uint4 *>(y + off + a.lo_off);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 __align__(16) __half hh[8], ll[8];
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
-                    const float w = (e >= nc || t + i >= len) ? 0.f : v[i][e];
-                    hh[e] = __float2half_rn(w);
-                    ll[e] = split_lo(w, hh[e]);
+                    hh[e] = __float2half_rn(v[i][e]);
+                    ll[e] = split_lo(v[i][e], hh[e]);
                 }
-                dst[i] = *reinterpret_cast<const uint4 *>(hh);
-                dlo[i] = *reinterpret_cast<const uint4 *>(ll);
+                const bool keep = whole || t + i < len;
+                dst[i] = keep ? *reinterpret_cast<const uint4 *>(hh) : make_uint4(0u, 0u, 0u, 0u);
+                dlo[i] = keep ? *reinterpret_cast<const uint4 *>(ll) : make_uint4(0u, 0u, 0u, 0u);
             }
         } else {
-            __align__(16) __half h[4][8];
+            uint4 h4[4];
 #pragma unroll
-            for (int e = 0; e < 8; ++e)
+            for (int i = 0; i < 4; ++i) {
+                __align__(16) __half2 p[4];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) h[i][e] = __float2half_rn((e >= nc || t + i >= len) ? 0.f : v[i][e]);
+                for (int j = 0; j < 4; ++j) p[j] = __floats2half2_rn(v[i][2 * j], v[i][2 * j + 1]);
+                h4[i] = *reinterpret_cast<const uint4 *>(p);
+            }
+            if (whole) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i) dst[i] = *reinterpret_cast<const uint4 *>(h[i]);
+                for (int i = 0; i < 4; ++i) dst[i] = h4[i];
+            } else {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) dst[i] = t + i < len ? h4[i] : make_uint4(0u, 0u, 0u, 0u);
+            }
         }
     }
 }
