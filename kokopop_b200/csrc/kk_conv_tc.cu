@@ -83,6 +83,10 @@ __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
@@ -258,6 +262,8 @@ struct TcParams {
     // k_convt_tc: channels per phase in one tile (the tile's MMA N is
     // omul * phase_nc, its rows phase-major)
     int phase_nc;
+    // k_conv_tct: non-null, the dynamic tile order (ConvTcArgs::sched)
+    int *sched;
 };
 
 // Positions x channels, register epilogue (strided row maps). Persistent: CTA
@@ -600,7 +606,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     uint8_t *sE = sW + NSW * TC_B_BYTES;    // STAGED: two 4 KB blocks per epilogue warp (1 KB aligned)
     uint64_t *bars = (uint64_t *)(sE + (STAGED ? TC_EPI_WARPS * 2 * TC_BLK_BYTES : 0));
     // A_full[NSA] A_empty[NSA] W_full[NSW] W_empty[NSW] acc_full[2] acc_empty[2]
-    // drain res[8 warps][2] tmem-slot
+    // drain res[8 warps][2] tmem-slot sched_full[4] sched_empty[4] sched_tile[4]
     const uint32_t bA_full = smem_u32(bars), bA_empty = smem_u32(bars + NSA);
     const uint32_t bW_full = smem_u32(bars + 2 * NSA), bW_empty = smem_u32(bars + 2 * NSA + NSW);
     const uint32_t bAcc_full = smem_u32(bars + 2 * NSA + 2 * NSW);
@@ -608,11 +614,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const uint32_t bDrain = smem_u32(bars + 2 * NSA + 2 * NSW + 4);
     const uint32_t bRes = smem_u32(bars + 2 * NSA + 2 * NSW + 5);
     uint32_t *tmem_slot = (uint32_t *)(bars + 2 * NSA + 2 * NSW + 5 + 2 * TC_EPI_WARPS);
+    // dynamic tile order: the producer publishes each tile index (-1: no
+    // more) in a 4-slot ring that the MMA thread and the epilogue warps read
+    const uint32_t bS_full = smem_u32(bars + 2 * NSA + 2 * NSW + 6 + 2 * TC_EPI_WARPS);
+    const uint32_t bS_empty = bS_full + 8 * 4;
+    volatile int64_t *s_tile = (volatile int64_t *)(bars + 2 * NSA + 2 * NSW + 14 + 2 * TC_EPI_WARPS);
+    const bool dyn = P.sched != nullptr;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t n_tiles_total = P.m_tiles * P.n_oc_tiles;
 
     if (threadIdx.x == 0) {
+        for (int i = 0; i < 4; ++i) {
+            mbar_init(bS_full + 8 * i, 1);
+            mbar_init(bS_empty + 8 * i, 1 + TC_EPI_WARPS);
+        }
         for (int i = 0; i < NSA; ++i) {
             mbar_init(bA_full + 8 * i, 1);
             mbar_init(bA_empty + 8 * i, 1);
@@ -645,12 +661,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            // producer
+            // producer (and, in the dynamic order, the tile scheduler)
             bool ok = true;
             uint32_t ia = 0, iw = 0;
-            for (int64_t tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x) {
+            int64_t tile = blockIdx.x;
+            for (uint32_t it = 0; ok; ++it) {
+                if (dyn) {
+                    const int q = it & 3;
+                    if (it >= 4) ok = mbar_wait(bS_empty + 8 * q, ((it >> 2) & 1) ^ 1, P.err, 22);
+                    if (!ok) break;
+                    s_tile[q] = tile < n_tiles_total ? tile : -1;
+                    mbar_arrive(bS_full + 8 * q);
+                }
+                if (tile >= n_tiles_total) break;
                 const int64_t mt = tile / P.n_oc_tiles;
                 const int nt = (int)(tile % P.n_oc_tiles);
+                // the next tile, asked for before this one's copies are issued
+                tile = dyn ? (int64_t)gridDim.x + atomicAdd(P.sched, 1) : tile + gridDim.x;
                 const int64_t row0 = mt * TC_BM - P.p;  // >= -kHalfLo (checked on the host)
                 for (int b = 0; b < P.IC_blocks && ok; ++b, ++ia) {
                     const int sa = ia % NSA;
@@ -687,7 +714,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const uint32_t idesc = idesc_f16(TC_BN, TC_BM);
             bool ok = true;
             uint32_t ia = 0, iw = 0, it = 0;
-            for (int64_t tile = blockIdx.x; tile < n_tiles_total && ok; tile += gridDim.x, ++it) {
+            int64_t tile = blockIdx.x;
+            for (; ok; ++it) {
+                if (dyn) {
+                    const int q = it & 3;
+                    ok = mbar_wait(bS_full + 8 * q, (it >> 2) & 1, P.err, 23);
+                    if (!ok) break;
+                    tile = s_tile[q];
+                    mbar_arrive(bS_empty + 8 * q);
+                    if (tile < 0) break;
+                } else if (it > 0) {
+                    tile += gridDim.x;
+                }
+                if (tile >= n_tiles_total) break;
                 const int ab = it & 1;
                 if (it >= 2) ok = mbar_wait(bAcc_empty + 8 * ab, ((it >> 1) & 1) ^ 1, P.err, 17);
                 if (!ok) break;
@@ -734,7 +773,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         uint32_t it = 0;
         uint32_t ci = 0, n_res = 0;  // STAGED: blocks done / residual blocks requested
         bool stop = false;
-        for (int64_t tile = blockIdx.x; tile < n_tiles_total && !stop; tile += gridDim.x, ++it) {
+        int64_t tile = blockIdx.x;
+        for (; !stop; ++it) {
+            if (dyn) {
+                const int q = it & 3;
+                int64_t tv = -1;
+                int okl = 1;
+                if (lane == 0) {
+                    okl = mbar_wait(bS_full + 8 * q, (it >> 2) & 1, P.err, 24) ? 1 : 0;
+                    if (okl) {
+                        tv = s_tile[q];
+                        mbar_arrive(bS_empty + 8 * q);
+                    }
+                }
+                if (__shfl_sync(0xffffffffu, okl, 0) == 0) break;
+                tile = __shfl_sync(0xffffffffu, tv, 0);
+                if (tile < 0) break;
+            } else if (it > 0) {
+                tile += gridDim.x;
+            }
+            if (tile >= n_tiles_total) break;
             const int64_t mt = tile / P.n_oc_tiles;
             const int n0 = (int)(tile % P.n_oc_tiles) * TC_BN;
             const int ab = it & 1;
@@ -895,6 +953,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         fence_after_sync();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS)
                      : "memory");
+    }
+    if (dyn && threadIdx.x == 0) {
+        // this CTA's producer asks for no more tiles; the last CTA to get here
+        // leaves the counters at zero for the next launch
+        __threadfence();
+        if (atomicAdd(P.sched + 1, 1) == (int)gridDim.x - 1) {
+            atomicExch(P.sched, 0);
+            atomicExch(P.sched + 1, 0);
+        }
     }
 }
 
@@ -2092,8 +2159,7 @@ cudaError_t conv_tc(const ConvTcArgs &a, cudaStream_t st) {
     if (a.stats && (a.sb.n < 1 || a.sm < 1 || a.sextra < 0 || a.omul != 1 || a.oadd != 0 || a.phase_oc != 0))
         return cudaErrorInvalidValue;
     const int64_t tiles = P.m_tiles * P.n_oc_tiles;
-    int64_t slots = g_num_sms > 0 ? g_num_sms : 148;
-    if (a.max_ctas > 0 && a.max_ctas < slots) slots = a.max_ctas;
+    const int64_t slots = g_num_sms > 0 ? g_num_sms : 148;
     const unsigned grid = (unsigned)(tiles < slots ? tiles : slots);
     // channels x positions kernel where output row = position
     // (a residual upsampled x2 by resid_half only on the unstaged epilogue;
@@ -2112,6 +2178,7 @@ cudaError_t conv_tc(const ConvTcArgs &a, cudaStream_t st) {
         // start on block boundaries (then R_out is a multiple of 128)
         const bool fused = a.stats && a.part && a.stats_aligned && a.n_pos == a.R_out && a.R_out % 128 == 0;
         if (fused) P.part = a.part;
+        P.sched = a.sched;
         if (staged)
             k_conv_tct<true><<<grid, TC_THREADS, tt_smem(true), st>>>(P, omap, rmap);
         else

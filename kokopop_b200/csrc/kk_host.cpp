@@ -1075,9 +1075,6 @@ struct Runner {
     float *gbase = nullptr, *bbase = nullptr;
     const bool tc;
     const bool split;  // F32 weights split over the half tensor cores
-    // > 0: the persistent convolutions launch at most this many CTAs (the
-    // SMs the harmonic source, running beside the decoder, leaves free)
-    int conv_cap = 0;
 
     // tc_path: the tensor-core path (default: the context's mode, split F32
     // included); split_path: with tc_path set, its operands split F32
@@ -1262,7 +1259,7 @@ struct Runner {
         ConvTcArgs a{};
         a.phase_oc = phase_oc;
         a.phase_nc = phase_nc;
-        a.max_ctas = conv_cap;
+        a.sched = (int *)((char *)c.d_err.p + offsetof(DevStatus, sched));
         a.in = in.h;
         a.R_in = in.Ry;
         a.IC_pad = pw.IC_pad;
@@ -1860,10 +1857,6 @@ struct Runner {
         scatter(noise, np, R2, 1, 2, 0, B, d_cum, 2 * P.maxT, st);
         c.n_launches += 3;
         float *har = source_and_har(f0p, 2);
-        // the source holds sinegen_blocks SMs while the decoder runs; the
-        // decoder's persistent convs take the others (a CTA that could not be
-        // resident would hold its tiles until the source ends)
-        conv_cap = std::max(1, num_sms() - sinegen_blocks(P.n));
         setup_adain(style);
         const std::string d = "kokopop.decoder.";
         const DevTensor &f0w = c.W(d + "F0_conv.weight"), &f0b = c.W(d + "F0_conv.bias");
@@ -1893,16 +1886,7 @@ struct Runner {
         });
         ++c.n_launches;
         check_cuda(cudaStreamWaitEvent(st, c.ev_src, 0), "wait source");
-        conv_cap = 0;
         generator(2, dec, har, audio);
-    }
-
-    int num_sms() const {
-        int dev = 0, n = 0;
-        if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) !=
-                                                      cudaSuccess)
-            return 148;
-        return n;
     }
 
     // sano_run_vocos (sano_vocos.cpp:94-230) over the chunks of the plan

@@ -187,10 +187,11 @@ struct ConvTcArgs {
     // phase r at input position q writes output row q * omul + oadd + r.
     // Epilogue: bias and residual only.
     int phase_nc;
-    // > 0: at most this many persistent CTAs (the SMs left while another
-    // stream's kernel holds the rest; a static tile split over CTAs that
-    // cannot all be resident would wait for that kernel)
-    int max_ctas;
+    // non-null (DevStatus::sched, zero at launch): the channels x positions
+    // kernel hands out its tiles past each CTA's first in the order CTAs ask
+    // for them, so that CTAs which start late (their SMs held by another
+    // stream's kernel) take fewer tiles instead of holding the launch's end
+    int *sched;
     // non-null: the instance-norm terms (mean, scale) of the output over each
     // utterance's valid rows at level (sm, sextra) of batch sb, into
     // stats[u * OC + c]. With stats_aligned (every utterance of the level
@@ -251,6 +252,10 @@ constexpr int kErrNonFinite = 60;  // + label
 struct DevStatus {
     int code;
     int pad;
+    // the dynamic tile order of the channels x positions convolution: the
+    // next tile past the static first ones, and the CTAs done (both zero
+    // between launches: the last CTA of a launch resets them)
+    int sched[2];
     unsigned long long first[kFiniteLabels];
 };
 // Records a non-finite value of x[0, n) (label's smallest index, and the
