@@ -803,10 +803,11 @@ void f0n_conv(const float *in, int64_t R_in, float *out0, float *out1, int64_t R
 // A block carries kSineGroups utterances, one group of 4 warps each with its
 // own named barrier and buffer, so the source occupies n / kSineGroups SMs
 // while it runs beside the decoder (sinegen_blocks), not one per utterance:
-// the decoder's persistent convolutions keep the other SMs. Measured at
-// batch 64 (whole forwards): one utterance per block 62.2-63.0 ms, two
-// 60.9-61.3 ms, four 63.2-63.9 ms (the source itself slower), against
-// 62.1 ms with one per block and no cap on the conv grids.
+// the decoder's persistent convolutions keep the other SMs (their CTAs take
+// tiles in dynamic order, so one that starts late takes fewer). Measured at
+// batch 64 (whole forwards, the conv grids then capped at the SMs the source
+// left): one utterance per block 62.2-63.0 ms, two 60.9-61.3 ms, four
+// 63.2-63.9 ms (the source itself slower).
 constexpr int kSineThreads = 128;  // per utterance
 constexpr int kSineGroups = 2;
 constexpr int kSineSmem = kSineGroups * 2 * kHarmonics * kUpsample * 4;
