@@ -808,9 +808,19 @@ void f0n_conv(const float *in, int64_t R_in, float *out0, float *out1, int64_t R
 // batch 64 (whole forwards, the conv grids then capped at the SMs the source
 // left): one utterance per block 62.2-63.0 ms, two 60.9-61.3 ms, four
 // 63.2-63.9 ms (the source itself slower).
+// Two more measures keep the recurrence, the source's critical path, short
+// (batch 64: the source 4.75 -> 3.37 ms beside the decoder, which waited for
+// it, the forward -0.6 ms): each group's recurrence warp is a different warp
+// of the block modulo 4, so the two recurrences run on different warp
+// schedulers; and the block reserves the SM's shared memory, so that no
+// block of another kernel (the issue-heavy operand pass) shares its SM.
+// (Computing every segment's rotation beforehand in a parallel kernel, which
+// leaves the recurrence warp the rotations alone, changed nothing.)
 constexpr int kSineThreads = 128;  // per utterance
 constexpr int kSineGroups = 2;
-constexpr int kSineSmem = kSineGroups * 2 * kHarmonics * kUpsample * 4;
+constexpr int kSineSmem = kSineGroups * 2 * kHarmonics * kUpsample * 4;  // used
+constexpr int kSineBlockSmem = 227 * 1024;                              // reserved
+static_assert(kSineSmem <= kSineBlockSmem, "source buffers");
 
 __global__ void __launch_bounds__(kSineThreads *kSineGroups) k_sinegen(const float *__restrict__ f0, int mf,
                                                                        float *__restrict__ source, Batch b,
@@ -823,13 +833,15 @@ __global__ void __launch_bounds__(kSineThreads *kSineGroups) k_sinegen(const flo
     float(*sbuf)[kHarmonics][kUpsample] =
         reinterpret_cast<float(*)[kHarmonics][kUpsample]>(sine_smem + grp * 2 * kHarmonics * kUpsample);
     const int tid = threadIdx.x % kSineThreads, lane = tid & 31, warp = tid >> 5;
+    const int cw = grp & 3;                             // this group's recurrence warp
+    const int mt = ((warp - cw - 1) & 3) * 32 + lane;  // the merge warps' thread index, 0..95
     const int64_t nseg = (int64_t)mf * b.T[u];
     const float *fp = f0 + (int64_t)mf * b.offT[u];
     float *src = source + (int64_t)kUpsample * mf * cumT[u];
     float ps = 0.f, pc = 1.f;
-    const bool chain = warp == 0 && lane < kHarmonics;
+    const bool chain = warp == cw && lane < kHarmonics;
     for (int64_t step = 0; step <= nseg; ++step) {
-        if (warp == 0) {
+        if (warp == cw) {
             // the phasors through segment `step`
             if (step < nseg && chain) {
                 const float base_f0 = fp[step];
@@ -863,14 +875,14 @@ __global__ void __launch_bounds__(kSineThreads *kSineGroups) k_sinegen(const flo
             float *out = src + seg * kUpsample;
             if (fp[seg] > 10.0f) {
                 const float(*sb)[kUpsample] = sbuf[seg & 1];
-                for (int j = tid - 32; j < kUpsample; j += kSineThreads - 32) {
+                for (int j = mt; j < kUpsample; j += kSineThreads - 32) {
                     float merged = a.mb;
 #pragma unroll
                     for (int h = 0; h < kHarmonics; ++h) merged = __fadd_rn(merged, __fmul_rn(a.mw_scaled[h], sb[h][j]));
                     out[j] = (float)tanh((double)merged);
                 }
             } else {
-                for (int j = tid - 32; j < kUpsample; j += kSineThreads - 32) out[j] = a.unvoiced;
+                for (int j = mt; j < kUpsample; j += kSineThreads - 32) out[j] = a.unvoiced;
             }
         }
         // this group's barrier (ids 1 .. kSineGroups; 0 is __syncthreads)
@@ -886,10 +898,10 @@ void sinegen(const float *f0, int mf, float *source, const Batch &b, const int64
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        cudaFuncSetAttribute(k_sinegen, cudaFuncAttributeMaxDynamicSharedMemorySize, kSineSmem);
+        cudaFuncSetAttribute(k_sinegen, cudaFuncAttributeMaxDynamicSharedMemorySize, kSineBlockSmem);
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
-    k_sinegen<<<sinegen_blocks(b.n), kSineThreads * kSineGroups, kSineSmem, st>>>(f0, mf, source, b, cumT, a);
+    k_sinegen<<<sinegen_blocks(b.n), kSineThreads * kSineGroups, kSineBlockSmem, st>>>(f0, mf, source, b, cumT, a);
 }
 
 // Forward STFT of the source (audio_utils.cpp:381-419): Hann-20 window, hop
