@@ -123,25 +123,39 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks / throttle reasons sampled during the timed region.
 
-    FIELDS = ("index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    nvidia-smi takes a while to print its first sample, and the timed region
+    lasts well under a second, so the sampler starts before the warm-up,
+    waits for its first sample, samples every 50 ms, and keeps the samples
+    whose timestamps fall inside the timed region (mark() brackets it)."""
+
+    FIELDS = ("timestamp,index,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, path):
         self.path = path
         self.proc = None
+        self.window = None
 
-    def start(self):
+    def start(self, wait_s=5.0):
         try:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader",
-                                          "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+                                          "-lms", "50"], stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+            return
+        t_end = time.time() + wait_s
+        while time.time() < t_end and os.path.getsize(self.path) == 0 and self.proc.poll() is None:
+            time.sleep(0.02)
+
+    def mark(self, t0, t1):
+        self.window = (t0, t1)
 
     def stop(self, uuid=None):
+        import datetime
         if self.proc is None:
             return None
         self.proc.terminate()
@@ -150,25 +164,29 @@ class ClockSampler:
         except Exception:
             self.proc.kill()
         self.f.close()
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        rows = []
         for line in open(self.path):
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 10:
+            if len(parts) < 11:
                 continue
-            if uuid and parts[1] != uuid:
+            if uuid and parts[2] != uuid:
                 continue
             try:
-                sm.append(float(parts[2].split()[0]))
-                mx = float(parts[3].split()[0])
+                ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                rows.append((ts, float(parts[3].split()[0]), float(parts[4].split()[0]), parts[7:11]))
             except ValueError:
                 continue
-            for n, v in zip(names, parts[6:10]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sm:
+        if self.window is not None:
+            t0, t1 = self.window
+            inside = [r for r in rows if t0 <= r[0] <= t1]
+            # a region shorter than the sampling period: the samples around it
+            rows = inside or [r for r in rows if t0 - 0.1 <= r[0] <= t1 + 0.1]
+        if not rows:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = {n for r in rows for n, v in zip(names, r[3]) if v.lower() == "active"}
+        return {"sm_mhz": statistics.median(r[1] for r in rows), "sm_max_mhz": rows[-1][2],
+                "reasons": sorted(reasons), "samples": len(rows)}
 
 
 def make_pool():
@@ -645,18 +663,19 @@ def main():
             step_host(k)
 
     # ---- device-resident throughput (value) ----
+    clocks = ClockSampler(os.path.join("/tmp", f"kk_clocks_{rank}.csv"))
+    if rank == 0:
+        clocks.start()
     for k in range(args.warmup):
         step_device(k)
     torch.cuda.synchronize()
     ctx.profile_read(reset=True)
     ctx.profile_enable(True)
-    clocks = ClockSampler(os.path.join("/tmp", f"kk_clocks_{rank}.csv"))
-    if rank == 0:
-        clocks.start()
     barrier()
     torch.cuda.synchronize()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
+    tw0 = time.time()
     ev0.record(stream)
     secs = 0.0
     th0 = time.perf_counter()
@@ -665,6 +684,7 @@ def main():
     host_enqueue_ms = (time.perf_counter() - th0) * 1e3 / max(1, args.steps)
     ev1.record(stream)
     torch.cuda.synchronize()
+    clocks.mark(tw0, time.time())
     barrier()
     elapsed = ev0.elapsed_time(ev1) / 1e3
     uuid = None
