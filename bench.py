@@ -758,24 +758,33 @@ def main():
             lat.append(time.perf_counter() - t)
         ttfa = 1e3 * statistics.median(lat)
         c0.close()
+    def leg(name, fn, *a):
+        # an NVTX range per leg, so that a profiler can select one leg's
+        # launches (ncu --nvtx --nvtx-include "<name>/")
+        torch.cuda.nvtx.range_push(name)
+        try:
+            return fn(*a)
+        finally:
+            torch.cuda.nvtx.range_pop()
+
     lstm = None
     if single and args.lstm_runs > 0:
-        lstm = bench_lstm(kb, W, local, args.lstm_runs)
+        lstm = leg("lstm", bench_lstm, kb, W, local, args.lstm_runs)
     prosody = None
     if single and args.prosody_runs > 0:
-        prosody = bench_prosody(kb, W, local, args.prosody_runs, pool, args.batch)
+        prosody = leg("prosody", bench_prosody, kb, W, local, args.prosody_runs, pool, args.batch)
     queue = None
     if single and not args.no_queue:
-        queue = bench_queue(kb, local, weights, [pool[i] for idx in batches for i in idx], args.batch)
+        queue = leg("queue", bench_queue, kb, local, weights, [pool[i] for idx in batches for i in idx], args.batch)
     stream = None
     if single and args.stream_runs > 0:
-        stream = bench_stream(kb, W, local, weights, args.stream_runs)
+        stream = leg("stream", bench_stream, kb, W, local, weights, args.stream_runs)
     frontend = None
     if single and args.frontend_runs > 0:
-        frontend = bench_frontend(kb, W, local, args.frontend_runs)
+        frontend = leg("frontend", bench_frontend, kb, W, local, args.frontend_runs)
     vocos = None
     if single and args.vocos_runs > 0:
-        vocos = bench_vocos(kb, W, local, args.vocos_runs)
+        vocos = leg("vocos", bench_vocos, kb, W, local, args.vocos_runs)
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
             sample = cpu_sample(pool)
