@@ -515,10 +515,10 @@ void prologue_h(const float *x, __half *y, int64_t R, int64_t Ry, int C, int m, 
                 int mean_len, const PrologueArgs &a, cudaStream_t st) {
     // about three passes per thread over an utterance of the mean length, so
     // the per-channel set-up of a thread is spread over several; blocks of
-    // 64 threads (256 rows a pass) where utterances are short (the decoder
-    // levels and generator stage 0: the finer blocks made the batch-64 stage-0
-    // passes 6 % faster than 256 threads), else 256 (1024 rows, stage 1)
-    const int nt = mean_len < 16384 ? 64 : 256;
+    // 64 threads (256 rows a pass): at batch 64 they made the generator's
+    // stage-1 passes 8 % and its stage-0 passes 6 % faster than blocks of 256
+    // (128: in between)
+    const int nt = 64;
     int bx = (mean_len + 3 * 4 * nt - 1) / (3 * 4 * nt);
     if (bx > 64) bx = 64;
     if (bx < 1) bx = 1;
